@@ -1,0 +1,138 @@
+"""ctypes binding of ``libkvs_b200.so`` (built in-tree by ``ops/build.py``).
+
+The structures below mirror ``csrc/kvs_types.h`` field for field; their
+sizes are checked against the library at load time.
+
+Loading policy: the library is loaded from this directory only.  When it is
+missing, CPU-only callers get a clear error on first use; on a machine with a
+CUDA device the import of any device op raises instead of falling back to a
+slower path (a fallback would hide a broken build).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from ctypes import (POINTER, c_double, c_float, c_int, c_longlong, c_uint8, c_uint32,
+                    c_uint64, c_ulonglong, c_void_p)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkvs_b200.so")
+
+MAX_HEADS = 16
+
+
+class PagedKV(ctypes.Structure):
+    _fields_ = [("base", c_void_p), ("block_stride", c_longlong), ("kv_stride", c_longlong),
+                ("num_blocks", c_int), ("block_size", c_int)]
+
+
+class ReqTable(ctypes.Structure):
+    _fields_ = [("block_table", c_void_p), ("bt_off", c_void_p), ("n_tokens", c_void_p),
+                ("n_rows", c_void_p), ("tile_prefix", c_void_p), ("code_off", c_void_p),
+                ("meta_off", c_void_p), ("num_req", c_int)]
+
+
+class LayerParams(ctypes.Structure):
+    _fields_ = [("H", c_int), ("n_groups", c_int),
+                ("key_levels", c_float * MAX_HEADS), ("value_levels", c_float * MAX_HEADS),
+                ("key_bits", c_int * MAX_HEADS), ("value_bits", c_int * MAX_HEADS),
+                ("group_of_head", c_int * MAX_HEADS),
+                ("seg_prefix", c_int * (2 * MAX_HEADS + 1)),
+                ("sign_bits", (c_uint32 * 4) * MAX_HEADS),
+                ("clamp_top", c_int), ("transform", c_int), ("out_scale", c_float)]
+
+
+class LayerLaunch(ctypes.Structure):
+    _fields_ = [("kv", PagedKV), ("rt", ReqTable), ("lp", LayerParams), ("bmat", c_void_p),
+                ("codes", c_void_p), ("meta", c_void_p), ("kstat", c_void_p), ("err", c_void_p),
+                ("total_tiles", c_int), ("engine", c_int), ("stream", c_void_p)]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    P = c_void_p
+    sig = {
+        "kvs_layer_launch_size": ([], c_int),
+        "kvs_init_key_stats": ([P, c_longlong, P], c_int),
+        "kvs_key_stats": ([POINTER(LayerLaunch)], c_int),
+        "kvs_quant_k": ([POINTER(LayerLaunch)], c_int),
+        "kvs_quant_v": ([POINTER(LayerLaunch)], c_int),
+        "kvs_dequant_inverse": ([POINTER(LayerLaunch)], c_int),
+        "kvs_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
+        "kvs_rans_staging_bytes": ([c_uint64, c_uint32], c_uint64),
+        "kvs_rans_encode": ([P, c_uint64, c_uint32, P, P, P, P, P, P, c_uint32, P], c_int),
+        "kvs_rans_decode": ([P, P, c_uint64, c_uint32, P, P], c_int),
+        "kvs_cpu_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
+        "kvs_cpu_rans_encode": ([P, c_uint64, c_uint32, P, c_uint64], c_uint64),
+        "kvs_cpu_rans_decode": ([P, c_uint64, P, c_uint64], c_int),
+        "kvs_cpu_bitpack": ([P, c_uint64, c_int, P], None),
+        "kvs_cpu_bitunpack": ([P, c_uint64, c_int, P], None),
+        "kvs_block_copy": ([POINTER(PagedKV), P, c_int, c_longlong, P, c_int, P, P, c_uint32, P],
+                           c_int),
+        "kvs_copy16": ([P, P, c_longlong, P, P, c_uint32, c_int, P], c_int),
+        "kvs_wait_flag": ([P, c_uint32, c_uint64, P, P, P], c_int),
+        "kvs_set_flag": ([P, c_uint32, P], c_int),
+        "kvs_probe_push": ([P, P, c_longlong, P, c_int, P], c_int),
+        "kvs_kv_error": ([P, P, c_longlong, P, P, P], c_int),
+        "kvs_logit_agreement": ([P, P, c_int, c_int, P, P], c_int),
+        "kvs_device_count": ([], c_int),
+        "kvs_malloc": ([c_int, c_uint64, POINTER(c_void_p)], c_int),
+        "kvs_free": ([c_int, P], c_int),
+        "kvs_memset": ([P, c_int, c_uint64, P], c_int),
+        "kvs_ipc_get_handle": ([c_int, P, POINTER(c_uint8)], c_int),
+        "kvs_ipc_open_handle": ([c_int, POINTER(c_uint8), POINTER(c_void_p)], c_int),
+        "kvs_ipc_close_handle": ([c_int, P], c_int),
+        "kvs_can_access_peer": ([c_int, c_int], c_int),
+        "kvs_enable_peer_access": ([c_int, c_int], c_int),
+        "kvs_last_error_string": ([], ctypes.c_char_p),
+        "kvs_stream_sync": ([P], c_int),
+        "kvs_library_version": ([], c_int),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded native library (raises with a build hint when missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"native library {LIB_PATH} is missing; build it with "
+                    "`python -m kvserve_hpdps_b200.ops.build`")
+            handle = ctypes.CDLL(LIB_PATH)
+            _declare(handle)
+            got = handle.kvs_layer_launch_size()
+            if got != ctypes.sizeof(LayerLaunch):
+                raise RuntimeError(f"LayerLaunch size mismatch: C {got} vs Python "
+                                   f"{ctypes.sizeof(LayerLaunch)}")
+            _lib = handle
+    return _lib
+
+
+def available() -> bool:
+    try:
+        lib()
+        return True
+    except (RuntimeError, OSError):
+        return False
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with code {rc}: "
+                           f"{lib().kvs_last_error_string().decode(errors='replace')}")
+
+
+__all__ = ["lib", "available", "check", "PagedKV", "ReqTable", "LayerParams", "LayerLaunch",
+           "MAX_HEADS", "c_double", "c_ulonglong"]

@@ -1,0 +1,272 @@
+// Shared device helpers for the sm_100a kernels of kvserve_hpdps_b200.
+//
+// Everything here is hand-written inline PTX for Blackwell (sm_100a):
+// mbarriers, TMA tiled loads (no multicast anywhere: these kernels run on
+// multi-GPU jobs), bulk copies, tcgen05 tensor-memory allocation, UMMA
+// (tcgen05.mma kind::f16) issue/commit and TMEM loads, plus bounded waits
+// that record an error code instead of spinning forever.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#define KVS_DEV __device__ __forceinline__
+
+namespace kvs {
+
+// Error codes written (first writer wins) into a device error word.
+enum : uint32_t {
+  ERR_NONE = 0,
+  ERR_MBAR_TIMEOUT = 1,   // a local mbarrier wait ran out of time
+  ERR_FLAG_TIMEOUT = 2,   // a cross-GPU ready flag never arrived
+  ERR_BOUNDS = 3,         // an index failed a bounds check
+  ERR_CORRUPT = 4,        // a stream header or checksum did not validate
+  ERR_OVERFLOW = 5,       // an output region was too small
+};
+
+constexpr uint64_t kLocalWaitNs = 2000000000ull;  // 2 s for on-chip waits
+
+KVS_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+KVS_DEV uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+KVS_DEV void record_error(uint32_t* err, uint32_t code) {
+  if (err != nullptr) atomicCAS(err, 0u, code);
+}
+
+// ---------------------------------------------------------------- mbarrier
+KVS_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+KVS_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+KVS_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t tx) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(tx)
+               : "memory");
+}
+KVS_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+KVS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on a phase of an mbarrier.  Returns false (and records
+// `code`) when the phase does not complete within `timeout_ns`.
+KVS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
+                       uint64_t timeout_ns = kLocalWaitNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > timeout_ns) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------ async copies
+// Generic-proxy smem writes must be fenced before the async proxy (UMMA,
+// TMA store) reads them.
+KVS_DEV void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// TMA tiled 3-D load of one box into shared memory (no multicast).
+KVS_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Untiled bulk copy global -> shared (16-byte aligned, size multiple of 16).
+KVS_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+// Allocate `ncols` TMEM columns (power of two >= 32); executed by a whole warp.
+KVS_DEV void tmem_alloc(uint32_t* slot_in_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot_in_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+KVS_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+KVS_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+KVS_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Instruction descriptor: bf16 x bf16 -> f32, A and B K-major, M=128, N=128.
+//   bits [4,6) c_format=1 (F32); [7,10) a_format=1 (BF16); [10,13) b_format=1;
+//   bit 15/16 a/b major = 0 (K); [17,23) N>>3; [24,29) M>>4.
+constexpr uint32_t kIdescBf16M128N128 =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte
+// swizzled canonical layout: 8-row groups 1024 B apart (SBO), rows 128 B
+// apart, 16-byte chunks XOR-swizzled by (row % 8).  The tile base must be
+// 1024-byte aligned; stepping along K inside the 128-byte row adds the byte
+// offset to the start address.
+KVS_DEV uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1u) << 16;                 // LBO (unused when swizzled)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;         // SBO = 1024 B
+  d |= static_cast<uint64_t>(1u) << 46;                 // descriptor version (sm100)
+  d |= static_cast<uint64_t>(2u) << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+KVS_DEV void umma_bf16_f32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every previously issued tcgen05.mma of this thread
+// has completed.
+KVS_DEV void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// One 128x128x128 product: D[tmem] = A(128xK) * B(128xK)^T over K=128 bf16.
+// Both operands are K-major SW128 tiles of 2 x 16 KB (k 0-63, k 64-127).
+KVS_DEV void umma_tile_128x128x128(uint32_t d_tmem, uint32_t a_base, uint32_t b_base) {
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t off = static_cast<uint32_t>((ks >> 2) * 16384 + (ks & 3) * 32);
+    umma_bf16_f32(d_tmem, sw128_kmajor_desc(a_base + off), sw128_kmajor_desc(b_base + off),
+                  kIdescBf16M128N128, ks > 0 ? 1u : 0u);
+  }
+}
+
+// Load 32 consecutive fp32 columns of this thread's TMEM lane.
+KVS_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ------------------------------------------------------- system-scope flags
+KVS_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+KVS_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+KVS_DEV uint64_t ld_acquire_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+KVS_DEV void st_release_sys64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// --------------------------------------------------------- float helpers
+// Order-preserving map float -> uint32 for atomicMin/atomicMax on floats.
+KVS_DEV uint32_t float_to_ordered(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+KVS_DEV float ordered_to_float(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+KVS_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Quantize one value: floor((v - mn) * rcp + 0.5) clamped to [0, top],
+// with explicit round-to-nearest steps (no FMA contraction) so the device
+// matches the CPU oracle bit for bit.
+KVS_DEV uint32_t quantize_one(float v, float mn, float rcp, float top) {
+  float q = floorf(__fadd_rn(__fmul_rn(__fsub_rn(v, mn), rcp), 0.5f));
+  q = fminf(fmaxf(q, 0.0f), top);
+  return static_cast<uint32_t>(q);
+}
+
+// bf16 dequantization as PyTorch evaluates q_bf16 * scale_bf16 + min_bf16:
+// each operation is computed in fp32 and rounded to bf16.
+KVS_DEV float dequant_bf16(uint32_t q, float scale_bf, float min_bf) {
+  const float prod = bf16_round(__fmul_rn(static_cast<float>(q), scale_bf));
+  return bf16_round(__fadd_rn(prod, min_bf));
+}
+
+// Pack 32 codes of `W` bits each (code j at bits [j*W, j*W+W) of a
+// little-endian bit stream) into W 32-bit words.
+template <int W>
+KVS_DEV void pack32(const uint32_t (&c)[32], uint32_t (&w)[8]) {
+#pragma unroll
+  for (int i = 0; i < W; ++i) w[i] = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int bit = j * W;
+    const int wi = bit >> 5, bo = bit & 31;
+    w[wi] |= c[j] << bo;
+    if (bo + W > 32) w[wi + 1] |= c[j] >> (32 - bo);
+  }
+}
+template <int W>
+KVS_DEV void unpack32(const uint32_t (&w)[8], uint32_t (&c)[32]) {
+  constexpr uint32_t mask = (W == 32) ? 0xFFFFFFFFu : ((1u << W) - 1u);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int bit = j * W;
+    const int wi = bit >> 5, bo = bit & 31;
+    uint32_t v = w[wi] >> bo;
+    if (bo + W > 32) v |= w[wi + 1] << (32 - bo);
+    c[j] = v & mask;
+  }
+}
+
+}  // namespace kvs

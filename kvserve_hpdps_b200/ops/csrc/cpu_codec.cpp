@@ -1,0 +1,238 @@
+// CPU implementation of the interleaved rANS stream (format: rans.cuh) and
+// of the fixed-width bit packing used by the fused kernels.
+//
+// The encoder emulates the 32 warp lanes of the device encoder step by step,
+// so for the same input it produces the same bytes as k_rans_encode +
+// k_rans_directory + k_rans_copy.  It is the oracle of the device codec and
+// the codec of CPU-only round trips.
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "rans.cuh"
+
+using namespace kvs::rans;
+
+namespace {
+
+inline uint32_t umulhi32(uint32_t a, uint32_t b) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(a) * b) >> 32);
+}
+
+inline uint32_t sym_at(const uint8_t* src, uint32_t n_sym, uint32_t idx) {
+  return idx < n_sym ? src[idx] : 0u;
+}
+
+// Encode one chunk into a slot buffer; returns (rec_off, rec_len).
+std::pair<uint32_t, uint32_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t cs,
+                                           uint8_t* slot) {
+  const uint64_t sb = slot_bytes(cs);
+  const uint32_t n_ss = (n_sym + kSuper - 1) / kSuper;
+  uint64_t hist[256] = {0};
+  for (uint32_t i = 0; i < n_ss * kSuper; ++i) hist[sym_at(src, n_sym, i)]++;
+  int top = -1;
+  for (int s = 0; s < 256; ++s)
+    if (hist[s]) top = s;
+  const uint32_t A = static_cast<uint32_t>(top + 1);
+  uint32_t freq[256] = {0};
+  normalize_counts(hist, A, static_cast<uint64_t>(n_ss) * kSuper, freq);
+  EncSym enc[256];
+  uint32_t cum = 0;
+  for (uint32_t s = 0; s < A; ++s) {
+    if (freq[s]) enc[s] = make_enc(freq[s], cum);
+    cum += freq[s];
+  }
+  uint16_t* words = reinterpret_cast<uint16_t*>(slot);
+  const int64_t cap = static_cast<int64_t>(sb / 2);
+  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  const int64_t min_w = (16 + fpad + 128) / 2;
+  int64_t wpos = cap;
+  uint32_t x[kLanes];
+  for (int l = 0; l < kLanes; ++l) x[l] = kStateLow;
+  bool overflow = false;
+  for (int ss = static_cast<int>(n_ss) - 1; ss >= 0 && !overflow; --ss) {
+    if (wpos - kSuper - 8 < min_w) {
+      overflow = true;
+      break;
+    }
+    for (int m = kSub - 1; m >= 0; --m) {
+      bool emit[kLanes];
+      int cnt = 0;
+      uint32_t sym[kLanes];
+      for (int l = 0; l < kLanes; ++l) {
+        sym[l] = sym_at(src, n_sym, static_cast<uint32_t>(ss) * kSuper + l * kSub + m);
+        emit[l] = x[l] >= enc[sym[l]].x_max;
+        cnt += emit[l];
+      }
+      int rank = 0;
+      for (int l = 0; l < kLanes; ++l) {
+        if (emit[l]) {
+          words[wpos - cnt + rank] = static_cast<uint16_t>(x[l] & 0xFFFFu);
+          ++rank;
+          x[l] >>= 16;
+        }
+        const EncSym& e = enc[sym[l]];
+        const uint32_t q = umulhi32(x[l], e.rcp) >> (e.cmpl_shift >> 16);
+        x[l] = x[l] + e.bias + q * (e.cmpl_shift & 0xFFFFu);
+      }
+      wpos -= cnt;
+    }
+  }
+  if (!overflow) {
+    const int64_t nw = cap - wpos;
+    const int64_t npad = (8 - (nw & 7)) & 7;
+    const int64_t wstart = wpos - npad;
+    const uint64_t rs = static_cast<uint64_t>(wstart) * 2 - 128 - fpad - 16;
+    uint8_t* rec = slot + rs;
+    ChunkHeader hd{n_sym, A, static_cast<uint32_t>(nw), static_cast<uint32_t>(npad)};
+    std::memcpy(rec, &hd, sizeof(hd));
+    uint16_t* fr = reinterpret_cast<uint16_t*>(rec + 16);
+    for (uint32_t s = 0; s < fpad / 2; ++s) fr[s] = static_cast<uint16_t>(s < A ? freq[s] : 0u);
+    std::memcpy(rec + 16 + fpad, x, sizeof(x));
+    for (int64_t i = 0; i < npad; ++i) words[wstart + i] = 0;
+    return {static_cast<uint32_t>(rs), static_cast<uint32_t>(sb - rs)};
+  }
+  ChunkHeader hd{n_sym, 0u, 0u, 0u};
+  std::memcpy(slot, &hd, sizeof(hd));
+  std::memset(slot + 16, 0, pad16(n_sym));
+  std::memcpy(slot + 16, src, n_sym);
+  return {0u, static_cast<uint32_t>(16 + pad16(n_sym))};
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t kvs_cpu_rans_max_bytes(uint64_t n, uint32_t cs) { return max_stream_bytes(n, cs); }
+
+// Encode n bytes; returns the stream size or 0 on error.
+uint64_t kvs_cpu_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* out,
+                             uint64_t out_cap) {
+  if (n == 0 || cs == 0 || cs % kSuper != 0) return 0;
+  const uint32_t nc = num_chunks(n, cs);
+  const uint64_t sb = slot_bytes(cs);
+  std::vector<uint8_t> slot(sb);
+  std::vector<std::pair<uint32_t, uint32_t>> rec(nc);
+  const uint64_t base = pad16(directory_bytes(nc));
+  uint64_t run = base;
+  std::vector<uint64_t> dir(nc + 1);
+  // Records are emitted into `out` directly; the slot buffer mirrors the
+  // device staging layout so offsets match.
+  for (uint32_t c = 0; c < nc; ++c) {
+    const uint64_t start = static_cast<uint64_t>(c) * cs;
+    const uint32_t n_sym = static_cast<uint32_t>(std::min<uint64_t>(cs, n - start));
+    std::fill(slot.begin(), slot.end(), 0);
+    rec[c] = encode_chunk(in + start, n_sym, cs, slot.data());
+    dir[c] = run;
+    if (run + rec[c].second > out_cap) return 0;
+    std::memcpy(out + run, slot.data() + rec[c].first, rec[c].second);
+    run += rec[c].second;
+  }
+  dir[nc] = run;
+  if (base > out_cap) return 0;
+  std::memset(out + sizeof(StreamHeader) + 8ull * (nc + 1), 0,
+              base - sizeof(StreamHeader) - 8ull * (nc + 1));
+  StreamHeader hd{kMagic, nc, n, cs, static_cast<uint32_t>(kProbBits), run};
+  std::memcpy(out, &hd, sizeof(hd));
+  std::memcpy(out + sizeof(StreamHeader), dir.data(), 8ull * (nc + 1));
+  return run;
+}
+
+// Decode a stream into n bytes; returns 0 on success, negative on error.
+int kvs_cpu_rans_decode(const uint8_t* stream, uint64_t stream_bytes, uint8_t* out, uint64_t n) {
+  if (stream_bytes < sizeof(StreamHeader)) return -1;
+  StreamHeader hd;
+  std::memcpy(&hd, stream, sizeof(hd));
+  if (hd.magic != kMagic || hd.n_symbols != n || hd.prob_bits != kProbBits) return -2;
+  if (hd.total_bytes > stream_bytes) return -3;
+  const uint64_t* dir = reinterpret_cast<const uint64_t*>(stream + sizeof(StreamHeader));
+  for (uint32_t c = 0; c < hd.n_chunks; ++c) {
+    if (dir[c] + 16 > stream_bytes) return -4;
+    const uint8_t* rec = stream + dir[c];
+    ChunkHeader ch;
+    std::memcpy(&ch, rec, sizeof(ch));
+    uint8_t* dst = out + static_cast<uint64_t>(c) * hd.chunk_symbols;
+    if (ch.n_sym > hd.chunk_symbols || ch.alphabet > 256) return -5;
+    if (ch.alphabet == 0) {
+      std::memcpy(dst, rec + 16, ch.n_sym);
+      continue;
+    }
+    const uint32_t A = ch.alphabet;
+    const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
+    const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+    uint32_t x[kLanes];
+    std::memcpy(x, rec + 16 + fpad, sizeof(x));
+    const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
+    const uint32_t total_words = ch.n_pad + ch.n_words;
+    uint32_t fc[256];
+    std::vector<uint8_t> lut(kProbScale);
+    uint32_t cum = 0;
+    for (uint32_t s = 0; s < A; ++s) {
+      fc[s] = freq[s] | (cum << 16);
+      for (uint32_t k = 0; k < freq[s] && cum + k < kProbScale; ++k) lut[cum + k] = static_cast<uint8_t>(s);
+      cum += freq[s];
+    }
+    if (cum != kProbScale) return -6;
+    uint32_t rptr = ch.n_pad;
+    const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
+    for (uint32_t ss = 0; ss < n_ss; ++ss) {
+      for (int m = 0; m < kSub; ++m) {
+        for (int l = 0; l < kLanes; ++l) {
+          const uint32_t sl = x[l] & (kProbScale - 1);
+          const uint32_t s = lut[sl];
+          x[l] = (fc[s] & 0xFFFFu) * (x[l] >> kProbBits) + sl - (fc[s] >> 16);
+          if (x[l] < kStateLow) {
+            if (rptr >= total_words) return -7;
+            x[l] = (x[l] << 16) | words[rptr++];
+          }
+          const uint32_t idx = ss * kSuper + l * kSub + m;
+          if (idx < ch.n_sym) dst[idx] = static_cast<uint8_t>(s);
+        }
+      }
+    }
+    for (int l = 0; l < kLanes; ++l)
+      if (x[l] != kStateLow) return -8;
+    if (rptr != total_words) return -9;
+  }
+  return 0;
+}
+
+// Fixed-width packing of rows of 128 codes (code j of a 32-code group at
+// bits [j*W, j*W+W) of W little-endian 32-bit words); the device kernels
+// read and write the same layout.
+void kvs_cpu_bitpack(const uint8_t* codes, uint64_t n_rows, int bits, uint8_t* out) {
+  for (uint64_t r = 0; r < n_rows; ++r) {
+    const uint8_t* c = codes + r * 128;
+    uint32_t* w = reinterpret_cast<uint32_t*>(out + r * 16ull * bits);
+    std::memset(w, 0, 16ull * bits);
+    for (int g = 0; g < 4; ++g) {
+      uint32_t* wg = w + g * bits;
+      for (int j = 0; j < 32; ++j) {
+        const uint32_t v = c[g * 32 + j] & ((1u << bits) - 1u);
+        const int bit = j * bits, wi = bit >> 5, bo = bit & 31;
+        wg[wi] |= v << bo;
+        if (bo + bits > 32) wg[wi + 1] |= v >> (32 - bo);
+      }
+    }
+  }
+}
+
+void kvs_cpu_bitunpack(const uint8_t* packed, uint64_t n_rows, int bits, uint8_t* codes) {
+  const uint32_t mask = bits >= 32 ? 0xFFFFFFFFu : ((1u << bits) - 1u);
+  for (uint64_t r = 0; r < n_rows; ++r) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(packed + r * 16ull * bits);
+    uint8_t* c = codes + r * 128;
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t* wg = w + g * bits;
+      for (int j = 0; j < 32; ++j) {
+        const int bit = j * bits, wi = bit >> 5, bo = bit & 31;
+        uint32_t v = wg[wi] >> bo;
+        if (bo + bits > 32) v |= wg[wi + 1] << (32 - bo);
+        c[g * 32 + j] = static_cast<uint8_t>(v & mask);
+      }
+    }
+  }
+}
+
+}  // extern "C"

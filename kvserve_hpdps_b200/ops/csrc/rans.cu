@@ -1,0 +1,351 @@
+// Device encoder / decoder of the interleaved rANS stream (format: rans.cuh).
+//
+// Encode = three launches on one stream:
+//   k_rans_encode    one warp per chunk: histogram, normalisation, reverse
+//                    encode into a per-chunk staging slot (raw fallback when
+//                    the coded record would not be smaller than the input);
+//   k_rans_directory one CTA: exclusive scan of record sizes, header + dir;
+//   k_rans_copy      one warp per chunk: compacts records into the output,
+//                    which may be a peer GPU's buffer (NVLink stores); the
+//                    last warp can publish a release flag for the consumer.
+// Decode = k_rans_decode, one warp per chunk, symbols written in place.
+#include "common.cuh"
+#include "rans.cuh"
+
+namespace kvs {
+namespace rans {
+
+constexpr int kEncWarps = 4;
+constexpr int kDecWarps = 8;
+constexpr int kRing = 2048;  // words of the decoder's shared-memory ring
+constexpr int kDecWarpSmem = 4096 + 1024 + kRing * 2;
+
+KVS_DEV uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// 16 symbols of lane `lane` in super-step `ss` (zero padded past n_sym).
+KVS_DEV uint4 load_syms(const uint8_t* src, uint32_t ss, int lane, uint32_t n_sym) {
+  const uint32_t off = ss * kSuper + lane * kSub;
+  if (off + kSub <= n_sym) return *reinterpret_cast<const uint4*>(src + off);
+  uint32_t w[4] = {0, 0, 0, 0};
+  for (uint32_t i = 0; i < kSub; ++i)
+    if (off + i < n_sym) w[i >> 2] |= static_cast<uint32_t>(src[off + i]) << ((i & 3) * 8);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
+    const uint8_t* __restrict__ in, uint64_t n, uint32_t cs, uint8_t* __restrict__ staging,
+    uint32_t* __restrict__ rec_off, uint32_t* __restrict__ rec_len, uint32_t n_chunks) {
+  __shared__ uint32_t hist[kEncWarps][4 * 256];
+  __shared__ EncSym enc[kEncWarps][256];
+  __shared__ uint32_t freq_s[kEncWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t chunk = blockIdx.x * kEncWarps + warp;
+  if (chunk >= n_chunks) return;  // warp-uniform
+  const uint64_t start = static_cast<uint64_t>(chunk) * cs;
+  const uint32_t n_sym = static_cast<uint32_t>(min(static_cast<uint64_t>(cs), n - start));
+  const uint32_t n_ss = (n_sym + kSuper - 1) / kSuper;
+  const uint8_t* src = in + start;
+  const uint64_t sb = slot_bytes(cs);
+  uint8_t* slot = staging + static_cast<uint64_t>(chunk) * sb;
+
+  uint32_t* h = hist[warp];
+  for (int i = lane; i < 4 * 256; i += 32) h[i] = 0;
+  __syncwarp();
+  uint32_t* hc = h + (lane & 3) * 256;
+  for (uint32_t ss = 0; ss < n_ss; ++ss) {
+    const uint4 v = load_syms(src, ss, lane, n_sym);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) atomicAdd(&hc[(w[i >> 2] >> ((i & 3) * 8)) & 0xFF], 1u);
+  }
+  __syncwarp();
+  int top = -1;
+  for (int k = 0; k < 8; ++k) {
+    const int s = lane * 8 + k;
+    const uint32_t c = h[s] + h[256 + s] + h[512 + s] + h[768 + s];
+    h[s] = c;
+    if (c > 0) top = s;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) top = max(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+  const uint32_t A = static_cast<uint32_t>(top + 1);
+  __syncwarp();
+  if (lane == 0) {
+    normalize_counts(h, A, static_cast<uint64_t>(n_ss) * kSuper, freq_s[warp]);
+    uint32_t cum = 0;
+    for (uint32_t s = 0; s < A; ++s) {
+      const uint32_t f = freq_s[warp][s];
+      if (f > 0) enc[warp][s] = make_enc(f, cum);
+      cum += f;
+    }
+  }
+  __syncwarp();
+
+  uint16_t* words = reinterpret_cast<uint16_t*>(slot);
+  const int64_t cap = static_cast<int64_t>(sb / 2);
+  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  const int64_t min_w = (16 + fpad + 128) / 2;
+  int64_t wpos = cap;
+  uint32_t x = kStateLow;
+  bool overflow = false;
+  const uint32_t lt = lanemask_lt();
+  for (int ss = static_cast<int>(n_ss) - 1; ss >= 0; --ss) {
+    if (wpos - kSuper - 8 < min_w) {
+      overflow = true;
+      break;
+    }
+    const uint4 v = load_syms(src, ss, lane, n_sym);
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int m = kSub - 1; m >= 0; --m) {
+      const uint32_t s = (w4[m >> 2] >> ((m & 3) * 8)) & 0xFFu;
+      const EncSym e = enc[warp][s];
+      const bool emit = x >= e.x_max;
+      const uint32_t mask = __ballot_sync(0xFFFFFFFFu, emit);
+      const int cnt = __popc(mask);
+      if (emit) {
+        words[wpos - cnt + __popc(mask & lt)] = static_cast<uint16_t>(x & 0xFFFFu);
+        x >>= 16;
+      }
+      wpos -= cnt;
+      const uint32_t q = __umulhi(x, e.rcp) >> (e.cmpl_shift >> 16);
+      x = x + e.bias + q * (e.cmpl_shift & 0xFFFFu);
+    }
+  }
+  if (!overflow) {
+    const int64_t nw = cap - wpos;
+    const int64_t npad = (8 - (nw & 7)) & 7;
+    const int64_t wstart = wpos - npad;
+    const uint64_t rs = static_cast<uint64_t>(wstart) * 2 - 128 - fpad - 16;
+    uint8_t* rec = slot + rs;
+    if (lane == 0) {
+      ChunkHeader hd{n_sym, A, static_cast<uint32_t>(nw), static_cast<uint32_t>(npad)};
+      *reinterpret_cast<ChunkHeader*>(rec) = hd;
+      rec_off[chunk] = static_cast<uint32_t>(rs);
+      rec_len[chunk] = static_cast<uint32_t>(sb - rs);
+    }
+    uint16_t* fr = reinterpret_cast<uint16_t*>(rec + 16);
+    for (uint32_t s = lane; s < fpad / 2; s += 32)
+      fr[s] = static_cast<uint16_t>(s < A ? freq_s[warp][s] : 0u);
+    reinterpret_cast<uint32_t*>(rec + 16 + fpad)[lane] = x;
+    if (lane < npad) words[wstart + lane] = 0;
+  } else {
+    if (lane == 0) {
+      ChunkHeader hd{n_sym, 0u, 0u, 0u};
+      *reinterpret_cast<ChunkHeader*>(slot) = hd;
+      rec_off[chunk] = 0;
+      rec_len[chunk] = static_cast<uint32_t>(16 + pad16(n_sym));
+    }
+    for (uint32_t ss = 0; ss < (n_sym + 511) / 512; ++ss) {
+      const uint4 v = load_syms(src, ss, lane, n_sym);
+      const uint32_t off = ss * kSuper + lane * kSub;
+      if (off < pad16(n_sym)) *reinterpret_cast<uint4*>(slot + 16 + off) = v;
+    }
+  }
+}
+
+// Single CTA: header, exclusive scan of record lengths, directory.
+__global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restrict__ rec_len,
+                                                         uint32_t n_chunks, uint64_t n,
+                                                         uint32_t cs, uint8_t* __restrict__ out,
+                                                         uint64_t* __restrict__ total_out) {
+  __shared__ uint64_t part[1024];
+  const int tid = threadIdx.x;
+  const uint32_t per = (n_chunks + 1023) / 1024;
+  const uint32_t b = tid * per, e = min(n_chunks, b + per);
+  uint64_t s = 0;
+  for (uint32_t i = b; i < e; ++i) s += rec_len[i];
+  part[tid] = s;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const uint64_t v = tid >= o ? part[tid - o] : 0;
+    __syncthreads();
+    part[tid] += v;
+    __syncthreads();
+  }
+  const uint64_t base = pad16(directory_bytes(n_chunks));
+  uint64_t* dir = reinterpret_cast<uint64_t*>(out + sizeof(StreamHeader));
+  uint64_t run = base + (tid > 0 ? part[tid - 1] : 0);
+  for (uint32_t i = b; i < e; ++i) {
+    dir[i] = run;
+    run += rec_len[i];
+  }
+  if (tid == 0) {
+    for (uint64_t i = sizeof(StreamHeader) + 8ull * (n_chunks + 1); i < base; ++i) out[i] = 0;
+  }
+  if (tid == 1023) {
+    const uint64_t total = base + part[1023];
+    dir[n_chunks] = total;
+    StreamHeader hd{kMagic, n_chunks, n, cs, static_cast<uint32_t>(kProbBits), total};
+    *reinterpret_cast<StreamHeader*>(out) = hd;
+    if (total_out) *total_out = total;
+  }
+  __threadfence_system();
+}
+
+// One warp per record: compact staging -> out (out may be a peer buffer).
+// With `counter` set, the last warp to finish publishes `flag_value` into
+// `flag` with release semantics after a system-scope fence.
+__global__ void __launch_bounds__(256) k_rans_copy(
+    const uint8_t* __restrict__ staging, const uint32_t* __restrict__ rec_off,
+    const uint32_t* __restrict__ rec_len, uint32_t n_chunks, uint32_t cs, uint8_t* out,
+    uint32_t* counter, uint32_t* flag, uint32_t flag_value) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t chunk = blockIdx.x * 8 + warp;
+  if (chunk < n_chunks) {
+    const uint64_t* dir = reinterpret_cast<const uint64_t*>(out + sizeof(StreamHeader));
+    const uint4* s = reinterpret_cast<const uint4*>(staging + static_cast<uint64_t>(chunk) * slot_bytes(cs) + rec_off[chunk]);
+    uint4* d = reinterpret_cast<uint4*>(out + dir[chunk]);
+    const uint32_t n16 = rec_len[chunk] / 16;
+    for (uint32_t i = lane; i < n16; i += 32) d[i] = s[i];
+  }
+  if (counter != nullptr) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(counter, 1u);
+      if (done == gridDim.x - 1) {
+        __threadfence_system();
+        st_release_sys(flag, flag_value);
+        *counter = 0;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ stream,
+                                                               uint8_t* __restrict__ out,
+                                                               uint64_t n_expected,
+                                                               uint32_t* err) {
+  extern __shared__ uint8_t dsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* lut = dsm + warp * kDecWarpSmem;
+  uint32_t* fc = reinterpret_cast<uint32_t*>(lut + 4096);
+  uint16_t* ring = reinterpret_cast<uint16_t*>(lut + 4096 + 1024);
+  const StreamHeader hd = *reinterpret_cast<const StreamHeader*>(stream);
+  if (hd.magic != kMagic || hd.n_symbols != n_expected || hd.prob_bits != kProbBits) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, ERR_CORRUPT);
+    return;
+  }
+  const uint32_t chunk = blockIdx.x * kDecWarps + warp;
+  if (chunk >= hd.n_chunks) return;
+  const uint64_t* dir = reinterpret_cast<const uint64_t*>(stream + sizeof(StreamHeader));
+  const uint8_t* rec = stream + dir[chunk];
+  const ChunkHeader ch = *reinterpret_cast<const ChunkHeader*>(rec);
+  uint8_t* dst = out + static_cast<uint64_t>(chunk) * hd.chunk_symbols;
+  if (ch.n_sym > hd.chunk_symbols || ch.alphabet > 256) {
+    if (lane == 0) record_error(err, ERR_CORRUPT);
+    return;
+  }
+  const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
+  if (ch.alphabet == 0) {
+    for (uint32_t i = lane; i < ch.n_sym; i += 32) dst[i] = rec[16 + i];
+    return;
+  }
+  const uint32_t A = ch.alphabet;
+  const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
+  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  const uint32_t* states = reinterpret_cast<const uint32_t*>(rec + 16 + fpad);
+  const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
+  const uint32_t total_words = ch.n_pad + ch.n_words;
+  if (lane == 0) {
+    uint32_t cum = 0;
+    for (uint32_t s = 0; s < A; ++s) {
+      const uint32_t f = freq[s];
+      fc[s] = f | (cum << 16);
+      cum += f;
+    }
+    if (cum != kProbScale) record_error(err, ERR_CORRUPT);
+  }
+  __syncwarp();
+  for (uint32_t s = 0; s < A; ++s) {
+    const uint32_t f = fc[s] & 0xFFFFu, c = fc[s] >> 16;
+    for (uint32_t k = lane; k < f; k += 32)
+      if (c + k < kProbScale) lut[c + k] = static_cast<uint8_t>(s);
+  }
+  uint32_t x = states[lane];
+  uint32_t rptr = ch.n_pad, loaded = 0;
+  const uint32_t lt = lanemask_lt();
+  __syncwarp();
+  for (uint32_t ss = 0; ss < n_ss; ++ss) {
+    while (loaded < rptr + 1024 && loaded < total_words) {
+      const uint32_t idx = loaded + lane * 8;
+      if (idx < total_words)
+        *reinterpret_cast<uint4*>(ring + (idx & (kRing - 1))) =
+            *reinterpret_cast<const uint4*>(words + idx);
+      loaded += 256;
+    }
+    __syncwarp();
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int m = 0; m < kSub; ++m) {
+      const uint32_t sl = x & (kProbScale - 1);
+      const uint32_t s = lut[sl];
+      const uint32_t e = fc[s];
+      x = (e & 0xFFFFu) * (x >> kProbBits) + sl - (e >> 16);
+      const bool need = x < kStateLow;
+      const uint32_t mask = __ballot_sync(0xFFFFFFFFu, need);
+      if (need) x = (x << 16) | ring[(rptr + __popc(mask & lt)) & (kRing - 1)];
+      rptr += __popc(mask);
+      o[m >> 2] |= s << ((m & 3) * 8);
+    }
+    const uint32_t off = ss * kSuper + lane * kSub;
+    if (off + kSub <= ch.n_sym) {
+      *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      for (uint32_t i = 0; i < kSub; ++i)
+        if (off + i < ch.n_sym) dst[off + i] = static_cast<uint8_t>(o[i >> 2] >> ((i & 3) * 8));
+    }
+  }
+  if (x != kStateLow || rptr != total_words) record_error(err, ERR_CORRUPT);
+}
+
+}  // namespace rans
+}  // namespace kvs
+
+using namespace kvs;
+using namespace kvs::rans;
+
+extern "C" {
+
+uint64_t kvs_rans_max_bytes(uint64_t n, uint32_t cs) { return max_stream_bytes(n, cs); }
+uint64_t kvs_rans_staging_bytes(uint64_t n, uint32_t cs) {
+  return static_cast<uint64_t>(num_chunks(n, cs)) * slot_bytes(cs);
+}
+
+// Encode n bytes into `out` (capacity kvs_rans_max_bytes).  `sizes` holds
+// 2*n_chunks uint32 (record offsets and lengths).  The stream size is
+// written to *total_out (device).  counter/flag (optional) publish
+// completion to a consumer polling `flag`.
+int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging, uint32_t* sizes,
+                    uint8_t* out, uint64_t* total_out, uint32_t* counter, uint32_t* flag,
+                    uint32_t flag_value, void* stream) {
+  if (n == 0 || cs == 0 || cs % kSuper != 0) return -2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint32_t nc = num_chunks(n, cs);
+  uint32_t* rec_off = sizes;
+  uint32_t* rec_len = sizes + nc;
+  k_rans_encode<<<(nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32, 0, s>>>(in, n, cs, staging,
+                                                                            rec_off, rec_len, nc);
+  k_rans_directory<<<1, 1024, 0, s>>>(rec_len, nc, n, cs, out, total_out);
+  k_rans_copy<<<(nc + 7) / 8, 256, 0, s>>>(staging, rec_off, rec_len, nc, cs, out, counter, flag,
+                                           flag_value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_rans_decode(const uint8_t* stream_buf, uint8_t* out, uint64_t n, uint32_t cs, uint32_t* err,
+                    void* stream) {
+  if (n == 0 || cs == 0) return -2;
+  const uint32_t nc = num_chunks(n, cs);
+  const int smem = kDecWarps * kDecWarpSmem;
+  cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  k_rans_decode<<<(nc + kDecWarps - 1) / kDecWarps, kDecWarps * 32, smem,
+                  static_cast<cudaStream_t>(stream)>>>(stream_buf, out, n, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // extern "C"

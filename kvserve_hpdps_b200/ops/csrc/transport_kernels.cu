@@ -1,0 +1,159 @@
+// Data-movement kernels of the transfer path:
+//  * raw paged-block gather / scatter (compression off), where the gather
+//    destination may be a peer GPU's receive ring (NVLink stores);
+//  * contiguous device-to-device / device-to-peer copies with an optional
+//    release flag published by the last CTA;
+//  * a bounded wait on a ready flag that records ERR_FLAG_TIMEOUT instead of
+//    spinning forever;
+//  * the NVLink bandwidth probe: a timed push of N bytes into a peer buffer,
+//    with start/end taken from %globaltimer on the device (no host clock).
+//
+// Raw transfers use the reference's raw layout per layer,
+// [2, nblocks, block_size, H, D] (kvserve_v1/utils/kv_utils.py:59-80).
+#include "common.cuh"
+#include "kvs_types.h"
+
+namespace kvs {
+
+// Copies `nblocks` blocks of both planes between a paged cache and a
+// contiguous [2, nblocks, block_elems] buffer. dir 0: paged -> flat (gather),
+// dir 1: flat -> paged (scatter).  grid (nblocks, 2), block 256.
+__global__ void __launch_bounds__(256) k_block_copy(PagedKV kv, const int32_t* __restrict__ blocks,
+                                                    int nblocks, long long block_elems,
+                                                    uint8_t* flat, int dir, uint32_t* counter,
+                                                    uint32_t* flag, uint32_t flag_value) {
+  const int b = blockIdx.x, plane = blockIdx.y;
+  const long long bytes = block_elems * 2;
+  uint8_t* paged = const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(kv.base)) +
+                   (static_cast<long long>(blocks[b]) * kv.block_stride + plane * kv.kv_stride) * 2;
+  uint8_t* lin = flat + (static_cast<long long>(plane) * nblocks + b) * bytes;
+  const uint4* s = reinterpret_cast<const uint4*>(dir == 0 ? paged : lin);
+  uint4* d = reinterpret_cast<uint4*>(dir == 0 ? lin : paged);
+  for (long long i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+  if (counter != nullptr) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(counter, 1u);
+      if (done == gridDim.x * gridDim.y - 1) {
+        __threadfence_system();
+        st_release_sys(flag, flag_value);
+        *counter = 0;
+      }
+    }
+  }
+}
+
+// Vectorised copy of `bytes` (multiple of 16) with an optional flag.
+__global__ void __launch_bounds__(256) k_copy16(const uint4* __restrict__ src, uint4* dst,
+                                                long long n16, uint32_t* counter, uint32_t* flag,
+                                                uint32_t flag_value) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+  if (counter != nullptr) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(counter, 1u);
+      if (done == gridDim.x - 1) {
+        __threadfence_system();
+        st_release_sys(flag, flag_value);
+        *counter = 0;
+      }
+    }
+  }
+}
+
+// Wait (bounded) until *flag == expected.  One thread spins; on timeout
+// the error word records ERR_FLAG_TIMEOUT and the kernel returns.
+__global__ void k_wait_flag(const uint32_t* flag, uint32_t expected, uint64_t timeout_ns,
+                            uint32_t* err, uint64_t* waited_ns) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (ld_acquire_sys(flag) == expected) break;
+    if (globaltimer() - t0 > timeout_ns) {
+      record_error(err, ERR_FLAG_TIMEOUT);
+      break;
+    }
+    __nanosleep(200);
+  }
+  if (waited_ns) *waited_ns = globaltimer() - t0;
+}
+
+__global__ void k_set_flag(uint32_t* flag, uint32_t value) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(flag, value);
+  }
+}
+
+// Timed push: every CTA stamps its first/last %globaltimer; the result is
+// [min start, max end] in stamps[0..1] (initialised by the host to
+// (UINT64_MAX, 0)).
+__global__ void __launch_bounds__(512) k_probe_push(const uint4* __restrict__ src, uint4* dst,
+                                                    long long n16, unsigned long long* stamps) {
+  __shared__ unsigned long long t_start;
+  if (threadIdx.x == 0) t_start = globaltimer();
+  __syncthreads();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicMin(&stamps[0], t_start);
+    atomicMax(&stamps[1], static_cast<unsigned long long>(globaltimer()));
+  }
+}
+
+}  // namespace kvs
+
+using namespace kvs;
+
+extern "C" {
+
+int kvs_block_copy(const PagedKV* kv, const int32_t* blocks, int nblocks, long long block_elems,
+                   uint8_t* flat, int dir, uint32_t* counter, uint32_t* flag, uint32_t flag_value,
+                   void* stream) {
+  if (nblocks <= 0) return 0;
+  if ((block_elems * 2) % 16 != 0) return -2;
+  k_block_copy<<<dim3(nblocks, 2), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      *kv, blocks, nblocks, block_elems, flat, dir, counter, flag, flag_value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_copy16(const void* src, void* dst, long long bytes, uint32_t* counter, uint32_t* flag,
+               uint32_t flag_value, int max_blocks, void* stream) {
+  if (bytes % 16 != 0) return -2;
+  const long long n16 = bytes / 16;
+  long long blocks = (n16 + 255) / 256;
+  if (blocks > max_blocks) blocks = max_blocks;
+  if (blocks < 1) blocks = 1;
+  k_copy16<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n16, counter, flag, flag_value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_wait_flag(const uint32_t* flag, uint32_t expected, uint64_t timeout_ns, uint32_t* err,
+                  uint64_t* waited_ns, void* stream) {
+  k_wait_flag<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag, expected, timeout_ns, err,
+                                                               waited_ns);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_set_flag(uint32_t* flag, uint32_t value, void* stream) {
+  k_set_flag<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag, value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_probe_push(const void* src, void* dst, long long bytes, unsigned long long* stamps,
+                   int blocks, void* stream) {
+  if (bytes % 16 != 0) return -2;
+  k_probe_push<<<blocks, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), bytes / 16, stamps);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // extern "C"

@@ -1,0 +1,586 @@
+"""Python entry points of the native kernels (torch tensors in, tensors out).
+
+Three groups:
+
+* fused layer ops (:func:`quantize_layer`, :func:`dequantize_layer`): the
+  producer's Hadamard + hybrid quantization of every request of one layer,
+  read straight from the paged KV cache through a block table, and the
+  consumer's dequantization + inverse transform + scatter into its own paged
+  cache;
+* the lossless codec (:func:`rans_encode`, :func:`rans_decode`,
+  :func:`bitpack`, :func:`bitunpack`), on CUDA or CPU tensors with the same
+  byte format;
+* transfer helpers (block gather/scatter, copies with a release flag,
+  bounded flag waits, the NVLink probe) and error metrics.
+
+All device ops run on the current CUDA stream and never synchronise the
+host, except where a function documents that it returns a host value.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import threading
+from dataclasses import dataclass, field
+from functools import lru_cache
+from typing import Optional, Sequence
+
+import torch
+
+from kvserve_hpdps_b200.compression.signs import hadamard_matrix, rademacher_signs
+from kvserve_hpdps_b200.ops import _lib
+from kvserve_hpdps_b200.ops._lib import LayerLaunch, PagedKV, check, lib
+
+HEAD_DIM = 128
+TILE_ROWS = 128
+RANS_CHUNK = 32768
+ENGINE_TCGEN05 = 0
+ENGINE_SIMT = 1
+
+ERR_NAMES = {0: "none", 1: "mbarrier timeout", 2: "ready-flag timeout", 3: "bounds",
+             4: "corrupt stream", 5: "overflow"}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+# ----------------------------------------------------------------- workspace
+class _Workspace:
+    """Per-device scratch reused across launches (grown on demand)."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.err = torch.zeros(4, dtype=torch.int32, device=device)
+        self.counters = torch.zeros(64, dtype=torch.int32, device=device)
+        self._bufs: dict[str, torch.Tensor] = {}
+        self._lock = threading.Lock()
+
+    def buf(self, name: str, nbytes: int, dtype=torch.uint8) -> torch.Tensor:
+        esz = torch.empty((), dtype=dtype).element_size()
+        n = max(1, (nbytes + esz - 1) // esz)
+        with self._lock:
+            t = self._bufs.get(name)
+            if t is None or t.numel() < n:
+                t = torch.empty(int(n * 1.25) + 16, dtype=dtype, device=self.device)
+                self._bufs[name] = t
+        return t[:n]
+
+
+_ws: dict[tuple, _Workspace] = {}
+_ws_lock = threading.Lock()
+
+
+def workspace(device: torch.device) -> _Workspace:
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    with _ws_lock:
+        if key not in _ws:
+            _ws[key] = _Workspace(torch.device("cuda", key[1]))
+        return _ws[key]
+
+
+def read_device_error(device: torch.device, reset: bool = True) -> int:
+    """Host read (synchronising) of the device error word; 0 = no error."""
+    ws = workspace(device)
+    code = int(ws.err[0].item())
+    if reset and code:
+        ws.err.zero_()
+    return code
+
+
+def check_device_error(device: torch.device, what: str = "kernel") -> None:
+    code = read_device_error(device)
+    if code:
+        raise RuntimeError(f"{what}: device error {code} ({ERR_NAMES.get(code, '?')})")
+
+
+# ---------------------------------------------------------- transform images
+def _sw128_offsets() -> torch.Tensor:
+    """Byte offset of element (a, b) of a 128x128 bf16 matrix in the K-major
+    128-byte-swizzled UMMA layout (two 16 KB halves, b = reduction index)."""
+    a = torch.arange(128).view(128, 1).expand(128, 128)
+    b = torch.arange(128).view(1, 128).expand(128, 128)
+    hb = b // 64
+    byte = (b % 64) * 2
+    chunk = (byte // 16) ^ (a % 8)
+    return hb * 16384 + (a // 8) * 1024 + (a % 8) * 128 + chunk * 16 + byte % 16
+
+
+@lru_cache(maxsize=1)
+def _offsets_cached() -> torch.Tensor:
+    return _sw128_offsets()
+
+
+def swizzle_image(mat: torch.Tensor) -> torch.Tensor:
+    """uint8[32768] image of a 128x128 matrix (bf16) in the SW128 K-major layout."""
+    bf = mat.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32) & 0xFFFF
+    img = torch.zeros(32768, dtype=torch.uint8)
+    off = _offsets_cached().flatten()
+    img[off] = (bf.flatten() & 0xFF).to(torch.uint8)
+    img[off + 1] = (bf.flatten() >> 8).to(torch.uint8)
+    return img
+
+
+def transform_images(signs: Optional[torch.Tensor], num_heads: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Forward and inverse operand images, uint8 [H*32768] each.
+
+    Forward: Bf[a][b] = s[b] H[a][b] (consumes the signed input).
+    Inverse: Bi[a][b] = s[a] H[a][b] (signs on the output channel).
+    ``signs=None`` gives identity images (no transform).
+    """
+    H = hadamard_matrix(HEAD_DIM)
+    fwd, inv = [], []
+    for h in range(num_heads):
+        if signs is None:
+            eye = torch.eye(HEAD_DIM)
+            fwd.append(swizzle_image(eye))
+            inv.append(swizzle_image(eye))
+        else:
+            s = signs[h].to(torch.float32)
+            fwd.append(swizzle_image(H * s.view(1, -1)))
+            inv.append(swizzle_image(H * s.view(-1, 1)))
+    return torch.cat(fwd), torch.cat(inv)
+
+
+def sign_bits(signs: Optional[torch.Tensor], num_heads: int) -> list[list[int]]:
+    out = []
+    for h in range(num_heads):
+        words = [0, 0, 0, 0]
+        if signs is not None:
+            for d in range(HEAD_DIM):
+                if float(signs[h, d]) < 0:
+                    words[d >> 5] |= 1 << (d & 31)
+        out.append(words)
+    return out
+
+
+# --------------------------------------------------------------- layer plan
+def code_bits(levels: float, packed: bool) -> int:
+    """Bits per code: 8 for byte codes, ceil(log2(levels)) when bit-packed."""
+    if not packed:
+        return 8
+    return max(1, min(8, math.ceil(math.log2(max(2.0, float(levels))))))
+
+
+@dataclass
+class LayerPlan:
+    """Quantization description of one layer on one rank."""
+    num_heads: int
+    key_levels: list[float]
+    value_levels: list[float]
+    signs: Optional[torch.Tensor]            # [H, 128] +-1, or None (identity)
+    packed: bool = False                     # fixed-width bit packing of codes
+    clamp_top: bool = True
+    group_of_head: list[int] = field(default_factory=list)
+    groups: list[list[int]] = field(default_factory=list)
+    key_bits: list[int] = field(default_factory=list)
+    value_bits: list[int] = field(default_factory=list)
+    seg_prefix: list[int] = field(default_factory=list)
+    _images: dict = field(default_factory=dict)
+    _params: Optional[_lib.LayerParams] = None
+
+    def __post_init__(self):
+        H = self.num_heads
+        if H > _lib.MAX_HEADS:
+            raise ValueError(f"at most {_lib.MAX_HEADS} KV heads per rank, got {H}")
+        gid: dict[float, int] = {}
+        self.group_of_head, self.groups = [], []
+        for h, v in enumerate(self.value_levels):
+            v = float(v)
+            if v not in gid:
+                gid[v] = len(gid)
+                self.groups.append([])
+            self.group_of_head.append(gid[v])
+            self.groups[gid[v]].append(h)
+        self.key_bits = [code_bits(v, self.packed) for v in self.key_levels]
+        self.value_bits = [code_bits(v, self.packed) for v in self.value_levels]
+        pref = [0]
+        for b in self.key_bits + self.value_bits:
+            pref.append(pref[-1] + 16 * b)
+        self.seg_prefix = pref
+
+    @property
+    def n_groups(self) -> int:
+        return len(self.groups)
+
+    def row_bytes(self) -> int:
+        """Code bytes per token row over every (kv, head) segment."""
+        return self.seg_prefix[-1]
+
+    def meta_bytes(self, rows: int) -> int:
+        return 2 * (2 * self.num_heads * HEAD_DIM + 2 * self.n_groups * rows)
+
+    def images(self, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+        key = str(device)
+        if key not in self._images:
+            f, i = transform_images(self.signs, self.num_heads)
+            self._images[key] = (f.to(device), i.to(device))
+        return self._images[key]
+
+    def params(self) -> _lib.LayerParams:
+        if self._params is None:
+            p = _lib.LayerParams()
+            H = self.num_heads
+            p.H = H
+            p.n_groups = self.n_groups
+            for h in range(H):
+                p.key_levels[h] = float(self.key_levels[h])
+                p.value_levels[h] = float(self.value_levels[h])
+                p.key_bits[h] = self.key_bits[h]
+                p.value_bits[h] = self.value_bits[h]
+                p.group_of_head[h] = self.group_of_head[h]
+            for i, v in enumerate(self.seg_prefix):
+                p.seg_prefix[i] = v
+            for h, words in enumerate(sign_bits(self.signs, H)):
+                for j in range(4):
+                    p.sign_bits[h][j] = words[j]
+            p.clamp_top = 1 if self.clamp_top else 0
+            p.transform = 1 if self.signs is not None else 0
+            p.out_scale = 1.0 / math.sqrt(HEAD_DIM) if self.signs is not None else 1.0
+            self._params = p
+        return self._params
+
+
+def make_layer_plan(num_heads: int, key_levels, value_levels, seed: Optional[int], layer_id: int,
+                    packed: bool = False, clamp_top: bool = True) -> LayerPlan:
+    signs = None if seed is None else rademacher_signs(layer_id, num_heads, HEAD_DIM, seed)
+    return LayerPlan(num_heads, [float(x) for x in key_levels], [float(x) for x in value_levels],
+                     signs, packed=packed, clamp_top=clamp_top)
+
+
+# ------------------------------------------------------------ request batch
+def _align16(x: int) -> int:
+    return (x + 15) & ~15
+
+
+class RequestBatch:
+    """Block tables and per-request layout of one layer launch.
+
+    ``block_ids[r]`` are the request's physical blocks in the paged cache,
+    ``n_tokens[r]`` its valid tokens (statistics use only these; rows past
+    them in the last block are zero-coded).  Region offsets depend on the
+    plan (bits per segment), so they are computed per plan.
+    """
+
+    def __init__(self, block_ids: Sequence[Sequence[int]], n_tokens: Sequence[int],
+                 block_size: int, device: torch.device):
+        self.block_ids = [list(map(int, b)) for b in block_ids]
+        self.n_tokens = [int(n) for n in n_tokens]
+        self.block_size = int(block_size)
+        self.device = device
+        self.n_rows = [len(b) * self.block_size for b in self.block_ids]
+        self.tiles = [(r + TILE_ROWS - 1) // TILE_ROWS for r in self.n_rows]
+        self.total_tiles = sum(self.tiles)
+        R = len(self.block_ids)
+        bt, off = [], []
+        for b in self.block_ids:
+            off.append(len(bt))
+            bt.extend(b)
+        prefix = [0]
+        for t in self.tiles:
+            prefix.append(prefix[-1] + t)
+        ints = bt + off + self.n_tokens + self.n_rows + prefix
+        host = torch.tensor(ints if ints else [0], dtype=torch.int32)
+        if device.type == "cuda":
+            host = host.pin_memory()
+        self._ints = host.to(device, non_blocking=True)
+        self._o_bt, self._o_off = 0, len(bt)
+        self._o_ntok = self._o_off + R
+        self._o_rows = self._o_ntok + R
+        self._o_prefix = self._o_rows + R
+        self._layouts: dict[tuple, tuple] = {}
+
+    @property
+    def num_req(self) -> int:
+        return len(self.block_ids)
+
+    def layout(self, plan: LayerPlan) -> tuple[list[int], list[int], int, int, torch.Tensor]:
+        """(code_off, meta_off, code_bytes, meta_bytes, device int64 offsets)."""
+        key = (plan.row_bytes(), plan.n_groups, plan.num_heads)
+        if key not in self._layouts:
+            code_off, meta_off = [], []
+            c = m = 0
+            for rows in self.n_rows:
+                code_off.append(c)
+                meta_off.append(m)
+                c += _align16(rows * plan.row_bytes())
+                m += _align16(plan.meta_bytes(rows))
+            host = torch.tensor(code_off + meta_off, dtype=torch.int64)
+            if self.device.type == "cuda":
+                host = host.pin_memory()
+            self._layouts[key] = (code_off, meta_off, c, m, host.to(self.device, non_blocking=True))
+        return self._layouts[key]
+
+    def req_table(self, plan: LayerPlan) -> _lib.ReqTable:
+        _, _, _, _, offs = self.layout(plan)
+        base = self._ints.data_ptr()
+        rt = _lib.ReqTable()
+        rt.block_table = base + 4 * self._o_bt
+        rt.bt_off = base + 4 * self._o_off
+        rt.n_tokens = base + 4 * self._o_ntok
+        rt.n_rows = base + 4 * self._o_rows
+        rt.tile_prefix = base + 4 * self._o_prefix
+        rt.code_off = offs.data_ptr()
+        rt.meta_off = offs.data_ptr() + 8 * self.num_req
+        rt.num_req = self.num_req
+        return rt
+
+    def block_tensor(self) -> torch.Tensor:
+        return self._ints[self._o_bt:self._o_off]
+
+
+def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
+    """Describe a paged KV layer tensor for the kernels.
+
+    Accepts [2, nb, bs, H, D] (FlashAttention / NHD) and [nb, 2, bs, H, D]
+    (FlashInfer) bf16 tensors with contiguous (bs, H, D) inner dims.
+    """
+    if kv_layer.dtype != torch.bfloat16:
+        raise TypeError(f"KV cache must be bf16, got {kv_layer.dtype}")
+    if kv_layer.dim() != 5 or kv_layer.shape[-1] != HEAD_DIM:
+        raise ValueError(f"expected a [2, nb, bs, H, {HEAD_DIM}] layer, got {tuple(kv_layer.shape)}")
+    st = kv_layer.stride()
+    H, D = kv_layer.shape[3], kv_layer.shape[4]
+    if st[4] != 1 or st[3] != D or st[2] != H * D:
+        raise ValueError("KV layer inner dims (bs, H, D) must be contiguous")
+    p = PagedKV()
+    p.base = kv_layer.data_ptr()
+    if kv_layer.shape[0] == 2 and kv_layer.shape[1] != 2:
+        p.kv_stride, p.block_stride = st[0], st[1]
+        p.num_blocks = kv_layer.shape[1]
+    elif kv_layer.shape[1] == 2:
+        p.block_stride, p.kv_stride = st[0], st[1]
+        p.num_blocks = kv_layer.shape[0]
+    else:  # shape[0] == shape[1] == 2: treat as FlashAttention layout
+        p.kv_stride, p.block_stride = st[0], st[1]
+        p.num_blocks = kv_layer.shape[1]
+    p.block_size = kv_layer.shape[2]
+    return p
+
+
+# ---------------------------------------------------------------- fused ops
+def _launch(kv_layer, batch, plan, bmat, codes, meta, kstat, engine) -> LayerLaunch:
+    dev = kv_layer.device
+    L = LayerLaunch()
+    L.kv = paged_kv(kv_layer)
+    L.rt = batch.req_table(plan)
+    L.lp = plan.params()
+    L.bmat = bmat.data_ptr()
+    L.codes = codes.data_ptr()
+    L.meta = meta.data_ptr()
+    L.kstat = 0 if kstat is None else kstat.data_ptr()
+    L.err = workspace(dev).err.data_ptr()
+    L.total_tiles = batch.total_tiles
+    L.engine = engine
+    L.stream = _stream(dev)
+    return L
+
+
+def quantize_layer(kv_layer: torch.Tensor, batch: RequestBatch, plan: LayerPlan,
+                   codes: Optional[torch.Tensor] = None, meta: Optional[torch.Tensor] = None,
+                   engine: int = ENGINE_TCGEN05) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantize every request of one layer; returns (codes u8, meta u8).
+
+    ``codes`` holds, per request at ``batch.layout(plan)[0][r]``, the
+    segments ``[kv][head][row][16*bits]``; ``meta`` holds per request the
+    fp16 arrays ``kmin[H,128] kscale[H,128] vmin[G,rows] vscale[G,rows]``.
+    """
+    dev = kv_layer.device
+    _, _, cbytes, mbytes, _ = batch.layout(plan)
+    ws = workspace(dev)
+    if codes is None:
+        codes = torch.empty(max(cbytes, 16), dtype=torch.uint8, device=dev)
+    if meta is None:
+        meta = torch.empty(max(mbytes, 16), dtype=torch.uint8, device=dev)
+    n_pairs = batch.num_req * plan.num_heads * HEAD_DIM
+    kstat = ws.buf("kstat", 8 * n_pairs, torch.int32)
+    fwd, _ = plan.images(dev)
+    L = _launch(kv_layer, batch, plan, fwd, codes, meta, kstat, engine)
+    lb = lib()
+    check(lb.kvs_init_key_stats(kstat.data_ptr(), n_pairs, L.stream), "init_key_stats")
+    check(lb.kvs_key_stats(ctypes.byref(L)), "key_stats")
+    check(lb.kvs_quant_k(ctypes.byref(L)), "quant_k")
+    check(lb.kvs_quant_v(ctypes.byref(L)), "quant_v")
+    return codes, meta
+
+
+def dequantize_layer(codes: torch.Tensor, meta: torch.Tensor, dst_layer: torch.Tensor,
+                     batch: RequestBatch, plan: LayerPlan, engine: int = ENGINE_TCGEN05) -> None:
+    """Dequantize + inverse transform every request of one layer into the
+    paged destination ``dst_layer`` at ``batch``'s block ids."""
+    dev = dst_layer.device
+    _, inv = plan.images(dev)
+    L = _launch(dst_layer, batch, plan, inv, codes, meta, None, engine)
+    check(lib().kvs_dequant_inverse(ctypes.byref(L)), "dequant_inverse")
+
+
+# ------------------------------------------------------------------- codec
+def rans_max_bytes(n: int, chunk: int = RANS_CHUNK) -> int:
+    return int(lib().kvs_rans_max_bytes(n, chunk))
+
+
+def rans_encode(data: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: int = RANS_CHUNK,
+                flag: Optional[torch.Tensor] = None, flag_value: int = 0,
+                trim: bool = True) -> torch.Tensor:
+    """Entropy-code the bytes of ``data``.
+
+    CUDA: returns the stream buffer; with ``trim`` (default) the host reads
+    the stream size (one synchronisation) and the result is trimmed to it,
+    otherwise the full worst-case buffer is returned (the size is in the
+    stream header).  CPU: always exact size.
+    """
+    src = data.contiguous().view(torch.uint8).reshape(-1)
+    n = src.numel()
+    lb = lib()
+    if src.device.type == "cpu":
+        cap = int(lb.kvs_cpu_rans_max_bytes(n, chunk))
+        buf = torch.empty(cap, dtype=torch.uint8)
+        size = int(lb.kvs_cpu_rans_encode(src.data_ptr(), n, chunk, buf.data_ptr(), cap))
+        if size == 0:
+            raise RuntimeError("CPU rANS encode failed")
+        return buf[:size].clone()
+    dev = src.device
+    ws = workspace(dev)
+    cap = int(lb.kvs_rans_max_bytes(n, chunk))
+    if out is None:
+        out = torch.empty(cap, dtype=torch.uint8, device=dev)
+    elif out.numel() < cap:
+        raise ValueError(f"output buffer too small ({out.numel()} < {cap})")
+    nchunks = (n + chunk - 1) // chunk
+    staging = ws.buf("rans_staging", int(lb.kvs_rans_staging_bytes(n, chunk)))
+    sizes = ws.buf("rans_sizes", 8 * nchunks, torch.int32)
+    total = ws.buf("rans_total", 8, torch.int64)
+    counter = ws.counters[0:1] if flag is not None else None
+    check(lb.kvs_rans_encode(src.data_ptr(), n, chunk, staging.data_ptr(), sizes.data_ptr(),
+                             out.data_ptr(), total.data_ptr(), _ptr(counter), _ptr(flag),
+                             flag_value, _stream(dev)), "rans_encode")
+    if trim:
+        return out[:int(total[0].item())]
+    return out
+
+
+def rans_stream_size(stream: torch.Tensor) -> int:
+    """Total bytes of a stream from its header (host read)."""
+    hdr = stream[:32].cpu().numpy().view("<u8")
+    return int(hdr[3])
+
+
+def rans_decode(stream: torch.Tensor, n: int, out: Optional[torch.Tensor] = None,
+                chunk: int = RANS_CHUNK) -> torch.Tensor:
+    """Decode ``n`` bytes (uint8 tensor on the stream's device)."""
+    lb = lib()
+    if stream.device.type == "cpu":
+        s = stream.contiguous()
+        res = torch.empty(n, dtype=torch.uint8) if out is None else out
+        rc = lb.kvs_cpu_rans_decode(s.data_ptr(), s.numel(), res.data_ptr(), n)
+        if rc != 0:
+            raise RuntimeError(f"CPU rANS decode failed ({rc})")
+        return res
+    dev = stream.device
+    res = torch.empty(n, dtype=torch.uint8, device=dev) if out is None else out
+    check(lb.kvs_rans_decode(stream.data_ptr(), res.data_ptr(), n, chunk,
+                             workspace(dev).err.data_ptr(), _stream(dev)), "rans_decode")
+    return res
+
+
+def bitpack(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """Pack rows of 128 codes to ``bits`` bits each (CPU reference of the
+    device layout): [rows, 128] u8 -> [rows, 16*bits] u8."""
+    c = codes.contiguous().to("cpu").view(-1, HEAD_DIM)
+    out = torch.empty((c.shape[0], 16 * bits), dtype=torch.uint8)
+    lib().kvs_cpu_bitpack(c.data_ptr(), c.shape[0], bits, out.data_ptr())
+    return out
+
+
+def bitunpack(packed: torch.Tensor, bits: int) -> torch.Tensor:
+    p = packed.contiguous().to("cpu").view(-1, 16 * bits)
+    out = torch.empty((p.shape[0], HEAD_DIM), dtype=torch.uint8)
+    lib().kvs_cpu_bitunpack(p.data_ptr(), p.shape[0], bits, out.data_ptr())
+    return out
+
+
+# ------------------------------------------------------------ data movement
+def block_copy(kv_layer: torch.Tensor, blocks: torch.Tensor, flat_ptr: int, gather: bool,
+               flag: Optional[torch.Tensor] = None, flag_value: int = 0) -> None:
+    """Gather (paged -> flat) or scatter (flat -> paged) whole blocks of both
+    planes.  ``flat_ptr`` may point into a peer GPU's memory."""
+    p = paged_kv(kv_layer)
+    nb = blocks.numel()
+    block_elems = kv_layer.shape[2] * kv_layer.shape[3] * kv_layer.shape[4]
+    ws = workspace(kv_layer.device)
+    counter = ws.counters[1:2] if flag is not None else None
+    check(lib().kvs_block_copy(ctypes.byref(p), blocks.data_ptr(), nb, block_elems, flat_ptr,
+                               0 if gather else 1, _ptr(counter), _ptr(flag), flag_value,
+                               _stream(kv_layer.device)), "block_copy")
+
+
+def copy_bytes(src_ptr: int, dst_ptr: int, nbytes: int, device: torch.device,
+               flag_ptr: Optional[int] = None, flag_value: int = 0, max_blocks: int = 592) -> None:
+    """Vectorised copy (16-byte multiple) on ``device``'s current stream."""
+    ws = workspace(device)
+    counter = ws.counters[2:3].data_ptr() if flag_ptr is not None else None
+    check(lib().kvs_copy16(src_ptr, dst_ptr, nbytes, counter, flag_ptr, flag_value, max_blocks,
+                           _stream(device)), "copy16")
+
+
+def wait_flag(flag_ptr: int, expected: int, device: torch.device, timeout_s: float = 2.0,
+              waited_ns: Optional[torch.Tensor] = None) -> None:
+    """Launch a bounded device wait until *flag == expected (ERR_FLAG_TIMEOUT
+    in the device error word when it expires)."""
+    check(lib().kvs_wait_flag(flag_ptr, expected, int(timeout_s * 1e9),
+                              workspace(device).err.data_ptr(), _ptr(waited_ns),
+                              _stream(device)), "wait_flag")
+
+
+def set_flag(flag_ptr: int, value: int, device: torch.device) -> None:
+    check(lib().kvs_set_flag(flag_ptr, value, _stream(device)), "set_flag")
+
+
+def probe_push(src: torch.Tensor, dst_ptr: int, nbytes: int, stamps: torch.Tensor,
+               blocks: int = 296) -> None:
+    """Timed push of ``nbytes`` from ``src`` to ``dst_ptr`` (peer memory);
+    ``stamps`` (int64[2], reset by the caller to (max, 0)) receives the
+    [first start, last end] globaltimer stamps in ns."""
+    check(lib().kvs_probe_push(src.data_ptr(), dst_ptr, nbytes, stamps.data_ptr(), blocks,
+                               _stream(src.device)), "probe_push")
+
+
+# ----------------------------------------------------------------- metrics
+def kv_error(ref: torch.Tensor, approx: torch.Tensor) -> dict:
+    """rel-MSE, MSE, cosine and max |a-r| between two bf16 tensors of the
+    same size, from one fused device reduction (one host read)."""
+    if ref.numel() != approx.numel():
+        raise ValueError("size mismatch")
+    r = ref.contiguous().view(-1)
+    a = approx.contiguous().view(-1)
+    if r.device.type != "cuda":
+        from kvserve_hpdps_b200.compression.oracle import error_metrics
+        return error_metrics(r, a)
+    acc = torch.zeros(4, dtype=torch.float64, device=r.device)
+    mx = torch.zeros(1, dtype=torch.int32, device=r.device)
+    check(lib().kvs_kv_error(r.data_ptr(), a.data_ptr(), r.numel(), acc.data_ptr(),
+                             mx.data_ptr(), _stream(r.device)), "kv_error")
+    sd, sr, sa, sx = acc.tolist()
+    maxabs = float(mx.view(torch.float32).item())
+    n = r.numel()
+    return {"rel_mse": sd / max(sr, 1e-300), "mse": sd / max(n, 1),
+            "cosine": sx / max(math.sqrt(sr * sa), 1e-300), "max_abs": maxabs}
+
+
+def logit_agreement(ref_logits: torch.Tensor, approx_logits: torch.Tensor) -> dict:
+    """Top-1 agreement and mean KL(ref || approx) of two [rows, vocab] fp32
+    logit matrices (one device pass, one host read)."""
+    r = ref_logits.float().contiguous()
+    a = approx_logits.float().contiguous()
+    rows, vocab = r.shape
+    out = torch.empty((rows, 3), dtype=torch.float32, device=r.device)
+    check(lib().kvs_logit_agreement(r.data_ptr(), a.data_ptr(), rows, vocab, out.data_ptr(),
+                                    _stream(r.device)), "logit_agreement")
+    o = out.cpu()
+    agree = float((o[:, 0] == o[:, 1]).float().mean())
+    return {"top1_agreement": agree, "kl_mean": float(o[:, 2].mean()), "rows": rows}

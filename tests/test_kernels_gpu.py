@@ -1,0 +1,256 @@
+"""Numerics of the sm_100a kernels against the float32 CPU oracle.
+
+Every test here needs a CUDA device.  Both transform engines are checked:
+engine 0 (TMA + tcgen05.mma) and engine 1 (SIMT butterfly).  Codes may
+differ from the oracle by one step where the transform's summation order
+moves a value across a rounding boundary; the tests bound how often.
+"""
+
+import pytest
+import torch
+
+from kvserve_hpdps_b200.compression import oracle
+from kvserve_hpdps_b200.models.synthetic import gather_request, paged_workload
+from kvserve_hpdps_b200.ops import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+ENGINES = [K.ENGINE_TCGEN05, K.ENGINE_SIMT]
+
+
+def _plan(H, layer_id=5, packed=False, seed=0x3333):
+    kl = [12.0 if h % 2 == 0 else 6.0 for h in range(H)]
+    vl = [8.0 if h % 3 == 0 else 4.0 for h in range(H)]
+    return K.make_layer_plan(H, kl, vl, seed, layer_id, packed=packed)
+
+
+def _segments(codes, batch, plan, r):
+    """[2, H, rows, 128] uint8 codes of request r (unpacked, CPU)."""
+    c = codes.cpu()
+    code_off = batch.layout(plan)[0][r]
+    rows = batch.n_rows[r]
+    H = plan.num_heads
+    out = torch.empty((2, H, rows, 128), dtype=torch.uint8)
+    for kv in range(2):
+        for h in range(H):
+            s = kv * H + h
+            bits = (plan.key_bits if kv == 0 else plan.value_bits)[h]
+            start = code_off + rows * plan.seg_prefix[s]
+            seg = c[start:start + rows * 16 * bits]
+            out[kv, h] = seg.view(rows, 128) if bits == 8 else K.bitunpack(seg, bits)
+    return out
+
+
+def _meta(meta, batch, plan, r):
+    m = meta.cpu()
+    off = batch.layout(plan)[1][r]
+    rows, H, G = batch.n_rows[r], plan.num_heads, plan.n_groups
+    f = m[off:off + plan.meta_bytes(rows)].view(torch.float16)
+    kmin = f[:H * 128].view(H, 128)
+    ksc = f[H * 128:2 * H * 128].view(H, 128)
+    vmin = f[2 * H * 128:2 * H * 128 + G * rows].view(G, rows)
+    vsc = f[2 * H * 128 + G * rows:].view(G, rows)
+    return kmin, ksc, vmin, vsc
+
+
+def _check_codes(got, exp, max_frac=2e-3):
+    d = (got.to(torch.int16) - exp.to(torch.int16)).abs()
+    assert int(d.max()) <= 1, f"code mismatch larger than one step: {int(d.max())}"
+    frac = float((d != 0).float().mean())
+    assert frac <= max_frac, f"too many code mismatches: {frac:.2e}"
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+@pytest.mark.parametrize("H", [1, 2, 4, 8])
+@pytest.mark.parametrize("packed", [False, True])
+def test_quantize_matches_oracle(engine, H, packed):
+    tokens = [300, 128, 37]
+    wl = paged_workload(1, tokens, H, block_size=16, device="cuda", seed=H + 10 * packed)
+    layer = wl.cache[0]
+    plan = _plan(H, packed=packed)
+    batch = K.RequestBatch(wl.block_ids, wl.n_tokens, 16, layer.device)
+    codes, meta = K.quantize_layer(layer, batch, plan, engine=engine)
+    torch.cuda.synchronize()
+    K.check_device_error(layer.device)
+    for r, t in enumerate(tokens):
+        dense = gather_request(layer, wl.block_ids[r]).cpu()
+        ref = oracle.compress_layer(dense, torch.tensor(plan.key_levels),
+                                    torch.tensor(plan.value_levels), plan.signs, n_valid=t)
+        rows = batch.n_rows[r]
+        got = _segments(codes, batch, plan, r)
+        exp = ref["codes"].reshape(2, H, rows, 128)
+        _check_codes(got, exp)
+        kmin, ksc, vmin, vsc = _meta(meta, batch, plan, r)
+        torch.testing.assert_close(kmin.float(), ref["key_min"].half().float(), rtol=2e-3, atol=2e-3)
+        torch.testing.assert_close(ksc.float(), ref["key_scale"].half().float(), rtol=2e-3, atol=1e-5)
+        torch.testing.assert_close(vmin.float()[:, :t], ref["value_min"].half().float()[:, :t],
+                                   rtol=2e-3, atol=2e-3)
+        torch.testing.assert_close(vsc.float()[:, :t], ref["value_scale"].half().float()[:, :t],
+                                   rtol=2e-3, atol=1e-5)
+
+
+def _oracle_buffers(dense_list, plan, batch, tokens):
+    """Codes/meta buffers in the device layout built from the oracle."""
+    _, _, cbytes, mbytes, _ = batch.layout(plan)
+    codes = torch.zeros(cbytes, dtype=torch.uint8)
+    meta = torch.zeros(mbytes, dtype=torch.uint8)
+    refs = []
+    H = plan.num_heads
+    for r, dense in enumerate(dense_list):
+        ref = oracle.compress_layer(dense, torch.tensor(plan.key_levels),
+                                    torch.tensor(plan.value_levels), plan.signs, n_valid=tokens[r])
+        refs.append(ref)
+        rows = batch.n_rows[r]
+        off = batch.layout(plan)[0][r]
+        cr = ref["codes"].reshape(2, H, rows, 128)
+        for kv in range(2):
+            for h in range(H):
+                bits = (plan.key_bits if kv == 0 else plan.value_bits)[h]
+                start = off + rows * plan.seg_prefix[kv * H + h]
+                seg = cr[kv, h].contiguous().view(-1) if bits == 8 else K.bitpack(cr[kv, h], bits).view(-1)
+                codes[start:start + seg.numel()] = seg
+        moff = batch.layout(plan)[1][r]
+        f = torch.cat([ref["key_min"].half().flatten(), ref["key_scale"].half().flatten(),
+                       ref["value_min"].half().flatten(), ref["value_scale"].half().flatten()])
+        meta[moff:moff + f.numel() * 2] = f.view(torch.uint8)
+    return codes, meta, refs
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+@pytest.mark.parametrize("H", [2, 4, 8])
+@pytest.mark.parametrize("packed", [False, True])
+def test_dequantize_matches_oracle(engine, H, packed):
+    tokens = [260, 64]
+    wl = paged_workload(1, tokens, H, block_size=16, device="cuda", seed=3 * H)
+    layer = wl.cache[0]
+    plan = _plan(H, layer_id=2, packed=packed)
+    dense = [gather_request(layer, b).cpu() for b in wl.block_ids]
+    dst = paged_workload(1, tokens, H, block_size=16, device="cuda", seed=99, fill=False,
+                         extra_blocks=5)
+    batch = K.RequestBatch(dst.block_ids, tokens, 16, layer.device)
+    codes, meta, refs = _oracle_buffers(dense, plan, batch, tokens)
+    K.dequantize_layer(codes.cuda(), meta.cuda(), dst.cache[0], batch, plan, engine=engine)
+    torch.cuda.synchronize()
+    K.check_device_error(layer.device)
+    for r, t in enumerate(tokens):
+        ref = refs[r]
+        exp = oracle.decompress_layer(ref["codes"], ref["key_min"], ref["key_scale"],
+                                      ref["value_min"], ref["value_scale"], ref["groups"],
+                                      plan.signs)
+        got = gather_request(dst.cache[0], dst.block_ids[r]).cpu()
+        nb = len(dst.block_ids[r])
+        g = got.view(2, nb * 16, H, 128)[:, :t].float()
+        e = exp.view(2, nb * 16, H, 128)[:, :t].float()
+        torch.testing.assert_close(g, e, rtol=1.6e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+def test_round_trip_error_close_to_oracle(engine):
+    H, tokens = 4, [1024, 333]
+    wl = paged_workload(1, tokens, H, block_size=16, device="cuda", seed=5)
+    layer = wl.cache[0]
+    plan = _plan(H, layer_id=7)
+    batch = K.RequestBatch(wl.block_ids, tokens, 16, layer.device)
+    codes, meta = K.quantize_layer(layer, batch, plan, engine=engine)
+    dst = torch.zeros_like(layer)
+    K.dequantize_layer(codes, meta, dst, batch, plan, engine=engine)
+    torch.cuda.synchronize()
+    K.check_device_error(layer.device)
+    for r, t in enumerate(tokens):
+        src = gather_request(layer, wl.block_ids[r])
+        rec = gather_request(dst, wl.block_ids[r])
+        nb = len(wl.block_ids[r])
+        s = src.view(2, nb * 16, H, 128)[:, :t]
+        g = rec.view(2, nb * 16, H, 128)[:, :t]
+        got = K.kv_error(s, g)
+        ref = oracle.compress_layer(src.cpu(), torch.tensor(plan.key_levels),
+                                    torch.tensor(plan.value_levels), plan.signs, n_valid=t)
+        exp_rec = oracle.decompress_layer(ref["codes"], ref["key_min"], ref["key_scale"],
+                                          ref["value_min"], ref["value_scale"], ref["groups"],
+                                          plan.signs)
+        exp = oracle.error_metrics(s.cpu(), exp_rec.view(2, nb * 16, H, 128)[:, :t])
+        assert abs(got["cosine"] - exp["cosine"]) < 2e-3
+        assert abs(got["rel_mse"] - exp["rel_mse"]) < 2e-2 * max(exp["rel_mse"], 1e-6) + 1e-4
+
+
+def test_engines_agree():
+    H, tokens = 4, [512]
+    wl = paged_workload(1, tokens, H, device="cuda", seed=11)
+    plan = _plan(H)
+    batch = K.RequestBatch(wl.block_ids, tokens, 16, wl.cache.device)
+    c0, m0 = K.quantize_layer(wl.cache[0], batch, plan, engine=K.ENGINE_TCGEN05)
+    c1, m1 = K.quantize_layer(wl.cache[0], batch, plan, engine=K.ENGINE_SIMT)
+    torch.cuda.synchronize()
+    _check_codes(c0.cpu(), c1.cpu())
+
+
+@pytest.mark.parametrize("n", [1, 511, 4096, 32768, 100000, 300001])
+@pytest.mark.parametrize("dist", ["skewed", "uniform256", "constant"])
+def test_rans_gpu_matches_cpu(n, dist):
+    g = torch.Generator().manual_seed(n)
+    if dist == "skewed":
+        p = torch.tensor([0.02, 0.18, 0.3, 0.3, 0.18, 0.02])
+        x = torch.multinomial(p, n, replacement=True, generator=g).to(torch.uint8)
+    elif dist == "uniform256":
+        x = torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8)
+    else:
+        x = torch.full((n,), 3, dtype=torch.uint8)
+    cpu_stream = K.rans_encode(x)
+    gpu_stream = K.rans_encode(x.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(gpu_stream.cpu(), cpu_stream), "device and host streams differ"
+    y = K.rans_decode(gpu_stream, n)
+    torch.cuda.synchronize()
+    K.check_device_error(y.device)
+    assert torch.equal(y.cpu(), x)
+    assert torch.equal(K.rans_decode(cpu_stream, n), x)
+
+
+def test_block_copy_gather_scatter():
+    H, tokens = 4, [80, 33]
+    wl = paged_workload(1, tokens, H, device="cuda", seed=21)
+    layer = wl.cache[0]
+    blocks = torch.tensor(wl.block_ids[0], dtype=torch.int32, device="cuda")
+    flat = torch.empty((2, blocks.numel(), 16, H, 128), dtype=torch.bfloat16, device="cuda")
+    K.block_copy(layer, blocks, flat.data_ptr(), gather=True)
+    torch.cuda.synchronize()
+    assert torch.equal(flat, gather_request(layer, wl.block_ids[0]))
+    dst = torch.zeros_like(layer)
+    K.block_copy(dst, blocks, flat.data_ptr(), gather=False)
+    torch.cuda.synchronize()
+    assert torch.equal(gather_request(dst, wl.block_ids[0]), flat)
+
+
+def test_kv_error_matches_cpu():
+    g = torch.Generator().manual_seed(3)
+    a = torch.randn(10007, generator=g).to(torch.bfloat16)
+    b = (a.float() + 0.01 * torch.randn(10007, generator=g)).to(torch.bfloat16)
+    got = K.kv_error(a.cuda(), b.cuda())
+    exp = oracle.error_metrics(a, b)
+    for k in ("rel_mse", "cosine", "max_abs"):
+        assert abs(got[k] - exp[k]) <= 1e-6 + 1e-5 * abs(exp[k])
+
+
+def test_logit_agreement():
+    g = torch.Generator().manual_seed(4)
+    r = torch.randn(8, 1000, generator=g)
+    a = r.clone()
+    a[3] += 5 * torch.randn(1000, generator=g)
+    out = K.logit_agreement(r.cuda(), a.cuda())
+    lp_r, lp_a = torch.log_softmax(r.double(), -1), torch.log_softmax(a.double(), -1)
+    kl = (lp_r.exp() * (lp_r - lp_a)).sum(-1).mean()
+    agree = (r.argmax(-1) == a.argmax(-1)).float().mean()
+    assert abs(out["kl_mean"] - float(kl)) < 1e-4
+    assert abs(out["top1_agreement"] - float(agree)) < 1e-6
+
+
+def test_wait_flag_times_out_with_error_status():
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.read_device_error(flag.device)  # clear
+    K.wait_flag(flag.data_ptr(), 1, flag.device, timeout_s=0.05)
+    torch.cuda.synchronize()
+    assert K.read_device_error(flag.device) == 2
+    K.set_flag(flag.data_ptr(), 1, flag.device)
+    K.wait_flag(flag.data_ptr(), 1, flag.device, timeout_s=0.05)
+    torch.cuda.synchronize()
+    assert K.read_device_error(flag.device) == 0
