@@ -30,8 +30,9 @@ class PagedKV(ctypes.Structure):
 
 class ReqTable(ctypes.Structure):
     _fields_ = [("block_table", c_void_p), ("bt_off", c_void_p), ("n_tokens", c_void_p),
-                ("n_rows", c_void_p), ("tile_prefix", c_void_p), ("code_off", c_void_p),
-                ("meta_off", c_void_p), ("num_req", c_int)]
+                ("n_rows", c_void_p), ("tile_prefix", c_void_p), ("slot", c_void_p),
+                ("code_off", c_void_p), ("meta_off", c_void_p), ("row_off", c_void_p),
+                ("num_req", c_int)]
 
 
 class LayerParams(ctypes.Structure):
@@ -45,9 +46,11 @@ class LayerParams(ctypes.Structure):
 
 
 class LayerLaunch(ctypes.Structure):
-    _fields_ = [("kv", PagedKV), ("rt", ReqTable), ("lp", LayerParams), ("bmat", c_void_p),
-                ("codes", c_void_p), ("meta", c_void_p), ("kstat", c_void_p), ("err", c_void_p),
-                ("total_tiles", c_int), ("engine", c_int), ("stream", c_void_p)]
+    _fields_ = [("kvs", c_void_p), ("maps", c_void_p), ("lps", c_void_p), ("rt", ReqTable),
+                ("bmat", c_void_p), ("bmat_stride", c_longlong), ("codes", c_void_p),
+                ("meta", c_void_p), ("kstat", c_void_p), ("vstat", c_void_p), ("err", c_void_p),
+                ("total_tiles", c_int), ("num_heads", c_int), ("engine", c_int),
+                ("stream", c_void_p)]
 
 
 _lock = threading.Lock()
@@ -59,9 +62,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     sig = {
         "kvs_layer_launch_size": ([], c_int),
         "kvs_init_key_stats": ([P, c_longlong, P], c_int),
-        "kvs_key_stats": ([POINTER(LayerLaunch)], c_int),
-        "kvs_quant_k": ([POINTER(LayerLaunch)], c_int),
-        "kvs_quant_v": ([POINTER(LayerLaunch)], c_int),
+        "kvs_layer_params_size": ([], c_int),
+        "kvs_paged_kv_size": ([], c_int),
+        "kvs_make_plane_maps": ([POINTER(PagedKV), c_int, P], c_int),
+        "kvs_stats": ([POINTER(LayerLaunch)], c_int),
+        "kvs_quant": ([POINTER(LayerLaunch)], c_int),
         "kvs_dequant_inverse": ([POINTER(LayerLaunch)], c_int),
         "kvs_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
         "kvs_rans_staging_bytes": ([c_uint64, c_uint32], c_uint64),
@@ -112,10 +117,13 @@ def lib() -> ctypes.CDLL:
                     "`python -m kvserve_hpdps_b200.ops.build`")
             handle = ctypes.CDLL(LIB_PATH)
             _declare(handle)
-            got = handle.kvs_layer_launch_size()
-            if got != ctypes.sizeof(LayerLaunch):
-                raise RuntimeError(f"LayerLaunch size mismatch: C {got} vs Python "
-                                   f"{ctypes.sizeof(LayerLaunch)}")
+            for name, cls in (("kvs_layer_launch_size", LayerLaunch),
+                              ("kvs_layer_params_size", LayerParams),
+                              ("kvs_paged_kv_size", PagedKV)):
+                got = getattr(handle, name)()
+                if got != ctypes.sizeof(cls):
+                    raise RuntimeError(f"{cls.__name__} size mismatch: C {got} vs Python "
+                                       f"{ctypes.sizeof(cls)}")
             _lib = handle
     return _lib
 

@@ -7,6 +7,15 @@
 // use per-token min/max over the heads that share a level count.  The CPU
 // oracle is kvserve_hpdps_b200/compression/oracle.py.
 //
+// One launch covers many work items, an item being a (layer, request) pair
+// (kvs_types.h).  The producer is three launches:
+//   k_init_key_stats                      reset the key min/max accumulators;
+//   k_stats_*   grid (tiles, H, 2)        plane 0: per-channel key min/max
+//                                         (atomics); plane 1: per-row value
+//                                         min/max (stores);
+//   k_quant_*   grid (tiles, H, 2)        codes + fp16 metadata of K and V.
+// The consumer is one launch: k_dequant_inverse_* grid (tiles, H, 2).
+//
 // Two engines with identical inputs/outputs:
 //  * engine 0 (default): 128-token tiles are fetched from the paged cache by
 //    TMA (one box per 16-row group and 64-channel half, no multicast), the
@@ -14,15 +23,8 @@
 //    against a +-1 Hadamard matrix with the Rademacher signs folded in, and
 //    the epilogue reads the accumulator back with tcgen05.ld;
 //  * engine 1: thread-per-row loads and an in-register fp32 butterfly.
-//
-// Launch shapes (one launch covers every request of a layer):
-//  key stats / key quant : grid (tiles, H), 128 threads
-//  value quant           : grid (tiles),    128 threads, loops over heads
-//  dequant + inverse     : grid (tiles, H, 2), 128 threads
 #include "common.cuh"
 #include "kvs_types.h"
-
-#include <cstdio>
 
 namespace kvs {
 
@@ -32,8 +34,8 @@ KVS_DEV uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// Request owning global tile `tile` (largest r with tile_prefix[r] <= tile).
-KVS_DEV int find_request(const int32_t* tile_prefix, int num_req, int tile) {
+// Item owning global tile `tile` (largest r with tile_prefix[r] <= tile).
+KVS_DEV int find_item(const int32_t* tile_prefix, int num_req, int tile) {
   int lo = 0, hi = num_req - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -42,45 +44,60 @@ KVS_DEV int find_request(const int32_t* tile_prefix, int num_req, int tile) {
   return lo;
 }
 
-struct TileCtx {
-  int r, row0, rows, ntok;
+struct ItemCtx {
+  int r, slot, row0, rows, ntok;
+  const LayerParams* lp;
+  PagedKV kv;
 };
 
-KVS_DEV TileCtx tile_ctx(const ReqTable& rt, int tile) {
-  TileCtx c;
-  c.r = find_request(rt.tile_prefix, rt.num_req, tile);
-  c.row0 = (tile - rt.tile_prefix[c.r]) * kTileRows;
-  c.rows = rt.n_rows[c.r];
-  c.ntok = rt.n_tokens[c.r];
+KVS_DEV ItemCtx item_ctx(const LayerLaunch& L, int tile) {
+  ItemCtx c;
+  c.r = find_item(L.rt.tile_prefix, L.rt.num_req, tile);
+  c.slot = L.rt.slot[c.r];
+  c.row0 = (tile - L.rt.tile_prefix[c.r]) * kTileRows;
+  c.rows = L.rt.n_rows[c.r];
+  c.ntok = L.rt.n_tokens[c.r];
+  c.lp = L.lps + c.slot;
+  c.kv = L.kvs[c.slot];
   return c;
 }
 
-KVS_DEV int phys_block(const ReqTable& rt, int r, int row, int bs) {
-  return rt.block_table[rt.bt_off[r] + row / bs];
+KVS_DEV int phys_block(const LayerLaunch& L, const ItemCtx& c, int row) {
+  return L.rt.block_table[L.rt.bt_off[c.r] + row / c.kv.block_size];
 }
 
-KVS_DEV const __nv_bfloat16* src_row(const PagedKV& kv, int plane, int phys, int slot, int H, int h) {
-  return reinterpret_cast<const __nv_bfloat16*>(kv.base) + phys * kv.block_stride +
-         plane * kv.kv_stride + (static_cast<long long>(slot) * H + h) * kHeadDim;
+KVS_DEV __nv_bfloat16* kv_row(const ItemCtx& c, int plane, int phys, int slot, int h) {
+  return const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(c.kv.base)) +
+         phys * c.kv.block_stride + plane * c.kv.kv_stride +
+         (static_cast<long long>(slot) * c.lp->H + h) * kHeadDim;
 }
 
-KVS_DEV __nv_bfloat16* dst_row(const PagedKV& kv, int plane, int phys, int slot, int H, int h) {
-  return const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(kv.base)) +
-         phys * kv.block_stride + plane * kv.kv_stride +
-         (static_cast<long long>(slot) * H + h) * kHeadDim;
+KVS_DEV int seg_bits(const ItemCtx& c, int kv, int h) {
+  return kv == 0 ? c.lp->key_bits[h] : c.lp->value_bits[h];
 }
 
-// Byte address of this request's code row for segment (kv, h).
-KVS_DEV uint8_t* code_row(const LayerLaunch& L, const TileCtx& c, int kv, int h, int row) {
-  const int bits = kv == 0 ? L.lp.key_bits[h] : L.lp.value_bits[h];
+// Byte address of an item's code row for segment (kv, h).
+KVS_DEV uint8_t* code_row(const LayerLaunch& L, const ItemCtx& c, int kv, int h, int row) {
   return L.codes + L.rt.code_off[c.r] +
-         static_cast<long long>(c.rows) * L.lp.seg_prefix[kv * L.lp.H + h] +
-         static_cast<long long>(row) * 16 * bits;
+         static_cast<long long>(c.rows) * c.lp->seg_prefix[kv * c.lp->H + h] +
+         static_cast<long long>(row) * 16 * seg_bits(c, kv, h);
 }
 
-// fp16 metadata of a request: [kmin H*128][kscale H*128][vmin G*rows][vscale G*rows]
+// fp16 metadata of an item: [kmin H*128][kscale H*128][vmin G*rows][vscale G*rows]
 KVS_DEV __half* meta_base(const LayerLaunch& L, int r) {
   return reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(L.meta) + L.rt.meta_off[r]);
+}
+
+KVS_DEV float* vstat_entry(const LayerLaunch& L, const ItemCtx& c, int h, int row) {
+  return L.vstat + (L.rt.row_off[c.r] * c.lp->H + static_cast<long long>(h) * c.rows + row) * 2;
+}
+
+KVS_DEV const uint8_t* bmat_of(const LayerLaunch& L, int slot, int h) {
+  return L.bmat + slot * L.bmat_stride + static_cast<long long>(h) * 32768;
+}
+
+KVS_DEV const CUtensorMap* map_of(const LayerLaunch& L, int slot, int plane) {
+  return reinterpret_cast<const CUtensorMap*>(L.maps) + slot * 2 + plane;
 }
 
 // ------------------------------------------------------- code (un)packing
@@ -140,10 +157,11 @@ KVS_DEV void load_row_f32(const __nv_bfloat16* p, float (&v)[128]) {
   }
 }
 
-KVS_DEV void apply_signs(float (&v)[128], const uint32_t (&sb)[4]) {
+KVS_DEV void apply_signs(float (&v)[128], const uint32_t* sb) {
+  uint32_t s[4] = {sb[0], sb[1], sb[2], sb[3]};
 #pragma unroll
   for (int d = 0; d < 128; ++d)
-    v[d] = __uint_as_float(__float_as_uint(v[d]) ^ (((sb[d >> 5] >> (d & 31)) & 1u) << 31));
+    v[d] = __uint_as_float(__float_as_uint(v[d]) ^ (((s[d >> 5] >> (d & 31)) & 1u) << 31));
 }
 
 KVS_DEV void fwht128(float (&v)[128]) {
@@ -161,31 +179,123 @@ KVS_DEV void fwht128(float (&v)[128]) {
 }
 
 // Forward transform of one source row (SIMT engine): signs, butterfly, scale.
-KVS_DEV void simt_forward_row(const LayerLaunch& L, int plane, int phys, int slot, int h,
+KVS_DEV void simt_forward_row(const ItemCtx& c, int plane, int phys, int slot, int h,
                               float (&v)[128]) {
-  load_row_f32(src_row(L.kv, plane, phys, slot, L.lp.H, h), v);
-  if (L.lp.transform) {
-    const uint32_t sb[4] = {L.lp.sign_bits[h][0], L.lp.sign_bits[h][1], L.lp.sign_bits[h][2],
-                            L.lp.sign_bits[h][3]};
-    apply_signs(v, sb);
+  load_row_f32(kv_row(c, plane, phys, slot, h), v);
+  if (c.lp->transform) {
+    apply_signs(v, c.lp->sign_bits[h]);
     fwht128(v);
   }
+  const float sc = c.lp->out_scale;
 #pragma unroll
-  for (int d = 0; d < 128; ++d) v[d] *= L.lp.out_scale;
+  for (int d = 0; d < 128; ++d) v[d] *= sc;
 }
 
-// ================================================================ key stats
-__global__ void __launch_bounds__(128) k_key_stats_simt(LayerLaunch L) {
-  extern __shared__ float buf[];  // [128][129]
-  const int tid = threadIdx.x, h = blockIdx.y;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
+// ------------------------------------------------------- shared prologues
+// Issue the TMA loads of one 128-row tile of head h (plane chosen by the
+// map) into a 2 x 16 KB SW128 tile, arriving on `bar` with the expected
+// byte count (plus `extra_tx` for other copies on the same barrier).
+KVS_DEV void issue_tile_loads(const LayerLaunch& L, const ItemCtx& c, const CUtensorMap* map,
+                              int h, uint8_t* tile, uint64_t* bar, uint32_t extra_tx) {
+  int nload = 0;
+  for (int g = 0; g < 8; ++g)
+    if (c.row0 + g * 16 < c.rows) ++nload;
+  mbar_arrive_expect_tx(bar, extra_tx + static_cast<uint32_t>(nload) * 4096u);
+  for (int g = 0; g < 8; ++g) {
+    const int rr = c.row0 + g * 16;
+    if (rr >= c.rows) break;
+    const int phys = phys_block(L, c, rr);
+    const int slot = rr % c.kv.block_size;
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb) {
+      asm volatile(
+          "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
+          "l"(reinterpret_cast<uint64_t>(map)), "r"(hb * 64), "r"(h), "r"(slot), "r"(phys),
+          "r"(smem_u32(bar))
+          : "memory");
+    }
+  }
+}
+
+// Key channel min / reciprocal scale of (item, head h) into smem; tile 0 of
+// the item publishes the fp16 metadata.
+KVS_DEV void key_channel_params(const LayerLaunch& L, const ItemCtx& c, int h, float* s_min,
+                                float* s_rcp) {
+  const int n = threadIdx.x;
+  const uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * c.lp->H + h) * 128 + n) * 2;
+  float kmin = 0.f, kmax = 0.f;
+  if (c.ntok > 0) {
+    kmin = ordered_to_float(ks[0]);
+    kmax = ordered_to_float(ks[1]);
+  }
+  const float lev = c.lp->key_levels[h];
+  const float scale = __fdiv_rn(fmaxf(__fsub_rn(kmax, kmin), kRangeEps), lev - 1.0f);
+  s_min[n] = kmin;
+  s_rcp[n] = __frcp_rn(scale);
+  if (c.row0 == 0) {
+    __half* m = meta_base(L, c.r);
+    m[h * 128 + n] = __float2half_rn(kmin);
+    m[c.lp->H * 128 + h * 128 + n] = __float2half_rn(scale);
+  }
+}
+
+// Value group min / reciprocal scale of row `row` for head h; the first
+// head of the group publishes the fp16 metadata.
+KVS_DEV void value_row_params(const LayerLaunch& L, const ItemCtx& c, int h, int row,
+                              float* out_min, float* out_rcp) {
+  const LayerParams* lp = c.lp;
+  const int g = lp->group_of_head[h];
+  float mn = INFINITY, mx = -INFINITY;
+  int first = -1;
+  for (int hh = 0; hh < lp->H; ++hh) {
+    if (lp->group_of_head[hh] != g) continue;
+    if (first < 0) first = hh;
+    const float* e = vstat_entry(L, c, hh, row);
+    mn = fminf(mn, e[0]);
+    mx = fmaxf(mx, e[1]);
+  }
+  const float scale = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), kRangeEps), lp->value_levels[h] - 1.0f);
+  *out_min = mn;
+  *out_rcp = __frcp_rn(scale);
+  if (h == first) {
+    __half* m = meta_base(L, c.r);
+    const int H = lp->H, G = lp->n_groups;
+    m[2 * H * 128 + g * c.rows + row] = __float2half_rn(mn);
+    m[2 * H * 128 + G * c.rows + g * c.rows + row] = __float2half_rn(scale);
+  }
+}
+
+// ================================================================== stats
+__global__ void __launch_bounds__(128) k_stats_simt(LayerLaunch L) {
+  extern __shared__ float buf[];  // [128][129] (keys only)
+  const int tid = threadIdx.x, h = blockIdx.y, plane = blockIdx.z;
+  const ItemCtx c = item_ctx(L, blockIdx.x);
+  const int row = c.row0 + tid;
+  if (plane == 1) {
+    if (row >= c.rows) return;
+    float mn = 0.f, mx = 0.f;
+    if (row < c.ntok) {
+      float v[128];
+      simt_forward_row(c, 1, phys_block(L, c, row), row % c.kv.block_size, h, v);
+      mn = INFINITY;
+      mx = -INFINITY;
+#pragma unroll
+      for (int d = 0; d < 128; ++d) {
+        mn = fminf(mn, v[d]);
+        mx = fmaxf(mx, v[d]);
+      }
+    }
+    float* e = vstat_entry(L, c, h, row);
+    e[0] = mn;
+    e[1] = mx;
+    return;
+  }
   const int nvalid = min(kTileRows, c.ntok - c.row0);
   if (nvalid <= 0) return;
-  const int row = c.row0 + tid;
   if (tid < nvalid) {
     float v[128];
-    const int bs = L.kv.block_size;
-    simt_forward_row(L, 0, phys_block(L.rt, c.r, row, bs), row % bs, h, v);
+    simt_forward_row(c, 0, phys_block(L, c, row), row % c.kv.block_size, h, v);
 #pragma unroll
     for (int d = 0; d < 128; ++d) buf[tid * 129 + d] = v[d];
   }
@@ -196,58 +306,24 @@ __global__ void __launch_bounds__(128) k_key_stats_simt(LayerLaunch L) {
     mn = fminf(mn, x);
     mx = fmaxf(mx, x);
   }
-  uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * L.lp.H + h) * 128 + tid) * 2;
+  uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * c.lp->H + h) * 128 + tid) * 2;
   atomicMin(ks, float_to_ordered(mn));
   atomicMax(ks + 1, float_to_ordered(mx));
 }
 
-// Issue the TMA loads of one 128-row tile of head h (plane chosen by the
-// map) into a 2 x 16 KB SW128 tile; returns the number of bytes expected.
-KVS_DEV uint32_t issue_tile_loads(const CUtensorMap* map, const ReqTable& rt, const TileCtx& c,
-                                  int bs, int h, uint8_t* tile, uint64_t* bar, bool arrive,
-                                  uint32_t extra_tx) {
-  int nload = 0;
-#pragma unroll 1
-  for (int g = 0; g < 8; ++g)
-    if (c.row0 + g * 16 < c.rows) ++nload;
-  const uint32_t tx = extra_tx + static_cast<uint32_t>(nload) * 4096u;
-  if (arrive) mbar_arrive_expect_tx(bar, tx);
-#pragma unroll 1
-  for (int g = 0; g < 8; ++g) {
-    const int rr = c.row0 + g * 16;
-    if (rr >= c.rows) break;
-    const int phys = phys_block(rt, c.r, rr, bs);
-    const int slot = rr % bs;
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + g * 2048)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(h), "r"(slot), "r"(phys),
-        "r"(smem_u32(bar))
-        : "memory");
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + 16384 + g * 2048)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(64), "r"(h), "r"(slot), "r"(phys),
-        "r"(smem_u32(bar))
-        : "memory");
-  }
-  return tx;
-}
+constexpr int kSmemTile = 65536 + 2048 + 1024;  // B image + tile + scratch + align slack
 
-constexpr int kSmemPair = 65536 + 1024 + 256;  // B image + tile + barriers + align slack
-
-__global__ void __launch_bounds__(128) k_key_stats_mma(const __grid_constant__ CUtensorMap kmap,
-                                                       LayerLaunch L) {
+__global__ void __launch_bounds__(128) k_stats_mma(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sB = smem;          // A operand: signed Hadamard image of head h
-  uint8_t* sT = smem + 32768;  // B operand: key tile [token][channel]
+  uint8_t* sB = smem;          // transform image of head h
+  uint8_t* sT = smem + 32768;  // data tile [token][channel]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 65536);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 65536 + 32);
-  const int tid = threadIdx.x, warp = tid >> 5, h = blockIdx.y;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
+  const int tid = threadIdx.x, warp = tid >> 5, h = blockIdx.y, plane = blockIdx.z;
+  const ItemCtx c = item_ctx(L, blockIdx.x);
   const int nvalid = min(kTileRows, c.ntok - c.row0);
-  if (nvalid <= 0) return;  // uniform across the CTA, before any barrier
+  if (plane == 0 && nvalid <= 0) return;  // uniform across the CTA, before any barrier
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -259,12 +335,17 @@ __global__ void __launch_bounds__(128) k_key_stats_mma(const __grid_constant__ C
   tc_fence_after();
   const uint32_t tmem = *tslot;
   if (tid == 0) {
-    issue_tile_loads(&kmap, L.rt, c, L.kv.block_size, h, sT, &bars[0], true, 32768u);
-    bulk_load(sB, L.bmat + static_cast<size_t>(h) * 32768, 32768, &bars[0]);
+    issue_tile_loads(L, c, map_of(L, c.slot, plane), h, sT, &bars[0], 32768u);
+    bulk_load(sB, bmat_of(L, c.slot, h), 32768, &bars[0]);
     if (mbar_wait(&bars[0], 0, L.err, ERR_MBAR_TIMEOUT)) {
       tc_fence_after();
-      // D[n][t] = sum_k Bf[n][k] * K[t][k]: lane n = output channel.
-      umma_tile_128x128x128(tmem, smem_u32(sB), smem_u32(sT));
+      if (plane == 0) {
+        // D[n][t] = sum_k Bf[n][k] K[t][k]: lane = output channel n.
+        umma_tile_128x128x128(tmem, smem_u32(sB), smem_u32(sT));
+      } else {
+        // D[t][n] = sum_k V[t][k] Bf[n][k]: lane = token row t.
+        umma_tile_128x128x128(tmem, smem_u32(sT), smem_u32(sB));
+      }
     } else {
       mbar_wait(&bars[0], 0, nullptr, 0);  // drain copies still in flight
     }
@@ -272,83 +353,78 @@ __global__ void __launch_bounds__(128) k_key_stats_mma(const __grid_constant__ C
   }
   mbar_wait(&bars[1], 0, L.err, ERR_MBAR_TIMEOUT);
   tc_fence_after();
-  float mn = INFINITY, mx = -INFINITY;
+  const float sc = c.lp->out_scale;
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
     float v[32];
     tmem_ld32(tmem + lane_base + cc * 32, v);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      if (cc * 32 + j < nvalid) {
-        const float x = v[j] * L.lp.out_scale;
+      if (plane == 1 || cc * 32 + j < nvalid) {
+        const float x = v[j] * sc;
         mn = fminf(mn, x);
         mx = fmaxf(mx, x);
       }
     }
   }
-  uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * L.lp.H + h) * 128 + tid) * 2;
-  atomicMin(ks, float_to_ordered(mn));
-  atomicMax(ks + 1, float_to_ordered(mx));
+  if (plane == 0) {
+    uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * c.lp->H + h) * 128 + tid) * 2;
+    atomicMin(ks, float_to_ordered(mn));
+    atomicMax(ks + 1, float_to_ordered(mx));
+  } else {
+    const int row = c.row0 + tid;
+    if (row < c.rows) {
+      if (row >= c.ntok) mn = mx = 0.f;
+      float* e = vstat_entry(L, c, h, row);
+      e[0] = mn;
+      e[1] = mx;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
-// Per-channel key min / reciprocal scale of (request r, head h) into smem;
-// tile 0 of the request also publishes the fp16 metadata.
-KVS_DEV void key_channel_params(const LayerLaunch& L, const TileCtx& c, int h, bool publish,
-                                float* s_min, float* s_rcp) {
-  const int n = threadIdx.x;
-  const uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * L.lp.H + h) * 128 + n) * 2;
-  float kmin = 0.f, kmax = 0.f;
-  if (c.ntok > 0) {
-    kmin = ordered_to_float(ks[0]);
-    kmax = ordered_to_float(ks[1]);
-  }
-  const float lev = L.lp.key_levels[h];
-  const float scale = __fdiv_rn(fmaxf(__fsub_rn(kmax, kmin), kRangeEps), lev - 1.0f);
-  s_min[n] = kmin;
-  s_rcp[n] = __frcp_rn(scale);
-  if (publish) {
-    __half* m = meta_base(L, c.r);
-    m[h * 128 + n] = __float2half_rn(kmin);
-    m[L.lp.H * 128 + h * 128 + n] = __float2half_rn(scale);
-  }
-}
-
-// ================================================================ key quant
-__global__ void __launch_bounds__(128) k_quant_k_simt(LayerLaunch L) {
+// ================================================================== quant
+__global__ void __launch_bounds__(128) k_quant_simt(LayerLaunch L) {
   __shared__ float s_min[128], s_rcp[128];
-  const int tid = threadIdx.x, h = blockIdx.y;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
-  key_channel_params(L, c, h, c.row0 == 0, s_min, s_rcp);
+  const int tid = threadIdx.x, h = blockIdx.y, plane = blockIdx.z;
+  const ItemCtx c = item_ctx(L, blockIdx.x);
+  if (plane == 0) key_channel_params(L, c, h, s_min, s_rcp);
   __syncthreads();
   const int row = c.row0 + tid;
   if (row >= c.rows) return;
-  const int bs = L.kv.block_size;
+  float vmin = 0.f, vrcp = 0.f;
+  if (plane == 1) value_row_params(L, c, h, row, &vmin, &vrcp);
   float v[128];
-  simt_forward_row(L, 0, phys_block(L.rt, c.r, row, bs), row % bs, h, v);
-  const float lev = L.lp.key_levels[h];
-  const float top = L.lp.clamp_top ? lev - 1.0f : lev;
   const bool valid = row < c.ntok;
-  uint8_t* out = code_row(L, c, 0, h, row);
-  const int bits = L.lp.key_bits[h];
+  if (valid) {
+    simt_forward_row(c, plane, phys_block(L, c, row), row % c.kv.block_size, h, v);
+  } else {
+#pragma unroll
+    for (int d = 0; d < 128; ++d) v[d] = 0.f;
+  }
+  const float lev = plane == 0 ? c.lp->key_levels[h] : c.lp->value_levels[h];
+  const float top = c.lp->clamp_top ? lev - 1.0f : lev;
+  uint8_t* out = code_row(L, c, plane, h, row);
+  const int bits = seg_bits(c, plane, h);
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
     uint32_t q[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int n = cc * 32 + j;
-      const float val = valid ? bf16_round(v[n]) : 0.0f;
-      q[j] = quantize_one(val, s_min[n], s_rcp[n], top);
+      const float val = bf16_round(v[n]);
+      q[j] = plane == 0 ? quantize_one(val, s_min[n], s_rcp[n], top)
+                        : quantize_one(val, vmin, vrcp, top);
     }
     store_chunk(out, cc, bits, q);
   }
 }
 
-__global__ void __launch_bounds__(128) k_quant_k_mma(const __grid_constant__ CUtensorMap kmap,
-                                                     LayerLaunch L) {
+__global__ void __launch_bounds__(128) k_quant_mma(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sB = smem;
@@ -357,8 +433,8 @@ __global__ void __launch_bounds__(128) k_quant_k_mma(const __grid_constant__ CUt
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 65536 + 32);
   float* s_min = reinterpret_cast<float*>(smem + 65536 + 64);
   float* s_rcp = s_min + 128;
-  const int tid = threadIdx.x, warp = tid >> 5, h = blockIdx.y;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
+  const int tid = threadIdx.x, warp = tid >> 5, h = blockIdx.y, plane = blockIdx.z;
+  const ItemCtx c = item_ctx(L, blockIdx.x);
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -370,14 +446,21 @@ __global__ void __launch_bounds__(128) k_quant_k_mma(const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = *tslot;
   if (tid == 0) {
-    issue_tile_loads(&kmap, L.rt, c, L.kv.block_size, h, sT, &bars[0], true, 32768u);
-    bulk_load(sB, L.bmat + static_cast<size_t>(h) * 32768, 32768, &bars[0]);
+    issue_tile_loads(L, c, map_of(L, c.slot, plane), h, sT, &bars[0], 32768u);
+    bulk_load(sB, bmat_of(L, c.slot, h), 32768, &bars[0]);
   }
-  key_channel_params(L, c, h, c.row0 == 0, s_min, s_rcp);
+  const int row = c.row0 + tid;
+  const bool exists = row < c.rows, valid = row < c.ntok;
+  float vmin = 0.f, vrcp = 0.f;
+  if (plane == 0) {
+    key_channel_params(L, c, h, s_min, s_rcp);
+  } else if (exists) {
+    value_row_params(L, c, h, row, &vmin, &vrcp);
+  }
   if (tid == 0) {
     if (mbar_wait(&bars[0], 0, L.err, ERR_MBAR_TIMEOUT)) {
       tc_fence_after();
-      // D[t][n] = sum_k K[t][k] * Bf[n][k]: lane t = token row.
+      // D[t][n] = sum_k X[t][k] Bf[n][k]: lane = token row t.
       umma_tile_128x128x128(tmem, smem_u32(sT), smem_u32(sB));
     } else {
       mbar_wait(&bars[0], 0, nullptr, 0);
@@ -387,12 +470,11 @@ __global__ void __launch_bounds__(128) k_quant_k_mma(const __grid_constant__ CUt
   __syncthreads();  // s_min / s_rcp visible
   mbar_wait(&bars[1], 0, L.err, ERR_MBAR_TIMEOUT);
   tc_fence_after();
-  const int row = c.row0 + tid;
-  const bool exists = row < c.rows, valid = row < c.ntok;
-  const float lev = L.lp.key_levels[h];
-  const float top = L.lp.clamp_top ? lev - 1.0f : lev;
-  uint8_t* out = exists ? code_row(L, c, 0, h, row) : nullptr;
-  const int bits = L.lp.key_bits[h];
+  const float lev = plane == 0 ? c.lp->key_levels[h] : c.lp->value_levels[h];
+  const float top = c.lp->clamp_top ? lev - 1.0f : lev;
+  const float sc = c.lp->out_scale;
+  uint8_t* out = exists ? code_row(L, c, plane, h, row) : nullptr;
+  const int bits = seg_bits(c, plane, h);
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
@@ -402,8 +484,9 @@ __global__ void __launch_bounds__(128) k_quant_k_mma(const __grid_constant__ CUt
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int n = cc * 32 + j;
-      const float val = valid ? bf16_round(v[j] * L.lp.out_scale) : 0.0f;
-      q[j] = quantize_one(val, s_min[n], s_rcp[n], top);
+      const float val = valid ? bf16_round(v[j] * sc) : 0.0f;
+      q[j] = plane == 0 ? quantize_one(val, s_min[n], s_rcp[n], top)
+                        : quantize_one(val, vmin, vrcp, top);
     }
     if (exists) store_chunk(out, cc, bits, q);
   }
@@ -412,216 +495,16 @@ __global__ void __launch_bounds__(128) k_quant_k_mma(const __grid_constant__ CUt
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
-// ============================================================== value quant
-// Per-row group statistics from the per-head row min/max in smem; the
-// thread owning row t computes and publishes its own entries.
-KVS_DEV void value_group_params(const LayerLaunch& L, const TileCtx& c, const float* rmin,
-                                const float* rmax, float* g_min, float* g_rcp) {
-  const int t = threadIdx.x, H = L.lp.H, G = L.lp.n_groups;
-  const int row = c.row0 + t;
-  __half* m = meta_base(L, c.r);
-  for (int g = 0; g < G; ++g) {
-    float mn = INFINITY, mx = -INFINITY, lev = 2.0f;
-    for (int h = 0; h < H; ++h) {
-      if (L.lp.group_of_head[h] != g) continue;
-      mn = fminf(mn, rmin[h * 128 + t]);
-      mx = fmaxf(mx, rmax[h * 128 + t]);
-      lev = L.lp.value_levels[h];
-    }
-    const float scale = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), kRangeEps), lev - 1.0f);
-    g_min[g * 128 + t] = mn;
-    g_rcp[g * 128 + t] = __frcp_rn(scale);
-    if (row < c.rows) {
-      m[2 * H * 128 + g * c.rows + row] = __float2half_rn(mn);
-      m[2 * H * 128 + G * c.rows + g * c.rows + row] = __float2half_rn(scale);
-    }
-  }
-}
-
-__global__ void __launch_bounds__(128) k_quant_v_simt(LayerLaunch L) {
-  extern __shared__ float vsm[];  // rmin[16*128] rmax[16*128] gmin[16*128] grcp[16*128]
-  float* rmin = vsm;
-  float* rmax = vsm + kMaxHeads * 128;
-  float* gmin = vsm + 2 * kMaxHeads * 128;
-  float* grcp = vsm + 3 * kMaxHeads * 128;
-  const int tid = threadIdx.x, H = L.lp.H;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
-  const int row = c.row0 + tid;
-  const bool exists = row < c.rows, valid = row < c.ntok;
-  const int bs = L.kv.block_size;
-  const int phys = exists ? phys_block(L.rt, c.r, row, bs) : 0;
-  for (int h = 0; h < H; ++h) {
-    float mn = 0.f, mx = 0.f;
-    if (exists && valid) {
-      float v[128];
-      simt_forward_row(L, 1, phys, row % bs, h, v);
-      mn = INFINITY;
-      mx = -INFINITY;
-#pragma unroll
-      for (int d = 0; d < 128; ++d) {
-        mn = fminf(mn, v[d]);
-        mx = fmaxf(mx, v[d]);
-      }
-    }
-    rmin[h * 128 + tid] = mn;
-    rmax[h * 128 + tid] = mx;
-  }
-  value_group_params(L, c, rmin, rmax, gmin, grcp);
-  if (!exists) return;
-  for (int h = 0; h < H; ++h) {
-    float v[128];
-    if (valid) {
-      simt_forward_row(L, 1, phys, row % bs, h, v);
-    } else {
-#pragma unroll
-      for (int d = 0; d < 128; ++d) v[d] = 0.f;
-    }
-    const int g = L.lp.group_of_head[h];
-    const float mn = gmin[g * 128 + tid], rcp = grcp[g * 128 + tid];
-    const float lev = L.lp.value_levels[h];
-    const float top = L.lp.clamp_top ? lev - 1.0f : lev;
-    uint8_t* out = code_row(L, c, 1, h, row);
-    const int bits = L.lp.value_bits[h];
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t q[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) q[j] = quantize_one(bf16_round(v[cc * 32 + j]), mn, rcp, top);
-      store_chunk(out, cc, bits, q);
-    }
-  }
-}
-
-constexpr int kSmemValue = 2 * 65536 + 4 * kMaxHeads * 128 * 4 + 256 + 1024;
-
-__global__ void __launch_bounds__(128, 1) k_quant_v_mma(const __grid_constant__ CUtensorMap vmap,
-                                                        LayerLaunch L) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint8_t* sB[2] = {smem, smem + 65536};
-  uint8_t* sA[2] = {smem + 32768, smem + 65536 + 32768};
-  float* rmin = reinterpret_cast<float*>(smem + 131072);
-  float* rmax = rmin + kMaxHeads * 128;
-  float* gmin = rmin + 2 * kMaxHeads * 128;
-  float* grcp = rmin + 3 * kMaxHeads * 128;
-  uint64_t* lbar = reinterpret_cast<uint64_t*>(smem + 131072 + 4 * kMaxHeads * 128 * 4);
-  uint64_t* mbar = lbar + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(lbar + 4);
-  const int tid = threadIdx.x, warp = tid >> 5, H = L.lp.H;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
-  const uint32_t ncols = H <= 1 ? 128u : (H == 2 ? 256u : 512u);
-  const bool recompute = H > 4;
-  if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&lbar[i], 1);
-      mbar_init(&mbar[i], 1);
-    }
-    fence_mbar_init();
-  }
-  if (warp == 0) tmem_alloc(tslot, ncols);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  const int row = c.row0 + tid;
-  const bool exists = row < c.rows, valid = row < c.ntok;
-  const int bs = L.kv.block_size;
-  uint32_t use[2] = {0u, 0u};
-
-  auto issue = [&](int hh, int st) {
-    issue_tile_loads(&vmap, L.rt, c, bs, hh, sA[st], &lbar[st], true, 32768u);
-    bulk_load(sB[st], L.bmat + static_cast<size_t>(hh) * 32768, 32768, &lbar[st]);
-  };
-  auto quant_head = [&](int hh) {
-    const int g = L.lp.group_of_head[hh];
-    const float mn = gmin[g * 128 + tid], rcp = grcp[g * 128 + tid];
-    const float lev = L.lp.value_levels[hh];
-    const float top = L.lp.clamp_top ? lev - 1.0f : lev;
-    uint8_t* out = exists ? code_row(L, c, 1, hh, row) : nullptr;
-    const int bits = L.lp.value_bits[hh];
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      float v[32];
-      tmem_ld32(tmem + lane_base + (hh & 3) * 128 + cc * 32, v);
-      uint32_t q[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float val = valid ? bf16_round(v[j] * L.lp.out_scale) : 0.0f;
-        q[j] = quantize_one(val, mn, rcp, top);
-      }
-      if (exists) store_chunk(out, cc, bits, q);
-    }
-  };
-  // mode 0: row statistics; mode 1: quantize (used when heads are recomputed)
-  auto run_pass = [&](int mode) {
-    if (tid == 0) {
-      issue(0, 0);
-      if (H > 1) issue(1, 1);
-    }
-    for (int hh = 0; hh < H; ++hh) {
-      const int st = hh & 1;
-      const uint32_t par = use[st] & 1u;
-      if (tid == 0) {
-        if (mbar_wait(&lbar[st], par, L.err, ERR_MBAR_TIMEOUT)) {
-          tc_fence_after();
-          umma_tile_128x128x128(tmem + (hh & 3) * 128, smem_u32(sA[st]), smem_u32(sB[st]));
-        } else {
-          mbar_wait(&lbar[st], par, nullptr, 0);
-        }
-        umma_commit(&mbar[st]);
-      }
-      mbar_wait(&mbar[st], par, L.err, ERR_MBAR_TIMEOUT);
-      use[st]++;
-      tc_fence_after();
-      if (tid == 0 && hh + 2 < H) issue(hh + 2, st);
-      if (mode == 0) {
-        float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float v[32];
-          tmem_ld32(tmem + lane_base + (hh & 3) * 128 + cc * 32, v);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = v[j] * L.lp.out_scale;
-            mn = fminf(mn, x);
-            mx = fmaxf(mx, x);
-          }
-        }
-        if (!valid) mn = mx = 0.f;
-        rmin[hh * 128 + tid] = mn;
-        rmax[hh * 128 + tid] = mx;
-      } else {
-        quant_head(hh);
-      }
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-    }
-  };
-
-  run_pass(0);
-  value_group_params(L, c, rmin, rmax, gmin, grcp);
-  if (recompute) {
-    run_pass(1);
-  } else {
-    for (int hh = 0; hh < H; ++hh) quant_head(hh);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, ncols);
-}
-
 // ========================================================== dequant+inverse
 // Dequantize one code row into 128 floats (bf16-valued).
-KVS_DEV void dequant_row(const LayerLaunch& L, const TileCtx& c, int kv, int h, int row,
+KVS_DEV void dequant_row(const LayerLaunch& L, const ItemCtx& c, int kv, int h, int row,
                          const float* kmin_bf, const float* ksc_bf, float (&v)[128]) {
   const uint8_t* src = code_row(L, c, kv, h, row);
-  const int bits = kv == 0 ? L.lp.key_bits[h] : L.lp.value_bits[h];
+  const int bits = seg_bits(c, kv, h);
   float vmn = 0.f, vsc = 0.f;
   if (kv == 1) {
     const __half* m = meta_base(L, c.r);
-    const int H = L.lp.H, G = L.lp.n_groups, g = L.lp.group_of_head[h];
+    const int H = c.lp->H, G = c.lp->n_groups, g = c.lp->group_of_head[h];
     vmn = bf16_round(__half2float(m[2 * H * 128 + g * c.rows + row]));
     vsc = bf16_round(__half2float(m[2 * H * 128 + G * c.rows + g * c.rows + row]));
   }
@@ -637,11 +520,12 @@ KVS_DEV void dequant_row(const LayerLaunch& L, const TileCtx& c, int kv, int h, 
   }
 }
 
-KVS_DEV void load_key_meta_bf(const LayerLaunch& L, int r, int h, float* kmin_bf, float* ksc_bf) {
+KVS_DEV void load_key_meta_bf(const LayerLaunch& L, const ItemCtx& c, int h, float* kmin_bf,
+                              float* ksc_bf) {
   const int n = threadIdx.x;
-  const __half* m = meta_base(L, r);
+  const __half* m = meta_base(L, c.r);
   kmin_bf[n] = bf16_round(__half2float(m[h * 128 + n]));
-  ksc_bf[n] = bf16_round(__half2float(m[L.lp.H * 128 + h * 128 + n]));
+  ksc_bf[n] = bf16_round(__half2float(m[c.lp->H * 128 + h * 128 + n]));
 }
 
 KVS_DEV void store_row_bf16(__nv_bfloat16* dst, const float (&v)[128]) {
@@ -661,23 +545,21 @@ KVS_DEV void store_row_bf16(__nv_bfloat16* dst, const float (&v)[128]) {
 __global__ void __launch_bounds__(128) k_dequant_inverse_simt(LayerLaunch L) {
   __shared__ float kmin_bf[128], ksc_bf[128];
   const int tid = threadIdx.x, h = blockIdx.y, kv = blockIdx.z;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
-  if (kv == 0) load_key_meta_bf(L, c.r, h, kmin_bf, ksc_bf);
+  const ItemCtx c = item_ctx(L, blockIdx.x);
+  if (kv == 0) load_key_meta_bf(L, c, h, kmin_bf, ksc_bf);
   __syncthreads();
   const int row = c.row0 + tid;
   if (row >= c.ntok || row >= c.rows) return;
   float v[128];
   dequant_row(L, c, kv, h, row, kmin_bf, ksc_bf, v);
-  if (L.lp.transform) {
+  if (c.lp->transform) {
     fwht128(v);
-    const uint32_t sb[4] = {L.lp.sign_bits[h][0], L.lp.sign_bits[h][1], L.lp.sign_bits[h][2],
-                            L.lp.sign_bits[h][3]};
+    const float sc = c.lp->out_scale;
 #pragma unroll
-    for (int d = 0; d < 128; ++d) v[d] = bf16_round(v[d] * L.lp.out_scale);
-    apply_signs(v, sb);
+    for (int d = 0; d < 128; ++d) v[d] = bf16_round(v[d] * sc);
+    apply_signs(v, c.lp->sign_bits[h]);
   }
-  const int bs = L.kv.block_size;
-  store_row_bf16(dst_row(L.kv, kv, phys_block(L.rt, c.r, row, bs), row % bs, L.lp.H, h), v);
+  store_row_bf16(kv_row(c, kv, phys_block(L, c, row), row % c.kv.block_size, h), v);
 }
 
 // Byte offset of element n of row t in a 2 x 16 KB K-major SW128 tile.
@@ -699,16 +581,16 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
   float* kmin_bf = reinterpret_cast<float*>(smem + 65536 + 64);
   float* ksc_bf = kmin_bf + 128;
   const int tid = threadIdx.x, warp = tid >> 5, h = blockIdx.y, kv = blockIdx.z;
-  const TileCtx c = tile_ctx(L.rt, blockIdx.x);
+  const ItemCtx c = item_ctx(L, blockIdx.x);
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&bars[0], 32768u);
-    bulk_load(sB, L.bmat + static_cast<size_t>(h) * 32768, 32768, &bars[0]);
+    bulk_load(sB, bmat_of(L, c.slot, h), 32768, &bars[0]);
   }
   if (warp == 0) tmem_alloc(tslot, 128);
-  if (kv == 0) load_key_meta_bf(L, c.r, h, kmin_bf, ksc_bf);
+  if (kv == 0) load_key_meta_bf(L, c, h, kmin_bf, ksc_bf);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -723,7 +605,6 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
 #pragma unroll
       for (int d = 0; d < 128; ++d) v[d] = 0.f;
     }
-    // 16-byte chunks: 8 consecutive channels per chunk.
 #pragma unroll
     for (int ch = 0; ch < 16; ++ch) {
       uint32_t w[4];
@@ -732,7 +613,8 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
         const __nv_bfloat162 p = __floats2bfloat162_rn(v[ch * 8 + 2 * j], v[ch * 8 + 2 * j + 1]);
         w[j] = *reinterpret_cast<const uint32_t*>(&p);
       }
-      *reinterpret_cast<uint4*>(sA + sw128_offset(tid, ch * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(sA + sw128_offset(tid, ch * 8)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
   fence_proxy_async_smem();
@@ -740,7 +622,7 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
   if (tid == 0) {
     if (mbar_wait(&bars[0], 0, L.err, ERR_MBAR_TIMEOUT)) {
       tc_fence_after();
-      // D[t][k] = sum_n Y[t][n] * Bi[k][n], Bi[k][n] = s[k] H[k][n].
+      // D[t][k] = sum_n Y[t][n] Bi[k][n], Bi[k][n] = s[k] H[k][n].
       umma_tile_128x128x128(tmem, smem_u32(sA), smem_u32(sB));
     } else {
       mbar_wait(&bars[0], 0, nullptr, 0);
@@ -750,9 +632,9 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
   mbar_wait(&bars[1], 0, L.err, ERR_MBAR_TIMEOUT);
   tc_fence_after();
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  const int bs = L.kv.block_size;
+  const float sc = c.lp->out_scale;
   __nv_bfloat16* dst =
-      valid ? dst_row(L.kv, kv, phys_block(L.rt, c.r, row, bs), row % bs, L.lp.H, h) : nullptr;
+      valid ? kv_row(c, kv, phys_block(L, c, row), row % c.kv.block_size, h) : nullptr;
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
     float v[32];
@@ -761,13 +643,13 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
       uint32_t w[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const __nv_bfloat162 p =
-            __floats2bfloat162_rn(v[2 * j] * L.lp.out_scale, v[2 * j + 1] * L.lp.out_scale);
+        const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j] * sc, v[2 * j + 1] * sc);
         w[j] = *reinterpret_cast<const uint32_t*>(&p);
       }
       uint4* d = reinterpret_cast<uint4*>(dst + cc * 32);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      for (int i = 0; i < 4; ++i)
+        d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     }
   }
   tc_fence_before();
@@ -802,24 +684,6 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 4-D map over one KV plane: (d=128, head, slot, block), box (64, 1, 16, 1).
-static int make_plane_map(const PagedKV& kv, int plane, int H, CUtensorMap* map) {
-  EncodeTiledFn fn = encode_fn();
-  if (fn == nullptr) return -100;
-  void* base = const_cast<void*>(reinterpret_cast<const void*>(
-      reinterpret_cast<const __nv_bfloat16*>(kv.base) + plane * kv.kv_stride));
-  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(kv.block_size),
-                        static_cast<cuuint64_t>(kv.num_blocks)};
-  cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(H) * 256,
-                           static_cast<cuuint64_t>(kv.block_stride) * 2};
-  cuuint32_t box[4] = {64, 1, 16, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : -101;
-}
-
 template <typename K>
 static int set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
@@ -828,15 +692,40 @@ static int set_smem(K kernel, int bytes) {
              : -102;
 }
 
-static int mma_supported(const LayerLaunch& L) {
-  return L.kv.block_size % 16 == 0 && L.lp.H <= kMaxHeads;
-}
-
 }  // namespace kvs
 
 using namespace kvs;
 
 extern "C" {
+
+int kvs_layer_launch_size(void) { return static_cast<int>(sizeof(LayerLaunch)); }
+int kvs_layer_params_size(void) { return static_cast<int>(sizeof(LayerParams)); }
+int kvs_paged_kv_size(void) { return static_cast<int>(sizeof(PagedKV)); }
+
+// Encode the K and V plane maps of one paged layer into out[0..1] (host
+// memory, 128 bytes each): 4-D (d=128, head, slot, block), box (64,1,16,1),
+// 128-byte swizzle, no OOB fill.
+int kvs_make_plane_maps(const PagedKV* kv, int H, void* out) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return -100;
+  CUtensorMap* maps = static_cast<CUtensorMap*>(out);
+  for (int plane = 0; plane < 2; ++plane) {
+    void* base = const_cast<void*>(reinterpret_cast<const void*>(
+        reinterpret_cast<const __nv_bfloat16*>(kv->base) + plane * kv->kv_stride));
+    cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(H),
+                          static_cast<cuuint64_t>(kv->block_size),
+                          static_cast<cuuint64_t>(kv->num_blocks)};
+    cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(H) * 256,
+                             static_cast<cuuint64_t>(kv->block_stride) * 2};
+    cuuint32_t box[4] = {64, 1, 16, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(&maps[plane], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -101;
+  }
+  return 0;
+}
 
 int kvs_init_key_stats(uint32_t* kstat, long long n_pairs, void* stream) {
   if (n_pairs <= 0) return 0;
@@ -845,55 +734,31 @@ int kvs_init_key_stats(uint32_t* kstat, long long n_pairs, void* stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int kvs_key_stats(const LayerLaunch* Lp) {
+int kvs_stats(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
-  dim3 grid(L.total_tiles, L.lp.H);
-  if (L.engine == 0 && mma_supported(L)) {
-    CUtensorMap map;
-    int rc = make_plane_map(L.kv, 0, L.lp.H, &map);
-    if (rc) return rc;
-    if (int rc = set_smem(k_key_stats_mma, kSmemPair)) return rc;
-    k_key_stats_mma<<<grid, 128, kSmemPair, s>>>(map, L);
+  dim3 grid(L.total_tiles, L.num_heads, 2);
+  if (L.engine == 0) {
+    if (int rc = set_smem(k_stats_mma, kSmemTile)) return rc;
+    k_stats_mma<<<grid, 128, kSmemTile, s>>>(L);
   } else {
-    if (int rc = set_smem(k_key_stats_simt, 128 * 129 * 4)) return rc;
-    k_key_stats_simt<<<grid, 128, 128 * 129 * 4, s>>>(L);
+    if (int rc = set_smem(k_stats_simt, 128 * 129 * 4)) return rc;
+    k_stats_simt<<<grid, 128, 128 * 129 * 4, s>>>(L);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int kvs_quant_k(const LayerLaunch* Lp) {
+int kvs_quant(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
-  dim3 grid(L.total_tiles, L.lp.H);
-  if (L.engine == 0 && mma_supported(L)) {
-    CUtensorMap map;
-    int rc = make_plane_map(L.kv, 0, L.lp.H, &map);
-    if (rc) return rc;
-    if (int rc = set_smem(k_quant_k_mma, kSmemPair + 1024)) return rc;
-    k_quant_k_mma<<<grid, 128, kSmemPair + 1024, s>>>(map, L);
+  dim3 grid(L.total_tiles, L.num_heads, 2);
+  if (L.engine == 0) {
+    if (int rc = set_smem(k_quant_mma, kSmemTile)) return rc;
+    k_quant_mma<<<grid, 128, kSmemTile, s>>>(L);
   } else {
-    k_quant_k_simt<<<grid, 128, 0, s>>>(L);
-  }
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
-}
-
-int kvs_quant_v(const LayerLaunch* Lp) {
-  const LayerLaunch& L = *Lp;
-  if (L.total_tiles <= 0) return 0;
-  cudaStream_t s = static_cast<cudaStream_t>(L.stream);
-  if (L.engine == 0 && mma_supported(L)) {
-    CUtensorMap map;
-    int rc = make_plane_map(L.kv, 1, L.lp.H, &map);
-    if (rc) return rc;
-    if (int rc = set_smem(k_quant_v_mma, kSmemValue)) return rc;
-    k_quant_v_mma<<<L.total_tiles, 128, kSmemValue, s>>>(map, L);
-  } else {
-    const int bytes = 4 * kMaxHeads * 128 * 4;
-    if (int rc = set_smem(k_quant_v_simt, bytes)) return rc;
-    k_quant_v_simt<<<L.total_tiles, 128, bytes, s>>>(L);
+    k_quant_simt<<<grid, 128, 0, s>>>(L);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
@@ -902,16 +767,14 @@ int kvs_dequant_inverse(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
-  dim3 grid(L.total_tiles, L.lp.H, 2);
-  if (L.engine == 0 && mma_supported(L)) {
-    if (int rc = set_smem(k_dequant_inverse_mma, kSmemPair + 1024)) return rc;
-    k_dequant_inverse_mma<<<grid, 128, kSmemPair + 1024, s>>>(L);
+  dim3 grid(L.total_tiles, L.num_heads, 2);
+  if (L.engine == 0) {
+    if (int rc = set_smem(k_dequant_inverse_mma, kSmemTile)) return rc;
+    k_dequant_inverse_mma<<<grid, 128, kSmemTile, s>>>(L);
   } else {
     k_dequant_inverse_simt<<<grid, 128, 0, s>>>(L);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
-
-int kvs_layer_launch_size(void) { return static_cast<int>(sizeof(LayerLaunch)); }
 
 }  // extern "C"

@@ -1,5 +1,6 @@
 // Plain-old-data argument blocks shared by the host launchers and the
-// kernels.  Everything is passed by value as kernel parameters.
+// kernels.  LayerLaunch is passed by value; the per-slot arrays it points
+// to live in device memory.
 #pragma once
 
 #include <cstdint>
@@ -22,15 +23,19 @@ struct PagedKV {
   int block_size;
 };
 
-// Per-request tables of one launch (all device pointers).
+// Work items of one launch.  An item is one (layer, request) pair: its
+// layer slot selects the paged tensor, tensor maps, quantizer parameters and
+// transform images; its block table rows select the request's blocks.
 struct ReqTable {
   const int32_t* block_table;  // concatenated physical block ids
-  const int32_t* bt_off;       // [R] first entry of request r
+  const int32_t* bt_off;       // [R] first entry of item r
   const int32_t* n_tokens;     // [R] valid tokens (statistics, written rows)
   const int32_t* n_rows;       // [R] rows = blocks * block_size
   const int32_t* tile_prefix;  // [R+1] cumulative 128-row tiles
-  const long long* code_off;   // [R] byte offset of the request's code region
-  const long long* meta_off;   // [R] byte offset of the request's fp16 metadata
+  const int32_t* slot;         // [R] layer slot of item r
+  const long long* code_off;   // [R] byte offset of the item's code region
+  const long long* meta_off;   // [R] byte offset of the item's fp16 metadata
+  const long long* row_off;    // [R] prefix of n_rows (value row-stat scratch)
   int num_req;
 };
 
@@ -44,7 +49,7 @@ struct LayerParams {
   int value_bits[kMaxHeads];
   int group_of_head[kMaxHeads];
   // seg_prefix[s] = sum over segments < s of bytes-per-row, segment s = kv*H + h;
-  // a request with n rows stores segment s at code_off + n*seg_prefix[s].
+  // an item with n rows stores segment s at code_off + n*seg_prefix[s].
   int seg_prefix[2 * kMaxHeads + 1];
   uint32_t sign_bits[kMaxHeads][4];  // bit d set <=> sign of channel d is -1
   int clamp_top;                     // 1: codes <= levels-1 ; 0: codes <= levels
@@ -52,19 +57,23 @@ struct LayerParams {
   float out_scale;                   // 1/sqrt(128) with the Hadamard, else 1
 };
 
-// One launch of a fused layer stage (producer or consumer side).
+// One launch of a fused stage over many items.
 struct LayerLaunch {
-  PagedKV kv;            // paged source (producer) or destination (consumer)
+  const PagedKV* kvs;      // [slots] paged source (producer) / destination (consumer)
+  const void* maps;        // [slots][2] CUtensorMap (64-B aligned), K and V planes
+  const LayerParams* lps;  // [slots]
   ReqTable rt;
-  LayerParams lp;
-  const uint8_t* bmat;   // [H][32768] swizzled bf16 transform images
-  uint8_t* codes;        // code region base (written by producer, read by consumer)
-  uint16_t* meta;        // fp16 metadata base
-  uint32_t* kstat;       // [R][H][128][2] order-mapped key min/max (producer)
-  uint32_t* err;         // device error word
+  const uint8_t* bmat;     // [slots][H][32768] swizzled bf16 transform images
+  long long bmat_stride;   // bytes per slot in bmat
+  uint8_t* codes;          // code region base (written by producer, read by consumer)
+  uint16_t* meta;          // fp16 metadata base
+  uint32_t* kstat;         // [R][H][128][2] order-mapped key min/max (producer)
+  float* vstat;            // [sum rows][H][2] per-row value min/max (producer)
+  uint32_t* err;           // device error word
   int total_tiles;
-  int engine;            // 0: tcgen05 + TMA ; 1: SIMT (in-register FWHT)
-  void* stream;          // cudaStream_t
+  int num_heads;           // H (identical for every slot of a launch)
+  int engine;              // 0: tcgen05 + TMA ; 1: SIMT (in-register FWHT)
+  void* stream;            // cudaStream_t
 };
 
 }  // namespace kvs

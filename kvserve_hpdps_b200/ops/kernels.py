@@ -253,85 +253,9 @@ def make_layer_plan(num_heads: int, key_levels, value_levels, seed: Optional[int
                      signs, packed=packed, clamp_top=clamp_top)
 
 
-# ------------------------------------------------------------ request batch
+# ------------------------------------------------------------ launch tables
 def _align16(x: int) -> int:
     return (x + 15) & ~15
-
-
-class RequestBatch:
-    """Block tables and per-request layout of one layer launch.
-
-    ``block_ids[r]`` are the request's physical blocks in the paged cache,
-    ``n_tokens[r]`` its valid tokens (statistics use only these; rows past
-    them in the last block are zero-coded).  Region offsets depend on the
-    plan (bits per segment), so they are computed per plan.
-    """
-
-    def __init__(self, block_ids: Sequence[Sequence[int]], n_tokens: Sequence[int],
-                 block_size: int, device: torch.device):
-        self.block_ids = [list(map(int, b)) for b in block_ids]
-        self.n_tokens = [int(n) for n in n_tokens]
-        self.block_size = int(block_size)
-        self.device = device
-        self.n_rows = [len(b) * self.block_size for b in self.block_ids]
-        self.tiles = [(r + TILE_ROWS - 1) // TILE_ROWS for r in self.n_rows]
-        self.total_tiles = sum(self.tiles)
-        R = len(self.block_ids)
-        bt, off = [], []
-        for b in self.block_ids:
-            off.append(len(bt))
-            bt.extend(b)
-        prefix = [0]
-        for t in self.tiles:
-            prefix.append(prefix[-1] + t)
-        ints = bt + off + self.n_tokens + self.n_rows + prefix
-        host = torch.tensor(ints if ints else [0], dtype=torch.int32)
-        if device.type == "cuda":
-            host = host.pin_memory()
-        self._ints = host.to(device, non_blocking=True)
-        self._o_bt, self._o_off = 0, len(bt)
-        self._o_ntok = self._o_off + R
-        self._o_rows = self._o_ntok + R
-        self._o_prefix = self._o_rows + R
-        self._layouts: dict[tuple, tuple] = {}
-
-    @property
-    def num_req(self) -> int:
-        return len(self.block_ids)
-
-    def layout(self, plan: LayerPlan) -> tuple[list[int], list[int], int, int, torch.Tensor]:
-        """(code_off, meta_off, code_bytes, meta_bytes, device int64 offsets)."""
-        key = (plan.row_bytes(), plan.n_groups, plan.num_heads)
-        if key not in self._layouts:
-            code_off, meta_off = [], []
-            c = m = 0
-            for rows in self.n_rows:
-                code_off.append(c)
-                meta_off.append(m)
-                c += _align16(rows * plan.row_bytes())
-                m += _align16(plan.meta_bytes(rows))
-            host = torch.tensor(code_off + meta_off, dtype=torch.int64)
-            if self.device.type == "cuda":
-                host = host.pin_memory()
-            self._layouts[key] = (code_off, meta_off, c, m, host.to(self.device, non_blocking=True))
-        return self._layouts[key]
-
-    def req_table(self, plan: LayerPlan) -> _lib.ReqTable:
-        _, _, _, _, offs = self.layout(plan)
-        base = self._ints.data_ptr()
-        rt = _lib.ReqTable()
-        rt.block_table = base + 4 * self._o_bt
-        rt.bt_off = base + 4 * self._o_off
-        rt.n_tokens = base + 4 * self._o_ntok
-        rt.n_rows = base + 4 * self._o_rows
-        rt.tile_prefix = base + 4 * self._o_prefix
-        rt.code_off = offs.data_ptr()
-        rt.meta_off = offs.data_ptr() + 8 * self.num_req
-        rt.num_req = self.num_req
-        return rt
-
-    def block_tensor(self) -> torch.Tensor:
-        return self._ints[self._o_bt:self._o_off]
 
 
 def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
@@ -348,75 +272,240 @@ def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
     H, D = kv_layer.shape[3], kv_layer.shape[4]
     if st[4] != 1 or st[3] != D or st[2] != H * D:
         raise ValueError("KV layer inner dims (bs, H, D) must be contiguous")
+    if kv_layer.shape[2] % 16:
+        raise ValueError("block_size must be a multiple of 16")
     p = PagedKV()
     p.base = kv_layer.data_ptr()
-    if kv_layer.shape[0] == 2 and kv_layer.shape[1] != 2:
-        p.kv_stride, p.block_stride = st[0], st[1]
-        p.num_blocks = kv_layer.shape[1]
-    elif kv_layer.shape[1] == 2:
+    if kv_layer.shape[1] == 2 and kv_layer.shape[0] != 2:
         p.block_stride, p.kv_stride = st[0], st[1]
         p.num_blocks = kv_layer.shape[0]
-    else:  # shape[0] == shape[1] == 2: treat as FlashAttention layout
+    else:
         p.kv_stride, p.block_stride = st[0], st[1]
         p.num_blocks = kv_layer.shape[1]
     p.block_size = kv_layer.shape[2]
     return p
 
 
+class LayerSlots:
+    """Device-side description of the layers one launch can address.
+
+    Slot i pairs a paged KV tensor with its LayerPlan.  Holds the device
+    arrays of PagedKV records, TMA tensor maps (K and V plane per slot),
+    LayerParams and the forward/inverse transform images.  All plans must
+    have the same number of heads.
+    """
+
+    def __init__(self, kv_layers: Sequence[torch.Tensor], plans: Sequence[LayerPlan]):
+        if len(kv_layers) != len(plans) or not plans:
+            raise ValueError("one plan per KV layer tensor is required")
+        self.kv_layers = list(kv_layers)
+        self.plans = list(plans)
+        self.device = kv_layers[0].device
+        self.num_heads = plans[0].num_heads
+        if any(p.num_heads != self.num_heads for p in plans):
+            raise ValueError("all slots of a launch must have the same number of heads")
+        for t in kv_layers:
+            if t.shape[3] != self.num_heads:
+                raise ValueError(f"KV tensor has {t.shape[3]} heads, plan has {self.num_heads}")
+        n = len(plans)
+        kvs = (PagedKV * n)(*[paged_kv(t) for t in kv_layers])
+        lps = (_lib.LayerParams * n)(*[p.params() for p in plans])
+        maps = (ctypes.c_uint8 * (256 * n))()
+        if self.device.type == "cuda":
+            for i in range(n):
+                rc = lib().kvs_make_plane_maps(ctypes.byref(kvs[i]), self.num_heads,
+                                               ctypes.addressof(maps) + 256 * i)
+                check(rc, "make_plane_maps")
+        self._kvs = self._to_dev(bytes(kvs))
+        self._lps = self._to_dev(bytes(lps))
+        self._maps = self._to_dev(bytes(maps))
+        fwd, inv = zip(*[p.images(torch.device("cpu")) for p in plans])
+        self.bmat_stride = self.num_heads * 32768
+        self.bmat_fwd = torch.cat(fwd).to(self.device)
+        self.bmat_inv = torch.cat(inv).to(self.device)
+
+    def _to_dev(self, raw: bytes) -> torch.Tensor:
+        t = torch.frombuffer(bytearray(raw), dtype=torch.uint8).clone()
+        return t.to(self.device) if self.device.type == "cuda" else t
+
+    @classmethod
+    def single(cls, kv_layer: torch.Tensor, plan: LayerPlan) -> "LayerSlots":
+        return cls([kv_layer], [plan])
+
+
+class WorkItems:
+    """Work items of a launch: (slot, block ids, valid tokens) triples.
+
+    Codes of item r start at ``code_off[r]`` (segments ``[kv][head][row]``
+    of ``16*bits`` bytes), its fp16 metadata at ``meta_off[r]``.
+    """
+
+    def __init__(self, slots: LayerSlots, items: Sequence[tuple[int, Sequence[int], int]]):
+        self.slots = slots
+        self.items = [(int(s), list(map(int, b)), int(n)) for s, b, n in items]
+        dev = slots.device
+        self.device = dev
+        bs = [slots.kv_layers[s].shape[2] for s, _, _ in self.items]
+        self.n_rows = [len(b) * k for (_, b, _), k in zip(self.items, bs)]
+        self.n_tokens = [n for _, _, n in self.items]
+        self.tiles = [(r + TILE_ROWS - 1) // TILE_ROWS for r in self.n_rows]
+        self.total_tiles = sum(self.tiles)
+        R = len(self.items)
+        bt, off = [], []
+        for _, b, _ in self.items:
+            off.append(len(bt))
+            bt.extend(b)
+        prefix = [0]
+        for t in self.tiles:
+            prefix.append(prefix[-1] + t)
+        self.code_off, self.meta_off, self.row_off = [], [], []
+        c = m = ro = 0
+        for (s, _, _), rows in zip(self.items, self.n_rows):
+            plan = slots.plans[s]
+            self.code_off.append(c)
+            self.meta_off.append(m)
+            self.row_off.append(ro)
+            c += _align16(rows * plan.row_bytes())
+            m += _align16(plan.meta_bytes(rows))
+            ro += rows
+        self.code_bytes, self.meta_bytes, self.total_rows = c, m, ro
+        ints = bt + off + self.n_tokens + self.n_rows + prefix + [s for s, _, _ in self.items]
+        longs = self.code_off + self.meta_off + self.row_off
+        hi = torch.tensor(ints if ints else [0], dtype=torch.int32)
+        hl = torch.tensor(longs if longs else [0], dtype=torch.int64)
+        if dev.type == "cuda":
+            hi, hl = hi.pin_memory(), hl.pin_memory()
+        self._ints = hi.to(dev, non_blocking=True)
+        self._longs = hl.to(dev, non_blocking=True)
+        self._o = {"bt": 0, "off": len(bt), "ntok": len(bt) + R, "rows": len(bt) + 2 * R,
+                   "prefix": len(bt) + 3 * R, "slot": len(bt) + 4 * R + 1}
+
+    @property
+    def num_items(self) -> int:
+        return len(self.items)
+
+    def req_table(self) -> _lib.ReqTable:
+        R = self.num_items
+        base = self._ints.data_ptr()
+        lb = self._longs.data_ptr()
+        rt = _lib.ReqTable()
+        rt.block_table = base + 4 * self._o["bt"]
+        rt.bt_off = base + 4 * self._o["off"]
+        rt.n_tokens = base + 4 * self._o["ntok"]
+        rt.n_rows = base + 4 * self._o["rows"]
+        rt.tile_prefix = base + 4 * self._o["prefix"]
+        rt.slot = base + 4 * self._o["slot"]
+        rt.code_off = lb
+        rt.meta_off = lb + 8 * R
+        rt.row_off = lb + 16 * R
+        rt.num_req = R
+        return rt
+
+    def item_codes(self, codes: torch.Tensor, r: int) -> torch.Tensor:
+        plan = self.slots.plans[self.items[r][0]]
+        return codes[self.code_off[r]:self.code_off[r] + self.n_rows[r] * plan.row_bytes()]
+
+    def item_meta(self, meta: torch.Tensor, r: int) -> torch.Tensor:
+        plan = self.slots.plans[self.items[r][0]]
+        return meta[self.meta_off[r]:self.meta_off[r] + plan.meta_bytes(self.n_rows[r])]
+
+
+class RequestBatch:
+    """Single-layer convenience: requests of one layer (slot 0)."""
+
+    def __init__(self, block_ids: Sequence[Sequence[int]], n_tokens: Sequence[int],
+                 block_size: int, device: torch.device):
+        self.block_ids = [list(map(int, b)) for b in block_ids]
+        self.n_tokens = [int(n) for n in n_tokens]
+        self.block_size = int(block_size)
+        self.device = device
+        self.n_rows = [len(b) * self.block_size for b in self.block_ids]
+        self._items: dict[int, WorkItems] = {}
+
+    def items_for(self, slots: LayerSlots) -> WorkItems:
+        key = id(slots)
+        if key not in self._items:
+            self._items[key] = WorkItems(slots, [(0, b, n) for b, n in zip(self.block_ids, self.n_tokens)])
+        return self._items[key]
+
+    def layout(self, plan: LayerPlan) -> tuple[list[int], list[int], int, int]:
+        code_off, meta_off = [], []
+        c = m = 0
+        for rows in self.n_rows:
+            code_off.append(c)
+            meta_off.append(m)
+            c += _align16(rows * plan.row_bytes())
+            m += _align16(plan.meta_bytes(rows))
+        return code_off, meta_off, c, m
+
+
 # ---------------------------------------------------------------- fused ops
-def _launch(kv_layer, batch, plan, bmat, codes, meta, kstat, engine) -> LayerLaunch:
-    dev = kv_layer.device
+def _launch(slots: LayerSlots, items: WorkItems, bmat: torch.Tensor, codes, meta, kstat, vstat,
+            engine: int) -> LayerLaunch:
+    dev = slots.device
     L = LayerLaunch()
-    L.kv = paged_kv(kv_layer)
-    L.rt = batch.req_table(plan)
-    L.lp = plan.params()
+    L.kvs = slots._kvs.data_ptr()
+    L.maps = slots._maps.data_ptr()
+    L.lps = slots._lps.data_ptr()
+    L.rt = items.req_table()
     L.bmat = bmat.data_ptr()
+    L.bmat_stride = slots.bmat_stride
     L.codes = codes.data_ptr()
     L.meta = meta.data_ptr()
     L.kstat = 0 if kstat is None else kstat.data_ptr()
+    L.vstat = 0 if vstat is None else vstat.data_ptr()
     L.err = workspace(dev).err.data_ptr()
-    L.total_tiles = batch.total_tiles
+    L.total_tiles = items.total_tiles
+    L.num_heads = slots.num_heads
     L.engine = engine
     L.stream = _stream(dev)
     return L
 
 
-def quantize_layer(kv_layer: torch.Tensor, batch: RequestBatch, plan: LayerPlan,
-                   codes: Optional[torch.Tensor] = None, meta: Optional[torch.Tensor] = None,
-                   engine: int = ENGINE_TCGEN05) -> tuple[torch.Tensor, torch.Tensor]:
-    """Quantize every request of one layer; returns (codes u8, meta u8).
-
-    ``codes`` holds, per request at ``batch.layout(plan)[0][r]``, the
-    segments ``[kv][head][row][16*bits]``; ``meta`` holds per request the
-    fp16 arrays ``kmin[H,128] kscale[H,128] vmin[G,rows] vscale[G,rows]``.
-    """
-    dev = kv_layer.device
-    _, _, cbytes, mbytes, _ = batch.layout(plan)
+def quantize(slots: LayerSlots, items: WorkItems, codes: Optional[torch.Tensor] = None,
+             meta: Optional[torch.Tensor] = None,
+             engine: int = ENGINE_TCGEN05) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantize every work item (layer, request) in three launches; returns
+    (codes u8, meta u8) laid out as described by ``items``."""
+    dev = slots.device
     ws = workspace(dev)
     if codes is None:
-        codes = torch.empty(max(cbytes, 16), dtype=torch.uint8, device=dev)
+        codes = torch.empty(max(items.code_bytes, 16), dtype=torch.uint8, device=dev)
     if meta is None:
-        meta = torch.empty(max(mbytes, 16), dtype=torch.uint8, device=dev)
-    n_pairs = batch.num_req * plan.num_heads * HEAD_DIM
+        meta = torch.empty(max(items.meta_bytes, 16), dtype=torch.uint8, device=dev)
+    n_pairs = items.num_items * slots.num_heads * HEAD_DIM
     kstat = ws.buf("kstat", 8 * n_pairs, torch.int32)
-    fwd, _ = plan.images(dev)
-    L = _launch(kv_layer, batch, plan, fwd, codes, meta, kstat, engine)
+    vstat = ws.buf("vstat", 8 * items.total_rows * slots.num_heads, torch.float32)
+    L = _launch(slots, items, slots.bmat_fwd, codes, meta, kstat, vstat, engine)
     lb = lib()
     check(lb.kvs_init_key_stats(kstat.data_ptr(), n_pairs, L.stream), "init_key_stats")
-    check(lb.kvs_key_stats(ctypes.byref(L)), "key_stats")
-    check(lb.kvs_quant_k(ctypes.byref(L)), "quant_k")
-    check(lb.kvs_quant_v(ctypes.byref(L)), "quant_v")
+    check(lb.kvs_stats(ctypes.byref(L)), "stats")
+    check(lb.kvs_quant(ctypes.byref(L)), "quant")
     return codes, meta
 
 
-def dequantize_layer(codes: torch.Tensor, meta: torch.Tensor, dst_layer: torch.Tensor,
-                     batch: RequestBatch, plan: LayerPlan, engine: int = ENGINE_TCGEN05) -> None:
-    """Dequantize + inverse transform every request of one layer into the
-    paged destination ``dst_layer`` at ``batch``'s block ids."""
-    dev = dst_layer.device
-    _, inv = plan.images(dev)
-    L = _launch(dst_layer, batch, plan, inv, codes, meta, None, engine)
+def dequantize(codes: torch.Tensor, meta: torch.Tensor, dst_slots: LayerSlots, items: WorkItems,
+               engine: int = ENGINE_TCGEN05) -> None:
+    """Dequantize + inverse transform every item into its destination slot
+    (paged cache) at the item's block ids (one launch)."""
+    L = _launch(dst_slots, items, dst_slots.bmat_inv, codes, meta, None, None, engine)
     check(lib().kvs_dequant_inverse(ctypes.byref(L)), "dequant_inverse")
+
+
+def quantize_layer(kv_layer: torch.Tensor, batch: RequestBatch, plan: LayerPlan,
+                   codes: Optional[torch.Tensor] = None, meta: Optional[torch.Tensor] = None,
+                   engine: int = ENGINE_TCGEN05,
+                   slots: Optional[LayerSlots] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Single-layer form of :func:`quantize` (codes at batch.layout(plan))."""
+    slots = slots or LayerSlots.single(kv_layer, plan)
+    return quantize(slots, batch.items_for(slots), codes, meta, engine)
+
+
+def dequantize_layer(codes: torch.Tensor, meta: torch.Tensor, dst_layer: torch.Tensor,
+                     batch: RequestBatch, plan: LayerPlan, engine: int = ENGINE_TCGEN05,
+                     slots: Optional[LayerSlots] = None) -> None:
+    slots = slots or LayerSlots.single(dst_layer, plan)
+    dequantize(codes, meta, slots, batch.items_for(slots), engine)
 
 
 # ------------------------------------------------------------------- codec

@@ -91,7 +91,7 @@ def test_quantize_matches_oracle(engine, H, packed):
 
 def _oracle_buffers(dense_list, plan, batch, tokens):
     """Codes/meta buffers in the device layout built from the oracle."""
-    _, _, cbytes, mbytes, _ = batch.layout(plan)
+    _, _, cbytes, mbytes = batch.layout(plan)
     codes = torch.zeros(cbytes, dtype=torch.uint8)
     meta = torch.zeros(mbytes, dtype=torch.uint8)
     refs = []
@@ -171,6 +171,50 @@ def test_round_trip_error_close_to_oracle(engine):
         exp = oracle.error_metrics(s.cpu(), exp_rec.view(2, nb * 16, H, 128)[:, :t])
         assert abs(got["cosine"] - exp["cosine"]) < 2e-3
         assert abs(got["rel_mse"] - exp["rel_mse"]) < 2e-2 * max(exp["rel_mse"], 1e-6) + 1e-4
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+def test_multi_layer_launch_matches_oracle(engine):
+    """One launch over several layers with different plans (levels, signs,
+    packing) and several requests per layer."""
+    H, tokens, L = 4, [200, 96], 3
+    wl = paged_workload(L, tokens, H, device="cuda", seed=77)
+    plans = [
+        K.make_layer_plan(H, [12, 6, 12, 6], [8, 4, 4, 8], 0x3333, 0),
+        K.make_layer_plan(H, [16, 16, 16, 16], [16, 16, 16, 16], 0x3333, 1, packed=True),
+        K.make_layer_plan(H, [6, 6, 12, 12], [4, 4, 8, 8], None, 2),
+    ]
+    slots = K.LayerSlots([wl.cache[l] for l in range(L)], plans)
+    items = K.WorkItems(slots, [(l, b, t) for l in range(L) for b, t in zip(wl.block_ids, tokens)])
+    codes, meta = K.quantize(slots, items, engine=engine)
+    dst = torch.zeros_like(wl.cache)
+    dslots = K.LayerSlots([dst[l] for l in range(L)], plans)
+    K.dequantize(codes, meta, dslots, items, engine=engine)
+    torch.cuda.synchronize()
+    K.check_device_error(wl.cache.device)
+    for r, (l, blocks, t) in enumerate(items.items):
+        plan = plans[l]
+        dense = gather_request(wl.cache[l], blocks).cpu()
+        ref = oracle.compress_layer(dense, torch.tensor(plan.key_levels),
+                                    torch.tensor(plan.value_levels), plan.signs, n_valid=t)
+        rows = items.n_rows[r]
+        cr = items.item_codes(codes, r).cpu()
+        got = torch.empty((2, H, rows, 128), dtype=torch.uint8)
+        for kv in range(2):
+            for h in range(H):
+                bits = (plan.key_bits if kv == 0 else plan.value_bits)[h]
+                st = rows * plan.seg_prefix[kv * H + h]
+                seg = cr[st:st + rows * 16 * bits]
+                got[kv, h] = seg.view(rows, 128) if bits == 8 else K.bitunpack(seg, bits)
+        _check_codes(got, ref["codes"].reshape(2, H, rows, 128))
+        exp = oracle.decompress_layer(ref["codes"], ref["key_min"], ref["key_scale"],
+                                      ref["value_min"], ref["value_scale"], ref["groups"],
+                                      plan.signs)
+        rec = gather_request(dst[l], blocks).cpu()
+        nb = len(blocks)
+        torch.testing.assert_close(rec.view(2, nb * 16, H, 128)[:, :t].float(),
+                                   exp.view(2, nb * 16, H, 128)[:, :t].float(),
+                                   rtol=1.6e-2, atol=4e-3)
 
 
 def test_engines_agree():
