@@ -1,0 +1,460 @@
+"""Default-mode compression manager on the fused sm_100a kernels.
+
+This is the default backend (reference: the TileLang manager,
+kvserve_v1/compression/tilelang_manager.py).  It offers the same surface:
+
+* whole-request: :meth:`compress_all_layers` / :meth:`decompress_all_layers`;
+* per-layer overlap API: :meth:`compress_quant_layer`, :meth:`finalize_codec`,
+  :meth:`compress_layer_full`, :meth:`finalize_chunked`,
+  :meth:`finalize_layer_group`, :meth:`decompress_layer_group`;
+
+and adds the paged fast path used by this framework's connector and
+benchmark: :meth:`quantize_paged` reads every (layer, request) item straight
+from the paged caches through block tables in one set of launches, and
+:meth:`dequantize_paged` scatters into the consumer's paged caches.
+
+Wire form (unchanged from the reference so envelopes interoperate):
+codes are ``uint8 [L, 2, H, B, bs, D]`` heads-outer; each layer's
+``quantization_params`` entry is ``{"key_meta": {"min_val": fp16[H, D],
+"quant_scale": fp16[H, D], "axis": "channel"}, "value_meta":
+{"per_group_list": [{"head_idx": int64[n], "min_val": fp16[rows, 1, 1],
+"quant_scale": fp16[rows, 1, 1]}, ...]}}``.  The code buffer is then
+entropy-coded by this framework's codec (``codec.py``); when the codec is
+``bitpack`` the kernels write bit-packed codes directly and the per-segment
+bit widths travel as ``code_bits``.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass
+from typing import Any, Optional, Sequence
+
+import torch
+
+from kvserve_hpdps_b200.compression.codec import decode_bytes, encode_bytes, resolve_codec
+from kvserve_hpdps_b200.compression.config import (DEFAULT_HADAMARD_SEED, FUSED_QUANTIZER_DEFAULTS,
+                                                   CompressedKVData)
+from kvserve_hpdps_b200.compression.head_scores import HybridPrecisionPlan
+from kvserve_hpdps_b200.utils.logger import get_logger
+
+logger = get_logger(__name__)
+
+BACKEND = "kvs_fused"
+
+
+def _engine_from_env() -> int:
+    v = os.environ.get("KVSERVE_ENGINE", "tcgen05").lower()
+    return 1 if v in ("simt", "1") else 0
+
+
+@dataclass
+class PagedBatch:
+    """Result of :meth:`FusedCompressionManager.quantize_paged`."""
+    codes: torch.Tensor          # uint8 code buffer (items in order)
+    meta: torch.Tensor           # uint8 view of the fp16 metadata buffer
+    items: Any                   # ops.kernels.WorkItems
+    layer_ids: list[int]         # layer id of each slot
+    plans: list[Any]             # LayerPlan of each slot
+
+    def item_nbytes(self, r: int) -> int:
+        plan = self.plans[self.items.items[r][0]]
+        return self.items.n_rows[r] * plan.row_bytes() + plan.meta_bytes(self.items.n_rows[r])
+
+
+class FusedCompressionManager:
+    """Hadamard + hybrid quantization + codec on the fused kernels."""
+
+    backend = BACKEND
+
+    def __init__(self, num_kv_heads: int, head_size: int, quantizer_config: Optional[dict],
+                 codec_config: Optional[dict], base_seed: int = DEFAULT_HADAMARD_SEED,
+                 tp_rank: int = 0, tp_size: int = 1, transform: bool = True,
+                 engine: Optional[int] = None, num_layers: Optional[int] = None):
+        if head_size != 128:
+            raise ValueError(f"the fused path needs head_size 128, got {head_size}")
+        qc = dict(FUSED_QUANTIZER_DEFAULTS)
+        qc.update(quantizer_config or {})
+        self.quantizer_config = qc
+        self.codec_config = dict(codec_config or {})
+        self.codec = resolve_codec(self.codec_config.get("codec_type", "nvcomp"),
+                                   self.codec_config.get("nvcomp_algorithm", "ANS"))
+        self.packed = self.codec == "bitpack"
+        self.stream_codec = "rans" if self.codec == "rans" else "none"
+        self.num_kv_heads = int(num_kv_heads)
+        self.head_size = int(head_size)
+        self.base_seed = int(base_seed) if transform else None
+        self.tp_rank, self.tp_size = int(tp_rank), int(tp_size)
+        self.engine = _engine_from_env() if engine is None else int(engine)
+        self.hybrid = HybridPrecisionPlan(
+            num_layers, self.num_kv_heads, qc.get("model_name"), qc["hybrid_ratio"],
+            qc["high_key_max_value"], qc["high_value_max_value"], qc["low_key_max_value"],
+            qc["low_value_max_value"], qc.get("split_type", "head"), self.tp_rank, self.tp_size)
+        self._plans: dict[int, Any] = {}
+        self._slot_cache: dict[tuple, Any] = {}
+        self._last_decompress_timing: Optional[dict] = None
+        logger.info("fused manager: heads=%d codec=%s packed=%s engine=%d seed=%s",
+                    self.num_kv_heads, self.codec, self.packed, self.engine, self.base_seed)
+
+    # ----------------------------------------------------------- plans
+    def plan(self, layer_id: int):
+        from kvserve_hpdps_b200.ops import kernels as K
+        layer_id = int(layer_id)
+        if layer_id not in self._plans:
+            self._plans[layer_id] = K.make_layer_plan(
+                self.num_kv_heads, self.hybrid.key_levels_for(layer_id).tolist(),
+                self.hybrid.value_levels_for(layer_id).tolist(), self.base_seed, layer_id,
+                packed=self.packed)
+        return self._plans[layer_id]
+
+    def _slots(self, tensors: Sequence[torch.Tensor], plans: Sequence[Any]):
+        from kvserve_hpdps_b200.ops import kernels as K
+        key = tuple((t.data_ptr(), tuple(t.shape), tuple(t.stride())) for t in tensors) + \
+            tuple(id(p) for p in plans)
+        sl = self._slot_cache.get(key)
+        if sl is None:
+            if len(self._slot_cache) > 64:
+                self._slot_cache.clear()
+            sl = K.LayerSlots(list(tensors), list(plans))
+            self._slot_cache[key] = sl
+        return sl
+
+    def supports_overlap(self) -> bool:
+        return True
+
+    # --------------------------------------------------- paged fast path
+    def quantize_paged(self, kv_layers: Sequence[torch.Tensor], layer_ids: Sequence[int],
+                       requests: Sequence[tuple[Sequence[int], int]],
+                       codes: Optional[torch.Tensor] = None,
+                       meta: Optional[torch.Tensor] = None) -> PagedBatch:
+        """Quantize every (layer, request) item: ``kv_layers[i]`` is the paged
+        cache of layer ``layer_ids[i]``; ``requests`` are (block ids, valid
+        tokens).  Items are ordered layer-major, so for one request the code
+        buffer is the reference's ``[L, 2, H, B, bs, D]`` layout."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        plans = [self.plan(l) for l in layer_ids]
+        slots = self._slots(kv_layers, plans)
+        items = K.WorkItems(slots, [(i, b, n) for i in range(len(kv_layers)) for b, n in requests])
+        codes, meta = K.quantize(slots, items, codes, meta, engine=self.engine)
+        return PagedBatch(codes, meta, items, list(layer_ids), plans)
+
+    def dequantize_paged(self, batch: PagedBatch, dst_layers: Sequence[torch.Tensor],
+                         dst_requests: Optional[Sequence[tuple[Sequence[int], int]]] = None,
+                         codes: Optional[torch.Tensor] = None,
+                         meta: Optional[torch.Tensor] = None) -> None:
+        """Dequantize ``batch`` into the destination paged caches (one per
+        layer of the batch) at ``dst_requests`` block ids (default: the
+        producer's)."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        slots = self._slots(dst_layers, batch.plans)
+        if dst_requests is None:
+            items = K.WorkItems(slots, batch.items.items)
+        else:
+            items = K.WorkItems(slots, [(i, b, n) for i in range(len(dst_layers))
+                                        for b, n in dst_requests])
+        K.dequantize(batch.codes if codes is None else codes,
+                     batch.meta if meta is None else meta, slots, items, engine=self.engine)
+
+    def compress_paged_requests(self, kv_layers: Sequence[torch.Tensor], layer_ids: Sequence[int],
+                                requests: Sequence[tuple[Sequence[int], int]],
+                                member_tids: Optional[Sequence[str]] = None,
+                                trim: bool = True) -> CompressedKVData:
+        """Compress the given layers of several requests into ONE message:
+        one codec stream over every (layer, request) item, layer-major.
+
+        Metadata: ``grouped=True, layout="items"``, ``member_tids``,
+        ``member_tokens``, ``member_blocks``, ``layer_ids`` and one wire-form
+        ``quantization_params`` entry per item (layer-major)."""
+        batch = self.quantize_paged(kv_layers, layer_ids, requests)
+        body = encode_bytes(batch.codes[:batch.items.code_bytes], self.stream_codec) if trim \
+            else self._encode_untrimmed(batch.codes[:batch.items.code_bytes])
+        items = batch.items
+        qparams = [self.canon_meta(batch.meta, items.meta_off[r], batch.plans[items.items[r][0]],
+                                   items.n_rows[r]) for r in range(items.num_items)]
+        H = self.num_kv_heads
+        meta = {"grouped": True, "layout": "items", "layer_ids": [int(l) for l in layer_ids],
+                "member_tids": list(member_tids) if member_tids else
+                [str(i) for i in range(len(requests))],
+                "member_tokens": [int(n) for _, n in requests],
+                "member_blocks": [len(b) for b, _ in requests],
+                "block_size": int(kv_layers[0].shape[2]), "num_heads": H,
+                "device": str(batch.codes.device), "quantization_params": qparams,
+                "code_bytes": int(items.code_bytes), "backend": BACKEND, "codec": self.codec,
+                "stream_codec": self.stream_codec, "transform_seed": self.base_seed}
+        orig = sum(len(kv_layers) * 2 * n * H * self.head_size * 2 for _, n in requests)
+        self._last_batch = batch
+        return CompressedKVData(request_id="grp", layer_id=int(layer_ids[-1]),
+                                compressed_tensor=body, metadata=meta, original_size=orig,
+                                compressed_size=int(body.numel()))
+
+    def _encode_untrimmed(self, codes: torch.Tensor) -> torch.Tensor:
+        from kvserve_hpdps_b200.compression.codec import _header
+        from kvserve_hpdps_b200.ops import kernels as K
+        if self.stream_codec != "rans":
+            return encode_bytes(codes, self.stream_codec)
+        hdr = _header("rans", codes.numel(), codes.device)
+        out = torch.empty(16 + K.rans_max_bytes(codes.numel()), dtype=torch.uint8,
+                          device=codes.device)
+        out[:16] = hdr
+        K.rans_encode(codes, out=out[16:], trim=False)
+        return out
+
+    def decompress_paged_requests(self, compressed: CompressedKVData,
+                                  dst_layers: Sequence[torch.Tensor],
+                                  dst_requests: Sequence[tuple[Sequence[int], int]]) -> None:
+        """Inverse of :meth:`compress_paged_requests` into the consumer's
+        paged caches (``dst_layers[i]`` for the message's i-th layer) at the
+        consumer's block ids."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        meta = compressed.metadata
+        device = dst_layers[0].device
+        codes = decode_bytes(compressed.compressed_tensor, device)
+        layer_ids = meta["layer_ids"]
+        seed = meta.get("transform_seed", self.base_seed)
+        qp = meta["quantization_params"]
+        R = len(dst_requests)
+        plans = [self.plan_from_canon(qp[i * R], layer_ids[i], seed) for i in range(len(layer_ids))]
+        slots = self._slots(dst_layers, plans)
+        items = K.WorkItems(slots, [(i, b, n) for i in range(len(dst_layers)) for b, n in dst_requests])
+        meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=device)
+        for r in range(items.num_items):
+            m = self.meta_from_canon(qp[r])
+            meta_buf[items.meta_off[r]:items.meta_off[r] + m.numel()] = m.to(device)
+        K.dequantize(codes, meta_buf, slots, items, engine=self.engine)
+
+    # ------------------------------------------------------ canon metadata
+    def canon_meta(self, meta: torch.Tensor, off: int, plan, rows: int) -> dict:
+        """Wire-form metadata of one item (views into ``meta``)."""
+        H, G = plan.num_heads, plan.n_groups
+        f = meta[off:off + plan.meta_bytes(rows)].view(torch.float16)
+        kmin = f[:H * 128].view(H, 128)
+        ksc = f[H * 128:2 * H * 128].view(H, 128)
+        vmin = f[2 * H * 128:2 * H * 128 + G * rows].view(G, rows)
+        vsc = f[2 * H * 128 + G * rows:2 * H * 128 + 2 * G * rows].view(G, rows)
+        groups = [{"head_idx": torch.tensor(plan.groups[g], dtype=torch.int64, device=meta.device),
+                   "min_val": vmin[g].view(rows, 1, 1), "quant_scale": vsc[g].view(rows, 1, 1)}
+                  for g in range(G)]
+        out = {"key_meta": {"min_val": kmin, "quant_scale": ksc, "axis": "channel"},
+               "value_meta": {"per_group_list": groups}}
+        if plan.packed:
+            out["code_bits"] = list(plan.key_bits) + list(plan.value_bits)
+        return out
+
+    def plan_from_canon(self, canon: dict, layer_id: int, seed: Optional[int]):
+        """Consumer-side plan rebuilt from one item's wire metadata."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        H = int(canon["key_meta"]["min_val"].shape[0])
+        goh = [0] * H
+        for g, grp in enumerate(canon["value_meta"]["per_group_list"]):
+            for h in grp["head_idx"].tolist():
+                goh[int(h)] = g
+        bits = list(canon.get("code_bits") or [8] * (2 * H))
+        key = (H, tuple(goh), tuple(bits), seed, int(layer_id))
+        cache = self.__dict__.setdefault("_decode_plans", {})
+        if key not in cache:
+            cache[key] = K.decode_plan(H, goh, bits[:H], bits[H:], seed, layer_id)
+        return cache[key]
+
+    @staticmethod
+    def meta_from_canon(canon: dict) -> torch.Tensor:
+        """Device-layout fp16 metadata (uint8 view) of one item."""
+        km = canon["key_meta"]
+        parts = [km["min_val"].reshape(-1), km["quant_scale"].reshape(-1)]
+        groups = canon["value_meta"]["per_group_list"]
+        parts += [g["min_val"].reshape(-1) for g in groups]
+        parts += [g["quant_scale"].reshape(-1) for g in groups]
+        return torch.cat([p.to(torch.float16) for p in parts]).view(torch.uint8)
+
+    # ------------------------------------------------------- whole request
+    def compress_all_layers(self, all_layers_data: torch.Tensor, request_id: str,
+                            config: Any = None, metadata: Optional[dict] = None
+                            ) -> Optional[CompressedKVData]:
+        """Compress a dense ``[L, 2, B, bs, H, D]`` request."""
+        if not isinstance(all_layers_data, torch.Tensor) or all_layers_data.dim() != 6:
+            logger.error("expected a 6-D tensor, got %s", getattr(all_layers_data, "shape", None))
+            return None
+        x = all_layers_data.contiguous()
+        L, _, B, bs, H, D = x.shape
+        t0 = time.monotonic()
+        batch = self.quantize_paged([x[l] for l in range(L)], list(range(L)),
+                                    [(list(range(B)), B * bs)])
+        body = encode_bytes(batch.codes[:batch.items.code_bytes], self.stream_codec)
+        if body.is_cuda:
+            torch.cuda.synchronize(body.device)
+        t_ms = (time.monotonic() - t0) * 1e3
+        qparams = [self.canon_meta(batch.meta, batch.items.meta_off[l], batch.plans[l],
+                                   batch.items.n_rows[l]) for l in range(L)]
+        meta = {
+            "request_id": request_id, "num_layers": L, "codec_applied": True,
+            "codec_shape": [L, 2, H, B, bs, D], "codec_dtype": "uint8",
+            "device": str(x.device), "original_dtype": str(x.dtype).replace("torch.", ""),
+            "original_shape": list(x.shape), "quantization_params": qparams,
+            "backend": BACKEND, "codec": self.codec, "transform_seed": self.base_seed,
+            "t_quant_ms": t_ms, "t_codec_ms": 0.0,
+        }
+        meta.update(metadata or {})
+        return CompressedKVData(request_id=request_id, layer_id=L - 1, compressed_tensor=body,
+                                metadata=meta, original_size=x.numel() * x.element_size(),
+                                compressed_size=body.numel())
+
+    def decompress_all_layers(self, compressed: CompressedKVData, config: Any = None
+                              ) -> Optional[torch.Tensor]:
+        if compressed.is_chunked:
+            return self._decompress_chunked(compressed)
+        meta = compressed.metadata
+        L = int(meta["num_layers"])
+        _, _, H, B, bs, D = [int(s) for s in meta["codec_shape"]]
+        device = torch.device(meta.get("device", "cuda"))
+        t0 = time.monotonic()
+        codes = decode_bytes(compressed.compressed_tensor, device)
+        t_codec = (time.monotonic() - t0) * 1e3
+        out = torch.empty((L, 2, B, bs, H, D), dtype=torch.bfloat16, device=device)
+        self._dequant_dense(codes, meta["quantization_params"], list(range(L)), out,
+                            meta.get("transform_seed", self.base_seed))
+        if out.is_cuda:
+            torch.cuda.synchronize(device)
+        self._last_decompress_timing = {"t_codec_decode_ms": t_codec,
+                                        "t_dequant_ms": (time.monotonic() - t0) * 1e3 - t_codec}
+        return out
+
+    def _dequant_dense(self, codes: torch.Tensor, qparams: Sequence[dict],
+                       layer_ids: Sequence[int], out: torch.Tensor, seed) -> None:
+        """Dequantize per-layer items of one request into dense ``out``
+        ``[L, 2, B, bs, H, D]`` (codes concatenated layer-major)."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        L, _, B, bs = out.shape[:4]
+        plans = [self.plan_from_canon(qparams[i], layer_ids[i], seed) for i in range(L)]
+        metas = [self.meta_from_canon(q) for q in qparams]
+        slots = K.LayerSlots([out[i] for i in range(L)], plans)
+        items = K.WorkItems(slots, [(i, list(range(B)), B * bs) for i in range(L)])
+        meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=out.device)
+        for i, m in enumerate(metas):
+            meta_buf[items.meta_off[i]:items.meta_off[i] + m.numel()] = m.to(out.device)
+        codes = codes.to(out.device)
+        if codes.numel() < items.code_bytes:
+            raise ValueError("code buffer shorter than the layout requires")
+        K.dequantize(codes, meta_buf, slots, items, engine=self.engine)
+
+    # ----------------------------------------------- per-layer overlap API
+    def compress_quant_layer(self, kv_layer: torch.Tensor, layer_id: int):
+        """Quantize one dense layer ``[2, B, bs, H, D]``; returns
+        (codes u8 ``[2, H, B, bs, D]`` or packed bytes, canon meta)."""
+        x = kv_layer.contiguous()
+        _, B, bs, H, D = x.shape
+        batch = self.quantize_paged([x], [layer_id], [(list(range(B)), B * bs)])
+        codes = batch.codes[:batch.items.code_bytes]
+        if not self.packed:
+            codes = codes.view(2, H, B, bs, D)
+        canon = self.canon_meta(batch.meta, 0, batch.plans[0], B * bs)
+        return codes, canon
+
+    def finalize_codec(self, q_perm_layers, canon_metas, request_id, original_dtype,
+                       original_shape) -> CompressedKVData:
+        buf = torch.cat([q.reshape(-1) for q in q_perm_layers])
+        body = encode_bytes(buf, self.stream_codec)
+        L = len(q_perm_layers)
+        _, _, B, bs, H, D = [int(s) for s in original_shape]
+        meta = {"request_id": request_id, "num_layers": L, "codec_applied": True,
+                "codec_shape": [L, 2, H, B, bs, D], "codec_dtype": "uint8",
+                "device": str(buf.device), "original_dtype": original_dtype,
+                "original_shape": list(original_shape), "quantization_params": list(canon_metas),
+                "backend": BACKEND, "codec": self.codec, "transform_seed": self.base_seed}
+        return CompressedKVData(request_id=request_id, layer_id=L - 1, compressed_tensor=body,
+                                metadata=meta, original_size=int(math.prod(original_shape)) * 2,
+                                compressed_size=body.numel())
+
+    def finalize_layer_group(self, q_perms, cmetas, member_tids, member_blocks,
+                             layer_id) -> CompressedKVData:
+        """One codec call over the independently quantized requests of a
+        layer (lossless merge; each member keeps its own scales)."""
+        buf = torch.cat([q.reshape(-1) for q in q_perms])
+        body = encode_bytes(buf, self.stream_codec)
+        H = self.num_kv_heads
+        bs = int(q_perms[0].shape[3]) if q_perms[0].dim() == 5 else None
+        meta = {"grouped": True, "num_members": len(q_perms), "member_tids": list(member_tids),
+                "member_blocks": [int(b) for b in member_blocks],
+                "member_bytes": [int(q.numel()) for q in q_perms],
+                "block_size": bs, "num_heads": H, "codec_dtype": "uint8",
+                "device": str(buf.device), "layer_id": int(layer_id),
+                "quantization_params": list(cmetas), "backend": BACKEND, "codec": self.codec,
+                "transform_seed": self.base_seed}
+        return CompressedKVData(request_id="grp", layer_id=int(layer_id), compressed_tensor=body,
+                                metadata=meta, original_size=sum(int(b) for b in member_blocks),
+                                compressed_size=body.numel())
+
+    def decompress_layer_group(self, compressed: CompressedKVData):
+        """Decode a grouped layer once and dequantize each member; returns
+        [(transfer_id, kv [2, blocks, bs, H, D])]."""
+        meta = compressed.metadata
+        device = torch.device(meta.get("device", "cuda"))
+        codes = decode_bytes(compressed.compressed_tensor, device)
+        layer_id = int(meta["layer_id"])
+        bs = int(meta["block_size"])
+        H = int(meta["num_heads"])
+        out, off = [], 0
+        for i, (tid, nb) in enumerate(zip(meta["member_tids"], meta["member_blocks"])):
+            n = int(meta["member_bytes"][i])
+            dense = torch.empty((1, 2, nb, bs, H, self.head_size), dtype=torch.bfloat16,
+                                device=device)
+            self._dequant_dense(codes[off:off + n], [meta["quantization_params"][i]], [layer_id],
+                                dense, meta.get("transform_seed", self.base_seed))
+            off += n
+            out.append((tid, dense[0]))
+        return out
+
+    def compress_layer_full(self, kv_layer: torch.Tensor, layer_id: int):
+        """One layer through quantization and codec; returns (bytes, chunk meta)."""
+        codes, canon = self.compress_quant_layer(kv_layer, layer_id)
+        body = encode_bytes(codes, self.stream_codec)
+        _, B, bs, H, D = kv_layer.shape
+        chunk_meta = {"codec_applied": True, "codec_shape": [2, H, B, bs, D],
+                      "codec_dtype": "uint8", "quantization_params": [canon],
+                      "layer_id": int(layer_id)}
+        return body, chunk_meta
+
+    def finalize_chunked(self, chunks, chunk_metas, request_id, original_dtype, original_shape):
+        return CompressedKVData(
+            request_id=request_id, layer_id=len(chunks) - 1, compressed_tensor=None,
+            metadata={"request_id": request_id, "num_layers": len(chunks),
+                      "device": str(chunks[0].device), "original_dtype": original_dtype,
+                      "original_shape": list(original_shape), "backend": BACKEND,
+                      "codec": self.codec, "transform_seed": self.base_seed},
+            original_size=int(math.prod(original_shape)) * 2,
+            compressed_size=sum(int(c.numel()) for c in chunks), is_chunked=True,
+            chunks=list(chunks), chunk_metadata=list(chunk_metas))
+
+    def _decompress_chunked(self, compressed: CompressedKVData) -> torch.Tensor:
+        meta = compressed.metadata
+        device = torch.device(meta.get("device", "cuda"))
+        seed = meta.get("transform_seed", self.base_seed)
+        outs = []
+        t0 = time.monotonic()
+        for chunk, cm in zip(compressed.chunks, compressed.chunk_metadata):
+            _, H, B, bs, D = [int(s) for s in cm["codec_shape"]]
+            codes = decode_bytes(chunk, device)
+            dense = torch.empty((1, 2, B, bs, H, D), dtype=torch.bfloat16, device=device)
+            self._dequant_dense(codes, cm["quantization_params"], [int(cm.get("layer_id", 0))],
+                                dense, seed)
+            outs.append(dense[0])
+        result = torch.stack(outs, 0)
+        if result.is_cuda:
+            torch.cuda.synchronize(device)
+        self._last_decompress_timing = {"t_codec_decode_ms": 0.0,
+                                        "t_dequant_ms": (time.monotonic() - t0) * 1e3}
+        return result
+
+    def warmup(self, block_size: int = 16) -> None:
+        """Run every kernel once on a dummy layer so lazy initialisation
+        (module load, tensor-map encoder lookup) is off the request path."""
+        if not torch.cuda.is_available():
+            return
+        try:
+            dummy = torch.randn(2, 1, block_size, self.num_kv_heads, self.head_size,
+                                dtype=torch.bfloat16, device="cuda")
+            cd = self.compress_all_layers(dummy.unsqueeze(0), "warmup")
+            self.decompress_all_layers(cd)
+            torch.cuda.synchronize()
+        except Exception as e:  # noqa: BLE001
+            logger.warning("fused warmup failed: %s", e)

@@ -42,6 +42,21 @@ ERR_NAMES = {0: "none", 1: "mbarrier timeout", 2: "ready-flag timeout", 3: "boun
              4: "corrupt stream", 5: "overflow"}
 
 
+_xfer = {"h2d": 0, "d2h": 0}
+
+
+def reset_transfer_counters() -> None:
+    """Reset the host<->device byte counters (benchmark accounting)."""
+    _xfer["h2d"] = 0
+    _xfer["d2h"] = 0
+
+
+def transfer_counters() -> dict:
+    """Bytes copied host->device (descriptor tables) and device->host (sizes,
+    headers, error words) by this module since the last reset."""
+    return dict(_xfer)
+
+
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -88,6 +103,7 @@ def read_device_error(device: torch.device, reset: bool = True) -> int:
     """Host read (synchronising) of the device error word; 0 = no error."""
     ws = workspace(device)
     code = int(ws.err[0].item())
+    _xfer["d2h"] += 4
     if reset and code:
         ws.err.zero_()
     return code
@@ -188,17 +204,23 @@ class LayerPlan:
         H = self.num_heads
         if H > _lib.MAX_HEADS:
             raise ValueError(f"at most {_lib.MAX_HEADS} KV heads per rank, got {H}")
-        gid: dict[float, int] = {}
-        self.group_of_head, self.groups = [], []
-        for h, v in enumerate(self.value_levels):
-            v = float(v)
-            if v not in gid:
-                gid[v] = len(gid)
-                self.groups.append([])
-            self.group_of_head.append(gid[v])
-            self.groups[gid[v]].append(h)
-        self.key_bits = [code_bits(v, self.packed) for v in self.key_levels]
-        self.value_bits = [code_bits(v, self.packed) for v in self.value_levels]
+        if not self.group_of_head:
+            gid: dict[float, int] = {}
+            self.groups = []
+            for h, v in enumerate(self.value_levels):
+                v = float(v)
+                if v not in gid:
+                    gid[v] = len(gid)
+                    self.groups.append([])
+                self.group_of_head.append(gid[v])
+                self.groups[gid[v]].append(h)
+        else:
+            G = max(self.group_of_head) + 1
+            self.groups = [[h for h in range(H) if self.group_of_head[h] == g] for g in range(G)]
+        if not self.key_bits:
+            self.key_bits = [code_bits(v, self.packed) for v in self.key_levels]
+        if not self.value_bits:
+            self.value_bits = [code_bits(v, self.packed) for v in self.value_levels]
         pref = [0]
         for b in self.key_bits + self.value_bits:
             pref.append(pref[-1] + 16 * b)
@@ -246,11 +268,27 @@ class LayerPlan:
         return self._params
 
 
+@lru_cache(maxsize=512)
+def _signs_cached(layer_id: int, num_heads: int, seed: int) -> torch.Tensor:
+    return rademacher_signs(layer_id, num_heads, HEAD_DIM, seed)
+
+
 def make_layer_plan(num_heads: int, key_levels, value_levels, seed: Optional[int], layer_id: int,
                     packed: bool = False, clamp_top: bool = True) -> LayerPlan:
-    signs = None if seed is None else rademacher_signs(layer_id, num_heads, HEAD_DIM, seed)
+    signs = None if seed is None else _signs_cached(int(layer_id), int(num_heads), int(seed))
     return LayerPlan(num_heads, [float(x) for x in key_levels], [float(x) for x in value_levels],
                      signs, packed=packed, clamp_top=clamp_top)
+
+
+def decode_plan(num_heads: int, group_of_head: Sequence[int], key_bits: Sequence[int],
+                value_bits: Sequence[int], seed: Optional[int], layer_id: int) -> LayerPlan:
+    """Plan for the consumer side, rebuilt from wire metadata (levels are
+    not needed to dequantize: only groups, bits and the transform)."""
+    signs = None if seed is None else _signs_cached(int(layer_id), int(num_heads), int(seed))
+    packed = any(b != 8 for b in list(key_bits) + list(value_bits))
+    return LayerPlan(num_heads, [2.0] * num_heads, [2.0] * num_heads, signs, packed=packed,
+                     group_of_head=list(group_of_head), key_bits=list(key_bits),
+                     value_bits=list(value_bits))
 
 
 # ------------------------------------------------------------ launch tables
@@ -377,6 +415,8 @@ class WorkItems:
             hi, hl = hi.pin_memory(), hl.pin_memory()
         self._ints = hi.to(dev, non_blocking=True)
         self._longs = hl.to(dev, non_blocking=True)
+        if dev.type == "cuda":
+            _xfer["h2d"] += hi.numel() * 4 + hl.numel() * 8
         self._o = {"bt": 0, "off": len(bt), "ntok": len(bt) + R, "rows": len(bt) + 2 * R,
                    "prefix": len(bt) + 3 * R, "slot": len(bt) + 4 * R + 1}
 
@@ -549,6 +589,7 @@ def rans_encode(data: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: i
                              out.data_ptr(), total.data_ptr(), _ptr(counter), _ptr(flag),
                              flag_value, _stream(dev)), "rans_encode")
     if trim:
+        _xfer["d2h"] += 8
         return out[:int(total[0].item())]
     return out
 
@@ -575,6 +616,31 @@ def rans_decode(stream: torch.Tensor, n: int, out: Optional[torch.Tensor] = None
     check(lb.kvs_rans_decode(stream.data_ptr(), res.data_ptr(), n, chunk,
                              workspace(dev).err.data_ptr(), _stream(dev)), "rans_decode")
     return res
+
+
+def rans_encode_ptr(src_ptr: int, n: int, out_ptr: int, device: torch.device,
+                    flag_ptr: Optional[int] = None, flag_value: int = 0,
+                    chunk: int = RANS_CHUNK) -> None:
+    """Encode ``n`` device bytes at ``src_ptr`` into ``out_ptr`` (capacity
+    :func:`rans_max_bytes`; may be a peer GPU's buffer).  With ``flag_ptr``
+    the last CTA publishes ``flag_value`` there after a system-scope fence.
+    No host synchronisation."""
+    lb = lib()
+    ws = workspace(device)
+    nchunks = (n + chunk - 1) // chunk
+    staging = ws.buf("rans_staging", int(lb.kvs_rans_staging_bytes(n, chunk)))
+    sizes = ws.buf("rans_sizes", 8 * nchunks, torch.int32)
+    total = ws.buf("rans_total", 8, torch.int64)
+    counter = ws.counters[3:4].data_ptr() if flag_ptr is not None else None
+    check(lb.kvs_rans_encode(src_ptr, n, chunk, staging.data_ptr(), sizes.data_ptr(), out_ptr,
+                             total.data_ptr(), counter, flag_ptr, flag_value, _stream(device)),
+          "rans_encode")
+
+
+def rans_decode_ptr(stream_ptr: int, n: int, out_ptr: int, device: torch.device,
+                    chunk: int = RANS_CHUNK) -> None:
+    check(lib().kvs_rans_decode(stream_ptr, out_ptr, n, chunk, workspace(device).err.data_ptr(),
+                                _stream(device)), "rans_decode")
 
 
 def bitpack(codes: torch.Tensor, bits: int) -> torch.Tensor:
