@@ -198,8 +198,9 @@ class Workload:
             for l in range(L):  # fill layer by layer to bound temporaries
                 self.src[l].normal_(generator=gd)
             m = outlier_channels(H, 128, fraction=0.03, seed=seed + 3).to(device)
-            k = self.src[:, 0]
-            k.view(-1, H, 128).mul_(torch.where(m, 12.0, 1.0).to(torch.bfloat16))
+            scale = torch.where(m, 12.0, 1.0).to(torch.bfloat16)
+            for l in range(L):
+                self.src[l, 0].view(-1, H, 128).mul_(scale)
         if role in ("both", "consumer"):
             self.dst = torch.zeros(shape, dtype=torch.bfloat16, device=device)
 
