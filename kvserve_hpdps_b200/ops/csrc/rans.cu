@@ -349,3 +349,112 @@ int kvs_rans_decode(const uint8_t* stream_buf, uint8_t* out, uint64_t n, uint32_
 }
 
 }  // extern "C"
+
+// ===================================================================
+// No-allocation variant of the encoder (declared in kvs_noalloc.h; no
+// counterpart in the reference).  Same kernels as kvs_rans_encode; the
+// staging slots, record sizes and total live in the file-scope device
+// arrays below instead of caller-provided buffers.
+// ===================================================================
+#include <cstdio>
+#include <mutex>
+
+#include "kvs_noalloc.h"
+
+namespace kvs {
+namespace rans {
+
+constexpr uint64_t kNoAllocMaxSymbols = 16ull << 20;  // 16 MiB of input
+constexpr uint32_t kNoAllocChunk = kChunkSymbols;
+constexpr uint32_t kNoAllocMaxChunks =
+    static_cast<uint32_t>((kNoAllocMaxSymbols + kNoAllocChunk - 1) / kNoAllocChunk);
+
+static __device__ __align__(256) uint8_t g_noalloc_staging[kNoAllocMaxChunks *
+                                                           slot_bytes(kNoAllocChunk)];
+static __device__ __align__(256) uint32_t g_noalloc_sizes[2 * kNoAllocMaxChunks];
+static __device__ __align__(256) uint64_t g_noalloc_total[2];
+
+// Device addresses of the scratch arrays, looked up once per device with
+// that device current (host code may not pass the array names themselves:
+// on the host they are stand-ins, not device addresses).
+struct NoAllocScratch {
+  uint8_t* staging;
+  uint32_t* sizes;
+  uint64_t* total;
+};
+constexpr int kNoAllocMaxDevices = 64;
+static NoAllocScratch g_noalloc_addr[kNoAllocMaxDevices];
+static bool g_noalloc_ready[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(NoAllocScratch* out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+    return KVS_NOALLOC_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ready[dev]) {
+    NoAllocScratch s{nullptr, nullptr, nullptr};
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.staging), g_noalloc_staging) !=
+            cudaSuccess ||
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&s.sizes), g_noalloc_sizes) !=
+            cudaSuccess ||
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&s.total), g_noalloc_total) !=
+            cudaSuccess) {
+      cudaGetLastError();
+      return KVS_NOALLOC_SYMBOL;
+    }
+    g_noalloc_addr[dev] = s;
+    g_noalloc_ready[dev] = true;
+  }
+  *out = g_noalloc_addr[dev];
+  return KVS_NOALLOC_OK;
+}
+
+}  // namespace rans
+}  // namespace kvs
+
+extern "C" {
+
+uint64_t kvs_rans_encode_noalloc_max_symbols(void) { return kvs::rans::kNoAllocMaxSymbols; }
+
+int kvs_rans_encode_noalloc(const uint8_t* in, uint64_t n, uint8_t* out, uint64_t out_capacity,
+                            void* stream) {
+  using namespace kvs::rans;
+  if (n == 0) return KVS_NOALLOC_EMPTY;
+  if (n > kNoAllocMaxSymbols) {
+    std::fprintf(stderr,
+                 "kvs_rans_encode_noalloc: input of %llu bytes exceeds the fixed scratch limit "
+                 "of %llu bytes; use kvs_rans_encode with caller-provided buffers\n",
+                 static_cast<unsigned long long>(n),
+                 static_cast<unsigned long long>(kNoAllocMaxSymbols));
+    return KVS_NOALLOC_TOO_LARGE;
+  }
+  if (out_capacity < max_stream_bytes(n, kNoAllocChunk)) return KVS_NOALLOC_OUT_TOO_SMALL;
+  NoAllocScratch s;
+  if (int rc = noalloc_scratch(&s)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint32_t nc = num_chunks(n, kNoAllocChunk);
+  uint32_t* rec_off = s.sizes;
+  uint32_t* rec_len = s.sizes + nc;
+  k_rans_encode<<<(nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32, 0, st>>>(
+      in, n, kNoAllocChunk, s.staging, rec_off, rec_len, nc);
+  k_rans_directory<<<1, 1024, 0, st>>>(rec_len, nc, n, kNoAllocChunk, out, s.total);
+  k_rans_copy<<<(nc + 7) / 8, 256, 0, st>>>(s.staging, rec_off, rec_len, nc, kNoAllocChunk, out,
+                                            nullptr, nullptr, 0u);
+  return cudaGetLastError() == cudaSuccess ? KVS_NOALLOC_OK : KVS_NOALLOC_LAUNCH;
+}
+
+const char* kvs_noalloc_strerror(int code) {
+  switch (code) {
+    case KVS_NOALLOC_OK: return "ok";
+    case KVS_NOALLOC_EMPTY: return "empty input";
+    case KVS_NOALLOC_TOO_LARGE: return "input exceeds the no-alloc scratch limit";
+    case KVS_NOALLOC_OUT_TOO_SMALL: return "output buffer smaller than kvs_rans_max_bytes(n)";
+    case KVS_NOALLOC_NO_DEVICE: return "no current CUDA device";
+    case KVS_NOALLOC_SYMBOL: return "cudaGetSymbolAddress of the scratch arrays failed";
+    case KVS_NOALLOC_LAUNCH: return "kernel launch failed";
+    default: return "unknown error";
+  }
+}
+
+}  // extern "C"
