@@ -1,0 +1,228 @@
+"""CPU tests of the compression layer: signs, head masks, oracle math, the
+lossless codecs (CPU implementation of the device stream format), the wire
+envelope, the generic pipeline and the adapter's mode dispatch."""
+
+import math
+
+import pytest
+import torch
+
+from kvserve_hpdps_b200.compression import codec as C
+from kvserve_hpdps_b200.compression import head_scores as HS
+from kvserve_hpdps_b200.compression import oracle, signs
+from kvserve_hpdps_b200.compression.config import CompressedKVData, validate_spec
+from kvserve_hpdps_b200.compression.wire import build_wire, restore_from_wire
+from kvserve_hpdps_b200.ops import kernels as K
+
+
+def test_rademacher_signs_follow_the_seeding_rule():
+    s = signs.rademacher_signs(layer_id=3, num_heads=4, head_dim=128, base_seed=0x3333)
+    g = torch.Generator().manual_seed(0x3333 ^ (3 << 16) ^ 2)
+    b = torch.randint(0, 2, (128,), generator=g, dtype=torch.int8).float() * 2 - 1
+    assert torch.equal(s[2], b)
+    assert set(s.unique().tolist()) == {-1.0, 1.0}
+
+
+def test_fwht_is_orthonormal_and_self_inverse():
+    x = torch.randn(5, 3, 128)
+    y = signs.fwht_fp32(x)
+    assert torch.allclose(signs.fwht_fp32(y), x, atol=1e-5)
+    assert torch.allclose(y.norm(dim=-1), x.norm(dim=-1), rtol=1e-5)
+    # non power-of-two head dims are transformed per power-of-two chunk
+    z = torch.randn(2, 96)
+    assert torch.allclose(signs.fwht_fp32(signs.fwht_fp32(z)), z, atol=1e-5)
+    assert signs.pow2_chunks(100) == [64, 32, 4]
+
+
+def test_head_masks_and_tp_slicing():
+    scores = HS.get_scores_from_csv("Qwen2.5-7B-Instruct")
+    assert scores.shape == (28, 4)
+    m = HS.head_low_mask(scores, 0.3)
+    assert int(m.sum()) == round(112 * 0.3)
+    low_scores = scores[m]
+    assert float(low_scores.max()) <= float(scores[~m].min())
+    assert HS.slice_for_tp(m, 2, tp_rank=1, tp_size=2).shape == (28, 2)
+    assert torch.equal(HS.slice_for_tp(m, 2, 1, 2), m[:, 2:4])
+    with pytest.raises(ValueError):
+        HS.slice_for_tp(m, 3)
+    lm = HS.layer_low_mask(28)
+    assert int(lm.sum()) == round(28 * 0.33) and bool(lm[-1]) and not bool(lm[0])
+    assert bool(HS.layer_low_mask(1).all())  # round(0.33) == 0 marks every layer low
+    assert HS.get_scores_from_csv("Meta-Llama-3-8B").shape == (32, 8)
+
+
+def test_hybrid_plan_levels():
+    p = HS.HybridPrecisionPlan(None, 4, "Qwen2.5-7B-Instruct", 0.8, 12, 8, 6, 4)
+    kl, vl = p.key_levels, p.value_levels
+    assert set(kl.unique().tolist()) <= {12.0, 6.0} and set(vl.unique().tolist()) <= {8.0, 4.0}
+    assert int((kl == 6).sum()) == round(112 * 0.8)
+    goh, heads = p.value_groups_for(0)
+    assert sorted(h for g in heads for h in g) == [0, 1, 2, 3]
+    q = HS.HybridPrecisionPlan(28, 4, "no-such-model", 0.8, 12, 8, 6, 4)
+    assert bool((q.key_levels == 12).all())
+
+
+def test_oracle_quantization_semantics():
+    torch.manual_seed(0)
+    kv = (torch.randn(2, 3, 16, 2, 128) * 2).to(torch.bfloat16)
+    s = signs.rademacher_signs(1, 2, 128, 0x3333)
+    r = oracle.compress_layer(kv, torch.tensor([12.0, 6.0]), torch.tensor([8.0, 4.0]), s)
+    c = r["codes"]
+    assert int(c[0, 0].max()) <= 11 and int(c[0, 1].max()) <= 5
+    assert int(c[1, 0].max()) <= 7 and int(c[1, 1].max()) <= 3
+    # key scale = range / (levels - 1) per (head, channel)
+    kt = oracle.forward_transform(kv[0].reshape(-1, 2, 128), s)
+    exp = torch.clamp(kt.amax(0) - kt.amin(0), min=1e-5) / torch.tensor([11.0, 5.0])[:, None]
+    assert torch.allclose(r["key_scale"], exp)
+    rec = oracle.decompress_layer(c, r["key_min"], r["key_scale"], r["value_min"],
+                                  r["value_scale"], r["groups"], s)
+    err = oracle.error_metrics(kv, rec)
+    assert err["cosine"] > 0.85
+    r2 = oracle.compress_layer(kv, torch.tensor([12.0, 6.0]), torch.tensor([8.0, 4.0]), s,
+                               clamp_top=False)
+    assert int(r2["codes"][0, 0].max()) <= 12
+
+
+@pytest.mark.parametrize("n", [1, 513, 32768, 70001])
+def test_cpu_rans_roundtrip(n):
+    g = torch.Generator().manual_seed(n)
+    p = torch.tensor([0.05, 0.45, 0.45, 0.05])
+    x = torch.multinomial(p, n, replacement=True, generator=g).to(torch.uint8)
+    s = K.rans_encode(x)
+    assert torch.equal(K.rans_decode(s, n), x)
+    if n > 10000:
+        ent = -(p * p.log2()).sum().item()
+        assert s.numel() * 8 / n < ent * 1.1 + 0.05
+
+
+def test_cpu_rans_detects_corruption():
+    x = torch.randint(0, 4, (40000,), dtype=torch.uint8)
+    s = K.rans_encode(x).clone()
+    bad = s.clone()
+    bad[0] ^= 0xFF
+    with pytest.raises(RuntimeError):
+        K.rans_decode(bad, x.numel())
+    with pytest.raises(RuntimeError):
+        K.rans_decode(s, x.numel() + 1)
+
+
+@pytest.mark.parametrize("codec", ["none", "rans", "bitpack"])
+def test_codec_stage_roundtrip_cpu(codec):
+    x = torch.randint(0, 11, (2, 4, 3, 16, 128), dtype=torch.uint8)
+    enc = C.encode_bytes(x, codec)
+    assert C.parse_header(enc) == (codec, x.numel())
+    out = C.decode_bytes(enc).view(x.shape)
+    assert torch.equal(out, x)
+    if codec == "bitpack":
+        assert enc.numel() < x.numel() * 0.6
+
+
+def test_codec_name_mapping():
+    assert C.resolve_codec("nvcomp", "ANS") == "rans"
+    assert C.resolve_codec("nvcomp", "Bitcomp") == "bitpack"
+    assert C.resolve_codec("lc") == "rans"
+    with pytest.raises(ValueError):
+        C.resolve_codec("nvcomp", "Brotli")
+    codec = C.KVServeCodec(codec_type="nvcomp", nvcomp_algorithm="ANS", data_type="|u1")
+    x = torch.randint(0, 5, (1000,), dtype=torch.uint8)
+    assert torch.equal(codec.decode(0, codec.encode(0, x), "uint8", [1000], "cpu"), x)
+
+
+def test_bitpack_matches_native_layout():
+    codes = torch.randint(0, 8, (9, 128), dtype=torch.uint8)
+    assert torch.equal(C._bitpack_rows(codes, 3), K.bitpack(codes, 3))
+    assert torch.equal(C._bitunpack_rows(K.bitpack(codes, 3), 3), codes)
+
+
+def test_wire_roundtrip_single_and_byte_chunks():
+    body = torch.arange(1000, dtype=torch.int32)
+    meta = {"request_id": "r1", "quantization_params": [
+        {"key_meta": {"min_val": torch.randn(2, 3), "axis": "channel"},
+         "value_meta": {"per_group_list": [{"head_idx": torch.tensor([0, 1])}]}}]}
+    cd = CompressedKVData("r1", 3, body, meta, 4000, 4000)
+    for max_chunk in (1 << 20, 1000):
+        w = build_wire(cd, max_chunk)
+        assert w.meta["body_mode"] == ("single" if max_chunk > 4000 else "byte_chunks")
+        assert len(w.aux_tensors) == 2
+        back = restore_from_wire(w)
+        assert torch.equal(back.compressed_tensor, body)
+        qp = back.metadata["quantization_params"][0]
+        assert torch.equal(qp["key_meta"]["min_val"], meta["quantization_params"][0]["key_meta"]["min_val"])
+        assert back.request_id == "r1"
+
+
+def test_wire_chunked_and_rejects_tensor_outside_qparams():
+    cd = CompressedKVData("r", 1, None, {"request_id": "r"}, 10, 4, is_chunked=True,
+                          chunks=[torch.zeros(2, dtype=torch.uint8), torch.ones(2, dtype=torch.uint8)],
+                          chunk_metadata=[{"quantization_params": [torch.zeros(1)]}, {}])
+    w = build_wire(cd)
+    back = restore_from_wire(w)
+    assert back.is_chunked and len(back.chunks) == 2
+    assert torch.equal(back.chunk_metadata[0]["quantization_params"][0], torch.zeros(1))
+    bad = CompressedKVData("r", 1, torch.zeros(1), {"stray": torch.zeros(1)}, 1, 1)
+    with pytest.raises(TypeError):
+        build_wire(bad)
+
+
+def test_validate_spec():
+    validate_spec(None)
+    validate_spec("default")
+    validate_spec({"pipeline": ["quantizer", "codec"], "quantizer_config": {"hybrid_ratio": 0.5}})
+    with pytest.raises(ValueError):
+        validate_spec({"pipeline": ["compressor"]})
+    with pytest.raises(ValueError):
+        validate_spec({"quantizer_config": {"hybrid_ratio": 1.5}})
+    with pytest.raises(ValueError):
+        validate_spec({"mode": "controller"})
+
+
+GENERIC = {"enabled": True, "pipeline": ["transformer", "quantizer", "codec"],
+           "transformer_config": {"transform_type": "hadamard", "seed": 0x3333},
+           "quantizer_config": {"model_name": "Qwen2.5-7B-Instruct", "hybrid_ratio": 0.3,
+                                "high_key_max_value": 16, "high_value_max_value": 16,
+                                "low_key_max_value": 12, "low_value_max_value": 12,
+                                "axis_key": "token", "axis_value": "token", "split_type": "head"},
+           "codec_config": {"codec_type": "nvcomp", "nvcomp_algorithm": "ANS"},
+           "min_compress_size": 0}
+
+
+def test_generic_pipeline_roundtrip_cpu():
+    from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter
+    from kvserve_hpdps_b200.compression.pipeline_manager import CompressionManager
+    ad = KVCompressionAdapter(GENERIC, num_kv_heads=4, head_size=128)
+    assert isinstance(ad.manager, CompressionManager)
+    x = torch.randn(3, 2, 2, 16, 4, 128).to(torch.bfloat16)
+    c = ad.compress(x, "req")
+    assert c is not None and c.compressed_size < x.numel() * 2 / 3
+    y = ad.decompress(c)
+    assert y.shape == x.shape
+    cos = torch.nn.functional.cosine_similarity(x.float().flatten(), y.float().flatten(), dim=0)
+    assert float(cos) > 0.97
+
+
+def test_generic_quantizer_matches_reference_formula():
+    from kvserve_hpdps_b200.compression.quantizer import dequantize, quantize
+    x = torch.randn(4, 16, 2, 128).to(torch.bfloat16)
+    q, m = quantize(12, x, "channel")
+    mx = x.amax(dim=(0, 1), keepdim=True)
+    mn = x.amin(dim=(0, 1), keepdim=True)
+    sc = (mx - mn).clamp(min=1e-5) / 11
+    exp = ((x - mn) / sc).round().clamp(0, 12).to(torch.uint8)
+    assert torch.equal(q, exp)
+    assert torch.equal(dequantize(q, m), q.to(torch.bfloat16) * sc + mn)
+
+
+def test_adapter_routes_compatible_custom_pipelines_to_fused():
+    from kvserve_hpdps_b200.compression.fused_manager import FusedCompressionManager
+    from kvserve_hpdps_b200.compression.manager import (KVCompressionAdapter, add_sentinel,
+                                                        is_compressed_layer_names, strip_sentinel)
+    spec = dict(GENERIC)
+    spec["quantizer_config"] = dict(GENERIC["quantizer_config"], axis_key="channel")
+    ad = KVCompressionAdapter(spec, num_kv_heads=4, head_size=128)
+    assert isinstance(ad.manager, FusedCompressionManager)
+    assert ad.supports_overlap() and ad.supports_paged()
+    ad2 = KVCompressionAdapter("default", num_kv_heads=4, head_size=128,
+                               model_name="Qwen2.5-7B-Instruct")
+    assert ad2.manager.base_seed == 0x3333 and ad2.manager.codec == "rans"
+    names = add_sentinel(["a", "b"])
+    assert is_compressed_layer_names(names) and strip_sentinel(names) == ["a", "b"]
