@@ -1,0 +1,94 @@
+"""ZMQ control channel between a producer and a consumer rank.
+
+One channel per TP rank on ``kv_port + tp_rank`` (reference:
+kvserve_v1/transport/nccl_transport.py:61-130): the consumer binds a ROUTER,
+the producer connects a DEALER whose identity is ``host:port``.  Messages are
+msgpack dicts with a ``cmd`` field; the reference's verbs ``INIT``, ``PUT``
+and ``PUT_BUNDLE`` (and its one-byte ACKs ``b"0"`` ok / ``b"1"`` refused)
+keep their meaning, and this framework adds ``RING_MAP`` (receive-ring
+handles), ``PUT_RING`` (a payload written into the ring by the producer's
+kernels) and ``FREE`` (ring space returned by the consumer).
+
+All receives take a timeout so no thread blocks forever on a dead peer.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Any, Optional
+
+import msgpack
+import zmq
+
+ACK_OK = b"0"
+ACK_REFUSED = b"1"
+
+
+def channel_port(kv_port: int, tp_rank: int) -> int:
+    return int(kv_port) + int(tp_rank)
+
+
+def pack(msg: dict[str, Any]) -> bytes:
+    return msgpack.dumps(msg, use_bin_type=True)
+
+
+def unpack(raw: bytes) -> dict[str, Any]:
+    return msgpack.loads(raw, raw=False)
+
+
+class ProducerChannel:
+    """DEALER side.  ``request`` sends a message and waits for the reply."""
+
+    def __init__(self, host: str, port: int, timeout_s: float = 60.0):
+        self.ctx = zmq.Context.instance()
+        self.sock = self.ctx.socket(zmq.DEALER)
+        self.sock.setsockopt_string(zmq.IDENTITY, f"{host}:{port}:{id(self)}")
+        self.sock.setsockopt(zmq.LINGER, 0)
+        self.sock.connect(f"tcp://{host}:{port}")
+        self.timeout_ms = int(timeout_s * 1000)
+        self.lock = threading.Lock()
+
+    def send(self, msg: dict[str, Any]) -> None:
+        with self.lock:
+            self.sock.send(pack(msg))
+
+    def recv(self, timeout_s: Optional[float] = None) -> Optional[bytes]:
+        t = self.timeout_ms if timeout_s is None else int(timeout_s * 1000)
+        if self.sock.poll(t, zmq.POLLIN):
+            return self.sock.recv()
+        return None
+
+    def request(self, msg: dict[str, Any], timeout_s: Optional[float] = None) -> Optional[bytes]:
+        with self.lock:
+            self.sock.send(pack(msg))
+            t = self.timeout_ms if timeout_s is None else int(timeout_s * 1000)
+            if self.sock.poll(t, zmq.POLLIN):
+                return self.sock.recv()
+        return None
+
+    def close(self) -> None:
+        self.sock.close(0)
+
+
+class ConsumerChannel:
+    """ROUTER side.  ``poll`` returns (identity, message) or None."""
+
+    def __init__(self, port: int, bind_host: str = "*"):
+        self.ctx = zmq.Context.instance()
+        self.sock = self.ctx.socket(zmq.ROUTER)
+        self.sock.setsockopt(zmq.LINGER, 0)
+        self.sock.bind(f"tcp://{bind_host}:{port}")
+        self.lock = threading.Lock()
+
+    def poll(self, timeout_ms: int = 100) -> Optional[tuple[bytes, dict[str, Any]]]:
+        if self.sock.poll(timeout_ms, zmq.POLLIN):
+            frames = self.sock.recv_multipart()
+            return frames[0], unpack(frames[-1])
+        return None
+
+    def reply(self, identity: bytes, payload: bytes) -> None:
+        with self.lock:
+            self.sock.send_multipart([identity, payload])
+
+    def close(self) -> None:
+        self.sock.close(0)

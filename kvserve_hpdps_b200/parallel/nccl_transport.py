@@ -1,0 +1,266 @@
+"""Point-to-point transport over a torch process group (NCCL; gloo for CPU tests).
+
+Public API of the reference transport (kvserve_v1/transport/nccl_transport.py:54-462):
+
+* producer: ``send(request_id, layer_names, stacked_kv)``,
+  ``send_bundle(request_id, layer_names, meta, body_chunks, aux_tensors,
+  member_tids=None)``, ``sent_layers(tid)``, ``clear_sent(tid)``,
+  ``wait_for_sent()``;
+* consumer: ``drain_received() -> {transfer_id: [(layer_names, payload)]}``
+  where payload is a tensor (raw), a bundle dict (``{"__bundle__": True,
+  "meta", "body_chunks", "aux_tensors"}``) or ``FAILED_PAYLOAD`` (None) when
+  the consumer refused the message (allocation failure, no channel).
+
+Protocol per message: the producer's send thread sends a ``PUT`` /
+``PUT_BUNDLE`` header over the ZMQ channel and waits for the consumer's ACK;
+the consumer allocates the tensors, ACKs, and posts the receives; the
+producer then posts its sends.  The consumer only posts receives after a
+header, so no receive is pending while the engine captures CUDA graphs.
+
+The 2-rank process group is built from a TCPStore the consumer hosts on
+``kv_port + tp_rank + STORE_PORT_OFFSET`` (producer rank 0, consumer rank 1).
+This transport is the baseline and the fallback of the NVLink ring transport
+(``p2p_transport.py``), e.g. across nodes.
+"""
+
+from __future__ import annotations
+
+import datetime
+import threading
+import time
+from collections import defaultdict, deque
+from typing import Any, Optional
+
+import torch
+
+from kvserve_hpdps_b200.parallel.control import (ACK_OK, ACK_REFUSED, ConsumerChannel,
+                                                 ProducerChannel, channel_port)
+from kvserve_hpdps_b200.utils.logger import get_logger
+from kvserve_hpdps_b200.utils.stats import write_transfer_stats
+
+logger = get_logger(__name__)
+
+FAILED_PAYLOAD: Any = None
+FAILED_LAYER_NAMES: list[str] = []
+STORE_PORT_OFFSET = 1000
+
+
+def tensor_spec(t: torch.Tensor) -> dict[str, Any]:
+    return {"shape": list(t.shape), "dtype": str(t.dtype).replace("torch.", "")}
+
+
+def alloc_from_spec(spec: dict[str, Any], device: torch.device) -> torch.Tensor:
+    return torch.empty(tuple(spec["shape"]), dtype=getattr(torch, spec["dtype"]), device=device)
+
+
+def make_pair_group(host: str, port: int, rank: int, backend: str, timeout_s: float = 120.0):
+    """2-rank process group over a TCPStore (rank 1 hosts the store)."""
+    import torch.distributed as dist
+    store = dist.TCPStore(host if rank == 0 else "0.0.0.0", port, 2, rank == 1,
+                          timeout=datetime.timedelta(seconds=timeout_s))
+    if backend == "nccl":
+        pg = dist.ProcessGroupNCCL(store, rank, 2)
+    else:
+        pg = dist.ProcessGroupGloo(store, rank, 2, datetime.timedelta(seconds=timeout_s))
+    return pg, store
+
+
+class NcclTransport:
+    def __init__(self, is_sender: bool, host: str, port: int, local_rank: int = 0,
+                 channel_rank: int = 0, backend: str = "nccl", timeout_s: float = 60.0):
+        self.is_sender = is_sender
+        self.backend = backend
+        self.port = channel_port(port, channel_rank)
+        self.store_port = self.port + STORE_PORT_OFFSET
+        self.host = host
+        self.timeout_s = timeout_s
+        self.device = torch.device("cuda", local_rank) if backend == "nccl" else torch.device("cpu")
+        self._pg = None
+        self._closed = False
+        if is_sender:
+            self._ctl = ProducerChannel(host, self.port, timeout_s)
+            self._ctl.send({"cmd": "INIT", "backend": backend, "store_port": self.store_port})
+            self._pg, self._store = make_pair_group(host, self.store_port, 0, backend)
+            self._cv = threading.Condition()
+            self._queue: deque = deque()
+            self._inflight = 0
+            self._sent_lock = threading.Lock()
+            self._sent: dict[str, int] = defaultdict(int)
+            self._thread = threading.Thread(target=self._send_loop, daemon=True,
+                                            name="kvs-send")
+            self._thread.start()
+        else:
+            self._ctl = ConsumerChannel(self.port)
+            self._lock = threading.Lock()
+            self._received: dict[str, deque] = defaultdict(deque)
+            self._thread = threading.Thread(target=self._listen_loop, daemon=True,
+                                            name="kvs-listen")
+            self._thread.start()
+
+    # ------------------------------------------------------------ producer
+    def _ready_event(self):
+        if self.device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            return ev
+        return None
+
+    def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
+        assert self.is_sender
+        t = stacked_kv.to(self.device).contiguous()
+        with self._cv:
+            self._queue.append(("tensor", request_id, list(layer_names), t, self._ready_event(), None))
+            self._cv.notify()
+
+    def send_bundle(self, request_id: str, layer_names: list[str], meta: dict,
+                    body_chunks: list[torch.Tensor], aux_tensors: list[torch.Tensor],
+                    member_tids: Optional[list[str]] = None) -> None:
+        assert self.is_sender
+        body = [t.to(self.device).contiguous() for t in body_chunks]
+        aux = [t.to(self.device).contiguous() for t in aux_tensors]
+        with self._cv:
+            self._queue.append(("bundle", request_id, list(layer_names), (meta, body, aux),
+                                self._ready_event(), member_tids))
+            self._cv.notify()
+
+    def sent_layers(self, transfer_id: str) -> int:
+        with self._sent_lock:
+            return self._sent.get(transfer_id, 0)
+
+    def clear_sent(self, transfer_id: str) -> None:
+        with self._sent_lock:
+            self._sent.pop(transfer_id, None)
+
+    def wait_for_sent(self, timeout_s: Optional[float] = None) -> bool:
+        deadline = None if timeout_s is None else time.monotonic() + timeout_s
+        with self._cv:
+            while self._queue or self._inflight:
+                left = None if deadline is None else deadline - time.monotonic()
+                if left is not None and left <= 0:
+                    return False
+                self._cv.wait(timeout=left if left is not None else 1.0)
+        return True
+
+    def _send_loop(self) -> None:
+        while not self._closed:
+            with self._cv:
+                while not self._queue and not self._closed:
+                    self._cv.wait(timeout=0.5)
+                if self._closed:
+                    return
+                item = self._queue.popleft()
+                self._inflight += 1
+            try:
+                self._send_item(*item)
+            except Exception as e:  # noqa: BLE001
+                logger.error("send of %s failed: %s", item[1], e)
+            finally:
+                with self._cv:
+                    self._inflight -= 1
+                    self._cv.notify_all()
+
+    def _p2p_send(self, tensors: list[torch.Tensor]) -> None:
+        works = [self._pg.send([t], 1, 0) for t in tensors if t.numel() > 0]
+        for w in works:
+            w.wait()
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+
+    def _send_item(self, kind, request_id, layer_names, payload, event, member_tids) -> None:
+        if kind == "tensor":
+            t = payload
+            msg = {"cmd": "PUT", "request_id": request_id, "layer_names": layer_names,
+                   **tensor_spec(t)}
+            tensors = [t]
+        else:
+            meta, body, aux = payload
+            msg = {"cmd": "PUT_BUNDLE", "request_id": request_id, "layer_names": layer_names,
+                   "meta": meta, "body_specs": [tensor_spec(t) for t in body],
+                   "aux_specs": [tensor_spec(t) for t in aux]}
+            tensors = body + aux
+        ack = self._ctl.request(msg, self.timeout_s)
+        if ack != ACK_OK:
+            logger.error("consumer refused %s (%r)", request_id, ack)
+            return
+        if event is not None:
+            event.synchronize()
+        t0 = time.monotonic()
+        self._p2p_send(tensors)
+        nbytes = sum(t.numel() * t.element_size() for t in tensors)
+        if kind == "bundle" and member_tids:
+            with self._sent_lock:
+                for tid in member_tids:
+                    self._sent[tid] += 1
+        write_transfer_stats(request_id, (time.monotonic() - t0) * 1e3, nbytes,
+                             transport="nccl" if self.backend == "nccl" else self.backend)
+
+    # ------------------------------------------------------------ consumer
+    def drain_received(self) -> dict[str, list[tuple[list[str], Any]]]:
+        assert not self.is_sender
+        with self._lock:
+            out = {k: list(v) for k, v in self._received.items() if v}
+            self._received.clear()
+        return out
+
+    def _mark_failed(self, request_id: str) -> None:
+        with self._lock:
+            self._received[request_id].append((FAILED_LAYER_NAMES, FAILED_PAYLOAD))
+
+    def _recv(self, tensors: list[torch.Tensor]) -> None:
+        works = [self._pg.recv([t], 0, 0) for t in tensors if t.numel() > 0]
+        for w in works:
+            w.wait()
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+
+    def _listen_loop(self) -> None:
+        while not self._closed:
+            try:
+                got = self._ctl.poll(200)
+                if got is None:
+                    continue
+                ident, msg = got
+                cmd = msg.get("cmd")
+                if cmd == "INIT":
+                    self._pg, self._store = make_pair_group("0.0.0.0", msg["store_port"], 1,
+                                                            msg.get("backend", self.backend))
+                    continue
+                if cmd not in ("PUT", "PUT_BUNDLE"):
+                    self._handle_extra(ident, msg)
+                    continue
+                rid = msg["request_id"]
+                if self._pg is None:
+                    self._ctl.reply(ident, ACK_REFUSED)
+                    self._mark_failed(rid)
+                    continue
+                try:
+                    if cmd == "PUT":
+                        tensors = [alloc_from_spec(msg, self.device)]
+                    else:
+                        body = [alloc_from_spec(s, self.device) for s in msg["body_specs"]]
+                        aux = [alloc_from_spec(s, self.device) for s in msg["aux_specs"]]
+                        tensors = body + aux
+                except (torch.cuda.OutOfMemoryError, RuntimeError) as e:
+                    logger.error("allocation for %s failed: %s", rid, e)
+                    self._ctl.reply(ident, ACK_REFUSED)
+                    self._mark_failed(rid)
+                    continue
+                self._ctl.reply(ident, ACK_OK)
+                self._recv(tensors)
+                payload = tensors[0] if cmd == "PUT" else {
+                    "__bundle__": True, "meta": msg["meta"], "body_chunks": body,
+                    "aux_tensors": aux}
+                with self._lock:
+                    self._received[rid].append((msg["layer_names"], payload))
+            except Exception as e:  # noqa: BLE001
+                logger.error("listener error: %s", e)
+
+    def _handle_extra(self, ident: bytes, msg: dict) -> None:
+        logger.warning("unknown control message %r", msg.get("cmd"))
+
+    def close(self) -> None:
+        self._closed = True
+        try:
+            self._ctl.close()
+        except Exception:  # noqa: BLE001
+            pass
