@@ -224,6 +224,43 @@ class FusedCompressionManager:
             meta_buf[items.meta_off[r]:items.meta_off[r] + m.numel()] = m.to(device)
         K.dequantize(codes, meta_buf, slots, items, engine=self.engine)
 
+    def decompress_members(self, compressed: CompressedKVData, dst_layers: Sequence[torch.Tensor],
+                           member_blocks: dict[int, Sequence[int]]) -> None:
+        """Decode a multi-request message once (cached) and dequantize only
+        the members in ``member_blocks`` (member index -> consumer block ids)
+        into ``dst_layers`` (one per layer of the message)."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        meta = compressed.metadata
+        device = dst_layers[0].device
+        key = id(compressed.compressed_tensor)
+        cache = self.__dict__.setdefault("_decoded", {})
+        if key not in cache:
+            if len(cache) > 8:
+                cache.pop(next(iter(cache)))
+            cache[key] = decode_bytes(compressed.compressed_tensor, device)
+        codes = cache[key]
+        layer_ids = meta["layer_ids"]
+        R = len(meta["member_tids"])
+        seed = meta.get("transform_seed", self.base_seed)
+        qp = meta["quantization_params"]
+        plans = [self.plan_from_canon(qp[l * R], layer_ids[l], seed) for l in range(len(layer_ids))]
+        bs = int(meta["block_size"])
+        # code offsets of every item of the original message (layer-major)
+        offs, c = [], 0
+        for l in range(len(layer_ids)):
+            for r in range(R):
+                offs.append(c)
+                c += ((meta["member_blocks"][r] * bs * plans[l].row_bytes()) + 15) & ~15
+        slots = self._slots(dst_layers, plans)
+        sel = [(l, r) for l in range(len(layer_ids)) for r in sorted(member_blocks)]
+        items = K.WorkItems(slots, [(l, member_blocks[r], meta["member_tokens"][r]) for l, r in sel],
+                            code_offsets=[offs[l * R + r] for l, r in sel])
+        meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=device)
+        for i, (l, r) in enumerate(sel):
+            m = self.meta_from_canon(qp[l * R + r])
+            meta_buf[items.meta_off[i]:items.meta_off[i] + m.numel()] = m.to(device)
+        K.dequantize(codes, meta_buf, slots, items, engine=self.engine)
+
     # ------------------------------------------------------ canon metadata
     def canon_meta(self, meta: torch.Tensor, off: int, plan, rows: int) -> dict:
         """Wire-form metadata of one item (views into ``meta``)."""

@@ -80,6 +80,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_block_copy": ([POINTER(PagedKV), P, c_int, c_longlong, P, c_int, P, P, c_uint32, P],
                            c_int),
         "kvs_copy16": ([P, P, c_longlong, P, P, c_uint32, c_int, P], c_int),
+        "kvs_copy_segments": ([P, c_int, c_int, P, P, c_uint32, P], c_int),
         "kvs_wait_flag": ([P, c_uint32, c_uint64, P, P, P], c_int),
         "kvs_set_flag": ([P, c_uint32, P], c_int),
         "kvs_probe_push": ([P, P, c_longlong, P, c_int, P], c_int),

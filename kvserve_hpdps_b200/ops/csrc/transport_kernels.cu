@@ -65,6 +65,45 @@ __global__ void __launch_bounds__(256) k_copy16(const uint4* __restrict__ src, u
   }
 }
 
+// Gather-copy of several byte ranges (any sizes and 16-byte aligned
+// destinations) in one launch: grid.y = segment.  The last CTA to finish
+// publishes `flag_value` into `flag` after a system-scope fence, so a
+// consumer on another GPU that observes the flag sees every segment.
+struct CopySeg {
+  const uint8_t* src;
+  uint8_t* dst;
+  long long bytes;
+};
+
+__global__ void __launch_bounds__(256) k_copy_segments(const CopySeg* __restrict__ segs,
+                                                       uint32_t* counter, uint32_t* flag,
+                                                       uint32_t flag_value) {
+  const CopySeg sg = segs[blockIdx.y];
+  const bool aligned = ((reinterpret_cast<uintptr_t>(sg.src) | reinterpret_cast<uintptr_t>(sg.dst)) & 15) == 0;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (aligned) {
+    const long long n16 = sg.bytes / 16;
+    for (long long i = tid; i < n16; i += stride)
+      reinterpret_cast<uint4*>(sg.dst)[i] = reinterpret_cast<const uint4*>(sg.src)[i];
+    for (long long i = n16 * 16 + tid; i < sg.bytes; i += stride) sg.dst[i] = sg.src[i];
+  } else {
+    for (long long i = tid; i < sg.bytes; i += stride) sg.dst[i] = sg.src[i];
+  }
+  __threadfence_system();
+  if (counter != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(counter, 1u);
+      if (done == gridDim.x * gridDim.y - 1) {
+        __threadfence_system();
+        st_release_sys(flag, flag_value);
+        *counter = 0;
+      }
+    }
+  }
+}
+
 // Wait (bounded) until *flag == expected.  One thread spins; on timeout
 // the error word records ERR_FLAG_TIMEOUT and the kernel returns.
 __global__ void k_wait_flag(const uint32_t* flag, uint32_t expected, uint64_t timeout_ns,
@@ -133,6 +172,15 @@ int kvs_copy16(const void* src, void* dst, long long bytes, uint32_t* counter, u
   if (blocks < 1) blocks = 1;
   k_copy16<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), static_cast<uint4*>(dst), n16, counter, flag, flag_value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// segs: device array of n CopySeg {src, dst, bytes}.
+int kvs_copy_segments(const void* segs, int n, int blocks_per_seg, uint32_t* counter,
+                      uint32_t* flag, uint32_t flag_value, void* stream) {
+  if (n <= 0) return 0;
+  k_copy_segments<<<dim3(blocks_per_seg, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const CopySeg*>(segs), counter, flag, flag_value);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

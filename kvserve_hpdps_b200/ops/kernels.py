@@ -378,7 +378,10 @@ class WorkItems:
     of ``16*bits`` bytes), its fp16 metadata at ``meta_off[r]``.
     """
 
-    def __init__(self, slots: LayerSlots, items: Sequence[tuple[int, Sequence[int], int]]):
+    def __init__(self, slots: LayerSlots, items: Sequence[tuple[int, Sequence[int], int]],
+                 code_offsets: Optional[Sequence[int]] = None):
+        """``code_offsets`` overrides where each item's codes start (used to
+        decode a subset of the items of a larger message in place)."""
         self.slots = slots
         self.items = [(int(s), list(map(int, b)), int(n)) for s, b, n in items]
         dev = slots.device
@@ -407,6 +410,12 @@ class WorkItems:
             m += _align16(plan.meta_bytes(rows))
             ro += rows
         self.code_bytes, self.meta_bytes, self.total_rows = c, m, ro
+        if code_offsets is not None:
+            if len(code_offsets) != len(self.items):
+                raise ValueError("one code offset per item is required")
+            self.code_off = [int(x) for x in code_offsets]
+            self.code_bytes = max((o + self.n_rows[i] * slots.plans[self.items[i][0]].row_bytes()
+                                   for i, o in enumerate(self.code_off)), default=0)
         ints = bt + off + self.n_tokens + self.n_rows + prefix + [s for s, _, _ in self.items]
         longs = self.code_off + self.meta_off + self.row_off
         hi = torch.tensor(ints if ints else [0], dtype=torch.int32)
@@ -681,6 +690,31 @@ def copy_bytes(src_ptr: int, dst_ptr: int, nbytes: int, device: torch.device,
     counter = ws.counters[2:3].data_ptr() if flag_ptr is not None else None
     check(lib().kvs_copy16(src_ptr, dst_ptr, nbytes, counter, flag_ptr, flag_value, max_blocks,
                            _stream(device)), "copy16")
+
+
+def copy_segments(segments: Sequence[tuple[int, int, int]], device: torch.device,
+                  flag_ptr: Optional[int] = None, flag_value: int = 0,
+                  blocks_per_seg: int = 32) -> None:
+    """Copy several (src_ptr, dst_ptr, nbytes) ranges in one launch on the
+    current stream; destinations may be peer memory.  With ``flag_ptr``, the
+    last CTA publishes ``flag_value`` there (release, system scope) after
+    every segment is written."""
+    segs = [s for s in segments if s[2] > 0]
+    if not segs:
+        if flag_ptr is not None:
+            set_flag(flag_ptr, flag_value, device)
+        return
+    host = torch.tensor([v for s in segs for v in s], dtype=torch.int64)
+    if device.type == "cuda":
+        host = host.pin_memory()
+        _xfer["h2d"] += host.numel() * 8
+    dev_segs = host.to(device, non_blocking=True)
+    ws = workspace(device)
+    counter = ws.counters[4:5].data_ptr() if flag_ptr is not None else None
+    check(lib().kvs_copy_segments(dev_segs.data_ptr(), len(segs), blocks_per_seg, counter,
+                                  flag_ptr, flag_value, _stream(device)), "copy_segments")
+    # dev_segs may be freed now: the caching allocator only reuses its block
+    # for work ordered after this launch on the same stream.
 
 
 def wait_flag(flag_ptr: int, expected: int, device: torch.device, timeout_s: float = 2.0,

@@ -1,0 +1,375 @@
+"""NVLink receive-ring transport: producer kernels store into the consumer's memory.
+
+Same public API as the NCCL transport (``send``, ``send_bundle``,
+``sent_layers``, ``clear_sent``, ``wait_for_sent``, ``drain_received``) plus
+two consumer hooks the connector calls around decoding:
+``prepare(payload, device)`` launches a bounded device wait on the payload's
+ready flag, ``release(payload, device)`` returns the payload's ring space once
+the work queued on the stream so far has finished.
+
+Design (one channel per TP rank, on ``kv_port + tp_rank``):
+
+* the consumer owns a receive ring allocated with cudaMalloc (so its CUDA
+  IPC handle names exactly the ring) followed by a table of ready flags;
+  the producer asks for it with ``RING_HELLO`` and maps it with
+  ``cudaIpcOpenMemHandle``;
+* the producer allocates ring space itself (first-fit free list over the
+  consumer's ring); the consumer returns space with ``FREE`` messages, so a
+  message costs no round trip;
+* a send enqueues one gather-copy kernel on the producer's transfer stream:
+  every tensor of the message is stored into the peer ring over NVLink and
+  the last CTA publishes the message's sequence number into its flag slot
+  (``__threadfence_system`` + ``st.release.sys``); the ``PUT_RING`` header
+  (tensor specs and ring offsets) goes over ZMQ right after the launch;
+* the consumer wraps ring slices as tensors (``__cuda_array_interface__``,
+  zero copy) and its decode kernels run after a bounded device wait on the
+  flag (``ERR_FLAG_TIMEOUT`` instead of a hang if the producer died).
+
+No TMA multicast and no library kernel reads the peer ring: only this
+framework's own store loop writes it and its own kernels read the local copy.
+"""
+
+from __future__ import annotations
+
+import queue
+import threading
+import time
+from collections import defaultdict, deque
+from typing import Any, Optional
+
+import torch
+
+from kvserve_hpdps_b200.parallel.control import (ConsumerChannel, ProducerChannel, channel_port,
+                                                 pack, unpack)
+from kvserve_hpdps_b200.parallel.nccl_transport import FAILED_LAYER_NAMES, FAILED_PAYLOAD
+from kvserve_hpdps_b200.utils.logger import get_logger
+from kvserve_hpdps_b200.utils.stats import write_transfer_stats
+
+logger = get_logger(__name__)
+
+ALIGN = 256
+FLAG_STRIDE = 16
+
+
+def _align(x: int) -> int:
+    return (x + ALIGN - 1) // ALIGN * ALIGN
+
+
+class RingAllocator:
+    """First-fit free-list allocator over [0, capacity) (producer side)."""
+
+    def __init__(self, capacity: int):
+        self.capacity = int(capacity)
+        self.free: list[tuple[int, int]] = [(0, self.capacity)]  # sorted (off, size)
+        self.cv = threading.Condition()
+
+    def try_alloc(self, size: int) -> Optional[int]:
+        size = _align(size)
+        for i, (off, sz) in enumerate(self.free):
+            if sz >= size:
+                if sz == size:
+                    self.free.pop(i)
+                else:
+                    self.free[i] = (off + size, sz - size)
+                return off
+        return None
+
+    def alloc(self, size: int, timeout_s: float) -> Optional[int]:
+        deadline = time.monotonic() + timeout_s
+        with self.cv:
+            while True:
+                off = self.try_alloc(size)
+                if off is not None:
+                    return off
+                left = deadline - time.monotonic()
+                if left <= 0:
+                    return None
+                self.cv.wait(timeout=min(left, 0.1))
+
+    def release(self, off: int, size: int) -> None:
+        size = _align(size)
+        with self.cv:
+            self.free.append((off, size))
+            self.free.sort()
+            merged = []
+            for o, s in self.free:
+                if merged and merged[-1][0] + merged[-1][1] == o:
+                    merged[-1] = (merged[-1][0], merged[-1][1] + s)
+                else:
+                    merged.append((o, s))
+            self.free = merged
+            self.cv.notify_all()
+
+    def free_bytes(self) -> int:
+        with self.cv:
+            return sum(s for _, s in self.free)
+
+
+class _CudaView:
+    """Zero-copy tensor view of raw device memory (__cuda_array_interface__)."""
+
+    _TYPESTR = {torch.uint8: "|u1", torch.int8: "|i1", torch.int16: "<i2", torch.int32: "<i4",
+                torch.int64: "<i8", torch.float16: "<f2", torch.float32: "<f4",
+                torch.float64: "<f8"}
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (int(nbytes),), "typestr": "|u1",
+                                         "data": (int(ptr), False), "version": 3}
+
+
+def tensor_view(ptr: int, nbytes: int, dtype: torch.dtype, shape, device: int) -> torch.Tensor:
+    if nbytes == 0:
+        return torch.empty(shape, dtype=dtype, device=f"cuda:{device}")
+    raw = torch.as_tensor(_CudaView(ptr, nbytes), device=f"cuda:{device}")
+    return raw.view(dtype).reshape(shape)
+
+
+class P2PTransport:
+    def __init__(self, is_sender: bool, host: str, port: int, local_rank: int = 0,
+                 channel_rank: int = 0, ring_bytes: int = 2 << 30, n_flags: int = 4096,
+                 timeout_s: float = 60.0, flag_timeout_s: float = 30.0):
+        self.is_sender = is_sender
+        self.port = channel_port(port, channel_rank)
+        self.device = torch.device("cuda", local_rank)
+        self.local_rank = local_rank
+        self.timeout_s = timeout_s
+        self.flag_timeout_s = flag_timeout_s
+        self._closed = False
+        self._outbox: queue.Queue = queue.Queue()
+        if is_sender:
+            self._ctl = ProducerChannel(host, self.port, timeout_s)
+            reply = self._ctl.request({"cmd": "RING_HELLO", "device": local_rank}, timeout_s)
+            if reply is None:
+                raise TimeoutError(f"no consumer on {host}:{self.port}")
+            info = unpack(reply)
+            from kvserve_hpdps_b200.parallel.p2p import PeerMapping
+            self._peer = PeerMapping(local_rank, info["handle"], info["nbytes"])
+            self.ring_bytes = int(info["ring_bytes"])
+            self.flag_off = int(info["flag_off"])
+            self.n_flags = int(info["n_flags"])
+            self._alloc = RingAllocator(self.ring_bytes)
+            self._stream = torch.cuda.Stream(device=self.device)
+            self._seq = 0
+            self._inflight_msgs = 0
+            self._lock = threading.Lock()
+            self._sent: dict[str, int] = defaultdict(int)
+            self._pending: deque = deque()  # (event, request_id, member_tids, nbytes, t0)
+            self._pending_cv = threading.Condition()
+            self._io = threading.Thread(target=self._producer_io, daemon=True, name="kvs-p2p-io")
+            self._io.start()
+            self._done = threading.Thread(target=self._completion_loop, daemon=True,
+                                          name="kvs-p2p-done")
+            self._done.start()
+        else:
+            from kvserve_hpdps_b200.parallel.p2p import DeviceRegion
+            self.n_flags = n_flags
+            self.ring_bytes = int(ring_bytes)
+            self.flag_off = _align(self.ring_bytes)
+            self._region = DeviceRegion(local_rank, self.flag_off + n_flags * FLAG_STRIDE)
+            self._ctl = ConsumerChannel(self.port)
+            self._producer_id: Optional[bytes] = None
+            self._lock = threading.Lock()
+            self._received: dict[str, deque] = defaultdict(deque)
+            self._releases: deque = deque()  # (event, off, size)
+            self._io = threading.Thread(target=self._consumer_io, daemon=True, name="kvs-p2p-io")
+            self._io.start()
+
+    # ============================================================ producer
+    def _producer_io(self) -> None:
+        while not self._closed:
+            try:
+                while True:
+                    try:
+                        self._ctl.send(self._outbox.get_nowait())
+                    except queue.Empty:
+                        break
+                raw = self._ctl.recv(timeout_s=0.005)
+                if raw is None:
+                    continue
+                msg = unpack(raw)
+                if msg.get("cmd") == "FREE":
+                    for off, size in msg["regions"]:
+                        self._alloc.release(off, size)
+                    with self._lock:
+                        self._inflight_msgs -= len(msg["regions"])
+            except Exception as e:  # noqa: BLE001
+                logger.error("p2p producer io error: %s", e)
+
+    def _completion_loop(self) -> None:
+        while not self._closed:
+            with self._pending_cv:
+                while not self._pending and not self._closed:
+                    self._pending_cv.wait(timeout=0.2)
+                if self._closed:
+                    return
+                ev, rid, tids, nbytes, t0 = self._pending[0]
+            ev.synchronize()
+            with self._pending_cv:
+                self._pending.popleft()
+                self._pending_cv.notify_all()
+            if tids:
+                with self._lock:
+                    for t in tids:
+                        self._sent[t] += 1
+            write_transfer_stats(rid, (time.monotonic() - t0) * 1e3, nbytes, transport="nvlink-p2p")
+
+    def _put(self, request_id: str, layer_names: list[str], tensors: list[torch.Tensor],
+             n_body: int, meta: Optional[dict], kind: str,
+             member_tids: Optional[list[str]]) -> None:
+        sizes = [t.numel() * t.element_size() for t in tensors]
+        offs, total = [], 0
+        for s in sizes:
+            offs.append(total)
+            total += _align(s)
+        total = max(total, ALIGN)
+        with self._lock:
+            wait_slots = self._inflight_msgs >= self.n_flags - 1
+        if wait_slots:
+            logger.warning("p2p: %d messages in flight, waiting for the consumer", self.n_flags)
+        base = self._alloc.alloc(total, self.timeout_s)
+        if base is None:
+            raise RuntimeError(f"receive ring full for {self.timeout_s}s ({total} bytes needed)")
+        with self._lock:
+            self._seq += 1
+            seq = self._seq
+            self._inflight_msgs += 1
+        slot = seq % self.n_flags
+        from kvserve_hpdps_b200.ops import kernels as K
+        ready = torch.cuda.current_stream(self.device).record_event()
+        t0 = time.monotonic()
+        with torch.cuda.stream(self._stream):
+            self._stream.wait_event(ready)
+            segs = [(t.data_ptr(), self._peer.ptr + base + o, s)
+                    for t, o, s in zip(tensors, offs, sizes)]
+            K.copy_segments(segs, self.device, flag_ptr=self._peer.ptr + self.flag_off +
+                            slot * FLAG_STRIDE, flag_value=seq & 0xFFFFFFFF)
+            for t in tensors:
+                t.record_stream(self._stream)
+            done = self._stream.record_event()
+        self._outbox.put({
+            "cmd": "PUT_RING", "kind": kind, "request_id": request_id,
+            "layer_names": list(layer_names), "meta": meta, "n_body": n_body,
+            "specs": [{"shape": list(t.shape), "dtype": str(t.dtype).replace("torch.", ""),
+                       "off": base + o, "nbytes": s} for t, o, s in zip(tensors, offs, sizes)],
+            "region": [base, total], "slot": slot, "seq": seq})
+        with self._pending_cv:
+            self._pending.append((done, request_id, member_tids, sum(sizes), t0))
+            self._pending_cv.notify_all()
+
+    def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
+        assert self.is_sender
+        self._put(request_id, layer_names, [stacked_kv.to(self.device).contiguous()], 1, None,
+                  "raw", None)
+
+    def send_bundle(self, request_id: str, layer_names: list[str], meta: dict,
+                    body_chunks: list[torch.Tensor], aux_tensors: list[torch.Tensor],
+                    member_tids: Optional[list[str]] = None) -> None:
+        assert self.is_sender
+        body = [t.to(self.device).contiguous() for t in body_chunks]
+        aux = [t.to(self.device).contiguous() for t in aux_tensors]
+        self._put(request_id, layer_names, body + aux, len(body), meta, "bundle", member_tids)
+
+    def sent_layers(self, transfer_id: str) -> int:
+        with self._lock:
+            return self._sent.get(transfer_id, 0)
+
+    def clear_sent(self, transfer_id: str) -> None:
+        with self._lock:
+            self._sent.pop(transfer_id, None)
+
+    def wait_for_sent(self, timeout_s: Optional[float] = None) -> bool:
+        deadline = None if timeout_s is None else time.monotonic() + timeout_s
+        with self._pending_cv:
+            while self._pending:
+                left = None if deadline is None else deadline - time.monotonic()
+                if left is not None and left <= 0:
+                    return False
+                self._pending_cv.wait(timeout=0.2 if left is None else min(left, 0.2))
+        return True
+
+    # ============================================================ consumer
+    def _consumer_io(self) -> None:
+        while not self._closed:
+            try:
+                self._flush_releases()
+                got = self._ctl.poll(5)
+                if got is None:
+                    continue
+                ident, msg = got
+                cmd = msg.get("cmd")
+                if cmd == "RING_HELLO":
+                    self._producer_id = ident
+                    self._ctl.reply(ident, pack({
+                        "handle": self._region.ipc_handle(), "nbytes": self._region.nbytes,
+                        "ring_bytes": self.ring_bytes, "flag_off": self.flag_off,
+                        "n_flags": self.n_flags}))
+                elif cmd == "PUT_RING":
+                    self._on_put(msg)
+                else:
+                    logger.warning("p2p: unknown control message %r", cmd)
+            except Exception as e:  # noqa: BLE001
+                logger.error("p2p consumer io error: %s", e)
+
+    def _on_put(self, msg: dict) -> None:
+        views = [tensor_view(self._region.ptr + s["off"], s["nbytes"], getattr(torch, s["dtype"]),
+                             s["shape"], self.local_rank) for s in msg["specs"]]
+        ring = {"slot": msg["slot"], "seq": msg["seq"], "region": tuple(msg["region"])}
+        if msg["kind"] == "raw":
+            payload = {"__ring_raw__": True, "tensor": views[0], "__ring__": ring}
+        else:
+            n = msg["n_body"]
+            payload = {"__bundle__": True, "meta": msg["meta"], "body_chunks": views[:n],
+                       "aux_tensors": views[n:], "__ring__": ring}
+        with self._lock:
+            self._received[msg["request_id"]].append((msg["layer_names"], payload))
+
+    def drain_received(self) -> dict[str, list[tuple[list[str], Any]]]:
+        assert not self.is_sender
+        with self._lock:
+            out = {k: list(v) for k, v in self._received.items() if v}
+            self._received.clear()
+        return out
+
+    def prepare(self, payload: Any, device: Optional[torch.device] = None) -> None:
+        """Make the current stream wait (bounded, on the device) until the
+        payload's bytes have landed."""
+        if not isinstance(payload, dict) or "__ring__" not in payload:
+            return
+        from kvserve_hpdps_b200.ops import kernels as K
+        r = payload["__ring__"]
+        K.wait_flag(self._region.ptr + self.flag_off + r["slot"] * FLAG_STRIDE,
+                    r["seq"] & 0xFFFFFFFF, device or self.device, timeout_s=self.flag_timeout_s)
+
+    def release(self, payload: Any, device: Optional[torch.device] = None) -> None:
+        """Return the payload's ring space once the work queued so far on the
+        current stream (its decode) has finished."""
+        if not isinstance(payload, dict) or "__ring__" not in payload:
+            return
+        ev = torch.cuda.current_stream(device or self.device).record_event()
+        off, size = payload["__ring__"]["region"]
+        with self._lock:
+            self._releases.append((ev, off, size))
+
+    def _flush_releases(self) -> None:
+        done = []
+        with self._lock:
+            while self._releases and self._releases[0][0].query():
+                _, off, size = self._releases.popleft()
+                done.append([off, size])
+        if done and self._producer_id is not None:
+            self._ctl.reply(self._producer_id, pack({"cmd": "FREE", "regions": done}))
+
+    def close(self) -> None:
+        self._closed = True
+        try:
+            self._ctl.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def is_ring_raw(payload: Any) -> bool:
+    return isinstance(payload, dict) and payload.get("__ring_raw__", False)
+
+
+__all__ = ["P2PTransport", "RingAllocator", "tensor_view", "is_ring_raw", "FAILED_PAYLOAD",
+           "FAILED_LAYER_NAMES"]

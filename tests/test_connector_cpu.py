@@ -1,0 +1,141 @@
+"""Connector tests on CPU with mocked vLLM objects and the in-process
+transport: scheduler bookkeeping, producer -> consumer handoff (raw and
+compressed through the generic pipeline) into different block ids, and
+failure paths injected on the host."""
+
+import os
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+os.environ["KVSERVE_TRANSPORT"] = "fake"
+
+from kvserve_hpdps_b200.connector.compressed_kv_connector import (  # noqa: E402
+    CompressedKVConnector, CompressedKVConnectorMetadata, KVConnectorRole, layer_index)
+from kvserve_hpdps_b200.parallel.fake_transport import FakeTransportPair  # noqa: E402
+
+L, H, D, BS = 3, 4, 128, 16
+
+
+def vllm_config(producer: bool, compression=None):
+    mc = SimpleNamespace(get_num_kv_heads=lambda pc: H, get_head_size=lambda: D,
+                         get_num_layers=lambda pc: L, model="/models/Qwen2.5-7B-Instruct",
+                         hf_text_config=SimpleNamespace(num_hidden_layers=L), use_mla=False)
+    kv = SimpleNamespace(is_kv_producer=producer, kv_ip="127.0.0.1", kv_port=25010,
+                         kv_connector_extra_config={"compression": compression})
+    return SimpleNamespace(kv_transfer_config=kv, cache_config=SimpleNamespace(block_size=BS),
+                           model_config=mc, parallel_config=SimpleNamespace())
+
+
+def make_pair(compression=None):
+    pair = FakeTransportPair()
+    p = CompressedKVConnector(vllm_config(True, compression), KVConnectorRole.WORKER)
+    c = CompressedKVConnector(vllm_config(False, compression), KVConnectorRole.WORKER)
+    p.attach_transport(pair.producer())
+    c.attach_transport(pair.consumer())
+    return p, c, pair
+
+
+def caches(nblocks, seed):
+    g = torch.Generator().manual_seed(seed)
+    return {f"model.layers.{l}.self_attn.attn":
+            torch.randn(2, nblocks, BS, H, D, generator=g).to(torch.bfloat16) for l in range(L)}
+
+
+def meta_for(rid, tid, ntok, blocks):
+    m = CompressedKVConnectorMetadata()
+    m.add_request(rid, tid, list(range(ntok)), blocks, BS)
+    return m
+
+
+def handoff(p, c, ntok=40, src_blocks=(5, 1, 7), dst_blocks=(2, 6, 0)):
+    pc, cc = caches(8, 1), caches(8, 2)
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    p.bind_connector_metadata(meta_for("r1", "tid-1", ntok, list(src_blocks)))
+    for name in sorted(pc, key=layer_index):
+        p.save_kv_layer(name, pc[name], None)
+    p.wait_for_save()
+    c.bind_connector_metadata(meta_for("d1", "tid-1", ntok, list(dst_blocks)))
+    c.start_load_kv(None)
+    return pc, cc
+
+
+def test_layer_index_and_layout():
+    assert layer_index("model.layers.10.self_attn.attn") == 10
+    assert CompressedKVConnector.get_required_kvcache_layout(vllm_config(True)) == "NHD"
+
+
+def test_raw_handoff_is_exact():
+    p, c, pair = make_pair(None)
+    pc, cc = handoff(p, c)
+    for name in pc:
+        assert torch.equal(cc[name][:, [2, 6, 0]], pc[name][:, [5, 1, 7]])
+    assert pair.messages == 1
+
+
+def test_generic_compressed_handoff():
+    spec = {"enabled": True, "pipeline": ["transformer", "quantizer", "codec"],
+            "transformer_config": {"seed": 0x3333},
+            "quantizer_config": {"hybrid_ratio": 0.3, "high_key_max_value": 16,
+                                 "high_value_max_value": 16, "low_key_max_value": 12,
+                                 "low_value_max_value": 12, "axis_key": "token",
+                                 "axis_value": "token"},
+            "codec_config": {"codec_type": "rans"}, "backend": "generic"}
+    p, c, pair = make_pair(spec)
+    pc, cc = handoff(p, c)
+    for name in pc:
+        a = pc[name][:, [5, 1, 7]].float().flatten()
+        b = cc[name][:, [2, 6, 0]].float().flatten()
+        assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.97
+
+
+def test_refused_and_dropped_messages_do_not_hang(monkeypatch):
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.3)
+    p, c, pair = make_pair(None)
+    pair.refuse_next = 1
+    pc, cc = handoff(p, c)  # FAILED sentinel: logged, blocks untouched
+    assert not torch.equal(cc[next(iter(cc))][:, [2, 6, 0]], pc[next(iter(pc))][:, [5, 1, 7]])
+    pair.drop_next = 1
+    p2, c2, _ = p, c, pair
+    handoff(p2, c2)  # nothing arrives: returns after the timeout
+
+
+def test_scheduler_side_bookkeeping():
+    prod = CompressedKVConnector(vllm_config(True), KVConnectorRole.SCHEDULER)
+    cons = CompressedKVConnector(vllm_config(False), KVConnectorRole.SCHEDULER)
+    req = SimpleNamespace(request_id="r", prompt_token_ids=list(range(50)),
+                          kv_transfer_params={"transfer_id": "T9"},
+                          all_token_ids=list(range(51)))
+    assert prod.get_num_new_matched_tokens(req, 0) == (0, False)
+    assert cons.get_num_new_matched_tokens(req, 0) == (49, False)
+    assert cons.get_num_new_matched_tokens(req, 49) == (0, False)
+    blocks = SimpleNamespace(get_block_ids=lambda: ([3, 4, 5, 6],))
+    cons.update_state_after_alloc(req, blocks, 49)
+    prod.update_state_after_alloc(req, blocks, 0)
+    new = SimpleNamespace(req_id="r", prompt_token_ids=list(range(50)), block_ids=([3, 4, 5, 6],),
+                          num_computed_tokens=0)
+    empty_cached = SimpleNamespace(req_ids=[], num_computed_tokens=[], new_block_ids=[],
+                                   resumed_req_ids=set())
+    so = SimpleNamespace(scheduled_new_reqs=[new], num_scheduled_tokens={"r": 50},
+                         scheduled_cached_reqs=empty_cached)
+    mc = cons.build_connector_meta(so)
+    assert [(m.request_id, m.transfer_id, m.block_ids) for m in mc.requests] == [("r", "T9", [3, 4, 5, 6])]
+    assert cons.build_connector_meta(so).requests == []  # loaded once
+    mp = prod.build_connector_meta(so)
+    assert mp.requests[0].transfer_id == "T9" and len(mp.requests[0].token_ids) == 50
+    assert mp.requests[0].slot_mapping[:3].tolist() == [48, 49, 50]
+    # chunked prefill: deferred until the whole prompt has KV
+    so1 = SimpleNamespace(scheduled_new_reqs=[SimpleNamespace(
+        req_id="c", prompt_token_ids=list(range(40)), block_ids=([1, 2],), num_computed_tokens=0)],
+        num_scheduled_tokens={"c": 32}, scheduled_cached_reqs=empty_cached)
+    assert prod.build_connector_meta(so1).requests == []
+    cached = SimpleNamespace(req_ids=["c"], num_computed_tokens=[32], new_block_ids=[([9],)],
+                             resumed_req_ids=set())
+    so2 = SimpleNamespace(scheduled_new_reqs=[], num_scheduled_tokens={"c": 8},
+                          scheduled_cached_reqs=cached)
+    m2 = prod.build_connector_meta(so2)
+    assert m2.requests[0].block_ids == [1, 2, 9]
+    assert prod.request_finished(req, []) == (False, None)
