@@ -1,0 +1,151 @@
+"""Connector on GPUs: the fused default-mode path through the in-process
+transport (1 GPU, both overlap modes) and the NVLink ring transport between
+two processes on two GPUs (raw and compressed)."""
+
+import multiprocessing as mp
+import os
+import socket
+import time
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+os.environ.setdefault("KVSERVE_TRANSPORT", "fake")
+
+pytestmark = pytest.mark.gpu
+
+L, H, D, BS = 4, 4, 128, 16
+
+
+def vllm_config(producer, compression, port=25010, transport=None):
+    mc = SimpleNamespace(get_num_kv_heads=lambda pc: H, get_head_size=lambda: D,
+                         get_num_layers=lambda pc: L, model="/m/Qwen2.5-7B-Instruct",
+                         hf_text_config=SimpleNamespace(num_hidden_layers=L), use_mla=False)
+    extra = {"compression": compression}
+    if transport:
+        extra["transport"] = transport
+    kv = SimpleNamespace(is_kv_producer=producer, kv_ip="127.0.0.1", kv_port=port,
+                         kv_connector_extra_config=extra)
+    return SimpleNamespace(kv_transfer_config=kv, cache_config=SimpleNamespace(block_size=BS),
+                           model_config=mc, parallel_config=SimpleNamespace())
+
+
+def _caches(nblocks, seed, device, fill=True):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    out = {}
+    for l in range(L):
+        t = torch.randn(2, nblocks, BS, H, D, generator=g) if fill else torch.zeros(2, nblocks, BS, H, D)
+        out[f"model.layers.{l}.self_attn.attn"] = t.to(device=device, dtype=torch.bfloat16)
+    return out
+
+
+def _meta(reqs):
+    from kvserve_hpdps_b200.connector.compressed_kv_connector import CompressedKVConnectorMetadata
+    m = CompressedKVConnectorMetadata()
+    for rid, tid, ntok, blocks in reqs:
+        m.add_request(rid, tid, list(range(ntok)), blocks, BS)
+    return m
+
+
+def _cos(a, b):
+    return float(torch.nn.functional.cosine_similarity(a.float().flatten(), b.float().flatten(), dim=0))
+
+
+@pytest.mark.parametrize("overlap", ["off", "stream"])
+def test_fused_default_handoff_in_process(overlap, monkeypatch):
+    monkeypatch.setenv("KVSERVE_OVERLAP_MODE", overlap)
+    from kvserve_hpdps_b200.connector.compressed_kv_connector import (CompressedKVConnector,
+                                                                      KVConnectorRole)
+    from kvserve_hpdps_b200.parallel.fake_transport import FakeTransportPair
+    pair = FakeTransportPair()
+    p = CompressedKVConnector(vllm_config(True, "default"), KVConnectorRole.WORKER)
+    c = CompressedKVConnector(vllm_config(False, "default"), KVConnectorRole.WORKER)
+    p.attach_transport(pair.producer())
+    c.attach_transport(pair.consumer())
+    pc, cc = _caches(24, 1, "cuda"), _caches(24, 2, "cuda", fill=False)
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    reqs_p = [("a", "ta", 100, [3, 9, 1, 17, 5, 20, 11]), ("b", "tb", 40, [0, 6, 22])]
+    reqs_c = [("da", "ta", 100, [4, 2, 8, 10, 12, 14, 16]), ("db", "tb", 40, [23, 1, 3])]
+    p.bind_connector_metadata(_meta(reqs_p))
+    for name in sorted(pc):
+        p.save_kv_layer(name, pc[name], None)
+    p.wait_for_save()
+    torch.cuda.synchronize()
+    c.bind_connector_metadata(_meta(reqs_c))
+    c.start_load_kv(None)
+    torch.cuda.synchronize()
+    for (rp, _, n, bp), (rc, _, _, bcs) in zip(reqs_p, reqs_c):
+        for name in pc:
+            src = pc[name][:, bp].reshape(2, -1, H, D)[:, :n]
+            dst = cc[name][:, bcs].reshape(2, -1, H, D)[:, :n]
+            assert _cos(src, dst) > 0.9, (rp, name)
+    assert pair.messages == (L if overlap == "stream" else 2)
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _role(producer, port, compression, q):
+    try:
+        torch.cuda.set_device(0 if producer else 1)
+        os.environ["KVSERVE_TRANSPORT"] = "p2p"
+        os.environ["KVSERVE_RING_BYTES"] = str(256 << 20)
+        from kvserve_hpdps_b200.connector.compressed_kv_connector import (CompressedKVConnector,
+                                                                          KVConnectorRole)
+        conn = CompressedKVConnector(vllm_config(producer, compression, port, "p2p"),
+                                     KVConnectorRole.WORKER)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        caches = _caches(16, 7, dev, fill=producer)
+        conn.register_kv_caches(caches)
+        blocks_p, blocks_c = [5, 1, 12, 7, 3], [2, 9, 0, 14, 6]
+        if producer:
+            conn.bind_connector_metadata(_meta([("r", "t", 70, blocks_p)]))
+            for name in sorted(caches):
+                conn.save_kv_layer(name, caches[name], None)
+            conn.wait_for_save()
+            conn._transport.wait_for_sent(30)
+            torch.cuda.synchronize()
+            time.sleep(2.0)
+            q.put(("p", "ok"))
+        else:
+            conn.bind_connector_metadata(_meta([("d", "t", 70, blocks_c)]))
+            conn.start_load_kv(None)
+            torch.cuda.synchronize()
+            from kvserve_hpdps_b200.ops import kernels as K
+            err = K.read_device_error(dev)
+            ref = _caches(16, 7, dev, fill=True)
+            cos = min(_cos(ref[n][:, blocks_p].reshape(2, -1, H, D)[:, :70],
+                           caches[n][:, blocks_c].reshape(2, -1, H, D)[:, :70]) for n in caches)
+            q.put(("c", (err, cos)))
+        conn.shutdown()
+    except Exception as e:  # noqa: BLE001
+        import traceback
+        q.put(("err", traceback.format_exc()))
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("compression", [None, "default"])
+def test_p2p_ring_handoff_two_gpus(compression):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    c = ctx.Process(target=_role, args=(False, port, compression, q))
+    c.start()
+    time.sleep(3.0)
+    p = ctx.Process(target=_role, args=(True, port, compression, q))
+    p.start()
+    results = {}
+    for _ in range(2):
+        k, v = q.get(timeout=240)
+        assert k != "err", v
+        results[k] = v
+    p.join(60)
+    c.join(60)
+    err, cos = results["c"]
+    assert err == 0
+    assert cos > (0.999 if compression is None else 0.9)
