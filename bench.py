@@ -364,7 +364,12 @@ def run_ours(args, rank, world, local):
     if not args.no_e2e:
         e2e = run_e2e_ours(args, mgr, wl, role, world, rank, pairs, device)
 
-    # aggregate compression stats
+    # aggregate compression stats; reconstruction error from a consumer rank
+    if world > 1:
+        import torch.distributed as dist
+        gathered = [None] * world
+        dist.all_gather_object(gathered, stats.get("error"))
+        stats["error"] = next((g for g in gathered if g is not None), None)
     stream_bytes = allreduce_sum(float(stats.get("stream_bytes", 0)), world)
     n_prod = pairs if world > 1 else 1
     orig = wl.bf16_bytes_per_request * wl.B * n_prod

@@ -266,6 +266,49 @@ KVS_DEV void value_row_params(const LayerLaunch& L, const ItemCtx& c, int h, int
   }
 }
 
+// Epilogue of the MMA quant kernel: read this thread's row (its TMEM lane),
+// quantize, pack to W bits and stage the 16*W-byte row in shared memory with
+// an odd pitch of (W|1) 16-byte chunks, so the 8 threads sharing a bank
+// group write different groups.
+struct QuantArgs {
+  uint32_t taddr;  // TMEM address of this warp's lanes
+  float out_scale, top;
+  bool valid;
+  int plane;
+  float vmin, vrcp;
+  const float* s_min;
+  const float* s_rcp;
+  uint8_t* stage;
+};
+
+template <int W>
+KVS_DEV void quant_epilogue(const QuantArgs& a) {
+  uint32_t words[4 * W];
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    float v[32];
+    tmem_ld32(a.taddr + cc * 32, v);
+    uint32_t q[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = cc * 32 + j;
+      const float val = a.valid ? bf16_round(v[j] * a.out_scale) : 0.0f;
+      q[j] = a.plane == 0 ? quantize_one(val, a.s_min[n], a.s_rcp[n], a.top)
+                          : quantize_one(val, a.vmin, a.vrcp, a.top);
+    }
+    uint32_t w[8];
+    pack32<W>(q, w);
+#pragma unroll
+    for (int i = 0; i < W; ++i) words[cc * W + i] = w[i];
+  }
+  constexpr int P = W | 1;
+  uint8_t* dst = a.stage + threadIdx.x * P * 16;
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    *reinterpret_cast<uint4*>(dst + k * 16) =
+        make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+}
+
 // ================================================================== stats
 __global__ void __launch_bounds__(128) k_stats_simt(LayerLaunch L) {
   extern __shared__ float buf[];  // [128][129] (keys only)
@@ -472,26 +515,31 @@ __global__ void __launch_bounds__(128) k_quant_mma(LayerLaunch L) {
   tc_fence_after();
   const float lev = plane == 0 ? c.lp->key_levels[h] : c.lp->value_levels[h];
   const float top = c.lp->clamp_top ? lev - 1.0f : lev;
-  const float sc = c.lp->out_scale;
-  uint8_t* out = exists ? code_row(L, c, plane, h, row) : nullptr;
-  const int bits = seg_bits(c, plane, h);
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {
-    float v[32];
-    tmem_ld32(tmem + lane_base + cc * 32, v);
-    uint32_t q[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = cc * 32 + j;
-      const float val = valid ? bf16_round(v[j] * sc) : 0.0f;
-      q[j] = plane == 0 ? quantize_one(val, s_min[n], s_rcp[n], top)
-                        : quantize_one(val, vmin, vrcp, top);
-    }
-    if (exists) store_chunk(out, cc, bits, q);
+  const QuantArgs qa{tmem + (static_cast<uint32_t>(warp * 32) << 16), c.lp->out_scale, top, valid,
+                     plane, vmin, vrcp, s_min, s_rcp, sT};
+  // sT (the data tile) is free: the MMA that read it has completed.
+  switch (seg_bits(c, plane, h)) {
+    case 1: quant_epilogue<1>(qa); break;
+    case 2: quant_epilogue<2>(qa); break;
+    case 3: quant_epilogue<3>(qa); break;
+    case 4: quant_epilogue<4>(qa); break;
+    case 5: quant_epilogue<5>(qa); break;
+    case 6: quant_epilogue<6>(qa); break;
+    case 7: quant_epilogue<7>(qa); break;
+    default: quant_epilogue<8>(qa); break;
   }
   tc_fence_before();
   __syncthreads();
+  // Coalesced copy of the tile's contiguous code region.
+  const int bits = seg_bits(c, plane, h);
+  const int nrows = min(kTileRows, c.rows - c.row0);
+  uint8_t* dst0 = code_row(L, c, plane, h, c.row0);
+  const int P = bits | 1;  // staging pitch in 16-byte chunks (odd: bank-conflict free)
+  for (int k = tid; k < nrows * bits; k += 128) {
+    const int r = k / bits, col = k - r * bits;
+    *reinterpret_cast<uint4*>(dst0 + static_cast<long long>(k) * 16) =
+        *reinterpret_cast<const uint4*>(sT + (r * P + col) * 16);
+  }
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
@@ -633,26 +681,49 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
   tc_fence_after();
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const float sc = c.lp->out_scale;
-  __nv_bfloat16* dst =
-      valid ? kv_row(c, kv, phys_block(L, c, row), row % c.kv.block_size, h) : nullptr;
+  // The dequantized tile sA was consumed by the MMA: reuse it to stage the
+  // bf16 output in the 128-byte swizzled layout of the destination map.
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
     float v[32];
     tmem_ld32(tmem + lane_base + cc * 32, v);
-    if (valid) {
-      uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j] * sc, v[2 * j + 1] * sc);
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 p =
+            __floats2bfloat162_rn(v[8 * q + 2 * j] * sc, v[8 * q + 2 * j + 1] * sc);
         w[j] = *reinterpret_cast<const uint32_t*>(&p);
       }
-      uint4* d = reinterpret_cast<uint4*>(dst + cc * 32);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      *reinterpret_cast<uint4*>(sA + sw128_offset(tid, cc * 32 + q * 8)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+  fence_proxy_async_smem();
   tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    // One TMA tensor store per 16-row group and 64-channel half (full
+    // 128-byte lines into the paged cache; the groups never straddle blocks).
+    const CUtensorMap* map = map_of(L, c.slot, kv);
+    for (int g = 0; g < 8; ++g) {
+      const int rr = c.row0 + g * 16;
+      if (rr >= c.rows) break;
+      const int phys = phys_block(L, c, rr);
+      const int slot = rr % c.kv.block_size;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        asm volatile(
+            "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
+                "l"(reinterpret_cast<uint64_t>(map)),
+            "r"(hb * 64), "r"(h), "r"(slot), "r"(phys), "r"(smem_u32(sA + hb * 16384 + g * 2048))
+            : "memory");
+      }
+    }
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 128);
 }

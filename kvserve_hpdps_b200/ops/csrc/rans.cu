@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
   uint32_t* h = hist[warp];
   for (int i = lane; i < 4 * 256; i += 32) h[i] = 0;
   __syncwarp();
+  // Histogram in four lane-interleaved copies (lane & 3): spreads the
+  // atomic traffic of skewed symbol distributions over four addresses.
   uint32_t* hc = h + (lane & 3) * 256;
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
     const uint4 v = load_syms(src, ss, lane, n_sym);
