@@ -170,5 +170,5 @@ class CompressionManager:
                                             "t_dequant_ms": (time.monotonic() - t0) * 1e3}
             return out
         except Exception as e:  # noqa: BLE001
-            logger.error("decompression failed for %s: %s", compressed.request_id, e)
+            logger.error("decompression failed for %s: %s", getattr(compressed, "request_id", None), e)
             return None
