@@ -155,8 +155,8 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._model_name = os.path.basename(str(mc.model).rstrip("/"))
         self._tp_rank, self._tp_size = 0, 1
         # overlap mode
-        self._overlap_mode = "off"
-        if isinstance(self._compression_cfg, dict):
+        self._overlap_mode = str(extra.get("overlap", "off"))
+        if isinstance(self._compression_cfg, dict) and "overlap" in self._compression_cfg:
             self._overlap_mode = self._compression_cfg.get("overlap", "off")
         self._overlap_mode = os.environ.get("KVSERVE_OVERLAP_MODE", self._overlap_mode)
         prio = int(self._compression_cfg.get("side_stream_priority", 0)) \

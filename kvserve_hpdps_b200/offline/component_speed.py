@@ -1,0 +1,127 @@
+"""Component speed of the compression kernels (encode / decode GB/s).
+
+The reference measures each stage separately (Hadamard, quantizer, codec)
+over 1K-32K tokens and records GB/s of original KV
+(kvserve_v1/offline_search/evaluation/component_speed/*.py, results/*.csv).
+Here the stages are the fused kernels of this package:
+
+* ``quant``:   paged gather + Hadamard (tcgen05) + stats + quantize
+               (one stats launch and one quantize launch per call);
+* ``dequant``: dequantize + inverse Hadamard + paged scatter;
+* ``rans_enc`` / ``rans_dec``: the interleaved rANS codec over the codes;
+* ``block_copy``: the paged gather of raw KV (the uncompressed path).
+
+Every figure is CUDA-event time on the launching stream after warm-up,
+averaged over ``--iters`` launches; the input of a full request (28 layers,
+8K tokens, 4 heads: 470 MB) is larger than L2, so no flush is needed at
+that size.  Rates are GB/s of ORIGINAL bf16 KV (the reference's unit).
+
+Usage::
+
+  python -m kvserve_hpdps_b200.offline.component_speed --layers 28 --tokens 8192
+  python -m kvserve_hpdps_b200.offline.component_speed --only quant --layers 2 --iters 3
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import torch
+
+STAGES = ("quant", "dequant", "rans_enc", "rans_dec", "block_copy")
+
+
+def _timeit(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
+        only: tuple[str, ...] = STAGES, engine: int = 0, seed: int = 1,
+        key_levels=(12, 6, 6, 6), value_levels=(8, 4, 4, 4), warmup: int = 3) -> list[dict]:
+    from kvserve_hpdps_b200.models.synthetic import paged_workload
+    from kvserve_hpdps_b200.ops import kernels as K
+    wl = paged_workload(layers, [tokens], heads, device="cuda", seed=seed, fill=False)
+    wl.cache.normal_()
+    wl.cache[:, 0, :, :, :, :4].mul_(12.0)  # outlier channels in K
+    kl = list(key_levels)[:heads] + [key_levels[-1]] * max(0, heads - len(key_levels))
+    vl = list(value_levels)[:heads] + [value_levels[-1]] * max(0, heads - len(value_levels))
+    plans = [K.make_layer_plan(heads, kl, vl, 0x3333, l) for l in range(layers)]
+    slots = K.LayerSlots([wl.cache[l] for l in range(layers)], plans)
+    items = K.WorkItems(slots, [(l, wl.block_ids[0], tokens) for l in range(layers)])
+    dst = torch.zeros_like(wl.cache)
+    dslots = K.LayerSlots([dst[l] for l in range(layers)], plans)
+    nbytes = layers * 2 * tokens * heads * 128 * 2
+    codes, meta = K.quantize(slots, items, engine=engine)
+    n = codes.numel()
+    stream = K.rans_encode(codes)
+    rows = []
+
+    def row(stage, ms, **kw):
+        rows.append({"stage": stage, "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
+                     "layers": layers, "tokens": tokens, "heads": heads, **kw})
+
+    if "quant" in only:
+        row("quant", _timeit(lambda: K.quantize(slots, items, codes=codes, meta=meta,
+                                                engine=engine), iters, warmup), engine=engine)
+    if "dequant" in only:
+        row("dequant", _timeit(lambda: K.dequantize(codes, meta, dslots, items, engine=engine),
+                               iters, warmup), engine=engine)
+    if "rans_enc" in only:
+        out = torch.empty(K.rans_max_bytes(n), dtype=torch.uint8, device="cuda")
+        row("rans_enc", _timeit(lambda: K.rans_encode(codes, out=out, trim=False), iters, warmup),
+            code_bytes=n, stream_bytes=int(stream.numel()),
+            bits_per_code=round(8 * stream.numel() / n, 4))
+    if "rans_dec" in only:
+        dec = torch.empty(n, dtype=torch.uint8, device="cuda")
+        row("rans_dec", _timeit(lambda: K.rans_decode(stream, n, out=dec), iters, warmup),
+            exact=bool(torch.equal(K.rans_decode(stream, n), codes)))
+    if "block_copy" in only:
+        flat = torch.empty(nbytes // layers, dtype=torch.uint8, device="cuda")
+        blocks = torch.tensor(wl.block_ids[0], dtype=torch.int32, device="cuda")
+
+        def copy_all():
+            for l in range(layers):
+                K.block_copy(wl.cache[l], blocks, flat.data_ptr(), True)
+        row("block_copy", _timeit(copy_all, iters, warmup))
+    K.dequantize(codes, meta, dslots, items, engine=engine)
+    err = K.kv_error(wl.cache[:, :, wl.block_ids[0]], dst[:, :, wl.block_ids[0]])
+    rows.append({"stage": "summary", "original_bytes": nbytes,
+                 "compressed_bytes": int(stream.numel() + meta.numel()),
+                 "compression_ratio": round(nbytes / (stream.numel() + meta.numel()), 3),
+                 "rel_mse": err["rel_mse"], "cosine": err["cosine"],
+                 "device_error": K.read_device_error(wl.cache.device)})
+    return rows
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description="component speed of the compression kernels")
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--heads", type=int, default=4)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--engine", type=int, default=0, help="0 = tcgen05, 1 = SIMT")
+    ap.add_argument("--only", default=",".join(STAGES))
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        print(json.dumps({"unavailable": "no CUDA device"}))
+        return 0
+    for r in run(args.layers, args.tokens, args.heads, args.iters,
+                 tuple(args.only.split(",")), args.engine, warmup=args.warmup):
+        print(json.dumps(r))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
