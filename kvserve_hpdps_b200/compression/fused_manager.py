@@ -47,7 +47,7 @@ BACKEND = "kvs_fused"
 
 def _engine_from_env() -> int:
     v = os.environ.get("KVSERVE_ENGINE", "tcgen05").lower()
-    return 1 if v in ("simt", "1") else 0
+    return {"simt": 1, "1": 1, "tile": 2, "2": 2}.get(v, 0)
 
 
 @dataclass
@@ -164,23 +164,30 @@ class FusedCompressionManager:
         """Compress the given layers of several requests into ONE message:
         one codec stream over every (layer, request) item, layer-major.
 
-        Metadata: ``grouped=True, layout="items"``, ``member_tids``,
-        ``member_tokens``, ``member_blocks``, ``layer_ids`` and one wire-form
-        ``quantization_params`` entry per item (layer-major)."""
+        Metadata: ``grouped=True, layout="items_packed"``, ``member_tids``,
+        ``member_tokens``, ``member_blocks``, ``layer_ids``, ``layer_plans``
+        (per layer: value group of each head and code bits, plain ints) and
+        ``quantization_params = [meta]``: the fp16 metadata of every item in
+        the kernels' device layout as ONE aux tensor (item offsets follow from
+        the plans and block counts).  Decoders also accept the per-item
+        ``layout="items"`` form."""
         batch = self.quantize_paged(kv_layers, layer_ids, requests)
         body = encode_bytes(batch.codes[:batch.items.code_bytes], self.stream_codec) if trim \
             else self._encode_untrimmed(batch.codes[:batch.items.code_bytes])
         items = batch.items
-        qparams = [self.canon_meta(batch.meta, items.meta_off[r], batch.plans[items.items[r][0]],
-                                   items.n_rows[r]) for r in range(items.num_items)]
         H = self.num_kv_heads
-        meta = {"grouped": True, "layout": "items", "layer_ids": [int(l) for l in layer_ids],
+        meta = {"grouped": True, "layout": "items_packed", "layer_ids": [int(l) for l in layer_ids],
                 "member_tids": list(member_tids) if member_tids else
                 [str(i) for i in range(len(requests))],
                 "member_tokens": [int(n) for _, n in requests],
                 "member_blocks": [len(b) for b, _ in requests],
                 "block_size": int(kv_layers[0].shape[2]), "num_heads": H,
-                "device": str(batch.codes.device), "quantization_params": qparams,
+                "device": str(batch.codes.device),
+                "layer_plans": [{"group_of_head": list(p.group_of_head),
+                                 "code_bits": list(p.key_bits) + list(p.value_bits)}
+                                for p in batch.plans],
+                "meta_bytes": int(items.meta_bytes),
+                "quantization_params": [batch.meta[:max(items.meta_bytes, 16)]],
                 "code_bytes": int(items.code_bytes), "backend": BACKEND, "codec": self.codec,
                 "stream_codec": self.stream_codec, "transform_seed": self.base_seed}
         orig = sum(len(kv_layers) * 2 * n * H * self.head_size * 2 for _, n in requests)
@@ -188,6 +195,42 @@ class FusedCompressionManager:
         return CompressedKVData(request_id="grp", layer_id=int(layer_ids[-1]),
                                 compressed_tensor=body, metadata=meta, original_size=orig,
                                 compressed_size=int(body.numel()))
+
+    def _message_plans(self, meta: dict) -> list:
+        """Consumer-side plans of a grouped message, one per layer."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        seed = meta.get("transform_seed", self.base_seed)
+        layer_ids = meta["layer_ids"]
+        if meta.get("layout") == "items_packed":
+            cache = self.__dict__.setdefault("_decode_plans", {})
+            out = []
+            for lid, lp in zip(layer_ids, meta["layer_plans"]):
+                goh, bits = tuple(lp["group_of_head"]), tuple(lp["code_bits"])
+                H = len(goh)
+                key = (H, goh, bits, seed, int(lid))
+                if key not in cache:
+                    cache[key] = K.decode_plan(H, list(goh), list(bits[:H]), list(bits[H:]),
+                                               seed, int(lid))
+                out.append(cache[key])
+            return out
+        R = len(meta["member_tids"])
+        qp = meta["quantization_params"]
+        return [self.plan_from_canon(qp[i * R], layer_ids[i], seed) for i in range(len(layer_ids))]
+
+    @staticmethod
+    def _message_offsets(meta: dict, plans: Sequence[Any]) -> tuple[list[int], list[int]]:
+        """Code and metadata offsets of every (layer, member) item of the
+        producer's message (layer-major; same rule as the kernels' layout)."""
+        bs = int(meta["block_size"])
+        co, mo, c, m = [], [], 0, 0
+        for plan in plans:
+            for nb in meta["member_blocks"]:
+                rows = nb * bs
+                co.append(c)
+                mo.append(m)
+                c += (rows * plan.row_bytes() + 15) & ~15
+                m += (plan.meta_bytes(rows) + 15) & ~15
+        return co, mo
 
     def _encode_untrimmed(self, codes: torch.Tensor) -> torch.Tensor:
         from kvserve_hpdps_b200.compression.codec import _header
@@ -211,17 +254,21 @@ class FusedCompressionManager:
         meta = compressed.metadata
         device = dst_layers[0].device
         codes = decode_bytes(compressed.compressed_tensor, device)
-        layer_ids = meta["layer_ids"]
-        seed = meta.get("transform_seed", self.base_seed)
-        qp = meta["quantization_params"]
-        R = len(dst_requests)
-        plans = [self.plan_from_canon(qp[i * R], layer_ids[i], seed) for i in range(len(layer_ids))]
+        plans = self._message_plans(meta)
         slots = self._slots(dst_layers, plans)
         items = K.WorkItems(slots, [(i, b, n) for i in range(len(dst_layers)) for b, n in dst_requests])
-        meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=device)
-        for r in range(items.num_items):
-            m = self.meta_from_canon(qp[r])
-            meta_buf[items.meta_off[r]:items.meta_off[r] + m.numel()] = m.to(device)
+        if meta.get("layout") == "items_packed":
+            if items.meta_bytes != int(meta["meta_bytes"]):
+                raise ValueError("consumer block counts do not match the message's")
+            meta_buf = meta["quantization_params"][0]
+            if meta_buf.device != device:
+                meta_buf = meta_buf.to(device)
+        else:
+            qp = meta["quantization_params"]
+            meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=device)
+            for r in range(items.num_items):
+                m = self.meta_from_canon(qp[r])
+                meta_buf[items.meta_off[r]:items.meta_off[r] + m.numel()] = m.to(device)
         K.dequantize(codes, meta_buf, slots, items, engine=self.engine)
 
     def decompress_members(self, compressed: CompressedKVData, dst_layers: Sequence[torch.Tensor],
@@ -241,24 +288,24 @@ class FusedCompressionManager:
         codes = cache[key]
         layer_ids = meta["layer_ids"]
         R = len(meta["member_tids"])
-        seed = meta.get("transform_seed", self.base_seed)
-        qp = meta["quantization_params"]
-        plans = [self.plan_from_canon(qp[l * R], layer_ids[l], seed) for l in range(len(layer_ids))]
-        bs = int(meta["block_size"])
-        # code offsets of every item of the original message (layer-major)
-        offs, c = [], 0
-        for l in range(len(layer_ids)):
-            for r in range(R):
-                offs.append(c)
-                c += ((meta["member_blocks"][r] * bs * plans[l].row_bytes()) + 15) & ~15
+        plans = self._message_plans(meta)
+        code_offs, meta_offs = self._message_offsets(meta, plans)
         slots = self._slots(dst_layers, plans)
         sel = [(l, r) for l in range(len(layer_ids)) for r in sorted(member_blocks)]
+        packed = meta.get("layout") == "items_packed"
         items = K.WorkItems(slots, [(l, member_blocks[r], meta["member_tokens"][r]) for l, r in sel],
-                            code_offsets=[offs[l * R + r] for l, r in sel])
-        meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=device)
-        for i, (l, r) in enumerate(sel):
-            m = self.meta_from_canon(qp[l * R + r])
-            meta_buf[items.meta_off[i]:items.meta_off[i] + m.numel()] = m.to(device)
+                            code_offsets=[code_offs[l * R + r] for l, r in sel],
+                            meta_offsets=[meta_offs[l * R + r] for l, r in sel] if packed else None)
+        if packed:
+            meta_buf = meta["quantization_params"][0]
+            if meta_buf.device != device:
+                meta_buf = meta_buf.to(device)
+        else:
+            qp = meta["quantization_params"]
+            meta_buf = torch.zeros(max(items.meta_bytes, 16), dtype=torch.uint8, device=device)
+            for i, (l, r) in enumerate(sel):
+                m = self.meta_from_canon(qp[l * R + r])
+                meta_buf[items.meta_off[i]:items.meta_off[i] + m.numel()] = m.to(device)
         K.dequantize(codes, meta_buf, slots, items, engine=self.engine)
 
     # ------------------------------------------------------ canon metadata

@@ -242,6 +242,69 @@ KVS_DEV float dequant_bf16(uint32_t q, float scale_bf, float min_bf) {
   return bf16_round(__fadd_rn(prod, min_bf));
 }
 
+// ---- integer/FMA-pipe forms of the same roundings (no XU conversions) ----
+// The conversions above (cvt to bf16, floor, float<->int) issue on the
+// quarter-rate XU pipe, which bounds the epilogues; these equivalents use
+// integer and FMA-pipe instructions only and give identical results for
+// finite inputs.
+
+// Round-to-nearest-even to bf16 of a finite float, by integer arithmetic:
+// add 0x7FFF plus the lowest kept bit, then truncate (IEEE RNE at bit 16).
+KVS_DEV uint32_t bf16_rne_bits(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return u + 0x7FFFu + ((u >> 16) & 1u);  // bf16 in the high half; low half is garbage
+}
+KVS_DEV float bf16_round_fast(float x) { return __uint_as_float(bf16_rne_bits(x) & 0xFFFF0000u); }
+
+// Two bf16 (high halves of a, b) -> packed bf16x2 {lo = a, hi = b}.
+KVS_DEV uint32_t pack_bf16_hi(uint32_t a, uint32_t b) { return __byte_perm(a, b, 0x7632); }
+
+// Exact float of a small unsigned integer (< 2^23): place it in the
+// mantissa of 2^23 and subtract 2^23.
+KVS_DEV float small_uint_to_float(uint32_t q) {
+  return __fsub_rn(__uint_as_float(q | 0x4B000000u), 8388608.0f);
+}
+
+// quantize_one without XU instructions: clamp t to [0, top] first (floor is
+// monotone and top is an integer, so clamp-then-floor == floor-then-clamp),
+// then floor by adding 2^23 with round-down: the sum's mantissa holds
+// floor(t) exactly for 0 <= t < 2^23.
+KVS_DEV uint32_t quantize_fast(float v, float mn, float rcp, float top) {
+  float t = __fadd_rn(__fmul_rn(__fsub_rn(v, mn), rcp), 0.5f);
+  t = fminf(fmaxf(t, 0.0f), top);
+  return __float_as_uint(__fadd_rd(t, 8388608.0f)) - 0x4B000000u;
+}
+
+// Two floats -> packed bf16x2 {lo, hi}, round-to-nearest-even (one
+// conversion instruction for the pair).
+KVS_DEV uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+KVS_DEV float bf16lo_to_float(uint32_t p) { return __uint_as_float(p << 16); }
+KVS_DEV float bf16hi_to_float(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
+
+// quantize_fast returning the raw bits of 2^23 + code (code in the low
+// mantissa bits): callers that pack codes take the bits they need directly.
+KVS_DEV uint32_t quantize_bits(float v, float mn, float rcp, float top) {
+  float t = __fadd_rn(__fmul_rn(__fsub_rn(v, mn), rcp), 0.5f);
+  t = fminf(fmaxf(t, 0.0f), top);
+  return __float_as_uint(__fadd_rd(t, 8388608.0f));
+}
+
+// q * scale rounded once, from f = float(2^23 + q) (bits 0x4B000000 | q):
+// fma(f, scale, -2^23*scale) is exact before its single rounding because
+// 2^23*scale is exact and (2^23 + q)*scale - 2^23*scale == q*scale.
+KVS_DEV float code_times_scale(uint32_t biased_bits, float scale, float neg_2p23_scale) {
+  return __fmaf_rn(__uint_as_float(biased_bits), scale, neg_2p23_scale);
+}
+
+KVS_DEV float dequant_fast(uint32_t q, float scale_bf, float min_bf) {
+  const float prod = bf16_round_fast(__fmul_rn(small_uint_to_float(q), scale_bf));
+  return bf16_round_fast(__fadd_rn(prod, min_bf));
+}
+
 // Pack 32 codes of `W` bits each (code j at bits [j*W, j*W+W) of a
 // little-endian bit stream) into W 32-bit words.
 template <int W>

@@ -16,12 +16,14 @@
 //   k_quant_*   grid (tiles, H, 2)        codes + fp16 metadata of K and V.
 // The consumer is one launch: k_dequant_inverse_* grid (tiles, H, 2).
 //
-// Two engines with identical inputs/outputs:
-//  * engine 0 (default): 128-token tiles are fetched from the paged cache by
-//    TMA (one box per 16-row group and 64-channel half, no multicast), the
-//    128-point transform is a tcgen05.mma (bf16 x bf16 -> fp32 in TMEM)
-//    against a +-1 Hadamard matrix with the Rademacher signs folded in, and
-//    the epilogue reads the accumulator back with tcgen05.ld;
+// Three engines with identical inputs/outputs:
+//  * engine 0 (default): persistent tcgen05 kernels (k_*_tc): 128-token
+//    tiles are fetched from the paged cache by TMA (one box per 16-row group
+//    and 64-channel half, no multicast), the 128-point transform is a
+//    tcgen05.mma (bf16 x bf16 -> fp32 in TMEM) against a +-1 Hadamard matrix
+//    with the Rademacher signs folded in, the epilogue reads the accumulator
+//    back with tcgen05.ld; each CTA pipelines a contiguous range of tiles;
+//  * engine 2: the same math with one CTA per tile (k_*_mma);
 //  * engine 1: thread-per-row loads and an in-register fp32 butterfly.
 #include "common.cuh"
 #include "kvs_types.h"
@@ -221,7 +223,7 @@ KVS_DEV void issue_tile_loads(const LayerLaunch& L, const ItemCtx& c, const CUte
 // Key channel min / reciprocal scale of (item, head h) into smem; tile 0 of
 // the item publishes the fp16 metadata.
 KVS_DEV void key_channel_params(const LayerLaunch& L, const ItemCtx& c, int h, float* s_min,
-                                float* s_rcp) {
+                                float* s_rcp, int stride = 1) {
   const int n = threadIdx.x;
   const uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * c.lp->H + h) * 128 + n) * 2;
   float kmin = 0.f, kmax = 0.f;
@@ -231,8 +233,8 @@ KVS_DEV void key_channel_params(const LayerLaunch& L, const ItemCtx& c, int h, f
   }
   const float lev = c.lp->key_levels[h];
   const float scale = __fdiv_rn(fmaxf(__fsub_rn(kmax, kmin), kRangeEps), lev - 1.0f);
-  s_min[n] = kmin;
-  s_rcp[n] = __frcp_rn(scale);
+  s_min[n * stride] = kmin;
+  s_rcp[n * stride] = __frcp_rn(scale);
   if (c.row0 == 0) {
     __half* m = meta_base(L, c.r);
     m[h * 128 + n] = __float2half_rn(kmin);
@@ -728,6 +730,650 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
+// ============================================= persistent tcgen05 engine
+// One CTA per half SM (2 CTAs/SM, 256 threads each) walks a contiguous range
+// of jobs; job j = (plane, head, tile) with the tile index fastest, so
+// consecutive jobs of a CTA share the transform image (reloaded only when
+// the (layer slot, head) changes) and the key-statistics accumulators.
+// Shared memory: transform image (32 KB) + two 32 KB tile stages; TMEM: two
+// 128-column fp32 accumulators (quant/stats) or one (dequant).  The TMA
+// load of job i+1 is in flight while job i runs its MMA and epilogue.
+//
+// Warp w of the 8 reads TMEM lanes 32*(w%4).. (its quadrant) and the
+// column half w/4 of the accumulator.
+constexpr int kPThreads = 256;
+// image + 2 stages + barriers/scalars (64 B) + f0,f1 (2 KB) + red (2 KB) + 1 KB alignment slack
+constexpr int kPSmem = 3 * 32768 + 64 + 2048 + 2048 + 1024;
+
+struct PJob {
+  int plane, h, tile;
+};
+KVS_DEV PJob pjob(int j, int H, int T) {
+  PJob o;
+  const int q = j / T;
+  o.tile = j - q * T;
+  o.h = q % H;
+  o.plane = q / H;
+  return o;
+}
+
+struct PSmem;
+KVS_DEV uint8_t* pstage(const PSmem& S, int k);
+
+struct PSmem {
+  uint8_t* img;     // stage k follows at img + 32768 * (k + 1)
+  uint64_t* full;   // [2] tile stage loaded
+  uint64_t* mma;    // [2] accumulator ready
+  uint64_t* imgb;   // image loaded
+  uint32_t* tslot;
+  int* abort_flag;
+  float* f0;        // 256 floats
+  float* f1;        // 256 floats
+  float* red;       // 512 floats (cross-half reductions)
+};
+
+KVS_DEV PSmem psmem(uint8_t* raw) {
+  uint8_t* s = align1024(raw);
+  PSmem p;
+  p.img = s;
+  uint8_t* m = s + 98304;
+  p.full = reinterpret_cast<uint64_t*>(m);
+  p.mma = p.full + 2;
+  p.imgb = p.full + 4;
+  p.tslot = reinterpret_cast<uint32_t*>(m + 48);
+  p.abort_flag = reinterpret_cast<int*>(m + 52);
+  p.f0 = reinterpret_cast<float*>(m + 64);
+  p.f1 = p.f0 + 256;
+  p.red = reinterpret_cast<float*>(m + 64 + 2048);
+  return p;
+}
+
+// Jobs [j0, j1) of this CTA (the host keeps 2*H*T below 2^31).
+KVS_DEV uint8_t* pstage(const PSmem& S, int k) { return S.img + 32768 * (k + 1); }
+
+KVS_DEV void pjob_range(int J, int& j0, int& j1) {
+  j0 = static_cast<int>(static_cast<long long>(blockIdx.x) * J / gridDim.x);
+  j1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * J / gridDim.x);
+}
+
+// Thread 0: issue the tile loads of job j into `stage` (phase completes on `bar`).
+KVS_DEV void p_issue_job(const LayerLaunch& L, int j, uint8_t* stage, uint64_t* bar) {
+  const PJob jb = pjob(j, L.num_heads, L.total_tiles);
+  const ItemCtx c = item_ctx(L, jb.tile);
+  issue_tile_loads(L, c, map_of(L, c.slot, jb.plane), jb.h, stage, bar, 0u);
+}
+
+// Thread 0 after an abort: wait (bounded, no error recording) for loads
+// issued for local jobs [from, to) so that no copy is in flight at exit.
+// The abort flag is written only by thread 0 before a __syncthreads and read
+// by every thread right after it, so all threads leave the loop together.
+KVS_DEV void p_drain(const PSmem& S, int from, int to) {
+  for (int k = from; k < to; ++k)
+    mbar_wait(&S.full[k & 1], static_cast<uint32_t>((k >> 1) & 1), nullptr, 0);
+}
+
+// ------------------------------------------------------------------ stats
+__global__ void __launch_bounds__(kPThreads, 2) k_stats_tc(LayerLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  const PSmem S = psmem(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int H = L.num_heads, T = L.total_tiles;
+  int j0, j1;
+  pjob_range(2 * H * T, j0, j1);
+  const int n = j1 - j0;
+  if (n <= 0) return;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.mma[i], 1);
+    }
+    mbar_init(S.imgb, 1);
+    *S.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(S.tslot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *S.tslot;
+  int issued = 0;
+  if (tid == 0) {
+    for (; issued < 2 && issued < n; ++issued)
+      p_issue_job(L, j0 + issued, pstage(S, issued & 1), &S.full[issued & 1]);
+  }
+  int cur_img = -1;
+  uint32_t img_phase = 0;
+  // running key min/max of this thread's channel over consecutive jobs of
+  // the same (item, head)
+  float run_mn = INFINITY, run_mx = -INFINITY;
+  int run_key = -1;  // r * H + h of the running accumulation, -1 = none
+  const int lane_id = quad * 32 + lane;  // TMEM lane = channel (keys) or row (values)
+  for (int i = 0; i < n; ++i) {
+    const int s = static_cast<int>(i & 1);
+    const uint32_t ph = static_cast<uint32_t>((i >> 1) & 1);
+    const PJob jb = pjob(j0 + i, H, T);
+    const ItemCtx c = item_ctx(L, jb.tile);
+    const int img_key = c.slot * H + jb.h;
+    const uint32_t acc = tmem + static_cast<uint32_t>(s * 128);
+    if (tid == 0) {
+      bool ok = true;
+      if (img_key != cur_img) {
+        mbar_arrive_expect_tx(S.imgb, 32768u);
+        bulk_load(S.img, bmat_of(L, c.slot, jb.h), 32768, S.imgb);
+        ok = mbar_wait(S.imgb, img_phase, L.err, ERR_MBAR_TIMEOUT);
+        img_phase ^= 1u;
+      }
+      ok = ok && mbar_wait(&S.full[s], ph, L.err, ERR_MBAR_TIMEOUT);
+      if (ok) {
+        tc_fence_after();
+        if (jb.plane == 0) {
+          umma_tile_128x128x128(acc, smem_u32(S.img), smem_u32(pstage(S, s)));  // lane = channel
+        } else {
+          umma_tile_128x128x128(acc, smem_u32(pstage(S, s)), smem_u32(S.img));  // lane = row
+        }
+      }
+      umma_commit(&S.mma[s]);
+      if (!ok) *S.abort_flag = 1;
+    }
+    cur_img = img_key;
+    __syncthreads();
+    if (*S.abort_flag) {
+      if (tid == 0) p_drain(S, i, issued);
+      break;
+    }
+    mbar_wait(&S.mma[s], ph, L.err, ERR_MBAR_TIMEOUT);  // a timeout is recorded in L.err
+    tc_fence_after();
+    if (tid == 0 && issued < n) {  // stage s is free: the MMA that read it is done
+      p_issue_job(L, j0 + issued, pstage(S, s), &S.full[s]);
+      ++issued;
+    }
+    const float sc = c.lp->out_scale;
+    const uint32_t taddr = acc + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+    float mn = INFINITY, mx = -INFINITY;
+    if (jb.plane == 0) {
+      const int nvalid = min(kTileRows, c.ntok - c.row0);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        tmem_ld32(taddr + cc * 32, v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          if (half * 64 + cc * 32 + k < nvalid) {
+            mn = fminf(mn, v[k]);
+            mx = fmaxf(mx, v[k]);
+          }
+        }
+      }
+      // fl(x*sc) is non-decreasing in x for sc > 0, so min/max commute with
+      // the scaling: one multiply per thread instead of one per element.
+      if (mn <= mx) {
+        mn *= sc;
+        mx *= sc;
+      }
+      const int key = c.r * H + jb.h;
+      if (key != run_key) {
+        if (run_key >= 0 && run_mn <= run_mx) {
+          uint32_t* ks = L.kstat + (static_cast<size_t>(run_key) * 128 + lane_id) * 2;
+          atomicMin(ks, float_to_ordered(run_mn));
+          atomicMax(ks + 1, float_to_ordered(run_mx));
+        }
+        run_key = key;
+        run_mn = INFINITY;
+        run_mx = -INFINITY;
+      }
+      run_mn = fminf(run_mn, mn);
+      run_mx = fmaxf(run_mx, mx);
+    } else {
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        tmem_ld32(taddr + cc * 32, v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          mn = fminf(mn, v[k]);
+          mx = fmaxf(mx, v[k]);
+        }
+      }
+      mn *= sc;
+      mx *= sc;
+      if (half == 1) {
+        S.red[lane_id * 2] = mn;
+        S.red[lane_id * 2 + 1] = mx;
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (jb.plane == 1 && half == 0) {
+      mn = fminf(mn, S.red[lane_id * 2]);
+      mx = fmaxf(mx, S.red[lane_id * 2 + 1]);
+      const int row = c.row0 + lane_id;
+      if (row < c.rows) {
+        if (row >= c.ntok) mn = mx = 0.f;
+        float* e = vstat_entry(L, c, jb.h, row);
+        e[0] = mn;
+        e[1] = mx;
+      }
+    }
+    __syncthreads();  // S.red reusable
+  }
+  if (run_key >= 0 && run_mn <= run_mx) {
+    uint32_t* ks = L.kstat + (static_cast<size_t>(run_key) * 128 + lane_id) * 2;
+    atomicMin(ks, float_to_ordered(run_mn));
+    atomicMax(ks + 1, float_to_ordered(run_mx));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------ quant
+// Epilogue of one half row: 64 values -> two 32-code groups of W bits,
+// staged at the row's pitch (W|1)*16 bytes, groups 2*half and 2*half+1.
+// Codes of 32 consecutive columns (raw bits of 2^23 + code) -> W-bit
+// packed words.  For W = 8 the code byte is the low byte of the bits.
+template <int W>
+KVS_DEV void pack_code_bits(const uint32_t (&b)[32], uint32_t (&w)[8]) {
+  if constexpr (W == 8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t lo = __byte_perm(b[4 * i], b[4 * i + 1], 0x0040);
+      const uint32_t hi = __byte_perm(b[4 * i + 2], b[4 * i + 3], 0x0040);
+      w[i] = __byte_perm(lo, hi, 0x5410);
+    }
+  } else {
+    uint32_t q[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) q[k] = b[k] & ((1u << W) - 1u);
+    pack32<W>(q, w);
+  }
+}
+
+// Epilogue of one half row: 64 values -> two 32-code groups of W bits,
+// staged at the row's pitch, groups 2*half and 2*half+1.  kp holds the key
+// (min, rcp) pairs per column, interleaved.
+template <int W>
+KVS_DEV void p_quant_half(uint32_t taddr, float sc, float top, bool valid, int plane,
+                          float vmin, float vrcp, const float* kp, int half,
+                          uint8_t* row_stage) {
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    float v[32];
+    tmem_ld32(taddr + cc * 32, v);
+    uint32_t b[32];
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      const uint32_t pr = valid ? cvt_bf16x2(v[k] * sc, v[k + 1] * sc) : 0u;
+      const float x0 = bf16lo_to_float(pr), x1 = bf16hi_to_float(pr);
+      if (plane == 0) {
+        const float4 m = *reinterpret_cast<const float4*>(kp + 2 * (half * 64 + cc * 32 + k));
+        b[k] = quantize_bits(x0, m.x, m.y, top);
+        b[k + 1] = quantize_bits(x1, m.z, m.w, top);
+      } else {
+        b[k] = quantize_bits(x0, vmin, vrcp, top);
+        b[k + 1] = quantize_bits(x1, vmin, vrcp, top);
+      }
+    }
+    uint32_t w[8];
+    pack_code_bits<W>(b, w);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(row_stage + (2 * half + cc) * 4 * W);
+#pragma unroll
+    for (int k = 0; k < W; ++k) dst[k] = w[k];
+  }
+}
+
+__global__ void __launch_bounds__(kPThreads, 2) k_quant_tc(LayerLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  const PSmem S = psmem(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int H = L.num_heads, T = L.total_tiles;
+  int j0, j1;
+  pjob_range(2 * H * T, j0, j1);
+  const int n = j1 - j0;
+  if (n <= 0) return;
+  float* kp = S.f0;  // [128][2] key (min, rcp), f0 and f1 contiguous
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.mma[i], 1);
+    }
+    mbar_init(S.imgb, 1);
+    *S.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(S.tslot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *S.tslot;
+  int issued = 0;
+  if (tid == 0) {
+    for (; issued < 2 && issued < n; ++issued)
+      p_issue_job(L, j0 + issued, pstage(S, issued & 1), &S.full[issued & 1]);
+  }
+  int cur_img = -1;
+  uint32_t img_phase = 0;
+  const int lane_id = quad * 32 + lane;  // TMEM lane = tile row
+  for (int i = 0; i < n; ++i) {
+    const int s = static_cast<int>(i & 1);
+    const uint32_t ph = static_cast<uint32_t>((i >> 1) & 1);
+    const PJob jb = pjob(j0 + i, H, T);
+    const ItemCtx c = item_ctx(L, jb.tile);
+    const int img_key = c.slot * H + jb.h;
+    const uint32_t acc = tmem + static_cast<uint32_t>(s * 128);
+    if (tid == 0) {
+      bool ok = true;
+      if (img_key != cur_img) {
+        mbar_arrive_expect_tx(S.imgb, 32768u);
+        bulk_load(S.img, bmat_of(L, c.slot, jb.h), 32768, S.imgb);
+        ok = mbar_wait(S.imgb, img_phase, L.err, ERR_MBAR_TIMEOUT);
+        img_phase ^= 1u;
+      }
+      ok = ok && mbar_wait(&S.full[s], ph, L.err, ERR_MBAR_TIMEOUT);
+      if (ok) {
+        tc_fence_after();
+        umma_tile_128x128x128(acc, smem_u32(pstage(S, s)), smem_u32(S.img));  // lane = row
+      }
+      umma_commit(&S.mma[s]);
+      if (!ok) *S.abort_flag = 1;
+    }
+    cur_img = img_key;
+    if (jb.plane == 0 && tid < 128) key_channel_params(L, c, jb.h, kp, kp + 1, 2);
+    const int row = c.row0 + lane_id;
+    const bool exists = row < c.rows, valid = row < c.ntok;
+    float vmin = 0.f, vrcp = 0.f;
+    if (jb.plane == 1 && exists) {
+      if (half == 0) {
+        value_row_params(L, c, jb.h, row, &vmin, &vrcp);
+        S.red[lane_id * 2] = vmin;
+        S.red[lane_id * 2 + 1] = vrcp;
+      }
+    }
+    __syncthreads();  // key params, value params, abort flag visible
+    if (*S.abort_flag) {
+      if (tid == 0) p_drain(S, i, issued);
+      break;
+    }
+    if (jb.plane == 1 && half == 1 && exists) {
+      vmin = S.red[lane_id * 2];
+      vrcp = S.red[lane_id * 2 + 1];
+    }
+    mbar_wait(&S.mma[s], ph, L.err, ERR_MBAR_TIMEOUT);  // a timeout is recorded in L.err
+    tc_fence_after();
+    const float lev = jb.plane == 0 ? c.lp->key_levels[jb.h] : c.lp->value_levels[jb.h];
+    const float top = c.lp->clamp_top ? lev - 1.0f : lev;
+    const int bits = seg_bits(c, jb.plane, jb.h);
+    const int P = (bits | 1) * 16;  // odd multiple of 16 B: spreads rows over bank groups
+    uint8_t* stage = pstage(S, s);    // the MMA that read this tile has completed
+    uint8_t* row_stage = stage + lane_id * P;
+    const uint32_t taddr = acc + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+    const float sc = c.lp->out_scale;
+    switch (bits) {
+      case 1: p_quant_half<1>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      case 2: p_quant_half<2>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      case 3: p_quant_half<3>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      case 4: p_quant_half<4>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      case 5: p_quant_half<5>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      case 6: p_quant_half<6>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      case 7: p_quant_half<7>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      default: p_quant_half<8>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+    }
+    tc_fence_before();
+    __syncthreads();
+    // Coalesced 16-byte copy of the tile's contiguous code region.
+    const int nrows = min(kTileRows, c.rows - c.row0);
+    uint8_t* dst0 = code_row(L, c, jb.plane, jb.h, c.row0);
+    for (int k = tid; k < nrows * bits; k += kPThreads) {
+      const int r = k / bits, col = k - r * bits;
+      *reinterpret_cast<uint4*>(dst0 + static_cast<long long>(k) * 16) =
+          *reinterpret_cast<const uint4*>(stage + r * P + col * 16);
+    }
+    fence_proxy_async_smem();  // generic accesses of the stage precede the next TMA write
+    __syncthreads();
+    if (tid == 0 && issued < n) {
+      p_issue_job(L, j0 + issued, pstage(S, s), &S.full[s]);
+      ++issued;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------- dequant
+// Unpack one 32-code group of a row into bf16 and store it into the
+// swizzled A tile (row t, channels 32*part..+31).
+// Unpack one 32-code group of a row into bf16 and store it into the
+// swizzled A tile (row t, channels 32*part..+31).  Each code becomes the
+// float 2^23 + q (one byte permute for 8-bit codes), then
+// bf16(bf16(q*scale) + min) with the exact-product FMA and paired
+// conversions.  kp holds the key (min, scale, -2^23*scale, 0) per column.
+template <int W>
+KVS_DEV void p_unpack_group(const uint8_t* src, int t, int part, int kv, const float* kp,
+                            float vmn, float vsc, uint8_t* sA) {
+  uint32_t w[8];
+  if constexpr (W == 8 || W == 4) {  // 4W-byte groups are 16-byte aligned
+    const uint4* s128 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int k = 0; k < W / 4; ++k) {
+      const uint4 u = __ldg(s128 + k);
+      w[4 * k] = u.x;
+      w[4 * k + 1] = u.y;
+      w[4 * k + 2] = u.z;
+      w[4 * k + 3] = u.w;
+    }
+  } else {
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src);
+#pragma unroll
+    for (int k = 0; k < W; ++k) w[k] = __ldg(s32 + k);
+  }
+  uint32_t fb[32];  // bits of 2^23 + q
+  if constexpr (W == 8) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      fb[k] = __byte_perm(w[k >> 2], 0x4B000000u, 0x7650u | (k & 3));
+  } else {
+    uint32_t q[32];
+    unpack32<W>(w, q);
+#pragma unroll
+    for (int k = 0; k < 32; ++k) fb[k] = q[k] | 0x4B000000u;
+  }
+  const float vneg = -8388608.0f * vsc;
+#pragma unroll
+  for (int c8 = 0; c8 < 4; ++c8) {
+    uint32_t o[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int k = c8 * 8 + 2 * p;
+      float a, b, ma, mb;
+      if (kv == 0) {
+        const float4 m0 = *reinterpret_cast<const float4*>(kp + 4 * (part * 32 + k));
+        const float4 m1 = *reinterpret_cast<const float4*>(kp + 4 * (part * 32 + k + 1));
+        a = code_times_scale(fb[k], m0.y, m0.z);
+        b = code_times_scale(fb[k + 1], m1.y, m1.z);
+        ma = m0.x;
+        mb = m1.x;
+      } else {
+        a = code_times_scale(fb[k], vsc, vneg);
+        b = code_times_scale(fb[k + 1], vsc, vneg);
+        ma = mb = vmn;
+      }
+      const uint32_t prod = cvt_bf16x2(a, b);
+      o[p] = cvt_bf16x2(__fadd_rn(bf16lo_to_float(prod), ma), __fadd_rn(bf16hi_to_float(prod), mb));
+    }
+    *reinterpret_cast<uint4*>(sA + sw128_offset(t, part * 32 + c8 * 8)) =
+        make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  const PSmem S = psmem(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int quad = warp & 3, half = warp >> 2;
+  const int H = L.num_heads, T = L.total_tiles;
+  int j0, j1;
+  pjob_range(2 * H * T, j0, j1);
+  const int n = j1 - j0;
+  if (n <= 0) return;
+  float* kp = S.f0;  // [128][4] key (min, scale, -2^23*scale, 0): f0 and f1 are contiguous
+  if (tid == 0) {
+    mbar_init(&S.mma[0], 1);
+    mbar_init(S.imgb, 1);
+    *S.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(S.tslot, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *S.tslot;
+  int cur_img = -1;
+  uint32_t img_phase = 0;
+  const int lane_id = (warp & 3) * 32 + (tid & 31);
+  if (tid == 0) {  // warm L2 with the first two jobs' code regions
+    for (int k = 0; k < 2 && k < n; ++k) {
+      const PJob jb = pjob(j0 + k, H, T);
+      const ItemCtx c = item_ctx(L, jb.tile);
+      const int nrows = min(kTileRows, c.rows - c.row0);
+      const uint32_t bytes = static_cast<uint32_t>(nrows * 16 * seg_bits(c, jb.plane, jb.h));
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                       code_row(L, c, jb.plane, jb.h, c.row0)),
+                   "r"(bytes)
+                   : "memory");
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    const int s = static_cast<int>(i & 1);
+    const PJob jb = pjob(j0 + i, H, T);
+    const ItemCtx c = item_ctx(L, jb.tile);
+    const int img_key = c.slot * H + jb.h;
+    uint8_t* sA = pstage(S, s);
+    if (jb.plane == 0 && tid < 128) {
+      const __half* m = meta_base(L, c.r);
+      const float mn = bf16_round(__half2float(m[jb.h * 128 + tid]));
+      const float sc = bf16_round(__half2float(m[c.lp->H * 128 + jb.h * 128 + tid]));
+      *reinterpret_cast<float4*>(kp + 4 * tid) = make_float4(mn, sc, -8388608.0f * sc, 0.f);
+    }
+    if (tid == 0) {
+      // the TMA store that read sA two jobs ago must have finished reading
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      if (i + 2 < n) {  // prefetch the code region two jobs ahead into L2
+        const PJob jn = pjob(j0 + i + 2, H, T);
+        const ItemCtx cn = item_ctx(L, jn.tile);
+        const int nrows = min(kTileRows, cn.rows - cn.row0);
+        const uint32_t bytes = static_cast<uint32_t>(nrows * 16 * seg_bits(cn, jn.plane, jn.h));
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                         code_row(L, cn, jn.plane, jn.h, cn.row0)),
+                     "r"(bytes)
+                     : "memory");
+      }
+    }
+    __syncthreads();  // key meta visible; sA free
+    // Unpack: 4 groups of 32 codes per row, 2 groups per thread.
+    const int bits = seg_bits(c, jb.plane, jb.h);
+    const int nrows = min(kTileRows, c.rows - c.row0);
+    const uint8_t* src0 = code_row(L, c, jb.plane, jb.h, c.row0);
+    const __half* meta = meta_base(L, c.r);
+    const int Hh = c.lp->H, G = c.lp->n_groups, grp = c.lp->group_of_head[jb.h];
+    for (int g = tid; g < kTileRows * 4; g += kPThreads) {
+      // lanes of a warp share `part` (broadcast key-parameter loads) and
+      // take consecutive rows (conflict-free swizzled stores)
+      const int t = g & (kTileRows - 1), part = g >> 7;
+      const int row = c.row0 + t;
+      if (t < nrows && row < c.ntok) {
+        float vmn = 0.f, vsc = 0.f;
+        if (jb.plane == 1) {
+          vmn = bf16_round(__half2float(meta[2 * Hh * 128 + grp * c.rows + row]));
+          vsc = bf16_round(__half2float(meta[2 * Hh * 128 + G * c.rows + grp * c.rows + row]));
+        }
+        const uint8_t* src = src0 + static_cast<long long>(t) * 16 * bits + part * 4 * bits;
+        switch (bits) {
+          case 1: p_unpack_group<1>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          case 2: p_unpack_group<2>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          case 3: p_unpack_group<3>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          case 4: p_unpack_group<4>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          case 5: p_unpack_group<5>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          case 6: p_unpack_group<6>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          case 7: p_unpack_group<7>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          default: p_unpack_group<8>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+        }
+      } else {
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          *reinterpret_cast<uint4*>(sA + sw128_offset(t, part * 32 + c8 * 8)) =
+              make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      bool ok = true;
+      if (img_key != cur_img) {
+        mbar_arrive_expect_tx(S.imgb, 32768u);
+        bulk_load(S.img, bmat_of(L, c.slot, jb.h), 32768, S.imgb);
+        ok = mbar_wait(S.imgb, img_phase, L.err, ERR_MBAR_TIMEOUT);
+        img_phase ^= 1u;
+      }
+      if (ok) {
+        tc_fence_after();
+        // D[t][k] = sum_n Y[t][n] Bi[k][n]
+        umma_tile_128x128x128(tmem, smem_u32(sA), smem_u32(S.img));
+      }
+      umma_commit(&S.mma[0]);
+      if (!ok) *S.abort_flag = 1;
+    }
+    cur_img = img_key;
+    mbar_wait(&S.mma[0], static_cast<uint32_t>(i & 1), L.err, ERR_MBAR_TIMEOUT);
+    tc_fence_after();
+    // Epilogue: this thread's row half -> bf16 -> swizzled sA (consumed by the MMA).
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+    const float sc = c.lp->out_scale;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      float v[32];
+      tmem_ld32(taddr + cc * 32, v);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t w[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+          w[p] = cvt_bf16x2(v[8 * q4 + 2 * p] * sc, v[8 * q4 + 2 * p + 1] * sc);
+        *reinterpret_cast<uint4*>(sA + sw128_offset(lane_id, half * 64 + cc * 32 + q4 * 8)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (*S.abort_flag) break;
+    if (tid == 0) {
+      const CUtensorMap* map = map_of(L, c.slot, jb.plane);
+      const int nst = min(kTileRows, c.ntok - c.row0);  // rows holding tokens
+      for (int g = 0; g < 8; ++g) {
+        const int rr = c.row0 + g * 16;
+        if (g * 16 >= nst) break;
+        const int phys = phys_block(L, c, rr);
+        const int slot = rr % c.kv.block_size;
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          asm volatile(
+              "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
+                  "l"(reinterpret_cast<uint64_t>(map)),
+              "r"(hb * 64), "r"(jb.h), "r"(slot), "r"(phys), "r"(smem_u32(sA + hb * 16384 + g * 2048))
+              : "memory");
+        }
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
 __global__ void k_init_key_stats(uint32_t* kstat, long long n_pairs) {
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n_pairs;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -753,6 +1399,17 @@ static EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   }
   return fn;
+}
+
+// Persistent grid: two CTAs per SM (the shared-memory limit), never more
+// CTAs than jobs.
+static int persistent_grid(const LayerLaunch& L) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    sms = 148;
+  const long long jobs = 2LL * L.num_heads * L.total_tiles;
+  return static_cast<int>(jobs < 2LL * sms ? jobs : 2LL * sms);  // jobs < 2^31: checked by the caller
 }
 
 template <typename K>
@@ -808,9 +1465,13 @@ int kvs_init_key_stats(uint32_t* kstat, long long n_pairs, void* stream) {
 int kvs_stats(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
+  if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
+    if (int rc = set_smem(k_stats_tc, kPSmem)) return rc;
+    k_stats_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
+  } else if (L.engine == 2) {
     if (int rc = set_smem(k_stats_mma, kSmemTile)) return rc;
     k_stats_mma<<<grid, 128, kSmemTile, s>>>(L);
   } else {
@@ -823,9 +1484,13 @@ int kvs_stats(const LayerLaunch* Lp) {
 int kvs_quant(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
+  if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
+    if (int rc = set_smem(k_quant_tc, kPSmem)) return rc;
+    k_quant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
+  } else if (L.engine == 2) {
     if (int rc = set_smem(k_quant_mma, kSmemTile)) return rc;
     k_quant_mma<<<grid, 128, kSmemTile, s>>>(L);
   } else {
@@ -837,9 +1502,13 @@ int kvs_quant(const LayerLaunch* Lp) {
 int kvs_dequant_inverse(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
+  if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
+    if (int rc = set_smem(k_dequant_tc, kPSmem)) return rc;
+    k_dequant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
+  } else if (L.engine == 2) {
     if (int rc = set_smem(k_dequant_inverse_mma, kSmemTile)) return rc;
     k_dequant_inverse_mma<<<grid, 128, kSmemTile, s>>>(L);
   } else {

@@ -72,7 +72,7 @@ struct LayerLaunch {
   uint32_t* err;           // device error word
   int total_tiles;
   int num_heads;           // H (identical for every slot of a launch)
-  int engine;              // 0: tcgen05 + TMA ; 1: SIMT (in-register FWHT)
+  int engine;              // 0: persistent tcgen05 + TMA ; 1: SIMT (in-register FWHT) ; 2: tcgen05, one CTA per tile
   void* stream;            // cudaStream_t
 };
 

@@ -35,8 +35,9 @@ from kvserve_hpdps_b200.ops._lib import LayerLaunch, PagedKV, check, lib
 HEAD_DIM = 128
 TILE_ROWS = 128
 RANS_CHUNK = 32768
-ENGINE_TCGEN05 = 0
-ENGINE_SIMT = 1
+ENGINE_TCGEN05 = 0       # persistent tcgen05 kernels (default)
+ENGINE_SIMT = 1          # SIMT butterfly
+ENGINE_TCGEN05_TILE = 2  # tcgen05, one CTA per tile
 
 ERR_NAMES = {0: "none", 1: "mbarrier timeout", 2: "ready-flag timeout", 3: "bounds",
              4: "corrupt stream", 5: "overflow"}
@@ -379,29 +380,44 @@ class WorkItems:
     """
 
     def __init__(self, slots: LayerSlots, items: Sequence[tuple[int, Sequence[int], int]],
-                 code_offsets: Optional[Sequence[int]] = None):
-        """``code_offsets`` overrides where each item's codes start (used to
-        decode a subset of the items of a larger message in place)."""
+                 code_offsets: Optional[Sequence[int]] = None,
+                 meta_offsets: Optional[Sequence[int]] = None):
+        """``code_offsets`` / ``meta_offsets`` override where each item's
+        codes / metadata start (used to decode a subset of the items of a
+        larger message in place).
+
+        Items that pass the same block-id sequence object (e.g. one request
+        at every layer) share one copy of it in the device block table."""
         self.slots = slots
-        self.items = [(int(s), list(map(int, b)), int(n)) for s, b, n in items]
         dev = slots.device
         self.device = dev
-        bs = [slots.kv_layers[s].shape[2] for s, _, _ in self.items]
-        self.n_rows = [len(b) * k for (_, b, _), k in zip(self.items, bs)]
-        self.n_tokens = [n for _, _, n in self.items]
+        uniq: dict[int, int] = {}  # id(block sequence) -> index into lists
+        lists: list[list[int]] = []
+        norm = []
+        for s, b, n in items:
+            k = id(b)
+            if k not in uniq:
+                uniq[k] = len(lists)
+                lists.append(b.tolist() if isinstance(b, torch.Tensor) else [int(x) for x in b])
+            norm.append((int(s), uniq[k], int(n)))
+        self.items = [(s, lists[li], n) for s, li, n in norm]
+        bs = [slots.kv_layers[s].shape[2] for s, _, _ in norm]
+        self.n_rows = [len(lists[li]) * k for (_, li, _), k in zip(norm, bs)]
+        self.n_tokens = [n for _, _, n in norm]
         self.tiles = [(r + TILE_ROWS - 1) // TILE_ROWS for r in self.n_rows]
         self.total_tiles = sum(self.tiles)
-        R = len(self.items)
-        bt, off = [], []
-        for _, b, _ in self.items:
-            off.append(len(bt))
+        R = len(norm)
+        bt, list_off = [], []
+        for b in lists:
+            list_off.append(len(bt))
             bt.extend(b)
+        off = [list_off[li] for _, li, _ in norm]
         prefix = [0]
         for t in self.tiles:
             prefix.append(prefix[-1] + t)
         self.code_off, self.meta_off, self.row_off = [], [], []
         c = m = ro = 0
-        for (s, _, _), rows in zip(self.items, self.n_rows):
+        for (s, _, _), rows in zip(norm, self.n_rows):
             plan = slots.plans[s]
             self.code_off.append(c)
             self.meta_off.append(m)
@@ -411,12 +427,18 @@ class WorkItems:
             ro += rows
         self.code_bytes, self.meta_bytes, self.total_rows = c, m, ro
         if code_offsets is not None:
-            if len(code_offsets) != len(self.items):
+            if len(code_offsets) != R:
                 raise ValueError("one code offset per item is required")
             self.code_off = [int(x) for x in code_offsets]
-            self.code_bytes = max((o + self.n_rows[i] * slots.plans[self.items[i][0]].row_bytes()
+            self.code_bytes = max((o + self.n_rows[i] * slots.plans[norm[i][0]].row_bytes()
                                    for i, o in enumerate(self.code_off)), default=0)
-        ints = bt + off + self.n_tokens + self.n_rows + prefix + [s for s, _, _ in self.items]
+        if meta_offsets is not None:
+            if len(meta_offsets) != R:
+                raise ValueError("one metadata offset per item is required")
+            self.meta_off = [int(x) for x in meta_offsets]
+            self.meta_bytes = max((o + slots.plans[norm[i][0]].meta_bytes(self.n_rows[i])
+                                   for i, o in enumerate(self.meta_off)), default=0)
+        ints = bt + off + self.n_tokens + self.n_rows + prefix + [s for s, _, _ in norm]
         longs = self.code_off + self.meta_off + self.row_off
         hi = torch.tensor(ints if ints else [0], dtype=torch.int32)
         hl = torch.tensor(longs if longs else [0], dtype=torch.int64)

@@ -1,7 +1,8 @@
 """Numerics of the sm_100a kernels against the float32 CPU oracle.
 
-Every test here needs a CUDA device.  Both transform engines are checked:
-engine 0 (TMA + tcgen05.mma) and engine 1 (SIMT butterfly).  Codes may
+Every test here needs a CUDA device.  All transform engines are checked:
+engine 0 (persistent TMA + tcgen05.mma), engine 2 (tcgen05, one CTA per
+tile) and engine 1 (SIMT butterfly).  Codes may
 differ from the oracle by one step where the transform's summation order
 moves a value across a rounding boundary; the tests bound how often.
 """
@@ -15,7 +16,7 @@ from kvserve_hpdps_b200.ops import kernels as K
 
 pytestmark = pytest.mark.gpu
 
-ENGINES = [K.ENGINE_TCGEN05, K.ENGINE_SIMT]
+ENGINES = [K.ENGINE_TCGEN05, K.ENGINE_SIMT, K.ENGINE_TCGEN05_TILE]
 
 
 def _plan(H, layer_id=5, packed=False, seed=0x3333):
@@ -226,6 +227,37 @@ def test_engines_agree():
     c1, m1 = K.quantize_layer(wl.cache[0], batch, plan, engine=K.ENGINE_SIMT)
     torch.cuda.synchronize()
     _check_codes(c0.cpu(), c1.cpu())
+
+
+@pytest.mark.parametrize("packed", [False, True])
+def test_persistent_engine_bit_exact_vs_tile_engine(packed):
+    """The persistent kernels walk many jobs per CTA (image reloads at
+    layer/head changes, key statistics carried across tiles, odd token
+    counts, partial tiles): codes, metadata and reconstruction must equal
+    the one-CTA-per-tile engine bit for bit."""
+    H, L = 4, 6
+    tokens = [1, 130, 2047, 4096, 777]
+    wl = paged_workload(L, tokens, H, device="cuda", seed=123)
+    plans = [K.make_layer_plan(H, [12, 6, 16, 6][:H], [8, 4, 4, 16][:H], 0x3333, l,
+                               packed=packed) for l in range(L)]
+    slots = K.LayerSlots([wl.cache[l] for l in range(L)], plans)
+    items = K.WorkItems(slots, [(l, b, t) for l in range(L) for b, t in zip(wl.block_ids, tokens)])
+    outs = []
+    for engine in (K.ENGINE_TCGEN05, K.ENGINE_TCGEN05_TILE):
+        codes, meta = K.quantize(slots, items, engine=engine)
+        dst = torch.zeros_like(wl.cache)
+        dslots = K.LayerSlots([dst[l] for l in range(L)], plans)
+        K.dequantize(codes, meta, dslots, items, engine=engine)
+        torch.cuda.synchronize()
+        K.check_device_error(wl.cache.device)
+        outs.append((codes.clone(), meta.clone(), dst))
+    assert torch.equal(outs[0][0], outs[1][0]), "codes differ"
+    assert torch.equal(outs[0][1], outs[1][1]), "metadata differ"
+    for l in range(L):
+        for b, t in zip(wl.block_ids, tokens):
+            a = gather_request(outs[0][2][l], b).view(2, -1, H, 128)[:, :t]
+            c = gather_request(outs[1][2][l], b).view(2, -1, H, 128)[:, :t]
+            assert torch.equal(a, c), f"reconstruction differs (layer {l}, {t} tokens)"
 
 
 @pytest.mark.parametrize("n", [1, 511, 4096, 32768, 100000, 300001])
