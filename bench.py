@@ -407,7 +407,7 @@ def run_e2e_ours(args, mgr, wl, role, world, rank, pairs, device):
         raise NotImplementedError
 
     if world > 1:
-        return None
+        return run_e2e_pairs(args, mgr, wl, role, world, rank, pairs, device)
     for _ in range(2):
         one()
     torch.cuda.synchronize(device)
@@ -426,14 +426,205 @@ def run_e2e_ours(args, mgr, wl, role, world, rank, pairs, device):
             "steps": steps}
 
 
+def side_port(offset, pair_id):
+    return int(os.environ.get("MASTER_PORT", "29500")) + offset + pair_id
+
+
+def _poll_message(tr, pending, key, timeout_s):
+    """Wait (bounded) until the transport delivered the message ``key``."""
+    deadline = time.monotonic() + timeout_s
+    while key not in pending or not pending[key]:
+        for k, v in tr.drain_received().items():
+            pending.setdefault(k, []).extend(v)
+        if key in pending and pending[key]:
+            break
+        if time.monotonic() > deadline:
+            raise TimeoutError(f"message {key} did not arrive within {timeout_s} s")
+        time.sleep(2e-5)
+    return pending[key].pop(0)
+
+
+def run_e2e_pairs(args, mgr, wl, role, world, rank, pairs, device):
+    """End to end through the public API on producer/consumer pairs: the
+    producer compresses the step's requests into one grouped message
+    (``compress_paged_requests``), builds the wire envelope and hands it to
+    the NVLink ring transport (``P2PTransport.send_bundle``: ZMQ header,
+    device stores into the consumer's receive ring); the consumer drains the
+    transport, waits on the ring flag, restores the envelope and decodes into
+    its paged cache (``decompress_paged_requests``), then reads the device
+    error word back.  Block tables go host -> device every step."""
+    from kvserve_hpdps_b200.compression.manager import add_sentinel
+    from kvserve_hpdps_b200.compression.wire import CompressedWire, build_wire, restore_from_wire
+    from kvserve_hpdps_b200.ops import kernels as K
+    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport
+    L = wl.L
+    pair_id = rank % pairs
+    tr = P2PTransport(role == "producer", "127.0.0.1", side_port(600, pair_id), device.index,
+                      0, ring_bytes=int(os.environ.get("KVSERVE_RING_BYTES", str(2 << 30))))
+    names = add_sentinel([f"model.layers.{l}.self_attn.attn" for l in range(L)])
+    pending: dict = {}
+    steps = max(2, min(args.steps, 10))
+
+    def one(s):
+        if role == "producer":
+            cd = mgr.compress_paged_requests([wl.src[l] for l in range(L)], list(range(L)),
+                                             wl.src_req, member_tids=[f"{s}:{r}" for r in range(wl.B)])
+            w = build_wire(cd)
+            tr.send_bundle(f"s{s}", names, w.meta, w.body_chunks, w.aux_tensors)
+        else:
+            _, payload = _poll_message(tr, pending, f"s{s}", 60.0)
+            tr.prepare(payload, device)
+            cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
+                                                  payload["aux_tensors"]))
+            mgr.decompress_paged_requests(cd, [wl.dst[l] for l in range(L)], wl.dst_req)
+            tr.release(payload, device)
+            K.read_device_error(device)
+
+    s = 0
+    for _ in range(2):
+        one(s)
+        s += 1
+    if role == "producer":
+        tr.wait_for_sent(60.0)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    K.reset_transfer_counters()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        one(s)
+        s += 1
+    if role == "producer":
+        if not tr.wait_for_sent(60.0):
+            raise TimeoutError("sends did not complete")
+    torch.cuda.synchronize(device)
+    ev1.record()
+    torch.cuda.synchronize(device)
+    ms = allreduce_max(ev0.elapsed_time(ev1), world)
+    c = K.transfer_counters()
+    h2d = allreduce_sum(float(c["h2d"]), world) / steps
+    d2h = allreduce_sum(float(c["d2h"] + (4 * steps if role == "consumer" else 0)), world) / steps
+    barrier(world)
+    tr.close()
+    return {"value": ms / (steps * wl.B * pairs), "unit": "ms/request",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "path": "compress_paged_requests -> build_wire -> P2PTransport.send_bundle -> "
+                    "drain_received/prepare -> restore_from_wire -> decompress_paged_requests"}
+
+
 # ------------------------------------------------------------------ reference
+def run_reference_pairs(args, rank, world, local):
+    """Reference arm on producer/consumer pairs, through the reference's own
+    public modules: its KVCompressionAdapter (quantizer pipeline), its wire
+    envelope (build_wire / restore_from_wire), its NcclTransport
+    (ZMQ PUT_BUNDLE header + ncclSend/ncclRecv on a 2-rank communicator per
+    pair) and its paged-block extract/inject utilities, in the order its
+    connector runs them in overlap mode "off"."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    sys.path.insert(0, ref_root)
+    from kvserve_v1.compression.manager import KVCompressionAdapter, add_sentinel  # noqa: E402
+    from kvserve_v1.compression.wire import (CompressedWire, build_wire,  # noqa: E402
+                                              restore_from_wire)
+    from kvserve_v1.transport.nccl_transport import NcclTransport  # noqa: E402
+    from kvserve_v1.utils.kv_utils import (extract_kv_from_layer_by_blocks,  # noqa: E402
+                                           inject_kv_into_layer_by_blocks)
+    import threading
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pairs = world // 2
+    role = "producer" if rank < pairs else "consumer"
+    pair_id = rank % pairs
+    cfg = quant_config(args)
+    spec = {"enabled": True, "pipeline": ["quantizer"],
+            "quantizer_config": dict(cfg["quantizer_config"]), "min_compress_size": 0}
+    adapter = KVCompressionAdapter(spec, num_kv_heads=args.kv_heads, head_size=128,
+                                   model_name=MODEL)
+    wl = Workload(args, device, args.seed + 101 * pair_id, role)
+    L = args.layers
+    names = add_sentinel([f"model.layers.{l}.self_attn.attn" for l in range(L)])
+    tr = NcclTransport(role == "producer", "127.0.0.1", side_port(500, pair_id), local, 0)
+    pending: dict = {}
+    sizes = []
+
+    def wait_sent(timeout_s=120.0):
+        t = threading.Thread(target=tr.wait_for_sent, daemon=True)
+        t.start()
+        t.join(timeout_s)
+        if t.is_alive():
+            raise TimeoutError("reference sends did not complete")
+
+    def step(s):
+        for r in range(wl.B):
+            key = f"s{s}r{r}"
+            if role == "producer":
+                layers = [extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0])
+                          for l in range(L)]
+                c = adapter.compress(torch.stack(layers, dim=0), key)
+                sizes.append(int(c.compressed_tensor.numel() * c.compressed_tensor.element_size()))
+                w = build_wire(c)
+                tr.send_bundle(key, names, w.meta, w.body_chunks, w.aux_tensors)
+            else:
+                _, payload = _poll_message(tr, pending, key, 120.0)
+                cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
+                                                      payload["aux_tensors"]))
+                out = adapter.decompress(cd)
+                for l in range(L):
+                    inject_kv_into_layer_by_blocks(wl.dst[l], out[l], wl.dst_req[r][0])
+
+    s = 0
+    for _ in range(args.warmup):
+        step(s)
+        s += 1
+    if role == "producer":
+        wait_sent()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    sampler = ClockSampler(range(world)) if local == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step(s)
+        s += 1
+    if role == "producer":
+        wait_sent()
+    torch.cuda.synchronize(device)
+    ev1.record()
+    torch.cuda.synchronize(device)
+    ms = allreduce_max(ev0.elapsed_time(ev1), world)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    err = None
+    if role == "consumer":
+        src = Workload(args, device, args.seed + 101 * pair_id, "producer")
+        a = src.src[:, :, torch.tensor(src.src_req[0][0], device=device)].float()
+        b = wl.dst[:, :, torch.tensor(wl.dst_req[0][0], device=device)].float()
+        err = {"cosine": float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)),
+               "rel_mse": float(((a - b) ** 2).sum() / (a ** 2).sum())}
+        del src
+    import torch.distributed as dist
+    gathered = [None] * world
+    dist.all_gather_object(gathered, err)
+    err = next((g for g in gathered if g is not None), None)
+    tot = allreduce_sum(float(sum(sizes)), world)
+    n = allreduce_sum(float(len(sizes)), world)
+    cr = wl.bf16_bytes_per_request / (tot / n) if n else None
+    return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "pairs": pairs,
+            "reference_path": "custom pipeline [quantizer] via KVCompressionAdapter + "
+                              "build_wire + NcclTransport.send_bundle (ncclSend/ncclRecv per pair)",
+            "transport": "reference NcclTransport (NCCL send/recv over NVLink)"}
+
+
 def run_reference(args, rank, world, local):
     ref_root = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "kvserve_v1")):
         return {"unavailable": "reference not installed in baseline/_ref"}
     if world > 1:
-        return {"unavailable": "reference multi-GPU arm needs its vLLM engines (NcclTransport "
-                               "bootstraps inside vLLM workers); only the 1-GPU round trip runs"}
+        return run_reference_pairs(args, rank, world, local)
     sys.path.insert(0, ref_root)
     from kvserve_v1.compression.manager import KVCompressionAdapter  # noqa: E402
     from kvserve_v1.utils.kv_utils import (extract_kv_from_layer_by_blocks,  # noqa: E402

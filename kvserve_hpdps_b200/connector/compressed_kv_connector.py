@@ -425,7 +425,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             cd = restore_from_wire(wire)
             md = cd.metadata or {}
             comp = self._get_compressor()
-            if md.get("layout") == "items":
+            if md.get("layout") in ("items", "items_packed"):
                 self._inject_items(rm, names, cd, comp, forward_context)
             else:
                 kv = comp.decompress(cd)
