@@ -561,7 +561,7 @@ def run_reference_pairs(args, rank, world, local):
                           for l in range(L)]
                 c = adapter.compress(torch.stack(layers, dim=0), key)
                 sizes.append(int(c.compressed_tensor.numel() * c.compressed_tensor.element_size()))
-                w = build_wire(c)
+                w = build_wire(c, 512 << 20)  # the connector's default chunk bound
                 tr.send_bundle(key, names, w.meta, w.body_chunks, w.aux_tensors)
             else:
                 _, payload = _poll_message(tr, pending, key, 120.0)
@@ -742,6 +742,9 @@ def main(argv=None):
     if args.impl == "reference":
         line["impl"] = "reference"
         line["config"]["reference_path"] = res.get("reference_path")
+        line["config"]["compression"] = ("reference quantizer pipeline, hybrid 0.8 12/8/6/4, u8 "
+                                         "codes, no entropy codec (its default mode needs nvCOMP, "
+                                         "CuPy and fast_hadamard_transform)")
     else:
         line["impl"] = "ours"
         line["gpu_launches"] = int(allreduce_sum(float(res["launches"]), world)) if world > 1 \
