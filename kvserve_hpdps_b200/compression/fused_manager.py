@@ -47,7 +47,7 @@ BACKEND = "kvs_fused"
 
 def _engine_from_env() -> int:
     v = os.environ.get("KVSERVE_ENGINE", "tcgen05").lower()
-    return {"simt": 1, "1": 1, "tile": 2, "2": 2}.get(v, 0)
+    return {"simt": 1, "1": 1, "tile": 2, "2": 2, "persistent": 3, "3": 3}.get(v, 0)
 
 
 @dataclass

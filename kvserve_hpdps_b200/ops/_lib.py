@@ -50,7 +50,7 @@ class LayerLaunch(ctypes.Structure):
                 ("bmat", c_void_p), ("bmat_stride", c_longlong), ("codes", c_void_p),
                 ("meta", c_void_p), ("kstat", c_void_p), ("vstat", c_void_p), ("err", c_void_p),
                 ("total_tiles", c_int), ("num_heads", c_int), ("engine", c_int),
-                ("stream", c_void_p)]
+                ("stream", c_void_p), ("trace", c_void_p), ("trace_jobs", c_int)]
 
 
 _lock = threading.Lock()

@@ -23,6 +23,9 @@
 //    tcgen05.mma (bf16 x bf16 -> fp32 in TMEM) against a +-1 Hadamard matrix
 //    with the Rademacher signs folded in, the epilogue reads the accumulator
 //    back with tcgen05.ld; each CTA pipelines a contiguous range of tiles;
+//    (k_stats_ws / k_quant_ws are warp-specialized: a control warp issues
+//    loads and MMAs, two epilogue groups of 8 warps alternate jobs);
+//  * engine 3: the persistent kernels without warp specialization (k_*_tc);
 //  * engine 2: the same math with one CTA per tile (k_*_mma);
 //  * engine 1: thread-per-row loads and an in-register fp32 butterfly.
 #include "common.cuh"
@@ -223,8 +226,8 @@ KVS_DEV void issue_tile_loads(const LayerLaunch& L, const ItemCtx& c, const CUte
 // Key channel min / reciprocal scale of (item, head h) into smem; tile 0 of
 // the item publishes the fp16 metadata.
 KVS_DEV void key_channel_params(const LayerLaunch& L, const ItemCtx& c, int h, float* s_min,
-                                float* s_rcp, int stride = 1) {
-  const int n = threadIdx.x;
+                                float* s_rcp, int stride = 1, int n = -1) {
+  if (n < 0) n = threadIdx.x;
   const uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * c.lp->H + h) * 128 + n) * 2;
   float kmin = 0.f, kmax = 0.f;
   if (c.ntok > 0) {
@@ -1141,6 +1144,527 @@ __global__ void __launch_bounds__(kPThreads, 2) k_quant_tc(LayerLaunch L) {
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+
+
+// Item context kept in registers across consecutive jobs: refreshed only
+// when the tile leaves [t0, t1), the current item's tile range.
+struct ItemCursor {
+  ItemCtx c;
+  int t0, t1;
+};
+KVS_DEV void cursor_init(ItemCursor& k) {
+  k.t0 = 1;
+  k.t1 = 0;  // empty range: the first seek loads
+}
+KVS_DEV void cursor_seek(const LayerLaunch& L, ItemCursor& k, int tile) {
+  if (tile < k.t0 || tile >= k.t1) {
+    int r;
+    if (tile >= k.t1 && k.t1 > k.t0 && k.c.r + 1 < L.rt.num_req && tile < L.rt.tile_prefix[k.c.r + 2])
+      r = k.c.r + 1;  // the next item (the common case when walking tiles)
+    else
+      r = find_item(L.rt.tile_prefix, L.rt.num_req, tile);
+    k.t0 = L.rt.tile_prefix[r];
+    k.t1 = L.rt.tile_prefix[r + 1];
+    k.c.r = r;
+    k.c.slot = L.rt.slot[r];
+    k.c.rows = L.rt.n_rows[r];
+    k.c.ntok = L.rt.n_tokens[r];
+    k.c.lp = L.lps + k.c.slot;
+    k.c.kv = L.kvs[k.c.slot];
+  }
+  k.c.row0 = (tile - k.t0) * kTileRows;
+}
+
+// Control warp: issue the TMA loads of one tile (16 boxes: 8 row groups x
+// 2 channel halves) with lanes 0-15 in parallel, so the block-table reads
+// overlap; lane 0 registers the byte count first.
+KVS_DEV void issue_tile_loads_warp(const LayerLaunch& L, const ItemCtx& c, const CUtensorMap* map,
+                                   int h, uint8_t* tile, uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  const int nload = min(8, (c.rows - c.row0 + 15) / 16);
+  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nload) * 4096u);
+  __syncwarp();
+  if (lane < 2 * nload) {
+    const int g = lane >> 1, hb = lane & 1;
+    const int rr = c.row0 + g * 16;
+    const int phys = phys_block(L, c, rr);
+    const int slot = rr % c.kv.block_size;
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(hb * 64), "r"(h), "r"(slot), "r"(phys),
+        "r"(smem_u32(bar))
+        : "memory");
+  }
+  __syncwarp();
+}
+
+// ====================================== warp-specialized tcgen05 engine
+// One CTA per SM: a control warp (lane 0 issues every TMA load into a
+// 3-stage ring and every MMA into four 128-column TMEM accumulators) and two
+// epilogue groups of 8 warps that take alternate jobs of the CTA's range.
+// Epilogue warps wait only on mbarriers (accumulator ready) and on their
+// group's named barrier, never on the control thread's loads, so the MMA of
+// job k+1 and the loads of jobs k+1..k+2 run while job k's epilogue runs.
+//
+// Barrier phases (job k of the CTA, acc a(k) = 2*(k&1) + ((k>>1)&1), used
+// by jobs k = a's residue mod 4, use index u = k>>2):
+//   full[k%3]   completes once per load (parity (k/3)&1);
+//   sfree[k%3]  tcgen05.commit after MMA k (stage reusable, old image free);
+//   mma[a]      tcgen05.commit after MMA k (parity u&1);
+//   afree[a]    8 warp arrivals after the epilogue read accumulator a (u&1).
+constexpr int kWsGroups = 2;
+constexpr int kWsGroupWarps = 8;
+constexpr int kWsGroupThreads = kWsGroupWarps * 32;
+constexpr int kWsCtrlWarp = kWsGroups * kWsGroupWarps;  // warp 16
+constexpr int kWsThreads = (kWsCtrlWarp + 1) * 32;       // 544
+constexpr int kWsMaxStages = 5;
+constexpr int kWsStagingBytes = 128 * 144;  // 128 rows x (W|1)*16 B for W <= 8
+// Layout from the 1024-aligned base: image | NS stages | staging (quant) |
+// barriers | kp | red.  NS = 5 for stats (no staging), 4 for quant.
+template <int NS, bool kStaging>
+struct WsLayout {
+  static constexpr int kOffStages = 32768;
+  static constexpr int kOffStaging = kOffStages + NS * 32768;
+  static constexpr int kOffBars = kOffStaging + (kStaging ? kWsGroups * kWsStagingBytes : 0);
+  static constexpr int kOffKp = kOffBars + 256;
+  static constexpr int kOffRed = kOffKp + kWsGroups * 256 * 4;
+  static constexpr int kUsed = kOffRed + kWsGroups * 2 * 256 * 4;
+  static constexpr int kSmem = kUsed + 1024;  // + alignment slack
+  static_assert(kSmem <= 227 * 1024, "warp-specialized shared memory");
+};
+using WsStatsLayout = WsLayout<5, false>;
+using WsQuantLayout = WsLayout<4, true>;
+
+struct WsSmem {
+  uint8_t* base;
+  int off_staging, off_kp, off_red;
+  uint64_t* full;   // [NS]
+  uint64_t* sfree;  // [NS]
+  uint64_t* mma;    // [4]
+  uint64_t* afree;  // [4]
+  uint64_t* imgb;
+  uint32_t* tslot;
+};
+template <class LY>
+KVS_DEV WsSmem ws_smem(uint8_t* raw) {
+  WsSmem w;
+  w.base = align1024(raw);
+  w.off_staging = LY::kOffStaging;
+  w.off_kp = LY::kOffKp;
+  w.off_red = LY::kOffRed;
+  uint64_t* b = reinterpret_cast<uint64_t*>(w.base + LY::kOffBars);
+  w.full = b;
+  w.sfree = b + kWsMaxStages;
+  w.mma = b + 2 * kWsMaxStages;
+  w.afree = b + 2 * kWsMaxStages + 4;
+  w.imgb = b + 2 * kWsMaxStages + 8;
+  w.tslot = reinterpret_cast<uint32_t*>(b + 2 * kWsMaxStages + 9);
+  return w;
+}
+KVS_DEV uint8_t* ws_img(const WsSmem& S) { return S.base; }
+KVS_DEV uint8_t* ws_stage(const WsSmem& S, int k) { return S.base + 32768 + 32768 * k; }
+KVS_DEV uint8_t* ws_staging(const WsSmem& S, int g) {
+  return S.base + S.off_staging + kWsStagingBytes * g;
+}
+KVS_DEV float* ws_kp(const WsSmem& S, int g) {
+  return reinterpret_cast<float*>(S.base + S.off_kp) + 256 * g;
+}
+KVS_DEV float* ws_red(const WsSmem& S, int g, int k) {
+  return reinterpret_cast<float*>(S.base + S.off_red) + 256 * (2 * g + ((k >> 1) & 1));
+}
+KVS_DEV int ws_acc(int k) { return 2 * (k & 1) + ((k >> 1) & 1); }
+KVS_DEV void group_sync(int g) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kWsGroupThreads) : "memory");
+}
+
+KVS_DEV void ws_init(const WsSmem& S, int NS) {
+  for (int i = 0; i < NS; ++i) {
+    mbar_init(&S.full[i], 1);
+    mbar_init(&S.sfree[i], 1);
+  }
+  for (int i = 0; i < 4; ++i) {
+    mbar_init(&S.mma[i], 1);
+    mbar_init(&S.afree[i], kWsGroupWarps);
+  }
+  mbar_init(S.imgb, 1);
+  fence_mbar_init();
+}
+
+
+KVS_DEV void trace_mark(const LayerLaunch& L, int k, int ev) {
+  if (L.trace != nullptr && blockIdx.x < kTraceCtas && k < L.trace_jobs)
+    L.trace[(static_cast<long long>(blockIdx.x) * L.trace_jobs + k) * 8 + ev] = globaltimer();
+}
+
+
+// Job mapping of the warp-specialized kernels: the grid is 2*H*R CTAs; CTA b
+// owns (plane, head) = (b % (2H)) and tile range r = b / (2H) of R equal
+// ranges.  The CTAs of one range (all heads, both planes) run concurrently
+// and stream the same tiles, so the heads' 256-byte pieces of each 1 KB
+// token row reach DRAM together (row-buffer locality); each CTA's transform
+// image changes only at layer boundaries.  Job k of a CTA is tile t0 + k.
+struct WsMap {
+  int plane, h, t0, n;
+};
+KVS_DEV WsMap ws_map(const LayerLaunch& L) {
+  const int PH = 2 * L.num_heads;
+  const int R = gridDim.x / PH;
+  const int b = blockIdx.x, ph = b % PH, r = b / PH;
+  WsMap m;
+  m.plane = ph / L.num_heads;
+  m.h = ph % L.num_heads;
+  m.t0 = static_cast<int>(static_cast<long long>(r) * L.total_tiles / R);
+  m.n = static_cast<int>(static_cast<long long>(r + 1) * L.total_tiles / R) - m.t0;
+  return m;
+}
+KVS_DEV PJob ws_job(const WsMap& m, int k) {
+  PJob j;
+  j.plane = m.plane;
+  j.h = m.h;
+  j.tile = m.t0 + k;
+  return j;
+}
+
+// One job's TMA boxes as seen by one control-warp lane: lane l < 16 owns
+// box (row group l/2, channel half l%2).  The block-table read is done when
+// the descriptor is prepared, one job before the loads are issued, so the
+// issue itself never waits on memory.
+struct BoxDesc {
+  const CUtensorMap* map;
+  int h, slot, phys, nload;
+  bool mine;
+};
+KVS_DEV BoxDesc box_desc(const LayerLaunch& L, ItemCursor& cur, const PJob& jb) {
+  const int lane = threadIdx.x & 31;
+  cursor_seek(L, cur, jb.tile);
+  const ItemCtx& c = cur.c;
+  BoxDesc d;
+  d.map = map_of(L, c.slot, jb.plane);
+  d.h = jb.h;
+  d.nload = min(8, (c.rows - c.row0 + 15) / 16);
+  d.mine = lane < 2 * d.nload;
+  d.slot = d.phys = 0;
+  if (d.mine) {
+    const int rr = c.row0 + (lane >> 1) * 16;
+    d.phys = phys_block(L, c, rr);
+    d.slot = rr % c.kv.block_size;
+  }
+  return d;
+}
+KVS_DEV void issue_boxes(const BoxDesc& d, uint8_t* tile, uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(d.nload) * 4096u);
+  __syncwarp();
+  if (d.mine) {
+    const int g = lane >> 1, hb = lane & 1;
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
+        "l"(reinterpret_cast<uint64_t>(d.map)), "r"(hb * 64), "r"(d.h), "r"(d.slot), "r"(d.phys),
+        "r"(smem_u32(bar))
+        : "memory");
+  }
+  __syncwarp();
+}
+
+// Control warp: loads and MMAs for local jobs [0, n) over an NS-stage ring.
+// Iteration k: wait for job k's tile and a free accumulator, issue MMA k,
+// then refill the stage of job k-1 (its MMA finished during iteration k-1's
+// work) with the job NS-1 ahead, whose block ids were read one iteration
+// earlier.  All 32 lanes run the loop; lane 0 waits on barriers (result
+// broadcast) and issues the MMAs.  After a failed wait the warp stops
+// waiting and issuing but keeps committing, so every epilogue barrier still
+// completes; copies still in flight are drained (bounded) before it returns.
+template <bool kStats, int NS>
+KVS_DEV void ws_control(const LayerLaunch& L, const WsSmem& S, uint32_t tmem, const WsMap& M) {
+  const int H = L.num_heads;
+  const int n = M.n;
+  const int lane = threadIdx.x & 31;
+  ItemCursor ld, mm;  // cursors of the load stream and of the MMA stream
+  cursor_init(ld);
+  cursor_init(mm);
+  auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
+    bool r = true;
+    if (lane == 0) r = mbar_wait(bar, parity, L.err, ERR_MBAR_TIMEOUT);
+    return __shfl_sync(0xFFFFFFFFu, r ? 1 : 0, 0) != 0;
+  };
+  int issued = 0, consumed = 0;
+  for (; issued < NS && issued < n; ++issued)
+    issue_boxes(box_desc(L, ld, ws_job(M, issued)), ws_stage(S, issued), &S.full[issued]);
+  BoxDesc next{};
+  if (issued < n) next = box_desc(L, ld, ws_job(M, issued));
+  int cur_img = -1;
+  uint32_t img_phase = 0;
+  bool ok = true;
+  for (int k = 0; k < n; ++k) {
+    const int st = k % NS;
+    const int a = ws_acc(k);
+    const PJob jb = ws_job(M, k);
+    cursor_seek(L, mm, jb.tile);
+    const int img_key = mm.c.slot * H + jb.h;
+    if (ok && img_key != cur_img) {
+      if (k >= 1)  // MMA k-1 done: the old image is no longer read
+        ok = wait0(&S.sfree[(k - 1) % NS], static_cast<uint32_t>(((k - 1) / NS) & 1));
+      if (ok) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(S.imgb, 32768u);
+          bulk_load(ws_img(S), bmat_of(L, mm.c.slot, jb.h), 32768, S.imgb);
+        }
+        ok = wait0(S.imgb, img_phase);
+        img_phase ^= 1u;
+      }
+      cur_img = img_key;
+    }
+    if (ok) {
+      ok = wait0(&S.full[st], static_cast<uint32_t>((k / NS) & 1));
+      if (ok) ++consumed;
+    }
+    if (lane == 0) trace_mark(L, k, 0);
+    if (ok && k >= 4) ok = wait0(&S.afree[a], static_cast<uint32_t>(((k >> 2) - 1) & 1));
+    if (lane == 0) trace_mark(L, k, 5);
+    if (lane == 0) {
+      if (ok) {
+        tc_fence_after();
+        const uint32_t acc = tmem + static_cast<uint32_t>(a * 128);
+        if (kStats && jb.plane == 0) {
+          umma_tile_128x128x128(acc, smem_u32(ws_img(S)), smem_u32(ws_stage(S, st)));  // lane = channel
+        } else {
+          umma_tile_128x128x128(acc, smem_u32(ws_stage(S, st)), smem_u32(ws_img(S)));  // lane = row
+        }
+      }
+      umma_commit(&S.mma[a]);
+      umma_commit(&S.sfree[st]);
+      trace_mark(L, k, 1);
+    }
+    __syncwarp();
+    if (k >= 1 && issued < n && ok) {  // refill the stage job k-1 used
+      const int ps = (k - 1) % NS;
+      ok = wait0(&S.sfree[ps], static_cast<uint32_t>(((k - 1) / NS) & 1));
+      if (ok) {
+        issue_boxes(next, ws_stage(S, ps), &S.full[ps]);
+        if (lane == 0) trace_mark(L, issued, 2);
+        ++issued;
+        if (issued < n) next = box_desc(L, ld, ws_job(M, issued));
+      }
+    }
+  }
+  if (lane == 0)
+    for (int k = consumed; k < issued; ++k)
+      mbar_wait(&S.full[k % NS], static_cast<uint32_t>((k / NS) & 1), nullptr, 0);
+}
+
+// ------------------------------------------------------------ stats (ws)
+__global__ void __launch_bounds__(kWsThreads, 1) k_stats_ws(LayerLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  constexpr int NS = 5;
+  const WsSmem S = ws_smem<WsStatsLayout>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = L.num_heads;
+  const WsMap M = ws_map(L);
+  const int n = M.n;
+  if (n <= 0) return;
+  if (tid == 0) ws_init(S, NS);
+  if (warp == kWsCtrlWarp) tmem_alloc(S.tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *S.tslot;
+  if (warp == kWsCtrlWarp) {
+    ws_control<true, NS>(L, S, tmem, M);
+  } else {
+    const int g = warp / kWsGroupWarps, gw = warp % kWsGroupWarps;
+    const int quad = gw & 3, half = gw >> 2;
+    const int lane_id = quad * 32 + lane;  // TMEM lane = channel (keys) or row (values)
+    float run_mn = INFINITY, run_mx = -INFINITY;
+    int run_key = -1;
+    ItemCursor cur;
+    cursor_init(cur);
+    for (int k = g; k < n; k += kWsGroups) {
+      const PJob jb = ws_job(M, k);
+      cursor_seek(L, cur, jb.tile);
+      const ItemCtx& c = cur.c;
+      const int a = ws_acc(k);
+      mbar_wait(&S.mma[a], static_cast<uint32_t>((k >> 2) & 1), L.err, ERR_MBAR_TIMEOUT);
+      if (gw == 0 && lane == 0) trace_mark(L, k, 3);
+      tc_fence_after();
+      const uint32_t taddr = tmem + static_cast<uint32_t>(a * 128) +
+                             (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+      float mn = INFINITY, mx = -INFINITY;
+      const int nvalid = jb.plane == 0 ? min(kTileRows, c.ntok - c.row0) : kTileRows;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        tmem_ld32(taddr + cc * 32, v);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          if (half * 64 + cc * 32 + q < nvalid) {
+            mn = fminf(mn, v[q]);
+            mx = fmaxf(mx, v[q]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.afree[a]);
+      // fl(x*sc) is non-decreasing in x for sc > 0: scale the extremes once.
+      const float sc = c.lp->out_scale;
+      if (mn <= mx) {
+        mn *= sc;
+        mx *= sc;
+      }
+      float* red = ws_red(S, g, k);
+      if (jb.plane == 0) {
+        const int key = c.r * H + jb.h;
+        if (key != run_key) {
+          if (run_key >= 0 && run_mn <= run_mx) {
+            uint32_t* ks = L.kstat + (static_cast<size_t>(run_key) * 128 + lane_id) * 2;
+            atomicMin(ks, float_to_ordered(run_mn));
+            atomicMax(ks + 1, float_to_ordered(run_mx));
+          }
+          run_key = key;
+          run_mn = INFINITY;
+          run_mx = -INFINITY;
+        }
+        run_mn = fminf(run_mn, mn);
+        run_mx = fmaxf(run_mx, mx);
+      } else if (half == 1) {
+        red[lane_id * 2] = mn;
+        red[lane_id * 2 + 1] = mx;
+      }
+      group_sync(g);
+      if (jb.plane == 1 && half == 0) {
+        mn = fminf(mn, red[lane_id * 2]);
+        mx = fmaxf(mx, red[lane_id * 2 + 1]);
+        const int row = c.row0 + lane_id;
+        if (row < c.rows) {
+          if (row >= c.ntok) mn = mx = 0.f;
+          float* e = vstat_entry(L, c, jb.h, row);
+          e[0] = mn;
+          e[1] = mx;
+        }
+      }
+      if (gw == 0 && lane == 0) trace_mark(L, k, 4);
+    }
+    if (run_key >= 0 && run_mn <= run_mx) {
+      uint32_t* ks = L.kstat + (static_cast<size_t>(run_key) * 128 + lane_id) * 2;
+      atomicMin(ks, float_to_ordered(run_mn));
+      atomicMax(ks + 1, float_to_ordered(run_mx));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWsCtrlWarp) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------ quant (ws)
+__global__ void __launch_bounds__(kWsThreads, 1) k_quant_ws(LayerLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  constexpr int NS = 4;
+  const WsSmem S = ws_smem<WsQuantLayout>(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = L.num_heads;
+  const WsMap M = ws_map(L);
+  const int n = M.n;
+  if (n <= 0) return;
+  if (tid == 0) ws_init(S, NS);
+  if (warp == kWsCtrlWarp) tmem_alloc(S.tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *S.tslot;
+  if (warp == kWsCtrlWarp) {
+    ws_control<false, NS>(L, S, tmem, M);
+  } else {
+    const int g = warp / kWsGroupWarps, gw = warp % kWsGroupWarps;
+    const int gtid = tid - g * kWsGroupThreads;
+    const int quad = gw & 3, half = gw >> 2;
+    const int lane_id = quad * 32 + lane;  // TMEM lane = tile row
+    float* kp = ws_kp(S, g);               // [128][2] key (min, rcp)
+    uint8_t* stage = ws_staging(S, g);
+    ItemCursor cur;
+    cursor_init(cur);
+    int kp_key = -1;  // (item, head) whose key parameters kp holds
+    for (int k = g; k < n; k += kWsGroups) {
+      const PJob jb = ws_job(M, k);
+      cursor_seek(L, cur, jb.tile);
+      const ItemCtx& c = cur.c;
+      const int pk = c.r * H + jb.h;
+      const int row = c.row0 + lane_id;
+      const bool exists = row < c.rows, valid = row < c.ntok;
+      float vmin = 0.f, vrcp = 0.f;
+      if (jb.plane == 1 && exists) {
+        // both halves of the row compute it (no exchange); half 0 publishes
+        if (half == 0) {
+          value_row_params(L, c, jb.h, row, &vmin, &vrcp);
+        } else {
+          const LayerParams* lp = c.lp;
+          const int grp = lp->group_of_head[jb.h];
+          float mn = INFINITY, mx = -INFINITY;
+          for (int hh = 0; hh < lp->H; ++hh) {
+            if (lp->group_of_head[hh] != grp) continue;
+            const float* e = vstat_entry(L, c, hh, row);
+            mn = fminf(mn, e[0]);
+            mx = fmaxf(mx, e[1]);
+          }
+          const float scale = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), kRangeEps),
+                                        lp->value_levels[jb.h] - 1.0f);
+          vmin = mn;
+          vrcp = __frcp_rn(scale);
+        }
+      }
+      if (jb.plane == 0 && (pk != kp_key || c.row0 == 0)) {  // row0 == 0 publishes the metadata
+        // kp's readers of an earlier job finished before that job's staging
+        // barrier, which this thread has passed
+        if (gtid < 128) key_channel_params(L, c, jb.h, kp, kp + 1, 2, gtid);
+        kp_key = pk;
+      }
+      // key parameters visible; every thread finished copying out the
+      // group's previous job, so the staging buffer is free
+      group_sync(g);
+      const int a = ws_acc(k);
+      mbar_wait(&S.mma[a], static_cast<uint32_t>((k >> 2) & 1), L.err, ERR_MBAR_TIMEOUT);
+      if (gw == 0 && lane == 0) trace_mark(L, k, 3);
+      tc_fence_after();
+      const float lev = jb.plane == 0 ? c.lp->key_levels[jb.h] : c.lp->value_levels[jb.h];
+      const float top = c.lp->clamp_top ? lev - 1.0f : lev;
+      const int bits = seg_bits(c, jb.plane, jb.h);
+      const int P = (bits | 1) * 16;  // odd multiple of 16 B: spreads rows over bank groups
+      uint8_t* row_stage = stage + lane_id * P;
+      const uint32_t taddr = tmem + static_cast<uint32_t>(a * 128) +
+                             (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+      const float sc = c.lp->out_scale;
+      switch (bits) {
+        case 1: p_quant_half<1>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 2: p_quant_half<2>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 3: p_quant_half<3>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 4: p_quant_half<4>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 5: p_quant_half<5>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 6: p_quant_half<6>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 7: p_quant_half<7>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        default: p_quant_half<8>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.afree[a]);
+      group_sync(g);  // staging complete
+      // Coalesced 16-byte copy of the tile's contiguous code region.
+      const int nrows = min(kTileRows, c.rows - c.row0);
+      uint8_t* dst0 = code_row(L, c, jb.plane, jb.h, c.row0);
+      const int total = nrows * bits;
+      for (int q = gtid; q < total; q += kWsGroupThreads) {
+        const int r = q / bits, col = q - r * bits;
+        *reinterpret_cast<uint4*>(dst0 + static_cast<long long>(q) * 16) =
+            *reinterpret_cast<const uint4*>(stage + r * P + col * 16);
+      }
+      if (gw == 0 && lane == 0) trace_mark(L, k, 4);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWsCtrlWarp) tmem_dealloc(tmem, 512);
+}
+
 // ---------------------------------------------------------------- dequant
 // Unpack one 32-code group of a row into bf16 and store it into the
 // swizzled A tile (row t, channels 32*part..+31).
@@ -1412,6 +1936,20 @@ static int persistent_grid(const LayerLaunch& L) {
   return static_cast<int>(jobs < 2LL * sms ? jobs : 2LL * sms);  // jobs < 2^31: checked by the caller
 }
 
+// Warp-specialized grid: 2*H*R CTAs (at most one per SM), R tile ranges
+// of at least one tile each.
+static int ws_grid(const LayerLaunch& L) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    sms = 148;
+  const int PH = 2 * L.num_heads;
+  int R = sms / PH;
+  if (R < 1) R = 1;
+  if (R > L.total_tiles) R = L.total_tiles;
+  return PH * R;
+}
+
 template <typename K>
 static int set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
@@ -1469,6 +2007,9 @@ int kvs_stats(const LayerLaunch* Lp) {
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
+    if (int rc = set_smem(k_stats_ws, WsStatsLayout::kSmem)) return rc;
+    k_stats_ws<<<ws_grid(L), kWsThreads, WsStatsLayout::kSmem, s>>>(L);
+  } else if (L.engine == 3) {
     if (int rc = set_smem(k_stats_tc, kPSmem)) return rc;
     k_stats_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
   } else if (L.engine == 2) {
@@ -1488,6 +2029,9 @@ int kvs_quant(const LayerLaunch* Lp) {
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
+    if (int rc = set_smem(k_quant_ws, WsQuantLayout::kSmem)) return rc;
+    k_quant_ws<<<ws_grid(L), kWsThreads, WsQuantLayout::kSmem, s>>>(L);
+  } else if (L.engine == 3) {
     if (int rc = set_smem(k_quant_tc, kPSmem)) return rc;
     k_quant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
   } else if (L.engine == 2) {
@@ -1505,7 +2049,7 @@ int kvs_dequant_inverse(const LayerLaunch* Lp) {
   if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
-  if (L.engine == 0) {
+  if (L.engine == 0 || L.engine == 3) {
     if (int rc = set_smem(k_dequant_tc, kPSmem)) return rc;
     k_dequant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
   } else if (L.engine == 2) {

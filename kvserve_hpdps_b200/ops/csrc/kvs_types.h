@@ -72,8 +72,13 @@ struct LayerLaunch {
   uint32_t* err;           // device error word
   int total_tiles;
   int num_heads;           // H (identical for every slot of a launch)
-  int engine;              // 0: persistent tcgen05 + TMA ; 1: SIMT (in-register FWHT) ; 2: tcgen05, one CTA per tile
+  int engine;              // 0: warp-specialized tcgen05 + TMA ; 1: SIMT ; 2: tcgen05 per tile ; 3: persistent tcgen05
   void* stream;            // cudaStream_t
+  // Optional device trace (nullptr = off): globaltimer stamps
+  // trace[(cta * trace_jobs + job) * 8 + event] for CTAs < kTraceCtas.
+  unsigned long long* trace;
+  int trace_jobs;
 };
+constexpr int kTraceCtas = 4;
 
 }  // namespace kvs

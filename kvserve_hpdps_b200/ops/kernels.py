@@ -35,9 +35,10 @@ from kvserve_hpdps_b200.ops._lib import LayerLaunch, PagedKV, check, lib
 HEAD_DIM = 128
 TILE_ROWS = 128
 RANS_CHUNK = 32768
-ENGINE_TCGEN05 = 0       # persistent tcgen05 kernels (default)
+ENGINE_TCGEN05 = 0       # warp-specialized persistent tcgen05 kernels (default)
 ENGINE_SIMT = 1          # SIMT butterfly
 ENGINE_TCGEN05_TILE = 2  # tcgen05, one CTA per tile
+ENGINE_TCGEN05_PERSISTENT = 3  # persistent tcgen05 without warp specialization
 
 ERR_NAMES = {0: "none", 1: "mbarrier timeout", 2: "ready-flag timeout", 3: "bounds",
              4: "corrupt stream", 5: "overflow"}
@@ -511,6 +512,26 @@ class RequestBatch:
 
 
 # ---------------------------------------------------------------- fused ops
+# Device trace of the warp-specialized kernels (diagnostics; off by default).
+TRACE_CTAS = 4
+TRACE_EVENTS = ("tile_ready", "mma_issued", "refill_issued", "epi_mma_seen", "epi_done",
+                "acc_free_seen", "unused6", "unused7")
+_trace = {"buf": None, "jobs": 0}
+
+
+def set_trace(device: Optional[torch.device], jobs_per_cta: int = 256) -> Optional[torch.Tensor]:
+    """Enable (device given) or disable (None) globaltimer tracing of the
+    warp-specialized kernels for the first TRACE_CTAS CTAs of each launch;
+    returns the trace buffer [TRACE_CTAS, jobs_per_cta, 8] (int64 ns, 0 =
+    no event).  Every traced launch overwrites it."""
+    if device is None:
+        _trace["buf"], _trace["jobs"] = None, 0
+        return None
+    _trace["buf"] = torch.zeros((TRACE_CTAS, jobs_per_cta, 8), dtype=torch.int64, device=device)
+    _trace["jobs"] = int(jobs_per_cta)
+    return _trace["buf"]
+
+
 def _launch(slots: LayerSlots, items: WorkItems, bmat: torch.Tensor, codes, meta, kstat, vstat,
             engine: int) -> LayerLaunch:
     dev = slots.device
@@ -530,6 +551,9 @@ def _launch(slots: LayerSlots, items: WorkItems, bmat: torch.Tensor, codes, meta
     L.num_heads = slots.num_heads
     L.engine = engine
     L.stream = _stream(dev)
+    if _trace["buf"] is not None:
+        L.trace = _trace["buf"].data_ptr()
+        L.trace_jobs = _trace["jobs"]
     return L
 
 

@@ -16,7 +16,7 @@ from kvserve_hpdps_b200.ops import kernels as K
 
 pytestmark = pytest.mark.gpu
 
-ENGINES = [K.ENGINE_TCGEN05, K.ENGINE_SIMT, K.ENGINE_TCGEN05_TILE]
+ENGINES = [K.ENGINE_TCGEN05, K.ENGINE_SIMT, K.ENGINE_TCGEN05_TILE, K.ENGINE_TCGEN05_PERSISTENT]
 
 
 def _plan(H, layer_id=5, packed=False, seed=0x3333):
@@ -230,8 +230,8 @@ def test_engines_agree():
 
 
 @pytest.mark.parametrize("packed", [False, True])
-def test_persistent_engine_bit_exact_vs_tile_engine(packed):
-    """The persistent kernels walk many jobs per CTA (image reloads at
+def test_persistent_engines_bit_exact_vs_tile_engine(packed):
+    """The persistent kernels (warp-specialized and not) walk many jobs per CTA (image reloads at
     layer/head changes, key statistics carried across tiles, odd token
     counts, partial tiles): codes, metadata and reconstruction must equal
     the one-CTA-per-tile engine bit for bit."""
@@ -243,7 +243,7 @@ def test_persistent_engine_bit_exact_vs_tile_engine(packed):
     slots = K.LayerSlots([wl.cache[l] for l in range(L)], plans)
     items = K.WorkItems(slots, [(l, b, t) for l in range(L) for b, t in zip(wl.block_ids, tokens)])
     outs = []
-    for engine in (K.ENGINE_TCGEN05, K.ENGINE_TCGEN05_TILE):
+    for engine in (K.ENGINE_TCGEN05_TILE, K.ENGINE_TCGEN05, K.ENGINE_TCGEN05_PERSISTENT):
         codes, meta = K.quantize(slots, items, engine=engine)
         dst = torch.zeros_like(wl.cache)
         dslots = K.LayerSlots([dst[l] for l in range(L)], plans)
@@ -251,13 +251,14 @@ def test_persistent_engine_bit_exact_vs_tile_engine(packed):
         torch.cuda.synchronize()
         K.check_device_error(wl.cache.device)
         outs.append((codes.clone(), meta.clone(), dst))
-    assert torch.equal(outs[0][0], outs[1][0]), "codes differ"
-    assert torch.equal(outs[0][1], outs[1][1]), "metadata differ"
-    for l in range(L):
-        for b, t in zip(wl.block_ids, tokens):
-            a = gather_request(outs[0][2][l], b).view(2, -1, H, 128)[:, :t]
-            c = gather_request(outs[1][2][l], b).view(2, -1, H, 128)[:, :t]
-            assert torch.equal(a, c), f"reconstruction differs (layer {l}, {t} tokens)"
+    for o in outs[1:]:
+        assert torch.equal(outs[0][0], o[0]), "codes differ"
+        assert torch.equal(outs[0][1], o[1]), "metadata differ"
+        for l in range(L):
+            for b, t in zip(wl.block_ids, tokens):
+                a = gather_request(outs[0][2][l], b).view(2, -1, H, 128)[:, :t]
+                c = gather_request(o[2][l], b).view(2, -1, H, 128)[:, :t]
+                assert torch.equal(a, c), f"reconstruction differs (layer {l}, {t} tokens)"
 
 
 @pytest.mark.parametrize("n", [1, 511, 4096, 32768, 100000, 300001])
