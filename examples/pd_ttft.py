@@ -1,0 +1,205 @@
+"""Prefill/decode disaggregated serving on one box: TTFT with the
+compressed KV connector.
+
+Two vLLM V1 engines run as two processes on two GPUs: the producer
+(``kv_producer``, prefill) and the consumer (``kv_consumer``, decode), each
+with the connector loaded through ``kv_connector_module_path``.  Every
+request is dispatched to both engines at the same moment with the same
+``transfer_id``; the consumer's scheduler claims the prompt's KV as external
+tokens and its worker waits for the producer's message, injects the KV and
+computes the first output token.  TTFT of a request = time from dispatch
+until the consumer returned its first token.
+
+Model: the Qwen2.5-7B architecture with random-init weights
+(``load_format="dummy"``, no checkpoint needed), synthetic prompts of uniform
+token ids.  ``--impl reference`` loads the reference connector
+(``kvserve_v1``) from ``baseline/_ref`` instead of this package's.
+
+Example::
+
+  python examples/pd_ttft.py --requests 32 --prompt-len 8192 --compression default
+  python examples/pd_ttft.py --compression none          # raw KV over the NVLink ring
+  python examples/pd_ttft.py --impl reference --compression none
+
+Prints one JSON line with p50 / p90 / mean TTFT and the producer-side
+prefill latency.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+QWEN25_7B = {
+    "architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2", "hidden_act": "silu",
+    "hidden_size": 3584, "intermediate_size": 18944, "num_hidden_layers": 28,
+    "num_attention_heads": 28, "num_key_value_heads": 4, "vocab_size": 152064,
+    "max_position_embeddings": 32768, "rope_theta": 1000000.0, "rms_norm_eps": 1e-6,
+    "tie_word_embeddings": False, "torch_dtype": "bfloat16", "use_sliding_window": False,
+    "sliding_window": None, "max_window_layers": 28, "bos_token_id": 151643,
+    "eos_token_id": 151645, "attention_dropout": 0.0, "initializer_range": 0.02,
+    "use_cache": True,
+}
+
+
+def write_model_dir(path: str) -> str:
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(QWEN25_7B, f)
+    return path
+
+
+def compression_spec(name: str):
+    if name == "none":
+        return None
+    if name == "default":
+        return "default"
+    if name == "quantizer":  # the reference's degraded custom pipeline (no codec)
+        return {"enabled": True, "pipeline": ["quantizer"],
+                "quantizer_config": {"hybrid_ratio": 0.8, "high_key_max_value": 12,
+                                     "high_value_max_value": 8, "low_key_max_value": 6,
+                                     "low_value_max_value": 4, "axis_key": "channel",
+                                     "axis_value": "token", "split_type": "head"},
+                "min_compress_size": 0}
+    raise ValueError(name)
+
+
+def engine(role: str, gpus: str, args, q_in, q_out) -> None:
+    os.environ["CUDA_VISIBLE_DEVICES"] = gpus
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        os.environ["PYTHONPATH"] = os.path.join(ROOT, "baseline", "_ref") + os.pathsep + \
+            os.environ.get("PYTHONPATH", "")
+    else:
+        sys.path.insert(0, ROOT)
+    try:
+        from vllm import LLM, SamplingParams
+        from vllm.config import KVTransferConfig
+        module = ("kvserve_v1.connector.compressed_kv_connector" if args.impl == "reference"
+                  else "kvserve_hpdps_b200.connector.compressed_kv_connector")
+        extra = {"compression": compression_spec(args.compression)}
+        if args.impl != "reference":
+            extra["transport"] = args.transport
+        ktc = KVTransferConfig(kv_connector="CompressedKVConnector",
+                               kv_connector_module_path=module,
+                               kv_role="kv_producer" if role == "p" else "kv_consumer",
+                               kv_rank=0 if role == "p" else 1, kv_parallel_size=2,
+                               kv_ip="127.0.0.1", kv_port=args.port,
+                               kv_connector_extra_config=extra)
+        llm = LLM(model=args.model_dir, dtype="bfloat16", load_format="dummy",
+                  skip_tokenizer_init=True, max_model_len=args.prompt_len + args.max_tokens + 64,
+                  max_num_batched_tokens=args.prompt_len + 64, max_num_seqs=8,
+                  gpu_memory_utilization=args.mem_util, enforce_eager=True,
+                  enable_prefix_caching=False, kv_transfer_config=ktc, seed=0)
+        q_out.put(("ready", role))
+        while True:
+            msg = q_in.get()
+            if msg[0] == "stop":
+                break
+            _, i, ids = msg
+            sp = SamplingParams(max_tokens=1 if role == "p" else args.max_tokens, temperature=0.0,
+                                detokenize=False,
+                                extra_args={"kv_transfer_params": {"transfer_id": f"req-{i}"}})
+            out = llm.generate([{"prompt_token_ids": ids}], sp, use_tqdm=False)
+            q_out.put(("done", role, i, time.time(), list(out[0].outputs[0].token_ids)))
+    except Exception:  # noqa: BLE001
+        import traceback
+        q_out.put(("error", role, traceback.format_exc()))
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--compression", choices=["default", "none", "quantizer"], default="default")
+    ap.add_argument("--transport", default="auto", help="ours: auto | p2p | nccl")
+    ap.add_argument("--requests", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--prompt-len", type=int, default=8192)
+    ap.add_argument("--max-tokens", type=int, default=1)
+    ap.add_argument("--gpus", default="0,1", help="producer GPU, consumer GPU")
+    ap.add_argument("--port", type=int, default=25010)
+    ap.add_argument("--mem-util", type=float, default=0.5)
+    ap.add_argument("--timeout", type=float, default=900.0)
+    args = ap.parse_args(argv)
+    args.model_dir = write_model_dir(os.path.join(tempfile.gettempdir(), "kvs_qwen25_7b_dummy"))
+    gp, gc = args.gpus.split(",")
+    ctx = mp.get_context("spawn")
+    qp, qc, qo = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    # each engine sees both GPUs, its own first (peer mappings need both visible)
+    pc = ctx.Process(target=engine, args=("c", f"{gc},{gp}", args, qc, qo))
+    pp = ctx.Process(target=engine, args=("p", f"{gp},{gc}", args, qp, qo))
+    pc.start()
+    time.sleep(1.0)
+    pp.start()
+    deadline = time.time() + args.timeout
+    ready = set()
+
+    def get():
+        left = deadline - time.time()
+        if left <= 0:
+            raise TimeoutError("engines did not answer in time")
+        m = qo.get(timeout=left)
+        if m[0] == "error":
+            raise RuntimeError(f"engine {m[1]} failed:\n{m[2]}")
+        return m
+
+    rc = 0
+    try:
+        while len(ready) < 2:
+            m = get()
+            ready.add(m[1])
+        import random
+        rng = random.Random(0)
+        ttft, prefill, first_tokens = [], [], []
+        for i in range(args.warmup + args.requests):
+            ids = [rng.randrange(0, QWEN25_7B["vocab_size"]) for _ in range(args.prompt_len)]
+            t0 = time.time()
+            qp.put(("go", i, ids))
+            qc.put(("go", i, ids))
+            got = {}
+            while len(got) < 2:
+                m = get()
+                got[m[1]] = m
+            if i >= args.warmup:
+                ttft.append((got["c"][3] - t0) * 1e3)
+                prefill.append((got["p"][3] - t0) * 1e3)
+                first_tokens.append(got["c"][4][:1])
+        q = sorted(ttft)
+        line = {"metric": "p50 TTFT, 1P1D (Qwen2.5-7B random-init, 8K prompt)",
+                "impl": args.impl, "compression": args.compression,
+                "transport": args.transport if args.impl == "ours" else "reference NcclTransport",
+                "requests": args.requests, "prompt_len": args.prompt_len,
+                "ttft_ms_p50": round(statistics.median(ttft), 2),
+                "ttft_ms_p90": round(q[int(0.9 * (len(q) - 1))], 2),
+                "ttft_ms_mean": round(statistics.mean(ttft), 2),
+                "producer_prefill_ms_p50": round(statistics.median(prefill), 2),
+                "handoff_ms_p50": round(statistics.median(
+                    [a - b for a, b in zip(ttft, prefill)]), 2),
+                "data": "synthetic uniform token ids; random-init weights (load_format=dummy)",
+                "timing": "host wall clock from dispatch to the consumer's first token"}
+        print(json.dumps(line), flush=True)
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"impl": args.impl, "compression": args.compression,
+                          "error": f"{type(e).__name__}: {e}"[:4000]}), flush=True)
+        rc = 1
+    finally:
+        for q in (qp, qc):
+            q.put(("stop",))
+        for p in (pp, pc):
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    return rc
+
+
+if __name__ == "__main__":
+    sys.exit(main())
