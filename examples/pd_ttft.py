@@ -189,7 +189,7 @@ def main(argv=None) -> int:
         print(json.dumps(line), flush=True)
     except Exception as e:  # noqa: BLE001
         print(json.dumps({"impl": args.impl, "compression": args.compression,
-                          "error": f"{type(e).__name__}: {e}"[:4000]}), flush=True)
+                          "error": f"{type(e).__name__}: {e}"[-6000:]}), flush=True)
         rc = 1
     finally:
         for q in (qp, qc):

@@ -293,15 +293,22 @@ class CompressedKVConnector(KVConnectorBase_V1):
             span = self._prefill_span(rid)
             layers = [self._layer_refs[n] for n in names]
             if comp is not None and comp.supports_paged():
-                cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],
-                                                  [(rm.block_ids, len(rm.token_ids))],
-                                                  member_tids=[tid])
-                nbytes = self._send_compressed(tid, names, cd, member_tids=[tid])
-                self._expected_msgs[tid] = 1
-                write_compression_stats(rid, tid, cd.original_size, nbytes,
-                                        compress_ms=(time.monotonic() - t0) * 1e3,
-                                        prefill_span_ms=span)
-                continue
+                try:
+                    cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],
+                                                      [(rm.block_ids, len(rm.token_ids))],
+                                                      member_tids=[tid])
+                except Exception:  # noqa: BLE001
+                    # as the reference does: a compression failure sends the raw KV
+                    logger.exception("compression of %s failed; sending raw KV", rid)
+                    cd = None
+                if cd is not None:
+                    nbytes = self._send_compressed(tid, names, cd, member_tids=[tid])
+                    self._expected_msgs[tid] = 1
+                    write_compression_stats(rid, tid, cd.original_size, nbytes,
+                                            compress_ms=(time.monotonic() - t0) * 1e3,
+                                            prefill_span_ms=span)
+                    continue
+                comp = None
             stacked = torch.stack([extract_kv_from_layer_by_blocks(l, rm.block_ids)
                                    for l in layers], 0)
             cd = comp.compress(stacked, rid) if comp is not None else None

@@ -25,7 +25,8 @@ MAX_HEADS = 16
 
 class PagedKV(ctypes.Structure):
     _fields_ = [("base", c_void_p), ("block_stride", c_longlong), ("kv_stride", c_longlong),
-                ("num_blocks", c_int), ("block_size", c_int)]
+                ("slot_stride", c_longlong), ("head_stride", c_longlong),
+                ("num_blocks", c_int), ("block_size", c_int), ("hnd", c_int), ("pad_", c_int)]
 
 
 class ReqTable(ctypes.Structure):

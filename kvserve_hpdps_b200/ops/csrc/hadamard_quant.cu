@@ -74,7 +74,8 @@ KVS_DEV int phys_block(const LayerLaunch& L, const ItemCtx& c, int row) {
 KVS_DEV __nv_bfloat16* kv_row(const ItemCtx& c, int plane, int phys, int slot, int h) {
   return const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(c.kv.base)) +
          phys * c.kv.block_stride + plane * c.kv.kv_stride +
-         (static_cast<long long>(slot) * c.lp->H + h) * kHeadDim;
+         static_cast<long long>(slot) * c.kv.slot_stride +
+         static_cast<long long>(h) * c.kv.head_stride;
 }
 
 KVS_DEV int seg_bits(const ItemCtx& c, int kv, int h) {
@@ -196,6 +197,12 @@ KVS_DEV void simt_forward_row(const ItemCtx& c, int plane, int phys, int slot, i
   for (int d = 0; d < 128; ++d) v[d] *= sc;
 }
 
+// TMA coordinates (y, z) of (head, slot) in a plane map: the maps order
+// their middle dimensions by stride (head then slot for NHD, slot then head
+// for HND), so a 16-slot box is 16 rows of 128 bytes either way.
+KVS_DEV int tma_y(const PagedKV& kv, int h, int slot) { return kv.hnd ? slot : h; }
+KVS_DEV int tma_z(const PagedKV& kv, int h, int slot) { return kv.hnd ? h : slot; }
+
 // ------------------------------------------------------- shared prologues
 // Issue the TMA loads of one 128-row tile of head h (plane chosen by the
 // map) into a 2 x 16 KB SW128 tile, arriving on `bar` with the expected
@@ -216,8 +223,8 @@ KVS_DEV void issue_tile_loads(const LayerLaunch& L, const ItemCtx& c, const CUte
       asm volatile(
           "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
           " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
-          "l"(reinterpret_cast<uint64_t>(map)), "r"(hb * 64), "r"(h), "r"(slot), "r"(phys),
-          "r"(smem_u32(bar))
+          "l"(reinterpret_cast<uint64_t>(map)), "r"(hb * 64), "r"(tma_y(c.kv, h, slot)),
+          "r"(tma_z(c.kv, h, slot)), "r"(phys), "r"(smem_u32(bar))
           : "memory");
     }
   }
@@ -722,7 +729,8 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
         asm volatile(
             "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
                 "l"(reinterpret_cast<uint64_t>(map)),
-            "r"(hb * 64), "r"(h), "r"(slot), "r"(phys), "r"(smem_u32(sA + hb * 16384 + g * 2048))
+            "r"(hb * 64), "r"(tma_y(c.kv, h, slot)), "r"(tma_z(c.kv, h, slot)), "r"(phys),
+            "r"(smem_u32(sA + hb * 16384 + g * 2048))
             : "memory");
       }
     }
@@ -1192,8 +1200,8 @@ KVS_DEV void issue_tile_loads_warp(const LayerLaunch& L, const ItemCtx& c, const
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(hb * 64), "r"(h), "r"(slot), "r"(phys),
-        "r"(smem_u32(bar))
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(hb * 64), "r"(tma_y(c.kv, h, slot)),
+        "r"(tma_z(c.kv, h, slot)), "r"(phys), "r"(smem_u32(bar))
         : "memory");
   }
   __syncwarp();
@@ -1332,7 +1340,7 @@ KVS_DEV PJob ws_job(const WsMap& m, int k) {
 // issue itself never waits on memory.
 struct BoxDesc {
   const CUtensorMap* map;
-  int h, slot, phys, nload;
+  int y, z, phys, nload;  // y, z: TMA coordinates of (head, slot)
   bool mine;
 };
 KVS_DEV BoxDesc box_desc(const LayerLaunch& L, ItemCursor& cur, const PJob& jb) {
@@ -1341,14 +1349,15 @@ KVS_DEV BoxDesc box_desc(const LayerLaunch& L, ItemCursor& cur, const PJob& jb) 
   const ItemCtx& c = cur.c;
   BoxDesc d;
   d.map = map_of(L, c.slot, jb.plane);
-  d.h = jb.h;
   d.nload = min(8, (c.rows - c.row0 + 15) / 16);
   d.mine = lane < 2 * d.nload;
-  d.slot = d.phys = 0;
+  d.y = d.z = d.phys = 0;
   if (d.mine) {
     const int rr = c.row0 + (lane >> 1) * 16;
+    const int slot = rr % c.kv.block_size;
     d.phys = phys_block(L, c, rr);
-    d.slot = rr % c.kv.block_size;
+    d.y = tma_y(c.kv, jb.h, slot);
+    d.z = tma_z(c.kv, jb.h, slot);
   }
   return d;
 }
@@ -1361,7 +1370,7 @@ KVS_DEV void issue_boxes(const BoxDesc& d, uint8_t* tile, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
-        "l"(reinterpret_cast<uint64_t>(d.map)), "r"(hb * 64), "r"(d.h), "r"(d.slot), "r"(d.phys),
+        "l"(reinterpret_cast<uint64_t>(d.map)), "r"(hb * 64), "r"(d.y), "r"(d.z), "r"(d.phys),
         "r"(smem_u32(bar))
         : "memory");
   }
@@ -1885,7 +1894,8 @@ __global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
           asm volatile(
               "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
                   "l"(reinterpret_cast<uint64_t>(map)),
-              "r"(hb * 64), "r"(jb.h), "r"(slot), "r"(phys), "r"(smem_u32(sA + hb * 16384 + g * 2048))
+              "r"(hb * 64), "r"(tma_y(c.kv, jb.h, slot)), "r"(tma_z(c.kv, jb.h, slot)), "r"(phys),
+              "r"(smem_u32(sA + hb * 16384 + g * 2048))
               : "memory");
         }
       }
@@ -1969,8 +1979,9 @@ int kvs_layer_params_size(void) { return static_cast<int>(sizeof(LayerParams)); 
 int kvs_paged_kv_size(void) { return static_cast<int>(sizeof(PagedKV)); }
 
 // Encode the K and V plane maps of one paged layer into out[0..1] (host
-// memory, 128 bytes each): 4-D (d=128, head, slot, block), box (64,1,16,1),
-// 128-byte swizzle, no OOB fill.
+// memory, 128 bytes each): 4-D (d=128, head, slot, block) with box
+// (64,1,16,1) for NHD blocks, (d, slot, head, block) with box (64,16,1,1) for
+// HND blocks; 128-byte swizzle, no OOB fill.
 int kvs_make_plane_maps(const PagedKV* kv, int H, void* out) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return -100;
@@ -1978,12 +1989,16 @@ int kvs_make_plane_maps(const PagedKV* kv, int H, void* out) {
   for (int plane = 0; plane < 2; ++plane) {
     void* base = const_cast<void*>(reinterpret_cast<const void*>(
         reinterpret_cast<const __nv_bfloat16*>(kv->base) + plane * kv->kv_stride));
-    cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(H),
-                          static_cast<cuuint64_t>(kv->block_size),
+    // (d, head, slot, block) for NHD, (d, slot, head, block) for HND: the
+    // middle dimensions in increasing stride order
+    const cuuint64_t hd = static_cast<cuuint64_t>(H), sl = static_cast<cuuint64_t>(kv->block_size);
+    cuuint64_t dims[4] = {128, kv->hnd ? sl : hd, kv->hnd ? hd : sl,
                           static_cast<cuuint64_t>(kv->num_blocks)};
-    cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(H) * 256,
+    const cuuint64_t hs = static_cast<cuuint64_t>(kv->head_stride) * 2;
+    const cuuint64_t ss = static_cast<cuuint64_t>(kv->slot_stride) * 2;
+    cuuint64_t strides[3] = {kv->hnd ? ss : hs, kv->hnd ? hs : ss,
                              static_cast<cuuint64_t>(kv->block_stride) * 2};
-    cuuint32_t box[4] = {64, 1, 16, 1};
+    cuuint32_t box[4] = {64, kv->hnd ? 16u : 1u, kv->hnd ? 1u : 16u, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = fn(&maps[plane], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

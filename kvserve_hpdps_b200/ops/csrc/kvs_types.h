@@ -12,15 +12,21 @@ constexpr int kHeadDim = 128;   // the fused kernels are specialised for D=128
 constexpr int kTileRows = 128;  // tokens per tile
 
 // Paged KV source/destination: element (block, slot, head, d) of plane kv
-// lives at base + block*block_stride + kv*kv_stride + (slot*H + head)*D + d
-// (element units, bf16).  Covers [2, nb, bs, H, D] (FlashAttention) and
-// [nb, 2, bs, H, D] (FlashInfer) layouts.
+// lives at base + block*block_stride + kv*kv_stride + slot*slot_stride +
+// head*head_stride + d (element units, bf16).  Covers the [2, nb, bs, H, D]
+// (FlashAttention) and [nb, 2, bs, H, D] (FlashInfer) block orders, each with
+// the (slot, head) plane token-major (NHD: slot_stride = H*D, head_stride = D)
+// or head-major (HND: head_stride = bs*D, slot_stride = D, hnd = 1).
 struct PagedKV {
   const void* base;
   long long block_stride;
   long long kv_stride;
+  long long slot_stride;
+  long long head_stride;
   int num_blocks;
   int block_size;
+  int hnd;
+  int pad_;
 };
 
 // Work items of one launch.  An item is one (layer, request) pair: its

@@ -301,18 +301,26 @@ def _align16(x: int) -> int:
 def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
     """Describe a paged KV layer tensor for the kernels.
 
-    Accepts [2, nb, bs, H, D] (FlashAttention / NHD) and [nb, 2, bs, H, D]
-    (FlashInfer) bf16 tensors with contiguous (bs, H, D) inner dims.
+    Accepts logical [2, nb, bs, H, D] (FlashAttention) and [nb, 2, bs, H, D]
+    (FlashInfer) bf16 tensors whose (slot, head, d) block is either
+    token-major (NHD: strides H*D, D, 1) or head-major (HND: strides D,
+    bs*D, 1), as vLLM's attention backends allocate them.
     """
     if kv_layer.dtype != torch.bfloat16:
         raise TypeError(f"KV cache must be bf16, got {kv_layer.dtype}")
     if kv_layer.dim() != 5 or kv_layer.shape[-1] != HEAD_DIM:
         raise ValueError(f"expected a [2, nb, bs, H, {HEAD_DIM}] layer, got {tuple(kv_layer.shape)}")
     st = kv_layer.stride()
-    H, D = kv_layer.shape[3], kv_layer.shape[4]
-    if st[4] != 1 or st[3] != D or st[2] != H * D:
-        raise ValueError("KV layer inner dims (bs, H, D) must be contiguous")
-    if kv_layer.shape[2] % 16:
+    bs, H, D = kv_layer.shape[2], kv_layer.shape[3], kv_layer.shape[4]
+    if st[4] != 1:
+        raise ValueError("KV layer head_dim must be contiguous")
+    if st[3] == D and st[2] == H * D:
+        hnd = 0
+    elif st[2] == D and st[3] == bs * D:
+        hnd = 1
+    else:
+        raise ValueError(f"unsupported KV block layout with strides {st}")
+    if bs % 16:
         raise ValueError("block_size must be a multiple of 16")
     p = PagedKV()
     p.base = kv_layer.data_ptr()
@@ -322,7 +330,9 @@ def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
     else:
         p.kv_stride, p.block_stride = st[0], st[1]
         p.num_blocks = kv_layer.shape[1]
-    p.block_size = kv_layer.shape[2]
+    p.slot_stride, p.head_stride = st[2], st[3]
+    p.block_size = bs
+    p.hnd = hnd
     return p
 
 

@@ -331,3 +331,45 @@ def test_wait_flag_times_out_with_error_status():
     K.wait_flag(flag.data_ptr(), 1, flag.device, timeout_s=0.05)
     torch.cuda.synchronize()
     assert K.read_device_error(flag.device) == 0
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+def test_head_major_block_layout_matches_token_major(engine):
+    """vLLM's FlashInfer cache on B200 is [nb, 2, bs, H, D] with a head-major
+    (HND) block: the kernels must read and write it exactly like the
+    token-major (NHD) form of the same logical values."""
+    H, L = 4, 2
+    tokens = [200, 33]
+    wl = paged_workload(L, tokens, H, device="cuda", seed=21)
+    nb, bs = wl.cache.shape[2], wl.cache.shape[3]
+    # same logical values in a FlashInfer-ordered, head-major cache
+    hnd = []
+    for l in range(L):
+        storage = torch.empty((nb, 2, H, bs, 128), dtype=torch.bfloat16, device="cuda")
+        view = storage.permute(0, 1, 3, 2, 4)  # logical [nb, 2, bs, H, D], HND strides
+        view.copy_(wl.cache[l].permute(1, 0, 2, 3, 4))
+        hnd.append(view)
+    plans = [K.make_layer_plan(H, [12, 6, 16, 6], [8, 4, 4, 16], 0x3333, l) for l in range(L)]
+    items_spec = [(l, b, t) for l in range(L) for b, t in zip(wl.block_ids, tokens)]
+    s_nhd = K.LayerSlots([wl.cache[l] for l in range(L)], plans)
+    s_hnd = K.LayerSlots(hnd, plans)
+    c0, m0 = K.quantize(s_nhd, K.WorkItems(s_nhd, items_spec), engine=engine)
+    c1, m1 = K.quantize(s_hnd, K.WorkItems(s_hnd, items_spec), engine=engine)
+    torch.cuda.synchronize()
+    K.check_device_error(wl.cache.device)
+    assert torch.equal(c0, c1) and torch.equal(m0, m1)
+    dst_nhd = torch.zeros_like(wl.cache)
+    dst_hnd = [torch.zeros((nb, 2, H, bs, 128), dtype=torch.bfloat16,
+                           device="cuda").permute(0, 1, 3, 2, 4) for _ in range(L)]
+    d0 = K.LayerSlots([dst_nhd[l] for l in range(L)], plans)
+    d1 = K.LayerSlots(dst_hnd, plans)
+    K.dequantize(c0, m0, d0, K.WorkItems(d0, items_spec), engine=engine)
+    K.dequantize(c1, m1, d1, K.WorkItems(d1, items_spec), engine=engine)
+    torch.cuda.synchronize()
+    K.check_device_error(wl.cache.device)
+    for l in range(L):
+        for b, t in zip(wl.block_ids, tokens):
+            idx = torch.tensor(b, device="cuda")
+            a = dst_nhd[l][:, idx].reshape(2, -1, H, 128)[:, :t]
+            c = dst_hnd[l][idx].permute(1, 0, 2, 3, 4).reshape(2, -1, H, 128)[:, :t]
+            assert torch.equal(a, c)
