@@ -83,6 +83,11 @@ class FusedCompressionManager:
                                    self.codec_config.get("nvcomp_algorithm", "ANS"))
         self.packed = self.codec == "bitpack"
         self.stream_codec = "rans" if self.codec == "rans" else "none"
+        # With the entropy coder, codes are stored as 4-bit nibbles (two codes
+        # per coded byte): half the symbols for the coder at the same
+        # compression ratio.  codec_config["symbol_bits"] = 8 keeps byte codes.
+        self.code_width = 4 if (self.stream_codec == "rans" and
+                                int(self.codec_config.get("symbol_bits", 4)) == 4) else None
         self.num_kv_heads = int(num_kv_heads)
         self.head_size = int(head_size)
         self.base_seed = int(base_seed) if transform else None
@@ -106,7 +111,7 @@ class FusedCompressionManager:
             self._plans[layer_id] = K.make_layer_plan(
                 self.num_kv_heads, self.hybrid.key_levels_for(layer_id).tolist(),
                 self.hybrid.value_levels_for(layer_id).tolist(), self.base_seed, layer_id,
-                packed=self.packed)
+                packed=self.packed, code_width=self.code_width)
         return self._plans[layer_id]
 
     def _slots(self, tensors: Sequence[torch.Tensor], plans: Sequence[Any]):
@@ -424,13 +429,15 @@ class FusedCompressionManager:
     # ----------------------------------------------- per-layer overlap API
     def compress_quant_layer(self, kv_layer: torch.Tensor, layer_id: int):
         """Quantize one dense layer ``[2, B, bs, H, D]``; returns
-        (codes u8 ``[2, H, B, bs, D]`` or packed bytes, canon meta)."""
+        (codes ``[2, H, B, bs, 16*bits]`` bytes when every segment has the same
+        code width, else flat bytes; canon meta)."""
         x = kv_layer.contiguous()
         _, B, bs, H, D = x.shape
         batch = self.quantize_paged([x], [layer_id], [(list(range(B)), B * bs)])
         codes = batch.codes[:batch.items.code_bytes]
-        if not self.packed:
-            codes = codes.view(2, H, B, bs, D)
+        widths = set(batch.plans[0].key_bits + batch.plans[0].value_bits)
+        if len(widths) == 1:  # one code width: [2, H, B, bs, 16 * width] bytes
+            codes = codes.view(2, H, B, bs, 16 * widths.pop())
         canon = self.canon_meta(batch.meta, 0, batch.plans[0], B * bs)
         return codes, canon
 

@@ -48,7 +48,8 @@ def _timeit(fn, iters: int, warmup: int = 3) -> float:
 
 def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
         only: tuple[str, ...] = STAGES, engine: int = 0, seed: int = 1,
-        key_levels=(12, 6, 6, 6), value_levels=(8, 4, 4, 4), warmup: int = 3) -> list[dict]:
+        key_levels=(12, 6, 6, 6), value_levels=(8, 4, 4, 4), warmup: int = 3,
+        code_width: int = 8) -> list[dict]:
     from kvserve_hpdps_b200.models.synthetic import paged_workload
     from kvserve_hpdps_b200.ops import kernels as K
     wl = paged_workload(layers, [tokens], heads, device="cuda", seed=seed, fill=False)
@@ -56,7 +57,8 @@ def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
     wl.cache[:, 0, :, :, :, :4].mul_(12.0)  # outlier channels in K
     kl = list(key_levels)[:heads] + [key_levels[-1]] * max(0, heads - len(key_levels))
     vl = list(value_levels)[:heads] + [value_levels[-1]] * max(0, heads - len(value_levels))
-    plans = [K.make_layer_plan(heads, kl, vl, 0x3333, l) for l in range(layers)]
+    cw = code_width if code_width != 8 else None
+    plans = [K.make_layer_plan(heads, kl, vl, 0x3333, l, code_width=cw) for l in range(layers)]
     slots = K.LayerSlots([wl.cache[l] for l in range(layers)], plans)
     items = K.WorkItems(slots, [(l, wl.block_ids[0], tokens) for l in range(layers)])
     dst = torch.zeros_like(wl.cache)
@@ -96,7 +98,7 @@ def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
         row("block_copy", _timeit(copy_all, iters, warmup))
     K.dequantize(codes, meta, dslots, items, engine=engine)
     err = K.kv_error(wl.cache[:, :, wl.block_ids[0]], dst[:, :, wl.block_ids[0]])
-    rows.append({"stage": "summary", "original_bytes": nbytes,
+    rows.append({"stage": "summary", "code_width": code_width, "original_bytes": nbytes,
                  "compressed_bytes": int(stream.numel() + meta.numel()),
                  "compression_ratio": round(nbytes / (stream.numel() + meta.numel()), 3),
                  "rel_mse": err["rel_mse"], "cosine": err["cosine"],
@@ -113,12 +115,15 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--engine", type=int, default=0, help="0 = tcgen05, 1 = SIMT")
     ap.add_argument("--only", default=",".join(STAGES))
+    ap.add_argument("--code-width", type=int, default=8,
+                    help="bits per code in the code buffer (4: two codes per rANS symbol)")
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print(json.dumps({"unavailable": "no CUDA device"}))
         return 0
     for r in run(args.layers, args.tokens, args.heads, args.iters,
-                 tuple(args.only.split(",")), args.engine, warmup=args.warmup):
+                 tuple(args.only.split(",")), args.engine, warmup=args.warmup,
+                 code_width=args.code_width):
         print(json.dumps(r))
     return 0
 

@@ -194,6 +194,10 @@ class LayerPlan:
     signs: Optional[torch.Tensor]            # [H, 128] +-1, or None (identity)
     packed: bool = False                     # fixed-width bit packing of codes
     clamp_top: bool = True
+    # Uniform code width in bits (e.g. 4: two codes per byte, the symbols an
+    # entropy coder sees); heads whose codes do not fit keep 8.  Overrides
+    # ``packed``'s per-head minimal widths.
+    code_width: Optional[int] = None
     group_of_head: list[int] = field(default_factory=list)
     groups: list[list[int]] = field(default_factory=list)
     key_bits: list[int] = field(default_factory=list)
@@ -219,6 +223,16 @@ class LayerPlan:
         else:
             G = max(self.group_of_head) + 1
             self.groups = [[h for h in range(H) if self.group_of_head[h] == g] for g in range(G)]
+        if self.code_width:
+            top = 0 if self.clamp_top else 1  # largest code is levels-1 (+1 unclamped)
+
+            def width(levels: float) -> int:
+                return self.code_width if float(levels) - 1 + top < 2 ** self.code_width else 8
+            if not self.key_bits:
+                self.key_bits = [width(v) for v in self.key_levels]
+            if not self.value_bits:
+                self.value_bits = [width(v) for v in self.value_levels]
+            self.packed = any(b != 8 for b in self.key_bits + self.value_bits)
         if not self.key_bits:
             self.key_bits = [code_bits(v, self.packed) for v in self.key_levels]
         if not self.value_bits:
@@ -276,10 +290,11 @@ def _signs_cached(layer_id: int, num_heads: int, seed: int) -> torch.Tensor:
 
 
 def make_layer_plan(num_heads: int, key_levels, value_levels, seed: Optional[int], layer_id: int,
-                    packed: bool = False, clamp_top: bool = True) -> LayerPlan:
+                    packed: bool = False, clamp_top: bool = True,
+                    code_width: Optional[int] = None) -> LayerPlan:
     signs = None if seed is None else _signs_cached(int(layer_id), int(num_heads), int(seed))
     return LayerPlan(num_heads, [float(x) for x in key_levels], [float(x) for x in value_levels],
-                     signs, packed=packed, clamp_top=clamp_top)
+                     signs, packed=packed, clamp_top=clamp_top, code_width=code_width)
 
 
 def decode_plan(num_heads: int, group_of_head: Sequence[int], key_bits: Sequence[int],
