@@ -36,6 +36,84 @@ KVS_DEV uint4 load_syms(const uint8_t* src, uint32_t ss, int lane, uint32_t n_sy
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+
+// Warp-parallel form of normalize_counts (rans.cuh) with identical integer
+// results: lanes compute the scaled frequencies of symbols lane, lane+32,
+// ...; the sum and the first symbol with the largest count are reduced
+// across the warp; lane 0 applies the (rare, short) correction loop.
+KVS_DEV void normalize_counts_warp(const uint32_t* cnt, uint32_t A, uint64_t total, uint32_t* freq,
+                                   int lane) {
+  uint32_t sum = 0, best = 0xFFFFFFFFu, best_cnt = 0;
+  for (uint32_t s = lane; s < A; s += 32) {
+    uint32_t f = 0;
+    const uint32_t c = cnt[s];
+    if (c > 0) {
+      f = static_cast<uint32_t>((static_cast<uint64_t>(c) * kProbScale) / total);
+      if (f < 1) f = 1;
+      if (c > best_cnt) {
+        best_cnt = c;
+        best = s;
+      }
+    }
+    freq[s] = f;
+    sum += f;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    const uint32_t oc = __shfl_xor_sync(0xFFFFFFFFu, best_cnt, o);
+    const uint32_t ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    if (oc > best_cnt || (oc == best_cnt && ob < best)) {
+      best_cnt = oc;
+      best = ob;
+    }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    int64_t diff = static_cast<int64_t>(kProbScale) - static_cast<int64_t>(sum);
+    while (diff != 0) {
+      if (diff > 0) {
+        freq[best] += static_cast<uint32_t>(diff);
+        diff = 0;
+      } else {
+        uint32_t s_max = 0, f_max = 0;
+        for (uint32_t s = 0; s < A; ++s)
+          if (freq[s] > f_max) {
+            f_max = freq[s];
+            s_max = s;
+          }
+        int64_t take = -diff;
+        if (take > static_cast<int64_t>(f_max) - 1) take = static_cast<int64_t>(f_max) - 1;
+        freq[s_max] -= static_cast<uint32_t>(take);
+        diff += take;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// Encoder table from frequencies: lane l owns the contiguous symbols
+// [l*per, (l+1)*per); cumulative frequencies come from a warp scan.
+KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncSym* enc, int lane) {
+  const uint32_t per = (A + 31) / 32;
+  const uint32_t b = lane * per, e = min(A, b + per);
+  uint32_t local = 0;
+  for (uint32_t s = b; s < e; ++s) local += freq[s];
+  uint32_t incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  uint32_t cum = incl - local;
+  for (uint32_t s = b; s < e; ++s) {
+    const uint32_t f = freq[s];
+    if (f > 0) enc[s] = make_enc(f, cum);
+    cum += f;
+  }
+  __syncwarp();
+}
+
 __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
     const uint8_t* __restrict__ in, uint64_t n, uint32_t cs, uint8_t* __restrict__ staging,
     uint32_t* __restrict__ rec_off, uint32_t* __restrict__ rec_len, uint32_t n_chunks) {
@@ -58,8 +136,11 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
   // Histogram in four lane-interleaved copies (lane & 3): spreads the
   // atomic traffic of skewed symbol distributions over four addresses.
   uint32_t* hc = h + (lane & 3) * 256;
+  // the next super-step's symbols are loaded while this one is counted
+  uint4 nxt = load_syms(src, 0, lane, n_sym);
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
-    const uint4 v = load_syms(src, ss, lane, n_sym);
+    const uint4 v = nxt;
+    if (ss + 1 < n_ss) nxt = load_syms(src, ss + 1, lane, n_sym);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 16; ++i) atomicAdd(&hc[(w[i >> 2] >> ((i & 3) * 8)) & 0xFF], 1u);
@@ -76,16 +157,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
   for (int o = 16; o > 0; o >>= 1) top = max(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
   const uint32_t A = static_cast<uint32_t>(top + 1);
   __syncwarp();
-  if (lane == 0) {
-    normalize_counts(h, A, static_cast<uint64_t>(n_ss) * kSuper, freq_s[warp]);
-    uint32_t cum = 0;
-    for (uint32_t s = 0; s < A; ++s) {
-      const uint32_t f = freq_s[warp][s];
-      if (f > 0) enc[warp][s] = make_enc(f, cum);
-      cum += f;
-    }
-  }
-  __syncwarp();
+  normalize_counts_warp(h, A, static_cast<uint64_t>(n_ss) * kSuper, freq_s[warp], lane);
+  build_enc_warp(freq_s[warp], A, enc[warp], lane);
 
   uint16_t* words = reinterpret_cast<uint16_t*>(slot);
   const int64_t cap = static_cast<int64_t>(sb / 2);
@@ -95,12 +168,14 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
   uint32_t x = kStateLow;
   bool overflow = false;
   const uint32_t lt = lanemask_lt();
+  uint4 pre = load_syms(src, n_ss - 1, lane, n_sym);  // prefetched one super-step ahead
   for (int ss = static_cast<int>(n_ss) - 1; ss >= 0; --ss) {
     if (wpos - kSuper - 8 < min_w) {
       overflow = true;
       break;
     }
-    const uint4 v = load_syms(src, ss, lane, n_sym);
+    const uint4 v = pre;
+    if (ss > 0) pre = load_syms(src, ss - 1, lane, n_sym);
     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int m = kSub - 1; m >= 0; --m) {
@@ -274,13 +349,20 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const uint32_t lt = lanemask_lt();
   __syncwarp();
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
+    // Keep >= 1024 words ahead of the read pointer with asynchronous 16-byte
+    // copies (one group per 256 words); a super-step reads at most 512
+    // words, so every group except the newest must have landed.
     while (loaded < rptr + 1024 && loaded < total_words) {
       const uint32_t idx = loaded + lane * 8;
       if (idx < total_words)
-        *reinterpret_cast<uint4*>(ring + (idx & (kRing - 1))) =
-            *reinterpret_cast<const uint4*>(words + idx);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         smem_u32(ring + (idx & (kRing - 1)))),
+                     "l"(words + idx)
+                     : "memory");
+      asm volatile("cp.async.commit_group;" ::: "memory");
       loaded += 256;
     }
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncwarp();
     uint32_t o[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -303,6 +385,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
         if (off + i < ch.n_sym) dst[off + i] = static_cast<uint8_t>(o[i >> 2] >> ((i & 3) * 8));
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (x != kStateLow || rptr != total_words) record_error(err, ERR_CORRUPT);
 }
 
