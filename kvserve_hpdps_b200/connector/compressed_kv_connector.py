@@ -224,10 +224,12 @@ class CompressedKVConnector(KVConnectorBase_V1):
             return None
         if self._compressor is None:
             from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter
+            bw = getattr(self._transport, "bandwidth_mbps", None) if self.is_producer else None
             self._compressor = KVCompressionAdapter(
                 self._compression_cfg, self._num_kv_heads, self._head_size,
                 model_name=self._model_name, tp_rank=self._tp_rank, tp_size=self._tp_size,
-                num_layers=self._num_layers or None)
+                num_layers=self._num_layers or None,
+                bandwidth_fn=bw)  # controller mode: device-timed link bandwidth
         return self._compressor
 
     @classmethod

@@ -256,6 +256,42 @@ class P2PTransport:
             self._pending.append((done, request_id, member_tids, sum(sizes), t0))
             self._pending_cv.notify_all()
 
+    def bandwidth_mbps(self, probe_bytes: int = 64 << 20, max_age_s: float = 30.0,
+                       timeout_s: float = 5.0) -> Optional[float]:
+        """Device-timed push bandwidth to the consumer in MB/s (1 MB = 2^20
+        bytes): ``probe_bytes`` are stored into a temporarily reserved part of
+        the consumer's ring by the probe kernel, timed between the first CTA's
+        start and the last CTA's end (globaltimer), with no host round trip in
+        the measured interval.  Cached for ``max_age_s``; None when ring space
+        is not available within ``timeout_s``."""
+        assert self.is_sender
+        now = time.monotonic()
+        cached = getattr(self, "_bw_cache", None)
+        if cached is not None and now - cached[1] < max_age_s:
+            return cached[0]
+        from kvserve_hpdps_b200.ops import kernels as K
+        n = _align(int(probe_bytes))
+        base = self._alloc.alloc(n, timeout_s)
+        if base is None:
+            return cached[0] if cached else None
+        try:
+            with torch.cuda.device(self.device), torch.cuda.stream(self._stream):
+                src = getattr(self, "_probe_src", None)
+                if src is None or src.numel() < n:
+                    src = torch.zeros(n, dtype=torch.uint8, device=self.device)
+                    self._probe_src = src
+                stamps = torch.tensor([2 ** 63 - 1, 0], dtype=torch.int64, device=self.device)
+                K.probe_push(src, self._peer.ptr + base, n, stamps)
+                self._stream.synchronize()
+                t0, t1 = stamps.tolist()
+        finally:
+            self._alloc.release(base, n)
+        if t1 <= t0:
+            return cached[0] if cached else None
+        mbps = n / (1 << 20) / ((t1 - t0) * 1e-9)
+        self._bw_cache = (mbps, now)
+        return mbps
+
     def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
         assert self.is_sender
         self._put(request_id, layer_names, [stacked_kv.to(self.device).contiguous()], 1, None,

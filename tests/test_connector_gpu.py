@@ -110,6 +110,10 @@ def _role(producer, port, compression, q):
             conn.wait_for_save()
             conn._transport.wait_for_sent(30)
             torch.cuda.synchronize()
+            # device-timed NVLink push bandwidth (feeds the controller)
+            bw = conn._transport.bandwidth_mbps(probe_bytes=32 << 20)
+            if bw is None or not 1e4 < bw < 2e6:
+                raise RuntimeError(f"implausible probe bandwidth {bw} MB/s")
             time.sleep(2.0)
             q.put(("p", "ok"))
         else:
