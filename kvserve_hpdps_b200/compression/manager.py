@@ -159,7 +159,13 @@ class KVCompressionAdapter:
     def _get_cached_manager(self, cfg: dict):
         key = _cfg_key(cfg)
         if key not in self._manager_cache:
-            self._manager_cache[key] = self._build(copy.deepcopy(cfg))
+            c = copy.deepcopy(cfg)
+            # profiles from a library name no model: use the served model's
+            # head-score table, as custom specs do
+            if self._model_name and "quantizer_config" in c and \
+                    not c["quantizer_config"].get("model_name"):
+                c["quantizer_config"]["model_name"] = self._model_name
+            self._manager_cache[key] = self._build(c)
         return self._manager_cache[key]
 
     @property

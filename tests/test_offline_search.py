@@ -99,3 +99,44 @@ def test_library_export_selection(tmp_path):
     V = 470e6
     prof, ctx = ctl.select_profile(V, 150.0, 10.0, 1e9, 0.96)
     assert prof is not None and prof.compression_ratio == 6.0, ctx
+
+
+def test_adapter_controller_mode_end_to_end(tmp_path):
+    """Library from the exporter -> adapter in controller mode: the selected
+    profile depends on the measured bandwidth, the payload round-trips, the
+    bandit learns from the observed latency, and fast links send raw KV."""
+    from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter
+
+    def spec(cfg):
+        return {"enabled": True, "pipeline": ["transformer", "quantizer", "codec"],
+                "transformer_config": {"transform_type": "hadamard", "seed": 0x3333},
+                "quantizer_config": dict(cfg), "codec_config": {"codec_type": "rans"},
+                "backend": "generic", "min_compress_size": 0}
+    evals = []
+    for c, acc, cr in [(Candidate(0.0, 16, 16, 8, 6), 0.995, 3.5),
+                       (Candidate(0.8, 12, 8, 6, 4), 0.97, 6.0)]:
+        evals.append({"candidate": c.key(), "config": c.quantizer_config(), "accuracy": acc,
+                      "compression_ratio": cr, "harmonic_speed_mbps": 30000.0})
+    path = tmp_path / "lib.json"
+    write_library(str(path), build_library(evals, "Qwen2.5-7B-Instruct", spec_builder=spec))
+    service = {"bandwidth_mbps": 1e9, "slo_ms": 1e9, "accuracy_requirement": 0.96,
+               "t_model_ms": 0.0}
+    bw = {"v": 150.0}
+    ad = KVCompressionAdapter({"mode": "controller", "library_path": str(path), "epsilon": 0.0,
+                               "service_config": service}, 4, 128,
+                              model_name="Qwen2.5-7B-Instruct", num_layers=28,
+                              bandwidth_fn=lambda: bw["v"])
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((2, 2, 64, 4 * 128), generator=g).to(torch.bfloat16)
+    cd = ad.compress(x, "r1")
+    assert cd is not None
+    assert cd.metadata["ctrl_profile_id"] == Candidate(0.8, 12, 8, 6, 4).key()
+    out = ad.decompress(cd)
+    assert out.shape == x.shape
+    cos = torch.nn.functional.cosine_similarity(out.float().flatten(), x.float().flatten(), dim=0)
+    assert float(cos) > 0.9
+    ad.update_controller("r1", 12.5)
+    st = ad.get_controller_stats()
+    assert st["total_decisions"] == 1 and st["bandit_states"] == 1
+    bw["v"] = 1e9  # a link faster than any profile's codec: send raw KV
+    assert ad.compress(x, "r2") is None
