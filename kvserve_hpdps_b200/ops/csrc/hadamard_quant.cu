@@ -24,7 +24,8 @@
 //    with the Rademacher signs folded in, the epilogue reads the accumulator
 //    back with tcgen05.ld; each CTA pipelines a contiguous range of tiles;
 //    (k_stats_ws / k_quant_ws are warp-specialized: a control warp issues
-//    loads and MMAs, two epilogue groups of 8 warps alternate jobs);
+//    loads and MMAs, two epilogue groups of 8 warps alternate jobs;
+//    k_dequant_ws: unpack warps, a control warp and epilogue warps);
 //  * engine 3: the persistent kernels without warp specialization (k_*_tc);
 //  * engine 2: the same math with one CTA per tile (k_*_mma);
 //  * engine 1: thread-per-row loads and an in-register fp32 butterfly.
@@ -1908,6 +1909,248 @@ __global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
+
+// ------------------------------------------------------- dequant (ws)
+// Warp-specialized dequantize + inverse transform + paged store.  Warps
+// 0-7 unpack codes into one of two A tiles, warp 16 issues the MMAs into one
+// of two TMEM accumulators, warps 8-15 convert the accumulator to bf16 into
+// one of two output tiles and issue the TMA stores.  Unpack of job k+1, the
+// MMA of job k and the epilogue and store of job k-1 overlap.  Barriers
+// (job k uses buffers b = k & 1, use index u = k >> 1):
+//   afull[b]   8 unpack-warp arrivals: A tile b holds job k;
+//   afree[b]   tcgen05.commit after MMA k: A tile b and the image are free;
+//   dmma[b]    tcgen05.commit after MMA k: accumulator b holds job k;
+//   accfree[b] 8 epilogue-warp arrivals: accumulator b has been read.
+constexpr int kDqOffA = 32768;
+constexpr int kDqOffO = kDqOffA + 2 * 32768;
+constexpr int kDqOffBars = kDqOffO + 2 * 32768;
+constexpr int kDqOffKp = kDqOffBars + 256;
+constexpr int kDqSmem = kDqOffKp + 128 * 4 * 4 + 1024;
+static_assert(kDqSmem <= 227 * 1024, "dequant ws shared memory");
+
+__global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* img = base;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kDqOffBars);
+  uint64_t* afull = bars;        // [2]
+  uint64_t* afree = bars + 2;    // [2]
+  uint64_t* dmma = bars + 4;     // [2]
+  uint64_t* accfree = bars + 6;  // [2]
+  uint64_t* imgb = bars + 8;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 9);
+  float* kp = reinterpret_cast<float*>(base + kDqOffKp);  // [128][4] key (min, scale, -2^23*scale, 0)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = L.num_heads;
+  const WsMap M = ws_map(L);
+  const int n = M.n;
+  if (n <= 0) return;
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&afull[b], kWsGroupWarps);
+      mbar_init(&afree[b], 1);
+      mbar_init(&dmma[b], 1);
+      mbar_init(&accfree[b], kWsGroupWarps);
+    }
+    mbar_init(imgb, 1);
+    fence_mbar_init();
+  }
+  if (warp == kWsCtrlWarp) tmem_alloc(tslot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  auto abuf = [&](int b) { return base + kDqOffA + 32768 * b; };
+  auto obuf = [&](int b) { return base + kDqOffO + 32768 * b; };
+
+  if (warp < kWsGroupWarps) {
+    // ------------------------------------------------------------ unpack
+    ItemCursor cur;
+    cursor_init(cur);
+    int kp_key = -1;
+    for (int k = 0; k < n; ++k) {
+      const int b = k & 1;
+      const PJob jb = ws_job(M, k);
+      cursor_seek(L, cur, jb.tile);
+      const ItemCtx& c = cur.c;
+      if (k >= 2)  // MMA k-2 finished reading A tile b
+        mbar_wait(&afree[b], static_cast<uint32_t>(((k >> 1) - 1) & 1), L.err, ERR_MBAR_TIMEOUT);
+      group_sync(0);  // every unpack thread finished job k-1 (kp may change)
+      const int pk = c.r * H + jb.h;
+      if (jb.plane == 0 && pk != kp_key) {
+        if (tid < 128) {
+          const __half* m = meta_base(L, c.r);
+          const float mn = bf16_round(__half2float(m[jb.h * 128 + tid]));
+          const float sc = bf16_round(__half2float(m[c.lp->H * 128 + jb.h * 128 + tid]));
+          *reinterpret_cast<float4*>(kp + 4 * tid) = make_float4(mn, sc, -8388608.0f * sc, 0.f);
+        }
+        kp_key = pk;
+        group_sync(0);  // key parameters visible
+      }
+      uint8_t* sA = abuf(b);
+      const int bits = seg_bits(c, jb.plane, jb.h);
+      const int nrows = min(kTileRows, c.rows - c.row0);
+      const uint8_t* src0 = code_row(L, c, jb.plane, jb.h, c.row0);
+      const __half* meta = meta_base(L, c.r);
+      const int Hh = c.lp->H, G = c.lp->n_groups, grp = c.lp->group_of_head[jb.h];
+      for (int g = tid; g < kTileRows * 4; g += kWsGroupThreads) {
+        const int t = g & (kTileRows - 1), part = g >> 7;
+        const int row = c.row0 + t;
+        if (t < nrows && row < c.ntok) {
+          float vmn = 0.f, vsc = 0.f;
+          if (jb.plane == 1) {
+            vmn = bf16_round(__half2float(meta[2 * Hh * 128 + grp * c.rows + row]));
+            vsc = bf16_round(__half2float(meta[2 * Hh * 128 + G * c.rows + grp * c.rows + row]));
+          }
+          const uint8_t* src = src0 + static_cast<long long>(t) * 16 * bits + part * 4 * bits;
+          switch (bits) {
+            case 1: p_unpack_group<1>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 2: p_unpack_group<2>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 3: p_unpack_group<3>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 4: p_unpack_group<4>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 5: p_unpack_group<5>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 6: p_unpack_group<6>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 7: p_unpack_group<7>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            default: p_unpack_group<8>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+          }
+        } else {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8)
+            *reinterpret_cast<uint4*>(sA + sw128_offset(t, part * 32 + c8 * 8)) =
+                make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();  // generic writes of A tile b before the MMA reads it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[b]);
+    }
+  } else if (warp < kWsCtrlWarp) {
+    // ---------------------------------------------------------- epilogue
+    const int ew = warp - kWsGroupWarps, etid = tid - kWsGroupThreads;
+    const int quad = ew & 3, half = ew >> 2;
+    const int lane_id = quad * 32 + lane;
+    ItemCursor cur;
+    cursor_init(cur);
+    for (int k = 0; k < n; ++k) {
+      const int b = k & 1;
+      const PJob jb = ws_job(M, k);
+      cursor_seek(L, cur, jb.tile);
+      const ItemCtx& c = cur.c;
+      if (etid == 0)  // the store that read output tile b (job k-2) has finished reading
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      group_sync(1);
+      mbar_wait(&dmma[b], static_cast<uint32_t>((k >> 1) & 1), L.err, ERR_MBAR_TIMEOUT);
+      tc_fence_after();
+      uint8_t* sO = obuf(b);
+      const uint32_t taddr = tmem + static_cast<uint32_t>(b * 128) +
+                             (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+      const float sc = c.lp->out_scale;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float v[32];
+        tmem_ld32(taddr + cc * 32, v);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            w[p] = cvt_bf16x2(v[8 * q4 + 2 * p] * sc, v[8 * q4 + 2 * p + 1] * sc);
+          *reinterpret_cast<uint4*>(sO + sw128_offset(lane_id, half * 64 + cc * 32 + q4 * 8)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accfree[b]);
+      fence_proxy_async_smem();  // generic writes of output tile b before the TMA store
+      group_sync(1);
+      if (etid == 0) {
+        const CUtensorMap* map = map_of(L, c.slot, jb.plane);
+        const int nst = min(kTileRows, c.ntok - c.row0);  // rows holding tokens
+        for (int g = 0; g < 8; ++g) {
+          const int rr = c.row0 + g * 16;
+          if (g * 16 >= nst) break;
+          const int phys = phys_block(L, c, rr);
+          const int slot = rr % c.kv.block_size;
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            asm volatile(
+                "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
+                    "l"(reinterpret_cast<uint64_t>(map)),
+                "r"(hb * 64), "r"(tma_y(c.kv, jb.h, slot)), "r"(tma_z(c.kv, jb.h, slot)),
+                "r"(phys), "r"(smem_u32(sO + hb * 16384 + g * 2048))
+                : "memory");
+          }
+        }
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+    }
+    if (etid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  } else {
+    // ----------------------------------------------------------- control
+    ItemCursor cur;
+    cursor_init(cur);
+    int cur_img = -1;
+    uint32_t img_phase = 0;
+    bool ok = true;
+    auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
+      bool r = true;
+      if (lane == 0) r = mbar_wait(bar, parity, L.err, ERR_MBAR_TIMEOUT);
+      return __shfl_sync(0xFFFFFFFFu, r ? 1 : 0, 0) != 0;
+    };
+    auto prefetch = [&](int k) {  // the code region of job k into L2
+      ItemCursor pc = cur;
+      const PJob jn = ws_job(M, k);
+      cursor_seek(L, pc, jn.tile);
+      const ItemCtx& c = pc.c;
+      const int nrows = min(kTileRows, c.rows - c.row0);
+      const uint32_t bytes = static_cast<uint32_t>(nrows * 16 * seg_bits(c, jn.plane, jn.h));
+      if (lane == 0)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                         code_row(L, c, jn.plane, jn.h, c.row0)),
+                     "r"(bytes)
+                     : "memory");
+    };
+    for (int k = 0; k < 3 && k < n; ++k) prefetch(k);
+    for (int k = 0; k < n; ++k) {
+      const int b = k & 1;
+      const PJob jb = ws_job(M, k);
+      cursor_seek(L, cur, jb.tile);
+      if (k + 3 < n) prefetch(k + 3);
+      const int img_key = cur.c.slot * H + jb.h;
+      if (ok && img_key != cur_img) {
+        if (k >= 1)  // MMA k-1 finished reading the old image
+          ok = wait0(&afree[(k - 1) & 1], static_cast<uint32_t>(((k - 1) >> 1) & 1));
+        if (ok) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(imgb, 32768u);
+            bulk_load(img, bmat_of(L, cur.c.slot, jb.h), 32768, imgb);
+          }
+          ok = wait0(imgb, img_phase);
+          img_phase ^= 1u;
+        }
+        cur_img = img_key;
+      }
+      if (ok) ok = wait0(&afull[b], static_cast<uint32_t>((k >> 1) & 1));
+      if (ok && k >= 2) ok = wait0(&accfree[b], static_cast<uint32_t>(((k >> 1) - 1) & 1));
+      if (lane == 0) {
+        if (ok) {
+          tc_fence_after();
+          // D[t][k] = sum_n Y[t][n] Bi[k][n]
+          umma_tile_128x128x128(tmem + static_cast<uint32_t>(b * 128), smem_u32(abuf(b)),
+                                smem_u32(img));
+        }
+        umma_commit(&dmma[b]);
+        umma_commit(&afree[b]);
+      }
+      __syncwarp();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWsCtrlWarp) tmem_dealloc(tmem, 256);
+}
+
 __global__ void k_init_key_stats(uint32_t* kstat, long long n_pairs) {
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n_pairs;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -2064,7 +2307,10 @@ int kvs_dequant_inverse(const LayerLaunch* Lp) {
   if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
-  if (L.engine == 0 || L.engine == 3) {
+  if (L.engine == 0) {
+    if (int rc = set_smem(k_dequant_ws, kDqSmem)) return rc;
+    k_dequant_ws<<<ws_grid(L), kWsThreads, kDqSmem, s>>>(L);
+  } else if (L.engine == 3) {
     if (int rc = set_smem(k_dequant_tc, kPSmem)) return rc;
     k_dequant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
   } else if (L.engine == 2) {
