@@ -175,6 +175,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._expected_msgs: dict[str, int] = {}
         self._rid2tid: dict[str, str] = {}
         self._pending_send_rids: set[str] = set()
+        self._err_monitor = None
         if role == KVConnectorRole.WORKER:
             self._init_worker(cfg)
 
@@ -379,6 +380,17 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     break
                 time.sleep(0.002)
                 self._drain()
+        if torch.cuda.is_available() and meta.requests:
+            # device-side failures of earlier loads (flag timeouts, checksum
+            # mismatches, corrupt streams), read without waiting on the GPU
+            if self._err_monitor is None:
+                from kvserve_hpdps_b200.ops import kernels as K
+                self._err_monitor = K.ErrorMonitor(torch.device("cuda", torch.cuda.current_device()))
+            code = self._err_monitor.poll()
+            if code:
+                from kvserve_hpdps_b200.ops import kernels as K
+                logger.error("device error %d (%s) while loading KV in an earlier step", code,
+                             K.ERR_NAMES.get(code, "?"))
         timeline("D load_exit")
 
     def _drain(self) -> None:

@@ -78,6 +78,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_cpu_rans_decode": ([P, c_uint64, P, c_uint64], c_int),
         "kvs_cpu_bitpack": ([P, c_uint64, c_int, P], None),
         "kvs_cpu_bitunpack": ([P, c_uint64, c_int, P], None),
+        "kvs_checksum": ([P, c_int, P, c_int, P], c_int),
+        "kvs_checksum_verify": ([P, c_int, P, P, P, c_int, P], c_int),
         "kvs_block_copy": ([POINTER(PagedKV), P, c_int, c_longlong, P, c_int, P, P, c_uint32, P],
                            c_int),
         "kvs_copy16": ([P, P, c_longlong, P, P, c_uint32, c_int, P], c_int),

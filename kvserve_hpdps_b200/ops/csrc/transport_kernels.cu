@@ -147,6 +147,64 @@ __global__ void __launch_bounds__(512) k_probe_push(const uint4* __restrict__ sr
   }
 }
 
+
+// Message checksum: over the bytes b_p of a message (p = offset inside the
+// message), S1 = sum_p b_p * 2^(8*(p%4)) and S2 = sum_p (p/4 + 1) * b_p *
+// 2^(8*(p%4)), both mod 2^64 -- i.e. the plain and the position-weighted sums
+// of the message's little-endian 32-bit words.  Integer sums are
+// order-independent, so any grid computes the same value.  A segment is
+// (src, message offset, bytes).
+struct CkSeg {
+  const uint8_t* src;
+  long long off;
+  long long bytes;
+};
+
+KVS_DEV void ck_byte(uint8_t b, long long p, unsigned long long& s1, unsigned long long& s2) {
+  const unsigned long long v = static_cast<unsigned long long>(b) << (8 * (p & 3));
+  s1 += v;
+  s2 += static_cast<unsigned long long>((p >> 2) + 1) * v;
+}
+
+__global__ void __launch_bounds__(256) k_checksum(const CkSeg* __restrict__ segs,
+                                                  unsigned long long* out) {
+  const CkSeg sg = segs[blockIdx.y];
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  unsigned long long s1 = 0, s2 = 0;
+  if (((reinterpret_cast<uintptr_t>(sg.src) | static_cast<uintptr_t>(sg.off)) & 15) == 0) {
+    const long long n16 = sg.bytes / 16;
+    for (long long i = tid; i < n16; i += stride) {
+      const uint4 v = reinterpret_cast<const uint4*>(sg.src)[i];
+      const unsigned long long w = static_cast<unsigned long long>((sg.off >> 2) + 4 * i + 1);
+      s1 += static_cast<unsigned long long>(v.x) + v.y + v.z + v.w;
+      s2 += w * v.x + (w + 1) * v.y + (w + 2) * v.z + (w + 3) * v.w;
+    }
+    for (long long i = n16 * 16 + tid; i < sg.bytes; i += stride) ck_byte(sg.src[i], sg.off + i, s1, s2);
+  } else {
+    for (long long i = tid; i < sg.bytes; i += stride) ck_byte(sg.src[i], sg.off + i, s1, s2);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, o);
+    s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+  }
+  if ((threadIdx.x & 31) == 0 && (s1 | s2)) {
+    atomicAdd(out, s1);
+    atomicAdd(out + 1, s2);
+  }
+}
+
+__global__ void k_zero2(unsigned long long* p) {
+  if (threadIdx.x < 2) p[threadIdx.x] = 0;
+}
+
+__global__ void k_checksum_compare(const unsigned long long* got,
+                                   const unsigned long long* expected, uint32_t* err) {
+  if (threadIdx.x == 0 && (got[0] != expected[0] || got[1] != expected[1]))
+    record_error(err, ERR_CORRUPT);
+}
+
 }  // namespace kvs
 
 using namespace kvs;
@@ -176,6 +234,27 @@ int kvs_copy16(const void* src, void* dst, long long bytes, uint32_t* counter, u
 }
 
 // segs: device array of n CopySeg {src, dst, bytes}.
+
+// Checksum of `n` segments (device array of CkSeg) into out[2] (device).
+int kvs_checksum(const void* segs, int n, unsigned long long* out, int blocks_per_seg,
+                 void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  k_zero2<<<1, 32, 0, s>>>(out);
+  if (n > 0)
+    k_checksum<<<dim3(blocks_per_seg, n), 256, 0, s>>>(static_cast<const CkSeg*>(segs), out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Recompute the checksum of `segs` into scratch[2] and record ERR_CORRUPT in
+// *err when it differs from expected[2] (all device memory; no host wait).
+int kvs_checksum_verify(const void* segs, int n, const unsigned long long* expected,
+                        unsigned long long* scratch, uint32_t* err, int blocks_per_seg,
+                        void* stream) {
+  if (int rc = kvs_checksum(segs, n, scratch, blocks_per_seg, stream)) return rc;
+  k_checksum_compare<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(scratch, expected, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 int kvs_copy_segments(const void* segs, int n, int blocks_per_seg, uint32_t* counter,
                       uint32_t* flag, uint32_t flag_value, void* stream) {
   if (n <= 0) return 0;

@@ -111,6 +111,35 @@ def read_device_error(device: torch.device, reset: bool = True) -> int:
     return code
 
 
+class ErrorMonitor:
+    """Non-blocking watch of a device's error word for serving loops.
+
+    ``poll()`` returns the code seen by the previous poll once that poll's
+    asynchronous copy has landed (0 while it is in flight or when no error
+    was recorded), then schedules a new copy of the word into pinned host
+    memory on the current stream followed by clearing the word, so kernels
+    that fail between two polls are reported at the second one without the
+    host ever waiting on the device."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self._host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._event: Optional[torch.cuda.Event] = None
+
+    def poll(self) -> int:
+        code = 0
+        if self._event is not None:
+            if not self._event.query():
+                return 0
+            code = int(self._host[0])
+        ws = workspace(self.device)
+        self._host.copy_(ws.err[:1], non_blocking=True)
+        ws.err.zero_()
+        self._event = torch.cuda.current_stream(self.device).record_event()
+        _xfer["d2h"] += 4
+        return code
+
+
 def check_device_error(device: torch.device, what: str = "kernel") -> None:
     code = read_device_error(device)
     if code:
@@ -786,6 +815,40 @@ def copy_segments(segments: Sequence[tuple[int, int, int]], device: torch.device
                                   flag_ptr, flag_value, _stream(device)), "copy_segments")
     # dev_segs may be freed now: the caching allocator only reuses its block
     # for work ordered after this launch on the same stream.
+
+
+def _ck_segments(segments: Sequence[tuple[int, int, int]], device: torch.device) -> torch.Tensor:
+    host = torch.tensor([v for s in segments for v in s] or [0, 0, 0], dtype=torch.int64)
+    if device.type == "cuda":
+        host = host.pin_memory()
+        _xfer["h2d"] += host.numel() * 8
+    return host.to(device, non_blocking=True)
+
+
+def checksum(segments: Sequence[tuple[int, int, int]], out: torch.Tensor,
+             blocks_per_seg: int = 16) -> None:
+    """Message checksum of (src_ptr, message_offset, nbytes) segments into
+    ``out`` (int64[2] on the device): the plain and the position-weighted
+    sums of the message's little-endian 32-bit words, mod 2^64."""
+    segs = [s for s in segments if s[2] > 0]
+    dev = out.device
+    d = _ck_segments(segs, dev)
+    check(lib().kvs_checksum(d.data_ptr(), len(segs), out.data_ptr(), blocks_per_seg,
+                             _stream(dev)), "checksum")
+
+
+def verify_checksum(segments: Sequence[tuple[int, int, int]], expected_ptr: int,
+                    device: torch.device, blocks_per_seg: int = 16) -> None:
+    """Recompute the checksum of ``segments`` on ``device`` and record
+    ERR_CORRUPT in the device error word when it differs from the int64[2]
+    at ``expected_ptr`` (device memory).  Nothing waits on the host."""
+    segs = [s for s in segments if s[2] > 0]
+    d = _ck_segments(segs, device)
+    ws = workspace(device)
+    scratch = torch.empty(2, dtype=torch.int64, device=device)  # stream-ordered reuse
+    check(lib().kvs_checksum_verify(d.data_ptr(), len(segs), expected_ptr, scratch.data_ptr(),
+                                    ws.err.data_ptr(), blocks_per_seg, _stream(device)),
+          "checksum_verify")
 
 
 def wait_flag(flag_ptr: int, expected: int, device: torch.device, timeout_s: float = 2.0,

@@ -221,7 +221,8 @@ class P2PTransport:
         for s in sizes:
             offs.append(total)
             total += _align(s)
-        total = max(total, ALIGN)
+        trailer = total           # 16-byte message checksum after the payload
+        total = total + ALIGN
         with self._lock:
             wait_slots = self._inflight_msgs >= self.n_flags - 1
         if wait_slots:
@@ -239,11 +240,14 @@ class P2PTransport:
         t0 = time.monotonic()
         with torch.cuda.stream(self._stream):
             self._stream.wait_event(ready)
+            ck = torch.empty(2, dtype=torch.int64, device=self.device)
+            K.checksum([(t.data_ptr(), o, s) for t, o, s in zip(tensors, offs, sizes)], ck)
             segs = [(t.data_ptr(), self._peer.ptr + base + o, s)
                     for t, o, s in zip(tensors, offs, sizes)]
+            segs.append((ck.data_ptr(), self._peer.ptr + base + trailer, 16))
             K.copy_segments(segs, self.device, flag_ptr=self._peer.ptr + self.flag_off +
                             slot * FLAG_STRIDE, flag_value=seq & 0xFFFFFFFF)
-            for t in tensors:
+            for t in tensors + [ck]:
                 t.record_stream(self._stream)
             done = self._stream.record_event()
         self._outbox.put({
@@ -251,7 +255,7 @@ class P2PTransport:
             "layer_names": list(layer_names), "meta": meta, "n_body": n_body,
             "specs": [{"shape": list(t.shape), "dtype": str(t.dtype).replace("torch.", ""),
                        "off": base + o, "nbytes": s} for t, o, s in zip(tensors, offs, sizes)],
-            "region": [base, total], "slot": slot, "seq": seq})
+            "region": [base, total], "slot": slot, "seq": seq, "trailer": base + trailer})
         with self._pending_cv:
             self._pending.append((done, request_id, member_tids, sum(sizes), t0))
             self._pending_cv.notify_all()
@@ -349,7 +353,9 @@ class P2PTransport:
     def _on_put(self, msg: dict) -> None:
         views = [tensor_view(self._region.ptr + s["off"], s["nbytes"], getattr(torch, s["dtype"]),
                              s["shape"], self.local_rank) for s in msg["specs"]]
-        ring = {"slot": msg["slot"], "seq": msg["seq"], "region": tuple(msg["region"])}
+        ring = {"slot": msg["slot"], "seq": msg["seq"], "region": tuple(msg["region"]),
+                "trailer": msg.get("trailer"),
+                "segs": [(s["off"] - msg["region"][0], s["nbytes"]) for s in msg["specs"]]}
         if msg["kind"] == "raw":
             payload = {"__ring_raw__": True, "tensor": views[0], "__ring__": ring}
         else:
@@ -368,13 +374,20 @@ class P2PTransport:
 
     def prepare(self, payload: Any, device: Optional[torch.device] = None) -> None:
         """Make the current stream wait (bounded, on the device) until the
-        payload's bytes have landed."""
+        payload's bytes have landed, then verify the message checksum the
+        producer stored behind the payload (a mismatch records ERR_CORRUPT in
+        the device error word; no host wait)."""
         if not isinstance(payload, dict) or "__ring__" not in payload:
             return
         from kvserve_hpdps_b200.ops import kernels as K
         r = payload["__ring__"]
+        dev = device or self.device
         K.wait_flag(self._region.ptr + self.flag_off + r["slot"] * FLAG_STRIDE,
-                    r["seq"] & 0xFFFFFFFF, device or self.device, timeout_s=self.flag_timeout_s)
+                    r["seq"] & 0xFFFFFFFF, dev, timeout_s=self.flag_timeout_s)
+        if r.get("trailer") is not None:  # corruption -> ERR_CORRUPT in the device error word
+            base = r["region"][0]
+            K.verify_checksum([(self._region.ptr + base + o, o, n) for o, n in r["segs"]],
+                              self._region.ptr + r["trailer"], dev)
 
     def release(self, payload: Any, device: Optional[torch.device] = None) -> None:
         """Return the payload's ring space once the work queued so far on the

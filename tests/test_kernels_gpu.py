@@ -373,3 +373,56 @@ def test_head_major_block_layout_matches_token_major(engine):
             a = dst_nhd[l][:, idx].reshape(2, -1, H, 128)[:, :t]
             c = dst_hnd[l][idx].permute(1, 0, 2, 3, 4).reshape(2, -1, H, 128)[:, :t]
             assert torch.equal(a, c)
+
+
+def test_message_checksum_detects_corruption():
+    """Producer checksum of a message's segments vs the consumer's
+    recomputation over its landed copy: equal copies pass, one flipped byte
+    records ERR_CORRUPT (host-injected corruption; nothing faults)."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    parts = [torch.randint(0, 256, (n,), generator=g, device=dev, dtype=torch.uint8)
+             for n in (1000, 4096, 37)]
+    offs, o = [], 0
+    for p in parts:
+        offs.append(o)
+        o += (p.numel() + 255) // 256 * 256
+    ring = torch.zeros(o + 256, dtype=torch.uint8, device=dev)
+    ck = torch.empty(2, dtype=torch.int64, device=dev)
+    K.checksum([(p.data_ptr(), off, p.numel()) for p, off in zip(parts, offs)], ck)
+    for p, off in zip(parts, offs):
+        ring[off:off + p.numel()] = p
+    ring[o:o + 16] = ck.view(torch.uint8)
+    segs = [(ring.data_ptr() + off, off, p.numel()) for p, off in zip(parts, offs)]
+    K.read_device_error(dev)
+    K.verify_checksum(segs, ring.data_ptr() + o, dev)
+    assert K.read_device_error(dev) == 0
+    ring[offs[1] + 777] ^= 0x10
+    K.verify_checksum(segs, ring.data_ptr() + o, dev)
+    assert K.read_device_error(dev) == 4  # ERR_CORRUPT
+    # a misaligned source checksums like the aligned one
+    buf = torch.zeros(4096 + 3, dtype=torch.uint8, device=dev)
+    buf[3:] = parts[1]
+    ck2 = torch.empty(2, dtype=torch.int64, device=dev)
+    K.checksum([(buf.data_ptr() + 3, 0, 4096)], ck2)
+    ck3 = torch.empty(2, dtype=torch.int64, device=dev)
+    K.checksum([(parts[1].data_ptr(), 0, 4096)], ck3)
+    assert torch.equal(ck2, ck3)
+
+
+def test_error_monitor_reports_without_waiting():
+    """A bounded flag wait that runs out (nothing sets the flag) records a
+    timeout; the non-blocking monitor reports it at a later poll."""
+    dev = torch.device("cuda")
+    K.read_device_error(dev)
+    mon = K.ErrorMonitor(dev)
+    assert mon.poll() == 0
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    K.wait_flag(flag.data_ptr(), 7, dev, timeout_s=0.05)
+    torch.cuda.synchronize()
+    code = 0
+    for _ in range(3):
+        code = code or mon.poll()
+        torch.cuda.synchronize()
+    assert code == 2  # ready-flag timeout
+    assert K.read_device_error(dev) == 0  # the monitor cleared the word
