@@ -40,6 +40,8 @@ from kvserve_hpdps_b200.compression.config import (DEFAULT_HADAMARD_SEED, FUSED_
 from kvserve_hpdps_b200.compression.head_scores import HybridPrecisionPlan
 from kvserve_hpdps_b200.utils.logger import get_logger
 
+from kvserve_hpdps_b200.utils.tracing import nvtx  # noqa: E402
+
 logger = get_logger(__name__)
 
 BACKEND = "kvs_fused"
@@ -176,9 +178,11 @@ class FusedCompressionManager:
         the kernels' device layout as ONE aux tensor (item offsets follow from
         the plans and block counts).  Decoders also accept the per-item
         ``layout="items"`` form."""
-        batch = self.quantize_paged(kv_layers, layer_ids, requests)
-        body = encode_bytes(batch.codes[:batch.items.code_bytes], self.stream_codec) if trim \
-            else self._encode_untrimmed(batch.codes[:batch.items.code_bytes])
+        with nvtx("kvs.quantize"):
+            batch = self.quantize_paged(kv_layers, layer_ids, requests)
+        with nvtx("kvs.encode"):
+            body = encode_bytes(batch.codes[:batch.items.code_bytes], self.stream_codec) if trim \
+                else self._encode_untrimmed(batch.codes[:batch.items.code_bytes])
         items = batch.items
         H = self.num_kv_heads
         meta = {"grouped": True, "layout": "items_packed", "layer_ids": [int(l) for l in layer_ids],

@@ -89,6 +89,8 @@ except Exception:  # noqa: BLE001
 if TYPE_CHECKING:
     pass
 
+from kvserve_hpdps_b200.utils.tracing import nvtx  # noqa: E402
+
 logger = get_logger(__name__)
 
 LOAD_TIMEOUT_S = float(os.environ.get("KVSERVE_LOAD_TIMEOUT_S", "60"))
@@ -297,9 +299,10 @@ class CompressedKVConnector(KVConnectorBase_V1):
             layers = [self._layer_refs[n] for n in names]
             if comp is not None and comp.supports_paged():
                 try:
-                    cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],
-                                                      [(rm.block_ids, len(rm.token_ids))],
-                                                      member_tids=[tid])
+                    with nvtx("kvs.compress"):
+                        cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],
+                                                          [(rm.block_ids, len(rm.token_ids))],
+                                                          member_tids=[tid])
                 except Exception:  # noqa: BLE001
                     # as the reference does: a compression failure sends the raw KV
                     logger.exception("compression of %s failed; sending raw KV", rid)
@@ -440,6 +443,15 @@ class CompressedKVConnector(KVConnectorBase_V1):
         else:
             payload_t = payload
         t0 = time.monotonic()
+        try:
+            with nvtx("kvs.inject"):
+                self._inject_body(rm, names, payload, payload_t, forward_context, t0)
+        finally:  # the ring space returns even when decoding fails
+            if hasattr(tr, "release"):
+                tr.release(payload, dev)
+
+    def _inject_body(self, rm: ReqMeta, names: list[str], payload: Any, payload_t: Any,
+                     forward_context: Any, t0: float) -> None:
         if is_compressed_layer_names(names):
             names = strip_sentinel(names)
             wire = CompressedWire(payload["meta"], payload["body_chunks"], payload["aux_tensors"])
@@ -462,8 +474,6 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 cache = self._layer_cache(name, forward_context)
                 if cache is not None:
                     inject_kv_into_layer_by_blocks(cache, payload_t[i], rm.block_ids, rm.request_id)
-        if hasattr(tr, "release"):
-            tr.release(payload, dev)
 
     def _inject_items(self, rm: ReqMeta, names: list[str], cd, comp, forward_context) -> None:
         """Fused message (one or more requests x layers): decode into the
