@@ -226,3 +226,20 @@ def test_adapter_routes_compatible_custom_pipelines_to_fused():
     assert ad2.manager.base_seed == 0x3333 and ad2.manager.codec == "rans"
     names = add_sentinel(["a", "b"])
     assert is_compressed_layer_names(names) and strip_sentinel(names) == ["a", "b"]
+
+
+def test_cpu_roundtrip_example_runs(capsys):
+    """The CPU-only round trip example (quantizer + codec fallback path) at a
+    reduced size: prints a compression ratio above 2 and a close
+    reconstruction."""
+    import importlib.util
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        "examples", "cpu_roundtrip.py")
+    spec = importlib.util.spec_from_file_location("cpu_roundtrip", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.main(["--layers", "2", "--tokens", "256"]) == 0
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["compression_ratio"] > 2.0 and line["cosine"] > 0.98
