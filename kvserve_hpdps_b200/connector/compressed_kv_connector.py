@@ -381,7 +381,11 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     logger.warning("timeout loading KV of %s (transfer %s): %d/%d messages",
                                    rm.request_id, rm.transfer_id, got, need)
                     break
-                time.sleep(0.002)
+                waiter = getattr(self._transport, "wait_received", None)
+                if waiter is not None:
+                    waiter(0.002)  # wakes as soon as a message header arrives
+                else:
+                    time.sleep(0.002)
                 self._drain()
         if torch.cuda.is_available() and meta.requests:
             # device-side failures of earlier loads (flag timeouts, checksum

@@ -169,6 +169,7 @@ class P2PTransport:
             self._ctl = ConsumerChannel(self.port)
             self._producer_id: Optional[bytes] = None
             self._lock = threading.Lock()
+            self._arrived = threading.Condition(self._lock)
             self._received: dict[str, deque] = defaultdict(deque)
             self._releases: deque = deque()  # (event, off, size)
             self._io = threading.Thread(target=self._consumer_io, daemon=True, name="kvs-p2p-io")
@@ -364,6 +365,16 @@ class P2PTransport:
                        "aux_tensors": views[n:], "__ring__": ring}
         with self._lock:
             self._received[msg["request_id"]].append((msg["layer_names"], payload))
+            self._arrived.notify_all()
+
+    def wait_received(self, timeout_s: float) -> bool:
+        """Block until some message is waiting to be drained or ``timeout_s``
+        passes; True when a message is waiting."""
+        assert not self.is_sender
+        with self._arrived:
+            if not any(self._received.values()):
+                self._arrived.wait(timeout=timeout_s)
+            return any(self._received.values())
 
     def drain_received(self) -> dict[str, list[tuple[list[str], Any]]]:
         assert not self.is_sender
