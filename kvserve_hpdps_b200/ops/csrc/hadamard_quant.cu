@@ -2026,7 +2026,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
     }
   } else if (warp < kWsCtrlWarp) {
     // ---------------------------------------------------------- epilogue
-    const int ew = warp - kWsGroupWarps, etid = tid - kWsGroupThreads;
+    const int ew = warp - kWsGroupWarps;
     const int quad = ew & 3, half = ew >> 2;
     const int lane_id = quad * 32 + lane;
     ItemCursor cur;
@@ -2036,7 +2036,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       const PJob jb = ws_job(M, k);
       cursor_seek(L, cur, jb.tile);
       const ItemCtx& c = cur.c;
-      if (etid == 0)  // the store that read output tile b (job k-2) has finished reading
+      if (ew == 0)  // the stores that read output tile b (job k-2) have finished reading
         asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
       group_sync(1);
       mbar_wait(&dmma[b], static_cast<uint32_t>((k >> 1) & 1), L.err, ERR_MBAR_TIMEOUT);
@@ -2064,28 +2064,28 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       if (lane == 0) mbar_arrive(&accfree[b]);
       fence_proxy_async_smem();  // generic writes of output tile b before the TMA store
       group_sync(1);
-      if (etid == 0) {
-        const CUtensorMap* map = map_of(L, c.slot, jb.plane);
+      if (ew == 0) {
+        // lane l < 16 stores box (row group l/2, channel half l%2): the
+        // block-table reads of the 16 boxes overlap; every lane commits its
+        // own (possibly empty) bulk group
         const int nst = min(kTileRows, c.ntok - c.row0);  // rows holding tokens
-        for (int g = 0; g < 8; ++g) {
+        const int g = lane >> 1, hb = lane & 1;
+        if (lane < 16 && g * 16 < nst) {
+          const CUtensorMap* map = map_of(L, c.slot, jb.plane);
           const int rr = c.row0 + g * 16;
-          if (g * 16 >= nst) break;
           const int phys = phys_block(L, c, rr);
           const int slot = rr % c.kv.block_size;
-#pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            asm volatile(
-                "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
-                    "l"(reinterpret_cast<uint64_t>(map)),
-                "r"(hb * 64), "r"(tma_y(c.kv, jb.h, slot)), "r"(tma_z(c.kv, jb.h, slot)),
-                "r"(phys), "r"(smem_u32(sO + hb * 16384 + g * 2048))
-                : "memory");
-          }
+          asm volatile(
+              "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
+                  "l"(reinterpret_cast<uint64_t>(map)),
+              "r"(hb * 64), "r"(tma_y(c.kv, jb.h, slot)), "r"(tma_z(c.kv, jb.h, slot)),
+              "r"(phys), "r"(smem_u32(sO + hb * 16384 + g * 2048))
+              : "memory");
         }
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       }
     }
-    if (etid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (ew == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   } else {
     // ----------------------------------------------------------- control
     ItemCursor cur;

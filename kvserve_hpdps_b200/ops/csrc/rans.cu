@@ -17,7 +17,7 @@ namespace rans {
 
 constexpr int kEncWarps = 4;
 constexpr int kDecWarps = 8;
-constexpr int kRing = 2048;  // words of the decoder's shared-memory ring
+constexpr int kRing = 1024;  // words of the decoder's shared-memory ring
 constexpr int kDecWarpSmem = 4096 + 1024 + kRing * 2;
 
 KVS_DEV uint32_t lanemask_lt() {
@@ -114,12 +114,14 @@ KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncSym* enc, int l
   __syncwarp();
 }
 
-__global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
+__global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
     const uint8_t* __restrict__ in, uint64_t n, uint32_t cs, uint8_t* __restrict__ staging,
     uint32_t* __restrict__ rec_off, uint32_t* __restrict__ rec_len, uint32_t n_chunks) {
-  __shared__ uint32_t hist[kEncWarps][4 * 256];
-  __shared__ EncSym enc[kEncWarps][256];
+  // a warp's histogram (4 x 256 counts) is dead once its frequencies are
+  // normalised, so its encoder table (256 x 16 B) reuses the same 4 KB
+  __shared__ __align__(16) uint32_t hist[kEncWarps][4 * 256];
   __shared__ uint32_t freq_s[kEncWarps][256];
+  static_assert(sizeof(EncSym) * 256 == sizeof(uint32_t) * 4 * 256, "table aliasing");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk = blockIdx.x * kEncWarps + warp;
   if (chunk >= n_chunks) return;  // warp-uniform
@@ -158,7 +160,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
   const uint32_t A = static_cast<uint32_t>(top + 1);
   __syncwarp();
   normalize_counts_warp(h, A, static_cast<uint64_t>(n_ss) * kSuper, freq_s[warp], lane);
-  build_enc_warp(freq_s[warp], A, enc[warp], lane);
+  EncSym* enc = reinterpret_cast<EncSym*>(hist[warp]);
+  build_enc_warp(freq_s[warp], A, enc, lane);
 
   uint16_t* words = reinterpret_cast<uint16_t*>(slot);
   const int64_t cap = static_cast<int64_t>(sb / 2);
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_rans_encode(
 #pragma unroll
     for (int m = kSub - 1; m >= 0; --m) {
       const uint32_t s = (w4[m >> 2] >> ((m & 3) * 8)) & 0xFFu;
-      const EncSym e = enc[warp][s];
+      const EncSym e = enc[s];
       const bool emit = x >= e.x_max;
       const uint32_t mask = __ballot_sync(0xFFFFFFFFu, emit);
       const int cnt = __popc(mask);
@@ -349,10 +352,11 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const uint32_t lt = lanemask_lt();
   __syncwarp();
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
-    // Keep >= 1024 words ahead of the read pointer with asynchronous 16-byte
-    // copies (one group per 256 words); a super-step reads at most 512
-    // words, so every group except the newest must have landed.
-    while (loaded < rptr + 1024 && loaded < total_words) {
+    // Keep kRing - 256 words ahead of the read pointer with asynchronous
+    // 16-byte copies (one group per 256 words, never over unread words); a
+    // super-step reads at most 512 words, so every group except the newest
+    // must have landed.
+    while (loaded < rptr + (kRing - 256) && loaded < total_words) {
       const uint32_t idx = loaded + lane * 8;
       if (idx < total_words)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
