@@ -68,8 +68,20 @@ KVS_DEV ItemCtx item_ctx(const LayerLaunch& L, int tile) {
   return c;
 }
 
+// Physical block holding an item row.  A block id outside the paged cache
+// (a corrupt or mismatched block table) records ERR_BOUNDS and returns -1:
+// loads then read block 0 (`load_block`) and stores skip the access, so a
+// bad table never makes a kernel touch memory outside the cache.
 KVS_DEV int phys_block(const LayerLaunch& L, const ItemCtx& c, int row) {
-  return L.rt.block_table[L.rt.bt_off[c.r] + row / c.kv.block_size];
+  const int p = L.rt.block_table[L.rt.bt_off[c.r] + row / c.kv.block_size];
+  if (static_cast<unsigned>(p) >= static_cast<unsigned>(c.kv.num_blocks)) {
+    record_error(L.err, ERR_BOUNDS);
+    return -1;
+  }
+  return p;
+}
+KVS_DEV int load_block(const LayerLaunch& L, const ItemCtx& c, int row) {
+  return max(0, phys_block(L, c, row));
 }
 
 KVS_DEV __nv_bfloat16* kv_row(const ItemCtx& c, int plane, int phys, int slot, int h) {
@@ -217,7 +229,7 @@ KVS_DEV void issue_tile_loads(const LayerLaunch& L, const ItemCtx& c, const CUte
   for (int g = 0; g < 8; ++g) {
     const int rr = c.row0 + g * 16;
     if (rr >= c.rows) break;
-    const int phys = phys_block(L, c, rr);
+    const int phys = load_block(L, c, rr);
     const int slot = rr % c.kv.block_size;
 #pragma unroll
     for (int hb = 0; hb < 2; ++hb) {
@@ -333,7 +345,7 @@ __global__ void __launch_bounds__(128) k_stats_simt(LayerLaunch L) {
     float mn = 0.f, mx = 0.f;
     if (row < c.ntok) {
       float v[128];
-      simt_forward_row(c, 1, phys_block(L, c, row), row % c.kv.block_size, h, v);
+      simt_forward_row(c, 1, load_block(L, c, row), row % c.kv.block_size, h, v);
       mn = INFINITY;
       mx = -INFINITY;
 #pragma unroll
@@ -351,7 +363,7 @@ __global__ void __launch_bounds__(128) k_stats_simt(LayerLaunch L) {
   if (nvalid <= 0) return;
   if (tid < nvalid) {
     float v[128];
-    simt_forward_row(c, 0, phys_block(L, c, row), row % c.kv.block_size, h, v);
+    simt_forward_row(c, 0, load_block(L, c, row), row % c.kv.block_size, h, v);
 #pragma unroll
     for (int d = 0; d < 128; ++d) buf[tid * 129 + d] = v[d];
   }
@@ -457,7 +469,7 @@ __global__ void __launch_bounds__(128) k_quant_simt(LayerLaunch L) {
   float v[128];
   const bool valid = row < c.ntok;
   if (valid) {
-    simt_forward_row(c, plane, phys_block(L, c, row), row % c.kv.block_size, h, v);
+    simt_forward_row(c, plane, load_block(L, c, row), row % c.kv.block_size, h, v);
   } else {
 #pragma unroll
     for (int d = 0; d < 128; ++d) v[d] = 0.f;
@@ -620,7 +632,9 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_simt(LayerLaunch L) {
     for (int d = 0; d < 128; ++d) v[d] = bf16_round(v[d] * sc);
     apply_signs(v, c.lp->sign_bits[h]);
   }
-  store_row_bf16(kv_row(c, kv, phys_block(L, c, row), row % c.kv.block_size, h), v);
+  const int phys = phys_block(L, c, row);
+  if (phys < 0) return;
+  store_row_bf16(kv_row(c, kv, phys, row % c.kv.block_size, h), v);
 }
 
 // Byte offset of element n of row t in a 2 x 16 KB K-major SW128 tile.
@@ -724,6 +738,7 @@ __global__ void __launch_bounds__(128) k_dequant_inverse_mma(LayerLaunch L) {
       const int rr = c.row0 + g * 16;
       if (rr >= c.rows) break;
       const int phys = phys_block(L, c, rr);
+      if (phys < 0) continue;  // bad block id: recorded, box skipped
       const int slot = rr % c.kv.block_size;
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
@@ -1196,7 +1211,7 @@ KVS_DEV void issue_tile_loads_warp(const LayerLaunch& L, const ItemCtx& c, const
   if (lane < 2 * nload) {
     const int g = lane >> 1, hb = lane & 1;
     const int rr = c.row0 + g * 16;
-    const int phys = phys_block(L, c, rr);
+    const int phys = load_block(L, c, rr);
     const int slot = rr % c.kv.block_size;
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -1356,7 +1371,7 @@ KVS_DEV BoxDesc box_desc(const LayerLaunch& L, ItemCursor& cur, const PJob& jb) 
   if (d.mine) {
     const int rr = c.row0 + (lane >> 1) * 16;
     const int slot = rr % c.kv.block_size;
-    d.phys = phys_block(L, c, rr);
+    d.phys = load_block(L, c, rr);
     d.y = tma_y(c.kv, jb.h, slot);
     d.z = tma_z(c.kv, jb.h, slot);
   }
@@ -1889,6 +1904,7 @@ __global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
         const int rr = c.row0 + g * 16;
         if (g * 16 >= nst) break;
         const int phys = phys_block(L, c, rr);
+        if (phys < 0) continue;  // bad block id: recorded, box skipped
         const int slot = rr % c.kv.block_size;
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
@@ -2070,10 +2086,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
         // own (possibly empty) bulk group
         const int nst = min(kTileRows, c.ntok - c.row0);  // rows holding tokens
         const int g = lane >> 1, hb = lane & 1;
-        if (lane < 16 && g * 16 < nst) {
+        const int rr = c.row0 + g * 16;
+        const int phys = (lane < 16 && g * 16 < nst) ? phys_block(L, c, rr) : -1;
+        if (phys >= 0) {  // a bad block id is recorded and its box skipped
           const CUtensorMap* map = map_of(L, c.slot, jb.plane);
-          const int rr = c.row0 + g * 16;
-          const int phys = phys_block(L, c, rr);
           const int slot = rr % c.kv.block_size;
           asm volatile(
               "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::

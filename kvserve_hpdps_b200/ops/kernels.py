@@ -342,6 +342,13 @@ def _align16(x: int) -> int:
     return (x + 15) & ~15
 
 
+def _num_blocks(kv_layer: torch.Tensor) -> int:
+    """Blocks of a [2, nb, ...] (FlashAttention) or [nb, 2, ...] (FlashInfer) layer."""
+    if kv_layer.shape[1] == 2 and kv_layer.shape[0] != 2:
+        return kv_layer.shape[0]
+    return kv_layer.shape[1]
+
+
 def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
     """Describe a paged KV layer tensor for the kernels.
 
@@ -370,10 +377,9 @@ def paged_kv(kv_layer: torch.Tensor) -> PagedKV:
     p.base = kv_layer.data_ptr()
     if kv_layer.shape[1] == 2 and kv_layer.shape[0] != 2:
         p.block_stride, p.kv_stride = st[0], st[1]
-        p.num_blocks = kv_layer.shape[0]
     else:
         p.kv_stride, p.block_stride = st[0], st[1]
-        p.num_blocks = kv_layer.shape[1]
+    p.num_blocks = _num_blocks(kv_layer)
     p.slot_stride, p.head_stride = st[2], st[3]
     p.block_size = bs
     p.hnd = hnd
@@ -456,6 +462,13 @@ class WorkItems:
                 lists.append(b.tolist() if isinstance(b, torch.Tensor) else [int(x) for x in b])
             norm.append((int(s), uniq[k], int(n)))
         self.items = [(s, lists[li], n) for s, li, n in norm]
+        span = [(min(b), max(b)) if b else (0, -1) for b in lists]
+        for s, li, n in norm:
+            lo, hi = span[li]
+            nb = _num_blocks(slots.kv_layers[s])
+            if lo < 0 or hi >= nb:
+                raise ValueError(f"block id {lo if lo < 0 else hi} outside the {nb} blocks "
+                                 f"of layer slot {s}")
         bs = [slots.kv_layers[s].shape[2] for s, _, _ in norm]
         self.n_rows = [len(lists[li]) * k for (_, li, _), k in zip(norm, bs)]
         self.n_tokens = [n for _, _, n in norm]

@@ -194,6 +194,8 @@ class P2PTransport:
                     with self._lock:
                         self._inflight_msgs -= len(msg["regions"])
             except Exception as e:  # noqa: BLE001
+                if self._closed:  # the socket went away under close()
+                    break
                 logger.error("p2p producer io error: %s", e)
 
     def _completion_loop(self) -> None:
@@ -349,6 +351,8 @@ class P2PTransport:
                 else:
                     logger.warning("p2p: unknown control message %r", cmd)
             except Exception as e:  # noqa: BLE001
+                if self._closed:  # the socket went away under close()
+                    break
                 logger.error("p2p consumer io error: %s", e)
 
     def _on_put(self, msg: dict) -> None:
@@ -421,6 +425,9 @@ class P2PTransport:
 
     def close(self) -> None:
         self._closed = True
+        io = getattr(self, "_io", None)
+        if io is not None and io is not threading.current_thread():
+            io.join(timeout=1.0)  # its polls return within a few ms
         try:
             self._ctl.close()
         except Exception:  # noqa: BLE001

@@ -426,3 +426,33 @@ def test_error_monitor_reports_without_waiting():
         torch.cuda.synchronize()
     assert code == 2  # ready-flag timeout
     assert K.read_device_error(dev) == 0  # the monitor cleared the word
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+def test_bad_block_id_is_recorded_not_followed(engine):
+    """A device block-table entry outside the cache (set after the host
+    check passed) records a bounds error: dequantize skips that block's rows
+    and writes the others, quantize reads block 0 in its place."""
+    H, tokens = 2, [64, 48]
+    wl = paged_workload(1, tokens, H, block_size=16, device="cuda", seed=3)
+    layer = wl.cache[0]
+    plan = _plan(H)
+    slots = K.LayerSlots.single(layer, plan)
+    items = K.WorkItems(slots, [(0, b, n) for b, n in zip(wl.block_ids, tokens)])
+    codes, meta = K.quantize(slots, items, engine=engine)
+    torch.cuda.synchronize()
+    assert K.read_device_error(layer.device) == 0
+    dst = torch.zeros_like(layer)
+    dslots = K.LayerSlots.single(dst, plan)
+    ditems = K.WorkItems(dslots, [(0, b, n) for b, n in zip(wl.block_ids, tokens)])
+    ditems._ints[1] = dst.shape[1] + 3  # entry 1 = second block of request 0
+    K.dequantize(codes, meta, dslots, ditems, engine=engine)
+    torch.cuda.synchronize()
+    assert K.read_device_error(dst.device) == 3
+    assert int(dst[:, wl.block_ids[0][1]].abs().sum()) == 0
+    for b in (wl.block_ids[0][0], wl.block_ids[1][0]):
+        assert float(dst[:, b].float().abs().sum()) > 0
+    items._ints[0] = -5
+    K.quantize(slots, items, engine=engine)
+    torch.cuda.synchronize()
+    assert K.read_device_error(layer.device) == 3
