@@ -60,6 +60,10 @@ def parse_args(argv=None):
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--codec", default="rans", choices=["rans", "bitpack", "none"])
     ap.add_argument("--engine", default="tcgen05", choices=["tcgen05", "simt"])
+    ap.add_argument("--compression", default="default", choices=["default", "off"],
+                    help="off: raw KV blocks (no transform, quantization or codec)")
+    ap.add_argument("--hybrid-ratio", type=float, default=None,
+                    help="override the default mode's hybrid_ratio")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args(argv)
@@ -213,6 +217,8 @@ def quant_config(args):
     from kvserve_hpdps_b200.compression.config import get_default_compression_config
     cfg = get_default_compression_config()
     cfg["quantizer_config"]["model_name"] = MODEL
+    if getattr(args, "hybrid_ratio", None) is not None:
+        cfg["quantizer_config"]["hybrid_ratio"] = float(args.hybrid_ratio)
     if args.codec == "bitpack":
         cfg["codec_config"] = {"codec_type": "bitpack"}
     elif args.codec == "none":
@@ -221,7 +227,129 @@ def quant_config(args):
 
 
 # ------------------------------------------------------------------ ours
+def _roles(world, rank):
+    pairs = max(1, world // 2)
+    if world == 1:
+        return "both", pairs
+    if world % 2:
+        raise SystemExit("--gpus must be 1 or even")
+    return ("producer" if rank < pairs else "consumer"), pairs
+
+
+def _timed(step, args, world, local, device, s0):
+    """Warm-up, then ``args.steps`` steps between barriers and device
+    synchronisations, timed with CUDA events; returns (max ms over ranks,
+    clocks, next step index, device error)."""
+    from kvserve_hpdps_b200.ops import kernels as K
+    s = s0
+    for _ in range(args.warmup):
+        step(s)
+        s += 1
+    torch.cuda.synchronize(device)
+    err = K.read_device_error(device)
+    if err:
+        raise RuntimeError(f"device error {err} during warmup ({K.ERR_NAMES.get(err)})")
+    sampler = ClockSampler(range(world)) if local == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step(s)
+        s += 1
+    ev1.record()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = ev0.elapsed_time(ev1)
+    err = K.read_device_error(device)
+    clocks = sampler.stop() if sampler else None
+    return allreduce_max(ms, world), clocks, s, int(allreduce_max(float(err), world))
+
+
+def run_ours_raw(args, rank, world, local):
+    """Compression off: raw KV blocks.  N = 1: one gather launch of every
+    (layer, request) item from the paged cache into a flat buffer and one
+    scatter launch into the second cache.  N >= 2: the producer's gather
+    stores straight into the consumer's receive slot over NVLink and
+    publishes a ready flag; the consumer waits (bounded) on it and scatters
+    into its cache, then returns a credit flag."""
+    from kvserve_hpdps_b200.ops import kernels as K
+    device = torch.device("cuda", local)
+    role, pairs = _roles(world, rank)
+    pair_id = rank % pairs
+    wl = Workload(args, device, args.seed + 101 * pair_id, role)
+    L = args.layers
+    layers_src = [wl.src[l] for l in range(L)] if wl.src is not None else None
+    layers_dst = [wl.dst[l] for l in range(L)] if wl.dst is not None else None
+    src_raw = K.RawItems(layers_src, [(l, b) for b, _ in wl.src_req for l in range(L)]) \
+        if layers_src else None
+    dst_raw = K.RawItems(layers_dst, [(l, b) for b, _ in wl.dst_req for l in range(L)]) \
+        if layers_dst else None
+    nbytes = (src_raw or dst_raw).flat_bytes
+    slot_bytes = ((nbytes + 255) // 256) * 256
+    if world == 1:
+        flat = torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+        def step(s):
+            K.paged_raw(src_raw, flat.data_ptr(), True)
+            K.paged_raw(dst_raw, flat.data_ptr(), False)
+        launches = 2
+        transport = "local"
+    else:
+        import torch.distributed as dist
+        from kvserve_hpdps_b200.parallel.p2p import DeviceRegion, PeerMapping
+        peer = rank + pairs if role == "producer" else rank - pairs
+        region = DeviceRegion(local, 2 * slot_bytes + 4096) if role == "consumer" else \
+            DeviceRegion(local, 4096)
+        handles = [None] * world
+        dist.all_gather_object(handles, (region.ipc_handle(), region.nbytes, local))
+        ph, pn, _ = handles[peer]
+        peer_map = PeerMapping(local, ph, pn)
+
+        def step(s):
+            slot = s % 2
+            if role == "producer":
+                if s >= 2:
+                    K.wait_flag(region.ptr + 256 * slot, s - 1, device, timeout_s=20.0)
+                K.paged_raw(src_raw, peer_map.ptr + slot * slot_bytes, True,
+                            flag_ptr=peer_map.ptr + 2 * slot_bytes + 256 * slot, flag_value=s + 1)
+            else:
+                K.wait_flag(region.ptr + 2 * slot_bytes + 256 * slot, s + 1, device,
+                            timeout_s=20.0)
+                K.paged_raw(dst_raw, region.ptr + slot * slot_bytes, False)
+                K.set_flag(peer_map.ptr + 256 * slot, s + 1, device)
+        launches = 2 if role == "producer" else 3
+        transport = "nvlink-p2p (one gather launch stores raw blocks into the consumer's slot)"
+
+    ms, clocks, _, err = _timed(step, args, world, local, device, 0)
+    error = None
+    if role in ("both", "consumer"):
+        ref = wl if wl.src is not None else Workload(args, device, args.seed + 101 * pair_id,
+                                                     "producer")
+        idx_s = torch.tensor(ref.src_req[0][0], device=device)
+        idx_d = torch.tensor(wl.dst_req[0][0], device=device)
+        error = {"exact": bool(torch.equal(ref.src[:, :, idx_s], wl.dst[:, :, idx_d]))}
+        del ref
+    if world > 1:
+        import torch.distributed as dist
+        gathered = [None] * world
+        dist.all_gather_object(gathered, error)
+        error = next((g for g in gathered if g is not None), None)
+        barrier(world)
+        peer_map.close()
+        barrier(world)
+        region.close()
+    return {"ms": ms, "cr": 1.0, "error": error, "transport": transport,
+            "launches": launches * args.steps, "clocks": clocks, "e2e": None,
+            "device_error": err, "pairs": pairs, "role": role}
+
+
 def run_ours(args, rank, world, local):
+    if getattr(args, "compression", "default") == "off":
+        return run_ours_raw(args, rank, world, local)
     from kvserve_hpdps_b200.compression.fused_manager import FusedCompressionManager
     from kvserve_hpdps_b200.ops import kernels as K
     device = torch.device("cuda", local)
@@ -370,6 +498,10 @@ def run_ours(args, rank, world, local):
         gathered = [None] * world
         dist.all_gather_object(gathered, stats.get("error"))
         stats["error"] = next((g for g in gathered if g is not None), None)
+        barrier(world)  # unmap the peer slot before its owner frees it
+        peer_map.close()
+        barrier(world)
+        region.close()
     stream_bytes = allreduce_sum(float(stats.get("stream_bytes", 0)), world)
     n_prod = pairs if world > 1 else 1
     orig = wl.bf16_bytes_per_request * wl.B * n_prod
@@ -513,6 +645,19 @@ def run_e2e_pairs(args, mgr, wl, role, world, rank, pairs, device):
 
 
 # ------------------------------------------------------------------ reference
+_REF_TRANSPORTS: dict = {}
+
+
+def _ref_compressed_bytes(c) -> int:
+    """Compressed body bytes of the reference's CompressedKVData (a single
+    tensor, or chunks above its 500 MiB chunking threshold)."""
+    if getattr(c, "is_chunked", False) and c.chunks:
+        return int(sum(t.numel() * t.element_size() for t in c.chunks))
+    if c.compressed_tensor is not None:
+        return int(c.compressed_tensor.numel() * c.compressed_tensor.element_size())
+    return int(c.compressed_size)
+
+
 def run_reference_pairs(args, rank, world, local):
     """Reference arm on producer/consumer pairs, through the reference's own
     public modules: its KVCompressionAdapter (quantizer pipeline), its wire
@@ -537,14 +682,21 @@ def run_reference_pairs(args, rank, world, local):
     cfg = quant_config(args)
     spec = {"enabled": True, "pipeline": ["quantizer"],
             "quantizer_config": dict(cfg["quantizer_config"]), "min_compress_size": 0}
-    adapter = KVCompressionAdapter(spec, num_kv_heads=args.kv_heads, head_size=128,
-                                   model_name=MODEL)
+    raw = getattr(args, "compression", "default") == "off"
+    adapter = None if raw else KVCompressionAdapter(spec, num_kv_heads=args.kv_heads,
+                                                    head_size=128, model_name=MODEL)
     wl = Workload(args, device, args.seed + 101 * pair_id, role)
     L = args.layers
-    names = add_sentinel([f"model.layers.{l}.self_attn.attn" for l in range(L)])
-    tr = NcclTransport(role == "producer", "127.0.0.1", side_port(500, pair_id), local, 0)
+    plain_names = [f"model.layers.{l}.self_attn.attn" for l in range(L)]
+    names = add_sentinel(plain_names)
+    tr = _REF_TRANSPORTS.get((role, pair_id))
+    if tr is None:  # one communicator per pair for the life of the process
+        tr = NcclTransport(role == "producer", "127.0.0.1", side_port(500, pair_id), local, 0)
+        _REF_TRANSPORTS[(role, pair_id)] = tr
+    tag = getattr(args, "tag", "")
     pending: dict = {}
     sizes = []
+    fallbacks = []  # requests its adapter returned None for (sent raw)
 
     def wait_sent(timeout_s=120.0):
         t = threading.Thread(target=tr.wait_for_sent, daemon=True)
@@ -555,19 +707,33 @@ def run_reference_pairs(args, rank, world, local):
 
     def step(s):
         for r in range(wl.B):
-            key = f"s{s}r{r}"
-            if role == "producer":
+            key = f"{tag}s{s}r{r}"
+            if role == "producer" and raw:  # the connector's path without compression
+                stacked = torch.stack([extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0])
+                                       for l in range(L)], dim=0)
+                sizes.append(int(stacked.numel() * stacked.element_size()))
+                tr.send(key, plain_names, stacked)
+            elif role == "producer":
                 layers = [extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0])
                           for l in range(L)]
-                c = adapter.compress(torch.stack(layers, dim=0), key)
-                sizes.append(int(c.compressed_tensor.numel() * c.compressed_tensor.element_size()))
+                stacked = torch.stack(layers, dim=0)
+                c = adapter.compress(stacked, key)
+                if c is None:  # as its connector does: send the raw KV instead
+                    fallbacks.append(key)
+                    sizes.append(int(stacked.numel() * stacked.element_size()))
+                    tr.send(key, plain_names, stacked)
+                    continue
+                sizes.append(_ref_compressed_bytes(c))
                 w = build_wire(c, 512 << 20)  # the connector's default chunk bound
                 tr.send_bundle(key, names, w.meta, w.body_chunks, w.aux_tensors)
             else:
                 _, payload = _poll_message(tr, pending, key, 120.0)
-                cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
-                                                      payload["aux_tensors"]))
-                out = adapter.decompress(cd)
+                if raw or isinstance(payload, torch.Tensor):
+                    out = payload
+                else:
+                    cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
+                                                          payload["aux_tensors"]))
+                    out = adapter.decompress(cd)
                 for l in range(L):
                     inject_kv_into_layer_by_blocks(wl.dst[l], out[l], wl.dst_req[r][0])
 
@@ -613,9 +779,15 @@ def run_reference_pairs(args, rank, world, local):
     tot = allreduce_sum(float(sum(sizes)), world)
     n = allreduce_sum(float(len(sizes)), world)
     cr = wl.bf16_bytes_per_request / (tot / n) if n else None
+    nfall = allreduce_sum(float(len(fallbacks)), world)
     return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "pairs": pairs,
-            "reference_path": "custom pipeline [quantizer] via KVCompressionAdapter + "
-                              "build_wire + NcclTransport.send_bundle (ncclSend/ncclRecv per pair)",
+            "fallback_raw": int(nfall),
+            "reference_path": ("raw: extract_kv_from_layer_by_blocks + stack + "
+                               "NcclTransport.send (ncclSend/ncclRecv per pair) + "
+                               "inject_kv_into_layer_by_blocks") if raw else
+                              ("custom pipeline [quantizer] via KVCompressionAdapter + "
+                               "build_wire + NcclTransport.send_bundle (ncclSend/ncclRecv per "
+                               "pair)"),
             "transport": "reference NcclTransport (NCCL send/recv over NVLink)"}
 
 
@@ -630,29 +802,40 @@ def run_reference(args, rank, world, local):
     from kvserve_v1.utils.kv_utils import (extract_kv_from_layer_by_blocks,  # noqa: E402
                                            inject_kv_into_layer_by_blocks)
     device = torch.device("cuda", local)
-    try:
-        KVCompressionAdapter("default", num_kv_heads=args.kv_heads, head_size=128,
-                             model_name=MODEL)
-        path = "default"
-    except Exception as e:  # noqa: BLE001
-        default_err = f"{type(e).__name__}: {e}"
-        path = None
-    cfg = quant_config(args)
-    spec = {"enabled": True, "pipeline": ["quantizer"],
-            "quantizer_config": dict(cfg["quantizer_config"]), "min_compress_size": 0}
-    adapter = KVCompressionAdapter(spec if path is None else "default", num_kv_heads=args.kv_heads,
-                                   head_size=128, model_name=MODEL)
+    raw = getattr(args, "compression", "default") == "off"
+    path, default_err, adapter = "raw", "", None
+    if not raw:
+        try:
+            KVCompressionAdapter("default", num_kv_heads=args.kv_heads, head_size=128,
+                                 model_name=MODEL)
+            path = "default"
+        except Exception as e:  # noqa: BLE001
+            default_err = f"{type(e).__name__}: {e}"
+            path = None
+        cfg = quant_config(args)
+        spec = {"enabled": True, "pipeline": ["quantizer"],
+                "quantizer_config": dict(cfg["quantizer_config"]), "min_compress_size": 0}
+        adapter = KVCompressionAdapter(spec if path is None else "default",
+                                       num_kv_heads=args.kv_heads, head_size=128,
+                                       model_name=MODEL)
     wl = Workload(args, device, args.seed)
     L = args.layers
     sizes = []
+    fallbacks = []
 
     def step(s):
         for r in range(wl.B):
             layers = [extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0]) for l in range(L)]
             stacked = torch.stack(layers, dim=0)
-            c = adapter.compress(stacked, f"r{s}_{r}")
-            sizes.append(int(c.compressed_tensor.numel() * c.compressed_tensor.element_size()))
-            out = adapter.decompress(c)
+            c = None if raw else adapter.compress(stacked, f"r{s}_{r}")
+            if c is None:  # compression off, or its adapter declined: raw KV
+                if not raw:
+                    fallbacks.append(r)
+                sizes.append(int(stacked.numel() * stacked.element_size()))
+                out = stacked
+            else:
+                sizes.append(_ref_compressed_bytes(c))
+                out = adapter.decompress(c)
             for l in range(L):
                 inject_kv_into_layer_by_blocks(wl.dst[l], out[l], wl.dst_req[r][0])
 
@@ -679,13 +862,25 @@ def run_reference(args, rank, world, local):
            "rel_mse": float(((a - b) ** 2).sum() / (a ** 2).sum())}
     del error_metrics
     cr = wl.bf16_bytes_per_request / statistics.mean(sizes)
-    return {"ms": ms, "cr": cr, "error": err, "clocks": clocks,
-            "reference_path": "custom pipeline [quantizer] via KVCompressionAdapter (default mode "
-                              "unavailable: " + (default_err if path is None else "n/a") + ")",
-            "transport": "local"}
+    ref_path = ("raw: extract_kv_from_layer_by_blocks + stack + inject_kv_into_layer_by_blocks"
+                if raw else "custom pipeline [quantizer] via KVCompressionAdapter (default mode "
+                "unavailable: " + (default_err if path is None else "n/a") + ")")
+    return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "reference_path": ref_path,
+            "transport": "local", "fallback_raw": len(fallbacks)}
 
 
 # ------------------------------------------------------------------ main
+def hybrid_ratio(args) -> float:
+    return float(quant_config(args)["quantizer_config"]["hybrid_ratio"])
+
+
+def compression_label(args) -> str:
+    if args.compression == "off":
+        return "off (raw bf16 blocks)"
+    codec = "rANS" if args.codec == "rans" else args.codec
+    return f"default (Hadamard + hybrid {hybrid_ratio(args)} 12/8/6/4 + {codec})"
+
+
 def main(argv=None):
     args = parse_args(argv)
     rank, world, local = dist_info()
@@ -728,8 +923,7 @@ def main(argv=None):
             "global_batch": args.requests_per_step * pairs,
             "seq_len": args.tokens,
             "parallelism": "1-GPU round trip" if world == 1 else f"1P1D x{pairs} pairs (TP1)",
-            "compression": "default (Hadamard + hybrid 0.8 12/8/6/4 + " +
-                           ("rANS" if args.codec == "rans" else args.codec) + ")",
+            "compression": compression_label(args),
             "requests_per_step": args.requests_per_step,
             "l2": "inputs larger than L2 (%.1f GB of KV per step per producer)"
                   % (args.layers * 2 * args.tokens * args.kv_heads * 256 * args.requests_per_step / 1e9),
@@ -741,10 +935,13 @@ def main(argv=None):
     }
     if args.impl == "reference":
         line["impl"] = "reference"
+        if res.get("fallback_raw"):
+            line["config"]["reference_fallback_raw_requests"] = res["fallback_raw"]
         line["config"]["reference_path"] = res.get("reference_path")
-        line["config"]["compression"] = ("reference quantizer pipeline, hybrid 0.8 12/8/6/4, u8 "
-                                         "codes, no entropy codec (its default mode needs nvCOMP, "
-                                         "CuPy and fast_hadamard_transform)")
+        line["config"]["compression"] = (
+            "off (raw bf16 blocks)" if args.compression == "off" else
+            f"reference quantizer pipeline, hybrid {hybrid_ratio(args)} 12/8/6/4, u8 codes, no "
+            "entropy codec (its default mode needs nvCOMP, CuPy and fast_hadamard_transform)")
     else:
         line["impl"] = "ours"
         line["gpu_launches"] = int(allreduce_sum(float(res["launches"]), world)) if world > 1 \

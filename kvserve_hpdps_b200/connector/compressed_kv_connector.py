@@ -315,6 +315,12 @@ class CompressedKVConnector(KVConnectorBase_V1):
                                             prefill_span_ms=span)
                     continue
                 comp = None
+            if comp is None and hasattr(self._transport, "send_paged") and layers[0].is_cuda:
+                # raw KV: one gather launch from the paged caches into the peer ring
+                with nvtx("kvs.send_raw"):
+                    self._transport.send_paged(tid, names, layers, rm.block_ids)
+                self._expected_msgs[tid] = 1
+                continue
             stacked = torch.stack([extract_kv_from_layer_by_blocks(l, rm.block_ids)
                                    for l in layers], 0)
             cd = comp.compress(stacked, rid) if comp is not None else None
@@ -474,10 +480,40 @@ class CompressedKVConnector(KVConnectorBase_V1):
                         inject_kv_into_layer_by_blocks(cache, kv[i], rm.block_ids, rm.request_id)
             write_decode_stats(rm.request_id, rm.transfer_id, (time.monotonic() - t0) * 1e3)
         else:
-            for i, name in enumerate(names):
-                cache = self._layer_cache(name, forward_context)
+            caches = [self._layer_cache(n, forward_context) for n in names]
+            if self._scatter_raw(rm, caches, payload, payload_t):
+                return
+            for cache, part in zip(caches, payload_t):
                 if cache is not None:
-                    inject_kv_into_layer_by_blocks(cache, payload_t[i], rm.block_ids, rm.request_id)
+                    inject_kv_into_layer_by_blocks(cache, part, rm.block_ids, rm.request_id)
+
+    @staticmethod
+    def _scatter_raw(rm: ReqMeta, caches: list, payload: Any, payload_t: Any) -> bool:
+        """Scatter a raw ``[L, 2, nb, ...]`` device payload into every layer
+        at this request's blocks in one launch.  Needs the same block count
+        and block order on both sides; False leaves it to the per-layer
+        path (which also handles partial overlaps)."""
+        if not (isinstance(payload_t, torch.Tensor) and payload_t.is_cuda
+                and payload_t.is_contiguous() and payload_t.dim() == 6):
+            return False
+        if any(c is None for c in caches) or payload_t.shape[0] != len(caches):
+            return False
+        if payload_t.shape[2] != len(rm.block_ids) or any(c.dtype != payload_t.dtype
+                                                           for c in caches):
+            return False
+        from kvserve_hpdps_b200.ops import kernels as K
+        order = payload.get("block_order", "nhd") if isinstance(payload, dict) else "nhd"
+        try:
+            orders = {K._raw_block_layout(c)[1] for c in caches}
+        except ValueError:
+            return False
+        if orders != {order} or any(c.shape[2:] != payload_t.shape[3:] for c in caches):
+            return False
+        ids = [int(b) for b in rm.block_ids]
+        raw = K.RawItems(caches, [(l, ids) for l in range(len(caches))])
+        with nvtx("kvs.scatter_raw"):
+            K.paged_raw(raw, payload_t.data_ptr(), gather=False)
+        return True
 
     def _inject_items(self, rm: ReqMeta, names: list[str], cd, comp, forward_context) -> None:
         """Fused message (one or more requests x layers): decode into the

@@ -49,7 +49,10 @@ def _timeit(fn, iters: int, warmup: int = 3) -> float:
 def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
         only: tuple[str, ...] = STAGES, engine: int = 0, seed: int = 1,
         key_levels=(12, 6, 6, 6), value_levels=(8, 4, 4, 4), warmup: int = 3,
-        code_width: int = 8) -> list[dict]:
+        code_width: int = 8, hybrid_ratio: float | None = None) -> list[dict]:
+    """Stage timings.  With ``hybrid_ratio`` the per-layer plans are the
+    default compression mode's (head-score mask at that ratio, nibble codes)
+    instead of the fixed ``key_levels``/``value_levels``."""
     from kvserve_hpdps_b200.models.synthetic import paged_workload
     from kvserve_hpdps_b200.ops import kernels as K
     wl = paged_workload(layers, [tokens], heads, device="cuda", seed=seed, fill=False)
@@ -58,7 +61,17 @@ def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
     kl = list(key_levels)[:heads] + [key_levels[-1]] * max(0, heads - len(key_levels))
     vl = list(value_levels)[:heads] + [value_levels[-1]] * max(0, heads - len(value_levels))
     cw = code_width if code_width != 8 else None
-    plans = [K.make_layer_plan(heads, kl, vl, 0x3333, l, code_width=cw) for l in range(layers)]
+    if hybrid_ratio is None:
+        plans = [K.make_layer_plan(heads, kl, vl, 0x3333, l, code_width=cw) for l in range(layers)]
+    else:
+        from kvserve_hpdps_b200.compression.config import get_default_compression_config
+        from kvserve_hpdps_b200.compression.fused_manager import FusedCompressionManager
+        cfg = get_default_compression_config()
+        qc = dict(cfg["quantizer_config"], model_name="Qwen2.5-7B-Instruct",
+                  hybrid_ratio=float(hybrid_ratio))
+        mgr = FusedCompressionManager(heads, 128, qc, cfg["codec_config"], num_layers=layers)
+        plans = [mgr.plan(l) for l in range(layers)]
+        code_width = mgr.code_width
     slots = K.LayerSlots([wl.cache[l] for l in range(layers)], plans)
     items = K.WorkItems(slots, [(l, wl.block_ids[0], tokens) for l in range(layers)])
     dst = torch.zeros_like(wl.cache)
@@ -117,13 +130,15 @@ def main(argv=None) -> int:
     ap.add_argument("--only", default=",".join(STAGES))
     ap.add_argument("--code-width", type=int, default=8,
                     help="bits per code in the code buffer (4: two codes per rANS symbol)")
+    ap.add_argument("--hybrid-ratio", type=float, default=None,
+                    help="use the default mode's per-layer plans at this hybrid_ratio")
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print(json.dumps({"unavailable": "no CUDA device"}))
         return 0
     for r in run(args.layers, args.tokens, args.heads, args.iters,
                  tuple(args.only.split(",")), args.engine, warmup=args.warmup,
-                 code_width=args.code_width):
+                 code_width=args.code_width, hybrid_ratio=args.hybrid_ratio):
         print(json.dumps(r))
     return 0
 

@@ -54,6 +54,20 @@ class LayerLaunch(ctypes.Structure):
                 ("stream", c_void_p), ("trace", c_void_p), ("trace_jobs", c_int)]
 
 
+class RawItem(ctypes.Structure):
+    _fields_ = [("bt_off", c_longlong), ("flat_off", c_longlong), ("slot", c_int),
+                ("nblocks", c_int)]
+
+
+class RawLaunch(ctypes.Structure):
+    _fields_ = [("kvs", c_void_p), ("items", c_void_p), ("unit_prefix", c_void_p),
+                ("block_table", c_void_p), ("flat", c_void_p), ("err", c_void_p), ("ck", c_void_p),
+                ("trailer", c_void_p), ("counter", c_void_p), ("flag", c_void_p),
+                ("n_units", c_longlong), ("n_items", c_int), ("dir", c_int),
+                ("block_bytes", c_int), ("elem_bytes", c_int), ("flag_value", c_uint32),
+                ("pad_", c_int)]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -80,8 +94,11 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_cpu_bitunpack": ([P, c_uint64, c_int, P], None),
         "kvs_checksum": ([P, c_int, P, c_int, P], c_int),
         "kvs_checksum_verify": ([P, c_int, P, P, P, c_int, P], c_int),
-        "kvs_block_copy": ([POINTER(PagedKV), P, c_int, c_longlong, P, c_int, P, P, c_uint32, P],
-                           c_int),
+        "kvs_block_copy": ([POINTER(PagedKV), P, c_int, c_longlong, P, c_int, P, P, c_uint32, P,
+                            P], c_int),
+        "kvs_raw_launch_size": ([], c_int),
+        "kvs_raw_item_size": ([], c_int),
+        "kvs_paged_raw": ([POINTER(RawLaunch), c_int, P], c_int),
         "kvs_copy16": ([P, P, c_longlong, P, P, c_uint32, c_int, P], c_int),
         "kvs_copy_segments": ([P, c_int, c_int, P, P, c_uint32, P], c_int),
         "kvs_wait_flag": ([P, c_uint32, c_uint64, P, P, P], c_int),
@@ -123,7 +140,9 @@ def lib() -> ctypes.CDLL:
             _declare(handle)
             for name, cls in (("kvs_layer_launch_size", LayerLaunch),
                               ("kvs_layer_params_size", LayerParams),
-                              ("kvs_paged_kv_size", PagedKV)):
+                              ("kvs_paged_kv_size", PagedKV),
+                              ("kvs_raw_launch_size", RawLaunch),
+                              ("kvs_raw_item_size", RawItem)):
                 got = getattr(handle, name)()
                 if got != ctypes.sizeof(cls):
                     raise RuntimeError(f"{cls.__name__} size mismatch: C {got} vs Python "

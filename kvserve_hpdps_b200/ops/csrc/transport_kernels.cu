@@ -21,15 +21,21 @@ namespace kvs {
 __global__ void __launch_bounds__(256) k_block_copy(PagedKV kv, const int32_t* __restrict__ blocks,
                                                     int nblocks, long long block_elems,
                                                     uint8_t* flat, int dir, uint32_t* counter,
-                                                    uint32_t* flag, uint32_t flag_value) {
+                                                    uint32_t* flag, uint32_t flag_value,
+                                                    uint32_t* err) {
   const int b = blockIdx.x, plane = blockIdx.y;
   const long long bytes = block_elems * 2;
-  uint8_t* paged = const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(kv.base)) +
-                   (static_cast<long long>(blocks[b]) * kv.block_stride + plane * kv.kv_stride) * 2;
-  uint8_t* lin = flat + (static_cast<long long>(plane) * nblocks + b) * bytes;
-  const uint4* s = reinterpret_cast<const uint4*>(dir == 0 ? paged : lin);
-  uint4* d = reinterpret_cast<uint4*>(dir == 0 ? lin : paged);
-  for (long long i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+  const int phys = blocks[b];
+  if (static_cast<unsigned>(phys) < static_cast<unsigned>(kv.num_blocks)) {
+    uint8_t* paged = const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(kv.base)) +
+                     (static_cast<long long>(phys) * kv.block_stride + plane * kv.kv_stride) * 2;
+    uint8_t* lin = flat + (static_cast<long long>(plane) * nblocks + b) * bytes;
+    const uint4* s = reinterpret_cast<const uint4*>(dir == 0 ? paged : lin);
+    uint4* d = reinterpret_cast<uint4*>(dir == 0 ? lin : paged);
+    for (long long i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+  } else if (threadIdx.x == 0) {
+    record_error(err, ERR_BOUNDS);  // block id outside the cache: nothing copied
+  }
   if (counter != nullptr) {
     __threadfence_system();
     __syncthreads();
@@ -195,6 +201,124 @@ __global__ void __launch_bounds__(256) k_checksum(const CkSeg* __restrict__ segs
   }
 }
 
+// ------------------------------------------------------- raw paged transfer
+// Uncompressed transfer of whole paged blocks for many (layer slot, block
+// list) items in one launch.  The flat side holds the items back to back,
+// item r at flat_off as [2][nblocks][block bytes] -- per layer, the
+// reference's raw layout [2, nblocks, block_size, H, D]
+// (kvserve_v1/utils/kv_utils.py:59-80); a request's L layer items in order
+// form its stacked [L, 2, nblocks, ...] tensor.  dir 0 gathers paged -> flat
+// (the flat side may be a peer GPU's receive ring: NVLink stores), dir 1
+// scatters flat -> paged.  A unit is one (item, plane, block); CTAs stride
+// over units.  Block ids outside a slot's cache record ERR_BOUNDS and the
+// unit is skipped.  With `ck` the gather also sums the message checksum of
+// the flat bytes (the definition of k_checksum, message offset = flat
+// offset); with `flag` the last CTA stores the checksum to `trailer`, fences
+// at system scope and publishes `flag_value`.
+struct RawItem {
+  long long bt_off;    // first block-table entry of the item
+  long long flat_off;  // byte offset of the item in the flat buffer
+  int slot;            // index into kvs[]
+  int nblocks;
+};
+
+struct RawLaunch {
+  const PagedKV* kvs;
+  const RawItem* items;
+  const long long* unit_prefix;  // [n_items + 1] units before item r
+  const int32_t* block_table;
+  uint8_t* flat;
+  uint32_t* err;
+  unsigned long long* ck;       // [2] checksum accumulators or null
+  unsigned long long* trailer;  // [2] checksum destination (may be peer memory) or null
+  uint32_t* counter;            // completion counter (zero before the launch) or null
+  uint32_t* flag;
+  long long n_units;
+  int n_items;
+  int dir;
+  int block_bytes;
+  int elem_bytes;
+  uint32_t flag_value;
+  int pad_;
+};
+
+__global__ void __launch_bounds__(256) k_paged_raw(const RawLaunch a) {
+  unsigned long long s1 = 0, s2 = 0;
+  const int n16 = a.block_bytes >> 4;
+  for (long long u = blockIdx.x; u < a.n_units; u += gridDim.x) {
+    int lo = 0, hi = a.n_items - 1;  // last item whose first unit is <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.unit_prefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    const RawItem it = a.items[lo];
+    const int local = static_cast<int>(u - a.unit_prefix[lo]);
+    const int plane = local >= it.nblocks ? 1 : 0;
+    const int b = local - plane * it.nblocks;
+    const PagedKV kv = a.kvs[it.slot];
+    const int phys = a.block_table[it.bt_off + b];
+    if (static_cast<unsigned>(phys) >= static_cast<unsigned>(kv.num_blocks)) {
+      if (threadIdx.x == 0) record_error(a.err, ERR_BOUNDS);
+      continue;
+    }
+    uint8_t* paged = const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(kv.base)) +
+                     (static_cast<long long>(phys) * kv.block_stride + plane * kv.kv_stride) *
+                         a.elem_bytes;
+    const long long foff = it.flat_off + static_cast<long long>(local) * a.block_bytes;
+    uint8_t* lin = a.flat + foff;
+    const uint4* src = reinterpret_cast<const uint4*>(a.dir == 0 ? paged : lin);
+    uint4* dst = reinterpret_cast<uint4*>(a.dir == 0 ? lin : paged);
+    for (int i0 = threadIdx.x; i0 < n16; i0 += 4 * blockDim.x) {
+      uint4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = i0 + k * blockDim.x;
+        if (i < n16) v[k] = __ldcs(src + i);  // read once: do not keep in L2
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = i0 + k * blockDim.x;
+        if (i < n16) {
+          dst[i] = v[k];
+          if (a.ck != nullptr) {
+            const unsigned long long w = static_cast<unsigned long long>((foff >> 2) + 4 * i + 1);
+            s1 += static_cast<unsigned long long>(v[k].x) + v[k].y + v[k].z + v[k].w;
+            s2 += w * v[k].x + (w + 1) * v[k].y + (w + 2) * v[k].z + (w + 3) * v[k].w;
+          }
+        }
+      }
+    }
+  }
+  if (a.ck != nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, o);
+      s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+    }
+    if ((threadIdx.x & 31) == 0 && (s1 | s2)) {
+      atomicAdd(a.ck, s1);
+      atomicAdd(a.ck + 1, s2);
+    }
+  }
+  if (a.counter != nullptr) {
+    __threadfence_system();  // this thread's stores (peer ones included) and sums first
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(a.counter, 1u);
+      if (done == gridDim.x - 1) {
+        __threadfence();
+        if (a.trailer != nullptr && a.ck != nullptr) {
+          a.trailer[0] = atomicAdd(a.ck, 0ull);  // coherent reads of the finished sums
+          a.trailer[1] = atomicAdd(a.ck + 1, 0ull);
+        }
+        __threadfence_system();
+        if (a.flag != nullptr) st_release_sys(a.flag, a.flag_value);
+        *a.counter = 0;
+      }
+    }
+  }
+}
+
 __global__ void k_zero2(unsigned long long* p) {
   if (threadIdx.x < 2) p[threadIdx.x] = 0;
 }
@@ -213,11 +337,11 @@ extern "C" {
 
 int kvs_block_copy(const PagedKV* kv, const int32_t* blocks, int nblocks, long long block_elems,
                    uint8_t* flat, int dir, uint32_t* counter, uint32_t* flag, uint32_t flag_value,
-                   void* stream) {
+                   uint32_t* err, void* stream) {
   if (nblocks <= 0) return 0;
   if ((block_elems * 2) % 16 != 0) return -2;
   k_block_copy<<<dim3(nblocks, 2), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      *kv, blocks, nblocks, block_elems, flat, dir, counter, flag, flag_value);
+      *kv, blocks, nblocks, block_elems, flat, dir, counter, flag, flag_value, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -280,6 +404,23 @@ int kvs_probe_push(const void* src, void* dst, long long bytes, unsigned long lo
   if (bytes % 16 != 0) return -2;
   k_probe_push<<<blocks, 512, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), static_cast<uint4*>(dst), bytes / 16, stamps);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_raw_launch_size() { return static_cast<int>(sizeof(RawLaunch)); }
+int kvs_raw_item_size() { return static_cast<int>(sizeof(RawItem)); }
+
+// Raw paged transfer (see k_paged_raw).  Zeroes the checksum accumulators
+// first when `ck` is set.  Grid: min(units, max_ctas), at least one CTA so
+// that a requested flag is published even for an empty transfer.
+int kvs_paged_raw(const RawLaunch* a, int max_ctas, void* stream) {
+  if (a->block_bytes <= 0 || a->block_bytes % 16 != 0 || a->n_items <= 0) return -2;
+  if ((reinterpret_cast<uintptr_t>(a->flat) & 15) != 0) return -2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->ck != nullptr) k_zero2<<<1, 32, 0, s>>>(a->ck);
+  long long grid = a->n_units < max_ctas ? a->n_units : max_ctas;
+  if (grid < 1) grid = 1;
+  k_paged_raw<<<static_cast<int>(grid), 256, 0, s>>>(*a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -586,6 +586,157 @@ TRACE_EVENTS = ("tile_ready", "mma_issued", "refill_issued", "epi_mma_seen", "ep
 _trace = {"buf": None, "jobs": 0}
 
 
+@lru_cache(maxsize=None)
+def _sm_count(index: int) -> int:
+    return torch.cuda.get_device_properties(index).multi_processor_count
+
+
+def _raw_block_layout(kv_layer: torch.Tensor) -> tuple[PagedKV, str]:
+    """Descriptor of a paged layer for whole-block raw copies (any dtype and
+    head size) and its block order ("nhd" or "hnd").  Each (plane, block)
+    must be one dense run of ``bs * H * D`` elements."""
+    if kv_layer.dim() != 5:
+        raise ValueError(f"expected a [2, nb, bs, H, D] layer, got {tuple(kv_layer.shape)}")
+    st, sh = kv_layer.stride(), kv_layer.shape
+    bs, H, D = sh[2], sh[3], sh[4]
+    if st[4] == 1 and st[3] == D and st[2] == H * D:
+        order = "nhd"
+    elif st[4] == 1 and st[2] == D and st[3] == bs * D:
+        order = "hnd"
+    else:
+        raise ValueError(f"KV blocks are not dense (strides {st})")
+    p = PagedKV()
+    p.base = kv_layer.data_ptr()
+    if sh[1] == 2 and sh[0] != 2:
+        p.block_stride, p.kv_stride = st[0], st[1]
+    else:
+        p.kv_stride, p.block_stride = st[0], st[1]
+    p.num_blocks = _num_blocks(kv_layer)
+    p.slot_stride, p.head_stride = st[2], st[3]
+    p.block_size = bs
+    p.hnd = 1 if order == "hnd" else 0
+    return p, order
+
+
+class RawItems:
+    """Uncompressed whole-block transfer of (layer, block ids) items between
+    paged KV layers and one flat buffer, in one launch per direction.
+
+    The flat buffer holds the items back to back, each as
+    ``[2, len(blocks), block_size, H, D]`` (the reference's per-layer raw
+    layout, kvserve_v1/utils/kv_utils.py:59-80); items (0, b), (1, b), ...
+    (L-1, b) therefore form the stacked ``[L, 2, nb, bs, H, D]`` request
+    tensor.  Block ids are checked here against each layer's cache and
+    again on the device.  Descriptors reach the device in one copy.
+    """
+
+    def __init__(self, kv_layers: Sequence[torch.Tensor],
+                 items: Sequence[tuple[int, Sequence[int]]]):
+        if not kv_layers or not items:
+            raise ValueError("at least one layer and one item are required")
+        self.device = kv_layers[0].device
+        descs = [_raw_block_layout(t) for t in kv_layers]
+        orders = {o for _, o in descs}
+        if len(orders) != 1:
+            raise ValueError("all layers of a raw transfer must share one block order")
+        self.block_order = orders.pop()
+        shapes = {tuple(t.shape[2:]) for t in kv_layers}
+        dtypes = {t.dtype for t in kv_layers}
+        if len(shapes) != 1 or len(dtypes) != 1:
+            raise ValueError("all layers of a raw transfer must share block shape and dtype")
+        self.block_shape = shapes.pop()
+        self.dtype = dtypes.pop()
+        self.elem_bytes = torch.empty((), dtype=self.dtype).element_size()
+        bs, H, D = self.block_shape
+        self.block_bytes = bs * H * D * self.elem_bytes
+        if self.block_bytes % 16:
+            raise ValueError("a KV block must be a multiple of 16 bytes")
+        uniq: dict[int, int] = {}
+        lists: list[list[int]] = []
+        norm = []
+        for s, b in items:
+            k = id(b)
+            if k not in uniq:
+                uniq[k] = len(lists)
+                lists.append(b.tolist() if isinstance(b, torch.Tensor) else [int(x) for x in b])
+            norm.append((int(s), uniq[k]))
+        span = [(min(b), max(b)) if b else (0, -1) for b in lists]
+        for s, li in norm:
+            if not 0 <= s < len(kv_layers):
+                raise ValueError(f"item layer {s} outside the {len(kv_layers)} layers")
+            lo, hi = span[li]
+            nb = descs[s][0].num_blocks
+            if lo < 0 or hi >= nb:
+                raise ValueError(f"block id {lo if lo < 0 else hi} outside the {nb} blocks "
+                                 f"of layer slot {s}")
+        bt, list_off = [], []
+        for b in lists:
+            list_off.append(len(bt))
+            bt.extend(b)
+        ritems = (_lib.RawItem * len(norm))()
+        prefix = [0]
+        flat = 0
+        self.item_offsets, self.item_blocks = [], []
+        for i, (s, li) in enumerate(norm):
+            nb = len(lists[li])
+            ritems[i].bt_off, ritems[i].flat_off = list_off[li], flat
+            ritems[i].slot, ritems[i].nblocks = s, nb
+            self.item_offsets.append(flat)
+            self.item_blocks.append(nb)
+            flat += 2 * nb * self.block_bytes
+            prefix.append(prefix[-1] + 2 * nb)
+        self.flat_bytes = flat
+        self.n_units = prefix[-1]
+        self.n_items = len(norm)
+        kvs = (PagedKV * len(descs))(*[d for d, _ in descs])
+        parts = [bytes(kvs), bytes(ritems),
+                 torch.tensor(prefix, dtype=torch.int64).numpy().tobytes(),
+                 torch.tensor(bt or [0], dtype=torch.int32).numpy().tobytes()]
+        offs, raw = [], bytearray()
+        for p in parts:
+            offs.append(len(raw))
+            raw += p
+            raw += bytes((-len(raw)) % 16)
+        host = torch.frombuffer(raw, dtype=torch.uint8).clone()
+        if self.device.type == "cuda":
+            host = host.pin_memory()
+            _xfer["h2d"] += host.numel()
+        self._desc = host.to(self.device, non_blocking=True)
+        base = self._desc.data_ptr()
+        self._ptrs = [base + o for o in offs]  # kvs, items, prefix, block table
+
+    def flat_shape(self, r: int = 0) -> tuple[int, ...]:
+        return (2, self.item_blocks[r]) + tuple(self.block_shape)
+
+
+def paged_raw(raw: RawItems, flat_ptr: int, gather: bool, flag_ptr: Optional[int] = None,
+              flag_value: int = 0, trailer_ptr: Optional[int] = None,
+              checksum: Optional[torch.Tensor] = None, max_ctas: Optional[int] = None) -> None:
+    """Gather (paged -> flat) or scatter (flat -> paged) every item of ``raw``
+    in one launch on the current stream.  ``flat_ptr`` may be a peer GPU's
+    memory for the gather.  With ``checksum`` (int64[2] on the device) the
+    gather also computes the message checksum of the flat bytes (as
+    :func:`checksum` would); ``trailer_ptr`` receives it and ``flag_ptr``
+    receives ``flag_value`` (release, system scope) once everything landed."""
+    dev = raw.device
+    ws = workspace(dev)
+    a = _lib.RawLaunch()
+    a.kvs, a.items, a.unit_prefix, a.block_table = raw._ptrs
+    a.flat = flat_ptr
+    a.err = ws.err.data_ptr()
+    a.ck = checksum.data_ptr() if checksum is not None else None
+    a.trailer = trailer_ptr if (checksum is not None and trailer_ptr is not None) else None
+    a.counter = ws.counters[6:7].data_ptr() if flag_ptr is not None else None
+    a.flag = flag_ptr
+    a.n_units, a.n_items = raw.n_units, raw.n_items
+    a.dir = 0 if gather else 1
+    a.block_bytes, a.elem_bytes = raw.block_bytes, raw.elem_bytes
+    a.flag_value = flag_value & 0xFFFFFFFF
+    if max_ctas is None:
+        max_ctas = 8 * _sm_count(dev.index if dev.index is not None else torch.cuda.current_device())
+    check(lib().kvs_paged_raw(ctypes.byref(a), int(max_ctas), _stream(dev)), "paged_raw")
+
+
 def set_trace(device: Optional[torch.device], jobs_per_cta: int = 256) -> Optional[torch.Tensor]:
     """Enable (device given) or disable (None) globaltimer tracing of the
     warp-specialized kernels for the first TRACE_CTAS CTAs of each launch;
@@ -793,7 +944,7 @@ def block_copy(kv_layer: torch.Tensor, blocks: torch.Tensor, flat_ptr: int, gath
     counter = ws.counters[1:2] if flag is not None else None
     check(lib().kvs_block_copy(ctypes.byref(p), blocks.data_ptr(), nb, block_elems, flat_ptr,
                                0 if gather else 1, _ptr(counter), _ptr(flag), flag_value,
-                               _stream(kv_layer.device)), "block_copy")
+                               ws.err.data_ptr(), _stream(kv_layer.device)), "block_copy")
 
 
 def copy_bytes(src_ptr: int, dst_ptr: int, nbytes: int, device: torch.device,

@@ -62,6 +62,13 @@ class _FakeEnd:
 
     def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
         self._deliver(request_id, (list(layer_names), stacked_kv.clone()))
+        self._count_sent(None, request_id)
+
+    def _count_sent(self, member_tids: Optional[list[str]], request_id: str) -> None:
+        """A message without member ids counts for its request id."""
+        with self.pair.lock:
+            for t in (member_tids or [request_id]):
+                self.pair.sent[t] += 1
 
     def send_bundle(self, request_id, layer_names, meta, body_chunks, aux_tensors,
                     member_tids: Optional[list[str]] = None) -> None:
@@ -69,10 +76,7 @@ class _FakeEnd:
                    "body_chunks": [t.clone() for t in body_chunks],
                    "aux_tensors": [t.clone() for t in aux_tensors]}
         self._deliver(request_id, (list(layer_names), payload))
-        if member_tids:
-            with self.pair.lock:
-                for t in member_tids:
-                    self.pair.sent[t] += 1
+        self._count_sent(member_tids, request_id)
 
     def sent_layers(self, tid: str) -> int:
         with self.pair.lock:

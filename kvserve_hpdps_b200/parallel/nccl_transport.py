@@ -187,10 +187,9 @@ class NcclTransport:
         t0 = time.monotonic()
         self._p2p_send(tensors)
         nbytes = sum(t.numel() * t.element_size() for t in tensors)
-        if kind == "bundle" and member_tids:
-            with self._sent_lock:
-                for tid in member_tids:
-                    self._sent[tid] += 1
+        with self._sent_lock:  # a message without member ids counts for its request id
+            for tid in (member_tids or [request_id]):
+                self._sent[tid] += 1
         write_transfer_stats(request_id, (time.monotonic() - t0) * 1e3, nbytes,
                              transport="nccl" if self.backend == "nccl" else self.backend)
 

@@ -210,10 +210,9 @@ class P2PTransport:
             with self._pending_cv:
                 self._pending.popleft()
                 self._pending_cv.notify_all()
-            if tids:
-                with self._lock:
-                    for t in tids:
-                        self._sent[t] += 1
+            with self._lock:  # a message without member ids counts for its request id
+                for t in (tids or [rid]):
+                    self._sent[t] += 1
             write_transfer_stats(rid, (time.monotonic() - t0) * 1e3, nbytes, transport="nvlink-p2p")
 
     def _put(self, request_id: str, layer_names: list[str], tensors: list[torch.Tensor],
@@ -226,18 +225,7 @@ class P2PTransport:
             total += _align(s)
         trailer = total           # 16-byte message checksum after the payload
         total = total + ALIGN
-        with self._lock:
-            wait_slots = self._inflight_msgs >= self.n_flags - 1
-        if wait_slots:
-            logger.warning("p2p: %d messages in flight, waiting for the consumer", self.n_flags)
-        base = self._alloc.alloc(total, self.timeout_s)
-        if base is None:
-            raise RuntimeError(f"receive ring full for {self.timeout_s}s ({total} bytes needed)")
-        with self._lock:
-            self._seq += 1
-            seq = self._seq
-            self._inflight_msgs += 1
-        slot = seq % self.n_flags
+        base, seq, slot = self._reserve(total)
         from kvserve_hpdps_b200.ops import kernels as K
         ready = torch.cuda.current_stream(self.device).record_event()
         t0 = time.monotonic()
@@ -261,6 +249,57 @@ class P2PTransport:
             "region": [base, total], "slot": slot, "seq": seq, "trailer": base + trailer})
         with self._pending_cv:
             self._pending.append((done, request_id, member_tids, sum(sizes), t0))
+            self._pending_cv.notify_all()
+
+    def _reserve(self, total: int) -> tuple[int, int, int]:
+        """Ring space, sequence number and flag slot of a new message."""
+        with self._lock:
+            wait_slots = self._inflight_msgs >= self.n_flags - 1
+        if wait_slots:
+            logger.warning("p2p: %d messages in flight, waiting for the consumer", self.n_flags)
+        base = self._alloc.alloc(total, self.timeout_s)
+        if base is None:
+            raise RuntimeError(f"receive ring full for {self.timeout_s}s ({total} bytes needed)")
+        with self._lock:
+            self._seq += 1
+            seq = self._seq
+            self._inflight_msgs += 1
+        return base, seq, seq % self.n_flags
+
+    def send_paged(self, request_id: str, layer_names: list[str], kv_layers: list[torch.Tensor],
+                   block_ids, member_tids: Optional[list[str]] = None) -> None:
+        """Raw (uncompressed) KV of one request straight from the paged
+        caches into the consumer's ring: one gather launch over every layer,
+        storing over NVLink, that also computes the message checksum and
+        publishes the ready flag.  It runs on the current stream, so it is
+        ordered before any later kernel that rewrites those blocks.  The
+        consumer sees the stacked ``[L, 2, nb, bs, H, D]`` raw tensor."""
+        assert self.is_sender
+        from kvserve_hpdps_b200.ops import kernels as K
+        ids = [int(b) for b in block_ids]
+        raw = K.RawItems(kv_layers, [(l, ids) for l in range(len(kv_layers))])
+        nbytes = raw.flat_bytes
+        trailer = _align(nbytes)
+        total = trailer + ALIGN
+        base, seq, slot = self._reserve(total)
+        t0 = time.monotonic()
+        dev = raw.device
+        ck = torch.empty(2, dtype=torch.int64, device=dev)
+        K.paged_raw(raw, self._peer.ptr + base, True,
+                    flag_ptr=self._peer.ptr + self.flag_off + slot * FLAG_STRIDE,
+                    flag_value=seq & 0xFFFFFFFF, trailer_ptr=self._peer.ptr + base + trailer,
+                    checksum=ck)
+        done = torch.cuda.current_stream(dev).record_event()
+        shape = [len(kv_layers), 2, len(ids)] + list(raw.block_shape)
+        self._outbox.put({
+            "cmd": "PUT_RING", "kind": "raw", "request_id": request_id,
+            "layer_names": list(layer_names), "meta": None, "n_body": 1,
+            "specs": [{"shape": shape, "dtype": str(raw.dtype).replace("torch.", ""),
+                       "off": base, "nbytes": nbytes}],
+            "block_order": raw.block_order,
+            "region": [base, total], "slot": slot, "seq": seq, "trailer": base + trailer})
+        with self._pending_cv:
+            self._pending.append((done, request_id, member_tids, nbytes, t0))
             self._pending_cv.notify_all()
 
     def bandwidth_mbps(self, probe_bytes: int = 64 << 20, max_age_s: float = 30.0,
@@ -362,7 +401,8 @@ class P2PTransport:
                 "trailer": msg.get("trailer"),
                 "segs": [(s["off"] - msg["region"][0], s["nbytes"]) for s in msg["specs"]]}
         if msg["kind"] == "raw":
-            payload = {"__ring_raw__": True, "tensor": views[0], "__ring__": ring}
+            payload = {"__ring_raw__": True, "tensor": views[0], "__ring__": ring,
+                       "block_order": msg.get("block_order", "nhd")}
         else:
             n = msg["n_body"]
             payload = {"__bundle__": True, "meta": msg["meta"], "body_chunks": views[:n],

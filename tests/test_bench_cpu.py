@@ -1,0 +1,48 @@
+"""Benchmark drivers on CPU: argument handling of ``bench.py`` and the
+size/step planning and report of the handoff sweep (the timed runs need
+GPUs)."""
+
+import importlib.util
+import os
+
+import bench
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _sweep():
+    spec = importlib.util.spec_from_file_location(
+        "handoff_sweep", os.path.join(ROOT, "examples", "handoff_sweep.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_bench_modes_and_labels():
+    a = bench.parse_args([])
+    assert a.compression == "default" and bench.hybrid_ratio(a) == 0.8
+    assert bench.compression_label(a).startswith("default (Hadamard + hybrid 0.8")
+    a = bench.parse_args(["--hybrid-ratio", "0.3", "--codec", "bitpack"])
+    assert bench.quant_config(a)["quantizer_config"]["hybrid_ratio"] == 0.3
+    assert "bitpack" in bench.compression_label(a)
+    assert bench.compression_label(bench.parse_args(["--compression", "off"])) == \
+        "off (raw bf16 blocks)"
+
+
+def test_sweep_plan_and_report():
+    sw = _sweep()
+    assert sw.BYTES_PER_TOKEN == 57344
+    assert sw.DEFAULT_TOKENS[0] * sw.BYTES_PER_TOKEN < 1.1e6
+    assert sw.DEFAULT_TOKENS[-1] * sw.BYTES_PER_TOKEN > 4 * 2 ** 30
+    assert sw.steps_for(16) == 40 and sw.steps_for(74912) == 3
+    a = sw.point_args(bench, 2, 4096, "h0.3", 3)
+    assert (a.tokens, a.requests_per_step, a.compression, a.hybrid_ratio, a.no_e2e) == \
+        (4096, 1, "default", 0.3, True)
+    assert sw.point_args(bench, 1, 16, "off", 3).compression == "off"
+    rows = [{"impl": "ours", "tokens": 16, "mode": "off", "ms_per_request": 0.01,
+             "raw_gbps": 91.0, "compression_ratio": 1.0},
+            {"impl": "reference", "tokens": 16, "mode": "off", "ms_per_request": 0.05,
+             "raw_gbps": 18.0, "compression_ratio": 1.0},
+            {"impl": "reference", "unavailable": "x"}]
+    table = sw.render(rows)
+    assert "| 0.9 | off | 0.01 | 91.0 | 1.0 | 0.05 | 18.0 | 1.0 | 5.0x |" in table

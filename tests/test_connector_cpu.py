@@ -91,6 +91,17 @@ def test_generic_compressed_handoff():
         assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.97
 
 
+def test_async_send_reports_raw_requests_finished():
+    """With asynchronous sends the producer frees a request's blocks only
+    after its message left; a raw (uncompressed) message counts too."""
+    p, c, pair = make_pair(None)
+    p._async_send = True
+    handoff(p, c)
+    done, _ = p.get_finished({"r1"})
+    assert done == {"r1"}
+    assert p.get_finished(set()) == (None, None)
+
+
 def test_refused_and_dropped_messages_do_not_hang(monkeypatch):
     import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
     monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.3)

@@ -298,6 +298,66 @@ def test_block_copy_gather_scatter():
     assert torch.equal(gather_request(dst, wl.block_ids[0]), flat)
 
 
+@pytest.mark.parametrize("layout", ["flash_attn", "flashinfer", "hnd"])
+def test_raw_paged_transfer_round_trip(layout):
+    """One-launch raw gather of several (layer, blocks) items into the
+    stacked flat layout, its fused message checksum, and the scatter back."""
+    L, H, nb = 3, 4, 12
+    g = torch.Generator(device="cuda").manual_seed(4)
+    if layout == "flash_attn":
+        layers = [torch.randn((2, nb, 16, H, 128), generator=g, device="cuda").to(torch.bfloat16)
+                  for _ in range(L)]
+    elif layout == "flashinfer":
+        layers = [torch.randn((nb, 2, 16, H, 128), generator=g, device="cuda").to(torch.bfloat16)
+                  for _ in range(L)]
+    else:  # head-major blocks: [nb, 2, H, bs, D] storage seen as [nb, 2, bs, H, D]
+        layers = [torch.randn((nb, 2, H, 16, 128), generator=g, device="cuda")
+                  .to(torch.bfloat16).transpose(2, 3) for _ in range(L)]
+    blocks = [7, 2, 11, 0, 5]
+    raw = K.RawItems(layers, [(l, blocks) for l in range(L)])
+    assert raw.block_order == ("hnd" if layout == "hnd" else "nhd")
+    flat = torch.empty(raw.flat_bytes, dtype=torch.uint8, device="cuda")
+    ck = torch.empty(2, dtype=torch.int64, device="cuda")
+    trailer = torch.zeros(2, dtype=torch.int64, device="cuda")
+    flag = torch.zeros(4, dtype=torch.int32, device="cuda")
+    K.paged_raw(raw, flat.data_ptr(), True, flag_ptr=flag.data_ptr(), flag_value=9,
+                trailer_ptr=trailer.data_ptr(), checksum=ck)
+    torch.cuda.synchronize()
+    assert K.read_device_error(flat.device) == 0
+    assert int(flag[0]) == 9
+    idx = torch.tensor(blocks, device="cuda")
+    for l in range(L):
+        t = layers[l]
+        part = flat[raw.item_offsets[l]:raw.item_offsets[l] + 2 * len(blocks) * raw.block_bytes]
+        if layout == "flash_attn":
+            exp = t[:, idx]
+        else:
+            exp = t[idx].transpose(0, 1)
+        if layout == "hnd":
+            exp = exp.transpose(2, 3)  # bytes of a block are in [H, bs, D] order
+        assert torch.equal(part.view(torch.bfloat16).view(exp.shape), exp.contiguous())
+    ref = torch.empty(2, dtype=torch.int64, device="cuda")
+    K.checksum([(flat.data_ptr(), 0, raw.flat_bytes)], ref)
+    torch.cuda.synchronize()
+    assert torch.equal(ck, ref) and torch.equal(trailer, ref)
+    dst = [torch.zeros_like(t) for t in layers]
+    draw = K.RawItems(dst, [(l, [1, 3, 4, 8, 10]) for l in range(L)])
+    K.paged_raw(draw, flat.data_ptr(), False)
+    torch.cuda.synchronize()
+    for l in range(L):
+        for a, b in zip(blocks, [1, 3, 4, 8, 10]):
+            if layout == "flash_attn":
+                assert torch.equal(dst[l][:, b], layers[l][:, a])
+            else:
+                assert torch.equal(dst[l][b], layers[l][a])
+    # a block id that turns bad after the host check is recorded and skipped
+    off = draw._ptrs[3] - draw._desc.data_ptr()  # first block-table entry
+    draw._desc[off:off + 4] = torch.tensor([100], dtype=torch.int32).view(torch.uint8).cuda()
+    K.paged_raw(draw, flat.data_ptr(), False)
+    torch.cuda.synchronize()
+    assert K.read_device_error(flat.device) == 3
+
+
 def test_kv_error_matches_cpu():
     g = torch.Generator().manual_seed(3)
     a = torch.randn(10007, generator=g).to(torch.bfloat16)
