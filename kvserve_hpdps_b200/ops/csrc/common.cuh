@@ -285,6 +285,54 @@ KVS_DEV uint32_t cvt_bf16x2(float lo, float hi) {
 KVS_DEV float bf16lo_to_float(uint32_t p) { return __uint_as_float(p << 16); }
 KVS_DEV float bf16hi_to_float(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): each instruction performs the
+// two IEEE operations of its scalar form, rounded the same way, so results
+// are bit-identical to the scalar code.
+typedef unsigned long long f32x2_t;
+KVS_DEV f32x2_t f2_pack(float lo, float hi) {
+  f32x2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+KVS_DEV void f2_unpack(f32x2_t p, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(p));
+}
+KVS_DEV f32x2_t f2_sub(f32x2_t a, f32x2_t b) {
+  f32x2_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+KVS_DEV f32x2_t f2_mul(f32x2_t a, f32x2_t b) {
+  f32x2_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+KVS_DEV f32x2_t f2_add(f32x2_t a, f32x2_t b) {
+  f32x2_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+KVS_DEV f32x2_t f2_add_rd(f32x2_t a, f32x2_t b) {
+  f32x2_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// quantize_bits on a pair of values with their own (min, rcp) pairs: the
+// biased bits 2^23 + code of both, by the same operations in the same order.
+KVS_DEV void quantize_bits2(float x0, float x1, f32x2_t mn2, f32x2_t rcp2, float top,
+                            uint32_t& b0, uint32_t& b1) {
+  const f32x2_t t = f2_add(f2_mul(f2_sub(f2_pack(x0, x1), mn2), rcp2), f2_pack(0.5f, 0.5f));
+  float t0, t1;
+  f2_unpack(t, t0, t1);
+  t0 = fminf(fmaxf(t0, 0.0f), top);
+  t1 = fminf(fmaxf(t1, 0.0f), top);
+  float r0, r1;
+  f2_unpack(f2_add_rd(f2_pack(t0, t1), f2_pack(8388608.0f, 8388608.0f)), r0, r1);
+  b0 = __float_as_uint(r0);
+  b1 = __float_as_uint(r1);
+}
+
 // quantize_fast returning the raw bits of 2^23 + code (code in the low
 // mantissa bits): callers that pack codes take the bits they need directly.
 KVS_DEV uint32_t quantize_bits(float v, float mn, float rcp, float top) {

@@ -23,8 +23,9 @@
 //    tcgen05.mma (bf16 x bf16 -> fp32 in TMEM) against a +-1 Hadamard matrix
 //    with the Rademacher signs folded in, the epilogue reads the accumulator
 //    back with tcgen05.ld; each CTA pipelines a contiguous range of tiles;
-//    (k_stats_ws / k_quant_ws are warp-specialized: a control warp issues
-//    loads and MMAs, two epilogue groups of 8 warps alternate jobs;
+//    (k_stats_ws / k_quant_ws are warp-specialized: a load warp issues the
+//    TMA boxes, an MMA warp issues the MMAs, two epilogue groups of 8 warps
+//    alternate jobs;
 //    k_dequant_ws: unpack warps, a control warp and epilogue warps);
 //  * engine 3: the persistent kernels without warp specialization (k_*_tc);
 //  * engine 2: the same math with one CTA per tile (k_*_mma);
@@ -82,6 +83,11 @@ KVS_DEV int phys_block(const LayerLaunch& L, const ItemCtx& c, int row) {
 }
 KVS_DEV int load_block(const LayerLaunch& L, const ItemCtx& c, int row) {
   return max(0, phys_block(L, c, row));
+}
+// Block-table entry without the check, for callers that validate it later
+// (when the value is used) so that the read's latency is not waited on now.
+KVS_DEV int raw_block(const LayerLaunch& L, const ItemCtx& c, int row) {
+  return L.rt.block_table[L.rt.bt_off[c.r] + row / c.kv.block_size];
 }
 
 KVS_DEV __nv_bfloat16* kv_row(const ItemCtx& c, int plane, int phys, int slot, int h) {
@@ -246,7 +252,7 @@ KVS_DEV void issue_tile_loads(const LayerLaunch& L, const ItemCtx& c, const CUte
 // Key channel min / reciprocal scale of (item, head h) into smem; tile 0 of
 // the item publishes the fp16 metadata.
 KVS_DEV void key_channel_params(const LayerLaunch& L, const ItemCtx& c, int h, float* s_min,
-                                float* s_rcp, int stride = 1, int n = -1) {
+                                float* s_rcp, int stride = 1, int n = -1, bool pairs = false) {
   if (n < 0) n = threadIdx.x;
   const uint32_t* ks = L.kstat + (static_cast<size_t>(c.r * c.lp->H + h) * 128 + n) * 2;
   float kmin = 0.f, kmax = 0.f;
@@ -256,8 +262,13 @@ KVS_DEV void key_channel_params(const LayerLaunch& L, const ItemCtx& c, int h, f
   }
   const float lev = c.lp->key_levels[h];
   const float scale = __fdiv_rn(fmaxf(__fsub_rn(kmax, kmin), kRangeEps), lev - 1.0f);
-  s_min[n * stride] = kmin;
-  s_rcp[n * stride] = __frcp_rn(scale);
+  if (pairs) {  // [min(2p), min(2p+1), rcp(2p), rcp(2p+1)] per channel pair p
+    s_min[4 * (n >> 1) + (n & 1)] = kmin;
+    s_min[4 * (n >> 1) + 2 + (n & 1)] = __frcp_rn(scale);
+  } else {
+    s_min[n * stride] = kmin;
+    s_rcp[n * stride] = __frcp_rn(scale);
+  }
   if (c.row0 == 0) {
     __half* m = meta_base(L, c.r);
     m[h * 128 + n] = __float2half_rn(kmin);
@@ -1049,6 +1060,65 @@ KVS_DEV void p_quant_half(uint32_t taddr, float sc, float top, bool valid, int p
   }
 }
 
+// Warp-specialized form of p_quant_half: values go through the quantizer in
+// pairs (f32x2 arithmetic), key parameters are read in the pair layout
+// [min(2p), min(2p+1), rcp(2p), rcp(2p+1)], and 4-bit codes are packed two
+// per byte with one shift-add (the low bytes of the biased bits are the
+// codes) and gathered four bytes per word with byte permutes.  Codes are
+// identical to p_quant_half's.
+template <int W>
+KVS_DEV void ws_quant_half(uint32_t taddr, float sc, float top, bool valid, int plane,
+                           float vmin, float vrcp, const float* kp, int half,
+                           uint8_t* row_stage) {
+  const f32x2_t sc2 = f2_pack(sc, sc);
+  const f32x2_t vmn2 = f2_pack(vmin, vmin), vrcp2 = f2_pack(vrcp, vrcp);
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    float v[32];
+    tmem_ld32(taddr + cc * 32, v);
+    uint32_t w[8];
+    uint32_t b[32];
+    uint32_t nib[16];
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      float y0, y1;
+      f2_unpack(f2_mul(f2_pack(v[k], v[k + 1]), sc2), y0, y1);
+      const uint32_t pr = valid ? cvt_bf16x2(y0, y1) : 0u;
+      const float x0 = bf16lo_to_float(pr), x1 = bf16hi_to_float(pr);
+      f32x2_t mn2 = vmn2, rcp2 = vrcp2;
+      if (plane == 0) {
+        const float4 m = *reinterpret_cast<const float4*>(kp + 2 * (half * 64 + cc * 32 + k));
+        mn2 = f2_pack(m.x, m.y);
+        rcp2 = f2_pack(m.z, m.w);
+      }
+      if constexpr (W == 4) {
+        uint32_t b0, b1;
+        quantize_bits2(x0, x1, mn2, rcp2, top, b0, b1);
+        nib[k >> 1] = b0 + (b1 << 4);  // low byte: code k | code k+1 << 4
+      } else {  // scalar form (fewer live registers for the wide codes)
+        float m0, m1, r0, r1;
+        f2_unpack(mn2, m0, m1);
+        f2_unpack(rcp2, r0, r1);
+        b[k] = quantize_bits(x0, m0, r0, top);
+        b[k + 1] = quantize_bits(x1, m1, r1, top);
+      }
+    }
+    if constexpr (W == 4) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = __byte_perm(nib[4 * i], nib[4 * i + 1], 0x0040);
+        const uint32_t hi = __byte_perm(nib[4 * i + 2], nib[4 * i + 3], 0x0040);
+        w[i] = __byte_perm(lo, hi, 0x5410);
+      }
+    } else {
+      pack_code_bits<W>(b, w);
+    }
+    uint32_t* dst = reinterpret_cast<uint32_t*>(row_stage + (2 * half + cc) * 4 * W);
+#pragma unroll
+    for (int k = 0; k < W; ++k) dst[k] = w[k];
+  }
+}
+
 __global__ void __launch_bounds__(kPThreads, 2) k_quant_tc(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   const PSmem S = psmem(smem_raw);
@@ -1240,8 +1310,10 @@ KVS_DEV void issue_tile_loads_warp(const LayerLaunch& L, const ItemCtx& c, const
 constexpr int kWsGroups = 2;
 constexpr int kWsGroupWarps = 8;
 constexpr int kWsGroupThreads = kWsGroupWarps * 32;
-constexpr int kWsCtrlWarp = kWsGroups * kWsGroupWarps;  // warp 16
-constexpr int kWsThreads = (kWsCtrlWarp + 1) * 32;       // 544
+constexpr int kWsCtrlWarp = kWsGroups * kWsGroupWarps;  // warp 16: MMAs (dequant: loads too)
+constexpr int kWsThreads = (kWsCtrlWarp + 1) * 32;       // 544 (dequantize kernel)
+constexpr int kWsLoadWarp = kWsCtrlWarp + 1;             // warp 17: TMA loads (stats, quant)
+constexpr int kWsProdThreads = (kWsLoadWarp + 1) * 32;   // 576 (stats, quantize kernels)
 constexpr int kWsMaxStages = 5;
 constexpr int kWsStagingBytes = 128 * 144;  // 128 rows x (W|1)*16 B for W <= 8
 // Layout from the 1024-aligned base: image | NS stages | staging (quant) |
@@ -1357,6 +1429,7 @@ KVS_DEV PJob ws_job(const WsMap& m, int k) {
 struct BoxDesc {
   const CUtensorMap* map;
   int y, z, phys, nload;  // y, z: TMA coordinates of (head, slot)
+  int num_blocks;         // phys is checked against it when the box is issued
   bool mine;
 };
 KVS_DEV BoxDesc box_desc(const LayerLaunch& L, ItemCursor& cur, const PJob& jb) {
@@ -1367,58 +1440,91 @@ KVS_DEV BoxDesc box_desc(const LayerLaunch& L, ItemCursor& cur, const PJob& jb) 
   d.map = map_of(L, c.slot, jb.plane);
   d.nload = min(8, (c.rows - c.row0 + 15) / 16);
   d.mine = lane < 2 * d.nload;
+  d.num_blocks = c.kv.num_blocks;
   d.y = d.z = d.phys = 0;
   if (d.mine) {
     const int rr = c.row0 + (lane >> 1) * 16;
     const int slot = rr % c.kv.block_size;
-    d.phys = load_block(L, c, rr);
+    d.phys = raw_block(L, c, rr);
     d.y = tma_y(c.kv, jb.h, slot);
     d.z = tma_z(c.kv, jb.h, slot);
   }
   return d;
 }
-KVS_DEV void issue_boxes(const BoxDesc& d, uint8_t* tile, uint64_t* bar) {
+KVS_DEV void issue_boxes(const BoxDesc& d, uint8_t* tile, uint64_t* bar, uint32_t* err) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(d.nload) * 4096u);
   __syncwarp();
   if (d.mine) {
+    int phys = d.phys;
+    if (static_cast<unsigned>(phys) >= static_cast<unsigned>(d.num_blocks)) {
+      record_error(err, ERR_BOUNDS);  // outside the cache: read block 0 instead
+      phys = 0;
+    }
     const int g = lane >> 1, hb = lane & 1;
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(tile + hb * 16384 + g * 2048)),
-        "l"(reinterpret_cast<uint64_t>(d.map)), "r"(hb * 64), "r"(d.y), "r"(d.z), "r"(d.phys),
+        "l"(reinterpret_cast<uint64_t>(d.map)), "r"(hb * 64), "r"(d.y), "r"(d.z), "r"(phys),
         "r"(smem_u32(bar))
         : "memory");
   }
   __syncwarp();
 }
 
-// Control warp: loads and MMAs for local jobs [0, n) over an NS-stage ring.
-// Iteration k: wait for job k's tile and a free accumulator, issue MMA k,
-// then refill the stage of job k-1 (its MMA finished during iteration k-1's
-// work) with the job NS-1 ahead, whose block ids were read one iteration
-// earlier.  All 32 lanes run the loop; lane 0 waits on barriers (result
-// broadcast) and issues the MMAs.  After a failed wait the warp stops
-// waiting and issuing but keeps committing, so every epilogue barrier still
-// completes; copies still in flight are drained (bounded) before it returns.
+// Load warp: TMA loads of local jobs [0, n) into the NS-stage ring.  Job j
+// goes into stage j % NS as soon as the MMA of job j - NS (the stage's
+// previous user) has retired; the block ids of job j + 1 are read while job
+// j's boxes are in flight, so an issue never waits on memory.  All 32 lanes
+// run the loop (lanes 0-15 issue one box each); lane 0 waits on barriers.
+// After a failed wait it stops issuing; before returning it waits (bounded)
+// for the copies it issued into the ring's last stages.
+template <int NS>
+KVS_DEV void ws_loader(const LayerLaunch& L, const WsSmem& S, const WsMap& M) {
+  const int n = M.n;
+  const int lane = threadIdx.x & 31;
+  ItemCursor ld;
+  cursor_init(ld);
+  auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
+    bool r = true;
+    if (lane == 0) r = mbar_wait(bar, parity, L.err, ERR_MBAR_TIMEOUT);
+    return __shfl_sync(0xFFFFFFFFu, r ? 1 : 0, 0) != 0;
+  };
+  int issued = 0;
+  BoxDesc next = box_desc(L, ld, ws_job(M, 0));
+  for (; issued < n; ++issued) {
+    const int st = issued % NS;
+    if (issued >= NS &&
+        !wait0(&S.sfree[st], static_cast<uint32_t>((issued / NS - 1) & 1)))
+      break;
+    issue_boxes(next, ws_stage(S, st), &S.full[st], L.err);
+    if (lane == 0) trace_mark(L, issued, 2);
+    if (issued + 1 < n) next = box_desc(L, ld, ws_job(M, issued + 1));
+  }
+  // Earlier jobs' copies landed before their stages were refilled.
+  if (lane == 0)
+    for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+      mbar_wait(&S.full[j % NS], static_cast<uint32_t>((j / NS) & 1), nullptr, 0);
+}
+
+// MMA warp: for local jobs [0, n), wait for the job's tile and a free
+// accumulator, issue its 128x128x128 MMA and commit the accumulator and the
+// stage.  The transform image is reloaded when the (layer slot, head)
+// changes, after the previous MMA has retired.  Lane 0 waits and issues.
+// After a failed wait it stops waiting and issuing but keeps committing, so
+// every epilogue and load barrier still completes.
 template <bool kStats, int NS>
-KVS_DEV void ws_control(const LayerLaunch& L, const WsSmem& S, uint32_t tmem, const WsMap& M) {
+KVS_DEV void ws_mma(const LayerLaunch& L, const WsSmem& S, uint32_t tmem, const WsMap& M) {
   const int H = L.num_heads;
   const int n = M.n;
   const int lane = threadIdx.x & 31;
-  ItemCursor ld, mm;  // cursors of the load stream and of the MMA stream
-  cursor_init(ld);
+  ItemCursor mm;
   cursor_init(mm);
   auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
     bool r = true;
     if (lane == 0) r = mbar_wait(bar, parity, L.err, ERR_MBAR_TIMEOUT);
     return __shfl_sync(0xFFFFFFFFu, r ? 1 : 0, 0) != 0;
   };
-  int issued = 0, consumed = 0;
-  for (; issued < NS && issued < n; ++issued)
-    issue_boxes(box_desc(L, ld, ws_job(M, issued)), ws_stage(S, issued), &S.full[issued]);
-  BoxDesc next{};
-  if (issued < n) next = box_desc(L, ld, ws_job(M, issued));
   int cur_img = -1;
   uint32_t img_phase = 0;
   bool ok = true;
@@ -1441,10 +1547,7 @@ KVS_DEV void ws_control(const LayerLaunch& L, const WsSmem& S, uint32_t tmem, co
       }
       cur_img = img_key;
     }
-    if (ok) {
-      ok = wait0(&S.full[st], static_cast<uint32_t>((k / NS) & 1));
-      if (ok) ++consumed;
-    }
+    if (ok) ok = wait0(&S.full[st], static_cast<uint32_t>((k / NS) & 1));
     if (lane == 0) trace_mark(L, k, 0);
     if (ok && k >= 4) ok = wait0(&S.afree[a], static_cast<uint32_t>(((k >> 2) - 1) & 1));
     if (lane == 0) trace_mark(L, k, 5);
@@ -1463,24 +1566,11 @@ KVS_DEV void ws_control(const LayerLaunch& L, const WsSmem& S, uint32_t tmem, co
       trace_mark(L, k, 1);
     }
     __syncwarp();
-    if (k >= 1 && issued < n && ok) {  // refill the stage job k-1 used
-      const int ps = (k - 1) % NS;
-      ok = wait0(&S.sfree[ps], static_cast<uint32_t>(((k - 1) / NS) & 1));
-      if (ok) {
-        issue_boxes(next, ws_stage(S, ps), &S.full[ps]);
-        if (lane == 0) trace_mark(L, issued, 2);
-        ++issued;
-        if (issued < n) next = box_desc(L, ld, ws_job(M, issued));
-      }
-    }
   }
-  if (lane == 0)
-    for (int k = consumed; k < issued; ++k)
-      mbar_wait(&S.full[k % NS], static_cast<uint32_t>((k / NS) & 1), nullptr, 0);
 }
 
 // ------------------------------------------------------------ stats (ws)
-__global__ void __launch_bounds__(kWsThreads, 1) k_stats_ws(LayerLaunch L) {
+__global__ void __launch_bounds__(kWsProdThreads, 1) k_stats_ws(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   constexpr int NS = 5;
   const WsSmem S = ws_smem<WsStatsLayout>(smem_raw);
@@ -1496,7 +1586,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_stats_ws(LayerLaunch L) {
   tc_fence_after();
   const uint32_t tmem = *S.tslot;
   if (warp == kWsCtrlWarp) {
-    ws_control<true, NS>(L, S, tmem, M);
+    ws_mma<true, NS>(L, S, tmem, M);
+  } else if (warp == kWsLoadWarp) {
+    ws_loader<NS>(L, S, M);
   } else {
     const int g = warp / kWsGroupWarps, gw = warp % kWsGroupWarps;
     const int quad = gw & 3, half = gw >> 2;
@@ -1583,7 +1675,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_stats_ws(LayerLaunch L) {
 }
 
 // ------------------------------------------------------------ quant (ws)
-__global__ void __launch_bounds__(kWsThreads, 1) k_quant_ws(LayerLaunch L) {
+__global__ void __launch_bounds__(kWsProdThreads, 1) k_quant_ws(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   constexpr int NS = 4;
   const WsSmem S = ws_smem<WsQuantLayout>(smem_raw);
@@ -1599,13 +1691,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_quant_ws(LayerLaunch L) {
   tc_fence_after();
   const uint32_t tmem = *S.tslot;
   if (warp == kWsCtrlWarp) {
-    ws_control<false, NS>(L, S, tmem, M);
+    ws_mma<false, NS>(L, S, tmem, M);
+  } else if (warp == kWsLoadWarp) {
+    ws_loader<NS>(L, S, M);
   } else {
     const int g = warp / kWsGroupWarps, gw = warp % kWsGroupWarps;
     const int gtid = tid - g * kWsGroupThreads;
     const int quad = gw & 3, half = gw >> 2;
     const int lane_id = quad * 32 + lane;  // TMEM lane = tile row
-    float* kp = ws_kp(S, g);               // [128][2] key (min, rcp)
+    float* kp = ws_kp(S, g);  // key (min, min, rcp, rcp) per channel pair
     uint8_t* stage = ws_staging(S, g);
     ItemCursor cur;
     cursor_init(cur);
@@ -1641,7 +1735,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_quant_ws(LayerLaunch L) {
       if (jb.plane == 0 && (pk != kp_key || c.row0 == 0)) {  // row0 == 0 publishes the metadata
         // kp's readers of an earlier job finished before that job's staging
         // barrier, which this thread has passed
-        if (gtid < 128) key_channel_params(L, c, jb.h, kp, kp + 1, 2, gtid);
+        if (gtid < 128) key_channel_params(L, c, jb.h, kp, kp, 0, gtid, true);
         kp_key = pk;
       }
       // key parameters visible; every thread finished copying out the
@@ -1660,19 +1754,21 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_quant_ws(LayerLaunch L) {
                              (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
       const float sc = c.lp->out_scale;
       switch (bits) {
-        case 1: p_quant_half<1>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        case 2: p_quant_half<2>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        case 3: p_quant_half<3>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        case 4: p_quant_half<4>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        case 5: p_quant_half<5>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        case 6: p_quant_half<6>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        case 7: p_quant_half<7>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
-        default: p_quant_half<8>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 1: ws_quant_half<1>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 2: ws_quant_half<2>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 3: ws_quant_half<3>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 4: ws_quant_half<4>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 5: ws_quant_half<5>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 6: ws_quant_half<6>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        case 7: ws_quant_half<7>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
+        default: ws_quant_half<8>(taddr, sc, top, valid, jb.plane, vmin, vrcp, kp, half, row_stage); break;
       }
+      if (gw == 0 && lane == 0) trace_mark(L, k, 6);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.afree[a]);
       group_sync(g);  // staging complete
+      if (gw == 0 && lane == 0) trace_mark(L, k, 7);
       // Coalesced 16-byte copy of the tile's contiguous code region.
       const int nrows = min(kTileRows, c.rows - c.row0);
       uint8_t* dst0 = code_row(L, c, jb.plane, jb.h, c.row0);
@@ -2282,7 +2378,7 @@ int kvs_stats(const LayerLaunch* Lp) {
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
     if (int rc = set_smem(k_stats_ws, WsStatsLayout::kSmem)) return rc;
-    k_stats_ws<<<ws_grid(L), kWsThreads, WsStatsLayout::kSmem, s>>>(L);
+    k_stats_ws<<<ws_grid(L), kWsProdThreads, WsStatsLayout::kSmem, s>>>(L);
   } else if (L.engine == 3) {
     if (int rc = set_smem(k_stats_tc, kPSmem)) return rc;
     k_stats_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
@@ -2304,7 +2400,7 @@ int kvs_quant(const LayerLaunch* Lp) {
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
     if (int rc = set_smem(k_quant_ws, WsQuantLayout::kSmem)) return rc;
-    k_quant_ws<<<ws_grid(L), kWsThreads, WsQuantLayout::kSmem, s>>>(L);
+    k_quant_ws<<<ws_grid(L), kWsProdThreads, WsQuantLayout::kSmem, s>>>(L);
   } else if (L.engine == 3) {
     if (int rc = set_smem(k_quant_tc, kPSmem)) return rc;
     k_quant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);

@@ -582,7 +582,7 @@ class RequestBatch:
 # Device trace of the warp-specialized kernels (diagnostics; off by default).
 TRACE_CTAS = 4
 TRACE_EVENTS = ("tile_ready", "mma_issued", "refill_issued", "epi_mma_seen", "epi_done",
-                "acc_free_seen", "unused6", "unused7")
+                "acc_free_seen", "epi_quantized", "epi_staged")
 _trace = {"buf": None, "jobs": 0}
 
 
