@@ -1852,6 +1852,68 @@ KVS_DEV void p_unpack_group(const uint8_t* src, int t, int part, int kv, const f
   }
 }
 
+// Warp-specialized form of p_unpack_group: codes come from the job's code
+// tile in shared memory (staged by a bulk copy), the arithmetic runs on
+// value pairs (f32x2), and key parameters are read in the pair layout
+// kq[p] = (scale(2p), scale(2p+1), -2^23*scale(2p), -2^23*scale(2p+1)),
+// km[p] = (min(2p), min(2p+1)).  Results are identical to p_unpack_group's.
+template <int W>
+KVS_DEV void ws_unpack_group(const uint8_t* src, int t, int part, int kv, const float4* kq,
+                             const float2* km, float vmn, float vsc, uint8_t* sA) {
+  uint32_t w[8];
+  if constexpr (W == 8 || W == 4) {  // 4W-byte groups are 16-byte aligned
+#pragma unroll
+    for (int k = 0; k < W / 4; ++k) {
+      const uint4 u = reinterpret_cast<const uint4*>(src)[k];
+      w[4 * k] = u.x;
+      w[4 * k + 1] = u.y;
+      w[4 * k + 2] = u.z;
+      w[4 * k + 3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < W; ++k) w[k] = reinterpret_cast<const uint32_t*>(src)[k];
+  }
+  uint32_t fb[32];  // bits of 2^23 + q
+  if constexpr (W == 8) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      fb[k] = __byte_perm(w[k >> 2], 0x4B000000u, 0x7650u | (k & 3));
+  } else {
+    uint32_t q[32];
+    unpack32<W>(w, q);
+#pragma unroll
+    for (int k = 0; k < 32; ++k) fb[k] = q[k] | 0x4B000000u;
+  }
+  const f32x2_t vsc2 = f2_pack(vsc, vsc), vneg2 = f2_pack(-8388608.0f * vsc, -8388608.0f * vsc);
+  const f32x2_t vmn2 = f2_pack(vmn, vmn);
+#pragma unroll
+  for (int c8 = 0; c8 < 4; ++c8) {
+    uint32_t o[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int k = c8 * 8 + 2 * p;
+      f32x2_t sc2 = vsc2, neg2 = vneg2, mn2 = vmn2;
+      if (kv == 0) {
+        const float4 q = kq[(part * 32 + k) >> 1];
+        const float2 m = km[(part * 32 + k) >> 1];
+        sc2 = f2_pack(q.x, q.y);
+        neg2 = f2_pack(q.z, q.w);
+        mn2 = f2_pack(m.x, m.y);
+      }
+      float a, b;
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(fb[k]), __uint_as_float(fb[k + 1])), sc2, neg2),
+                a, b);
+      const uint32_t prod = cvt_bf16x2(a, b);
+      float c0, c1;
+      f2_unpack(f2_add(f2_pack(bf16lo_to_float(prod), bf16hi_to_float(prod)), mn2), c0, c1);
+      o[p] = cvt_bf16x2(c0, c1);
+    }
+    *reinterpret_cast<uint4*>(sA + sw128_offset(t, part * 32 + c8 * 8)) =
+        make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   const PSmem S = psmem(smem_raw);
@@ -2033,11 +2095,15 @@ __global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
 //   afree[b]   tcgen05.commit after MMA k: A tile b and the image are free;
 //   dmma[b]    tcgen05.commit after MMA k: accumulator b holds job k;
 //   accfree[b] 8 epilogue-warp arrivals: accumulator b has been read.
+// image | A tiles [2] | output tiles [2] | code tiles [2] (128 rows x 128 B
+// at most) | value (min, scale) rows [2] | barriers | key parameters
 constexpr int kDqOffA = 32768;
 constexpr int kDqOffO = kDqOffA + 2 * 32768;
-constexpr int kDqOffBars = kDqOffO + 2 * 32768;
+constexpr int kDqOffC = kDqOffO + 2 * 32768;
+constexpr int kDqOffVm = kDqOffC + 2 * 16384;
+constexpr int kDqOffBars = kDqOffVm + 2 * 512;
 constexpr int kDqOffKp = kDqOffBars + 256;
-constexpr int kDqSmem = kDqOffKp + 128 * 4 * 4 + 1024;
+constexpr int kDqSmem = kDqOffKp + 64 * 16 + 64 * 8 + 1024;
 static_assert(kDqSmem <= 227 * 1024, "dequant ws shared memory");
 
 __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
@@ -2051,7 +2117,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
   uint64_t* accfree = bars + 6;  // [2]
   uint64_t* imgb = bars + 8;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 9);
-  float* kp = reinterpret_cast<float*>(base + kDqOffKp);  // [128][4] key (min, scale, -2^23*scale, 0)
+  uint64_t* cfull = bars + 10;   // [2] code tile (and value rows) landed
+  uint64_t* cfree = bars + 12;   // [2] unpack finished reading them
+  float4* kq = reinterpret_cast<float4*>(base + kDqOffKp);         // [64] key scale pairs
+  float2* km = reinterpret_cast<float2*>(base + kDqOffKp + 1024);  // [64] key min pairs
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = L.num_heads;
   const WsMap M = ws_map(L);
@@ -2063,6 +2132,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       mbar_init(&afree[b], 1);
       mbar_init(&dmma[b], 1);
       mbar_init(&accfree[b], kWsGroupWarps);
+      mbar_init(&cfull[b], 1);
+      mbar_init(&cfree[b], kWsGroupWarps);
     }
     mbar_init(imgb, 1);
     fence_mbar_init();
@@ -2074,6 +2145,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
   const uint32_t tmem = *tslot;
   auto abuf = [&](int b) { return base + kDqOffA + 32768 * b; };
   auto obuf = [&](int b) { return base + kDqOffO + 32768 * b; };
+  auto cbuf = [&](int b) { return base + kDqOffC + 16384 * b; };
+  auto vmbuf = [&](int b) { return reinterpret_cast<__half*>(base + kDqOffVm + 512 * b); };
 
   if (warp < kWsGroupWarps) {
     // ------------------------------------------------------------ unpack
@@ -2088,13 +2161,17 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       if (k >= 2)  // MMA k-2 finished reading A tile b
         mbar_wait(&afree[b], static_cast<uint32_t>(((k >> 1) - 1) & 1), L.err, ERR_MBAR_TIMEOUT);
       group_sync(0);  // every unpack thread finished job k-1 (kp may change)
+      if (tid == 0) trace_mark(L, k, 0);
       const int pk = c.r * H + jb.h;
       if (jb.plane == 0 && pk != kp_key) {
         if (tid < 128) {
           const __half* m = meta_base(L, c.r);
           const float mn = bf16_round(__half2float(m[jb.h * 128 + tid]));
           const float sc = bf16_round(__half2float(m[c.lp->H * 128 + jb.h * 128 + tid]));
-          *reinterpret_cast<float4*>(kp + 4 * tid) = make_float4(mn, sc, -8388608.0f * sc, 0.f);
+          float* q = reinterpret_cast<float*>(kq + (tid >> 1));
+          q[tid & 1] = sc;
+          q[2 + (tid & 1)] = -8388608.0f * sc;
+          reinterpret_cast<float*>(km + (tid >> 1))[tid & 1] = mn;
         }
         kp_key = pk;
         group_sync(0);  // key parameters visible
@@ -2102,28 +2179,28 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       uint8_t* sA = abuf(b);
       const int bits = seg_bits(c, jb.plane, jb.h);
       const int nrows = min(kTileRows, c.rows - c.row0);
-      const uint8_t* src0 = code_row(L, c, jb.plane, jb.h, c.row0);
-      const __half* meta = meta_base(L, c.r);
-      const int Hh = c.lp->H, G = c.lp->n_groups, grp = c.lp->group_of_head[jb.h];
+      const uint8_t* src0 = cbuf(b);
+      const __half* vm = vmbuf(b);  // [0, 128): group min of the tile's rows, [128, 256): scale
+      mbar_wait(&cfull[b], static_cast<uint32_t>((k >> 1) & 1), L.err, ERR_MBAR_TIMEOUT);
       for (int g = tid; g < kTileRows * 4; g += kWsGroupThreads) {
         const int t = g & (kTileRows - 1), part = g >> 7;
         const int row = c.row0 + t;
         if (t < nrows && row < c.ntok) {
           float vmn = 0.f, vsc = 0.f;
           if (jb.plane == 1) {
-            vmn = bf16_round(__half2float(meta[2 * Hh * 128 + grp * c.rows + row]));
-            vsc = bf16_round(__half2float(meta[2 * Hh * 128 + G * c.rows + grp * c.rows + row]));
+            vmn = bf16_round(__half2float(vm[t]));
+            vsc = bf16_round(__half2float(vm[128 + t]));
           }
-          const uint8_t* src = src0 + static_cast<long long>(t) * 16 * bits + part * 4 * bits;
+          const uint8_t* src = src0 + t * 16 * bits + part * 4 * bits;
           switch (bits) {
-            case 1: p_unpack_group<1>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            case 2: p_unpack_group<2>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            case 3: p_unpack_group<3>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            case 4: p_unpack_group<4>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            case 5: p_unpack_group<5>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            case 6: p_unpack_group<6>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            case 7: p_unpack_group<7>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
-            default: p_unpack_group<8>(src, t, part, jb.plane, kp, vmn, vsc, sA); break;
+            case 1: ws_unpack_group<1>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 2: ws_unpack_group<2>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 3: ws_unpack_group<3>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 4: ws_unpack_group<4>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 5: ws_unpack_group<5>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 6: ws_unpack_group<6>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 7: ws_unpack_group<7>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            default: ws_unpack_group<8>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
           }
         } else {
 #pragma unroll
@@ -2132,9 +2209,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
                 make_uint4(0, 0, 0, 0);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&cfree[b]);  // code tile b may be refilled
       fence_proxy_async_smem();  // generic writes of A tile b before the MMA reads it
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[b]);
+      if (tid == 0) trace_mark(L, k, 1);
     }
   } else if (warp < kWsCtrlWarp) {
     // ---------------------------------------------------------- epilogue
@@ -2148,10 +2228,18 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       const PJob jb = ws_job(M, k);
       cursor_seek(L, cur, jb.tile);
       const ItemCtx& c = cur.c;
+      // lane l < 16 of warp 0 stores box (row group l/2, channel half l%2);
+      // its block-table entry is read now so the load overlaps the epilogue
+      const int nst = min(kTileRows, c.ntok - c.row0);  // rows holding tokens
+      const int sg = lane >> 1, shb = lane & 1;
+      const int srow = c.row0 + sg * 16;
+      const bool sbox = ew == 0 && lane < 16 && sg * 16 < nst;
+      const int sphys = sbox ? raw_block(L, c, srow) : 0;
       if (ew == 0)  // the stores that read output tile b (job k-2) have finished reading
         asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
       group_sync(1);
       mbar_wait(&dmma[b], static_cast<uint32_t>((k >> 1) & 1), L.err, ERR_MBAR_TIMEOUT);
+      if (ew == 0 && lane == 0) trace_mark(L, k, 3);
       tc_fence_after();
       uint8_t* sO = obuf(b);
       const uint32_t taddr = tmem + static_cast<uint32_t>(b * 128) +
@@ -2177,24 +2265,21 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       fence_proxy_async_smem();  // generic writes of output tile b before the TMA store
       group_sync(1);
       if (ew == 0) {
-        // lane l < 16 stores box (row group l/2, channel half l%2): the
-        // block-table reads of the 16 boxes overlap; every lane commits its
-        // own (possibly empty) bulk group
-        const int nst = min(kTileRows, c.ntok - c.row0);  // rows holding tokens
-        const int g = lane >> 1, hb = lane & 1;
-        const int rr = c.row0 + g * 16;
-        const int phys = (lane < 16 && g * 16 < nst) ? phys_block(L, c, rr) : -1;
-        if (phys >= 0) {  // a bad block id is recorded and its box skipped
+        // every lane commits its own (possibly empty) bulk group
+        if (sbox && static_cast<unsigned>(sphys) >= static_cast<unsigned>(c.kv.num_blocks)) {
+          record_error(L.err, ERR_BOUNDS);  // outside the cache: the box is skipped
+        } else if (sbox) {
           const CUtensorMap* map = map_of(L, c.slot, jb.plane);
-          const int slot = rr % c.kv.block_size;
+          const int slot = srow % c.kv.block_size;
           asm volatile(
               "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::
                   "l"(reinterpret_cast<uint64_t>(map)),
-              "r"(hb * 64), "r"(tma_y(c.kv, jb.h, slot)), "r"(tma_z(c.kv, jb.h, slot)),
-              "r"(phys), "r"(smem_u32(sO + hb * 16384 + g * 2048))
+              "r"(shb * 64), "r"(tma_y(c.kv, jb.h, slot)), "r"(tma_z(c.kv, jb.h, slot)),
+              "r"(sphys), "r"(smem_u32(sO + shb * 16384 + sg * 2048))
               : "memory");
         }
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        if (lane == 0) trace_mark(L, k, 4);
       }
     }
     if (ew == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -2223,7 +2308,35 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
                      "r"(bytes)
                      : "memory");
     };
+    ItemCursor ccur;
+    cursor_init(ccur);
+    // Code tile of job kk (and, for values, the group min / scale of its
+    // rows) into buffer kk & 1.  After a failed wait only the arrival is
+    // made, so the unpack warps never wait past their limit.
+    auto issue_codes = [&](int kk) {
+      const int cb = kk & 1;
+      const PJob jn = ws_job(M, kk);
+      cursor_seek(L, ccur, jn.tile);
+      const ItemCtx& c = ccur.c;
+      if (lane != 0) return;
+      if (!ok) {
+        mbar_arrive(&cfull[cb]);
+        return;
+      }
+      const int nrows = min(kTileRows, c.rows - c.row0);
+      const uint32_t cbytes = static_cast<uint32_t>(nrows * 16 * seg_bits(c, jn.plane, jn.h));
+      const uint32_t vbytes = jn.plane == 1 ? static_cast<uint32_t>(nrows * 2) : 0u;
+      mbar_arrive_expect_tx(&cfull[cb], cbytes + 2 * vbytes);
+      bulk_load(cbuf(cb), code_row(L, c, jn.plane, jn.h, c.row0), cbytes, &cfull[cb]);
+      if (vbytes) {
+        const __half* meta = meta_base(L, c.r) + 2 * c.lp->H * 128;
+        const int G = c.lp->n_groups, grp = c.lp->group_of_head[jn.h];
+        bulk_load(vmbuf(cb), meta + grp * c.rows + c.row0, vbytes, &cfull[cb]);
+        bulk_load(vmbuf(cb) + 128, meta + (G + grp) * c.rows + c.row0, vbytes, &cfull[cb]);
+      }
+    };
     for (int k = 0; k < 3 && k < n; ++k) prefetch(k);
+    for (int k = 0; k < 2 && k < n; ++k) issue_codes(k);
     for (int k = 0; k < n; ++k) {
       const int b = k & 1;
       const PJob jb = ws_job(M, k);
@@ -2244,6 +2357,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
         cur_img = img_key;
       }
       if (ok) ok = wait0(&afull[b], static_cast<uint32_t>((k >> 1) & 1));
+      if (lane == 0) trace_mark(L, k, 5);
       if (ok && k >= 2) ok = wait0(&accfree[b], static_cast<uint32_t>(((k >> 1) - 1) & 1));
       if (lane == 0) {
         if (ok) {
@@ -2254,8 +2368,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
         }
         umma_commit(&dmma[b]);
         umma_commit(&afree[b]);
+        trace_mark(L, k, 2);
       }
       __syncwarp();
+      if (k + 2 < n) {  // job k's unpack has read code buffer b: refill it
+        if (ok) ok = wait0(&cfree[b], static_cast<uint32_t>((k >> 1) & 1));
+        issue_codes(k + 2);
+      }
     }
   }
   tc_fence_before();
@@ -2419,10 +2538,14 @@ int kvs_dequant_inverse(const LayerLaunch* Lp) {
   if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
-  if (L.engine == 0) {
+  // k_dequant_ws bulk-copies code tiles and metadata rows: their bases must
+  // be 16-byte aligned (item offsets are); otherwise the persistent kernel runs
+  const bool aligned = ((reinterpret_cast<uintptr_t>(L.codes) |
+                         reinterpret_cast<uintptr_t>(L.meta)) & 15) == 0;
+  if (L.engine == 0 && aligned) {
     if (int rc = set_smem(k_dequant_ws, kDqSmem)) return rc;
     k_dequant_ws<<<ws_grid(L), kWsThreads, kDqSmem, s>>>(L);
-  } else if (L.engine == 3) {
+  } else if (L.engine == 3 || L.engine == 0) {
     if (int rc = set_smem(k_dequant_tc, kPSmem)) return rc;
     k_dequant_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
   } else if (L.engine == 2) {

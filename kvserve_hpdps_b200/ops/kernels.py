@@ -494,6 +494,9 @@ class WorkItems:
             m += _align16(plan.meta_bytes(rows))
             ro += rows
         self.code_bytes, self.meta_bytes, self.total_rows = c, m, ro
+        for offs in (code_offsets, meta_offsets):
+            if offs is not None and any(int(o) % 16 for o in offs):
+                raise ValueError("item code / metadata offsets must be multiples of 16 bytes")
         if code_offsets is not None:
             if len(code_offsets) != R:
                 raise ValueError("one code offset per item is required")
@@ -583,6 +586,9 @@ class RequestBatch:
 TRACE_CTAS = 4
 TRACE_EVENTS = ("tile_ready", "mma_issued", "refill_issued", "epi_mma_seen", "epi_done",
                 "acc_free_seen", "epi_quantized", "epi_staged")
+# the dequantize kernel's events, same slots
+TRACE_EVENTS_DEQUANT = ("unpack_start", "unpack_done", "mma_issued", "epi_mma_seen",
+                        "epi_stores_issued", "a_full_seen", "unused6", "unused7")
 _trace = {"buf": None, "jobs": 0}
 
 
