@@ -9,14 +9,17 @@ framework's own:
   (sm_100a kernels) or the CPU (same byte stream);
 * ``"bitpack"``: fixed-width packing at ceil(log2(max+1)) bits of the byte
   stream (lossless for any input);
+* ``"lc"``: LC-style BIT_2 (16-bit bit-plane shuffle) + RZE_1 (zero-byte
+  elimination) after the published LC stages, this framework's own device
+  kernels and numpy reference (the reference calls a closed external
+  library for ``codec_type: "lc"``);
 * ``"none"``: raw bytes.
 
-The reference's closed nvCOMP algorithms and the external LC library are
-not used.  Their names map to the nearest own codec: ``nvcomp``/``ANS``,
-``nvcomp``/``Cascaded``, ``Deflate``, ``GDeflate``, ``LZ4``, ``Zstd`` and
-``lc`` -> ``rans``; ``nvcomp``/``Bitcomp`` -> ``bitpack``.  The resolved
-codec is recorded in the stream header, so decoding never depends on the
-configured name.
+The reference's closed nvCOMP algorithms are not used.  Their names map to
+the nearest own codec: ``nvcomp``/``ANS``, ``Cascaded``, ``Deflate``,
+``GDeflate``, ``LZ4``, ``Zstd`` -> ``rans``; ``nvcomp``/``Bitcomp`` ->
+``bitpack``.  The resolved codec is recorded in the stream header, so
+decoding never depends on the configured name.
 
 Encoded stream = 16-byte header ``[magic u32 'KVC1', codec u32, n u64]``
 followed by the codec payload (for ``bitpack`` one more 16-byte block
@@ -34,7 +37,7 @@ import torch
 from kvserve_hpdps_b200.compression.components import Codec
 
 MAGIC = 0x3143564B  # "KVC1"
-CODEC_IDS = {"none": 0, "rans": 1, "bitpack": 2}
+CODEC_IDS = {"none": 0, "rans": 1, "bitpack": 2, "lc": 3}
 CODEC_NAMES = {v: k for k, v in CODEC_IDS.items()}
 
 _NVCOMP_ALGOS = ("ANS", "Bitcomp", "Cascaded", "Deflate", "GDeflate", "LZ4", "Zstd")
@@ -43,10 +46,8 @@ _NVCOMP_ALGOS = ("ANS", "Bitcomp", "Cascaded", "Deflate", "GDeflate", "LZ4", "Zs
 def resolve_codec(codec_type: Optional[str], algorithm: Optional[str] = None) -> str:
     """Map a reference or own codec name to one of none | rans | bitpack."""
     ct = (codec_type or "nvcomp").lower()
-    if ct in ("rans", "bitpack", "none"):
+    if ct in ("rans", "bitpack", "none", "lc"):
         return ct
-    if ct == "lc":
-        return "rans"
     if ct == "nvcomp":
         algo = algorithm or "ANS"
         if algo not in _NVCOMP_ALGOS:
@@ -84,6 +85,8 @@ def encode_bytes(data: torch.Tensor, codec: str) -> torch.Tensor:
         return torch.cat([hdr, src])
     if codec == "rans":
         return torch.cat([hdr, K.rans_encode(src)])
+    if codec == "lc":
+        return torch.cat([hdr, K.lc_encode(src)])
     if codec == "bitpack":
         mx = int(src.max().item())
         bits = max(1, math.ceil(math.log2(mx + 1))) if mx > 0 else 1
@@ -108,6 +111,8 @@ def decode_bytes(stream: torch.Tensor, device=None) -> torch.Tensor:
         return body[:n].contiguous()
     if codec == "rans":
         return K.rans_decode(body.contiguous(), n)
+    if codec == "lc":
+        return K.lc_decode(body, n)
     if codec == "bitpack":
         bits = int(body[0].item())
         rows = (n + 127) // 128
@@ -171,9 +176,9 @@ class KVServeCodec(Codec):
         return raw.view(dtype).reshape([int(s) for s in original_shape])
 
 
-# Reference-compatible alias for the external LC codec slot.
+# Reference-compatible class for the LC codec slot.
 class LCCodec(KVServeCodec):
-    """``codec_type: "lc"`` slot; encodes with the own rANS codec."""
+    """``codec_type: "lc"``: BIT_2 + RZE_1 (see :mod:`compression.lc`)."""
 
     def __init__(self, **kwargs: Any):
         kwargs = dict(kwargs)

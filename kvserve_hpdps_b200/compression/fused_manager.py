@@ -84,7 +84,7 @@ class FusedCompressionManager:
         self.codec = resolve_codec(self.codec_config.get("codec_type", "nvcomp"),
                                    self.codec_config.get("nvcomp_algorithm", "ANS"))
         self.packed = self.codec == "bitpack"
-        self.stream_codec = "rans" if self.codec == "rans" else "none"
+        self.stream_codec = self.codec if self.codec in ("rans", "lc") else "none"
         # With the entropy coder, codes are stored as 4-bit nibbles (two codes
         # per coded byte): half the symbols for the coder at the same
         # compression ratio.  codec_config["symbol_bits"] = 8 keeps byte codes.

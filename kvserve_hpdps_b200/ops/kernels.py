@@ -832,6 +832,49 @@ def rans_max_bytes(n: int, chunk: int = RANS_CHUNK) -> int:
     return int(lib().kvs_rans_max_bytes(n, chunk))
 
 
+def lc_encode(data: torch.Tensor, trim: bool = True) -> torch.Tensor:
+    """LC-style (BIT_2 + RZE_1) stream of the bytes of ``data`` (format in
+    ``csrc/lc_codec.cu``).  CUDA: three launches; with ``trim`` the host
+    reads the stream size (one synchronisation).  CPU: the numpy reference,
+    which writes the identical stream."""
+    from kvserve_hpdps_b200.compression import lc as lc_ref
+    src = data.contiguous().view(torch.uint8).reshape(-1)
+    n = src.numel()
+    if n == 0:
+        raise ValueError("empty input")
+    if src.device.type == "cpu":
+        return torch.from_numpy(lc_ref.encode(src.numpy()))
+    dev = src.device
+    lb = lib()
+    ws = workspace(dev)
+    out = torch.empty(int(lb.kvs_lc_max_bytes(n)), dtype=torch.uint8, device=dev)
+    staging = ws.buf("lc_staging", int(lb.kvs_lc_staging_bytes(n)))
+    nchunks = (n + lc_ref.CHUNK - 1) // lc_ref.CHUNK
+    rec_len = ws.buf("lc_len", 4 * nchunks, torch.int32)
+    total = ws.buf("lc_total", 8, torch.int64)
+    check(lb.kvs_lc_encode(src.data_ptr(), n, staging.data_ptr(), rec_len.data_ptr(),
+                           out.data_ptr(), total.data_ptr(), _stream(dev)), "lc_encode")
+    if trim:
+        _xfer["d2h"] += 8
+        return out[:int(total[0].item())]
+    return out
+
+
+def lc_decode(stream: torch.Tensor, n: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Bytes of an LC stream; a corrupt stream records ERR_CORRUPT in the
+    device error word (CUDA) or raises ValueError (CPU)."""
+    from kvserve_hpdps_b200.compression import lc as lc_ref
+    if stream.device.type == "cpu":
+        return torch.from_numpy(lc_ref.decode(stream.contiguous().numpy(), int(n)))
+    dev = stream.device
+    if out is None:
+        out = torch.empty(int(n), dtype=torch.uint8, device=dev)
+    s = stream.contiguous()
+    check(lib().kvs_lc_decode(s.data_ptr(), s.numel(), out.data_ptr(), int(n),
+                              workspace(dev).err.data_ptr(), _stream(dev)), "lc_decode")
+    return out
+
+
 def rans_encode(data: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: int = RANS_CHUNK,
                 flag: Optional[torch.Tensor] = None, flag_value: int = 0,
                 trim: bool = True) -> torch.Tensor:

@@ -120,12 +120,33 @@ def test_codec_stage_roundtrip_cpu(codec):
 def test_codec_name_mapping():
     assert C.resolve_codec("nvcomp", "ANS") == "rans"
     assert C.resolve_codec("nvcomp", "Bitcomp") == "bitpack"
-    assert C.resolve_codec("lc") == "rans"
+    assert C.resolve_codec("lc") == "lc"
     with pytest.raises(ValueError):
         C.resolve_codec("nvcomp", "Brotli")
     codec = C.KVServeCodec(codec_type="nvcomp", nvcomp_algorithm="ANS", data_type="|u1")
     x = torch.randint(0, 5, (1000,), dtype=torch.uint8)
     assert torch.equal(codec.decode(0, codec.encode(0, x), "uint8", [1000], "cpu"), x)
+
+
+@pytest.mark.parametrize("n", [1, 63, 16384, 16385, 70000])
+def test_lc_codec_round_trip_and_format(n):
+    """BIT_2 + RZE_1: lossless at any size; small codes compress, random
+    bytes fall back to raw chunks; the stream names its codec."""
+    from kvserve_hpdps_b200.compression import lc
+    g = torch.Generator().manual_seed(n)
+    x = torch.randint(0, 16, (n,), generator=g, dtype=torch.uint8)
+    codec = C.LCCodec()
+    enc = codec.encode(0, x)
+    assert C.parse_header(enc) == ("lc", n)
+    assert torch.equal(codec.decode(0, enc, "uint8", [n], "cpu"), x)
+    if n >= 16384:
+        assert enc.numel() < 0.7 * n
+    r = torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8)
+    s = lc.encode(r.numpy())
+    assert s.size <= lc.max_bytes(n)
+    assert torch.equal(torch.from_numpy(lc.decode(s, n)), r)
+    with pytest.raises(ValueError):
+        lc.decode(s[:16], n)
 
 
 def test_bitpack_matches_native_layout():

@@ -88,6 +88,26 @@ def test_grouped_message_round_trip_and_members():
         assert int(untouched.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("codec", ["lc", "bitpack", "none"])
+def test_paged_message_round_trip_other_codecs(codec):
+    """The grouped paged message with the LC, bitpack and raw stream codecs
+    reconstructs what the plain paged round trip reconstructs."""
+    L = 2
+    src, dst, _, reqs, dreqs = _setup(L)
+    mgr = FusedCompressionManager(4, 128, QC, {"codec_type": codec}, num_layers=28)
+    ref = _expected(mgr, src, reqs, L)
+    cd = mgr.compress_paged_requests([src.cache[l] for l in range(L)], list(range(L)), reqs,
+                                     member_tids=["a", "b", "c"])
+    back = restore_from_wire(build_wire(cd))
+    mgr.decompress_paged_requests(back, [dst.cache[l] for l in range(L)], dreqs)
+    torch.cuda.synchronize()
+    for (sb, t), (db, _) in zip(reqs, dreqs):
+        for l in range(L):
+            a = gather_request(ref[l], sb).view(2, -1, 4, 128)[:, :t]
+            b = gather_request(dst.cache[l], db).view(2, -1, 4, 128)[:, :t]
+            assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("symbol_bits", [4, 8])
 def test_dense_and_layer_group_apis_match_paged_round_trip(symbol_bits):
     """The reference-compatible dense APIs (whole request, per-layer groups of

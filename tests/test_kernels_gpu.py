@@ -516,3 +516,30 @@ def test_bad_block_id_is_recorded_not_followed(engine):
     K.quantize(slots, items, engine=engine)
     torch.cuda.synchronize()
     assert K.read_device_error(layer.device) == 3
+
+
+@pytest.mark.parametrize("n", [1, 1000, 16384, 16385, 300000])
+def test_lc_gpu_matches_cpu_reference(n):
+    """Device BIT_2 + RZE_1 writes the numpy reference's stream byte for byte
+    and decodes it; a corrupt stream records ERR_CORRUPT instead of reading
+    outside it."""
+    from kvserve_hpdps_b200.compression import lc
+    g = torch.Generator().manual_seed(n)
+    x = torch.randint(0, 16, (n,), generator=g, dtype=torch.uint8)
+    x[: n // 3] = torch.randint(0, 256, (n // 3,), generator=g, dtype=torch.uint8)  # raw chunks too
+    ref = torch.from_numpy(lc.encode(x.numpy()))
+    s = K.lc_encode(x.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(s.cpu(), ref)
+    out = K.lc_decode(s, n)
+    torch.cuda.synchronize()
+    assert K.read_device_error(out.device) == 0
+    assert torch.equal(out.cpu(), x)
+    bad = s.clone()
+    bad[0] ^= 0xFF
+    K.lc_decode(bad, n)
+    torch.cuda.synchronize()
+    assert K.read_device_error(out.device) == 4
+    K.lc_decode(s[:32], n)
+    torch.cuda.synchronize()
+    assert K.read_device_error(out.device) == 4
