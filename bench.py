@@ -391,7 +391,8 @@ def run_ours(args, rank, world, local):
             K.quantize(src_slots, src_items, codes, meta, engine=engine)
             if use_rans:
                 K.rans_encode_ptr(codes.data_ptr(), code_bytes, stream_buf.data_ptr(), device)
-                K.rans_decode_ptr(stream_buf.data_ptr(), code_bytes, dec_codes.data_ptr(), device)
+                K.rans_decode_ptr(stream_buf.data_ptr(), code_bytes, dec_codes.data_ptr(), device,
+                                  stream_bytes=cap)
                 K.dequantize(dec_codes, meta, dst_slots, dst_items, engine=engine)
             else:
                 K.dequantize(codes, meta, dst_slots, dst_items, engine=engine)
@@ -430,7 +431,8 @@ def run_ours(args, rank, world, local):
                 K.wait_flag(region.ptr + flags_off + 256 * slot, s + 1, device, timeout_s=20.0)
                 K.copy_bytes(base + cap, meta.data_ptr(), meta_bytes, device)
                 if use_rans:
-                    K.rans_decode_ptr(base, code_bytes, dec_codes.data_ptr(), device)
+                    K.rans_decode_ptr(base, code_bytes, dec_codes.data_ptr(), device,
+                                      stream_bytes=cap)
                     K.dequantize(dec_codes, meta, dst_slots, dst_items, engine=engine)
                 else:
                     K.copy_bytes(base, dec_codes.data_ptr(), code_bytes, device)
@@ -533,7 +535,7 @@ def run_e2e_ours(args, mgr, wl, role, world, rank, pairs, device):
         nonlocal h2d, d2h
         if role == "both":
             cd = mgr.compress_paged_requests([wl.src[l] for l in range(L)], list(range(L)),
-                                             wl.src_req)
+                                             wl.src_req, trim=False)
             mgr.decompress_paged_requests(cd, [wl.dst[l] for l in range(L)], wl.dst_req)
             return
         raise NotImplementedError
@@ -600,7 +602,8 @@ def run_e2e_pairs(args, mgr, wl, role, world, rank, pairs, device):
     def one(s):
         if role == "producer":
             cd = mgr.compress_paged_requests([wl.src[l] for l in range(L)], list(range(L)),
-                                             wl.src_req, member_tids=[f"{s}:{r}" for r in range(wl.B)])
+                                             wl.src_req, member_tids=[f"{s}:{r}" for r in range(wl.B)],
+                                             trim=False)
             w = build_wire(cd)
             tr.send_bundle(f"s{s}", names, w.meta, w.body_chunks, w.aux_tensors)
         else:

@@ -58,11 +58,18 @@ def resolve_codec(codec_type: Optional[str], algorithm: Optional[str] = None) ->
 
 
 def _header(codec: str, n: int, device) -> torch.Tensor:
+    """16-byte container header.  On a CUDA device it is written by two fill
+    kernels (a copy from pageable host memory would synchronise the stream)."""
+    if torch.device(device).type == "cuda":
+        h = torch.empty(2, dtype=torch.int64, device=device)
+        h[0] = MAGIC | (CODEC_IDS[codec] << 32)  # little-endian [magic u32, codec u32]
+        h[1] = int(n)
+        return h.view(torch.uint8)
     h = np.zeros(2, dtype="<u8")
     h.view("<u4")[0] = MAGIC
     h.view("<u4")[1] = CODEC_IDS[codec]
     h[1] = n
-    return torch.from_numpy(h.view(np.uint8).copy()).to(device)
+    return torch.from_numpy(h.view(np.uint8).copy())
 
 
 def parse_header(stream: torch.Tensor) -> tuple[str, int]:

@@ -177,7 +177,13 @@ class FusedCompressionManager:
         ``quantization_params = [meta]``: the fp16 metadata of every item in
         the kernels' device layout as ONE aux tensor (item offsets follow from
         the plans and block counts).  Decoders also accept the per-item
-        ``layout="items"`` form."""
+        ``layout="items"`` form.
+
+        ``trim=False`` sends the codec's worst-case stream buffer instead of
+        reading the stream size back (which synchronises the host with the
+        device); the stream records its own length and the decoder takes the
+        code byte count from the metadata, so nothing else changes.  The
+        connector uses it: the extra bytes cost far less than the stall."""
         with nvtx("kvs.quantize"):
             batch = self.quantize_paged(kv_layers, layer_ids, requests)
         with nvtx("kvs.encode"):
@@ -242,8 +248,13 @@ class FusedCompressionManager:
         return co, mo
 
     def _encode_untrimmed(self, codes: torch.Tensor) -> torch.Tensor:
+        """Container header + the worst-case stream buffer (no host read of the
+        stream size); the stream records its own length."""
         from kvserve_hpdps_b200.compression.codec import _header
         from kvserve_hpdps_b200.ops import kernels as K
+        if self.stream_codec == "lc" and codes.is_cuda:
+            return torch.cat([_header("lc", codes.numel(), codes.device),
+                              K.lc_encode(codes, trim=False)])
         if self.stream_codec != "rans":
             return encode_bytes(codes, self.stream_codec)
         hdr = _header("rans", codes.numel(), codes.device)
@@ -252,6 +263,25 @@ class FusedCompressionManager:
         out[:16] = hdr
         K.rans_encode(codes, out=out[16:], trim=False)
         return out
+
+    @staticmethod
+    def _decode_body(body: torch.Tensor, meta: dict, device) -> torch.Tensor:
+        """Codes of a message body.  The codec and the code byte count come
+        from the message metadata, so nothing is read back to the host (the
+        body may be an untrimmed stream buffer); other bodies go through the
+        self-describing container."""
+        from kvserve_hpdps_b200.ops import kernels as K
+        sc, n = meta.get("stream_codec"), meta.get("code_bytes")
+        if sc is None or n is None or body.device.type != "cuda":
+            return decode_bytes(body, device)
+        if body.device != torch.device(device):
+            body = body.to(device)
+        data = body.view(torch.uint8).reshape(-1)[16:]
+        if sc == "rans":
+            return K.rans_decode(data, int(n))
+        if sc == "lc":
+            return K.lc_decode(data, int(n))
+        return data[:int(n)]
 
     def decompress_paged_requests(self, compressed: CompressedKVData,
                                   dst_layers: Sequence[torch.Tensor],
@@ -262,7 +292,7 @@ class FusedCompressionManager:
         from kvserve_hpdps_b200.ops import kernels as K
         meta = compressed.metadata
         device = dst_layers[0].device
-        codes = decode_bytes(compressed.compressed_tensor, device)
+        codes = self._decode_body(compressed.compressed_tensor, meta, device)
         plans = self._message_plans(meta)
         slots = self._slots(dst_layers, plans)
         items = K.WorkItems(slots, [(i, b, n) for i in range(len(dst_layers)) for b, n in dst_requests])
@@ -293,7 +323,7 @@ class FusedCompressionManager:
         if key not in cache:
             if len(cache) > 8:
                 cache.pop(next(iter(cache)))
-            cache[key] = decode_bytes(compressed.compressed_tensor, device)
+            cache[key] = self._decode_body(compressed.compressed_tensor, meta, device)
         codes = cache[key]
         layer_ids = meta["layer_ids"]
         R = len(meta["member_tids"])

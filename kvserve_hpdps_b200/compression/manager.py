@@ -242,8 +242,10 @@ class KVCompressionAdapter:
         return self._manager.finalize_chunked(chunks, chunk_metas, request_id, original_dtype,
                                               original_shape)
 
-    def compress_paged_requests(self, kv_layers, layer_ids, requests, member_tids=None):
-        return self._manager.compress_paged_requests(kv_layers, layer_ids, requests, member_tids)
+    def compress_paged_requests(self, kv_layers, layer_ids, requests, member_tids=None,
+                                trim: bool = True):
+        return self._manager.compress_paged_requests(kv_layers, layer_ids, requests, member_tids,
+                                                     trim=trim)
 
     def decompress_paged_requests(self, compressed, dst_layers, dst_requests):
         return self._manager.decompress_paged_requests(compressed, dst_layers, dst_requests)

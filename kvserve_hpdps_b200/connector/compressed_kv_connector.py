@@ -265,7 +265,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             with torch.cuda.stream(self._side_stream):
                 self._side_stream.wait_event(ready)
                 cd = comp.compress_paged_requests([kv_layer], [layer_index(layer_name)], requests,
-                                                  member_tids=tids)
+                                                  member_tids=tids, trim=False)
                 self._send_compressed(tids[0], [layer_name], cd, member_tids=tids)
             for t in tids:
                 self._expected_msgs[t] = self._num_layers
@@ -302,7 +302,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     with nvtx("kvs.compress"):
                         cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],
                                                           [(rm.block_ids, len(rm.token_ids))],
-                                                          member_tids=[tid])
+                                                          member_tids=[tid], trim=False)
                 except Exception:  # noqa: BLE001
                     # as the reference does: a compression failure sends the raw KV
                     logger.exception("compression of %s failed; sending raw KV", rid)

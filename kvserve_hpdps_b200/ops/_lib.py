@@ -86,7 +86,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
         "kvs_rans_staging_bytes": ([c_uint64, c_uint32], c_uint64),
         "kvs_rans_encode": ([P, c_uint64, c_uint32, P, P, P, P, P, P, c_uint32, P], c_int),
-        "kvs_rans_decode": ([P, P, c_uint64, c_uint32, P, P], c_int),
+        "kvs_rans_decode": ([P, c_uint64, P, c_uint64, c_uint32, P, P], c_int),
         "kvs_lc_max_bytes": ([c_uint64], c_uint64),
         "kvs_lc_staging_bytes": ([c_uint64], c_uint64),
         "kvs_lc_encode": ([P, c_uint64, P, P, P, P, P], c_int),

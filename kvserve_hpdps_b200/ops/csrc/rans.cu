@@ -297,27 +297,53 @@ __global__ void __launch_bounds__(256) k_rans_copy(
   }
 }
 
+// Every length and offset read from the stream is checked against the
+// expected geometry (n symbols in chunks of cs) and the stream length `len`
+// (~0 when unknown: then against the header's own total): a corrupt stream
+// records ERR_CORRUPT and its chunks are skipped, nothing is read or written
+// outside the buffers.
 __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ stream,
+                                                               uint64_t len,
                                                                uint8_t* __restrict__ out,
-                                                               uint64_t n_expected,
+                                                               uint64_t n_expected, uint32_t cs,
                                                                uint32_t* err) {
   extern __shared__ uint8_t dsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* lut = dsm + warp * kDecWarpSmem;
   uint32_t* fc = reinterpret_cast<uint32_t*>(lut + 4096);
   uint16_t* ring = reinterpret_cast<uint16_t*>(lut + 4096 + 1024);
+  const uint32_t nc = num_chunks(n_expected, cs);
+  if (len < sizeof(StreamHeader)) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, ERR_CORRUPT);
+    return;
+  }
   const StreamHeader hd = *reinterpret_cast<const StreamHeader*>(stream);
-  if (hd.magic != kMagic || hd.n_symbols != n_expected || hd.prob_bits != kProbBits) {
+  const uint64_t dir_end = sizeof(StreamHeader) + 8ull * (nc + 1);
+  if (hd.magic != kMagic || hd.n_symbols != n_expected || hd.prob_bits != kProbBits ||
+      hd.chunk_symbols != cs || hd.n_chunks != nc || hd.total_bytes > len || hd.total_bytes < dir_end) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, ERR_CORRUPT);
     return;
   }
   const uint32_t chunk = blockIdx.x * kDecWarps + warp;
-  if (chunk >= hd.n_chunks) return;
+  if (chunk >= nc) return;
   const uint64_t* dir = reinterpret_cast<const uint64_t*>(stream + sizeof(StreamHeader));
-  const uint8_t* rec = stream + dir[chunk];
+  const uint64_t roff = dir[chunk];
+  const uint64_t expect = min(static_cast<uint64_t>(cs), n_expected - static_cast<uint64_t>(chunk) * cs);
+  if (roff < dir_end || roff + 16 > hd.total_bytes) {
+    if (lane == 0) record_error(err, ERR_CORRUPT);
+    return;
+  }
+  const uint8_t* rec = stream + roff;
   const ChunkHeader ch = *reinterpret_cast<const ChunkHeader*>(rec);
-  uint8_t* dst = out + static_cast<uint64_t>(chunk) * hd.chunk_symbols;
-  if (ch.n_sym > hd.chunk_symbols || ch.alphabet > 256) {
+  uint8_t* dst = out + static_cast<uint64_t>(chunk) * cs;
+  const uint64_t room = hd.total_bytes - roff;  // record bytes available in the stream
+  const uint64_t fpad64 = pad16(2ull * ch.alphabet);
+  const bool bad = ch.n_sym != expect || ch.alphabet > 256 ||
+                   (ch.alphabet == 0 && 16ull + ch.n_sym > room) ||
+                   (ch.alphabet != 0 &&
+                    16ull + fpad64 + 128 + 2ull * (static_cast<uint64_t>(ch.n_pad) + ch.n_words) >
+                        room);
+  if (bad) {
     if (lane == 0) record_error(err, ERR_CORRUPT);
     return;
   }
@@ -328,7 +354,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   }
   const uint32_t A = ch.alphabet;
   const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
-  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  const uint32_t fpad = static_cast<uint32_t>(fpad64);
   const uint32_t* states = reinterpret_cast<const uint32_t*>(rec + 16 + fpad);
   const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
   const uint32_t total_words = ch.n_pad + ch.n_words;
@@ -426,14 +452,16 @@ int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int kvs_rans_decode(const uint8_t* stream_buf, uint8_t* out, uint64_t n, uint32_t cs, uint32_t* err,
-                    void* stream) {
+// Decode n bytes from a stream of `len` bytes (~0: unknown, the header's
+// total bounds the reads).
+int kvs_rans_decode(const uint8_t* stream_buf, uint64_t len, uint8_t* out, uint64_t n, uint32_t cs,
+                    uint32_t* err, void* stream) {
   if (n == 0 || cs == 0) return -2;
   const uint32_t nc = num_chunks(n, cs);
   const int smem = kDecWarps * kDecWarpSmem;
   cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   k_rans_decode<<<(nc + kDecWarps - 1) / kDecWarps, kDecWarps * 32, smem,
-                  static_cast<cudaStream_t>(stream)>>>(stream_buf, out, n, err);
+                  static_cast<cudaStream_t>(stream)>>>(stream_buf, len, out, n, cs, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -935,7 +935,8 @@ def rans_decode(stream: torch.Tensor, n: int, out: Optional[torch.Tensor] = None
         return res
     dev = stream.device
     res = torch.empty(n, dtype=torch.uint8, device=dev) if out is None else out
-    check(lb.kvs_rans_decode(stream.data_ptr(), res.data_ptr(), n, chunk,
+    s = stream.contiguous()
+    check(lb.kvs_rans_decode(s.data_ptr(), s.numel(), res.data_ptr(), n, chunk,
                              workspace(dev).err.data_ptr(), _stream(dev)), "rans_decode")
     return res
 
@@ -960,9 +961,12 @@ def rans_encode_ptr(src_ptr: int, n: int, out_ptr: int, device: torch.device,
 
 
 def rans_decode_ptr(stream_ptr: int, n: int, out_ptr: int, device: torch.device,
-                    chunk: int = RANS_CHUNK) -> None:
-    check(lib().kvs_rans_decode(stream_ptr, out_ptr, n, chunk, workspace(device).err.data_ptr(),
-                                _stream(device)), "rans_decode")
+                    chunk: int = RANS_CHUNK, stream_bytes: Optional[int] = None) -> None:
+    """Decode from a raw device pointer; ``stream_bytes`` (the buffer's size,
+    when known) bounds every read of a corrupt stream."""
+    length = (1 << 64) - 1 if stream_bytes is None else int(stream_bytes)
+    check(lib().kvs_rans_decode(stream_ptr, length, out_ptr, n, chunk,
+                                workspace(device).err.data_ptr(), _stream(device)), "rans_decode")
 
 
 def bitpack(codes: torch.Tensor, bits: int) -> torch.Tensor:

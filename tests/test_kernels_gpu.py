@@ -543,3 +543,29 @@ def test_lc_gpu_matches_cpu_reference(n):
     K.lc_decode(s[:32], n)
     torch.cuda.synchronize()
     assert K.read_device_error(out.device) == 4
+
+
+def test_rans_decode_rejects_corrupt_streams():
+    """A corrupt header, directory or length records ERR_CORRUPT; the decoder
+    never reads or writes outside the buffers it was given."""
+    g = torch.Generator().manual_seed(7)
+    x = torch.randint(0, 6, (200000,), generator=g, dtype=torch.uint8).cuda()
+    s = K.rans_encode(x)
+    out = K.rans_decode(s, x.numel())
+    torch.cuda.synchronize()
+    assert K.read_device_error(out.device) == 0 and torch.equal(out, x)
+    for field, value in ((0, 0x12345678), (4, 1 << 20), (16, 1 << 30), (24, 1 << 40)):
+        bad = s.clone()
+        bad[field:field + 4] = torch.tensor([value & 0xFFFFFFFF], dtype=torch.int64) \
+            .to(torch.int32).view(torch.uint8).cuda()
+        K.rans_decode(bad, x.numel())
+        torch.cuda.synchronize()
+        assert K.read_device_error(out.device) == 4, field
+    dir0 = s.clone()  # first record offset far past the stream
+    dir0[32:40] = torch.tensor([1 << 40], dtype=torch.int64).view(torch.uint8).cuda()
+    K.rans_decode(dir0, x.numel())
+    torch.cuda.synchronize()
+    assert K.read_device_error(out.device) == 4
+    K.rans_decode(s[:1000], x.numel())  # truncated: the header's total exceeds the buffer
+    torch.cuda.synchronize()
+    assert K.read_device_error(out.device) == 4
