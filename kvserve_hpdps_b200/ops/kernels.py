@@ -1009,9 +1009,16 @@ def copy_bytes(src_ptr: int, dst_ptr: int, nbytes: int, device: torch.device,
                            _stream(device)), "copy16")
 
 
+def _grid_per_seg(segs: Sequence[tuple[int, int, int]], floor: int) -> int:
+    """CTAs per segment: enough for the largest segment to use the whole GPU
+    (one CTA per 256 KB, up to 8 per SM), at least ``floor``."""
+    big = max((int(s[2]) for s in segs), default=0)
+    return int(max(floor, min(1184, big >> 18)))
+
+
 def copy_segments(segments: Sequence[tuple[int, int, int]], device: torch.device,
                   flag_ptr: Optional[int] = None, flag_value: int = 0,
-                  blocks_per_seg: int = 32) -> None:
+                  blocks_per_seg: Optional[int] = None) -> None:
     """Copy several (src_ptr, dst_ptr, nbytes) ranges in one launch on the
     current stream; destinations may be peer memory.  With ``flag_ptr``, the
     last CTA publishes ``flag_value`` there (release, system scope) after
@@ -1028,6 +1035,8 @@ def copy_segments(segments: Sequence[tuple[int, int, int]], device: torch.device
     dev_segs = host.to(device, non_blocking=True)
     ws = workspace(device)
     counter = ws.counters[4:5].data_ptr() if flag_ptr is not None else None
+    if blocks_per_seg is None:
+        blocks_per_seg = _grid_per_seg(segs, 32)
     check(lib().kvs_copy_segments(dev_segs.data_ptr(), len(segs), blocks_per_seg, counter,
                                   flag_ptr, flag_value, _stream(device)), "copy_segments")
     # dev_segs may be freed now: the caching allocator only reuses its block
@@ -1043,19 +1052,21 @@ def _ck_segments(segments: Sequence[tuple[int, int, int]], device: torch.device)
 
 
 def checksum(segments: Sequence[tuple[int, int, int]], out: torch.Tensor,
-             blocks_per_seg: int = 16) -> None:
+             blocks_per_seg: Optional[int] = None) -> None:
     """Message checksum of (src_ptr, message_offset, nbytes) segments into
     ``out`` (int64[2] on the device): the plain and the position-weighted
     sums of the message's little-endian 32-bit words, mod 2^64."""
     segs = [s for s in segments if s[2] > 0]
     dev = out.device
     d = _ck_segments(segs, dev)
+    if blocks_per_seg is None:
+        blocks_per_seg = _grid_per_seg(segs, 16)
     check(lib().kvs_checksum(d.data_ptr(), len(segs), out.data_ptr(), blocks_per_seg,
                              _stream(dev)), "checksum")
 
 
 def verify_checksum(segments: Sequence[tuple[int, int, int]], expected_ptr: int,
-                    device: torch.device, blocks_per_seg: int = 16) -> None:
+                    device: torch.device, blocks_per_seg: Optional[int] = None) -> None:
     """Recompute the checksum of ``segments`` on ``device`` and record
     ERR_CORRUPT in the device error word when it differs from the int64[2]
     at ``expected_ptr`` (device memory).  Nothing waits on the host."""
@@ -1063,6 +1074,8 @@ def verify_checksum(segments: Sequence[tuple[int, int, int]], expected_ptr: int,
     d = _ck_segments(segs, device)
     ws = workspace(device)
     scratch = torch.empty(2, dtype=torch.int64, device=device)  # stream-ordered reuse
+    if blocks_per_seg is None:
+        blocks_per_seg = _grid_per_seg(segs, 16)
     check(lib().kvs_checksum_verify(d.data_ptr(), len(segs), expected_ptr, scratch.data_ptr(),
                                     ws.err.data_ptr(), blocks_per_seg, _stream(device)),
           "checksum_verify")
