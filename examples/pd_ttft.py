@@ -21,13 +21,16 @@ Example::
   python examples/pd_ttft.py --compression none          # raw KV over the NVLink ring
   python examples/pd_ttft.py --impl reference --compression none
 
-Prints one JSON line with p50 / p90 / mean TTFT and the producer-side
-prefill latency.
+Prints one JSON line with p50 / p90 / mean TTFT, the producer-side prefill
+latency, the agreement of the consumer's first token with the producer's own
+greedy token (a full prefill without transfer; 1.0 is required for raw KV)
+and an md5 fingerprint of the consumer's greedy outputs.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import multiprocessing as mp
 import os
@@ -159,7 +162,7 @@ def main(argv=None) -> int:
             ready.add(m[1])
         import random
         rng = random.Random(0)
-        ttft, prefill, first_tokens = [], [], []
+        ttft, prefill, first_tokens, agree = [], [], [], []
         for i in range(args.warmup + args.requests):
             ids = [rng.randrange(0, QWEN25_7B["vocab_size"]) for _ in range(args.prompt_len)]
             t0 = time.time()
@@ -172,7 +175,10 @@ def main(argv=None) -> int:
             if i >= args.warmup:
                 ttft.append((got["c"][3] - t0) * 1e3)
                 prefill.append((got["p"][3] - t0) * 1e3)
-                first_tokens.append(got["c"][4][:1])
+                first_tokens.append(got["c"][4])
+                # the producer's token comes from its own full prefill (no
+                # transfer): the consumer's must match it exactly for raw KV
+                agree.append(got["c"][4][:1] == got["p"][4][:1])
         q = sorted(ttft)
         line = {"metric": "p50 TTFT, 1P1D (Qwen2.5-7B random-init, 8K prompt)",
                 "impl": args.impl, "compression": args.compression,
@@ -184,6 +190,8 @@ def main(argv=None) -> int:
                 "producer_prefill_ms_p50": round(statistics.median(prefill), 2),
                 "handoff_ms_p50": round(statistics.median(
                     [a - b for a, b in zip(ttft, prefill)]), 2),
+                "first_token_agreement": round(sum(agree) / len(agree), 4),
+                "output_md5": hashlib.md5(json.dumps(first_tokens).encode()).hexdigest(),
                 "data": "synthetic uniform token ids; random-init weights (load_format=dummy)",
                 "timing": "host wall clock from dispatch to the consumer's first token"}
         print(json.dumps(line), flush=True)
