@@ -9,6 +9,7 @@ Here the stages are the fused kernels of this package:
                (one stats launch and one quantize launch per call);
 * ``dequant``: dequantize + inverse Hadamard + paged scatter;
 * ``rans_enc`` / ``rans_dec``: the interleaved rANS codec over the codes;
+* ``lc_enc`` / ``lc_dec``: the LC-style BIT_2 + RZE_1 codec over the codes;
 * ``block_copy``: the paged gather of raw KV (the uncompressed path).
 
 Every figure is CUDA-event time on the launching stream after warm-up,
@@ -30,7 +31,7 @@ import sys
 
 import torch
 
-STAGES = ("quant", "dequant", "rans_enc", "rans_dec", "block_copy")
+STAGES = ("quant", "dequant", "rans_enc", "rans_dec", "lc_enc", "lc_dec", "block_copy")
 
 
 def _timeit(fn, iters: int, warmup: int = 3) -> float:
@@ -101,6 +102,16 @@ def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
         dec = torch.empty(n, dtype=torch.uint8, device="cuda")
         row("rans_dec", _timeit(lambda: K.rans_decode(stream, n, out=dec), iters, warmup),
             exact=bool(torch.equal(K.rans_decode(stream, n), codes)))
+    if "lc_enc" in only or "lc_dec" in only:
+        lc_stream = K.lc_encode(codes)
+        if "lc_enc" in only:
+            row("lc_enc", _timeit(lambda: K.lc_encode(codes, trim=False), iters, warmup),
+                stream_bytes=int(lc_stream.numel()),
+                bits_per_code=round(8 * lc_stream.numel() / n, 4))
+        if "lc_dec" in only:
+            dec_lc = torch.empty(n, dtype=torch.uint8, device="cuda")
+            row("lc_dec", _timeit(lambda: K.lc_decode(lc_stream, n, out=dec_lc), iters, warmup),
+                exact=bool(torch.equal(K.lc_decode(lc_stream, n), codes)))
     if "block_copy" in only:
         flat = torch.empty(nbytes // layers, dtype=torch.uint8, device="cuda")
         blocks = torch.tensor(wl.block_ids[0], dtype=torch.int32, device="cuda")
@@ -111,7 +122,14 @@ def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
         row("block_copy", _timeit(copy_all, iters, warmup))
     K.dequantize(codes, meta, dslots, items, engine=engine)
     err = K.kv_error(wl.cache[:, :, wl.block_ids[0]], dst[:, :, wl.block_ids[0]])
+    # order-0 entropy of the code bytes: the size an ideal per-buffer entropy
+    # coder would reach, against which the chunked coder is judged
+    hist = torch.bincount(codes, minlength=256).double()
+    p = hist[hist > 0] / n
+    entropy = float(-(p * torch.log2(p)).sum())
     rows.append({"stage": "summary", "code_width": code_width, "original_bytes": nbytes,
+                 "entropy_bits_per_code_byte": round(entropy, 4),
+                 "rans_bits_per_code_byte": round(8 * stream.numel() / n, 4),
                  "compressed_bytes": int(stream.numel() + meta.numel()),
                  "compression_ratio": round(nbytes / (stream.numel() + meta.numel()), 3),
                  "rel_mse": err["rel_mse"], "cosine": err["cosine"],
