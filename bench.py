@@ -23,7 +23,9 @@ with CUDA events between barriers, the maximum over ranks is used.
 
 ``--impl reference`` runs the unmodified reference package from
 ``baseline/_ref`` through its public ``KVCompressionAdapter`` on the same
-workload (see DESIGN.md for which of its paths can run on this box).
+workload.  Its default mode needs nvCOMP, CuPy and fast_hadamard_transform,
+which are not installed, so the arm runs its quantizer-only custom pipeline
+(the degraded mode of its own tests) and, for N >= 2, its NcclTransport.
 """
 
 from __future__ import annotations
