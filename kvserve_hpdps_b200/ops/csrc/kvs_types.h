@@ -85,6 +85,6 @@ struct LayerLaunch {
   unsigned long long* trace;
   int trace_jobs;
 };
-constexpr int kTraceCtas = 4;
+constexpr int kTraceCtas = 8;
 
 }  // namespace kvs

@@ -583,7 +583,7 @@ class RequestBatch:
 
 # ---------------------------------------------------------------- fused ops
 # Device trace of the warp-specialized kernels (diagnostics; off by default).
-TRACE_CTAS = 4
+TRACE_CTAS = 8
 TRACE_EVENTS = ("tile_ready", "mma_issued", "refill_issued", "epi_mma_seen", "epi_done",
                 "acc_free_seen", "epi_quantized", "epi_staged")
 # the dequantize kernel's events, same slots
