@@ -891,8 +891,9 @@ def main(argv=None):
     rank, world, local = dist_info()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    if args.warmup < 3 and args.impl == "ours":
-        pass
+    if args.warmup < 3:  # timed numbers need at least three untimed warm-up steps
+        print(f"bench: --warmup {args.warmup} raised to 3", file=sys.stderr)
+        args.warmup = 3
     init_dist(world, local)
     try:
         res = run_reference(args, rank, world, local) if args.impl == "reference" else \

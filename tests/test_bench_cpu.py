@@ -46,3 +46,10 @@ def test_sweep_plan_and_report():
             {"impl": "reference", "unavailable": "x"}]
     table = sw.render(rows)
     assert "| 0.9 | off | 0.01 | 91.0 | 1.0 | 0.05 | 18.0 | 1.0 | 5.0x |" in table
+
+
+def test_copy_grids_scale_with_segment_size():
+    from kvserve_hpdps_b200.ops import kernels as K
+    assert K._grid_per_seg([(0, 0, 1000)], 16) == 16
+    assert K._grid_per_seg([(0, 0, 64 << 20), (0, 0, 100)], 16) == 256
+    assert K._grid_per_seg([(0, 0, 4 << 30)], 32) == 1184
