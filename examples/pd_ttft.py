@@ -20,6 +20,10 @@ Example::
   python examples/pd_ttft.py --requests 32 --prompt-len 8192 --compression default
   python examples/pd_ttft.py --compression none          # raw KV over the NVLink ring
   python examples/pd_ttft.py --impl reference --compression none
+  python examples/pd_ttft.py --tp 2 --gpus 0,1,2,3      # TP2 producer and consumer
+  # across two nodes (consumer first), transport nccl:
+  python examples/pd_ttft.py --role consumer --gpus 0 --kv-ip <consumer host> --transport nccl
+  python examples/pd_ttft.py --role producer --gpus 0 --kv-ip <consumer host> --transport nccl
 
 Prints one JSON line with p50 / p90 / mean TTFT, the producer-side prefill
 latency, the agreement of the consumer's first token with the producer's own
@@ -96,13 +100,14 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
                                kv_connector_module_path=module,
                                kv_role="kv_producer" if role == "p" else "kv_consumer",
                                kv_rank=0 if role == "p" else 1, kv_parallel_size=2,
-                               kv_ip="127.0.0.1", kv_port=args.port,
+                               kv_ip=args.kv_ip, kv_port=args.port,
                                kv_connector_extra_config=extra)
         llm = LLM(model=args.model_dir, dtype="bfloat16", load_format="dummy",
                   skip_tokenizer_init=True, max_model_len=args.prompt_len + args.max_tokens + 64,
                   max_num_batched_tokens=args.prompt_len + 64, max_num_seqs=8,
                   gpu_memory_utilization=args.mem_util, enforce_eager=True,
-                  enable_prefix_caching=False, kv_transfer_config=ktc, seed=0)
+                  enable_prefix_caching=False, kv_transfer_config=ktc, seed=0,
+                  tensor_parallel_size=args.tp)
         q_out.put(("ready", role))
         while True:
             msg = q_in.get()
@@ -128,16 +133,27 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--prompt-len", type=int, default=8192)
     ap.add_argument("--max-tokens", type=int, default=1)
-    ap.add_argument("--gpus", default="0,1", help="producer GPU, consumer GPU")
+    ap.add_argument("--gpus", default="0,1",
+                    help="producer GPUs then consumer GPUs (tp of each; one role: its tp GPUs)")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel size of each engine")
+    ap.add_argument("--role", choices=["both", "producer", "consumer"], default="both",
+                    help="producer / consumer: run one engine here and pair with --kv-ip "
+                         "(the consumer's host) across nodes")
+    ap.add_argument("--kv-ip", default="127.0.0.1", help="the consumer engine's host")
     ap.add_argument("--port", type=int, default=25010)
     ap.add_argument("--mem-util", type=float, default=0.5)
     ap.add_argument("--timeout", type=float, default=900.0)
     args = ap.parse_args(argv)
     args.model_dir = write_model_dir(os.path.join(tempfile.gettempdir(), "kvs_qwen25_7b_dummy"))
-    gp, gc = args.gpus.split(",")
+    if args.role != "both":
+        return run_one_role(args)
+    gpus = args.gpus.split(",")
+    if len(gpus) != 2 * args.tp:
+        raise SystemExit(f"--gpus needs {2 * args.tp} ids for --tp {args.tp}")
+    gp, gc = ",".join(gpus[:args.tp]), ",".join(gpus[args.tp:])
     ctx = mp.get_context("spawn")
     qp, qc, qo = ctx.Queue(), ctx.Queue(), ctx.Queue()
-    # each engine sees both GPUs, its own first (peer mappings need both visible)
+    # each engine sees every GPU, its own first (peer mappings need both visible)
     pc = ctx.Process(target=engine, args=("c", f"{gc},{gp}", args, qc, qo))
     pp = ctx.Process(target=engine, args=("p", f"{gp},{gc}", args, qp, qo))
     pc.start()
@@ -160,11 +176,8 @@ def main(argv=None) -> int:
         while len(ready) < 2:
             m = get()
             ready.add(m[1])
-        import random
-        rng = random.Random(0)
         ttft, prefill, first_tokens, agree = [], [], [], []
-        for i in range(args.warmup + args.requests):
-            ids = [rng.randrange(0, QWEN25_7B["vocab_size"]) for _ in range(args.prompt_len)]
+        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len)):
             t0 = time.time()
             qp.put(("go", i, ids))
             qc.put(("go", i, ids))
@@ -206,6 +219,59 @@ def main(argv=None) -> int:
             p.join(timeout=60)
             if p.is_alive():
                 p.terminate()
+    return rc
+
+
+def prompts(n: int, prompt_len: int) -> list:
+    """The deterministic request sequence both sides generate on their own."""
+    import random
+    rng = random.Random(0)
+    return [[rng.randrange(0, QWEN25_7B["vocab_size"]) for _ in range(prompt_len)]
+            for _ in range(n)]
+
+
+def run_one_role(args) -> int:
+    """One engine on this host (cross-node PD, one role per node).  Both sides
+    submit the same deterministic requests with the same transfer ids; the
+    consumer's latency per request runs from its own submission to its first
+    token, so it includes waiting for the producer's KV.  The consumer prints
+    median latency and an md5 fingerprint of its outputs (compare it with a
+    raw-KV run to catch silent corruption); the producer its prefill latency.
+    Start the consumer first: its control socket must be listening."""
+    role = "p" if args.role == "producer" else "c"
+    ctx = mp.get_context("spawn")
+    q_in, q_out = ctx.Queue(), ctx.Queue()
+    proc = ctx.Process(target=engine, args=(role, args.gpus, args, q_in, q_out))
+    proc.start()
+    lat, outs, rc = [], [], 0
+    try:
+        m = q_out.get(timeout=args.timeout)
+        if m[0] == "error":
+            raise RuntimeError(m[2])
+        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len)):
+            t0 = time.time()
+            q_in.put(("go", i, ids))
+            m = q_out.get(timeout=args.timeout)
+            if m[0] == "error":
+                raise RuntimeError(m[2])
+            if i >= args.warmup:
+                lat.append((m[3] - t0) * 1e3)
+                outs.append(m[4])
+        print(json.dumps({"metric": "per-request latency, one PD role per node",
+                          "role": args.role, "impl": args.impl,
+                          "compression": args.compression, "requests": args.requests,
+                          "latency_ms_p50": round(statistics.median(lat), 2),
+                          "output_md5": hashlib.md5(json.dumps(outs).encode()).hexdigest()}),
+              flush=True)
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"role": args.role, "error": f"{type(e).__name__}: {e}"[-4000:]}),
+              flush=True)
+        rc = 1
+    finally:
+        q_in.put(("stop",))
+        proc.join(timeout=60)
+        if proc.is_alive():
+            proc.terminate()
     return rc
 
 

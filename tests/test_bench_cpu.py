@@ -53,3 +53,14 @@ def test_copy_grids_scale_with_segment_size():
     assert K._grid_per_seg([(0, 0, 1000)], 16) == 16
     assert K._grid_per_seg([(0, 0, 64 << 20), (0, 0, 100)], 16) == 256
     assert K._grid_per_seg([(0, 0, 4 << 30)], 32) == 1184
+
+
+def test_ttft_harness_prompts_are_deterministic():
+    """Both sides of a cross-node run generate the same requests."""
+    spec = importlib.util.spec_from_file_location(
+        "pd_ttft", os.path.join(ROOT, "examples", "pd_ttft.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    a, b = mod.prompts(4, 64), mod.prompts(4, 64)
+    assert a == b and len(a) == 4 and all(len(p) == 64 for p in a)
+    assert all(0 <= t < mod.QWEN25_7B["vocab_size"] for p in a for t in p)
