@@ -26,6 +26,7 @@ from dataclasses import dataclass, field
 from functools import lru_cache
 from typing import Optional, Sequence
 
+import numpy as np
 import torch
 
 from kvserve_hpdps_b200.compression.signs import hadamard_matrix, rademacher_signs
@@ -428,6 +429,19 @@ class LayerSlots:
         t = torch.frombuffer(bytearray(raw), dtype=torch.uint8).clone()
         return t.to(self.device) if self.device.type == "cuda" else t
 
+    def item_constants(self) -> tuple[np.ndarray, ...]:
+        """Per slot (cached): number of blocks, block size, code bytes per
+        token row, value groups; WorkItems indexes them by item slot."""
+        c = self.__dict__.get("_item_consts")
+        if c is None:
+            c = tuple(np.asarray(v, dtype=np.int64) for v in (
+                [_num_blocks(t) for t in self.kv_layers],
+                [t.shape[2] for t in self.kv_layers],
+                [p.row_bytes() for p in self.plans],
+                [p.n_groups for p in self.plans]))
+            self._item_consts = c
+        return c
+
     @classmethod
     def single(cls, kv_layer: torch.Tensor, plan: LayerPlan) -> "LayerSlots":
         return cls([kv_layer], [plan])
@@ -452,48 +466,54 @@ class WorkItems:
         self.slots = slots
         dev = slots.device
         self.device = dev
-        uniq: dict[int, int] = {}  # id(block sequence) -> index into lists
-        lists: list[list[int]] = []
-        norm = []
+        uniq: dict[int, int] = {}  # id(block sequence) -> index into arrs
+        arrs: list[np.ndarray] = []
+        s_l, li_l, n_l = [], [], []
         for s, b, n in items:
             k = id(b)
-            if k not in uniq:
-                uniq[k] = len(lists)
-                lists.append(b.tolist() if isinstance(b, torch.Tensor) else [int(x) for x in b])
-            norm.append((int(s), uniq[k], int(n)))
-        self.items = [(s, lists[li], n) for s, li, n in norm]
-        span = [(min(b), max(b)) if b else (0, -1) for b in lists]
-        for s, li, n in norm:
-            lo, hi = span[li]
-            nb = _num_blocks(slots.kv_layers[s])
-            if lo < 0 or hi >= nb:
-                raise ValueError(f"block id {lo if lo < 0 else hi} outside the {nb} blocks "
-                                 f"of layer slot {s}")
-        bs = [slots.kv_layers[s].shape[2] for s, _, _ in norm]
-        self.n_rows = [len(lists[li]) * k for (_, li, _), k in zip(norm, bs)]
-        self.n_tokens = [n for _, _, n in norm]
-        self.tiles = [(r + TILE_ROWS - 1) // TILE_ROWS for r in self.n_rows]
-        self.total_tiles = sum(self.tiles)
-        R = len(norm)
-        bt, list_off = [], []
-        for b in lists:
-            list_off.append(len(bt))
-            bt.extend(b)
-        off = [list_off[li] for _, li, _ in norm]
-        prefix = [0]
-        for t in self.tiles:
-            prefix.append(prefix[-1] + t)
-        self.code_off, self.meta_off, self.row_off = [], [], []
-        c = m = ro = 0
-        for (s, _, _), rows in zip(norm, self.n_rows):
-            plan = slots.plans[s]
-            self.code_off.append(c)
-            self.meta_off.append(m)
-            self.row_off.append(ro)
-            c += _align16(rows * plan.row_bytes())
-            m += _align16(plan.meta_bytes(rows))
-            ro += rows
-        self.code_bytes, self.meta_bytes, self.total_rows = c, m, ro
+            li = uniq.get(k)
+            if li is None:
+                li = uniq[k] = len(arrs)
+                src = b.detach().cpu() if isinstance(b, torch.Tensor) else b
+                arrs.append(np.asarray(src, dtype=np.int64).reshape(-1))
+            s_l.append(int(s))
+            li_l.append(li)
+            n_l.append(int(n))
+        lists = [a.tolist() for a in arrs]
+        self.items = [(s, lists[li], n) for s, li, n in zip(s_l, li_l, n_l)]
+        R = len(s_l)
+        s_a = np.asarray(s_l, dtype=np.int64)
+        li_a = np.asarray(li_l, dtype=np.int64)
+        n_a = np.asarray(n_l, dtype=np.int64)
+        consts = slots.item_constants()  # per slot: blocks, block size, row bytes, groups
+        nb_s, bs_s, rb_s, g_s = (c[s_a] for c in consts)
+        lens = np.asarray([a.size for a in arrs], dtype=np.int64)
+        lo = np.asarray([a.min() if a.size else 0 for a in arrs], dtype=np.int64)
+        hi = np.asarray([a.max() if a.size else -1 for a in arrs], dtype=np.int64)
+        bad = np.nonzero((lo[li_a] < 0) | (hi[li_a] >= nb_s))[0]
+        if bad.size:
+            r = int(bad[0])
+            v = int(lo[li_a[r]]) if lo[li_a[r]] < 0 else int(hi[li_a[r]])
+            raise ValueError(f"block id {v} outside the {int(nb_s[r])} blocks "
+                             f"of layer slot {int(s_a[r])}")
+        rows = lens[li_a] * bs_s
+        tiles = (rows + TILE_ROWS - 1) // TILE_ROWS
+        prefix = np.concatenate([[0], np.cumsum(tiles)])
+        list_off = np.concatenate([[0], np.cumsum(lens)[:-1]]) if arrs else np.zeros(0, np.int64)
+        csz = (rows * rb_s + 15) & ~15
+        msz = (2 * (2 * slots.num_heads * HEAD_DIM + 2 * g_s * rows) + 15) & ~15
+        code_off = np.concatenate([[0], np.cumsum(csz)])
+        meta_off = np.concatenate([[0], np.cumsum(msz)])
+        row_off = np.concatenate([[0], np.cumsum(rows)])
+        self.n_rows = rows.tolist()
+        self.n_tokens = n_l
+        self.tiles = tiles.tolist()
+        self.total_tiles = int(prefix[-1])
+        self.code_off = code_off[:-1].tolist()
+        self.meta_off = meta_off[:-1].tolist()
+        self.row_off = row_off[:-1].tolist()
+        self.code_bytes, self.meta_bytes = int(code_off[-1]), int(meta_off[-1])
+        self.total_rows = int(row_off[-1])
         for offs in (code_offsets, meta_offsets):
             if offs is not None and any(int(o) % 16 for o in offs):
                 raise ValueError("item code / metadata offsets must be multiples of 16 bytes")
@@ -501,26 +521,33 @@ class WorkItems:
             if len(code_offsets) != R:
                 raise ValueError("one code offset per item is required")
             self.code_off = [int(x) for x in code_offsets]
-            self.code_bytes = max((o + self.n_rows[i] * slots.plans[norm[i][0]].row_bytes()
-                                   for i, o in enumerate(self.code_off)), default=0)
+            self.code_bytes = int(max((o + r * b for o, r, b in
+                                       zip(self.code_off, rows.tolist(), rb_s.tolist())),
+                                      default=0))
         if meta_offsets is not None:
             if len(meta_offsets) != R:
                 raise ValueError("one metadata offset per item is required")
             self.meta_off = [int(x) for x in meta_offsets]
-            self.meta_bytes = max((o + slots.plans[norm[i][0]].meta_bytes(self.n_rows[i])
-                                   for i, o in enumerate(self.meta_off)), default=0)
-        ints = bt + off + self.n_tokens + self.n_rows + prefix + [s for s, _, _ in norm]
-        longs = self.code_off + self.meta_off + self.row_off
-        hi = torch.tensor(ints if ints else [0], dtype=torch.int32)
-        hl = torch.tensor(longs if longs else [0], dtype=torch.int64)
+            self.meta_bytes = int(max((o + 2 * (2 * slots.num_heads * HEAD_DIM + 2 * g * r)
+                                       for o, r, g in
+                                       zip(self.meta_off, rows.tolist(), g_s.tolist())),
+                                      default=0))
+        bt = np.concatenate(arrs) if arrs else np.zeros(0, np.int64)
+        nbt = int(bt.size)
+        ints = np.concatenate([bt, list_off[li_a] if R else np.zeros(0, np.int64), n_a, rows,
+                               prefix, s_a]).astype(np.int32)
+        longs = np.asarray(self.code_off + self.meta_off + self.row_off, dtype=np.int64)
+        hi_t = torch.from_numpy(ints if ints.size else np.zeros(1, np.int32))
+        hl_t = torch.from_numpy(longs if longs.size else np.zeros(1, np.int64))
         if dev.type == "cuda":
-            hi, hl = hi.pin_memory(), hl.pin_memory()
-        self._ints = hi.to(dev, non_blocking=True)
-        self._longs = hl.to(dev, non_blocking=True)
-        if dev.type == "cuda":
-            _xfer["h2d"] += hi.numel() * 4 + hl.numel() * 8
-        self._o = {"bt": 0, "off": len(bt), "ntok": len(bt) + R, "rows": len(bt) + 2 * R,
-                   "prefix": len(bt) + 3 * R, "slot": len(bt) + 4 * R + 1}
+            hi_t, hl_t = hi_t.pin_memory(), hl_t.pin_memory()
+            self._ints = hi_t.to(dev, non_blocking=True)
+            self._longs = hl_t.to(dev, non_blocking=True)
+            _xfer["h2d"] += hi_t.numel() * 4 + hl_t.numel() * 8
+        else:
+            self._ints, self._longs = hi_t.clone(), hl_t.clone()
+        self._o = {"bt": 0, "off": nbt, "ntok": nbt + R, "rows": nbt + 2 * R,
+                   "prefix": nbt + 3 * R, "slot": nbt + 4 * R + 1}
 
     @property
     def num_items(self) -> int:
