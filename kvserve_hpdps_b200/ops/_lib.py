@@ -51,7 +51,8 @@ class LayerLaunch(ctypes.Structure):
                 ("bmat", c_void_p), ("bmat_stride", c_longlong), ("codes", c_void_p),
                 ("meta", c_void_p), ("kstat", c_void_p), ("vstat", c_void_p), ("err", c_void_p),
                 ("total_tiles", c_int), ("num_heads", c_int), ("engine", c_int),
-                ("stream", c_void_p), ("trace", c_void_p), ("trace_jobs", c_int)]
+                ("stream", c_void_p), ("trace", c_void_p), ("trace_jobs", c_int),
+                ("vparam", c_void_p)]
 
 
 class RawItem(ctypes.Structure):
@@ -82,6 +83,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_make_plane_maps": ([POINTER(PagedKV), c_int, P], c_int),
         "kvs_stats": ([POINTER(LayerLaunch)], c_int),
         "kvs_quant": ([POINTER(LayerLaunch)], c_int),
+        "kvs_value_params": ([POINTER(LayerLaunch), c_int], c_int),
         "kvs_dequant_inverse": ([POINTER(LayerLaunch)], c_int),
         "kvs_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
         "kvs_rans_staging_bytes": ([c_uint64, c_uint32], c_uint64),

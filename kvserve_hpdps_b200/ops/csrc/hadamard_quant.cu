@@ -302,6 +302,40 @@ KVS_DEV void value_row_params(const LayerLaunch& L, const ItemCtx& c, int h, int
   }
 }
 
+// Value parameters of every (item, row, group) in one pass, for the
+// warp-specialized quantize kernel: the same operations as value_row_params
+// (min / max over the group's heads, scale = max(range, eps) / (levels - 1),
+// its reciprocal), written to L.vparam and, as fp16, to the metadata.  Grid
+// (ceil(max rows / 256), items).
+__global__ void __launch_bounds__(256) k_value_params(LayerLaunch L) {
+  const int r = blockIdx.y;
+  const int row = blockIdx.x * 256 + threadIdx.x;
+  const int rows = L.rt.n_rows[r];
+  if (row >= rows) return;
+  const LayerParams* lp = L.lps + L.rt.slot[r];
+  const int H = lp->H, G = lp->n_groups;
+  const long long base = L.rt.row_off[r] * H;
+  __half* m = meta_base(L, r);
+  for (int g = 0; g < G; ++g) {
+    float mn = INFINITY, mx = -INFINITY;
+    int first = -1;
+    for (int hh = 0; hh < H; ++hh) {
+      if (lp->group_of_head[hh] != g) continue;
+      if (first < 0) first = hh;
+      const float* e = L.vstat + (base + static_cast<long long>(hh) * rows + row) * 2;
+      mn = fminf(mn, e[0]);
+      mx = fmaxf(mx, e[1]);
+    }
+    if (first < 0) continue;
+    const float scale =
+        __fdiv_rn(fmaxf(__fsub_rn(mx, mn), kRangeEps), lp->value_levels[first] - 1.0f);
+    reinterpret_cast<float2*>(L.vparam)[base + static_cast<long long>(g) * rows + row] =
+        make_float2(mn, __frcp_rn(scale));
+    m[2 * H * 128 + g * rows + row] = __float2half_rn(mn);
+    m[2 * H * 128 + G * rows + g * rows + row] = __float2half_rn(scale);
+  }
+}
+
 // Epilogue of the MMA quant kernel: read this thread's row (its TMEM lane),
 // quantize, pack to W bits and stage the 16*W-byte row in shared memory with
 // an odd pitch of (W|1) 16-byte chunks, so the 8 threads sharing a bank
@@ -1704,34 +1738,37 @@ __global__ void __launch_bounds__(kWsProdThreads, 1) k_quant_ws(LayerLaunch L) {
     ItemCursor cur;
     cursor_init(cur);
     int kp_key = -1;  // (item, head) whose key parameters kp holds
+    // Value (min, 1/scale) of this thread's row in job kk (k_value_params
+    // computed them); loaded one job of the group ahead, so the load's
+    // latency hides behind the current job.  The plane is the CTA's; the
+    // item of job kk is tracked by (pr, tiles [pt0, pt1)) only.
+    int pr = 0, pt0 = 0, pt1 = 0;
+    auto load_vp = [&](int kk) -> float2 {
+      if (M.plane != 1 || kk >= n) return make_float2(0.f, 0.f);
+      const int tile = ws_job(M, kk).tile;
+      if (tile < pt0 || tile >= pt1) {
+        pr = find_item(L.rt.tile_prefix, L.rt.num_req, tile);
+        pt0 = L.rt.tile_prefix[pr];
+        pt1 = L.rt.tile_prefix[pr + 1];
+      }
+      const int rows = L.rt.n_rows[pr];
+      const int prow = (tile - pt0) * kTileRows + lane_id;
+      if (prow >= rows) return make_float2(0.f, 0.f);
+      const int grp = L.lps[L.rt.slot[pr]].group_of_head[M.h];
+      return reinterpret_cast<const float2*>(L.vparam)[L.rt.row_off[pr] * H +
+                                                       static_cast<long long>(grp) * rows + prow];
+    };
+    float2 vp_next = load_vp(g);
     for (int k = g; k < n; k += kWsGroups) {
       const PJob jb = ws_job(M, k);
       cursor_seek(L, cur, jb.tile);
       const ItemCtx& c = cur.c;
       const int pk = c.r * H + jb.h;
       const int row = c.row0 + lane_id;
-      const bool exists = row < c.rows, valid = row < c.ntok;
-      float vmin = 0.f, vrcp = 0.f;
-      if (jb.plane == 1 && exists) {
-        // both halves of the row compute it (no exchange); half 0 publishes
-        if (half == 0) {
-          value_row_params(L, c, jb.h, row, &vmin, &vrcp);
-        } else {
-          const LayerParams* lp = c.lp;
-          const int grp = lp->group_of_head[jb.h];
-          float mn = INFINITY, mx = -INFINITY;
-          for (int hh = 0; hh < lp->H; ++hh) {
-            if (lp->group_of_head[hh] != grp) continue;
-            const float* e = vstat_entry(L, c, hh, row);
-            mn = fminf(mn, e[0]);
-            mx = fmaxf(mx, e[1]);
-          }
-          const float scale = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), kRangeEps),
-                                        lp->value_levels[jb.h] - 1.0f);
-          vmin = mn;
-          vrcp = __frcp_rn(scale);
-        }
-      }
+      const bool valid = row < c.ntok;
+      const float2 vp = vp_next;
+      vp_next = load_vp(k + kWsGroups);
+      const float vmin = vp.x, vrcp = vp.y;
       if (jb.plane == 0 && (pk != kp_key || c.row0 == 0)) {  // row0 == 0 publishes the metadata
         // kp's readers of an earlier job finished before that job's staging
         // barrier, which this thread has passed
@@ -2529,6 +2566,17 @@ int kvs_quant(const LayerLaunch* Lp) {
   } else {
     k_quant_simt<<<grid, 128, 0, s>>>(L);
   }
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Value parameters for the warp-specialized quantize kernel (engine 0),
+// after the stats kernel; max_rows = the largest item's row count.
+int kvs_value_params(const LayerLaunch* Lp, int max_rows) {
+  const LayerLaunch& L = *Lp;
+  if (L.rt.num_req <= 0 || max_rows <= 0) return 0;
+  if (L.vparam == nullptr) return -2;
+  dim3 grid((max_rows + 255) / 256, L.rt.num_req);
+  k_value_params<<<grid, 256, 0, static_cast<cudaStream_t>(L.stream)>>>(L);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -84,6 +84,10 @@ struct LayerLaunch {
   // trace[(cta * trace_jobs + job) * 8 + event] for CTAs < kTraceCtas.
   unsigned long long* trace;
   int trace_jobs;
+  // Per-row value group (min, 1/scale), [sum rows][H][2] indexed by group
+  // like vstat by head; written by k_value_params before the
+  // warp-specialized quantize kernel, which reads it (engine 0 only).
+  float* vparam;
 };
 constexpr int kTraceCtas = 8;
 

@@ -826,6 +826,11 @@ def quantize(slots: LayerSlots, items: WorkItems, codes: Optional[torch.Tensor] 
     lb = lib()
     check(lb.kvs_init_key_stats(kstat.data_ptr(), n_pairs, L.stream), "init_key_stats")
     check(lb.kvs_stats(ctypes.byref(L)), "stats")
+    if engine == ENGINE_TCGEN05:  # value (min, 1/scale) per row and group, once
+        vparam = ws.buf("vparam", 2 * items.total_rows * slots.num_heads * 4, torch.float32)
+        L.vparam = vparam.data_ptr()
+        check(lb.kvs_value_params(ctypes.byref(L), max(items.n_rows, default=0)),
+              "value_params")
     check(lb.kvs_quant(ctypes.byref(L)), "quant")
     return codes, meta
 
