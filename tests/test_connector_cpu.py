@@ -150,3 +150,41 @@ def test_scheduler_side_bookkeeping():
     m2 = prod.build_connector_meta(so2)
     assert m2.requests[0].block_ids == [1, 2, 9]
     assert prod.request_finished(req, []) == (False, None)
+
+
+def test_stats_files_and_summary(tmp_path, monkeypatch, capsys):
+    """A compressed handoff writes one compression and one decode row; the
+    summary joins them with transfer rows (a truncated row is skipped) into
+    the mean compression ratio and the median compress + comm + decompress
+    path."""
+    import json
+
+    from kvserve_hpdps_b200.utils import stats
+    paths = {k: str(tmp_path / f"{k}.jsonl") for k in ("compression", "decode", "transfer")}
+    monkeypatch.setenv("KVSERVE_COMPRESSION_STATS_PATH", paths["compression"])
+    monkeypatch.setenv("KVSERVE_DECODE_STATS_PATH", paths["decode"])
+    monkeypatch.setenv("KVSERVE_TRANSFER_STATS_PATH", paths["transfer"])
+    spec = {"enabled": True, "pipeline": ["transformer", "quantizer", "codec"],
+            "quantizer_config": {"hybrid_ratio": 0.3, "axis_key": "token",
+                                 "axis_value": "token"},
+            "codec_config": {"codec_type": "rans"}, "backend": "generic"}
+    p, c, _ = make_pair(spec)
+    handoff(p, c)
+    crow = stats.read_rows(paths["compression"])
+    assert len(crow) == 1 and len(stats.read_rows(paths["decode"])) == 1
+    assert crow[0]["original_bytes"] == L * 2 * 3 * BS * H * D * 2
+    stats.write_transfer_stats("r1", 2.0, 3_000_000, transport="fake")
+    stats.write_transfer_stats("r2", 4.0, 5_000_000, transport="fake")
+    with open(paths["transfer"], "a") as f:
+        f.write('{"request_id": "r3", "transfer_ms": \n')
+    s = stats.summarize(**paths)
+    ratio = crow[0]["original_bytes"] / crow[0]["compressed_bytes"]
+    assert s["avg_compression_ratio"] == pytest.approx(ratio) and ratio > 2
+    assert s["transfer_rows"] == 2 and s["comm_ms"] == 3.0 and s["comm_mb"] == 4.0
+    assert s["transports"] == ["fake"]
+    assert s["xfer_path_ms"] == pytest.approx(s["compress_ms"] + 3.0 + s["decompress_ms"])
+    assert s["xfer_if_overlap_ms"] == pytest.approx(s["compress_ms"] + 3.0)
+    assert stats.main([]) == 0  # paths from the environment
+    assert json.loads(capsys.readouterr().out)["transfer_rows"] == 2
+    empty = stats.summarize(str(tmp_path / "missing.jsonl"))
+    assert empty["avg_compression_ratio"] is None and empty["xfer_path_ms"] == 0.0
