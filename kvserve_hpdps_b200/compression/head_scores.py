@@ -93,6 +93,24 @@ def synthetic_scores(num_layers: int, num_heads: int, seed: int = 0x5EED) -> tor
     return torch.rand((num_layers, num_heads), generator=g, dtype=torch.float32)
 
 
+class DuoConfigGenerator:
+    """The reference's entry points for the scores
+    (kvserve_v1/compression/config/duo_config/get_config.py:8-117):
+    ``get_scores_from_csv`` reads a shipped or saved table,
+    ``duo_attention_on_the_fly`` computes one from a model and samples
+    (:func:`kvserve_hpdps_b200.offline.duo_scores.duo_scores_on_the_fly`)."""
+
+    @staticmethod
+    def duo_attention_on_the_fly(model, samples, q_len: int = 1024, max_tokens: int = 2048,
+                                 tokenizer=None) -> torch.Tensor:
+        from kvserve_hpdps_b200.offline.duo_scores import duo_scores_on_the_fly
+        return duo_scores_on_the_fly(model, samples, q_len, max_tokens, tokenizer)
+
+    @classmethod
+    def get_scores_from_csv(cls, model_name: str) -> Optional[torch.Tensor]:
+        return get_scores_from_csv(model_name)
+
+
 def head_low_mask(scores: torch.Tensor, hybrid_ratio: float) -> torch.Tensor:
     """Bool [L, H]: True where the (layer, head) pair is LOW precision."""
     n_low = round(scores.numel() * float(hybrid_ratio))

@@ -154,3 +154,53 @@ def test_cr_methods_tool_runs():
                           methods=("custom", "kivi", "cachegen"), max_new_tokens=2)
     assert [r["method"] for r in rows] == ["custom", "kivi", "cachegen"]
     assert all(r["compression_ratio"] > 1.5 for r in rows)
+
+
+def _duo_brute_force(model, ids, q_len):
+    """The scorer's definition evaluated directly: stored layer inputs, the
+    full repeated query matrix, every query row's attention computed."""
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+    cfg = model.config
+    n_q, n_kv = cfg.num_attention_heads, cfg.num_key_value_heads
+    hs = model(ids.view(1, -1), output_hidden_states=True).hidden_states[:-1]
+    out = torch.zeros(len(hs), n_kv)
+    pos = torch.arange(q_len).view(1, -1)
+    for i, h in enumerate(hs):
+        layer = model.model.layers[i]
+        h = layer.input_layernorm(h)
+        q = layer.self_attn.q_proj(h).view(1, -1, n_q, D).mean(1, keepdim=True)
+        k = layer.self_attn.k_proj(h).view(1, -1, n_kv, D).mean(1, keepdim=True)
+        q = q.repeat(1, q_len, 1, 1).transpose(1, 2)
+        k = k.repeat(1, q_len, 1, 1).transpose(1, 2)
+        cos, sin = model.model.rotary_emb(h, pos)
+        q, k = apply_rotary_pos_emb(q, k, cos, sin)
+        k = k.repeat_interleave(n_q // n_kv, dim=1)
+        w = (q @ k.transpose(2, 3) / D ** 0.5).softmax(-1)[0, :, -1]  # last query row
+        out[i] = w.cumsum(-1).mean(-1).view(n_kv, -1).mean(1)
+    return out
+
+
+def test_duo_scores_on_the_fly_match_definition(model, tmp_path, monkeypatch):
+    from kvserve_hpdps_b200.compression.head_scores import DuoConfigGenerator
+    from kvserve_hpdps_b200.offline.duo_scores import duo_scores_on_the_fly, main, \
+        save_scores_csv
+    g = torch.Generator().manual_seed(7)
+    samples = [torch.randint(0, 256, (n,), generator=g) for n in (90, 140)]
+    with torch.no_grad():
+        want = sum(_duo_brute_force(model, s, 64) for s in samples) / 2
+    got = duo_scores_on_the_fly(model, samples, q_len=64, max_tokens=512)
+    assert got.shape == (L, H)
+    assert torch.allclose(got, want, atol=1e-5, rtol=1e-5)
+    assert bool(((got > 1 / 64 - 1e-6) & (got <= 1 + 1e-6)).all())
+    # truncation to max_tokens, the class entry point and the CSV round trip
+    short = duo_scores_on_the_fly(model, [samples[1][:50]], q_len=64)
+    assert torch.allclose(DuoConfigGenerator.duo_attention_on_the_fly(
+        model, [samples[1]], q_len=64, max_tokens=50), short)
+    monkeypatch.chdir(tmp_path)
+    save_scores_csv(got, "tiny-duo-model_scores.csv")
+    back = DuoConfigGenerator.get_scores_from_csv("/models/tiny-duo-model")
+    assert torch.allclose(back, got)
+    assert main(["--model", "random:Qwen2.5-7B", "--layers", "2", "--hidden", "512",
+                 "--q-len", "32", "--max-tokens", "64", "--random-samples", "1",
+                 "--out", "r.csv"]) == 0
+    assert (tmp_path / "r.csv").read_text().count("\n") == 2
