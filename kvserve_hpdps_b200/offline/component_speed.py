@@ -12,7 +12,18 @@ Here the stages are the fused kernels of this package:
 * ``lc_enc`` / ``lc_dec``: the LC-style BIT_2 + RZE_1 codec over the codes;
 * ``block_copy``: the paged gather of raw KV (the uncompressed path).
 
-Every figure is CUDA-event time on the launching stream after warm-up,
+``--methods custom,kivi,cachegen,hadamard,minmax`` times the offline methods
+instead (the reference's kivi_speed.py, cachegen-*_speed.py,
+hadamard_speed.py and quantizer_speed.py), on any device, through the
+caches the accuracy harness uses: ``compress`` is a fresh cache's prefill
+update over every layer, ``reconstruct`` the first decode step (one token per
+layer), which rebuilds the layer's KV from its codes.  ``hadamard`` is the
+per-head randomized Hadamard (transform / inverse) and ``minmax`` the
+reference quantizer formula per (head, channel) for keys and per token for
+values (quantize / dequantize).  CUDA figures are event times; CPU figures
+are wall time.
+
+Every fused-stage figure is CUDA-event time on the launching stream after warm-up,
 averaged over ``--iters`` launches; the input of a full request (28 layers,
 8K tokens, 4 heads: 470 MB) is larger than L2, so no flush is needed at
 that size.  Rates are GB/s of ORIGINAL bf16 KV (the reference's unit).
@@ -21,6 +32,7 @@ Usage::
 
   python -m kvserve_hpdps_b200.offline.component_speed --layers 28 --tokens 8192
   python -m kvserve_hpdps_b200.offline.component_speed --only quant --layers 2 --iters 3
+  python -m kvserve_hpdps_b200.offline.component_speed --methods kivi,cachegen --tokens 4096
 """
 
 from __future__ import annotations
@@ -32,6 +44,7 @@ import sys
 import torch
 
 STAGES = ("quant", "dequant", "rans_enc", "rans_dec", "lc_enc", "lc_dec", "block_copy")
+METHODS = ("custom", "kivi", "cachegen", "hadamard", "minmax")
 
 
 def _timeit(fn, iters: int, warmup: int = 3) -> float:
@@ -45,6 +58,93 @@ def _timeit(fn, iters: int, warmup: int = 3) -> float:
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
+
+
+def _timeit_on(device: torch.device, fn, iters: int, warmup: int = 3) -> float:
+    """Mean ms per call: CUDA events on the current stream, else wall time."""
+    if device.type == "cuda":
+        return _timeit(fn, iters, warmup)
+    import time
+    for _ in range(warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        fn()
+    return (time.perf_counter() - t0) * 1e3 / iters
+
+
+def run_methods(methods: tuple[str, ...] = METHODS, layers: int = 28, tokens: int = 8192,
+                heads: int = 4, head_dim: int = 128, iters: int = 5, warmup: int = 2,
+                device: str | None = None, dtype: torch.dtype = torch.bfloat16,
+                seed: int = 1) -> list[dict]:
+    """Compress / reconstruct times of the offline methods on random KV with
+    outlier key channels (``[1, heads, tokens, head_dim]`` per layer)."""
+    from kvserve_hpdps_b200.compression.head_scores import synthetic_scores
+    from kvserve_hpdps_b200.offline.caches import HeadHadamard
+    from kvserve_hpdps_b200.offline.caches.common import minmax_codes, minmax_values
+    from kvserve_hpdps_b200.offline.lm_harness import make_cache
+    dev = torch.device(device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    ks, vs = [], []
+    for _ in range(layers):
+        k = torch.randn(1, heads, tokens, head_dim, generator=g)
+        k[..., :4] *= 12.0
+        ks.append(k.to(dev, dtype))
+        vs.append(torch.randn(1, heads, tokens, head_dim, generator=g).to(dev, dtype))
+    nk = torch.randn(1, heads, 1, head_dim, generator=g).to(dev, dtype)
+    nbytes = layers * 2 * tokens * heads * head_dim * ks[0].element_size()
+    scores = synthetic_scores(layers, heads)
+    params = {"custom": dict(transform_type="hadamard", heads_selection=0.5,
+                             high_key_max_value=16, high_value_max_value=16,
+                             low_key_max_value=8, low_value_max_value=8),
+              "kivi": dict(nbits=2, q_group_size=32, residual_length=128),
+              "cachegen": dict(quantization_level=1)}
+    rows = []
+
+    def row(method, phase, ms, **kw):
+        rows.append({"method": method, "phase": phase, "ms": round(ms, 4),
+                     "gbps": round(nbytes / ms / 1e6, 3), "layers": layers, "tokens": tokens,
+                     "heads": heads, "device": dev.type, **kw})
+
+    for m in methods:
+        if m in params:
+            def prefill(m=m):
+                c = make_cache(m, layers, scores if m == "custom" else None, **params[m])
+                for l in range(layers):
+                    c.update(ks[l], vs[l], l)
+                return c
+
+            def decode(c):
+                for l in range(layers):
+                    c.update(nk, nk, l)
+
+            row(m, "compress", _timeit_on(dev, prefill, iters, warmup))
+            caches = [prefill() for _ in range(iters + warmup)]
+            it = iter(caches)
+            row(m, "reconstruct", _timeit_on(dev, lambda: decode(next(it)), iters, warmup),
+                compression_ratio=round(float(caches[0].compute_compression_ratio()), 3)
+                if hasattr(caches[0], "compute_compression_ratio") else None)
+        elif m == "hadamard":
+            had = HeadHadamard()
+            ys = [had.transform(ks[l], l) for l in range(layers)]
+            row(m, "compress", _timeit_on(dev, lambda: [had.transform(ks[l], l)
+                                                         for l in range(layers)
+                                                         for _ in (0, 1)], iters, warmup))
+            row(m, "reconstruct", _timeit_on(dev, lambda: [had.inverse(ys[l], l)
+                                                            for l in range(layers)
+                                                            for _ in (0, 1)], iters, warmup))
+        elif m == "minmax":
+            def quant():
+                return [(minmax_codes(ks[l], 16, [2]), minmax_codes(vs[l], 16, [1, 3]))
+                        for l in range(layers)]
+            packs = quant()
+            row(m, "compress", _timeit_on(dev, quant, iters, warmup))
+            row(m, "reconstruct", _timeit_on(dev, lambda: [(minmax_values(*a), minmax_values(*b))
+                                                            for a, b in packs],
+                                             iters, warmup))
+        else:
+            raise ValueError(f"unknown method {m!r}; expected one of {METHODS}")
+    return rows
 
 
 def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
@@ -150,7 +250,15 @@ def main(argv=None) -> int:
                     help="bits per code in the code buffer (4: two codes per rANS symbol)")
     ap.add_argument("--hybrid-ratio", type=float, default=None,
                     help="use the default mode's per-layer plans at this hybrid_ratio")
+    ap.add_argument("--methods", default=None,
+                    help=f"time offline methods instead of the fused stages: {','.join(METHODS)}")
+    ap.add_argument("--device", default=None, help="--methods device (default: cuda if present)")
     args = ap.parse_args(argv)
+    if args.methods:
+        for r in run_methods(tuple(args.methods.split(",")), args.layers, args.tokens, args.heads,
+                             iters=args.iters, warmup=args.warmup, device=args.device):
+            print(json.dumps(r))
+        return 0
     if not torch.cuda.is_available():
         print(json.dumps({"unavailable": "no CUDA device"}))
         return 0

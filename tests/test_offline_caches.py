@@ -204,3 +204,21 @@ def test_duo_scores_on_the_fly_match_definition(model, tmp_path, monkeypatch):
                  "--q-len", "32", "--max-tokens", "64", "--random-samples", "1",
                  "--out", "r.csv"]) == 0
     assert (tmp_path / "r.csv").read_text().count("\n") == 2
+
+
+def test_component_speed_methods_run_on_cpu(capsys):
+    import json
+
+    from kvserve_hpdps_b200.offline import component_speed as CS
+    rows = CS.run_methods(layers=2, tokens=256, heads=2, iters=1, warmup=1, device="cpu")
+    got = {(r["method"], r["phase"]) for r in rows}
+    assert got == {(m, p) for m in CS.METHODS for p in ("compress", "reconstruct")}
+    assert all(r["ms"] > 0 and r["gbps"] > 0 for r in rows)
+    crs = {r["method"]: r["compression_ratio"] for r in rows if r.get("compression_ratio")}
+    assert set(crs) == {"custom", "kivi", "cachegen"} and min(crs.values()) > 1.5
+    with pytest.raises(ValueError):
+        CS.run_methods(("zip",), layers=1, tokens=16, heads=1, device="cpu")
+    assert CS.main(["--methods", "minmax", "--layers", "1", "--tokens", "64", "--heads", "1",
+                    "--iters", "1", "--warmup", "1", "--device", "cpu"]) == 0
+    assert [json.loads(x)["phase"] for x in capsys.readouterr().out.splitlines()] == \
+        ["compress", "reconstruct"]
