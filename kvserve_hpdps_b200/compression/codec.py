@@ -191,3 +191,30 @@ class LCCodec(KVServeCodec):
         kwargs = dict(kwargs)
         kwargs["codec_type"] = "lc"
         super().__init__(**kwargs)
+
+
+class nvCOMPCodec:  # noqa: N801 - the reference's class name
+    """The reference's standalone nvCOMP wrapper interface
+    (kvserve_v1/compression/codec/nvcomp_func.py:10-121): ``encode(tensor)``
+    returns the uint8 stream of the tensor's bytes, ``decode(stream,
+    original_dtype, original_shape, device)`` rebuilds the tensor.  The
+    algorithm name selects this package's codec as in
+    :func:`resolve_codec` (``Bitcomp`` -> bit-packing, the others -> rANS);
+    no nvCOMP library is involved."""
+
+    def __init__(self, algorithm: str = "ANS", **kwargs: Any):
+        self.algorithm = algorithm
+        self.codec = resolve_codec("nvcomp", algorithm)
+
+    def encode(self, tensor: torch.Tensor) -> torch.Tensor:
+        if tensor.numel() == 0:
+            return torch.empty(0, dtype=torch.uint8, device=tensor.device)
+        return encode_bytes(tensor, self.codec)
+
+    def decode(self, compressed_tensor: torch.Tensor, original_dtype: str,
+               original_shape: list, device: str, **kwargs: Any) -> torch.Tensor:
+        dtype = getattr(torch, str(original_dtype).replace("torch.", ""))
+        if compressed_tensor.numel() == 0:
+            return torch.empty([int(s) for s in original_shape], dtype=dtype, device=device)
+        raw = decode_bytes(compressed_tensor, device)
+        return raw.view(dtype).reshape([int(s) for s in original_shape])

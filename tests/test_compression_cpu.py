@@ -264,3 +264,78 @@ def test_cpu_roundtrip_example_runs(capsys):
     assert mod.main(["--layers", "2", "--tokens", "256"]) == 0
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["compression_ratio"] > 2.0 and line["cosine"] > 0.98
+
+
+def test_split_helpers_match_the_quantizer_layout():
+    """head_split / head_restore / head_reconstruct and the layer forms
+    invert each other, and the generic quantizer packs LOW heads first in
+    exactly the order head_split gives."""
+    from kvserve_hpdps_b200.compression import split as S
+    from kvserve_hpdps_b200.compression.quantizer import KVServeQuantizer
+    x = torch.randn(3, 16, 4, 128).to(torch.bfloat16)
+    mask = torch.tensor([[True, False, True, False], [False, False, False, False]])
+    low, high = S.head_split(0, x, mask)
+    assert torch.equal(low, x[:, :, [0, 2]]) and torch.equal(high, x[:, :, [1, 3]])
+    packed = torch.cat([low, high], dim=2)
+    lo2, hi2 = S.head_restore(0, packed, mask)
+    assert torch.equal(lo2, low) and torch.equal(hi2, high)
+    assert torch.equal(S.head_reconstruct(0, lo2, hi2, mask), x)
+    lo3, hi3 = S.head_split(1, x, mask)  # no LOW head in layer 1
+    assert lo3.shape[2] == 0 and torch.equal(S.head_reconstruct(1, lo3, hi3, mask), x)
+    lm = torch.tensor([False, True])
+    a, b = S.layer_split(1, x, lm)
+    assert a is x and b.numel() == 0 and S.layer_reconstruct(1, a, b, lm) is x
+    a, b = S.layer_restore(0, x, lm)
+    assert a.numel() == 0 and b is x and S.layer_reconstruct(0, a, b, lm) is x
+    for bad in (None, mask.float()):
+        with pytest.raises(ValueError):
+            S.head_split(0, x, bad)
+        with pytest.raises(ValueError):
+            S.layer_split(0, x, None if bad is None else lm.float())
+    qz = KVServeQuantizer(model_name="Qwen2.5-7B-Instruct", hybrid_ratio=0.5,
+                          axis_key="token", axis_value="token")
+    m = qz.head_scores_mask
+    layer = next(i for i in range(m.shape[0]) if 0 < int(m[i].sum()) < m.shape[1])
+    kv = torch.randn(2, 3, 16, m.shape[1], 128).to(torch.bfloat16)
+    q, meta = qz.quantize(layer, kv)
+    lo_k, hi_k = S.head_restore(layer, q[0], m)
+    from kvserve_hpdps_b200.compression.quantizer import quantize
+    want_lo, _ = quantize(qz.low_key_max_value, S.head_split(layer, kv[0], m)[0], "token")
+    want_hi, _ = quantize(qz.high_key_max_value, S.head_split(layer, kv[0], m)[1], "token")
+    assert torch.equal(lo_k, want_lo) and torch.equal(hi_k, want_hi)
+
+
+def test_reference_module_paths_alias_this_package():
+    """With the compat directory on PYTHONPATH every reference module path
+    imports (in a child process, so the alias never meets a real
+    ``kvserve_v1`` here) and exposes the same objects as this package."""
+    import os
+    import subprocess
+    import sys
+
+    import kvserve_hpdps_b200.compat as compat
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = "\n".join([
+        "import importlib, kvserve_v1",
+        "from kvserve_v1 import _ALIASES",
+        "for a in _ALIASES: importlib.import_module('kvserve_v1.' + a)",
+        "from kvserve_v1.connector.compressed_kv_connector import CompressedKVConnector as A",
+        "from kvserve_hpdps_b200.connector.compressed_kv_connector import "
+        "CompressedKVConnector as B",
+        "assert A is B and kvserve_v1.CompressedKVConnector is B",
+        "from kvserve_v1.compression.tilelang_manager import TileLangCompressionManager as T",
+        "from kvserve_hpdps_b200.compression.fused_manager import FusedCompressionManager as F",
+        "assert T is F",
+        "from kvserve_v1.compression.quantizer.split_func import head_restore",
+        "from kvserve_v1.compression.codec.nvcomp_func import nvCOMPCodec",
+        "from kvserve_v1.compression.controller.analytical_model import AnalyticalModel",
+        "from kvserve_v1.compression.compression_manager import DEFAULT_COMPRESSION_CONFIG",
+        "import kvserve_v1.compression.wire as w, kvserve_hpdps_b200.compression.wire as w2",
+        "assert w.build_wire is w2.build_wire and w._unpack is w2._unpack",
+        "print('ALIASES', len(_ALIASES))",
+    ])
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([compat.path(), root]))
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=300, cwd=str(root))
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "ALIASES" in out.stdout
