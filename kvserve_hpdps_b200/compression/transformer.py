@@ -31,6 +31,9 @@ class HadamardTransform:
             self._signs[key] = s.to(device=device, dtype=dtype).view(1, 1, num_heads, head_dim)
         return self._signs[key]
 
+    # the reference's name (hadamard_func.py:105-159): [1, 1, heads, head_dim] +-1
+    get_rademacher_signs = signs
+
     def transform(self, layer_id: int, x: torch.Tensor) -> torch.Tensor:
         s = self.signs(layer_id, x.shape[2], x.shape[3], x.device, x.dtype)
         return fwht_fp32(x * s).to(x.dtype)

@@ -21,6 +21,10 @@ def test_rademacher_signs_follow_the_seeding_rule():
     b = torch.randint(0, 2, (128,), generator=g, dtype=torch.int8).float() * 2 - 1
     assert torch.equal(s[2], b)
     assert set(s.unique().tolist()) == {-1.0, 1.0}
+    from kvserve_hpdps_b200.compression.transformer import HadamardTransform
+    ref_api = HadamardTransform(0x3333).get_rademacher_signs(3, 4, 128, torch.device("cpu"),
+                                                              torch.float32)
+    assert ref_api.shape == (1, 1, 4, 128) and torch.equal(ref_api[0, 0], s)
 
 
 def test_fwht_is_orthonormal_and_self_inverse():
