@@ -58,6 +58,18 @@ class ProducerChannel:
             return self.sock.recv()
         return None
 
+    def discard_pending(self) -> int:
+        """Drop replies already queued on the socket (a late answer to a
+        request that timed out) so that the next ``request`` reads its own
+        reply; returns how many were dropped.  Only for channels whose every
+        incoming message is a reply."""
+        n = 0
+        with self.lock:
+            while self.sock.poll(0, zmq.POLLIN):
+                self.sock.recv()
+                n += 1
+        return n
+
     def request(self, msg: dict[str, Any], timeout_s: Optional[float] = None) -> Optional[bytes]:
         with self.lock:
             self.sock.send(pack(msg))
@@ -81,9 +93,18 @@ class ConsumerChannel:
         self.lock = threading.Lock()
 
     def poll(self, timeout_ms: int = 100) -> Optional[tuple[bytes, dict[str, Any]]]:
+        """(identity, message); a frame that is not a msgpack dict comes back
+        as ``{"cmd": None, "error": ...}`` so that the caller can refuse it
+        instead of leaving the sender waiting for a reply."""
         if self.sock.poll(timeout_ms, zmq.POLLIN):
             frames = self.sock.recv_multipart()
-            return frames[0], unpack(frames[-1])
+            try:
+                msg = unpack(frames[-1])
+            except Exception as e:  # noqa: BLE001 - any decode failure
+                return frames[0], {"cmd": None, "error": f"undecodable frame: {e}"}
+            if not isinstance(msg, dict):
+                return frames[0], {"cmd": None, "error": f"not a dict: {type(msg).__name__}"}
+            return frames[0], msg
         return None
 
     def reply(self, identity: bytes, payload: bytes) -> None:

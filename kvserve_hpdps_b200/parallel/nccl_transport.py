@@ -17,6 +17,14 @@ the consumer allocates the tensors, ACKs, and posts the receives; the
 producer then posts its sends.  The consumer only posts receives after a
 header, so no receive is pending while the engine captures CUDA graphs.
 
+Every header gets an answer: the consumer refuses (``b"1"``) a header it
+cannot read or allocate for, and an unknown command, so a producer never
+waits out its timeout on a live consumer.  A producer whose request timed
+out cannot tell whether the consumer accepted it and posted receives, and
+the next message's tensors could then be matched with those receives, so
+after a control timeout the producer refuses every later send at once
+(``ctl_failed``; logged) and the pair needs a new transport.
+
 The 2-rank process group is built from a TCPStore the consumer hosts on
 ``kv_port + tp_rank + STORE_PORT_OFFSET`` (producer rank 0, consumer rank 1).
 This transport is the baseline and the fallback of the NVLink ring transport
@@ -86,6 +94,7 @@ class NcclTransport:
             self._inflight = 0
             self._sent_lock = threading.Lock()
             self._sent: dict[str, int] = defaultdict(int)
+            self.ctl_failed = False
             self._thread = threading.Thread(target=self._send_loop, daemon=True,
                                             name="kvs-send")
             self._thread.start()
@@ -178,7 +187,18 @@ class NcclTransport:
                    "meta": meta, "body_specs": [tensor_spec(t) for t in body],
                    "aux_specs": [tensor_spec(t) for t in aux]}
             tensors = body + aux
+        if self.ctl_failed:
+            logger.error("control channel failed earlier; %s not sent", request_id)
+            return
+        stale = self._ctl.discard_pending()
+        if stale:
+            logger.warning("dropped %d stale control replies", stale)
         ack = self._ctl.request(msg, self.timeout_s)
+        if ack is None:
+            self.ctl_failed = True
+            logger.error("no answer to %s within %.1f s: the pair's message order can no longer "
+                         "be trusted, later sends are refused", request_id, self.timeout_s)
+            return
         if ack != ACK_OK:
             logger.error("consumer refused %s (%r)", request_id, ack)
             return
@@ -227,7 +247,13 @@ class NcclTransport:
                 if cmd not in ("PUT", "PUT_BUNDLE"):
                     self._handle_extra(ident, msg)
                     continue
-                rid = msg["request_id"]
+                rid = msg.get("request_id")
+                if not isinstance(rid, str) or not isinstance(msg.get("layer_names"), list):
+                    logger.error("malformed %s header refused", cmd)
+                    self._ctl.reply(ident, ACK_REFUSED)
+                    if isinstance(rid, str):
+                        self._mark_failed(rid)
+                    continue
                 if self._pg is None:
                     self._ctl.reply(ident, ACK_REFUSED)
                     self._mark_failed(rid)
@@ -239,7 +265,8 @@ class NcclTransport:
                         body = [alloc_from_spec(s, self.device) for s in msg["body_specs"]]
                         aux = [alloc_from_spec(s, self.device) for s in msg["aux_specs"]]
                         tensors = body + aux
-                except (torch.cuda.OutOfMemoryError, RuntimeError) as e:
+                except (torch.cuda.OutOfMemoryError, RuntimeError, KeyError, TypeError,
+                        ValueError, AttributeError) as e:
                     logger.error("allocation for %s failed: %s", rid, e)
                     self._ctl.reply(ident, ACK_REFUSED)
                     self._mark_failed(rid)
@@ -255,7 +282,12 @@ class NcclTransport:
                 logger.error("listener error: %s", e)
 
     def _handle_extra(self, ident: bytes, msg: dict) -> None:
-        logger.warning("unknown control message %r", msg.get("cmd"))
+        """Unknown or undecodable message: refused, so a sender waiting for
+        an answer gets one (a sender that expects none drops it before its
+        next request)."""
+        logger.warning("unknown control message %r%s", msg.get("cmd"),
+                       f" ({msg['error']})" if msg.get("error") else "")
+        self._ctl.reply(ident, ACK_REFUSED)
 
     def close(self) -> None:
         self._closed = True

@@ -110,3 +110,112 @@ def test_control_request_times_out_without_consumer():
     assert ch.request({"cmd": "PUT"}, timeout_s=0.2) is None
     assert time.time() - t0 < 5
     ch.close()
+
+
+def _collect(tr, want, seconds=60):
+    got = {}
+    deadline = time.time() + seconds
+    while time.time() < deadline and sum(len(v) for v in got.values()) < want:
+        for k, v in tr.drain_received().items():
+            got.setdefault(k, []).extend(v)
+        time.sleep(0.01)
+    return got
+
+
+def _plain_consumer(port, q, want, slow_first=0.0):
+    import kvserve_hpdps_b200.parallel.nccl_transport as nt
+    if slow_first:
+        orig = nt.alloc_from_spec
+        state = {"n": 0}
+
+        def late(spec, device):  # answers the first header only after the producer gave up
+            state["n"] += 1
+            if state["n"] == 1:
+                time.sleep(slow_first)
+                raise RuntimeError("injected late refusal")
+            return orig(spec, device)
+        nt.alloc_from_spec = late
+    tr = nt.NcclTransport(False, "127.0.0.1", port, backend="gloo", timeout_s=20)
+    got = _collect(tr, want)
+    q.put({k: [(n, None if p is None else p.tolist()) for n, p in v] for k, v in got.items()})
+    time.sleep(0.5)
+    tr.close()
+
+
+def _bad_header_producer(port, q):
+    from kvserve_hpdps_b200.parallel.control import ACK_REFUSED
+    from kvserve_hpdps_b200.parallel.nccl_transport import NcclTransport
+    tr = NcclTransport(True, "127.0.0.1", port, backend="gloo", timeout_s=20)
+    out = {}
+    for name, msg in (("no_rid", {"cmd": "PUT"}),
+                      ("bad_dtype", {"cmd": "PUT", "request_id": "bad_dtype",
+                                     "layer_names": ["l0"], "shape": [2], "dtype": "nope"}),
+                      ("unknown", {"cmd": "WHAT"})):
+        t0 = time.time()
+        out[name] = (tr._ctl.request(msg, 20) == ACK_REFUSED, time.time() - t0)
+    t0 = time.time()
+    tr._ctl.sock.send(b"\xc1\xc1")  # 0xc1 is not a msgpack type byte
+    out["garbage"] = (tr._ctl.recv(20) == ACK_REFUSED, time.time() - t0)
+    tr.send("ok", ["l0"], torch.arange(6, dtype=torch.float32))
+    out["sent"] = tr.wait_for_sent(60) and tr.sent_layers("ok") == 1 and not tr.ctl_failed
+    q.put(out)
+    time.sleep(0.5)
+    tr.close()
+
+
+def test_bad_headers_are_refused_and_the_pair_keeps_working():
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    qc, qp = ctx.Queue(), ctx.Queue()
+    c = ctx.Process(target=_plain_consumer, args=(port, qc, 2))
+    c.start()
+    time.sleep(1.0)
+    p = ctx.Process(target=_bad_header_producer, args=(port, qp))
+    p.start()
+    prod = qp.get(timeout=120)
+    got = qc.get(timeout=120)
+    p.join(30)
+    c.join(30)
+    for name in ("no_rid", "bad_dtype", "unknown", "garbage"):
+        refused, seconds = prod[name]
+        assert refused and seconds < 5, (name, prod[name])  # answered, not timed out
+    assert prod["sent"]
+    assert got["bad_dtype"] == [([], None)]  # FAILED sentinel for the refused request
+    assert got["ok"] == [(["l0"], [0.0, 1.0, 2.0, 3.0, 4.0, 5.0])]
+
+
+def _impatient_producer(port, q):
+    from kvserve_hpdps_b200.parallel.nccl_transport import NcclTransport
+    tr = NcclTransport(True, "127.0.0.1", port, backend="gloo", timeout_s=1.5)
+    tr.send("slow", ["l0"], torch.zeros(4))
+    ok1 = tr.wait_for_sent(30)
+    t0 = time.time()
+    tr.send("after", ["l0"], torch.ones(4))
+    ok2 = tr.wait_for_sent(30)
+    second_s = time.time() - t0
+    time.sleep(3.0)  # the late refusal arrives meanwhile
+    q.put({"ok": ok1 and ok2, "failed": tr.ctl_failed, "second_s": second_s,
+           "sent": tr.sent_layers("slow") + tr.sent_layers("after"),
+           "stale": tr._ctl.discard_pending()})
+    tr.close()
+
+
+def test_producer_refuses_sends_after_a_control_timeout():
+    """A header answered after the producer's timeout leaves the message
+    order unknown: the producer refuses later sends at once instead of
+    pairing their tensors with receives it cannot account for."""
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    qc, qp = ctx.Queue(), ctx.Queue()
+    c = ctx.Process(target=_plain_consumer, args=(port, qc, 1, 4.0))
+    c.start()
+    time.sleep(1.0)
+    p = ctx.Process(target=_impatient_producer, args=(port, qp))
+    p.start()
+    prod = qp.get(timeout=120)
+    got = qc.get(timeout=120)
+    p.join(30)
+    c.join(30)
+    assert prod["ok"] and prod["failed"] and prod["sent"] == 0
+    assert prod["second_s"] < 1.0 and prod["stale"] == 1
+    assert got == {"slow": [([], None)]}  # the consumer refused it (late); nothing else came
