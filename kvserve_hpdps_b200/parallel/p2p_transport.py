@@ -152,6 +152,9 @@ class P2PTransport:
             self._seq = 0
             self._inflight_msgs = 0
             self._lock = threading.Lock()
+            self._slots_cv = threading.Condition(self._lock)  # FREE returned flag slots
+            self._free_slots: deque = deque(range(self.n_flags))
+            self._slot_of: dict[int, int] = {}  # ring offset of a message -> its flag slot
             self._sent: dict[str, int] = defaultdict(int)
             self._pending: deque = deque()  # (event, request_id, member_tids, nbytes, t0)
             self._pending_cv = threading.Condition()
@@ -189,14 +192,25 @@ class P2PTransport:
                     continue
                 msg = unpack(raw)
                 if msg.get("cmd") == "FREE":
-                    for off, size in msg["regions"]:
-                        self._alloc.release(off, size)
-                    with self._lock:
-                        self._inflight_msgs -= len(msg["regions"])
+                    self._on_free(msg["regions"])
             except Exception as e:  # noqa: BLE001
                 if self._closed:  # the socket went away under close()
                     break
                 logger.error("p2p producer io error: %s", e)
+
+    def _on_free(self, regions) -> None:
+        """The consumer returned these (offset, size) ring regions: their flag
+        slots go back to the free list first (once its ring space is
+        released, an offset can belong to a new message), then the space."""
+        with self._lock:
+            for off, _ in regions:
+                slot = self._slot_of.pop(int(off), None)
+                if slot is not None:
+                    self._free_slots.append(slot)
+            self._inflight_msgs -= len(regions)
+            self._slots_cv.notify_all()
+        for off, size in regions:
+            self._alloc.release(off, size)
 
     def _completion_loop(self) -> None:
         while not self._closed:
@@ -252,19 +266,36 @@ class P2PTransport:
             self._pending_cv.notify_all()
 
     def _reserve(self, total: int) -> tuple[int, int, int]:
-        """Ring space, sequence number and flag slot of a new message."""
-        with self._lock:
-            wait_slots = self._inflight_msgs >= self.n_flags - 1
-        if wait_slots:
-            logger.warning("p2p: %d messages in flight, waiting for the consumer", self.n_flags)
-        base = self._alloc.alloc(total, self.timeout_s)
-        if base is None:
-            raise RuntimeError(f"receive ring full for {self.timeout_s}s ({total} bytes needed)")
-        with self._lock:
-            self._seq += 1
-            seq = self._seq
+        """Ring space, sequence number and flag slot of a new message.
+
+        A flag slot belongs to one message from here until the consumer's FREE
+        of that message's ring region returns it (messages may be returned
+        out of order), so a slot is never rewritten while its message is
+        pending.  With every slot taken this waits at most ``timeout_s``."""
+        deadline = time.monotonic() + self.timeout_s
+        with self._slots_cv:
+            if not self._free_slots:
+                logger.warning("p2p: %d messages in flight, waiting for the consumer",
+                               self._inflight_msgs)
+            while not self._free_slots:
+                left = deadline - time.monotonic()
+                if left <= 0:
+                    raise RuntimeError(f"{self._inflight_msgs} messages unreturned by the "
+                                       f"consumer for {self.timeout_s}s")
+                self._slots_cv.wait(timeout=min(left, 0.1))
+            slot = self._free_slots.popleft()
             self._inflight_msgs += 1
-        return base, seq, seq % self.n_flags
+        base = self._alloc.alloc(total, self.timeout_s)
+        with self._slots_cv:
+            if base is None:
+                self._free_slots.appendleft(slot)
+                self._inflight_msgs -= 1
+                self._slots_cv.notify_all()
+                raise RuntimeError(f"receive ring full for {self.timeout_s}s "
+                                   f"({total} bytes needed)")
+            self._seq += 1
+            self._slot_of[base] = slot
+            return base, self._seq, slot
 
     def send_paged(self, request_id: str, layer_names: list[str], kv_layers: list[torch.Tensor],
                    block_ids, member_tids: Optional[list[str]] = None) -> None:

@@ -219,3 +219,50 @@ def test_producer_refuses_sends_after_a_control_timeout():
     assert prod["ok"] and prod["failed"] and prod["sent"] == 0
     assert prod["second_s"] < 1.0 and prod["stale"] == 1
     assert got == {"slow": [([], None)]}  # the consumer refused it (late); nothing else came
+
+
+def _slot_state(n_flags, ring_bytes, timeout_s):
+    """The producer-side slot and ring bookkeeping of a P2PTransport, without
+    a device or a peer."""
+    import threading
+    from collections import deque
+
+    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport, RingAllocator
+    t = object.__new__(P2PTransport)
+    t.n_flags, t.timeout_s = n_flags, timeout_s
+    t._lock = threading.Lock()
+    t._slots_cv = threading.Condition(t._lock)
+    t._free_slots = deque(range(n_flags))
+    t._slot_of, t._inflight_msgs, t._seq = {}, 0, 0
+    t._alloc = RingAllocator(ring_bytes)
+    return t
+
+
+def test_p2p_flag_slots_are_reused_only_after_their_message_is_returned():
+    import threading
+    t = _slot_state(3, 1024, 0.3)
+    a, b, c = (t._reserve(256) for _ in range(3))
+    assert [m[1] for m in (a, b, c)] == [1, 2, 3]
+    assert sorted(m[2] for m in (a, b, c)) == [0, 1, 2] and t._inflight_msgs == 3
+    with pytest.raises(RuntimeError):  # every slot pending: bounded wait, then an error
+        t._reserve(256)
+    # returned out of order: the next message takes exactly the freed slot
+    # (seq 4 modulo 3 would be b's slot, still pending)
+    t._on_free([[a[0], 256]])
+    d = t._reserve(256)
+    assert d[1] == 4 and d[2] == a[2] and d[0] == a[0] and t._slot_of[d[0]] == a[2]
+    # ring space short: the slot taken for the message goes back
+    t._on_free([[b[0], 256]])
+    with pytest.raises(RuntimeError):
+        t._reserve(512)
+    assert b[2] in t._free_slots and t._inflight_msgs == 2
+    # a FREE from the io thread wakes a waiting reservation
+    t.timeout_s = 5.0
+    t._reserve(256)
+    timer = threading.Timer(0.2, t._on_free, args=([[c[0], 256]],))
+    timer.start()
+    t0 = time.time()
+    e = t._reserve(256)
+    timer.join()
+    assert e[2] == c[2] and 0.1 < time.time() - t0 < 3
+    assert t._alloc.free_bytes() == 256 and t._inflight_msgs == 3  # [768, 1024) never used
