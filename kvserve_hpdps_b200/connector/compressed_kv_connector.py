@@ -375,10 +375,12 @@ class CompressedKVConnector(KVConnectorBase_V1):
         if not isinstance(meta, CompressedKVConnectorMetadata):
             return
         streaming = self._overlap_mode == "stream" and self._num_layers > 0
+        # one deadline for the step: with a dead producer the step returns
+        # after LOAD_TIMEOUT_S, not after that long for each of its requests
+        deadline = time.monotonic() + LOAD_TIMEOUT_S
         for rm in meta.requests:
             need = self._num_layers if streaming else 1
             got = 0
-            deadline = time.monotonic() + LOAD_TIMEOUT_S
             while got < need:
                 got += self._load_available(rm, forward_context)
                 if got >= need:

@@ -188,3 +188,21 @@ def test_stats_files_and_summary(tmp_path, monkeypatch, capsys):
     assert json.loads(capsys.readouterr().out)["transfer_rows"] == 2
     empty = stats.summarize(str(tmp_path / "missing.jsonl"))
     assert empty["avg_compression_ratio"] is None and empty["xfer_path_ms"] == 0.0
+
+
+def test_load_timeout_bounds_the_whole_step(monkeypatch):
+    """Three requests whose KV never arrives: the consumer's step returns
+    after one load timeout, not one per request."""
+    import time
+
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.4)
+    _, c, _ = make_pair(None)
+    c.register_kv_caches(caches(8, 2))
+    m = CompressedKVConnectorMetadata()
+    for i in range(3):
+        m.add_request(f"d{i}", f"missing-{i}", list(range(16)), [i], BS)
+    c.bind_connector_metadata(m)
+    t0 = time.monotonic()
+    c.start_load_kv(None)
+    assert 0.35 < time.monotonic() - t0 < 1.0
