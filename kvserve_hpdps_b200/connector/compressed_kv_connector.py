@@ -353,9 +353,13 @@ class CompressedKVConnector(KVConnectorBase_V1):
             return None, None
         self._pending_send_rids |= set(finished_req_ids or ())
         done = set()
+        failed = getattr(self._transport, "failed_layers", None)
         for rid in list(self._pending_send_rids):
             tid = self._rid2tid.get(rid)
-            if tid is None or self._transport.sent_layers(tid) >= self._expected_msgs.get(tid, 1):
+            # refused or unsent messages count as out: the blocks are free to reuse
+            out = 0 if tid is None else self._transport.sent_layers(tid) + (
+                failed(tid) if failed is not None else 0)
+            if tid is None or out >= self._expected_msgs.get(tid, 1):
                 done.add(rid)
         self._pending_send_rids -= done
         for rid in done:

@@ -2,9 +2,11 @@
 
 ``FakeTransportPair.producer()`` / ``.consumer()`` implement the transport
 API; messages are cloned into the consumer's inbox in send order.  Failure
-injection on the host: ``drop_next`` silently drops the next message,
-``refuse_next`` delivers the FAILED sentinel (as a consumer that could not
-allocate), ``delay_s`` delays delivery on a timer thread.
+injection on the host: ``drop_next`` silently drops the next message (the
+producer counts it as sent), ``refuse_next`` delivers the FAILED sentinel
+(as a consumer that could not allocate; the producer counts it in
+``failed_layers``, as the refusing ACK would tell it), ``delay_s`` delays
+delivery on a timer thread.
 """
 
 from __future__ import annotations
@@ -23,6 +25,7 @@ class FakeTransportPair:
         self.lock = threading.Lock()
         self.inbox: dict[str, deque] = defaultdict(deque)
         self.sent: dict[str, int] = defaultdict(int)
+        self.failed: dict[str, int] = defaultdict(int)
         self.drop_next = 0
         self.refuse_next = 0
         self.delay_s = 0.0
@@ -40,16 +43,20 @@ class _FakeEnd:
         self.pair = pair
         self.is_sender = is_sender
 
-    def _deliver(self, rid: str, item) -> None:
+    def _deliver(self, rid: str, item) -> bool:
+        """Queue a message for the consumer; False when it was refused."""
         p = self.pair
         with p.lock:
             p.messages += 1
             if p.drop_next > 0:
                 p.drop_next -= 1
-                return
+                return True
             if p.refuse_next > 0:
                 p.refuse_next -= 1
                 item = (FAILED_LAYER_NAMES, FAILED_PAYLOAD)
+                refused = True
+            else:
+                refused = False
 
         def put():
             with p.lock:
@@ -59,32 +66,40 @@ class _FakeEnd:
             threading.Timer(p.delay_s, put).start()
         else:
             put()
+        return not refused
 
     def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
-        self._deliver(request_id, (list(layer_names), stacked_kv.clone()))
-        self._count_sent(None, request_id)
+        ok = self._deliver(request_id, (list(layer_names), stacked_kv.clone()))
+        self._count_sent(None, request_id, ok)
 
-    def _count_sent(self, member_tids: Optional[list[str]], request_id: str) -> None:
+    def _count_sent(self, member_tids: Optional[list[str]], request_id: str,
+                    ok: bool = True) -> None:
         """A message without member ids counts for its request id."""
+        table = self.pair.sent if ok else self.pair.failed
         with self.pair.lock:
             for t in (member_tids or [request_id]):
-                self.pair.sent[t] += 1
+                table[t] += 1
 
     def send_bundle(self, request_id, layer_names, meta, body_chunks, aux_tensors,
                     member_tids: Optional[list[str]] = None) -> None:
         payload = {"__bundle__": True, "meta": meta,
                    "body_chunks": [t.clone() for t in body_chunks],
                    "aux_tensors": [t.clone() for t in aux_tensors]}
-        self._deliver(request_id, (list(layer_names), payload))
-        self._count_sent(member_tids, request_id)
+        ok = self._deliver(request_id, (list(layer_names), payload))
+        self._count_sent(member_tids, request_id, ok)
 
     def sent_layers(self, tid: str) -> int:
         with self.pair.lock:
             return self.pair.sent.get(tid, 0)
 
+    def failed_layers(self, tid: str) -> int:
+        with self.pair.lock:
+            return self.pair.failed.get(tid, 0)
+
     def clear_sent(self, tid: str) -> None:
         with self.pair.lock:
             self.pair.sent.pop(tid, None)
+            self.pair.failed.pop(tid, None)
 
     def wait_for_sent(self, timeout_s: Optional[float] = None) -> bool:
         return True

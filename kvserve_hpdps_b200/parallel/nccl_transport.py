@@ -5,7 +5,9 @@ Public API of the reference transport (kvserve_v1/transport/nccl_transport.py:54
 * producer: ``send(request_id, layer_names, stacked_kv)``,
   ``send_bundle(request_id, layer_names, meta, body_chunks, aux_tensors,
   member_tids=None)``, ``sent_layers(tid)``, ``clear_sent(tid)``,
-  ``wait_for_sent()``;
+  ``wait_for_sent()``; ``failed_layers(tid)`` (new) counts the messages the
+  consumer refused or that could not be sent, so that a caller that frees a
+  request's blocks once its messages are out does not wait for them forever;
 * consumer: ``drain_received() -> {transfer_id: [(layer_names, payload)]}``
   where payload is a tensor (raw), a bundle dict (``{"__bundle__": True,
   "meta", "body_chunks", "aux_tensors"}``) or ``FAILED_PAYLOAD`` (None) when
@@ -94,6 +96,7 @@ class NcclTransport:
             self._inflight = 0
             self._sent_lock = threading.Lock()
             self._sent: dict[str, int] = defaultdict(int)
+            self._failed: dict[str, int] = defaultdict(int)
             self.ctl_failed = False
             self._thread = threading.Thread(target=self._send_loop, daemon=True,
                                             name="kvs-send")
@@ -136,9 +139,19 @@ class NcclTransport:
         with self._sent_lock:
             return self._sent.get(transfer_id, 0)
 
+    def failed_layers(self, transfer_id: str) -> int:
+        with self._sent_lock:
+            return self._failed.get(transfer_id, 0)
+
+    def _count(self, table: dict, request_id: str, member_tids) -> None:
+        with self._sent_lock:  # a message without member ids counts for its request id
+            for tid in (member_tids or [request_id]):
+                table[tid] += 1
+
     def clear_sent(self, transfer_id: str) -> None:
         with self._sent_lock:
             self._sent.pop(transfer_id, None)
+            self._failed.pop(transfer_id, None)
 
     def wait_for_sent(self, timeout_s: Optional[float] = None) -> bool:
         deadline = None if timeout_s is None else time.monotonic() + timeout_s
@@ -160,9 +173,11 @@ class NcclTransport:
                 item = self._queue.popleft()
                 self._inflight += 1
             try:
-                self._send_item(*item)
+                if not self._send_item(*item):
+                    self._count(self._failed, item[1], item[5])
             except Exception as e:  # noqa: BLE001
                 logger.error("send of %s failed: %s", item[1], e)
+                self._count(self._failed, item[1], item[5])
             finally:
                 with self._cv:
                     self._inflight -= 1
@@ -175,7 +190,8 @@ class NcclTransport:
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
 
-    def _send_item(self, kind, request_id, layer_names, payload, event, member_tids) -> None:
+    def _send_item(self, kind, request_id, layer_names, payload, event, member_tids) -> bool:
+        """One message; False when it was refused or not sent."""
         if kind == "tensor":
             t = payload
             msg = {"cmd": "PUT", "request_id": request_id, "layer_names": layer_names,
@@ -189,7 +205,7 @@ class NcclTransport:
             tensors = body + aux
         if self.ctl_failed:
             logger.error("control channel failed earlier; %s not sent", request_id)
-            return
+            return False
         stale = self._ctl.discard_pending()
         if stale:
             logger.warning("dropped %d stale control replies", stale)
@@ -198,20 +214,19 @@ class NcclTransport:
             self.ctl_failed = True
             logger.error("no answer to %s within %.1f s: the pair's message order can no longer "
                          "be trusted, later sends are refused", request_id, self.timeout_s)
-            return
+            return False
         if ack != ACK_OK:
             logger.error("consumer refused %s (%r)", request_id, ack)
-            return
+            return False
         if event is not None:
             event.synchronize()
         t0 = time.monotonic()
         self._p2p_send(tensors)
         nbytes = sum(t.numel() * t.element_size() for t in tensors)
-        with self._sent_lock:  # a message without member ids counts for its request id
-            for tid in (member_tids or [request_id]):
-                self._sent[tid] += 1
+        self._count(self._sent, request_id, member_tids)
         write_transfer_stats(request_id, (time.monotonic() - t0) * 1e3, nbytes,
                              transport="nccl" if self.backend == "nccl" else self.backend)
+        return True
 
     # ------------------------------------------------------------ consumer
     def drain_received(self) -> dict[str, list[tuple[list[str], Any]]]:

@@ -156,6 +156,7 @@ class P2PTransport:
             self._free_slots: deque = deque(range(self.n_flags))
             self._slot_of: dict[int, int] = {}  # ring offset of a message -> its flag slot
             self._sent: dict[str, int] = defaultdict(int)
+            self._failed: dict[str, int] = defaultdict(int)
             self._pending: deque = deque()  # (event, request_id, member_tids, nbytes, t0)
             self._pending_cv = threading.Condition()
             self._io = threading.Thread(target=self._producer_io, daemon=True, name="kvs-p2p-io")
@@ -239,7 +240,11 @@ class P2PTransport:
             total += _align(s)
         trailer = total           # 16-byte message checksum after the payload
         total = total + ALIGN
-        base, seq, slot = self._reserve(total)
+        try:
+            base, seq, slot = self._reserve(total)
+        except RuntimeError as e:
+            self._unsent(request_id, member_tids, e)
+            return
         from kvserve_hpdps_b200.ops import kernels as K
         ready = torch.cuda.current_stream(self.device).record_event()
         t0 = time.monotonic()
@@ -297,6 +302,15 @@ class P2PTransport:
             self._slot_of[base] = slot
             return base, self._seq, slot
 
+    def _unsent(self, request_id: str, member_tids: Optional[list[str]], err: Exception) -> None:
+        """A message that got no ring space in time is dropped (logged) and
+        counted in ``failed_layers``, as a refused message of the NCCL
+        transport; the consumer's load times out for it."""
+        logger.error("p2p: %s not sent: %s", request_id, err)
+        with self._lock:
+            for t in (member_tids or [request_id]):
+                self._failed[t] += 1
+
     def send_paged(self, request_id: str, layer_names: list[str], kv_layers: list[torch.Tensor],
                    block_ids, member_tids: Optional[list[str]] = None) -> None:
         """Raw (uncompressed) KV of one request straight from the paged
@@ -312,7 +326,11 @@ class P2PTransport:
         nbytes = raw.flat_bytes
         trailer = _align(nbytes)
         total = trailer + ALIGN
-        base, seq, slot = self._reserve(total)
+        try:
+            base, seq, slot = self._reserve(total)
+        except RuntimeError as e:
+            self._unsent(request_id, member_tids, e)
+            return
         t0 = time.monotonic()
         dev = raw.device
         ck = torch.empty(2, dtype=torch.int64, device=dev)
@@ -386,9 +404,14 @@ class P2PTransport:
         with self._lock:
             return self._sent.get(transfer_id, 0)
 
+    def failed_layers(self, transfer_id: str) -> int:
+        with self._lock:
+            return self._failed.get(transfer_id, 0)
+
     def clear_sent(self, transfer_id: str) -> None:
         with self._lock:
             self._sent.pop(transfer_id, None)
+            self._failed.pop(transfer_id, None)
 
     def wait_for_sent(self, timeout_s: Optional[float] = None) -> bool:
         deadline = None if timeout_s is None else time.monotonic() + timeout_s

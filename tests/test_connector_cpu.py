@@ -206,3 +206,16 @@ def test_load_timeout_bounds_the_whole_step(monkeypatch):
     t0 = time.monotonic()
     c.start_load_kv(None)
     assert 0.35 < time.monotonic() - t0 < 1.0
+
+
+def test_async_send_frees_blocks_of_refused_requests():
+    """A message the consumer refused still leaves the producer: with
+    asynchronous sends the request is reported finished (its blocks are
+    freed) instead of waiting for a send count that never comes."""
+    p, c, pair = make_pair(None)
+    p._async_send = True
+    pair.refuse_next = 1
+    handoff(p, c)
+    assert p._transport.sent_layers("tid-1") == 0 and p._transport.failed_layers("tid-1") == 1
+    done, _ = p.get_finished({"r1"})
+    assert done == {"r1"} and p._transport.failed_layers("tid-1") == 0

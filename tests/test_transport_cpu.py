@@ -59,7 +59,8 @@ def _producer(port, q):
     tr.send("t_fail", ["l0"], torch.zeros(13, 13))
     ok = tr.wait_for_sent(60)
     q.put({"ok": ok, "sent_a": tr.sent_layers("a"), "sent_b": tr.sent_layers("b"),
-           "sent_x": tr.sent_layers("x")})
+           "sent_x": tr.sent_layers("x"), "failed": tr.failed_layers("t_fail"),
+           "sent_fail": tr.sent_layers("t_fail")})
     time.sleep(0.5)
     tr.close()
 
@@ -78,6 +79,7 @@ def test_nccl_transport_protocol_over_gloo():
     p.join(30)
     c.join(30)
     assert prod["ok"] and prod["sent_a"] == 1 and prod["sent_b"] == 1 and prod["sent_x"] == 0
+    assert prod["failed"] == 1 and prod["sent_fail"] == 0  # the refusal is counted
     assert got["t_raw"][0][0] == ["l0", "l1"]
     assert got["t_raw"][0][1] == torch.arange(12, dtype=torch.float32).view(2, 6).tolist()
     names, b = got["t_bundle"][0]
@@ -194,8 +196,9 @@ def _impatient_producer(port, q):
     ok2 = tr.wait_for_sent(30)
     second_s = time.time() - t0
     time.sleep(3.0)  # the late refusal arrives meanwhile
-    q.put({"ok": ok1 and ok2, "failed": tr.ctl_failed, "second_s": second_s,
+    q.put({"ok": ok1 and ok2, "ctl_failed": tr.ctl_failed, "second_s": second_s,
            "sent": tr.sent_layers("slow") + tr.sent_layers("after"),
+           "failed": tr.failed_layers("slow") + tr.failed_layers("after"),
            "stale": tr._ctl.discard_pending()})
     tr.close()
 
@@ -216,7 +219,7 @@ def test_producer_refuses_sends_after_a_control_timeout():
     got = qc.get(timeout=120)
     p.join(30)
     c.join(30)
-    assert prod["ok"] and prod["failed"] and prod["sent"] == 0
+    assert prod["ok"] and prod["ctl_failed"] and prod["failed"] == 2 and prod["sent"] == 0
     assert prod["second_s"] < 1.0 and prod["stale"] == 1
     assert got == {"slow": [([], None)]}  # the consumer refused it (late); nothing else came
 
