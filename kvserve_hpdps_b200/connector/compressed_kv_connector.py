@@ -262,11 +262,20 @@ class CompressedKVConnector(KVConnectorBase_V1):
             ready = torch.cuda.current_stream().record_event()
             requests = [(rm.block_ids, len(rm.token_ids)) for rm in meta.requests]
             tids = [rm.transfer_id for rm in meta.requests]
-            with torch.cuda.stream(self._side_stream):
-                self._side_stream.wait_event(ready)
-                cd = comp.compress_paged_requests([kv_layer], [layer_index(layer_name)], requests,
-                                                  member_tids=tids, trim=False)
-                self._send_compressed(tids[0], [layer_name], cd, member_tids=tids)
+            try:
+                with torch.cuda.stream(self._side_stream):
+                    self._side_stream.wait_event(ready)
+                    cd = comp.compress_paged_requests([kv_layer], [layer_index(layer_name)],
+                                                      requests, member_tids=tids, trim=False)
+                    self._send_compressed(tids[0], [layer_name], cd, member_tids=tids)
+            except Exception:  # noqa: BLE001
+                # as in the off mode: a compression failure sends this layer's raw
+                # KV, one message per request (the consumer still counts one
+                # message per layer for each transfer id)
+                logger.exception("compression of %s failed; sending raw KV", layer_name)
+                for rm in meta.requests:
+                    raw = extract_kv_from_layer_by_blocks(kv_layer, rm.block_ids).unsqueeze(0)
+                    self._transport.send(rm.transfer_id, [layer_name], raw)
             for t in tids:
                 self._expected_msgs[t] = self._num_layers
 

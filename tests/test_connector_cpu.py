@@ -219,3 +219,22 @@ def test_async_send_frees_blocks_of_refused_requests():
     assert p._transport.sent_layers("tid-1") == 0 and p._transport.failed_layers("tid-1") == 1
     done, _ = p.get_finished({"r1"})
     assert done == {"r1"} and p._transport.failed_layers("tid-1") == 0
+
+
+def test_stream_mode_consumer_takes_raw_per_layer_messages():
+    """The stream mode's fallback when compression fails: one raw message per
+    layer and request ([1, 2, blocks, block_size, heads, dim]); the consumer
+    waits for one message per layer and scatters each into its layer."""
+    from kvserve_hpdps_b200.utils.kv_utils import extract_kv_from_layer_by_blocks
+    p, c, pair = make_pair(None)
+    c._overlap_mode, c._num_layers = "stream", L
+    pc, cc = caches(8, 1), caches(8, 2)
+    c.register_kv_caches(cc)
+    for name in sorted(pc, key=layer_index):
+        raw = extract_kv_from_layer_by_blocks(pc[name], [5, 1, 7]).unsqueeze(0)
+        p._transport.send("tid-s", [name], raw)
+    c.bind_connector_metadata(meta_for("d1", "tid-s", 40, [2, 6, 0]))
+    c.start_load_kv(None)
+    for name in pc:
+        assert torch.equal(cc[name][:, [2, 6, 0]], pc[name][:, [5, 1, 7]])
+    assert pair.messages == L
