@@ -343,3 +343,24 @@ def test_reference_module_paths_alias_this_package():
                          timeout=300, cwd=str(root))
     assert out.returncode == 0, out.stderr[-2000:]
     assert "ALIASES" in out.stdout
+
+
+def test_codec_ops_are_registered_torch_operators():
+    """torch.ops.kvserve codecs: round trip on CPU, fake (meta) shapes with a
+    data-dependent stream length, and torch.library.opcheck."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from torch.fx.experimental.symbolic_shapes import ShapeEnv
+
+    import kvserve_hpdps_b200.ops.library  # noqa: F401 - registers the ops
+    x = torch.randint(0, 12, (70000,), dtype=torch.uint8)
+    ops = torch.ops.kvserve
+    for enc, dec in ((ops.rans_encode, ops.rans_decode), (ops.lc_encode, ops.lc_decode)):
+        s = enc(x)
+        assert s.dtype == torch.uint8 and s.numel() < x.numel()
+        assert torch.equal(dec(s, x.numel()), x)
+        torch.library.opcheck(enc.default, (x,))
+        torch.library.opcheck(dec.default, (s, x.numel()))
+    with FakeTensorMode(shape_env=ShapeEnv()):
+        fs = ops.rans_encode(torch.empty(1000, dtype=torch.uint8))
+        assert fs.dtype == torch.uint8 and not isinstance(fs.shape[0], int)
+        assert ops.lc_decode(fs, 1000).shape == (1000,)
