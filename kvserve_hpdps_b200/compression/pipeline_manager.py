@@ -76,8 +76,19 @@ class CompressionManager:
 
     def _compress_range(self, data: torch.Tensor, start: int, request_id: str, meta: dict):
         qparams: list = []
-        layers = [self._forward_layer(start + i, data[i], qparams) for i in range(data.shape[0])]
-        buf = torch.stack(layers, 0).contiguous()
+        if "quantizer" in self.config.pipeline and hasattr(self.quantizer, "quantize_into"):
+            # codes land in the heads-outer buffer directly (no per-layer stack)
+            L, _, B, bs, H, D = data.shape
+            buf = torch.empty((L, 2, H, B, bs, D), dtype=torch.uint8, device=data.device)
+            for i in range(L):
+                x = data[i]
+                if "transformer" in self.config.pipeline:
+                    x = self.transformer.transform(start + i, x)
+                qparams.append(self.quantizer.quantize_into(start + i, x, buf[i]))
+        else:
+            layers = [self._forward_layer(start + i, data[i], qparams)
+                      for i in range(data.shape[0])]
+            buf = torch.stack(layers, 0).contiguous()
         if qparams:
             meta["quantization_params"] = qparams
             meta["quantization_applied"] = True
@@ -146,8 +157,16 @@ class CompressionManager:
         target = getattr(torch, meta.get("original_dtype", "bfloat16"))
         out = torch.empty((L, cur.shape[1], cur.shape[3], cur.shape[4], cur.shape[2],
                            cur.shape[5]), dtype=target, device=cur.device)
+        direct = "quantizer" in self.config.pipeline and hasattr(self.quantizer, "dequantize_into")
         for i in range(L):
             x = cur[i].permute(0, 2, 3, 1, 4)
+            if direct:
+                # dequantized parts land in the output layer directly
+                self.quantizer.dequantize_into(start + i, x, meta["quantization_params"][i],
+                                               out[i])
+                if "transformer" in self.config.pipeline:
+                    out[i].copy_(self.transformer.inverse(start + i, out[i]).to(target))
+                continue
             if "quantizer" in self.config.pipeline:
                 x = self.quantizer.dequantize(start + i, x, meta["quantization_params"][i])
             if "transformer" in self.config.pipeline:

@@ -31,18 +31,26 @@ from kvserve_hpdps_b200.compression.head_scores import (get_scores_from_csv, hea
 _AXES = {"channel": (0, 1), "token": (2, 3), "tensor": (0, 1, 2, 3)}
 
 
-def quantize(max_value: float, x: torch.Tensor, axis: str) -> tuple[torch.Tensor, dict]:
+def _levels(max_value: float, x: torch.Tensor, axis: str) -> tuple[torch.Tensor, dict]:
+    """Quantized levels in ``x``'s dtype (whole numbers in [0, max_value])
+    and the metadata."""
     dtype = str(x.dtype).replace("torch.", "")
-    if x.numel() == 0:
-        return x.to(torch.uint8), {"min_val": None, "quant_scale": None,
-                                   "original_dtype": dtype, "quant_dtype": "uint8"}
     dims = _AXES[axis]
     mx = torch.amax(x, dim=dims, keepdim=True)
     mn = torch.amin(x, dim=dims, keepdim=True)
     scale = (mx - mn).clamp_(min=1e-5).div_(max_value - 1)
-    q = x.sub(mn).div_(scale).round_().clamp_(0, max_value).to(torch.uint8)
+    q = x.sub(mn).div_(scale).round_().clamp_(0, max_value)
     return q, {"min_val": mn.to(x.dtype), "quant_scale": scale.to(x.dtype),
                "original_dtype": dtype, "quant_dtype": "uint8"}
+
+
+def quantize(max_value: float, x: torch.Tensor, axis: str) -> tuple[torch.Tensor, dict]:
+    if x.numel() == 0:
+        return x.to(torch.uint8), {"min_val": None, "quant_scale": None,
+                                   "original_dtype": str(x.dtype).replace("torch.", ""),
+                                   "quant_dtype": "uint8"}
+    q, meta = _levels(max_value, x, axis)
+    return q.to(torch.uint8), meta
 
 
 def dequantize(q: torch.Tensor, meta: dict) -> torch.Tensor:
@@ -125,6 +133,58 @@ class KVServeQuantizer(Quantizer):
         return torch.stack([k, v], 0), {
             "high_key_meta": hkm, "high_value_meta": hvm, "low_key_meta": lkm,
             "low_value_meta": lvm, "original_dtype": str(tensor.dtype).replace("torch.", "")}
+
+    def quantize_into(self, layer_id: int, tensor: torch.Tensor, out: torch.Tensor) -> dict:
+        """:meth:`quantize` of one layer ``[2, blocks, block_size, heads,
+        dim]`` written straight into ``out`` (uint8 ``[2, heads, blocks,
+        block_size, dim]``: the quantized tensor in heads-outer order, LOW
+        heads first), the codes cast to uint8 as they are stored; returns the
+        metadata.  Same codes and metadata as ``quantize`` followed by
+        ``permute(0, 3, 1, 2, 4)``, without the concatenation and stacking
+        copies."""
+        empty = {"min_val": None, "quant_scale": None,
+                 "original_dtype": str(tensor.dtype).replace("torch.", ""),
+                 "quant_dtype": "uint8"}
+        meta = {"original_dtype": str(tensor.dtype).replace("torch.", "")}
+        for kv, (x, hi_v, lo_v, axis, hi_k, lo_k) in enumerate((
+                (tensor[0], self.high_key_max_value, self.low_key_max_value, self.axis_key,
+                 "high_key_meta", "low_key_meta"),
+                (tensor[1], self.high_value_max_value, self.low_value_max_value,
+                 self.axis_value, "high_value_meta", "low_value_meta"))):
+            low, high = self._split(layer_id, x)
+            n_low = low.shape[2] if low.dim() == 4 else 0
+            for part, levels, key, dst in ((low, lo_v, lo_k, out[kv, :n_low]),
+                                           (high, hi_v, hi_k, out[kv, n_low:])):
+                if part.numel() == 0:
+                    meta[key] = dict(empty)
+                    continue
+                q, meta[key] = _levels(levels, part, axis)
+                dst.copy_(q.permute(2, 0, 1, 3))
+        return {k: meta[k] for k in ("high_key_meta", "high_value_meta", "low_key_meta",
+                                     "low_value_meta", "original_dtype")}
+
+    def dequantize_into(self, layer_id: int, tensor: torch.Tensor, meta_data: Any,
+                        out: torch.Tensor) -> None:
+        """:meth:`dequantize` of one layer's codes (``[2, blocks, block_size,
+        heads, dim]``, LOW heads first) written into ``out`` (same shape, the
+        original dtype): each part is dequantized with the same arithmetic
+        and placed at its heads with one index copy, without the full-size
+        temporary and the stacking copy."""
+        for kv, (hi, lo) in enumerate((("high_key_meta", "low_key_meta"),
+                                       ("high_value_meta", "low_value_meta"))):
+            part, dst = tensor[kv], out[kv]
+            if self.split_type == "head":
+                m = self._head_mask(layer_id, part.shape[2]).cpu()
+                nlow = int(m.sum())
+                idx = torch.arange(m.numel())
+                for codes, key, heads in ((part[:, :, :nlow], lo, idx[m]),
+                                          (part[:, :, nlow:], hi, idx[~m])):
+                    if codes.numel():
+                        dst.index_copy_(2, heads.to(dst.device),
+                                        dequantize(codes, meta_data[key]).to(dst.dtype))
+            else:
+                key = lo if self._layer_low(layer_id) else hi
+                dst.copy_(dequantize(part, meta_data[key]))
 
     def dequantize(self, layer_id: int, tensor: torch.Tensor, meta_data: Any, **kwargs: Any):
         keys, values = tensor[0], tensor[1]

@@ -364,3 +364,37 @@ def test_codec_ops_are_registered_torch_operators():
         fs = ops.rans_encode(torch.empty(1000, dtype=torch.uint8))
         assert fs.dtype == torch.uint8 and not isinstance(fs.shape[0], int)
         assert ops.lc_decode(fs, 1000).shape == (1000,)
+
+
+@pytest.mark.parametrize("split_type", ["head", "layer"])
+@pytest.mark.parametrize("axes", [("channel", "token"), ("token", "token"), ("tensor", "channel")])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_quantize_into_matches_quantize(split_type, axes, dtype):
+    """The generic pipeline's direct-write quantizer gives the same codes (in
+    the heads-outer layout) and metadata as quantize + permute."""
+    from kvserve_hpdps_b200.compression.quantizer import KVServeQuantizer
+    qz = KVServeQuantizer(model_name="Qwen2.5-7B-Instruct", hybrid_ratio=0.5,
+                          high_key_max_value=16, high_value_max_value=12,
+                          low_key_max_value=8, low_value_max_value=6,
+                          axis_key=axes[0], axis_value=axes[1], split_type=split_type)
+    g = torch.Generator().manual_seed(3)
+    for layer in (0, 3, 27):  # layer split: 27 is LOW, 0 and 3 HIGH
+        x = (torch.randn(2, 5, 16, 4, 128, generator=g) * 3).to(dtype)
+        q, m = qz.quantize(layer, x)
+        out = torch.full((2, 4, 5, 16, 128), 255, dtype=torch.uint8)
+        m2 = qz.quantize_into(layer, x, out)
+        assert torch.equal(out, q.permute(0, 3, 1, 2, 4))
+        assert list(m2) == list(m)
+        for k in m:
+            if isinstance(m[k], dict):
+                for f in m[k]:
+                    a, b = m[k][f], m2[k][f]
+                    assert (a is None and b is None) or (torch.is_tensor(a) and torch.equal(a, b)) \
+                        or a == b, (k, f)
+            else:
+                assert m[k] == m2[k]
+        # and back: the direct-write dequantizer equals dequantize
+        codes = q  # [2, blocks, block_size, heads, dim], LOW heads first
+        back = torch.full((2, 5, 16, 4, 128), float("nan"), dtype=dtype)
+        qz.dequantize_into(layer, codes, m, back)
+        assert torch.equal(back, qz.dequantize(layer, codes, m))
