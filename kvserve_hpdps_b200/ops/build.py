@@ -59,7 +59,7 @@ def _compile(src: str, obj: str, cuda: str, verbose: bool) -> tuple[str, str]:
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
     else:
-        cmd = ["g++", "-O3", "-fPIC", "-std=c++17", "-I", CSRC,
+        cmd = ["g++", "-O3", "-fPIC", "-std=c++17", "-pthread", "-I", CSRC,
                "-I", os.path.join(cuda, "include"), "-c", src, "-o", obj]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
@@ -91,7 +91,7 @@ def build(verbose: bool = False, force: bool = False, jobs: int | None = None) -
             os.path.getmtime(o) > os.path.getmtime(LIB_PATH) for o in objs):
         tmp = LIB_PATH + ".tmp"
         cmd = [os.path.join(cuda, "bin", "nvcc"), *ARCH_FLAGS, "-shared", "-o", tmp, *objs,
-               "-cudart", "static"]
+               "-cudart", "static", "-lpthread"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{res.stdout}\n{res.stderr}")

@@ -5,9 +5,20 @@
 // so for the same input it produces the same bytes as k_rans_encode +
 // k_rans_directory + k_rans_copy.  It is the oracle of the device codec and
 // the codec of CPU-only round trips.
+//
+// Chunks are independent, so both directions run them on a pool of host
+// threads (``KVS_CPU_THREADS`` caps the count; default: the hardware
+// concurrency): the encoder writes each chunk's record, then places the
+// records at their prefix-sum offsets, so the stream is the same bytes for any
+// thread count; the decoder reports the error of the lowest failing chunk,
+// as a chunk-by-chunk loop would.
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
+#include <system_error>
+#include <thread>
 #include <vector>
 
 #include "rans.cuh"
@@ -100,6 +111,96 @@ std::pair<uint32_t, uint32_t> encode_chunk(const uint8_t* src, uint32_t n_sym, u
   return {0u, static_cast<uint32_t>(16 + pad16(n_sym))};
 }
 
+// Runs fn(i) for every i in [0, n) on up to hardware-concurrency threads,
+// the calling thread included; returns when all are done.
+template <class F>
+void parallel_for(uint32_t n, F&& fn) {
+  unsigned t = std::thread::hardware_concurrency();
+  if (t == 0) t = 1;
+  if (const char* e = std::getenv("KVS_CPU_THREADS")) {
+    const int v = std::atoi(e);
+    if (v > 0) t = std::min<unsigned>(t, static_cast<unsigned>(v));
+  }
+  t = std::min<unsigned>(t, n);
+  if (t <= 1) {
+    for (uint32_t i = 0; i < n; ++i) fn(i);
+    return;
+  }
+  std::atomic<uint32_t> next{0};
+  auto work = [&] {
+    for (uint32_t i = next.fetch_add(1); i < n; i = next.fetch_add(1)) fn(i);
+  };
+  std::vector<std::thread> pool;
+  pool.reserve(t - 1);
+  for (unsigned k = 1; k < t; ++k) {
+    try {
+      pool.emplace_back(work);
+    } catch (const std::system_error&) {
+      break;  // fewer threads: the others take the remaining items
+    }
+  }
+  work();
+  for (auto& th : pool) th.join();
+}
+
+// Decode chunk c of a validated stream header; 0 or a negative error code.
+int decode_chunk(const uint8_t* stream, uint64_t stream_bytes, const uint64_t* dir,
+                 const StreamHeader& hd, uint32_t c, uint8_t* out, uint64_t n) {
+  if (dir[c] > stream_bytes || stream_bytes - dir[c] < 16) return -4;
+  const uint8_t* rec = stream + dir[c];
+  const uint64_t room = stream_bytes - dir[c] - 16;  // bytes after the chunk header
+  ChunkHeader ch;
+  std::memcpy(&ch, rec, sizeof(ch));
+  const uint64_t first = static_cast<uint64_t>(c) * hd.chunk_symbols;
+  if (ch.n_sym > hd.chunk_symbols || ch.alphabet > 256 || ch.n_sym > n - first) return -5;
+  uint8_t* dst = out + first;
+  if (ch.alphabet == 0) {
+    if (ch.n_sym > room) return -4;
+    std::memcpy(dst, rec + 16, ch.n_sym);
+    return 0;
+  }
+  const uint32_t A = ch.alphabet;
+  const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
+  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  const uint64_t total_words = static_cast<uint64_t>(ch.n_pad) + ch.n_words;
+  if (fpad + 128ull + 2 * total_words > room) return -4;
+  uint32_t x[kLanes];
+  std::memcpy(x, rec + 16 + fpad, sizeof(x));
+  const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
+  uint32_t fc[256];
+  thread_local std::vector<uint8_t> lut;
+  lut.assign(kProbScale, 0);
+  uint32_t cum = 0;
+  for (uint32_t s = 0; s < A; ++s) {
+    fc[s] = freq[s] | (cum << 16);
+    for (uint32_t k = 0; k < freq[s] && cum + k < kProbScale; ++k)
+      lut[cum + k] = static_cast<uint8_t>(s);
+    cum += freq[s];
+  }
+  if (cum != kProbScale) return -6;
+  uint64_t rptr = ch.n_pad;
+  const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
+  for (uint32_t ss = 0; ss < n_ss; ++ss) {
+    for (int m = 0; m < kSub; ++m) {
+      for (int l = 0; l < kLanes; ++l) {
+        const uint32_t sl = x[l] & (kProbScale - 1);
+        const uint32_t s = lut[sl];
+        x[l] = (fc[s] & 0xFFFFu) * (x[l] >> kProbBits) + sl - (fc[s] >> 16);
+        if (x[l] < kStateLow) {
+          if (rptr >= total_words) return -7;
+          x[l] = (x[l] << 16) | words[rptr++];
+        }
+        const uint32_t idx = ss * kSuper + l * kSub + m;
+        if (idx < ch.n_sym) dst[idx] = static_cast<uint8_t>(s);
+      }
+    }
+  }
+  for (int l = 0; l < kLanes; ++l)
+    if (x[l] != kStateLow) return -8;
+  if (rptr != total_words) return -9;
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -112,25 +213,27 @@ uint64_t kvs_cpu_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t
   if (n == 0 || cs == 0 || cs % kSuper != 0) return 0;
   const uint32_t nc = num_chunks(n, cs);
   const uint64_t sb = slot_bytes(cs);
-  std::vector<uint8_t> slot(sb);
-  std::vector<std::pair<uint32_t, uint32_t>> rec(nc);
-  const uint64_t base = pad16(directory_bytes(nc));
-  uint64_t run = base;
-  std::vector<uint64_t> dir(nc + 1);
-  // Records are emitted into `out` directly; the slot buffer mirrors the
-  // device staging layout so offsets match.
-  for (uint32_t c = 0; c < nc; ++c) {
+  // Each chunk is encoded into a zeroed slot that mirrors the device staging
+  // layout (so record offsets match) and its record is kept for placement.
+  std::vector<std::vector<uint8_t>> recs(nc);
+  parallel_for(nc, [&](uint32_t c) {
+    thread_local std::vector<uint8_t> slot;
+    slot.assign(sb, 0);
     const uint64_t start = static_cast<uint64_t>(c) * cs;
     const uint32_t n_sym = static_cast<uint32_t>(std::min<uint64_t>(cs, n - start));
-    std::fill(slot.begin(), slot.end(), 0);
-    rec[c] = encode_chunk(in + start, n_sym, cs, slot.data());
+    const auto r = encode_chunk(in + start, n_sym, cs, slot.data());
+    recs[c].assign(slot.data() + r.first, slot.data() + r.first + r.second);
+  });
+  const uint64_t base = pad16(directory_bytes(nc));
+  std::vector<uint64_t> dir(nc + 1);
+  uint64_t run = base;
+  for (uint32_t c = 0; c < nc; ++c) {
     dir[c] = run;
-    if (run + rec[c].second > out_cap) return 0;
-    std::memcpy(out + run, slot.data() + rec[c].first, rec[c].second);
-    run += rec[c].second;
+    run += recs[c].size();
   }
   dir[nc] = run;
-  if (base > out_cap) return 0;
+  if (run > out_cap) return 0;
+  parallel_for(nc, [&](uint32_t c) { std::memcpy(out + dir[c], recs[c].data(), recs[c].size()); });
   std::memset(out + sizeof(StreamHeader) + 8ull * (nc + 1), 0,
               base - sizeof(StreamHeader) - 8ull * (nc + 1));
   StreamHeader hd{kMagic, nc, n, cs, static_cast<uint32_t>(kProbBits), run};
@@ -139,62 +242,25 @@ uint64_t kvs_cpu_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t
   return run;
 }
 
-// Decode a stream into n bytes; returns 0 on success, negative on error.
+// Decode a stream into n bytes; returns 0 on success, negative on error.  The
+// header, the directory and every record are checked against the stream
+// length and n before anything is read or written through them.
 int kvs_cpu_rans_decode(const uint8_t* stream, uint64_t stream_bytes, uint8_t* out, uint64_t n) {
   if (stream_bytes < sizeof(StreamHeader)) return -1;
   StreamHeader hd;
   std::memcpy(&hd, stream, sizeof(hd));
   if (hd.magic != kMagic || hd.n_symbols != n || hd.prob_bits != kProbBits) return -2;
   if (hd.total_bytes > stream_bytes) return -3;
-  const uint64_t* dir = reinterpret_cast<const uint64_t*>(stream + sizeof(StreamHeader));
-  for (uint32_t c = 0; c < hd.n_chunks; ++c) {
-    if (dir[c] + 16 > stream_bytes) return -4;
-    const uint8_t* rec = stream + dir[c];
-    ChunkHeader ch;
-    std::memcpy(&ch, rec, sizeof(ch));
-    uint8_t* dst = out + static_cast<uint64_t>(c) * hd.chunk_symbols;
-    if (ch.n_sym > hd.chunk_symbols || ch.alphabet > 256) return -5;
-    if (ch.alphabet == 0) {
-      std::memcpy(dst, rec + 16, ch.n_sym);
-      continue;
-    }
-    const uint32_t A = ch.alphabet;
-    const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
-    const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
-    uint32_t x[kLanes];
-    std::memcpy(x, rec + 16 + fpad, sizeof(x));
-    const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
-    const uint32_t total_words = ch.n_pad + ch.n_words;
-    uint32_t fc[256];
-    std::vector<uint8_t> lut(kProbScale);
-    uint32_t cum = 0;
-    for (uint32_t s = 0; s < A; ++s) {
-      fc[s] = freq[s] | (cum << 16);
-      for (uint32_t k = 0; k < freq[s] && cum + k < kProbScale; ++k) lut[cum + k] = static_cast<uint8_t>(s);
-      cum += freq[s];
-    }
-    if (cum != kProbScale) return -6;
-    uint32_t rptr = ch.n_pad;
-    const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
-    for (uint32_t ss = 0; ss < n_ss; ++ss) {
-      for (int m = 0; m < kSub; ++m) {
-        for (int l = 0; l < kLanes; ++l) {
-          const uint32_t sl = x[l] & (kProbScale - 1);
-          const uint32_t s = lut[sl];
-          x[l] = (fc[s] & 0xFFFFu) * (x[l] >> kProbBits) + sl - (fc[s] >> 16);
-          if (x[l] < kStateLow) {
-            if (rptr >= total_words) return -7;
-            x[l] = (x[l] << 16) | words[rptr++];
-          }
-          const uint32_t idx = ss * kSuper + l * kSub + m;
-          if (idx < ch.n_sym) dst[idx] = static_cast<uint8_t>(s);
-        }
-      }
-    }
-    for (int l = 0; l < kLanes; ++l)
-      if (x[l] != kStateLow) return -8;
-    if (rptr != total_words) return -9;
-  }
+  if (hd.chunk_symbols == 0 || hd.n_chunks != num_chunks(n, hd.chunk_symbols)) return -2;
+  if (directory_bytes(hd.n_chunks) > stream_bytes) return -4;
+  std::vector<uint64_t> dir(hd.n_chunks + 1);
+  std::memcpy(dir.data(), stream + sizeof(StreamHeader), 8ull * (hd.n_chunks + 1));
+  std::vector<int> rc(hd.n_chunks, 0);
+  parallel_for(hd.n_chunks, [&](uint32_t c) {
+    rc[c] = decode_chunk(stream, stream_bytes, dir.data(), hd, c, out, n);
+  });
+  for (uint32_t c = 0; c < hd.n_chunks; ++c)
+    if (rc[c] != 0) return rc[c];
   return 0;
 }
 

@@ -398,3 +398,32 @@ def test_quantize_into_matches_quantize(split_type, axes, dtype):
         back = torch.full((2, 5, 16, 4, 128), float("nan"), dtype=dtype)
         qz.dequantize_into(layer, codes, m, back)
         assert torch.equal(back, qz.dequantize(layer, codes, m))
+
+
+def test_cpu_rans_threads_and_corrupt_streams(monkeypatch):
+    """The CPU coder runs chunks on host threads: the stream is the same
+    bytes for one thread and for many, and corrupt or truncated streams are
+    rejected with an error (every read and write is bounds-checked)."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randint(0, 6, (300000,), dtype=torch.uint8, generator=g)
+    x[40000:72768] = torch.randint(0, 256, (32768,), dtype=torch.uint8, generator=g)  # raw chunk
+    many = K.rans_encode(x)
+    monkeypatch.setenv("KVS_CPU_THREADS", "1")
+    one = K.rans_encode(x)
+    assert torch.equal(one, many)
+    assert torch.equal(K.rans_decode(one, x.numel()), x)
+    monkeypatch.delenv("KVS_CPU_THREADS")
+    rejected = 0
+    for i in range(300):
+        bad = many.clone()
+        if i % 3 == 0:
+            bad = bad[:int(torch.randint(0, bad.numel(), (1,), generator=g))].clone()
+        else:
+            pos = torch.randint(0, 96 if i % 3 == 1 else bad.numel(), (4,), generator=g)
+            bad[pos] ^= torch.randint(1, 256, (4,), dtype=torch.uint8, generator=g)
+        try:
+            out = K.rans_decode(bad, x.numel())
+            assert out.numel() == x.numel()
+        except RuntimeError:
+            rejected += 1
+    assert rejected > 100
