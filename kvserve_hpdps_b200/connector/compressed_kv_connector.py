@@ -94,6 +94,7 @@ from kvserve_hpdps_b200.utils.tracing import nvtx  # noqa: E402
 logger = get_logger(__name__)
 
 LOAD_TIMEOUT_S = float(os.environ.get("KVSERVE_LOAD_TIMEOUT_S", "60"))
+CONTROLLER_FEEDBACK_TTL_S = 300.0  # as the adapter's controller contexts
 DEFAULT_MAX_CHUNK_BYTES = 512 * 1024 * 1024
 _LAYER_RE = re.compile(r"layers?\.(\d+)")
 
@@ -178,6 +179,11 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._rid2tid: dict[str, str] = {}
         self._pending_send_rids: set[str] = set()
         self._err_monitor = None
+        # controller feedback: transfer id -> (request id, compress ms, time) until the
+        # transport reports the message sent; completions queued by its thread
+        self._ctl_wait: dict[str, tuple[str, float, float]] = {}
+        self._ctl_done: deque = deque()
+        self._listening = False
         if role == KVConnectorRole.WORKER:
             self._init_worker(cfg)
 
@@ -194,6 +200,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             local_rank = torch.cuda.current_device() if torch.cuda.is_available() else 0
         self._local_rank = local_rank
         self._transport = self._build_transport(cfg, local_rank, self._tp_rank)
+        self._watch_transport()
         if self._compression_cfg is not None:
             comp = self._get_compressor()
             if comp is not None:
@@ -221,6 +228,36 @@ class CompressedKVConnector(KVConnectorBase_V1):
 
     def attach_transport(self, transport) -> None:
         self._transport = transport
+        self._listening = False
+        self._watch_transport()
+
+    # ----------------------------------------------- controller feedback
+    def _watch_transport(self) -> None:
+        """Producer: hear from the transport when a message has left, so the
+        controller learns from compress + transfer time (the reference feeds
+        it the host time of compress + enqueue, taken before the transfer)."""
+        tr = self._transport
+        if self.is_producer and not self._listening and hasattr(tr, "add_sent_listener"):
+            tr.add_sent_listener(self._on_sent)
+            self._listening = True
+
+    def _on_sent(self, request_id: str, transfer_ids: list[str], latency_ms: float) -> None:
+        # transport thread: only queue; the engine thread applies the updates
+        for t in transfer_ids:
+            if t in self._ctl_wait:
+                self._ctl_done.append((t, latency_ms))
+
+    def _apply_controller_feedback(self) -> None:
+        comp = self._compressor
+        while self._ctl_done:
+            tid, latency_ms = self._ctl_done.popleft()
+            entry = self._ctl_wait.pop(tid, None)
+            if entry is not None and comp is not None:
+                comp.update_controller(entry[0], entry[1] + latency_ms)
+        if self._ctl_wait:  # messages that never left (refused, dropped)
+            cutoff = time.monotonic() - CONTROLLER_FEEDBACK_TTL_S
+            for tid in [t for t, e in self._ctl_wait.items() if e[2] < cutoff]:
+                self._ctl_wait.pop(tid, None)
 
     def _get_compressor(self):
         if self._compression_cfg is None:
@@ -292,6 +329,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         if not isinstance(meta, CompressedKVConnectorMetadata):
             return
         timeline("P save_enter")
+        self._apply_controller_feedback()
         if self._side_stream is not None:
             torch.cuda.current_stream().wait_stream(self._side_stream)
             self._finish_step(meta)
@@ -334,8 +372,12 @@ class CompressedKVConnector(KVConnectorBase_V1):
                                    for l in layers], 0)
             cd = comp.compress(stacked, rid) if comp is not None else None
             if cd is not None:
+                compress_ms = (time.monotonic() - t0) * 1e3
+                if self._listening:  # completed by _apply_controller_feedback
+                    self._ctl_wait[tid] = (rid, compress_ms, time.monotonic())
                 nbytes = self._send_compressed(tid, names, cd)
-                comp.update_controller(rid, (time.monotonic() - t0) * 1e3)
+                if not self._listening:
+                    comp.update_controller(rid, (time.monotonic() - t0) * 1e3)
                 write_compression_stats(rid, tid, stacked.numel() * stacked.element_size(), nbytes,
                                         compress_ms=(time.monotonic() - t0) * 1e3,
                                         prefill_span_ms=span)
@@ -358,6 +400,8 @@ class CompressedKVConnector(KVConnectorBase_V1):
             self._transport.wait_for_sent()
 
     def get_finished(self, finished_req_ids: set[str]):
+        if self.is_producer:
+            self._apply_controller_feedback()
         if not self._async_send:
             return None, None
         self._pending_send_rids |= set(finished_req_ids or ())

@@ -26,6 +26,7 @@ class FakeTransportPair:
         self.inbox: dict[str, deque] = defaultdict(deque)
         self.sent: dict[str, int] = defaultdict(int)
         self.failed: dict[str, int] = defaultdict(int)
+        self.listeners: list = []
         self.drop_next = 0
         self.refuse_next = 0
         self.delay_s = 0.0
@@ -79,6 +80,9 @@ class _FakeEnd:
         with self.pair.lock:
             for t in (member_tids or [request_id]):
                 table[t] += 1
+        if ok:
+            for fn in list(self.pair.listeners):
+                fn(request_id, list(member_tids or [request_id]), self.pair.delay_s * 1e3)
 
     def send_bundle(self, request_id, layer_names, meta, body_chunks, aux_tensors,
                     member_tids: Optional[list[str]] = None) -> None:
@@ -91,6 +95,11 @@ class _FakeEnd:
     def sent_layers(self, tid: str) -> int:
         with self.pair.lock:
             return self.pair.sent.get(tid, 0)
+
+    def add_sent_listener(self, fn) -> None:
+        """``fn(request_id, transfer_ids, latency_ms)`` for every message the
+        consumer accepted (latency: the injected delay)."""
+        self.pair.listeners.append(fn)
 
     def failed_layers(self, tid: str) -> int:
         with self.pair.lock:

@@ -8,6 +8,9 @@ Public API of the reference transport (kvserve_v1/transport/nccl_transport.py:54
   ``wait_for_sent()``; ``failed_layers(tid)`` (new) counts the messages the
   consumer refused or that could not be sent, so that a caller that frees a
   request's blocks once its messages are out does not wait for them forever;
+  ``add_sent_listener(fn)`` (new) calls ``fn(request_id, transfer_ids,
+  latency_ms)`` on the send thread when a message has left, with the time
+  from its ``send``/``send_bundle`` call;
 * consumer: ``drain_received() -> {transfer_id: [(layer_names, payload)]}``
   where payload is a tensor (raw), a bundle dict (``{"__bundle__": True,
   "meta", "body_chunks", "aux_tensors"}``) or ``FAILED_PAYLOAD`` (None) when
@@ -97,6 +100,7 @@ class NcclTransport:
             self._sent_lock = threading.Lock()
             self._sent: dict[str, int] = defaultdict(int)
             self._failed: dict[str, int] = defaultdict(int)
+            self._listeners: list = []
             self.ctl_failed = False
             self._thread = threading.Thread(target=self._send_loop, daemon=True,
                                             name="kvs-send")
@@ -121,7 +125,8 @@ class NcclTransport:
         assert self.is_sender
         t = stacked_kv.to(self.device).contiguous()
         with self._cv:
-            self._queue.append(("tensor", request_id, list(layer_names), t, self._ready_event(), None))
+            self._queue.append(("tensor", request_id, list(layer_names), t, self._ready_event(), None,
+                                time.monotonic()))
             self._cv.notify()
 
     def send_bundle(self, request_id: str, layer_names: list[str], meta: dict,
@@ -132,12 +137,16 @@ class NcclTransport:
         aux = [t.to(self.device).contiguous() for t in aux_tensors]
         with self._cv:
             self._queue.append(("bundle", request_id, list(layer_names), (meta, body, aux),
-                                self._ready_event(), member_tids))
+                                self._ready_event(), member_tids, time.monotonic()))
             self._cv.notify()
 
     def sent_layers(self, transfer_id: str) -> int:
         with self._sent_lock:
             return self._sent.get(transfer_id, 0)
+
+    def add_sent_listener(self, fn) -> None:
+        """``fn(request_id, transfer_ids, latency_ms)`` after each message left."""
+        self._listeners.append(fn)
 
     def failed_layers(self, transfer_id: str) -> int:
         with self._sent_lock:
@@ -190,7 +199,8 @@ class NcclTransport:
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
 
-    def _send_item(self, kind, request_id, layer_names, payload, event, member_tids) -> bool:
+    def _send_item(self, kind, request_id, layer_names, payload, event, member_tids,
+                   t_enqueued: float) -> bool:
         """One message; False when it was refused or not sent."""
         if kind == "tensor":
             t = payload
@@ -224,8 +234,14 @@ class NcclTransport:
         self._p2p_send(tensors)
         nbytes = sum(t.numel() * t.element_size() for t in tensors)
         self._count(self._sent, request_id, member_tids)
-        write_transfer_stats(request_id, (time.monotonic() - t0) * 1e3, nbytes,
+        now = time.monotonic()
+        write_transfer_stats(request_id, (now - t0) * 1e3, nbytes,
                              transport="nccl" if self.backend == "nccl" else self.backend)
+        for fn in list(self._listeners):
+            try:
+                fn(request_id, list(member_tids or [request_id]), (now - t_enqueued) * 1e3)
+            except Exception as e:  # noqa: BLE001
+                logger.error("sent listener failed: %s", e)
         return True
 
     # ------------------------------------------------------------ consumer

@@ -157,6 +157,7 @@ class P2PTransport:
             self._slot_of: dict[int, int] = {}  # ring offset of a message -> its flag slot
             self._sent: dict[str, int] = defaultdict(int)
             self._failed: dict[str, int] = defaultdict(int)
+            self._listeners: list = []
             self._pending: deque = deque()  # (event, request_id, member_tids, nbytes, t0)
             self._pending_cv = threading.Condition()
             self._io = threading.Thread(target=self._producer_io, daemon=True, name="kvs-p2p-io")
@@ -228,7 +229,13 @@ class P2PTransport:
             with self._lock:  # a message without member ids counts for its request id
                 for t in (tids or [rid]):
                     self._sent[t] += 1
-            write_transfer_stats(rid, (time.monotonic() - t0) * 1e3, nbytes, transport="nvlink-p2p")
+            ms = (time.monotonic() - t0) * 1e3
+            write_transfer_stats(rid, ms, nbytes, transport="nvlink-p2p")
+            for fn in list(self._listeners):
+                try:
+                    fn(rid, list(tids or [rid]), ms)
+                except Exception as e:  # noqa: BLE001
+                    logger.error("sent listener failed: %s", e)
 
     def _put(self, request_id: str, layer_names: list[str], tensors: list[torch.Tensor],
              n_body: int, meta: Optional[dict], kind: str,
@@ -403,6 +410,11 @@ class P2PTransport:
     def sent_layers(self, transfer_id: str) -> int:
         with self._lock:
             return self._sent.get(transfer_id, 0)
+
+    def add_sent_listener(self, fn) -> None:
+        """``fn(request_id, transfer_ids, latency_ms)`` on the completion thread
+        once a message's stores have finished (time from its send call)."""
+        self._listeners.append(fn)
 
     def failed_layers(self, transfer_id: str) -> int:
         with self._lock:

@@ -238,3 +238,40 @@ def test_stream_mode_consumer_takes_raw_per_layer_messages():
     for name in pc:
         assert torch.equal(cc[name][:, [2, 6, 0]], pc[name][:, [5, 1, 7]])
     assert pair.messages == L
+
+
+def test_controller_learns_from_compress_plus_transfer_time(tmp_path):
+    """Controller mode: the latency fed to the bandit is the compression time
+    plus the transfer time the transport reports once the message has left
+    (here a 50 ms delivery delay), applied on the engine thread at the next
+    step rather than right after the asynchronous send call."""
+    import time
+
+    from kvserve_hpdps_b200.offline.library_export import build_library, write_library
+    from kvserve_hpdps_b200.offline.search_space import Candidate
+
+    def spec(cfg):
+        return {"enabled": True, "pipeline": ["quantizer", "codec"], "quantizer_config": dict(cfg),
+                "codec_config": {"codec_type": "rans"}, "backend": "generic",
+                "min_compress_size": 0}
+    evals = [{"candidate": c.key(), "config": c.quantizer_config(), "accuracy": acc,
+              "compression_ratio": cr, "harmonic_speed_mbps": 30000.0}
+             for c, acc, cr in [(Candidate(0.0, 16, 16, 8, 6), 0.995, 3.5),
+                                (Candidate(0.8, 12, 8, 6, 4), 0.97, 6.0)]]
+    path = tmp_path / "lib.json"
+    write_library(str(path), build_library(evals, "Qwen2.5-7B-Instruct", spec_builder=spec))
+    ctl = {"mode": "controller", "library_path": str(path), "epsilon": 0.0,
+           "service_config": {"bandwidth_mbps": 150.0, "slo_ms": 1e9,
+                              "accuracy_requirement": 0.96, "t_model_ms": 0.0}}
+    p, c, pair = make_pair(ctl)
+    pair.delay_s = 0.05
+    comp = p._get_compressor()
+    seen = []
+    orig = comp.update_controller
+    comp.update_controller = lambda rid, ms: (seen.append((rid, ms)), orig(rid, ms))
+    handoff(p, c)
+    assert seen == []  # nothing applied from the transport thread
+    time.sleep(0.1)
+    p.get_finished(set())
+    assert [r for r, _ in seen] == ["r1"] and seen[0][1] >= 50.0
+    assert comp.get_controller_stats()["bandit_states"] == 1 and not p._ctl_wait

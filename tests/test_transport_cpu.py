@@ -52,6 +52,8 @@ def _consumer(port, q, fail_rid):
 def _producer(port, q):
     from kvserve_hpdps_b200.parallel.nccl_transport import NcclTransport
     tr = NcclTransport(True, "127.0.0.1", port, backend="gloo", timeout_s=20)
+    heard = []
+    tr.add_sent_listener(lambda rid, tids, ms: heard.append((rid, tids, ms >= 0)))
     tr.send("t_raw", ["l0", "l1"], torch.arange(12, dtype=torch.float32).view(2, 6))
     tr.send_bundle("t_bundle", ["__compressed__", "l0"], {"k": 1},
                    [torch.arange(5, dtype=torch.uint8)], [torch.ones(2, 3)],
@@ -60,7 +62,7 @@ def _producer(port, q):
     ok = tr.wait_for_sent(60)
     q.put({"ok": ok, "sent_a": tr.sent_layers("a"), "sent_b": tr.sent_layers("b"),
            "sent_x": tr.sent_layers("x"), "failed": tr.failed_layers("t_fail"),
-           "sent_fail": tr.sent_layers("t_fail")})
+           "sent_fail": tr.sent_layers("t_fail"), "heard": heard})
     time.sleep(0.5)
     tr.close()
 
@@ -80,6 +82,7 @@ def test_nccl_transport_protocol_over_gloo():
     c.join(30)
     assert prod["ok"] and prod["sent_a"] == 1 and prod["sent_b"] == 1 and prod["sent_x"] == 0
     assert prod["failed"] == 1 and prod["sent_fail"] == 0  # the refusal is counted
+    assert prod["heard"] == [("t_raw", ["t_raw"], True), ("t_bundle", ["a", "b"], True)]
     assert got["t_raw"][0][0] == ["l0", "l1"]
     assert got["t_raw"][0][1] == torch.arange(12, dtype=torch.float32).view(2, 6).tolist()
     names, b = got["t_bundle"][0]
