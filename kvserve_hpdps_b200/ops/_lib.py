@@ -96,6 +96,9 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_cpu_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
         "kvs_cpu_rans_encode": ([P, c_uint64, c_uint32, P, c_uint64], c_uint64),
         "kvs_cpu_rans_decode": ([P, c_uint64, P, c_uint64], c_int),
+        "kvs_cpu_lc_max_bytes": ([c_uint64], c_uint64),
+        "kvs_cpu_lc_encode": ([P, c_uint64, P, c_uint64], c_uint64),
+        "kvs_cpu_lc_decode": ([P, c_uint64, P, c_uint64], c_int),
         "kvs_cpu_bitpack": ([P, c_uint64, c_int, P], None),
         "kvs_cpu_bitunpack": ([P, c_uint64, c_int, P], None),
         "kvs_checksum": ([P, c_int, P, c_int, P], c_int),

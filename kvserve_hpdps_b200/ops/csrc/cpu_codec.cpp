@@ -201,6 +201,108 @@ int decode_chunk(const uint8_t* stream, uint64_t stream_bytes, const uint64_t* d
   return 0;
 }
 
+// ---- LC (BIT_2 + RZE_1), the format of lc_codec.cu and compression/lc.py:
+// header {magic "LCB2", chunk 16384, n (u64), n_chunks, 0, u32 offsets[n_chunks + 1]
+// relative to the 16-byte aligned end of the header}; per chunk either a raw record
+// {0, cb, 0, 0, bytes} or {1, nz, 0, 0, bitmap of the shuffled chunk's nonzero bytes,
+// those bytes}, each padded to 16 bytes.  The shuffle views the chunk (zero padded to
+// groups * 64 bytes) as groups of 32 little-endian 16-bit words and stores, plane-major,
+// the 32-bit word whose bit l is bit b of word l, for b = 0..15.
+constexpr uint32_t kLcMagic = 0x3242434Cu;
+constexpr uint32_t kLcChunk = 16384;
+
+inline uint32_t lc_groups(uint32_t cb) { return ((cb + 1) / 2 + 31) / 32; }
+inline uint64_t lc_head(uint32_t nc) { return pad16(24 + 4ull * (nc + 1)); }
+
+void lc_shuffle(const uint8_t* chunk, uint32_t cb, uint8_t* sb) {
+  const uint32_t G = lc_groups(cb);
+  for (uint32_t g = 0; g < G; ++g) {
+    uint32_t w[32];
+    for (uint32_t l = 0; l < 32; ++l) {
+      const uint64_t i = 2ull * (g * 32 + l);
+      w[l] = (i < cb ? chunk[i] : 0u) | ((i + 1 < cb ? chunk[i + 1] : 0u) << 8);
+    }
+    for (uint32_t bit = 0; bit < 16; ++bit) {
+      uint32_t plane = 0;
+      for (uint32_t l = 0; l < 32; ++l) plane |= ((w[l] >> bit) & 1u) << l;
+      std::memcpy(sb + 4ull * (bit * G + g), &plane, 4);
+    }
+  }
+}
+
+void lc_unshuffle(const uint8_t* sb, uint32_t cb, uint8_t* chunk) {
+  const uint32_t G = lc_groups(cb);
+  for (uint32_t g = 0; g < G; ++g) {
+    uint32_t plane[16];
+    for (uint32_t bit = 0; bit < 16; ++bit) std::memcpy(&plane[bit], sb + 4ull * (bit * G + g), 4);
+    for (uint32_t l = 0; l < 32; ++l) {
+      uint32_t w = 0;
+      for (uint32_t bit = 0; bit < 16; ++bit) w |= ((plane[bit] >> l) & 1u) << bit;
+      const uint64_t i = 2ull * (g * 32 + l);
+      if (i < cb) chunk[i] = static_cast<uint8_t>(w);
+      if (i + 1 < cb) chunk[i + 1] = static_cast<uint8_t>(w >> 8);
+    }
+  }
+}
+
+// One record (padded to 16 bytes) for a chunk of cb bytes.
+std::vector<uint8_t> lc_record(const uint8_t* chunk, uint32_t cb) {
+  const uint32_t S = lc_groups(cb) * 64;
+  std::vector<uint8_t> sb(S);
+  lc_shuffle(chunk, cb, sb.data());
+  uint32_t nz = 0;
+  for (uint32_t i = 0; i < S; ++i) nz += sb[i] != 0;
+  const uint64_t coded = 16ull + S / 8 + nz;
+  if (coded >= 16 + pad16(cb)) {
+    std::vector<uint8_t> rec(16 + pad16(cb), 0);
+    const uint32_t hd[4] = {0u, cb, 0u, 0u};
+    std::memcpy(rec.data(), hd, 16);
+    std::memcpy(rec.data() + 16, chunk, cb);
+    return rec;
+  }
+  std::vector<uint8_t> rec(pad16(coded), 0);
+  const uint32_t hd[4] = {1u, nz, 0u, 0u};
+  std::memcpy(rec.data(), hd, 16);
+  uint8_t* bitmap = rec.data() + 16;
+  uint8_t* vals = bitmap + S / 8;
+  for (uint32_t i = 0; i < S; ++i) {
+    if (sb[i]) {
+      bitmap[i >> 3] |= static_cast<uint8_t>(1u << (i & 7));
+      *vals++ = sb[i];
+    }
+  }
+  return rec;
+}
+
+// Decode record c into out; 0 or a negative error code.
+int lc_decode_chunk(const uint8_t* rec, uint64_t rec_len, uint32_t cb, uint8_t* out) {
+  if (rec_len < 16) return -4;
+  uint32_t hd[4];
+  std::memcpy(hd, rec, 16);
+  if (hd[0] == 0) {
+    if (hd[1] != cb || 16ull + cb > rec_len) return -5;
+    std::memcpy(out, rec + 16, cb);
+    return 0;
+  }
+  if (hd[0] != 1) return -5;
+  const uint32_t S = lc_groups(cb) * 64;
+  const uint32_t nz = hd[1];
+  if (nz > S || 16ull + S / 8 + nz > rec_len) return -5;
+  const uint8_t* bitmap = rec + 16;
+  const uint8_t* vals = bitmap + S / 8;
+  std::vector<uint8_t> sb(S, 0);
+  uint32_t k = 0;
+  for (uint32_t i = 0; i < S; ++i) {
+    if (bitmap[i >> 3] >> (i & 7) & 1u) {
+      if (k >= nz) return -6;
+      sb[i] = vals[k++];
+    }
+  }
+  if (k != nz) return -6;
+  lc_unshuffle(sb.data(), cb, out);
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -260,6 +362,71 @@ int kvs_cpu_rans_decode(const uint8_t* stream, uint64_t stream_bytes, uint8_t* o
     rc[c] = decode_chunk(stream, stream_bytes, dir.data(), hd, c, out, n);
   });
   for (uint32_t c = 0; c < hd.n_chunks; ++c)
+    if (rc[c] != 0) return rc[c];
+  return 0;
+}
+
+uint64_t kvs_cpu_lc_max_bytes(uint64_t n) {
+  const uint32_t nc = static_cast<uint32_t>((n + kLcChunk - 1) / kLcChunk);
+  return lc_head(nc) + nc * (16 + pad16(kLcChunk));
+}
+
+// LC stream of n bytes (chunks on host threads); returns its size or 0.
+uint64_t kvs_cpu_lc_encode(const uint8_t* in, uint64_t n, uint8_t* out, uint64_t out_cap) {
+  if (n == 0) return 0;
+  const uint32_t nc = static_cast<uint32_t>((n + kLcChunk - 1) / kLcChunk);
+  std::vector<std::vector<uint8_t>> recs(nc);
+  parallel_for(nc, [&](uint32_t c) {
+    const uint64_t first = static_cast<uint64_t>(c) * kLcChunk;
+    recs[c] = lc_record(in + first, static_cast<uint32_t>(std::min<uint64_t>(kLcChunk, n - first)));
+  });
+  const uint64_t head = lc_head(nc);
+  std::vector<uint32_t> offs(nc + 1);
+  uint64_t run = 0;
+  for (uint32_t c = 0; c < nc; ++c) {
+    offs[c] = static_cast<uint32_t>(run);
+    run += recs[c].size();
+  }
+  offs[nc] = static_cast<uint32_t>(run);
+  if (head + run > out_cap || run > 0xFFFFFFFFull) return 0;
+  std::memset(out, 0, head);
+  const uint32_t h0[2] = {kLcMagic, kLcChunk};
+  std::memcpy(out, h0, 8);
+  std::memcpy(out + 8, &n, 8);
+  const uint32_t h2[2] = {nc, 0u};
+  std::memcpy(out + 16, h2, 8);
+  std::memcpy(out + 24, offs.data(), 4ull * (nc + 1));
+  parallel_for(nc, [&](uint32_t c) {
+    std::memcpy(out + head + offs[c], recs[c].data(), recs[c].size());
+  });
+  return head + run;
+}
+
+// Decode an LC stream into n bytes; 0 or a negative error code (the lowest
+// failing chunk's).  Offsets and records are checked against the stream.
+int kvs_cpu_lc_decode(const uint8_t* stream, uint64_t len, uint8_t* out, uint64_t n) {
+  const uint32_t nc = static_cast<uint32_t>((n + kLcChunk - 1) / kLcChunk);
+  const uint64_t head = lc_head(nc);
+  if (n == 0 || len < head) return -1;
+  uint32_t h0[2], h2[2];
+  uint64_t hn;
+  std::memcpy(h0, stream, 8);
+  std::memcpy(&hn, stream + 8, 8);
+  std::memcpy(h2, stream + 16, 8);
+  if (h0[0] != kLcMagic || h0[1] != kLcChunk || hn != n || h2[0] != nc) return -2;
+  std::vector<uint32_t> offs(nc + 1);
+  std::memcpy(offs.data(), stream + 24, 4ull * (nc + 1));
+  for (uint32_t c = 0; c < nc; ++c)
+    if (offs[c] > offs[c + 1]) return -3;
+  if (head + offs[nc] > len) return -3;
+  std::vector<int> rc(nc, 0);
+  parallel_for(nc, [&](uint32_t c) {
+    const uint64_t first = static_cast<uint64_t>(c) * kLcChunk;
+    rc[c] = lc_decode_chunk(stream + head + offs[c], offs[c + 1] - offs[c],
+                            static_cast<uint32_t>(std::min<uint64_t>(kLcChunk, n - first)),
+                            out + first);
+  });
+  for (uint32_t c = 0; c < nc; ++c)
     if (rc[c] != 0) return rc[c];
   return 0;
 }

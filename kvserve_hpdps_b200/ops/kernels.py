@@ -867,15 +867,22 @@ def rans_max_bytes(n: int, chunk: int = RANS_CHUNK) -> int:
 def lc_encode(data: torch.Tensor, trim: bool = True) -> torch.Tensor:
     """LC-style (BIT_2 + RZE_1) stream of the bytes of ``data`` (format in
     ``csrc/lc_codec.cu``).  CUDA: three launches; with ``trim`` the host
-    reads the stream size (one synchronisation).  CPU: the numpy reference,
-    which writes the identical stream."""
+    reads the stream size (one synchronisation).  CPU: the native coder
+    (chunks on host threads), which writes the identical stream; the numpy
+    module ``compression.lc`` is the reference of both."""
     from kvserve_hpdps_b200.compression import lc as lc_ref
     src = data.contiguous().view(torch.uint8).reshape(-1)
     n = src.numel()
     if n == 0:
         raise ValueError("empty input")
     if src.device.type == "cpu":
-        return torch.from_numpy(lc_ref.encode(src.numpy()))
+        lb = lib()
+        cap = int(lb.kvs_cpu_lc_max_bytes(n))
+        buf = torch.empty(cap, dtype=torch.uint8)
+        size = int(lb.kvs_cpu_lc_encode(src.data_ptr(), n, buf.data_ptr(), cap))
+        if size == 0:
+            raise RuntimeError("CPU LC encode failed")
+        return buf[:size].clone()
     dev = src.device
     lb = lib()
     ws = workspace(dev)
@@ -895,9 +902,13 @@ def lc_encode(data: torch.Tensor, trim: bool = True) -> torch.Tensor:
 def lc_decode(stream: torch.Tensor, n: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Bytes of an LC stream; a corrupt stream records ERR_CORRUPT in the
     device error word (CUDA) or raises ValueError (CPU)."""
-    from kvserve_hpdps_b200.compression import lc as lc_ref
     if stream.device.type == "cpu":
-        return torch.from_numpy(lc_ref.decode(stream.contiguous().numpy(), int(n)))
+        s = stream.contiguous()
+        res = torch.empty(int(n), dtype=torch.uint8) if out is None else out
+        rc = lib().kvs_cpu_lc_decode(s.data_ptr(), s.numel(), res.data_ptr(), int(n))
+        if rc != 0:
+            raise ValueError(f"corrupt LC stream ({rc})")
+        return res
     dev = stream.device
     if out is None:
         out = torch.empty(int(n), dtype=torch.uint8, device=dev)

@@ -427,3 +427,27 @@ def test_cpu_rans_threads_and_corrupt_streams(monkeypatch):
         except RuntimeError:
             rejected += 1
     assert rejected > 100
+
+
+def test_native_cpu_lc_matches_reference_and_rejects_corruption():
+    """The native CPU LC coder writes the numpy reference's stream byte for
+    byte (codes, raw chunks, tails) and rejects corrupt streams."""
+    from kvserve_hpdps_b200.compression import lc
+    g = torch.Generator().manual_seed(9)
+    x = torch.randint(0, 6, (90001,), dtype=torch.uint8, generator=g)
+    x[20000:40000] = torch.randint(0, 256, (20000,), dtype=torch.uint8, generator=g)
+    s = K.lc_encode(x)
+    assert torch.equal(s, torch.from_numpy(lc.encode(x.numpy())))
+    assert torch.equal(K.lc_decode(s, x.numel()), x)
+    assert torch.equal(torch.from_numpy(lc.decode(s.numpy(), x.numel())), x)
+    rejected = 0
+    for i in range(200):
+        bad = s[:int(torch.randint(0, s.numel(), (1,), generator=g))].clone() if i % 2 else s.clone()
+        if i % 2 == 0:
+            pos = torch.randint(0, bad.numel(), (3,), generator=g)
+            bad[pos] ^= torch.randint(1, 256, (3,), dtype=torch.uint8, generator=g)
+        try:
+            assert K.lc_decode(bad, x.numel()).numel() == x.numel()
+        except ValueError:
+            rejected += 1
+    assert rejected >= 100
