@@ -11,8 +11,9 @@ framework's own:
   stream (lossless for any input);
 * ``"lc"``: LC-style BIT_2 (16-bit bit-plane shuffle) + RZE_1 (zero-byte
   elimination) after the published LC stages, this framework's own device
-  kernels and numpy reference (the reference calls a closed external
-  library for ``codec_type: "lc"``);
+  kernels and threaded CPU coder (same byte stream as the numpy reference
+  in ``compression/lc.py``; the reference calls a closed external library
+  for ``codec_type: "lc"``);
 * ``"none"``: raw bytes.
 
 The reference's closed nvCOMP algorithms are not used.  Their names map to
