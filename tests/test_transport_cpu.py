@@ -272,3 +272,73 @@ def test_p2p_flag_slots_are_reused_only_after_their_message_is_returned():
     timer.join()
     assert e[2] == c[2] and 0.1 < time.time() - t0 < 3
     assert t._alloc.free_bytes() == 256 and t._inflight_msgs == 3  # [768, 1024) never used
+
+
+def _stress_producer(port, q, threads, per_thread):
+    import threading
+
+    from kvserve_hpdps_b200.parallel.nccl_transport import NcclTransport
+    tr = NcclTransport(True, "127.0.0.1", port, backend="gloo", timeout_s=20)
+
+    def worker(k):
+        for i in range(per_thread):
+            rid = f"t{k}-{i}"
+            if i % 2:
+                tr.send(rid, ["l0"], torch.full((k + 1, i + 1), float(i), dtype=torch.float32))
+            else:
+                tr.send_bundle(rid, ["__compressed__", "l0"], {"k": k, "i": i},
+                               [torch.full((i + 3,), k, dtype=torch.uint8)], [],
+                               member_tids=[rid, f"m{k}-{i}"])
+    ts = [threading.Thread(target=worker, args=(k,)) for k in range(threads)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    ok = tr.wait_for_sent(120)
+    counts = {f"t{k}-{i}": tr.sent_layers(f"t{k}-{i}") for k in range(threads)
+              for i in range(per_thread)}
+    q.put({"ok": ok, "counts": counts, "failed": sum(tr.failed_layers(r) for r in counts)})
+    time.sleep(0.5)
+    tr.close()
+
+
+def _stress_consumer(port, q, want):
+    from kvserve_hpdps_b200.parallel.nccl_transport import NcclTransport
+    tr = NcclTransport(False, "127.0.0.1", port, backend="gloo", timeout_s=20)
+    got = _collect(tr, want, seconds=120)
+    out = {}
+    for rid, msgs in got.items():
+        out[rid] = [(n, p["meta"], [t.tolist() for t in p["body_chunks"]]) if isinstance(p, dict)
+                    else (n, None, p.tolist()) for n, p in msgs]
+    q.put(out)
+    time.sleep(0.5)
+    tr.close()
+
+
+def test_transport_under_concurrent_senders():
+    """Host-thread stress: four threads send 25 messages each (raw and
+    bundles) through one producer; every message arrives once and intact,
+    and the send counters match."""
+    threads, per = 4, 25
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    qc, qp = ctx.Queue(), ctx.Queue()
+    c = ctx.Process(target=_stress_consumer, args=(port, qc, threads * per))
+    c.start()
+    time.sleep(1.0)
+    p = ctx.Process(target=_stress_producer, args=(port, qp, threads, per))
+    p.start()
+    prod = qp.get(timeout=240)
+    got = qc.get(timeout=240)
+    p.join(30)
+    c.join(30)
+    assert prod["ok"] and prod["failed"] == 0
+    assert all(v == 1 for v in prod["counts"].values())
+    assert len(got) == threads * per
+    for k in range(threads):
+        for i in range(per):
+            (names, meta, body), = got[f"t{k}-{i}"]
+            if i % 2:
+                assert names == ["l0"] and body == [[float(i)] * (i + 1)] * (k + 1)
+            else:
+                assert meta == {"k": k, "i": i} and body == [[k] * (i + 3)]
