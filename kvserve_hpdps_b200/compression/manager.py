@@ -84,6 +84,7 @@ class KVCompressionAdapter:
         self._last_contexts: dict[str, tuple[float, dict]] = {}
         self._manager_cache: dict[str, tuple[Any, Optional[CompressionConfig]]] = {}
         self._last_decompress_timing: Optional[dict] = None
+        self._cpu_fallback_mgr = None
         self.spec = compression_spec
         if compression_spec == "default":
             cfg = get_default_compression_config()
@@ -172,6 +173,31 @@ class KVCompressionAdapter:
     def manager(self):
         return self._manager
 
+    def _fused(self) -> bool:
+        return getattr(self._manager, "backend", None) == "kvs_fused"
+
+    def _cpu_fallback(self):
+        """Generic-pipeline twin of the fused manager for tensors off the GPU
+        (the fused kernels need CUDA), as the reference falls back to its
+        quantizer + codec manager when its fused op is unavailable: the same
+        quantizer settings (fused defaults filled in), the Hadamard with the
+        same seed when the fused path applies it, and the same codec.  Its
+        messages carry ``backend: generic`` and decode on any device."""
+        if self._cpu_fallback_mgr is None:
+            m = self._manager
+            pipeline = (["transformer"] if m.base_seed is not None else []) + ["quantizer"]
+            if m.codec != "none":
+                pipeline.append("codec")
+            spec = {"enabled": True, "pipeline": pipeline, "backend": "generic",
+                    "transformer_config": {"transform_type": "hadamard",
+                                           "seed": m.base_seed if m.base_seed is not None
+                                           else DEFAULT_HADAMARD_SEED},
+                    "quantizer_config": dict(m.quantizer_config),
+                    "codec_config": dict(m.codec_config),
+                    "min_compress_size": int(getattr(m, "min_compress_size", 0))}
+            self._cpu_fallback_mgr = self._build(spec)
+        return self._cpu_fallback_mgr
+
     # ------------------------------------------------------------ public
     def _to_6d(self, stacked: torch.Tensor) -> torch.Tensor:
         if stacked.dim() == 6:
@@ -189,6 +215,9 @@ class KVCompressionAdapter:
             return self._compress_controller(x, request_id, meta)
         if x.numel() * x.element_size() < getattr(self._manager, "min_compress_size", 0):
             return None
+        if self._fused() and not x.is_cuda:
+            mgr, conf = self._cpu_fallback()
+            return mgr.compress_all_layers(x, request_id, conf, meta)
         return self._manager.compress_all_layers(x, request_id, self._config, meta)
 
     def decompress(self, compressed: CompressedKVData) -> Optional[torch.Tensor]:
@@ -198,6 +227,8 @@ class KVCompressionAdapter:
                 logger.error("controller mode: ctrl_profile_cfg missing from metadata")
                 return None
             mgr, conf = self._get_cached_manager(cfg)
+        elif self._fused() and (compressed.metadata or {}).get("backend") == "generic":
+            mgr, conf = self._cpu_fallback()  # a message of the CPU fallback
         else:
             mgr, conf = self._manager, self._config
         res = mgr.decompress_all_layers(compressed, conf)
@@ -219,6 +250,7 @@ class KVCompressionAdapter:
         return self._manager is not None and hasattr(self._manager, "compress_quant_layer")
 
     def supports_paged(self) -> bool:
+        """Paged multi-request compression (the fused kernels: CUDA tensors)."""
         return self._manager is not None and hasattr(self._manager, "compress_paged_requests")
 
     def compress_quant_layer(self, kv_layer, layer_id):

@@ -344,7 +344,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             t0 = time.monotonic()
             span = self._prefill_span(rid)
             layers = [self._layer_refs[n] for n in names]
-            if comp is not None and comp.supports_paged():
+            if comp is not None and comp.supports_paged() and layers[0].is_cuda:
                 try:
                     with nvtx("kvs.compress"):
                         cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],

@@ -451,3 +451,26 @@ def test_native_cpu_lc_matches_reference_and_rejects_corruption():
         except ValueError:
             rejected += 1
     assert rejected >= 100
+
+
+def test_default_mode_falls_back_to_the_generic_pipeline_on_cpu():
+    """Default mode builds the fused manager; a CPU tensor goes through its
+    generic twin (same quantizer settings, Hadamard seed and codec) instead
+    of failing on CUDA initialisation, and the message decodes back."""
+    from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter
+    ad = KVCompressionAdapter("default", 4, 128, model_name="Qwen2.5-7B-Instruct", num_layers=28)
+    assert ad.manager.backend == "kvs_fused"
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(28, 2, 3, 16, 4, 128, generator=g)
+    x[:, 0, ..., :4] *= 12
+    x = x.to(torch.bfloat16)
+    cd = ad.compress(x, "r1")
+    assert cd.metadata["backend"] == "generic" and cd.metadata.get("transformer_applied")
+    assert cd.original_size / cd.compressed_size > 3
+    mgr, conf = ad._cpu_fallback()
+    assert conf.quantizer_config["hybrid_ratio"] == ad.manager.quantizer_config["hybrid_ratio"]
+    assert mgr.transformer.seed == 0x3333
+    out = ad.decompress(cd)
+    assert out.shape == x.shape
+    cos = torch.nn.functional.cosine_similarity(out.float().flatten(), x.float().flatten(), dim=0)
+    assert float(cos) > 0.95

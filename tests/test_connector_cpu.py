@@ -275,3 +275,15 @@ def test_controller_learns_from_compress_plus_transfer_time(tmp_path):
     p.get_finished(set())
     assert [r for r, _ in seen] == ["r1"] and seen[0][1] >= 50.0
     assert comp.get_controller_stats()["bandit_states"] == 1 and not p._ctl_wait
+
+
+def test_default_mode_handoff_on_cpu():
+    """compression "default" on CPU caches: the adapter's generic twin of the
+    fused path compresses, the consumer decodes into its own block ids."""
+    p, c, pair = make_pair("default")
+    pc, cc = handoff(p, c)
+    assert pair.messages == 1
+    for name in pc:
+        a = pc[name][:, [5, 1, 7]].float().flatten()
+        b = cc[name][:, [2, 6, 0]].float().flatten()
+        assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.9
