@@ -452,13 +452,32 @@ class P2PTransport:
                         "ring_bytes": self.ring_bytes, "flag_off": self.flag_off,
                         "n_flags": self.n_flags}))
                 elif cmd == "PUT_RING":
-                    self._on_put(msg)
+                    try:
+                        self._on_put(msg)
+                    except Exception as e:  # noqa: BLE001
+                        logger.error("p2p: unusable PUT_RING for %r: %s", msg.get("request_id"), e)
+                        self._reject_put(msg)
                 else:
                     logger.warning("p2p: unknown control message %r", cmd)
             except Exception as e:  # noqa: BLE001
                 if self._closed:  # the socket went away under close()
                     break
                 logger.error("p2p consumer io error: %s", e)
+
+    def _reject_put(self, msg: dict) -> None:
+        """A header that cannot be turned into tensors: the request is
+        reported failed at once (no wait for the load timeout) and its ring
+        region goes back to the producer, whose later stores into it queue on
+        the same transfer stream behind this message's."""
+        rid = msg.get("request_id")
+        if isinstance(rid, str):
+            with self._lock:
+                self._received[rid].append((FAILED_LAYER_NAMES, FAILED_PAYLOAD))
+                self._arrived.notify_all()
+        region = msg.get("region")
+        if (isinstance(region, (list, tuple)) and len(region) == 2
+                and all(isinstance(v, int) for v in region) and self._producer_id is not None):
+            self._ctl.reply(self._producer_id, pack({"cmd": "FREE", "regions": [list(region)]}))
 
     def _on_put(self, msg: dict) -> None:
         views = [tensor_view(self._region.ptr + s["off"], s["nbytes"], getattr(torch, s["dtype"]),

@@ -342,3 +342,38 @@ def test_transport_under_concurrent_senders():
                 assert names == ["l0"] and body == [[float(i)] * (i + 1)] * (k + 1)
             else:
                 assert meta == {"k": k, "i": i} and body == [[k] * (i + 3)]
+
+
+def test_p2p_consumer_rejects_unusable_headers():
+    """A PUT_RING header whose payload cannot be mapped (here: no device)
+    reports the request failed at once and returns its ring region."""
+    import threading
+    from collections import defaultdict, deque
+
+    from kvserve_hpdps_b200.parallel.control import unpack
+    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport
+
+    class Ctl:
+        def __init__(self):
+            self.sent = []
+
+        def reply(self, ident, payload):
+            self.sent.append((ident, unpack(payload)))
+
+    t = object.__new__(P2PTransport)
+    t._lock = threading.Lock()
+    t._arrived = threading.Condition(t._lock)
+    t._received = defaultdict(deque)
+    t._ctl, t._producer_id = Ctl(), b"prod"
+    t._region = type("R", (), {"ptr": 4096})()
+    t.local_rank, t.is_sender = 0, False
+    msg = {"cmd": "PUT_RING", "kind": "bundle", "request_id": "r9", "layer_names": ["a"],
+           "meta": {}, "n_body": 1, "region": [512, 1024], "slot": 3, "seq": 7,
+           "specs": [{"shape": [4], "dtype": "uint8", "off": 512, "nbytes": 4}]}
+    with pytest.raises(Exception):
+        t._on_put(msg)  # tensor views need a CUDA device
+    t._reject_put(msg)
+    assert t.drain_received() == {"r9": [([], None)]}
+    assert t._ctl.sent == [(b"prod", {"cmd": "FREE", "regions": [[512, 1024]]})]
+    t._reject_put({"cmd": "PUT_RING"})  # nothing to report or return
+    assert t.drain_received() == {} and len(t._ctl.sent) == 1
