@@ -58,3 +58,70 @@ def test_wire_messages_cross_between_the_frameworks():
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                          timeout=600, cwd="/tmp" if os.path.isdir("/tmp") else ROOT)
     assert out.returncode == 0 and "INTEROP OK" in out.stdout, out.stderr[-3000:]
+
+
+CTL = r"""
+import json, sys
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+from kvserve_hpdps_b200.controller.analytical_model import AnalyticalModel
+from kvserve_hpdps_b200.controller.online_controller import OnlineController as Ours
+from kvserve_hpdps_b200.controller.profile_library import ProfileLibrary as OursLib
+from kvserve_hpdps_b200.offline.library_export import build_library, write_library
+from kvserve_hpdps_b200.offline.search_space import Candidate
+from kvserve_v1.compression.controller.online_controller import OnlineController as Ref
+from kvserve_v1.compression.controller.profile_library import ProfileLibrary as RefLib
+evals = []
+for c, acc, cr, s in [(Candidate(0.0, 16, 16, 8, 6), 0.995, 3.5, 30000.0),
+                      (Candidate(0.3, 16, 12, 8, 6), 0.985, 4.6, 24000.0),
+                      (Candidate(0.8, 12, 8, 6, 4), 0.97, 6.0, 20000.0),
+                      (Candidate(1.0, 12, 8, 6, 4), 0.93, 7.4, 16000.0)]:
+    evals.append({"candidate": c.key(), "config": c.quantizer_config(), "accuracy": acc,
+                  "compression_ratio": cr, "harmonic_speed_mbps": s})
+path = TMP + "/lib.json"
+write_library(path, build_library(evals, "Qwen2.5-7B-Instruct"))
+ours = Ours(OursLib(path), epsilon=0.0, model=AnalyticalModel(reference_transfer_term=True))
+ref = Ref(RefLib(path), epsilon=0.0)
+n = 0
+compared = set()
+for V in (64e6, 470e6, 2e9):
+    for B in (2.0, 10.0, 50.0, 150.0, 400.0, 1000.0, 3000.0, 1e6):
+        for slo in (50.0, 500.0, 1e9):
+            for acc in (0.9, 0.96, 0.99, 0.999):
+                po, co = ours.select_profile(V, B, 10.0, slo, acc)
+                pr, cr_ = ref.select_profile(V, B, 10.0, slo, acc)
+                ido = None if po is None else po.profile_id
+                idr = None if pr is None else pr.profile_id
+                assert ido == idr, (V, B, slo, acc, ido, idr)
+                for k in ("bucket_id", "interval_id", "profile_id", "action", "num_candidates",
+                          "T_hat", "T_eff", "delta_bar", "baseline_latency", "speedup_predicted"):
+                    if k in cr_:
+                        a, b = co.get(k), cr_[k]
+                        assert a == b or (isinstance(b, float) and abs(a - b) <= 1e-9 * max(1, abs(b))), \
+                            (k, co, cr_)
+                        compared.add(k)
+                if po is not None:
+                    t = 5.0 + (n % 7)
+                    ours.update(co, t)
+                    ref.update(cr_, t)
+                n += 1
+so, sr = ours.get_statistics(), ref.get_statistics()
+for k in ("total_decisions", "exploit_count", "explore_count", "no_compression_count"):
+    assert so[k] == sr[k], (k, so, sr)
+assert {"profile_id", "T_hat", "T_eff", "delta_bar"} <= compared, compared
+print("CONTROLLER OK", n)
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_controller_decisions_match_the_reference(tmp_path):
+    """Same library, same requests: both controllers (with the reference's
+    transfer term selected here) pick the same profile, with the same bucket,
+    interval and predicted latency, and keep the same statistics."""
+    code = CTL.replace("ROOT", repr(ROOT)).replace("REF", repr(REF)) \
+        .replace("TMP", repr(str(tmp_path)))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0 and "CONTROLLER OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
