@@ -125,3 +125,75 @@ def test_controller_decisions_match_the_reference(tmp_path):
                          timeout=600, cwd=str(tmp_path))
     assert out.returncode == 0 and "CONTROLLER OK" in out.stdout, \
         (out.stdout[-1500:] + out.stderr[-3000:])
+
+
+PARTS = r"""
+import sys, types
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+# the reference's transform module imports its FWHT extension at import time;
+# only its sign generation (plain torch) is called here
+sys.modules.setdefault("fast_hadamard_transform", types.ModuleType("fast_hadamard_transform"))
+import torch
+from kvserve_hpdps_b200.compression import wire as OW
+from kvserve_hpdps_b200.compression.head_scores import slice_for_tp
+from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter as Ours
+from kvserve_hpdps_b200.compression.quantizer import KVServeQuantizer as OQ
+from kvserve_hpdps_b200.compression.transformer import HadamardTransform as OH
+from kvserve_v1.compression import wire as RW
+from kvserve_v1.compression.manager import KVCompressionAdapter as Ref
+from kvserve_v1.compression.quantizer.kvserve_quantizer import KVServeQuantizer as RQ
+from kvserve_v1.compression.transformer.hadamard_func import HadamardTransform as RH
+# Rademacher signs
+for seed in (0x3333, 0xC0FEBABE):
+    for layer in (0, 5, 27):
+        a = OH(seed).get_rademacher_signs(layer, 8, 128, torch.device("cpu"), torch.float32)
+        b = RH(seed).get_rademacher_signs(layer, 8, 128, torch.device("cpu"), torch.float32)
+        assert torch.equal(a, b), ("signs", seed, layer)
+# hybrid head / layer masks and their TP slices
+for model in ("Qwen2.5-7B-Instruct", "Llama-3.1-8B-Instruct", "Qwen2.5-32B-Instruct"):
+    for hr in (0.0, 0.3, 0.5, 0.8, 1.0):
+        o, r = OQ(model_name=model, hybrid_ratio=hr), RQ(model_name=model, hybrid_ratio=hr)
+        assert torch.equal(o.head_scores_mask, r.head_scores_mask), ("head mask", model, hr)
+        assert torch.equal(o.layer_scores_mask, r.layer_scores_mask), ("layer mask", model, hr)
+        H = r.head_scores_mask.shape[1]
+        for tp in (2,):
+            for rank in range(tp):
+                rt = RQ(model_name=model, hybrid_ratio=hr, tensor_parallel_size=tp, tp_rank=rank)
+                got = slice_for_tp(o.head_scores_mask, H // tp, rank, tp)
+                assert torch.equal(got, rt._get_tp_head_scores_mask(H // tp)), ("tp", model, hr, rank)
+# chunked wire bodies (byte_chunks) in both directions
+L, T, H, D = 2, 128, 4, 128
+x = torch.randn((L, 2, 1, T, H, D), generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+qc = {"model_name": "Qwen2.5-7B-Instruct", "hybrid_ratio": 0.5, "axis_key": "channel",
+      "axis_value": "token", "split_type": "head"}
+ours = Ours({"enabled": True, "pipeline": ["quantizer"], "backend": "generic",
+             "quantizer_config": qc, "min_compress_size": 0}, H, D,
+            model_name="Qwen2.5-7B-Instruct", num_layers=28)
+ref = Ref({"enabled": True, "pipeline": ["quantizer"], "quantizer_config": qc}, H, D,
+          model_name="Qwen2.5-7B-Instruct")
+cd = ours.compress(x, "a")
+w = OW.build_wire(cd, 4096)
+assert w.meta["body_mode"] == "byte_chunks" and len(w.body_chunks) > 1
+by_ref = ref.decompress(RW.restore_from_wire(RW.CompressedWire(w.meta, w.body_chunks,
+                                                               w.aux_tensors)))
+assert torch.equal(by_ref.reshape(-1), ours.decompress(cd).reshape(-1)), "chunked ours -> ref"
+rw = RW.build_wire(ref.compress(x, "b"), 4096)
+assert rw.meta["body_mode"] == "byte_chunks"
+by_ours = ours.decompress(OW.restore_from_wire(OW.CompressedWire(rw.meta, rw.body_chunks,
+                                                                 rw.aux_tensors)))
+assert torch.equal(by_ours.reshape(-1), by_ref.reshape(-1)), "chunked ref -> ours"
+print("PARTS OK")
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_signs_masks_and_chunked_wire_match_the_reference(tmp_path):
+    """Rademacher signs, hybrid head/layer masks (and their TP slices) equal
+    the reference's, and chunked wire bodies cross in both directions."""
+    code = PARTS.replace("ROOT", repr(ROOT)).replace("REF", repr(REF))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0 and "PARTS OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
