@@ -197,3 +197,95 @@ def test_signs_masks_and_chunked_wire_match_the_reference(tmp_path):
                          timeout=600, cwd=str(tmp_path))
     assert out.returncode == 0 and "PARTS OK" in out.stdout, \
         (out.stdout[-1500:] + out.stderr[-3000:])
+
+
+SCHED = r"""
+import sys
+from types import SimpleNamespace as NS
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+import os
+os.environ["KVSERVE_TRANSPORT"] = "fake"
+from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+from kvserve_hpdps_b200.connector.compressed_kv_connector import CompressedKVConnector as Ours
+from kvserve_v1.connector.compressed_kv_connector import CompressedKVConnector as Ref
+
+def cfg(producer):
+    mc = NS(get_num_kv_heads=lambda pc: 4, get_head_size=lambda: 128,
+            get_num_layers=lambda pc: 2, model="/models/Qwen2.5-7B-Instruct",
+            hf_text_config=NS(num_hidden_layers=2), use_mla=False)
+    kv = NS(is_kv_producer=producer, kv_ip="127.0.0.1", kv_port=29999, kv_role="kv_both",
+            kv_connector_extra_config={"compression": None}, kv_parallel_size=2, kv_rank=0)
+    return NS(kv_transfer_config=kv, cache_config=NS(block_size=16), model_config=mc,
+              parallel_config=NS())
+
+def meta_rows(m):
+    return [(r.request_id, r.transfer_id, list(r.token_ids), list(r.block_ids),
+             r.slot_mapping.tolist()) for r in m.requests]
+
+def script(conn, producer):
+    out = []
+    reqs = {"r": NS(request_id="r", prompt_token_ids=list(range(50)),
+                    kv_transfer_params={"transfer_id": "T9"}, all_token_ids=list(range(51))),
+            "c": NS(request_id="c", prompt_token_ids=list(range(40)),
+                    kv_transfer_params={"transfer_id": "TC"}, all_token_ids=list(range(40))),
+            "n": NS(request_id="n", prompt_token_ids=list(range(20)), kv_transfer_params=None,
+                    all_token_ids=list(range(20))),
+            "p": NS(request_id="p", prompt_token_ids=list(range(33)),
+                    kv_transfer_params={"transfer_id": "TP"}, all_token_ids=list(range(35))),
+            "q": NS(request_id="q", prompt_token_ids=list(range(40)),
+                    kv_transfer_params={"transfer_id": "TQ"}, all_token_ids=list(range(40)))}
+    for rid, r in reqs.items():
+        out.append(("matched", rid, conn.get_num_new_matched_tokens(r, 0),
+                    conn.get_num_new_matched_tokens(r, 16)))
+    blocks = {"r": [3, 4, 5, 6], "c": [1, 2], "n": [7, 8], "p": [10, 11, 12], "q": [16]}
+    for rid, r in reqs.items():
+        n_ext = 0 if producer else max(0, len(r.prompt_token_ids) - 1)
+        conn.update_state_after_alloc(r, NS(get_block_ids=lambda b=blocks[rid]: (b,)), n_ext)
+    empty = NS(req_ids=[], num_computed_tokens=[], new_block_ids=[], resumed_req_ids=set())
+    new = lambda rid, n0=0: NS(req_id=rid, prompt_token_ids=reqs[rid].prompt_token_ids,
+                               block_ids=(blocks[rid],), num_computed_tokens=n0)
+    so1 = NS(scheduled_new_reqs=[new("r"), new("c"), new("n"), new("q")],
+             num_scheduled_tokens={"r": 50, "c": 32, "n": 20, "q": 16},
+             scheduled_cached_reqs=empty)
+    out.append(("step1", meta_rows(conn.build_connector_meta(so1))))
+    cached = NS(req_ids=["c"], num_computed_tokens=[32], new_block_ids=[([9],)],
+                resumed_req_ids=set())
+    so2 = NS(scheduled_new_reqs=[], num_scheduled_tokens={"c": 8}, scheduled_cached_reqs=cached)
+    out.append(("step2", meta_rows(conn.build_connector_meta(so2))))
+    # resumed after preemption: the producer's chunked prefill "q" restarts in new
+    # blocks; the consumer's "p" (never scheduled before) loads into its new blocks
+    rid3 = "q" if producer else "p"
+    resumed = NS(req_ids=[rid3], num_computed_tokens=[0 if producer else 32],
+                 new_block_ids=[([20, 21, 22],)], resumed_req_ids={rid3})
+    so3 = NS(scheduled_new_reqs=[], num_scheduled_tokens={rid3: 40 if producer else 1},
+             scheduled_cached_reqs=resumed)
+    out.append(("step3", meta_rows(conn.build_connector_meta(so3))))
+    out.append(("finished", conn.request_finished(reqs["r"], blocks["r"])))
+    return out
+
+for producer in (True, False):
+    a = script(Ours(cfg(producer), KVConnectorRole.SCHEDULER), producer)
+    b = script(Ref(cfg(producer), KVConnectorRole.SCHEDULER), producer)
+    for x, y in zip(a, b):
+        assert x == y, ("producer" if producer else "consumer", x, y)
+    assert len(a) == len(b)
+print("SCHEDULER OK")
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_scheduler_side_matches_the_reference(tmp_path):
+    """Producer and consumer scheduler-side connectors on the same scripted
+    steps (full prompt, chunked prefill over two steps, a request without a
+    transfer id, a request resumed after preemption) build the same request
+    metadata as the reference's connector: ids, tokens, blocks, slots.  (The
+    steps are ones the reference accepts: its producer asserts that every
+    scheduled cached request is a chunked prefill.)"""
+    pytest.importorskip("vllm")
+    code = SCHED.replace("ROOT", repr(ROOT)).replace("REF", repr(REF))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=900, cwd=str(tmp_path))
+    assert out.returncode == 0 and "SCHEDULER OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
