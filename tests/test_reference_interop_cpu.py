@@ -109,6 +109,22 @@ so, sr = ours.get_statistics(), ref.get_statistics()
 for k in ("total_decisions", "exploit_count", "explore_count", "no_compression_count"):
     assert so[k] == sr[k], (k, so, sr)
 assert {"profile_id", "T_hat", "T_eff", "delta_bar"} <= compared, compared
+# bandit state files cross both ways and keep learning identically
+ref.save_state(TMP + "/ref_state.json")
+ours.save_state(TMP + "/ours_state.json")
+o2 = Ours(OursLib(path), epsilon=0.0, model=AnalyticalModel(reference_transfer_term=True))
+r2 = Ref(RefLib(path), epsilon=0.0)
+o2.load_state(TMP + "/ref_state.json")
+r2.load_state(TMP + "/ours_state.json")
+po, co = o2.select_profile(470e6, 50.0, 10.0, 1e9, 0.96)
+pr, cr_ = r2.select_profile(470e6, 50.0, 10.0, 1e9, 0.96)
+assert po is not None and pr is not None and po.profile_id == pr.profile_id
+assert abs(co["delta_bar"] - cr_["delta_bar"]) < 1e-9 and co["delta_bar"] != 0.0, (co, cr_)
+o2.update(co, 42.0)
+r2.update(cr_, 42.0)
+b, i, pid = co["bucket_id"], co["interval_id"], co["profile_id"]
+so, sr = o2.bandit.get_stats(b, i, pid), r2.bandit.get_stats(b, i, pid)
+assert so[0] == sr[0] and abs(so[1] - sr[1]) < 1e-9, (so, sr)
 print("CONTROLLER OK", n)
 """
 
