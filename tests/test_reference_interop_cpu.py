@@ -305,3 +305,63 @@ def test_scheduler_side_matches_the_reference(tmp_path):
                          timeout=900, cwd=str(tmp_path))
     assert out.returncode == 0 and "SCHEDULER OK" in out.stdout, \
         (out.stdout[-1500:] + out.stderr[-3000:])
+
+
+OFFLINE = r"""
+import sys, types
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+# the reference's offline caches were written for transformers 4.x
+# (CacheConfig) and import its FWHT extension; only pure functions run here
+import transformers.cache_utils as cu
+if not hasattr(cu, "CacheConfig"):
+    class CacheConfig:
+        def __init__(self, *a, **k):
+            pass
+    cu.CacheConfig = CacheConfig
+sys.modules.setdefault("fast_hadamard_transform", types.ModuleType("fast_hadamard_transform"))
+import torch
+from kvserve_hpdps_b200.offline import caches as C
+from kvserve_hpdps_b200.offline.caches.common import minmax_codes, minmax_values
+from kvserve_v1.offline_search.src.cache import cache_utils as RU
+from kvserve_v1.offline_search.src.cache import cachegen_utils as RC
+from kvserve_v1.offline_search.src.cache import duoattn_utils as RD
+for L in (4, 28, 32, 64):
+    for lvl in (1, 2, 3):
+        r = RC.CacheGenCacheConfig(model_layers=L, quantization_level=lvl)
+        ns = types.SimpleNamespace(**{k: getattr(r, k) for k in (
+            "model_layers", "quantization_level", "high_max_value", "mid_max_value",
+            "low_max_value")})
+        assert RC.CacheGenCache.make_quantized_bins(ns) == C.cachegen_bins(
+            C.CacheGenCacheConfig(model_layers=L, quantization_level=lvl)), ("bins", L, lvl)
+g = torch.Generator().manual_seed(0)
+x = torch.randn(3, 50, 16, generator=g) + 2.0
+assert torch.equal(RD.search_hyperplane(x.clone()), C.search_hyperplane(x.clone())), "hyperplane"
+for dtype in (torch.bfloat16, torch.float16, torch.float32):
+    kv = (torch.randn(1, 4, 97, 128, generator=g) * 3).to(dtype)
+    for maxv in (4, 12, 16, 255):
+        for axis in ([2], [1, 3], [-1], [0, 1, 2, 3]):
+            qr, mr = RU.CustomCache._quantize(None, maxv, kv, axis)
+            qo, mo = minmax_codes(kv, maxv, axis)
+            assert torch.equal(qr, qo) and torch.equal(mr, mo), ("quantize", dtype, maxv, axis)
+            assert torch.equal(RU.CustomCache._dequantize(None, qr, mr),
+                               minmax_values(qo, mo)), ("dequantize", dtype, maxv, axis)
+    empty = kv[:, :0]
+    qr, mr = RU.CustomCache._quantize(None, 12, empty, [2])
+    qo, mo = minmax_codes(empty, 12, [2])
+    assert qr.shape == qo.shape and mr.shape == mo.shape, "empty"
+print("OFFLINE OK")
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_offline_cache_math_matches_the_reference(tmp_path):
+    """Pure pieces of the reference's offline caches against ours: CacheGen's
+    per-layer bins, DuoAttention's streaming-head hyperplane, and the custom
+    cache's min-max quantize/dequantize over every axis choice and dtype."""
+    code = OFFLINE.replace("ROOT", repr(ROOT)).replace("REF", repr(REF))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0 and "OFFLINE OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
