@@ -123,6 +123,15 @@ class AffineTransform:
             self._inv_cache[int(layer_idx)] = inv
         return y @ inv.to(y).t()
 
+    # the reference's older names (cache_utils.py AffineTransform); its
+    # forward_transform hands ``kind`` to transform's layer slot, here each
+    # argument goes where its name says
+    def forward_transform(self, x: torch.Tensor, kind: str, layer_idx: int) -> torch.Tensor:
+        return self.transform(x, layer_idx, kind)
+
+    def inverse_transform(self, x: torch.Tensor, layer_idx: int) -> torch.Tensor:
+        return self.inverse(x, layer_idx)
+
 
 def make_transform(kind: str, base_seed: int = 0x3333, head_dim: int = 128,
                    params_path: Optional[str] = None, device="cpu"):

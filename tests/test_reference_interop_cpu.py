@@ -350,6 +350,32 @@ for dtype in (torch.bfloat16, torch.float16, torch.float32):
     qr, mr = RU.CustomCache._quantize(None, 12, empty, [2])
     qo, mo = minmax_codes(empty, 12, [2])
     assert qr.shape == qo.shape and mr.shape == mo.shape, "empty"
+# affine transforms from one parameter file in the reference's format
+import os, tempfile
+from kvserve_hpdps_b200.offline.caches.transforms import AffineTransform as OA
+D = 128
+for mode in ("diag", "full"):
+    params = {}
+    for layer in range(2):
+        sd = {"clip_k": torch.randn(D, generator=g) + 3, "clip_v": torch.randn(D, generator=g) + 3}
+        if mode == "diag":
+            sd["log_scale"] = torch.randn(D, generator=g) * 2
+        else:
+            sd["linear.weight"] = torch.eye(D) + 0.05 * torch.randn(D, D, generator=g)
+        params[layer] = {"state_dict": sd}
+    path = os.path.join(tempfile.mkdtemp(), "affine.pt")
+    torch.save(params, path)
+    ra = RU.AffineTransform(D, mode=mode, params_path=path, device="cpu")
+    oa = OA(D, mode=mode, params_path=path)
+    for dtype in (torch.float32, torch.bfloat16):
+        x = (torch.randn(1, 4, 33, D, generator=g) * 4).to(dtype)
+        for layer in (0, 1, 5):  # layer 5: default parameters on both sides
+            for kind in ("k", "v"):
+                yr, yo = ra.transform(x, layer, kind), oa.transform(x, layer, kind)
+                assert torch.equal(yr, yo), ("affine", mode, dtype, layer, kind)
+                assert torch.equal(ra.inverse(yr, layer), oa.inverse(yo, layer)), \
+                    ("affine inverse", mode, dtype, layer)
+        assert torch.equal(oa.forward_transform(x, "v", 1), oa.transform(x, 1, "v"))
 print("OFFLINE OK")
 """
 
