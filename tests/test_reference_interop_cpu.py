@@ -199,6 +199,29 @@ assert rw.meta["body_mode"] == "byte_chunks"
 by_ours = ours.decompress(OW.restore_from_wire(OW.CompressedWire(rw.meta, rw.body_chunks,
                                                                  rw.aux_tensors)))
 assert torch.equal(by_ours.reshape(-1), by_ref.reshape(-1)), "chunked ref -> ours"
+# paged KV block utilities: both cache layouts, shuffled and repeated block ids
+from kvserve_hpdps_b200.utils import kv_utils as OK_
+from kvserve_v1.utils import kv_utils as RK_
+tok = list(range(45))
+assert torch.equal(OK_.make_slot_mapping(tok, [7, 2, 9], 16), RK_.make_slot_mapping(tok, [7, 2, 9], 16))
+gk = torch.Generator().manual_seed(4)
+for shape in ((2, 10, 16, 4, 128), (10, 2, 16, 4, 128)):
+    layer = torch.randn(shape, generator=gk).to(torch.bfloat16)
+    ids = [7, 2, 9, 0]
+    a, b = OK_.extract_kv_from_layer_by_blocks(layer, ids), RK_.extract_kv_from_layer_by_blocks(layer, ids)
+    assert torch.equal(a, b), ("extract", shape)
+    l1, l2 = torch.zeros_like(layer), torch.zeros_like(layer)
+    OK_.inject_kv_into_layer_by_blocks(l1, a, [3, 1, 8, 5])
+    RK_.inject_kv_into_layer_by_blocks(l2, b, [3, 1, 8, 5])
+    assert torch.equal(l1, l2), ("inject", shape)
+    sm = OK_.make_slot_mapping(list(range(40)), [3, 1, 8], 16)
+    x1 = OK_.extract_kv_from_layer(layer, sm) if shape[0] == 2 else None
+    if x1 is not None:
+        assert torch.equal(x1, RK_.extract_kv_from_layer(layer, sm)), "extract slots"
+        m1, m2 = torch.zeros_like(layer), torch.zeros_like(layer)
+        OK_.inject_kv_into_layer(m1, x1, sm)
+        RK_.inject_kv_into_layer(m2, x1, sm)
+        assert torch.equal(m1, m2), "inject slots"
 print("PARTS OK")
 """
 
