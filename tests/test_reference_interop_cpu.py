@@ -199,6 +199,27 @@ assert rw.meta["body_mode"] == "byte_chunks"
 by_ours = ours.decompress(OW.restore_from_wire(OW.CompressedWire(rw.meta, rw.body_chunks,
                                                                  rw.aux_tensors)))
 assert torch.equal(by_ours.reshape(-1), by_ref.reshape(-1)), "chunked ref -> ours"
+# the hybrid quantizer itself: codes, metadata and reconstruction per layer
+def _same(a, b):
+    if torch.is_tensor(a):
+        return torch.is_tensor(b) and a.shape == b.shape and torch.equal(a, b)
+    if isinstance(a, dict):
+        return isinstance(b, dict) and a.keys() == b.keys() and all(_same(a[k], b[k]) for k in a)
+    return a == b
+gq = torch.Generator().manual_seed(6)
+for split in ("head", "layer"):
+    for ak, av in (("channel", "token"), ("token", "token"), ("tensor", "channel")):
+        kw = dict(model_name="Qwen2.5-7B-Instruct", hybrid_ratio=0.5, high_key_max_value=16,
+                  high_value_max_value=12, low_key_max_value=8, low_value_max_value=6,
+                  axis_key=ak, axis_value=av, split_type=split)
+        oq, rq = OQ(**kw), RQ(**kw)
+        for layer in (0, 13, 27):
+            x = (torch.randn(2, 5, 16, 4, 128, generator=gq) * 3).to(torch.bfloat16)
+            qo, mo = oq.quantize(layer, x)
+            qr, mr = rq.quantize(layer, x)
+            assert torch.equal(qo, qr) and _same(mo, mr), ("quantize", split, ak, av, layer)
+            assert torch.equal(oq.dequantize(layer, qo, mo), rq.dequantize(layer, qr, mr)), \
+                ("dequantize", split, ak, av, layer)
 # paged KV block utilities: both cache layouts, shuffled and repeated block ids
 from kvserve_hpdps_b200.utils import kv_utils as OK_
 from kvserve_v1.utils import kv_utils as RK_
