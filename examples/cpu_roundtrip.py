@@ -13,6 +13,7 @@ Example::
 
   python examples/cpu_roundtrip.py
   python examples/cpu_roundtrip.py --pipeline quantizer,codec --codec bitpack
+  python examples/cpu_roundtrip.py --mode default
 """
 
 from __future__ import annotations
@@ -36,6 +37,9 @@ def main(argv=None) -> int:
     ap.add_argument("--pipeline", default="transformer,quantizer,codec")
     ap.add_argument("--codec", default="rans", help="rans | bitpack | nvcomp | lc")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--mode", default="custom", choices=("custom", "default"),
+                    help="default: the 'default' compression spec (on the CPU the adapter runs "
+                         "the fused path's generic twin)")
     args = ap.parse_args(argv)
     from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter
     from kvserve_hpdps_b200.compression.oracle import error_metrics
@@ -53,6 +57,8 @@ def main(argv=None) -> int:
                                  "axis_key": "channel", "axis_value": "token",
                                  "split_type": "head"},
             "codec_config": {"codec_type": args.codec}, "min_compress_size": 0}
+    if args.mode == "default":
+        spec = "default"
     ad = KVCompressionAdapter(spec, H, D, model_name="Qwen2.5-7B-Instruct", num_layers=L)
     x = kv.view(L, 2, 1, T, H, D)
     t0 = time.perf_counter()
@@ -64,9 +70,13 @@ def main(argv=None) -> int:
     nbytes = build_wire(cd).nbytes
     err = error_metrics(x.float(), out.float())
     print(json.dumps({
-        "config": "CPU round trip, Qwen2.5-7B shapes [28, 2, 2048, 4, 128], hybrid 0.3, "
-                  "high 16/16, low key 12",
-        "pipeline": spec["pipeline"], "codec": args.codec,
+        "config": f"CPU round trip, Qwen2.5-7B shapes [{L}, 2, {T}, {H}, 128], " + (
+            "hybrid 0.3, high 16/16, low key 12" if isinstance(spec, dict) else
+            "default spec (hybrid 0.8, levels 12/8 high, 6/4 low, Hadamard, rANS)"),
+        "mode": args.mode,
+        "pipeline": spec["pipeline"] if isinstance(spec, dict) else
+        ad._cpu_fallback()[1].pipeline,
+        "codec": args.codec if isinstance(spec, dict) else "default",
         "original_bytes": kv.numel() * 2, "compressed_bytes": int(nbytes),
         "compression_ratio": round(kv.numel() * 2 / nbytes, 3),
         "rel_mse": err["rel_mse"], "cosine": err["cosine"],

@@ -268,6 +268,9 @@ def test_cpu_roundtrip_example_runs(capsys):
     assert mod.main(["--layers", "2", "--tokens", "256"]) == 0
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["compression_ratio"] > 2.0 and line["cosine"] > 0.98
+    assert mod.main(["--layers", "2", "--tokens", "256", "--mode", "default"]) == 0
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["mode"] == "default" and line["compression_ratio"] > 3.0 and line["cosine"] > 0.9
 
 
 def test_split_helpers_match_the_quantizer_layout():
