@@ -124,6 +124,17 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
         q_out.put(("error", role, traceback.format_exc()))
 
 
+def _stats_summary():
+    """With KVSERVE_*_STATS_PATH set (the engines inherit it), the summary of
+    the stats rows they wrote: mean compression ratio and the median
+    compress + comm + decompress path."""
+    import os
+    from kvserve_hpdps_b200.utils.stats import summarize
+    paths = [os.environ.get(f"KVSERVE_{k}_STATS_PATH") for k in ("COMPRESSION", "DECODE",
+                                                                    "TRANSFER")]
+    return summarize(*paths) if any(paths) else None
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -207,6 +218,9 @@ def main(argv=None) -> int:
                 "output_md5": hashlib.md5(json.dumps(first_tokens).encode()).hexdigest(),
                 "data": "synthetic uniform token ids; random-init weights (load_format=dummy)",
                 "timing": "host wall clock from dispatch to the consumer's first token"}
+        stats = _stats_summary()
+        if stats:
+            line["stats"] = stats
         print(json.dumps(line), flush=True)
     except Exception as e:  # noqa: BLE001
         print(json.dumps({"impl": args.impl, "compression": args.compression,
@@ -261,7 +275,8 @@ def run_one_role(args) -> int:
                           "role": args.role, "impl": args.impl,
                           "compression": args.compression, "requests": args.requests,
                           "latency_ms_p50": round(statistics.median(lat), 2),
-                          "output_md5": hashlib.md5(json.dumps(outs).encode()).hexdigest()}),
+                          "output_md5": hashlib.md5(json.dumps(outs).encode()).hexdigest(),
+                          **({"stats": _stats_summary()} if _stats_summary() else {})}),
               flush=True)
     except Exception as e:  # noqa: BLE001
         print(json.dumps({"role": args.role, "error": f"{type(e).__name__}: {e}"[-4000:]}),
