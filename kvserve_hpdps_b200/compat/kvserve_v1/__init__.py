@@ -57,17 +57,34 @@ _ALIASES: dict[str, tuple[str, ...]] = {
     "utils.logger": ("utils.logger",),
     "tilelang_ops": ("ops.hadamard_quant_op",),
     "tilelang_ops.kv_hadamard_quant": ("ops.hadamard_quant_op",),
+    "offline_search": ("offline",),
+    "offline_search.src": ("offline.caches",),
+    "offline_search.src.cache": ("offline.caches",),
+    "offline_search.src.cache.cache_utils": ("offline.caches",),
+    "offline_search.src.cache.kivi_utils": ("offline.caches",),
+    "offline_search.src.cache.cachegen_utils": ("offline.caches",),
+    "offline_search.src.cache.duoattn_utils": ("offline.caches",),
+    "offline_search.duo_config": ("offline.duo_scores",),
+    "offline_search.duo_config.duo_config": ("offline.duo_scores",),
 }
 
 # reference name -> name in the target modules
 _RENAMES = {"TileLangCompressionManager": "FusedCompressionManager"}
 
+# names that differ only under one alias (the offline Hadamard of the reference's
+# cache_utils is this package's HeadHadamard; compression.transformer keeps its own)
+_ALIAS_RENAMES: dict[str, dict[str, str]] = {
+    "offline_search.src.cache.cache_utils": {"HadamardTransform": "HeadHadamard"},
+    "offline_search.duo_config": {"duo_attention_on_the_fly": "duo_scores_on_the_fly"},
+    "offline_search.duo_config.duo_config": {"duo_attention_on_the_fly": "duo_scores_on_the_fly"},
+}
+
 # aliases that have submodules (get a __path__)
 _PACKAGES = {a.rsplit(".", 1)[0] for a in _ALIASES if "." in a}
 
 
-def _resolve(targets: tuple[str, ...], name: str):
-    real = _RENAMES.get(name, name)
+def _resolve(targets: tuple[str, ...], name: str, renames: dict = _RENAMES):
+    real = renames.get(name, name)
     for t in targets:
         mod = importlib.import_module(_P + t)
         if hasattr(mod, real):
@@ -95,7 +112,8 @@ class _AliasLoader(importlib.abc.Loader):
                 if n not in names and hasattr(mod, n):
                     names.append(n)
                     setattr(module, n, getattr(mod, n))
-        for ref_name, real in _RENAMES.items():
+        renames = {**_RENAMES, **_ALIAS_RENAMES.get(self.alias, {})}
+        for ref_name, real in renames.items():
             for t in targets:
                 mod = importlib.import_module(_P + t)
                 if hasattr(mod, real):
@@ -103,7 +121,7 @@ class _AliasLoader(importlib.abc.Loader):
                     names.append(ref_name)
                     break
         module.__all__ = names
-        module.__getattr__ = lambda name: _resolve(targets, name)
+        module.__getattr__ = lambda name: _resolve(targets, name, renames)
         module.__doc__ = f"Alias of {', '.join(_P + t for t in targets)}."
 
 

@@ -339,6 +339,15 @@ def test_reference_module_paths_alias_this_package():
         "from kvserve_v1.compression.compression_manager import DEFAULT_COMPRESSION_CONFIG",
         "import kvserve_v1.compression.wire as w, kvserve_hpdps_b200.compression.wire as w2",
         "assert w.build_wire is w2.build_wire and w._unpack is w2._unpack",
+        "from kvserve_v1.offline_search.src.cache.cache_utils import CustomCache, HadamardTransform",
+        "from kvserve_hpdps_b200.offline import caches as OC",
+        "assert CustomCache is OC.CustomCache and HadamardTransform is OC.HeadHadamard",
+        "from kvserve_v1.compression.transformer import HadamardTransform as RT",
+        "from kvserve_hpdps_b200.compression.transformer import HadamardTransform as CT",
+        "assert RT is CT",
+        "from kvserve_v1.offline_search.duo_config.duo_config import duo_attention_on_the_fly as D",
+        "from kvserve_hpdps_b200.offline.duo_scores import duo_scores_on_the_fly",
+        "assert D is duo_scores_on_the_fly",
         "print('ALIASES', len(_ALIASES))",
     ])
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([compat.path(), root]))
