@@ -95,6 +95,22 @@ logger = get_logger(__name__)
 
 LOAD_TIMEOUT_S = float(os.environ.get("KVSERVE_LOAD_TIMEOUT_S", "60"))
 CONTROLLER_FEEDBACK_TTL_S = 300.0  # as the adapter's controller contexts
+
+
+def normalize_overlap_mode(mode) -> str:
+    """``off`` or ``stream``.  The reference's ``tq`` and ``full`` modes
+    (per-layer transform/quantize on a side stream, codec and send at step
+    end) map to ``off``: its step-end chain already runs every layer of a
+    request in one launch per stage.  Anything else is ``off`` with a
+    warning."""
+    m = str(mode or "off").lower()
+    if m in ("off", "stream"):
+        return m
+    if m in ("tq", "full"):
+        logger.info("overlap mode %r: the fused step-end chain covers it; using 'off'", m)
+        return "off"
+    logger.warning("unknown overlap mode %r; using 'off'", mode)
+    return "off"
 DEFAULT_MAX_CHUNK_BYTES = 512 * 1024 * 1024
 _LAYER_RE = re.compile(r"layers?\.(\d+)")
 
@@ -162,6 +178,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         if isinstance(self._compression_cfg, dict) and "overlap" in self._compression_cfg:
             self._overlap_mode = self._compression_cfg.get("overlap", "off")
         self._overlap_mode = os.environ.get("KVSERVE_OVERLAP_MODE", self._overlap_mode)
+        self._overlap_mode = normalize_overlap_mode(self._overlap_mode)
         prio = int(self._compression_cfg.get("side_stream_priority", 0)) \
             if isinstance(self._compression_cfg, dict) else 0
         self._side_priority = int(os.environ.get("KVSERVE_SIDE_PRIORITY", prio))

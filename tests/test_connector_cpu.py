@@ -287,3 +287,13 @@ def test_default_mode_handoff_on_cpu():
         a = pc[name][:, [5, 1, 7]].float().flatten()
         b = cc[name][:, [2, 6, 0]].float().flatten()
         assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.9
+
+
+def test_overlap_modes_are_normalized(monkeypatch):
+    from kvserve_hpdps_b200.connector.compressed_kv_connector import normalize_overlap_mode
+    assert [normalize_overlap_mode(m) for m in ("off", "stream", "tq", "full", "FULL", None,
+                                                "bogus")] == \
+        ["off", "stream", "off", "off", "off", "off", "off"]
+    monkeypatch.setenv("KVSERVE_OVERLAP_MODE", "tq")
+    p, _, _ = make_pair(None)
+    assert p._overlap_mode == "off"
