@@ -5,6 +5,8 @@ GPUs)."""
 import importlib.util
 import os
 
+import pytest
+
 import bench
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -64,3 +66,19 @@ def test_ttft_harness_prompts_are_deterministic():
     a, b = mod.prompts(4, 64), mod.prompts(4, 64)
     assert a == b and len(a) == 4 and all(len(p) == 64 for p in a)
     assert all(0 <= t < mod.QWEN25_7B["vocab_size"] for p in a for t in p)
+
+
+def test_rank_pairing_for_every_scaling_point():
+    """N = 1, 2, 4, 8: rank r < N/2 produces for consumer r + N/2, both with
+    the same pair id; N = 1 runs both roles; odd N is rejected."""
+    import bench
+    assert bench._roles(1, 0) == ("both", 1)
+    for world in (2, 4, 8):
+        pairs = world // 2
+        roles = [bench._roles(world, r) for r in range(world)]
+        assert all(p == pairs for _, p in roles)
+        assert [r for r, _ in roles] == ["producer"] * pairs + ["consumer"] * pairs
+        for r in range(pairs):
+            assert r % pairs == (r + pairs) % pairs  # the pair id both sides derive
+    with pytest.raises(SystemExit):
+        bench._roles(3, 0)
