@@ -135,11 +135,44 @@ def evaluate_method(model, prompts: Sequence[torch.Tensor], method: str,
         test.close()
 
 
-def register_lm_eval(name: str = "kvserve_cache_model"):
+_CONFIGS = {"custom": "CustomCacheConfig", "kivi": "KIVICacheConfig",
+            "cachegen": "CacheGenCacheConfig", "duoattn": "DuoAttentionCacheConfig"}
+
+
+def split_cache_args(cache_type: str, kwargs: dict) -> tuple[dict, Optional[str], dict]:
+    """Split lm-eval ``model_args`` into (cache parameters, score-table name,
+    the rest for ``HFLM``).  A cache parameter is a field of the method's
+    config, written bare as the reference's wrapper takes it
+    (``transform_type=hadamard``) or prefixed (``cache_transform_type=...``);
+    ``scores`` / ``scores_model`` name a head-score table (model name or
+    CSV).  ``model_layers`` is filled in from the model for CacheGen."""
+    import dataclasses
+
+    from kvserve_hpdps_b200.offline import caches as C
+    if cache_type not in METHODS:
+        raise ValueError(f"unknown cache method {cache_type!r}; expected one of {METHODS}")
+    fields = set()
+    if cache_type in _CONFIGS:
+        fields = {f.name for f in dataclasses.fields(getattr(C, _CONFIGS[cache_type]))}
+    fields -= {"scores", "model_layers"}
+    params, rest, scores = {}, {}, None
+    for k, v in kwargs.items():
+        bare = k[len("cache_"):] if k.startswith("cache_") else k
+        if bare in ("scores", "scores_model"):
+            scores = v
+        elif bare in fields:
+            params[bare] = v
+        else:
+            rest[k] = v
+    return params, scores, rest
+
+
+def register_lm_eval(name: str = "my_custom_model"):
     """Register an lm-eval model class (``HFLM`` subclass) that generates
-    with a cache method: ``model_args="pretrained=...,cache_type=custom,..."``
-    (the remaining keyword arguments go to :func:`make_cache`).  Needs the
-    ``lm_eval`` package."""
+    with a cache method, under the reference's model name by default:
+    ``--model my_custom_model --model_args pretrained=...,cache_type=custom,
+    transform_type=hadamard,heads_selection=0.5,...`` (see
+    :func:`split_cache_args`).  Needs the ``lm_eval`` package."""
     try:
         from lm_eval.api.registry import register_model
         from lm_eval.models.huggingface import HFLM
@@ -148,13 +181,11 @@ def register_lm_eval(name: str = "kvserve_cache_model"):
 
     @register_model(name)
     class KVServeCacheLM(HFLM):
-        def __init__(self, *args, cache_type: str = "default", scores_model: str = "",
-                     **kwargs):
-            cache_params = {k: kwargs.pop(k) for k in list(kwargs) if k.startswith("cache_")}
-            super().__init__(*args, **kwargs)
+        def __init__(self, *args, cache_type: str = "default", **kwargs):
+            params, scores_name, rest = split_cache_args(cache_type, kwargs)
+            super().__init__(*args, **rest)
             from kvserve_hpdps_b200.compression.head_scores import get_scores_from_csv
-            scores = get_scores_from_csv(scores_model) if scores_model else None
-            params = {k[len("cache_"):]: v for k, v in cache_params.items()}
+            scores = get_scores_from_csv(scores_name) if scores_name else None
             self._kvs = CacheMethodModel(self.model, cache_type, scores, **params)
 
         def _model_generate(self, context, max_length, stop, **generation_kwargs):

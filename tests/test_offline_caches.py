@@ -222,3 +222,20 @@ def test_component_speed_methods_run_on_cpu(capsys):
                     "--iters", "1", "--warmup", "1", "--device", "cpu"]) == 0
     assert [json.loads(x)["phase"] for x in capsys.readouterr().out.splitlines()] == \
         ["compress", "reconstruct"]
+
+
+def test_lm_eval_model_args_split():
+    """lm-eval model_args as the reference's wrapper takes them (bare) or
+    prefixed: cache parameters go to the method's config, the rest to HFLM."""
+    from kvserve_hpdps_b200.offline.lm_harness import split_cache_args
+    p, scores, rest = split_cache_args("custom", {
+        "pretrained": "m", "transform_type": "hadamard", "cache_heads_selection": 0.3,
+        "high_key_max_value": 16, "scores": "Qwen2.5-7B-Instruct", "dtype": "bfloat16"})
+    assert p == {"transform_type": "hadamard", "heads_selection": 0.3, "high_key_max_value": 16}
+    assert scores == "Qwen2.5-7B-Instruct" and rest == {"pretrained": "m", "dtype": "bfloat16"}
+    p, _, rest = split_cache_args("kivi", {"nbits": 2, "q_group_size": 32, "batch_size": 4})
+    assert p == {"nbits": 2, "q_group_size": 32} and rest == {"batch_size": 4}
+    p, _, rest = split_cache_args("default", {"nbits": 2})
+    assert p == {} and rest == {"nbits": 2}
+    with pytest.raises(ValueError):
+        split_cache_args("zip", {})
