@@ -47,6 +47,26 @@ by_ours = ours.decompress(OW.restore_from_wire(OW.CompressedWire(rw.meta, rw.bod
 assert torch.equal(by_ours.reshape(-1), ref.decompress(rc).reshape(-1)), "reference -> ours"
 assert torch.equal(cd.compressed_tensor.view(torch.uint8).reshape(-1),
                    rc.compressed_tensor.view(torch.uint8).reshape(-1)), "bodies"
+# layer-chunked messages (manager_chunks body mode): the size threshold is
+# lowered on our side and the reference's chunked path is called directly
+from kvserve_hpdps_b200.compression import pipeline_manager as PM
+L2 = 20
+x2 = torch.randn((L2, 2, 1, 64, H, D), generator=g).to(torch.bfloat16)
+PM.CHUNK_THRESHOLD_BYTES = 1024
+cd2 = ours.compress(x2, "c")
+assert cd2.is_chunked and len(cd2.chunks) == 3
+w2 = OW.build_wire(cd2, 512 << 20)
+assert w2.meta["body_mode"] == "manager_chunks"
+r2 = ref.decompress(RW.restore_from_wire(RW.CompressedWire(w2.meta, w2.body_chunks,
+                                                           w2.aux_tensors)))
+assert torch.equal(r2.reshape(-1), ours.decompress(cd2).reshape(-1)), "chunked ours -> reference"
+rc2 = ref._manager._compress_all_layers_chunked(
+    x2, "d", {"original_dtype": "bfloat16", "original_shape": list(x2.shape)}, chunk_size=8)
+rw2 = RW.build_wire(rc2, 512 << 20)
+assert rw2.meta["body_mode"] == "manager_chunks"
+o2 = ours.decompress(OW.restore_from_wire(OW.CompressedWire(rw2.meta, rw2.body_chunks,
+                                                            rw2.aux_tensors)))
+assert torch.equal(o2.reshape(-1), ref.decompress(rc2).reshape(-1)), "chunked reference -> ours"
 print("INTEROP OK")
 """
 
