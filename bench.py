@@ -7,25 +7,48 @@ Metric: "PD KV-transfer ms/request & p50 TTFT (Qwen2.5-7B,
 synthetic N(0,1) KV with 3% outlier key channels x12 stored in a paged cache
 (16-token blocks) at shuffled block ids.
 
+Both arms run the same stages on the same workload: the default mode's
+randomized Hadamard + hybrid min-max quantization (hybrid_ratio 0.8, levels
+12/8 high, 6/4 low) with one byte per code and no entropy coder, the
+transfer, and dequantization + inverse transform into the consumer's paged
+cache.  That is the stage set the reference can run on this machine: its
+entropy coders (nvCOMP ANS through CuPy, the LC library) are not installed.
+This framework's own default path (4-bit codes + interleaved rANS) is timed
+as well and reported under ``full_path``.
+
 One step hands off ``--requests-per-step`` requests:
+
 * N = 1: round trip on one GPU -- fused quantize of every (layer, request)
-  item from the paged cache, rANS encode, rANS decode, fused dequantize +
+  item from the paged cache, [rANS encode, decode,] fused dequantize +
   inverse transform + scatter into a second paged cache;
 * N >= 2 (torchrun, one rank per GPU): ranks [0, N/2) are producers, rank
-  r + N/2 is r's consumer.  The producer's encoder writes the stream
-  straight into the consumer's receive slot over NVLink and publishes a
-  ready flag; the consumer waits (bounded) on the flag, decodes and scatters
-  into its paged cache, then returns a credit flag to the producer.
+  r + N/2 is r's consumer.  Each step is one message sent through the
+  product path: ``FusedCompressionManager.send_paged_requests`` over the
+  NVLink ring transport (``P2PTransport``), where the quantize kernel (byte
+  codes) or the rANS compaction kernel stores straight into the consumer's
+  receive ring and the last CTA publishes the ready flag; the consumer waits
+  on the flag on the device, verifies the message checksum and decodes into
+  its paged cache (``decompress_paged_requests``).
 
-``value`` is the job-wide device time divided by the requests handed off
-by the whole job (ms/request, lower is better): each rank times its stream
-with CUDA events between barriers, the maximum over ranks is used.
+``value`` is ms per request of one producer/consumer pair (lower is
+better): each rank times its stream with CUDA events between barriers, the
+maximum over ranks is divided by the requests one pair handed off.  Per-pair
+work is fixed as N grows (weak scaling), so equal values at every N mean
+linear scaling.  ``e2e`` is the same path with every step's request
+descriptors copied host->device from pinned memory and the step's result
+(the device error word) read back.  At N >= 2 ``single_request_latency_ms``
+is one un-pipelined request, from the producer's first kernel to the
+consumer's scatter completing (the consumer's release flag lands back in
+the producer's memory), device-timed on the producer.
 
 ``--impl reference`` runs the unmodified reference package from
-``baseline/_ref`` through its public ``KVCompressionAdapter`` on the same
-workload.  Its default mode needs nvCOMP, CuPy and fast_hadamard_transform,
-which are not installed, so the arm runs its quantizer-only custom pipeline
-(the degraded mode of its own tests) and, for N >= 2, its NcclTransport.
+``baseline/_ref``: its fused TileLang op ``KVHadamardQuantOp.compress_v3`` /
+``decompress_v3`` per layer, in the order of its TileLang manager
+(kvserve_v1/compression/tilelang_manager.py:158-216, :353-385) minus the
+codec stage, its block extract/inject utilities, and at N >= 2 its wire
+envelope and ``NcclTransport``.  ``decompress_v3`` imports
+``fast_hadamard_transform`` (not installed); the arm supplies the plain
+PyTorch stand-in in ``baseline/standin`` (one matrix product).
 """
 
 from __future__ import annotations
@@ -47,6 +70,7 @@ if ROOT not in sys.path:
 
 METRIC = "PD KV-transfer ms/request & p50 TTFT (Qwen2.5-7B, 8K prompt); compression ratio"
 MODEL = "Qwen2.5-7B-Instruct"
+HADAMARD_SEED = 0x3333  # the reference manager's default seed (manager.py:159)
 
 
 def parse_args(argv=None):
@@ -60,13 +84,17 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--kv-heads", type=int, default=4)
     ap.add_argument("--block-size", type=int, default=16)
-    ap.add_argument("--codec", default="rans", choices=["rans", "bitpack", "none"])
+    ap.add_argument("--codec", default="none", choices=["none", "rans", "bitpack"],
+                    help="codec of the headline path (none: the stages both arms can run)")
+    ap.add_argument("--no-full-path", action="store_true",
+                    help="skip timing this framework's default path (4-bit codes + rANS)")
     ap.add_argument("--engine", default="tcgen05", choices=["tcgen05", "simt"])
     ap.add_argument("--compression", default="default", choices=["default", "off"],
                     help="off: raw KV blocks (no transform, quantization or codec)")
     ap.add_argument("--hybrid-ratio", type=float, default=None,
                     help="override the default mode's hybrid_ratio")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--latency-reps", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args(argv)
 
@@ -113,6 +141,16 @@ def allreduce_sum(x: float, world: int) -> float:
     return float(t.item())
 
 
+def first_non_none(x, world: int):
+    """The value of the first rank that has one (all ranks call this)."""
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    gathered = [None] * world
+    dist.all_gather_object(gathered, x)
+    return next((g for g in gathered if g is not None), None)
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons (200 ms)."""
@@ -125,7 +163,6 @@ class ClockSampler:
         self.gpus = set(gpus)
         self.proc = None
         self.path = None
-        self.window = None
 
     def start(self):
         try:
@@ -137,9 +174,6 @@ class ClockSampler:
                  "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
-
-    def mark(self, t0, t1):
-        self.window = (t0, t1)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -214,21 +248,41 @@ class Workload:
     def bf16_bytes_per_request(self) -> int:
         return self.L * 2 * self.T * self.H * 128 * 2
 
+    def src_layers(self):
+        return [self.src[l] for l in range(self.L)]
 
-def quant_config(args):
+    def dst_layers(self):
+        return [self.dst[l] for l in range(self.L)]
+
+
+def quant_config(args, codec=None):
     from kvserve_hpdps_b200.compression.config import get_default_compression_config
     cfg = get_default_compression_config()
     cfg["quantizer_config"]["model_name"] = MODEL
     if getattr(args, "hybrid_ratio", None) is not None:
         cfg["quantizer_config"]["hybrid_ratio"] = float(args.hybrid_ratio)
-    if args.codec == "bitpack":
+    codec = codec or args.codec
+    if codec == "bitpack":
         cfg["codec_config"] = {"codec_type": "bitpack"}
-    elif args.codec == "none":
+    elif codec == "none":
         cfg["codec_config"] = {"codec_type": "none"}
     return cfg
 
 
-# ------------------------------------------------------------------ ours
+def hybrid_ratio(args) -> float:
+    return float(quant_config(args)["quantizer_config"]["hybrid_ratio"])
+
+
+def compression_label(args, codec=None) -> str:
+    """The ``config.compression`` string: identical for both arms."""
+    if args.compression == "off":
+        return "off (raw bf16 blocks)"
+    codec = codec or args.codec
+    codes = {"none": "u8 codes, no entropy codec", "rans": "4-bit codes + rANS",
+             "bitpack": "bit-packed codes"}[codec]
+    return f"default mode: Hadamard + hybrid {hybrid_ratio(args)} 12/8/6/4, {codes}"
+
+
 def _roles(world, rank):
     pairs = max(1, world // 2)
     if world == 1:
@@ -238,332 +292,30 @@ def _roles(world, rank):
     return ("producer" if rank < pairs else "consumer"), pairs
 
 
-def _timed(step, args, world, local, device, s0):
-    """Warm-up, then ``args.steps`` steps between barriers and device
-    synchronisations, timed with CUDA events; returns (max ms over ranks,
-    clocks, next step index, device error)."""
-    from kvserve_hpdps_b200.ops import kernels as K
-    s = s0
-    for _ in range(args.warmup):
-        step(s)
-        s += 1
-    torch.cuda.synchronize(device)
-    err = K.read_device_error(device)
-    if err:
-        raise RuntimeError(f"device error {err} during warmup ({K.ERR_NAMES.get(err)})")
-    sampler = ClockSampler(range(world)) if local == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize(device)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(args.steps):
-        step(s)
-        s += 1
-    ev1.record()
-    torch.cuda.synchronize(device)
-    barrier(world)
-    ms = ev0.elapsed_time(ev1)
-    err = K.read_device_error(device)
-    clocks = sampler.stop() if sampler else None
-    return allreduce_max(ms, world), clocks, s, int(allreduce_max(float(err), world))
-
-
-def run_ours_raw(args, rank, world, local):
-    """Compression off: raw KV blocks.  N = 1: one gather launch of every
-    (layer, request) item from the paged cache into a flat buffer and one
-    scatter launch into the second cache.  N >= 2: the producer's gather
-    stores straight into the consumer's receive slot over NVLink and
-    publishes a ready flag; the consumer waits (bounded) on it and scatters
-    into its cache, then returns a credit flag."""
-    from kvserve_hpdps_b200.ops import kernels as K
-    device = torch.device("cuda", local)
-    role, pairs = _roles(world, rank)
-    pair_id = rank % pairs
-    wl = Workload(args, device, args.seed + 101 * pair_id, role)
-    L = args.layers
-    layers_src = [wl.src[l] for l in range(L)] if wl.src is not None else None
-    layers_dst = [wl.dst[l] for l in range(L)] if wl.dst is not None else None
-    src_raw = K.RawItems(layers_src, [(l, b) for b, _ in wl.src_req for l in range(L)]) \
-        if layers_src else None
-    dst_raw = K.RawItems(layers_dst, [(l, b) for b, _ in wl.dst_req for l in range(L)]) \
-        if layers_dst else None
-    nbytes = (src_raw or dst_raw).flat_bytes
-    slot_bytes = ((nbytes + 255) // 256) * 256
-    if world == 1:
-        flat = torch.empty(nbytes, dtype=torch.uint8, device=device)
-
-        def step(s):
-            K.paged_raw(src_raw, flat.data_ptr(), True)
-            K.paged_raw(dst_raw, flat.data_ptr(), False)
-        launches = 2
-        transport = "local"
-    else:
-        import torch.distributed as dist
-        from kvserve_hpdps_b200.parallel.p2p import DeviceRegion, PeerMapping
-        peer = rank + pairs if role == "producer" else rank - pairs
-        region = DeviceRegion(local, 2 * slot_bytes + 4096) if role == "consumer" else \
-            DeviceRegion(local, 4096)
-        handles = [None] * world
-        dist.all_gather_object(handles, (region.ipc_handle(), region.nbytes, local))
-        ph, pn, _ = handles[peer]
-        peer_map = PeerMapping(local, ph, pn)
-
-        def step(s):
-            slot = s % 2
-            if role == "producer":
-                if s >= 2:
-                    K.wait_flag(region.ptr + 256 * slot, s - 1, device, timeout_s=20.0)
-                K.paged_raw(src_raw, peer_map.ptr + slot * slot_bytes, True,
-                            flag_ptr=peer_map.ptr + 2 * slot_bytes + 256 * slot, flag_value=s + 1)
-            else:
-                K.wait_flag(region.ptr + 2 * slot_bytes + 256 * slot, s + 1, device,
-                            timeout_s=20.0)
-                K.paged_raw(dst_raw, region.ptr + slot * slot_bytes, False)
-                K.set_flag(peer_map.ptr + 256 * slot, s + 1, device)
-        launches = 2 if role == "producer" else 3
-        transport = "nvlink-p2p (one gather launch stores raw blocks into the consumer's slot)"
-
-    ms, clocks, _, err = _timed(step, args, world, local, device, 0)
-    error = None
-    if role in ("both", "consumer"):
-        ref = wl if wl.src is not None else Workload(args, device, args.seed + 101 * pair_id,
-                                                     "producer")
-        idx_s = torch.tensor(ref.src_req[0][0], device=device)
-        idx_d = torch.tensor(wl.dst_req[0][0], device=device)
-        error = {"exact": bool(torch.equal(ref.src[:, :, idx_s], wl.dst[:, :, idx_d]))}
-        del ref
-    if world > 1:
-        import torch.distributed as dist
-        gathered = [None] * world
-        dist.all_gather_object(gathered, error)
-        error = next((g for g in gathered if g is not None), None)
-        barrier(world)
-        peer_map.close()
-        barrier(world)
-        region.close()
-    return {"ms": ms, "cr": 1.0, "error": error, "transport": transport,
-            "launches": launches * args.steps, "clocks": clocks, "e2e": None,
-            "device_error": err, "pairs": pairs, "role": role}
-
-
-def run_ours(args, rank, world, local):
-    if getattr(args, "compression", "default") == "off":
-        return run_ours_raw(args, rank, world, local)
-    from kvserve_hpdps_b200.compression.fused_manager import FusedCompressionManager
-    from kvserve_hpdps_b200.ops import kernels as K
-    device = torch.device("cuda", local)
-    cfg = quant_config(args)
-    engine = 1 if args.engine == "simt" else 0
-    mgr = FusedCompressionManager(args.kv_heads, 128, cfg["quantizer_config"], cfg["codec_config"],
-                                  engine=engine)
-    pairs = max(1, world // 2)
-    if world == 1:
-        role = "both"
-    else:
-        if world % 2:
-            raise SystemExit("--gpus must be 1 or even")
-        role = "producer" if rank < pairs else "consumer"
-    pair_id = rank % pairs
-    wl = Workload(args, device, args.seed + 101 * pair_id, role)
-    L = args.layers
-    plans = [mgr.plan(l) for l in range(L)]
-    src_slots = K.LayerSlots([wl.src[l] for l in range(L)], plans) if wl.src is not None else None
-    dst_slots = K.LayerSlots([wl.dst[l] for l in range(L)], plans) if wl.dst is not None else None
-    any_slots = src_slots or dst_slots
-    src_items = K.WorkItems(any_slots, [(l, b, n) for l in range(L) for b, n in wl.src_req])
-    dst_items = K.WorkItems(any_slots if dst_slots is None else dst_slots,
-                            [(l, b, n) for l in range(L) for b, n in wl.dst_req])
-    code_bytes = src_items.code_bytes
-    meta_bytes = src_items.meta_bytes
-    codes = torch.empty(code_bytes, dtype=torch.uint8, device=device)
-    meta = torch.empty(meta_bytes, dtype=torch.uint8, device=device)
-    cap = K.rans_max_bytes(code_bytes) if mgr.stream_codec == "rans" else code_bytes
-    slot_bytes = ((cap + meta_bytes + 255) // 256) * 256
-    dec_codes = torch.empty(code_bytes, dtype=torch.uint8, device=device)
-    launches_per_step = 0
-    use_rans = mgr.stream_codec == "rans"
-
-    if world == 1:
-        stream_buf = torch.empty(cap, dtype=torch.uint8, device=device)
-
-        def step(s):
-            K.quantize(src_slots, src_items, codes, meta, engine=engine)
-            if use_rans:
-                K.rans_encode_ptr(codes.data_ptr(), code_bytes, stream_buf.data_ptr(), device)
-                K.rans_decode_ptr(stream_buf.data_ptr(), code_bytes, dec_codes.data_ptr(), device,
-                                  stream_bytes=cap)
-                K.dequantize(dec_codes, meta, dst_slots, dst_items, engine=engine)
-            else:
-                K.dequantize(codes, meta, dst_slots, dst_items, engine=engine)
-        launches_per_step = 3 + (5 if use_rans else 1)
-        transport = "local"
-    else:
-        import torch.distributed as dist
-        from kvserve_hpdps_b200.parallel.p2p import DeviceRegion, PeerMapping
-        peer = rank + pairs if role == "producer" else rank - pairs
-        # consumer: 2 receive slots (stream + meta) + ready flags; producer: credit flags
-        region = DeviceRegion(local, 2 * slot_bytes + 4096) if role == "consumer" else \
-            DeviceRegion(local, 4096)
-        handles = [None] * world
-        dist.all_gather_object(handles, (region.ipc_handle(), region.nbytes, local))
-        ph, pn, pdev = handles[peer]
-        peer_map = PeerMapping(local, ph, pn)
-        flags_off = 2 * slot_bytes if role == "consumer" else 0
-
-        def step(s):
-            slot = s % 2
-            if role == "producer":
-                if s >= 2:  # receive slot reused: wait for the consumer's credit
-                    K.wait_flag(region.ptr + 256 * slot, s - 1, device, timeout_s=20.0)
-                K.quantize(src_slots, src_items, codes, meta, engine=engine)
-                dst = peer_map.ptr + slot * slot_bytes
-                K.copy_bytes(meta.data_ptr(), dst + cap, meta_bytes, device)
-                flag = peer_map.ptr + 2 * slot_bytes + 256 * slot
-                if use_rans:
-                    K.rans_encode_ptr(codes.data_ptr(), code_bytes, dst, device, flag_ptr=flag,
-                                      flag_value=s + 1)
-                else:
-                    K.copy_bytes(codes.data_ptr(), dst, code_bytes, device, flag_ptr=flag,
-                                 flag_value=s + 1)
-            else:
-                base = region.ptr + slot * slot_bytes
-                K.wait_flag(region.ptr + flags_off + 256 * slot, s + 1, device, timeout_s=20.0)
-                K.copy_bytes(base + cap, meta.data_ptr(), meta_bytes, device)
-                if use_rans:
-                    K.rans_decode_ptr(base, code_bytes, dec_codes.data_ptr(), device,
-                                      stream_bytes=cap)
-                    K.dequantize(dec_codes, meta, dst_slots, dst_items, engine=engine)
-                else:
-                    K.copy_bytes(base, dec_codes.data_ptr(), code_bytes, device)
-                    K.dequantize(dec_codes, meta, dst_slots, dst_items, engine=engine)
-                K.set_flag(peer_map.ptr + 256 * slot, s + 1, device)
-        launches_per_step = (1 + 3 + 1 + 3) if role == "producer" else (1 + 1 + 2 + 1)
-        transport = "nvlink-p2p (producer kernels store into the consumer's IPC receive slots)"
-
-    # ---------------- warmup + correctness/CR sample (untimed)
-    s_global = 0
-    for _ in range(args.warmup):
-        step(s_global)
-        s_global += 1
-    torch.cuda.synchronize(device)
-    err = K.read_device_error(device)
-    if err:
-        raise RuntimeError(f"device error {err} during warmup ({K.ERR_NAMES.get(err)})")
-    stats = {}
-    if role in ("both", "producer"):
-        if use_rans:
-            probe_buf = torch.empty(cap, dtype=torch.uint8, device=device)
-            sz = K.rans_encode(codes, out=probe_buf, trim=True).numel()
-        else:
-            sz = code_bytes
-        stats["stream_bytes"] = sz + meta_bytes
-    if role in ("both", "consumer"):
-        # a pair's consumer regenerates its producer's (deterministic) source
-        ref_wl = wl if wl.src is not None else Workload(args, device, args.seed + 101 * pair_id,
-                                                          "producer")
-        idx_s = torch.tensor(ref_wl.src_req[0][0], device=device)
-        idx_d = torch.tensor(wl.dst_req[0][0], device=device)
-        stats["error"] = K.kv_error(ref_wl.src[:, :, idx_s], wl.dst[:, :, idx_d])
-        if ref_wl is not wl:
-            del ref_wl
-
-    # ---------------- timed region
-    sampler = ClockSampler(range(world)) if local == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize(device)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(args.steps):
-        step(s_global)
-        s_global += 1
-    ev1.record()
-    torch.cuda.synchronize(device)
-    barrier(world)
-    ms = ev0.elapsed_time(ev1)
-    err = K.read_device_error(device)
-    clocks = sampler.stop() if sampler else None
-    ms_max = allreduce_max(ms, world)
-    err_any = allreduce_max(float(err), world)
-
-    # ---------------- end-to-end through the public API
-    e2e = None
-    if not args.no_e2e:
-        e2e = run_e2e_ours(args, mgr, wl, role, world, rank, pairs, device)
-
-    # aggregate compression stats; reconstruction error from a consumer rank
-    if world > 1:
-        import torch.distributed as dist
-        gathered = [None] * world
-        dist.all_gather_object(gathered, stats.get("error"))
-        stats["error"] = next((g for g in gathered if g is not None), None)
-        barrier(world)  # unmap the peer slot before its owner frees it
-        peer_map.close()
-        barrier(world)
-        region.close()
-    stream_bytes = allreduce_sum(float(stats.get("stream_bytes", 0)), world)
-    n_prod = pairs if world > 1 else 1
-    orig = wl.bf16_bytes_per_request * wl.B * n_prod
-    cr = orig / stream_bytes if stream_bytes else None
-    out = {
-        "ms": ms_max, "cr": cr, "error": stats.get("error"), "transport": transport,
-        "launches": launches_per_step * args.steps, "clocks": clocks, "e2e": e2e,
-        "device_error": int(err_any), "pairs": n_prod, "role": role,
-    }
-    return out
-
-
-def run_e2e_ours(args, mgr, wl, role, world, rank, pairs, device):
-    """End to end through the public manager API.
-
-    Every step copies the step's request descriptors (block tables, token
-    counts) from pinned host memory to the device, compresses the requests'
-    KV into one wire message (``compress_paged_requests``, which reads the
-    stream size back to the host), and decompresses it into the consumer's
-    paged cache (``decompress_paged_requests``), then reads the device error
-    word back.  With N >= 2 the message travels by NCCL send/recv between the
-    pair (public wire envelope path)."""
-    from kvserve_hpdps_b200.ops import kernels as K
-    L = wl.L
-    h2d = d2h = 0
-    steps = max(2, min(args.steps, 10))
-
-    def one():
-        nonlocal h2d, d2h
-        if role == "both":
-            cd = mgr.compress_paged_requests([wl.src[l] for l in range(L)], list(range(L)),
-                                             wl.src_req, trim=False)
-            mgr.decompress_paged_requests(cd, [wl.dst[l] for l in range(L)], wl.dst_req)
-            return
-        raise NotImplementedError
-
-    if world > 1:
-        return run_e2e_pairs(args, mgr, wl, role, world, rank, pairs, device)
-    for _ in range(2):
-        one()
-    torch.cuda.synchronize(device)
-    K.reset_transfer_counters()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(steps):
-        one()
-        K.read_device_error(device)
-    ev1.record()
-    torch.cuda.synchronize(device)
-    ms = ev0.elapsed_time(ev1)
-    c = K.transfer_counters()
-    return {"value": ms / (steps * wl.B), "unit": "ms/request",
-            "h2d_bytes_per_step": c["h2d"] // steps, "d2h_bytes_per_step": c["d2h"] // steps + 4,
-            "steps": steps}
-
-
 def side_port(offset, pair_id):
     return int(os.environ.get("MASTER_PORT", "29500")) + offset + pair_id
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _timed_loop(step, s0: int, steps: int, world: int, device, sampler=None):
+    """``steps`` steps between a barrier + device synchronisation on both
+    sides, timed with CUDA events on the current stream; returns (max ms
+    over ranks, next step index)."""
+    barrier(world)
+    torch.cuda.synchronize(device)
+    ev0, ev1 = _events()
+    ev0.record()
+    s = s0
+    for _ in range(steps):
+        step(s)
+        s += 1
+    ev1.record()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    return allreduce_max(ev0.elapsed_time(ev1), world), s
 
 
 def _poll_message(tr, pending, key, timeout_s):
@@ -576,103 +328,594 @@ def _poll_message(tr, pending, key, timeout_s):
             break
         if time.monotonic() > deadline:
             raise TimeoutError(f"message {key} did not arrive within {timeout_s} s")
-        time.sleep(2e-5)
+        waiter = getattr(tr, "wait_received", None)
+        if waiter is not None:
+            waiter(0.0005)
+        else:
+            time.sleep(2e-5)
     return pending[key].pop(0)
 
 
-def run_e2e_pairs(args, mgr, wl, role, world, rank, pairs, device):
-    """End to end through the public API on producer/consumer pairs: the
-    producer compresses the step's requests into one grouped message
-    (``compress_paged_requests``), builds the wire envelope and hands it to
-    the NVLink ring transport (``P2PTransport.send_bundle``: ZMQ header,
-    device stores into the consumer's receive ring); the consumer drains the
-    transport, waits on the ring flag, restores the envelope and decodes into
-    its paged cache (``decompress_paged_requests``), then reads the device
-    error word back.  Block tables go host -> device every step."""
-    from kvserve_hpdps_b200.compression.manager import add_sentinel
-    from kvserve_hpdps_b200.compression.wire import CompressedWire, build_wire, restore_from_wire
+# ------------------------------------------------------------------ ours
+def make_manager(args, codec):
+    from kvserve_hpdps_b200.compression.fused_manager import FusedCompressionManager
+    cfg = quant_config(args, codec)
+    engine = 1 if args.engine == "simt" else 0
+    return FusedCompressionManager(args.kv_heads, 128, cfg["quantizer_config"],
+                                   cfg["codec_config"], base_seed=HADAMARD_SEED, engine=engine)
+
+
+def run_ours_raw(args, rank, world, local, wl):
+    """Compression off: raw KV blocks.  N = 1: one gather launch of every
+    (layer, request) item from the paged cache into a flat buffer and one
+    scatter launch into the second cache.  N >= 2: through the ring
+    transport's ``send_paged`` (one gather launch storing straight into the
+    consumer's ring, checksum and ready flag included); the consumer scatters
+    with one launch."""
     from kvserve_hpdps_b200.ops import kernels as K
-    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport
-    L = wl.L
+    device = torch.device("cuda", local)
+    role, pairs = _roles(world, rank)
     pair_id = rank % pairs
-    tr = P2PTransport(role == "producer", "127.0.0.1", side_port(600, pair_id), device.index,
-                      0, ring_bytes=int(os.environ.get("KVSERVE_RING_BYTES", str(2 << 30))))
+    L = args.layers
+    if world == 1:
+        src_raw = K.RawItems(wl.src_layers(), [(l, b) for b, _ in wl.src_req for l in range(L)])
+        dst_raw = K.RawItems(wl.dst_layers(), [(l, b) for b, _ in wl.dst_req for l in range(L)])
+        flat = torch.empty(src_raw.flat_bytes, dtype=torch.uint8, device=device)
+
+        def step(s):
+            K.paged_raw(src_raw, flat.data_ptr(), True)
+            K.paged_raw(dst_raw, flat.data_ptr(), False)
+        launches, transport = 2, "local"
+    else:
+        tr = _open_transport(args, role, pair_id, device, wl.bf16_bytes_per_request * wl.B)
+        names = [f"model.layers.{l}.self_attn.attn" for l in range(L)]
+        pending: dict = {}
+        blocks_all = [b for blocks, _ in wl.src_req for b in blocks]
+        dst_all = [b for blocks, _ in wl.dst_req for b in blocks] if wl.dst is not None else None
+
+        def step(s):
+            if role == "producer":
+                tr.send_paged(f"s{s}", names, wl.src_layers(), blocks_all)
+            else:
+                _, payload = _poll_message(tr, pending, f"s{s}", 60.0)
+                tr.prepare(payload, device)
+                dst_raw = K.RawItems(wl.dst_layers(), [(l, dst_all) for l in range(L)])
+                K.paged_raw(dst_raw, payload["tensor"].data_ptr(), False)
+                tr.release(payload, device)
+        launches = 1 if role == "producer" else 4
+        transport = "nvlink-p2p ring (P2PTransport.send_paged: one gather launch stores raw " \
+                    "blocks into the consumer's ring)"
+    s = 0
+    for _ in range(args.warmup):
+        step(s)
+        s += 1
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler(range(world)) if local == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ms, s = _timed_loop(step, s, args.steps, world, device)
+    clocks = sampler.stop() if sampler else None
+    err = int(allreduce_max(float(K.read_device_error(device)), world))
+    error = None
+    if role in ("both", "consumer"):
+        ref = wl if wl.src is not None else Workload(args, device, args.seed + 101 * pair_id,
+                                                     "producer")
+        idx_s = torch.tensor(ref.src_req[0][0], device=device)
+        idx_d = torch.tensor(wl.dst_req[0][0], device=device)
+        error = {"exact": bool(torch.equal(ref.src[:, :, idx_s], wl.dst[:, :, idx_d]))}
+        del ref
+    error = first_non_none(error, world)
+    if world > 1:
+        if role == "producer":
+            tr.wait_for_sent(60.0)
+        barrier(world)
+        tr.close()
+    return {"ms": ms, "cr": 1.0, "error": error, "transport": transport,
+            "launches": launches * args.steps, "clocks": clocks, "device_error": err,
+            "pairs": pairs, "role": role}
+
+
+def _open_transport(args, role, pair_id, device, message_bytes: int):
+    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport
+    ring = int(os.environ.get("KVSERVE_RING_BYTES", str(max(2 << 30, int(3.2 * message_bytes)))))
+    return P2PTransport(role == "producer", "127.0.0.1", side_port(600, pair_id), device.index, 0,
+                        ring_bytes=ring, n_flags=256)
+
+
+def run_path(args, mgr, wl, rank, world, local, e2e: bool, latency: bool, clocks: bool):
+    """Time one codec path of this framework (headline or full path)."""
+    listener = _SizeListener()
+    from kvserve_hpdps_b200.ops import kernels as K
+    device = torch.device("cuda", local)
+    role, pairs = _roles(world, rank)
+    pair_id = rank % pairs
+    L = args.layers
+    engine = mgr.engine
+    use_rans = mgr.stream_codec == "rans"
+    plans = [mgr.plan(l) for l in range(L)]
+    out = {"pairs": pairs, "role": role}
+    sampler = None
+    if world == 1:
+        src_slots = K.LayerSlots(wl.src_layers(), plans)
+        dst_slots = K.LayerSlots(wl.dst_layers(), plans)
+        src_items = K.WorkItems(src_slots, [(l, b, n) for l in range(L) for b, n in wl.src_req])
+        dst_items = K.WorkItems(dst_slots, [(l, b, n) for l in range(L) for b, n in wl.dst_req])
+        code_bytes, meta_bytes = src_items.code_bytes, src_items.meta_bytes
+        codes = torch.empty(code_bytes, dtype=torch.uint8, device=device)
+        meta = torch.empty(meta_bytes, dtype=torch.uint8, device=device)
+        cap = K.rans_max_bytes(code_bytes) if use_rans else code_bytes
+        stream_buf = torch.empty(cap, dtype=torch.uint8, device=device) if use_rans else None
+        dec_codes = torch.empty(code_bytes, dtype=torch.uint8, device=device) if use_rans else codes
+
+        def compress(s):
+            K.quantize(src_slots, src_items, codes, meta, engine=engine)
+            if use_rans:
+                K.rans_encode_ptr(codes.data_ptr(), code_bytes, stream_buf.data_ptr(), device)
+
+        def decompress(s):
+            if use_rans:
+                K.rans_decode_ptr(stream_buf.data_ptr(), code_bytes, dec_codes.data_ptr(), device,
+                                  stream_bytes=cap)
+            K.dequantize(dec_codes, meta, dst_slots, dst_items, engine=engine)
+
+        def step(s):
+            compress(s)
+            decompress(s)
+        launches = 4 + (4 if use_rans else 0) + 1
+        out["transport"] = "local"
+        s = 0
+        for _ in range(args.warmup):
+            step(s)
+            s += 1
+        torch.cuda.synchronize(device)
+        K.check_device_error(device, "warm-up")
+        if use_rans:
+            stream_bytes = K.rans_encode(codes, out=torch.empty_like(stream_buf)).numel() + 16
+        else:
+            stream_bytes = code_bytes
+        out["wire_bytes_per_step"] = stream_bytes + meta_bytes
+        out["error"] = K.kv_error(wl.src[:, :, torch.tensor(wl.src_req[0][0], device=device)],
+                                  wl.dst[:, :, torch.tensor(wl.dst_req[0][0], device=device)])
+        if clocks:
+            sampler = ClockSampler([local])
+            sampler.start()
+            time.sleep(0.3)
+        out["ms"], s = _timed_loop(step, s, args.steps, world, device)
+        if sampler:
+            out["clocks"] = sampler.stop()
+        out["launches"] = launches * args.steps
+        ms_c, s = _timed_loop(compress, s, args.steps, world, device)
+        ms_d, s = _timed_loop(decompress, s, args.steps, world, device)
+        n = args.steps * wl.B
+        out["stage_ms_per_request"] = {"compress": round(ms_c / n, 5),
+                                       "decompress": round(ms_d / n, 5)}
+        out["device_error"] = K.read_device_error(device)
+        if e2e:
+            out["e2e"] = _e2e_local(args, mgr, wl, device)
+        return out
+
+    # ---------------- N >= 2: producer/consumer pairs over the ring transport
+    from kvserve_hpdps_b200.compression.manager import add_sentinel
+    from kvserve_hpdps_b200.compression.wire import CompressedWire, restore_from_wire
+    from kvserve_hpdps_b200.parallel.p2p import DeviceRegion, PeerMapping
+    tr = _open_transport(args, role, pair_id, device, wl.bf16_bytes_per_request * wl.B)
+    if role == "producer":  # exact bytes on the link of each sent message
+        tr.add_sent_listener(listener)
     names = add_sentinel([f"model.layers.{l}.self_attn.attn" for l in range(L)])
     pending: dict = {}
+    # producer-owned release flags, written by its consumer (single-request latency)
+    region = DeviceRegion(local, 4096)
+    handles = [None] * world
+    import torch.distributed as dist
+    dist.all_gather_object(handles, (region.ipc_handle(), region.nbytes))
+    peer = rank + pairs if role == "producer" else rank - pairs
+    peer_map = PeerMapping(local, handles[peer][0], handles[peer][1])
+    sizes = []
+
+    def produce(s, reqs, tids):
+        info = mgr.send_paged_requests(tr, f"s{s}", names, wl.src_layers(), list(range(L)), reqs,
+                                       member_tids=tids)
+        sizes.append(info["wire_nbytes"])
+
+    def consume(s, reqs):
+        _, payload = _poll_message(tr, pending, f"s{s}", 60.0)
+        tr.prepare(payload, device)
+        cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
+                                              payload["aux_tensors"]))
+        mgr.decompress_paged_requests(cd, wl.dst_layers(), reqs)
+        tr.release(payload, device)
+
+    def step(s):
+        if role == "producer":
+            produce(s, wl.src_req, [f"{s}:{r}" for r in range(wl.B)])
+        else:
+            consume(s, wl.dst_req)
+    out["transport"] = ("nvlink-p2p ring: FusedCompressionManager.send_paged_requests -> "
+                        "P2PTransport.open_message/commit_message; quantize "
+                        + ("-> rANS compaction kernel" if use_rans else "kernel")
+                        + " stores into the consumer's ring, last CTA publishes the flag")
+    s = 0
+    for _ in range(args.warmup):
+        step(s)
+        s += 1
+    if role == "producer":
+        tr.wait_for_sent(120.0)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    err = K.read_device_error(device)
+    if err:
+        raise RuntimeError(f"device error {err} during warm-up ({K.ERR_NAMES.get(err)})")
+    error = None
+    if role == "consumer":
+        ref = Workload(args, device, args.seed + 101 * pair_id, "producer")
+        error = K.kv_error(ref.src[:, :, torch.tensor(ref.src_req[0][0], device=device)],
+                           wl.dst[:, :, torch.tensor(wl.dst_req[0][0], device=device)])
+        del ref
+        torch.cuda.empty_cache()
+    out["error"] = first_non_none(error, world)
+    if clocks and local == 0:
+        sampler = ClockSampler(range(world))
+        sampler.start()
+        time.sleep(0.3)
+
+    def timed_step(s):
+        step(s)
+    out["ms"], s = _timed_loop(timed_step, s, args.steps, world, device)
+    if sampler:
+        out["clocks"] = sampler.stop()
+    if role == "producer":
+        tr.wait_for_sent(120.0)
+    # wire bytes: the exact coded sizes come back through the transport's listeners
+    launches = (7 + (4 if use_rans else 0)) if role == "producer" else 6
+    out["launches"] = launches * args.steps
+    out["device_error"] = int(allreduce_max(float(K.read_device_error(device)), world))
+
+    if latency and args.latency_reps > 0:
+        lat = []
+        for i in range(args.latency_reps):
+            tag = 1000 + i
+            barrier(world)
+            torch.cuda.synchronize(device)
+            if role == "producer":
+                ev0, ev1 = _events()
+                ev0.record()
+                produce(f"lat{i}", wl.src_req[:1], [f"lat{i}"])
+                K.wait_flag(region.ptr, tag, device, timeout_s=20.0)
+                ev1.record()
+                torch.cuda.synchronize(device)
+                lat.append(ev0.elapsed_time(ev1))
+            else:
+                consume(f"lat{i}", wl.dst_req[:1])
+                K.set_flag(peer_map.ptr, tag, device)
+                torch.cuda.synchronize(device)
+        med = statistics.median(lat) if lat else 0.0
+        out["single_request_latency_ms"] = round(allreduce_max(med, world), 4)
+        if K.read_device_error(device):
+            raise RuntimeError("device error during the latency probe")
+    if e2e:
+        out["e2e"] = _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending)
+    if role == "producer":
+        tr.wait_for_sent(120.0)
+    out["wire_bytes_per_step"] = statistics.median(listener.sizes) if listener.sizes else None
+    out["ring_reserved_bytes_per_step"] = statistics.median(sizes) if sizes else None
+    barrier(world)
+    tr.close()
+    peer_map.close()
+    barrier(world)
+    region.close()
+    return out
+
+
+def _e2e_local(args, mgr, wl, device):
+    """N = 1 through the public manager API: every step builds the request
+    descriptors on the host and copies them host->device from pinned memory
+    (inside compress/decompress_paged_requests), compresses into one wire
+    message and decodes it into the consumer cache, then reads the device
+    error word back (the step's result)."""
+    from kvserve_hpdps_b200.ops import kernels as K
+    L = wl.L
+    steps = max(2, min(args.steps, 10))
+
+    def one():
+        cd = mgr.compress_paged_requests(wl.src_layers(), list(range(L)), wl.src_req, trim=False)
+        mgr.decompress_paged_requests(cd, wl.dst_layers(), wl.dst_req)
+        K.read_device_error(device)
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize(device)
+    K.reset_transfer_counters()
+    ev0, ev1 = _events()
+    ev0.record()
+    for _ in range(steps):
+        one()
+    ev1.record()
+    torch.cuda.synchronize(device)
+    c = K.transfer_counters()
+    return {"value": round(ev0.elapsed_time(ev1) / (steps * wl.B), 5), "unit": "ms/request",
+            "h2d_bytes_per_step": c["h2d"] // steps, "d2h_bytes_per_step": c["d2h"] // steps,
+            "steps": steps,
+            "path": "compress_paged_requests -> decompress_paged_requests, error word read"}
+
+
+def _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending):
+    """N >= 2 through the public API, as the connector drives it: the
+    producer's ``send_paged_requests`` (descriptors host->device from pinned
+    memory, kernels storing into the consumer's ring), the consumer's drain
+    -> ``prepare`` (bounded flag wait, checksum) -> ``restore_from_wire`` ->
+    ``decompress_paged_requests``; every step both ranks read their device
+    error word back."""
+    from kvserve_hpdps_b200.compression.wire import CompressedWire, restore_from_wire
+    from kvserve_hpdps_b200.ops import kernels as K
+    L = wl.L
     steps = max(2, min(args.steps, 10))
 
     def one(s):
         if role == "producer":
-            cd = mgr.compress_paged_requests([wl.src[l] for l in range(L)], list(range(L)),
-                                             wl.src_req, member_tids=[f"{s}:{r}" for r in range(wl.B)],
-                                             trim=False)
-            w = build_wire(cd)
-            tr.send_bundle(f"s{s}", names, w.meta, w.body_chunks, w.aux_tensors)
+            mgr.send_paged_requests(tr, f"e{s}", names, wl.src_layers(), list(range(L)),
+                                    wl.src_req, member_tids=[f"e{s}:{r}" for r in range(wl.B)])
         else:
-            _, payload = _poll_message(tr, pending, f"s{s}", 60.0)
+            _, payload = _poll_message(tr, pending, f"e{s}", 60.0)
             tr.prepare(payload, device)
             cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
                                                   payload["aux_tensors"]))
-            mgr.decompress_paged_requests(cd, [wl.dst[l] for l in range(L)], wl.dst_req)
+            mgr.decompress_paged_requests(cd, wl.dst_layers(), wl.dst_req)
             tr.release(payload, device)
-            K.read_device_error(device)
-
+        K.read_device_error(device)
     s = 0
     for _ in range(2):
         one(s)
         s += 1
     if role == "producer":
-        tr.wait_for_sent(60.0)
+        tr.wait_for_sent(120.0)
     torch.cuda.synchronize(device)
     barrier(world)
     K.reset_transfer_counters()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0, ev1 = _events()
     ev0.record()
     for _ in range(steps):
         one(s)
         s += 1
-    if role == "producer":
-        if not tr.wait_for_sent(60.0):
-            raise TimeoutError("sends did not complete")
-    torch.cuda.synchronize(device)
+    if role == "producer" and not tr.wait_for_sent(120.0):
+        raise TimeoutError("sends did not complete")
     ev1.record()
     torch.cuda.synchronize(device)
     ms = allreduce_max(ev0.elapsed_time(ev1), world)
     c = K.transfer_counters()
-    h2d = allreduce_sum(float(c["h2d"]), world) / steps
-    d2h = allreduce_sum(float(c["d2h"] + (4 * steps if role == "consumer" else 0)), world) / steps
-    barrier(world)
-    tr.close()
-    return {"value": ms / (steps * wl.B * pairs), "unit": "ms/request",
+    h2d = allreduce_sum(float(c["h2d"]), world) / (steps * pairs)
+    d2h = allreduce_sum(float(c["d2h"]), world) / (steps * pairs)
+    return {"value": round(ms / (steps * wl.B), 5), "unit": "ms/request",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
-            "path": "compress_paged_requests -> build_wire -> P2PTransport.send_bundle -> "
-                    "drain_received/prepare -> restore_from_wire -> decompress_paged_requests"}
+            "path": "send_paged_requests -> P2PTransport ring -> drain_received/prepare -> "
+                    "restore_from_wire -> decompress_paged_requests, error word read per step"}
+
+
+class _SizeListener:
+    """Exact coded bytes of each sent message (the transport's completion thread)."""
+
+    def __init__(self):
+        self.sizes = []
+
+    def __call__(self, request_id, tids, ms, nbytes=None):
+        if nbytes is not None and not str(request_id).startswith(("lat", "e")):
+            self.sizes.append(int(nbytes))
+
+
+def run_ours(args, rank, world, local):
+    device = torch.device("cuda", local)
+    role, pairs = _roles(world, rank)
+    pair_id = rank % pairs
+    wl = Workload(args, device, args.seed + 101 * pair_id, role)
+    if args.compression == "off":
+        return run_ours_raw(args, rank, world, local, wl)
+    paths = [(args.codec, True)]
+    if not args.no_full_path and args.codec != "rans":
+        paths.append(("rans", False))
+    results = []
+    for codec, headline in paths:
+        mgr = make_manager(args, codec)
+        res = run_path(args, mgr, wl, rank, world, local, e2e=not args.no_e2e,
+                       latency=world > 1, clocks=headline)
+        torch.cuda.synchronize(device)
+        results.append((codec, res))
+        torch.cuda.empty_cache()
+    head = results[0][1]
+    head["codec"] = results[0][0]
+    for codec, res in results[1:]:
+        head["full_path"] = _summary(args, wl, res, world, codec)
+    head["cr"] = _cr(args, wl, head, world)
+    head["launches_total"] = head["launches"] + sum(r["launches"] for _, r in results[1:])
+    return head
+
+
+def _cr(args, wl, res, world):
+    """Whole-job compression ratio: raw bytes over the bytes on the wire."""
+    b = res.get("wire_bytes_per_step")
+    tot = allreduce_sum(float(b or 0), world) if world > 1 else float(b or 0)
+    n_prod = res["pairs"] if world > 1 else 1
+    orig = wl.bf16_bytes_per_request * wl.B * n_prod
+    return orig / tot if tot else None
+
+
+def _summary(args, wl, res, world, codec):
+    ms = res["ms"] / (args.steps * wl.B)
+    out = {"compression": compression_label(args, codec), "value": round(ms, 5),
+           "unit": "ms/request", "compression_ratio": None,
+           "reconstruction": res.get("error"), "launches": res["launches"]}
+    cr = _cr(args, wl, res, world)
+    out["compression_ratio"] = round(cr, 3) if cr else None
+    for k in ("e2e", "stage_ms_per_request", "single_request_latency_ms"):
+        if res.get(k) is not None:
+            out[k] = res[k]
+    return out
 
 
 # ------------------------------------------------------------------ reference
 _REF_TRANSPORTS: dict = {}
 
 
-def _ref_compressed_bytes(c) -> int:
-    """Compressed body bytes of the reference's CompressedKVData (a single
-    tensor, or chunks above its 500 MiB chunking threshold)."""
-    if getattr(c, "is_chunked", False) and c.chunks:
-        return int(sum(t.numel() * t.element_size() for t in c.chunks))
-    if c.compressed_tensor is not None:
-        return int(c.compressed_tensor.numel() * c.compressed_tensor.element_size())
-    return int(c.compressed_size)
+def _ref_imports():
+    """Put the reference install and the fast_hadamard_transform stand-in on
+    sys.path; nothing of this repository's package is imported on this arm."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    standin = os.path.join(ROOT, "baseline", "standin")
+    for p in (standin, ref_root):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+class _RefPipeline:
+    """The reference's fused op driven as its TileLang manager does
+    (kvserve_v1/compression/tilelang_manager.py:158-216 and :353-385), with
+    the codec stage left out: per layer ``compress_v3`` then the heads-outer
+    permute and ``_canon_meta``; on the way back ``_decanon_meta``, the
+    inverse permute and ``decompress_v3`` per layer."""
+
+    def __init__(self, args):
+        from kvserve_v1.compression.compression_manager import CompressedKVData
+        from kvserve_v1.compression.tilelang_manager import _canon_meta, _decanon_meta
+        from kvserve_v1.tilelang_ops.kv_hadamard_quant import KVHadamardQuantOp
+        qc = {"model_name": MODEL, "hybrid_ratio": hybrid_ratio(args), "high_key_max_value": 12,
+              "high_value_max_value": 8, "low_key_max_value": 6, "low_value_max_value": 4}
+        self.op = KVHadamardQuantOp(num_heads=args.kv_heads, head_dim=128, base_seed=HADAMARD_SEED,
+                                    dtype=torch.bfloat16, quant_type="minmax",
+                                    axis_key="channel", axis_value="token", split_type="head",
+                                    **qc)
+        self.CompressedKVData = CompressedKVData
+        self._canon, self._decanon = _canon_meta, _decanon_meta
+
+    def compress(self, stacked: torch.Tensor, request_id: str):
+        L = stacked.shape[0]
+        q_layers, qparams = [], []
+        for l in range(L):
+            q, m = self.op.compress_v3(stacked[l].contiguous(), layer_id=l)
+            q_layers.append(q.permute(0, 3, 1, 2, 4).contiguous())
+            qparams.append(self._canon(m))
+        buffer = torch.stack(q_layers, dim=0).contiguous()
+        meta = {"request_id": request_id, "num_layers": L, "codec_applied": False,
+                "codec_shape": list(buffer.shape), "codec_dtype": "uint8",
+                "device": str(buffer.device), "original_dtype": "bfloat16",
+                "original_shape": list(stacked.shape), "quantization_params": qparams,
+                "backend": "tilelang_v3"}
+        return self.CompressedKVData(request_id=request_id, layer_id=L - 1,
+                                     compressed_tensor=buffer, metadata=meta,
+                                     original_size=stacked.numel() * stacked.element_size(),
+                                     compressed_size=buffer.numel() * buffer.element_size())
+
+    def decompress(self, c) -> torch.Tensor:
+        meta = c.metadata
+        buffer = c.compressed_tensor.view(torch.uint8).reshape(meta["codec_shape"])
+        outs = []
+        for l in range(int(meta["num_layers"])):
+            layer_q = buffer[l].permute(0, 2, 3, 1, 4).contiguous()
+            outs.append(self.op.decompress_v3(layer_q, self._decanon(meta["quantization_params"][l]),
+                                              layer_id=l))
+        return torch.stack(outs, dim=0)
+
+
+def _ref_error(src_wl, dst_wl, device):
+    a = src_wl.src[:, :, torch.tensor(src_wl.src_req[0][0], device=device)].float()
+    b = dst_wl.dst[:, :, torch.tensor(dst_wl.dst_req[0][0], device=device)].float()
+    return {"cosine": float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)),
+            "rel_mse": float(((a - b) ** 2).sum() / (a ** 2).sum())}
+
+
+REF_PIPELINE = ("reference KVHadamardQuantOp.compress_v3 / decompress_v3 per layer (TileLang "
+                "kernels), in its TileLang manager's order without the codec stage (nvCOMP/CuPy "
+                "and LC not installed); fast_hadamard_transform not installed: plain-PyTorch "
+                "stand-in (baseline/standin); its extract/inject block utilities")
+
+
+def run_reference(args, rank, world, local):
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "kvserve_v1")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    _ref_imports()
+    if world > 1:
+        return run_reference_pairs(args, rank, world, local)
+    from kvserve_v1.utils.kv_utils import (extract_kv_from_layer_by_blocks,  # noqa: E402
+                                           inject_kv_into_layer_by_blocks)
+    device = torch.device("cuda", local)
+    raw = args.compression == "off"
+    pipe = None if raw else _RefPipeline(args)
+    wl = Workload(args, device, args.seed)
+    L = args.layers
+    sizes = []
+
+    def extract(r):
+        return torch.stack([extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0])
+                            for l in range(L)], dim=0)
+
+    def inject(r, out):
+        for l in range(L):
+            inject_kv_into_layer_by_blocks(wl.dst[l], out[l], wl.dst_req[r][0])
+
+    def step(s):
+        for r in range(wl.B):
+            stacked = extract(r)
+            if raw:
+                sizes.append(int(stacked.numel() * stacked.element_size()))
+                out = stacked
+            else:
+                c = pipe.compress(stacked, f"r{s}_{r}")
+                sizes.append(int(c.compressed_size) + _aux_bytes(c.metadata))
+                out = pipe.decompress(c)
+            inject(r, out)
+
+    def compress_only(s):
+        for r in range(wl.B):
+            pipe.compress(extract(r), f"c{s}_{r}")
+
+    s = 0
+    for _ in range(args.warmup):
+        step(s)
+        s += 1
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler([local])
+    sampler.start()
+    time.sleep(0.3)
+    ms, s = _timed_loop(step, s, args.steps, world, device)
+    clocks = sampler.stop()
+    out = {"ms": ms, "error": _ref_error(wl, wl, device), "clocks": clocks,
+           "pipeline": "raw: extract_kv_from_layer_by_blocks + stack + "
+                       "inject_kv_into_layer_by_blocks" if raw else REF_PIPELINE,
+           "transport": "local", "pairs": 1}
+    out["cr"] = wl.bf16_bytes_per_request / statistics.mean(sizes[-args.steps * wl.B:])
+    if not raw:
+        ms_c, s = _timed_loop(compress_only, s, args.steps, world, device)
+        n = args.steps * wl.B
+        out["stage_ms_per_request"] = {"compress": round(ms_c / n, 5),
+                                       "decompress": round((ms - ms_c) / n, 5)}
+    return out
+
+
+def _aux_bytes(meta) -> int:
+    """Bytes of the tensors in a message's quantization parameters (the
+    metadata that travels next to the codes)."""
+    tot = 0
+
+    def walk(x):
+        nonlocal tot
+        if isinstance(x, torch.Tensor):
+            tot += x.numel() * x.element_size()
+        elif isinstance(x, dict):
+            for v in x.values():
+                walk(v)
+        elif isinstance(x, (list, tuple)):
+            for v in x:
+                walk(v)
+    walk(meta.get("quantization_params"))
+    return tot
 
 
 def run_reference_pairs(args, rank, world, local):
     """Reference arm on producer/consumer pairs, through the reference's own
-    public modules: its KVCompressionAdapter (quantizer pipeline), its wire
-    envelope (build_wire / restore_from_wire), its NcclTransport
-    (ZMQ PUT_BUNDLE header + ncclSend/ncclRecv on a 2-rank communicator per
-    pair) and its paged-block extract/inject utilities, in the order its
-    connector runs them in overlap mode "off"."""
-    ref_root = os.path.join(ROOT, "baseline", "_ref")
-    sys.path.insert(0, ref_root)
-    from kvserve_v1.compression.manager import KVCompressionAdapter, add_sentinel  # noqa: E402
+    public modules: the fused op pipeline above, its wire envelope
+    (build_wire / restore_from_wire), its NcclTransport (ZMQ PUT_BUNDLE header
+    + ncclSend/ncclRecv on a 2-rank communicator per pair) and its paged-block
+    extract/inject utilities, in the order its connector runs them in overlap
+    mode "off" (one message per request)."""
+    from kvserve_v1.compression.manager import add_sentinel  # noqa: E402
     from kvserve_v1.compression.wire import (CompressedWire, build_wire,  # noqa: E402
                                               restore_from_wire)
     from kvserve_v1.transport.nccl_transport import NcclTransport  # noqa: E402
@@ -684,12 +927,8 @@ def run_reference_pairs(args, rank, world, local):
     pairs = world // 2
     role = "producer" if rank < pairs else "consumer"
     pair_id = rank % pairs
-    cfg = quant_config(args)
-    spec = {"enabled": True, "pipeline": ["quantizer"],
-            "quantizer_config": dict(cfg["quantizer_config"]), "min_compress_size": 0}
-    raw = getattr(args, "compression", "default") == "off"
-    adapter = None if raw else KVCompressionAdapter(spec, num_kv_heads=args.kv_heads,
-                                                    head_size=128, model_name=MODEL)
+    raw = args.compression == "off"
+    pipe = None if raw else _RefPipeline(args)
     wl = Workload(args, device, args.seed + 101 * pair_id, role)
     L = args.layers
     plain_names = [f"model.layers.{l}.self_attn.attn" for l in range(L)]
@@ -698,10 +937,8 @@ def run_reference_pairs(args, rank, world, local):
     if tr is None:  # one communicator per pair for the life of the process
         tr = NcclTransport(role == "producer", "127.0.0.1", side_port(500, pair_id), local, 0)
         _REF_TRANSPORTS[(role, pair_id)] = tr
-    tag = getattr(args, "tag", "")
     pending: dict = {}
     sizes = []
-    fallbacks = []  # requests its adapter returned None for (sent raw)
 
     def wait_sent(timeout_s=120.0):
         t = threading.Thread(target=tr.wait_for_sent, daemon=True)
@@ -712,24 +949,17 @@ def run_reference_pairs(args, rank, world, local):
 
     def step(s):
         for r in range(wl.B):
-            key = f"{tag}s{s}r{r}"
-            if role == "producer" and raw:  # the connector's path without compression
+            key = f"s{s}r{r}"
+            if role == "producer":
                 stacked = torch.stack([extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0])
                                        for l in range(L)], dim=0)
-                sizes.append(int(stacked.numel() * stacked.element_size()))
-                tr.send(key, plain_names, stacked)
-            elif role == "producer":
-                layers = [extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0])
-                          for l in range(L)]
-                stacked = torch.stack(layers, dim=0)
-                c = adapter.compress(stacked, key)
-                if c is None:  # as its connector does: send the raw KV instead
-                    fallbacks.append(key)
+                if raw:
                     sizes.append(int(stacked.numel() * stacked.element_size()))
                     tr.send(key, plain_names, stacked)
                     continue
-                sizes.append(_ref_compressed_bytes(c))
+                c = pipe.compress(stacked, key)
                 w = build_wire(c, 512 << 20)  # the connector's default chunk bound
+                sizes.append(int(w.nbytes))
                 tr.send_bundle(key, names, w.meta, w.body_chunks, w.aux_tensors)
             else:
                 _, payload = _poll_message(tr, pending, key, 120.0)
@@ -738,7 +968,7 @@ def run_reference_pairs(args, rank, world, local):
                 else:
                     cd = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
                                                           payload["aux_tensors"]))
-                    out = adapter.decompress(cd)
+                    out = pipe.decompress(cd)
                 for l in range(L):
                     inject_kv_into_layer_by_blocks(wl.dst[l], out[l], wl.dst_req[r][0])
 
@@ -754,16 +984,19 @@ def run_reference_pairs(args, rank, world, local):
     if sampler:
         sampler.start()
         time.sleep(0.3)
+
+    def timed(s):
+        step(s)
+
     barrier(world)
     torch.cuda.synchronize(device)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0, ev1 = _events()
     ev0.record()
     for _ in range(args.steps):
-        step(s)
+        timed(s)
         s += 1
     if role == "producer":
         wait_sent()
-    torch.cuda.synchronize(device)
     ev1.record()
     torch.cuda.synchronize(device)
     ms = allreduce_max(ev0.elapsed_time(ev1), world)
@@ -772,144 +1005,26 @@ def run_reference_pairs(args, rank, world, local):
     err = None
     if role == "consumer":
         src = Workload(args, device, args.seed + 101 * pair_id, "producer")
-        a = src.src[:, :, torch.tensor(src.src_req[0][0], device=device)].float()
-        b = wl.dst[:, :, torch.tensor(wl.dst_req[0][0], device=device)].float()
-        err = {"cosine": float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)),
-               "rel_mse": float(((a - b) ** 2).sum() / (a ** 2).sum())}
+        err = _ref_error(src, wl, device)
         del src
-    import torch.distributed as dist
-    gathered = [None] * world
-    dist.all_gather_object(gathered, err)
-    err = next((g for g in gathered if g is not None), None)
-    tot = allreduce_sum(float(sum(sizes)), world)
-    n = allreduce_sum(float(len(sizes)), world)
+    err = first_non_none(err, world)
+    tot = allreduce_sum(float(sum(sizes[-args.steps * wl.B:])), world)
+    n = allreduce_sum(float(len(sizes[-args.steps * wl.B:])), world)
     cr = wl.bf16_bytes_per_request / (tot / n) if n else None
-    nfall = allreduce_sum(float(len(fallbacks)), world)
     return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "pairs": pairs,
-            "fallback_raw": int(nfall),
-            "reference_path": ("raw: extract_kv_from_layer_by_blocks + stack + "
-                               "NcclTransport.send (ncclSend/ncclRecv per pair) + "
-                               "inject_kv_into_layer_by_blocks") if raw else
-                              ("custom pipeline [quantizer] via KVCompressionAdapter + "
-                               "build_wire + NcclTransport.send_bundle (ncclSend/ncclRecv per "
-                               "pair)"),
-            "transport": "reference NcclTransport (NCCL send/recv over NVLink)"}
-
-
-def run_reference(args, rank, world, local):
-    ref_root = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "kvserve_v1")):
-        return {"unavailable": "reference not installed in baseline/_ref"}
-    if world > 1:
-        return run_reference_pairs(args, rank, world, local)
-    sys.path.insert(0, ref_root)
-    from kvserve_v1.compression.manager import KVCompressionAdapter  # noqa: E402
-    from kvserve_v1.utils.kv_utils import (extract_kv_from_layer_by_blocks,  # noqa: E402
-                                           inject_kv_into_layer_by_blocks)
-    device = torch.device("cuda", local)
-    raw = getattr(args, "compression", "default") == "off"
-    path, default_err, adapter = "raw", "", None
-    if not raw:
-        try:
-            KVCompressionAdapter("default", num_kv_heads=args.kv_heads, head_size=128,
-                                 model_name=MODEL)
-            path = "default"
-        except Exception as e:  # noqa: BLE001
-            default_err = f"{type(e).__name__}: {e}"
-            path = None
-        cfg = quant_config(args)
-        spec = {"enabled": True, "pipeline": ["quantizer"],
-                "quantizer_config": dict(cfg["quantizer_config"]), "min_compress_size": 0}
-        adapter = KVCompressionAdapter(spec if path is None else "default",
-                                       num_kv_heads=args.kv_heads, head_size=128,
-                                       model_name=MODEL)
-    wl = Workload(args, device, args.seed)
-    L = args.layers
-    sizes = []
-    fallbacks = []
-
-    def step(s):
-        for r in range(wl.B):
-            layers = [extract_kv_from_layer_by_blocks(wl.src[l], wl.src_req[r][0]) for l in range(L)]
-            stacked = torch.stack(layers, dim=0)
-            c = None if raw else adapter.compress(stacked, f"r{s}_{r}")
-            if c is None:  # compression off, or its adapter declined: raw KV
-                if not raw:
-                    fallbacks.append(r)
-                sizes.append(int(stacked.numel() * stacked.element_size()))
-                out = stacked
-            else:
-                sizes.append(_ref_compressed_bytes(c))
-                out = adapter.decompress(c)
-            for l in range(L):
-                inject_kv_into_layer_by_blocks(wl.dst[l], out[l], wl.dst_req[r][0])
-
-    for s in range(args.warmup):
-        step(s)
-    torch.cuda.synchronize(device)
-    sampler = ClockSampler([local])
-    sampler.start()
-    time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for s in range(args.steps):
-        step(1000 + s)
-    ev1.record()
-    torch.cuda.synchronize(device)
-    ms = ev0.elapsed_time(ev1)
-    clocks = sampler.stop()
-    idx_s = torch.tensor(wl.src_req[0][0], device=device)
-    idx_d = torch.tensor(wl.dst_req[0][0], device=device)
-    from kvserve_hpdps_b200.compression.oracle import error_metrics
-    a = wl.src[:, :, idx_s].float()
-    b = wl.dst[:, :, idx_d].float()
-    err = {"cosine": float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)),
-           "rel_mse": float(((a - b) ** 2).sum() / (a ** 2).sum())}
-    del error_metrics
-    cr = wl.bf16_bytes_per_request / statistics.mean(sizes)
-    ref_path = ("raw: extract_kv_from_layer_by_blocks + stack + inject_kv_into_layer_by_blocks"
-                if raw else "custom pipeline [quantizer] via KVCompressionAdapter (default mode "
-                "unavailable: " + (default_err if path is None else "n/a") + ")")
-    return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "reference_path": ref_path,
-            "transport": "local", "fallback_raw": len(fallbacks)}
+            "pipeline": ("raw: extract_kv_from_layer_by_blocks + stack + NcclTransport.send "
+                         "+ inject_kv_into_layer_by_blocks") if raw else
+                        REF_PIPELINE + "; its build_wire + NcclTransport.send_bundle",
+            "transport": "reference NcclTransport (ZMQ header + NCCL send/recv per pair)"}
 
 
 # ------------------------------------------------------------------ main
-def hybrid_ratio(args) -> float:
-    return float(quant_config(args)["quantizer_config"]["hybrid_ratio"])
-
-
-def compression_label(args) -> str:
-    if args.compression == "off":
-        return "off (raw bf16 blocks)"
-    codec = "rANS" if args.codec == "rans" else args.codec
-    return f"default (Hadamard + hybrid {hybrid_ratio(args)} 12/8/6/4 + {codec})"
-
-
-def main(argv=None):
-    args = parse_args(argv)
-    rank, world, local = dist_info()
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    if args.warmup < 3:  # timed numbers need at least three untimed warm-up steps
-        print(f"bench: --warmup {args.warmup} raised to 3", file=sys.stderr)
-        args.warmup = 3
-    init_dist(world, local)
-    try:
-        res = run_reference(args, rank, world, local) if args.impl == "reference" else \
-            run_ours(args, rank, world, local)
-    finally:
-        pass
-    if "unavailable" in res:
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return 0
+def build_line(args, res, world):
+    """The one JSON line rank 0 prints."""
     pairs = res.get("pairs", 1)
-    reqs = args.steps * args.requests_per_step * pairs
-    value = res["ms"] / reqs
+    per_pair_requests = args.steps * args.requests_per_step
+    value = res["ms"] / per_pair_requests
+    raw_bytes = args.layers * 2 * args.tokens * args.kv_heads * 128 * 2
     line = {
         "metric": METRIC,
         "value": round(value, 5),
@@ -931,32 +1046,65 @@ def main(argv=None):
             "parallelism": "1-GPU round trip" if world == 1 else f"1P1D x{pairs} pairs (TP1)",
             "compression": compression_label(args),
             "requests_per_step": args.requests_per_step,
+            "value_definition": "ms per request of one producer/consumer pair (N=1: one GPU "
+                                "does both halves)",
             "l2": "inputs larger than L2 (%.1f GB of KV per step per producer)"
-                  % (args.layers * 2 * args.tokens * args.kv_heads * 256 * args.requests_per_step / 1e9),
-            "transport": res.get("transport"),
+                  % (raw_bytes * args.requests_per_step / 1e9),
         },
         "compression_ratio": round(res["cr"], 3) if res.get("cr") else None,
         "reconstruction": res.get("error"),
         "clocks": res.get("clocks"),
+        "aggregate_gbps": round(raw_bytes * args.requests_per_step * pairs * args.steps /
+                                (res["ms"] * 1e6), 1),
+        "pipeline": res.get("pipeline"),
+        "transport": res.get("transport"),
     }
+    for k in ("stage_ms_per_request", "single_request_latency_ms", "full_path"):
+        if res.get(k) is not None:
+            line[k] = res[k]
     if args.impl == "reference":
         line["impl"] = "reference"
-        if res.get("fallback_raw"):
-            line["config"]["reference_fallback_raw_requests"] = res["fallback_raw"]
-        line["config"]["reference_path"] = res.get("reference_path")
-        line["config"]["compression"] = (
-            "off (raw bf16 blocks)" if args.compression == "off" else
-            f"reference quantizer pipeline, hybrid {hybrid_ratio(args)} 12/8/6/4, u8 codes, no "
-            "entropy codec (its default mode needs nvCOMP, CuPy and fast_hadamard_transform)")
     else:
         line["impl"] = "ours"
-        line["gpu_launches"] = int(allreduce_sum(float(res["launches"]), world)) if world > 1 \
-            else res["launches"]
+        line["gpu_launches"] = int(res.get("launches_job", res.get("launches_total",
+                                                                  res["launches"])))
         line["engine"] = args.engine
         if res.get("e2e"):
             line["e2e"] = res["e2e"]
         if res.get("device_error"):
             line["device_error"] = res["device_error"]
+    return line
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    rank, world, local = dist_info()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.warmup < 3:  # timed numbers need at least three untimed warm-up steps
+        print(f"bench: --warmup {args.warmup} raised to 3", file=sys.stderr)
+        args.warmup = 3
+    init_dist(world, local)
+    if args.impl == "reference":
+        res = run_reference(args, rank, world, local)
+    else:
+        res = run_ours(args, rank, world, local)
+    if "unavailable" in res:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return 0
+    if args.impl == "ours" and res.get("pipeline") is None:
+        res["pipeline"] = ("fused sm_100a kernels: tcgen05 Hadamard (TMA from the paged cache) "
+                           "+ hybrid quantization, " + ("rANS, " if res.get("codec") == "rans"
+                                                        else "") +
+                           "dequantization + inverse Hadamard + paged scatter")
+    if args.impl == "ours":  # every rank's own kernels, summed over the job
+        total = res.get("launches_total", res["launches"])
+        res["launches_job"] = allreduce_sum(float(total), world) if world > 1 else total
+    line = build_line(args, res, world)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -11,7 +11,8 @@ CUDA events between barriers, the maximum over ranks.
 
 * 1 GPU: compress -> decompress round trip (or raw gather -> scatter);
 * N >= 2 GPUs (torchrun, one rank per GPU): pairs r <-> r + N/2, the
-  producer's kernels store into the consumer's receive slot over NVLink.
+  producer's kernels store into the consumer's receive ring over NVLink
+  (times are per pair).
 
 ``--impl reference`` (or ``both``) also runs the unmodified reference from
 ``baseline/_ref`` through its public adapter and NCCL transport on the same
@@ -56,14 +57,18 @@ def parse_args(argv=None):
     ap.add_argument("--modes", nargs="+", default=list(MODES), choices=list(MODES))
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--max-reference-tokens", type=int, default=16384)
+    ap.add_argument("--codec", default="none", choices=["none", "rans"],
+                    help="this framework's codec (none: the reference's runnable stage set)")
     ap.add_argument("--out", default=None, help="markdown table (rank 0)")
     return ap.parse_args(argv)
 
 
-def point_args(bench, world: int, tokens: int, mode: str, warmup: int):
+def point_args(bench, world: int, tokens: int, mode: str, warmup: int,
+               codec: str = "none"):
     comp, hr = MODES[mode]
     argv = ["--gpus", str(world), "--steps", str(steps_for(tokens)), "--warmup", str(warmup),
-            "--tokens", str(tokens), "--requests-per-step", "1", "--compression", comp, "--no-e2e"]
+            "--tokens", str(tokens), "--requests-per-step", "1", "--compression", comp, "--no-e2e",
+            "--no-full-path", "--codec", codec, "--latency-reps", "0"]
     if hr is not None:
         argv += ["--hybrid-ratio", str(hr)]
     a = bench.parse_args(argv)
@@ -86,15 +91,14 @@ def main(argv=None) -> int:
             for impl in impls:
                 if impl == "reference" and tokens > opts.max_reference_tokens:
                     continue
-                a = point_args(bench, world, tokens, mode, opts.warmup)
+                a = point_args(bench, world, tokens, mode, opts.warmup, opts.codec)
                 res = bench.run_reference(a, rank, world, local) if impl == "reference" else \
                     bench.run_ours(a, rank, world, local)
                 torch.cuda.empty_cache()
                 if "unavailable" in res:
                     row = {"impl": impl, "unavailable": res["unavailable"]}
                 else:
-                    pairs = res.get("pairs", 1)
-                    ms = res["ms"] / (a.steps * pairs)
+                    ms = res["ms"] / a.steps  # per pair: every pair hands off one request a step
                     raw = tokens * BYTES_PER_TOKEN
                     err = res.get("error") or {}
                     row = {"impl": impl, "n_gpus": world, "tokens": tokens, "raw_bytes": raw,

@@ -167,7 +167,7 @@ class FusedCompressionManager:
     def compress_paged_requests(self, kv_layers: Sequence[torch.Tensor], layer_ids: Sequence[int],
                                 requests: Sequence[tuple[Sequence[int], int]],
                                 member_tids: Optional[Sequence[str]] = None,
-                                trim: bool = True) -> CompressedKVData:
+                                trim: bool = True, deferred: bool = False) -> CompressedKVData:
         """Compress the given layers of several requests into ONE message:
         one codec stream over every (layer, request) item, layer-major.
 
@@ -179,16 +179,29 @@ class FusedCompressionManager:
         the plans and block counts).  Decoders also accept the per-item
         ``layout="items"`` form.
 
-        ``trim=False`` sends the codec's worst-case stream buffer instead of
+        ``trim=False`` returns the codec's worst-case stream buffer instead of
         reading the stream size back (which synchronises the host with the
         device); the stream records its own length and the decoder takes the
-        code byte count from the metadata, so nothing else changes.  The
-        connector uses it: the extra bytes cost far less than the stall."""
+        code byte count from the metadata.  ``deferred=True`` (entropy coder
+        only) returns the codes themselves with ``deferred_codec`` set in the
+        metadata: a transport encodes them on its way out and sends only the
+        stream's bytes (the NCCL transport on its send thread), and a
+        consumer that receives them unencoded decodes them as plain codes.
+        Without an entropy coder the body is always the code buffer itself
+        (``container=False``: no header, no copy)."""
         with nvtx("kvs.quantize"):
             batch = self.quantize_paged(kv_layers, layer_ids, requests)
+        codes = batch.codes[:batch.items.code_bytes]
+        container = True
         with nvtx("kvs.encode"):
-            body = encode_bytes(batch.codes[:batch.items.code_bytes], self.stream_codec) if trim \
-                else self._encode_untrimmed(batch.codes[:batch.items.code_bytes])
+            if self.stream_codec == "none":
+                body, container = codes, False
+            elif deferred and self.stream_codec == "rans":
+                body, container = codes, False
+            elif trim:
+                body = encode_bytes(codes, self.stream_codec)
+            else:
+                body = self._encode_untrimmed(codes)
         items = batch.items
         H = self.num_kv_heads
         meta = {"grouped": True, "layout": "items_packed", "layer_ids": [int(l) for l in layer_ids],
@@ -205,11 +218,116 @@ class FusedCompressionManager:
                 "quantization_params": [batch.meta[:max(items.meta_bytes, 16)]],
                 "code_bytes": int(items.code_bytes), "backend": BACKEND, "codec": self.codec,
                 "stream_codec": self.stream_codec, "transform_seed": self.base_seed}
+        if not container:
+            meta["container"] = False
+            if self.stream_codec != "none":
+                meta["deferred_codec"] = self.stream_codec
         orig = sum(len(kv_layers) * 2 * n * H * self.head_size * 2 for _, n in requests)
         self._last_batch = batch
         return CompressedKVData(request_id="grp", layer_id=int(layer_ids[-1]),
                                 compressed_tensor=body, metadata=meta, original_size=orig,
                                 compressed_size=int(body.numel()))
+
+    def send_paged_requests(self, transport, request_id: str, layer_names: Sequence[str],
+                            kv_layers: Sequence[torch.Tensor], layer_ids: Sequence[int],
+                            requests: Sequence[tuple[Sequence[int], int]],
+                            member_tids: Optional[Sequence[str]] = None) -> dict:
+        """Compress the requests and hand them to ``transport`` as ONE
+        message, written by the producer kernels straight into the
+        consumer's receive ring when the transport offers it (NVLink ring
+        transport: ``open_message``), else through ``send_bundle``.
+
+        Direct path, on the current stream, no host synchronisation:
+        statistics and quantization read the paged caches; without an
+        entropy coder the quantize kernel stores the codes into the ring over
+        NVLink and sums their message checksum on the way; with rANS the
+        codes stay local and the encoder's compaction kernel stores only the
+        coded stream (its worst case is reserved, only its own bytes cross
+        the link); a final copy brings the fp16 metadata and its last CTA
+        stores the checksum and publishes the ready flag.
+
+        Returns ``{"original_size", "wire_nbytes", "direct"}`` where
+        ``wire_nbytes`` is the reserved (upper-bound) size on the direct
+        path; the exact size reaches the transport's sent listeners."""
+        from kvserve_hpdps_b200.compression.codec import CODEC_IDS, MAGIC
+        from kvserve_hpdps_b200.compression.wire import build_wire
+        from kvserve_hpdps_b200.ops import kernels as K
+        direct = (hasattr(transport, "open_message") and self.engine == 0
+                  and self.stream_codec in ("none", "rans") and kv_layers[0].is_cuda)
+        if not direct:
+            cd = self.compress_paged_requests(kv_layers, layer_ids, requests, member_tids,
+                                              trim=False, deferred=True)
+            wire = build_wire(cd)
+            transport.send_bundle(request_id, list(layer_names), wire.meta, wire.body_chunks,
+                                  wire.aux_tensors, member_tids=list(member_tids or []) or None)
+            return {"original_size": cd.original_size, "wire_nbytes": wire.nbytes,
+                    "direct": False}
+        plans = [self.plan(l) for l in layer_ids]
+        slots = self._slots(kv_layers, plans)
+        items = K.WorkItems(slots, [(i, b, n) for i in range(len(kv_layers)) for b, n in requests])
+        dev = kv_layers[0].device
+        code_bytes, meta_bytes = max(items.code_bytes, 16), max(items.meta_bytes, 16)
+        rans = self.stream_codec == "rans"
+        body_cap = 16 + K.rans_max_bytes(code_bytes) if rans else code_bytes
+        try:
+            msg = transport.open_message([body_cap, meta_bytes])
+        except RuntimeError as e:
+            transport.record_unsent(request_id, list(member_tids or []) or None, e)
+            return {"original_size": 0, "wire_nbytes": 0, "direct": True}
+        meta_local = torch.empty(meta_bytes, dtype=torch.uint8, device=dev)
+        total = None
+        with nvtx("kvs.quantize_to_ring"):
+            if rans:
+                codes = torch.empty(code_bytes, dtype=torch.uint8, device=dev)
+                K.quantize(slots, items, codes, meta_local, engine=self.engine)
+            else:  # codes straight into the peer ring, checksummed as they are stored
+                K.quantize(slots, items, transport.view(msg, 0), meta_local, engine=self.engine,
+                           ck=msg.ck, ck_off=0)
+        with nvtx("kvs.encode_to_ring"):
+            if rans:
+                K.copy_segments([(meta_local.data_ptr(), msg.ptrs[1], meta_bytes, msg.offsets[1])],
+                                dev, ck=msg.ck)
+                total = torch.empty(1, dtype=torch.int64, device=dev)
+                K.rans_encode_message(codes.data_ptr(), code_bytes, msg.ptrs[0] + 16, dev,
+                                      total=total,
+                                      prefix=[MAGIC, CODEC_IDS["rans"], code_bytes & 0xFFFFFFFF,
+                                              code_bytes >> 32],
+                                      msg_off=16, ck=msg.ck, trailer_ptr=msg.trailer_ptr,
+                                      flag_ptr=msg.flag_ptr, flag_value=msg.flag_value)
+            else:
+                K.copy_segments([(meta_local.data_ptr(), msg.ptrs[1], meta_bytes, msg.offsets[1])],
+                                dev, flag_ptr=msg.flag_ptr, flag_value=msg.flag_value,
+                                ck=msg.ck, trailer_ptr=msg.trailer_ptr)
+        H = self.num_kv_heads
+        body_view = transport.view(msg, 0)
+        meta_view = transport.view(msg, 1)
+        info = {"grouped": True, "layout": "items_packed", "layer_ids": [int(l) for l in layer_ids],
+                "member_tids": list(member_tids) if member_tids else
+                [str(i) for i in range(len(requests))],
+                "member_tokens": [int(n) for _, n in requests],
+                "member_blocks": [len(b) for b, _ in requests],
+                "block_size": int(kv_layers[0].shape[2]), "num_heads": H, "device": str(dev),
+                "layer_plans": [{"group_of_head": list(p.group_of_head),
+                                 "code_bits": list(p.key_bits) + list(p.value_bits)}
+                                for p in plans],
+                "meta_bytes": int(items.meta_bytes), "quantization_params": [meta_view],
+                "code_bytes": int(items.code_bytes), "backend": BACKEND, "codec": self.codec,
+                "stream_codec": self.stream_codec, "transform_seed": self.base_seed}
+        if not rans:
+            info["container"] = False
+        orig = sum(len(kv_layers) * 2 * n * H * self.head_size * 2 for _, n in requests)
+        cd = CompressedKVData(request_id="grp", layer_id=int(layer_ids[-1]),
+                              compressed_tensor=body_view, metadata=info, original_size=orig,
+                              compressed_size=int(body_cap))
+        wire = build_wire(cd, max_chunk_bytes=1 << 62)
+        specs = [{"shape": [body_cap], "dtype": "uint8"}, {"shape": [meta_bytes], "dtype": "uint8"}]
+        # the stream's length sits at byte 24 of its header, 16 bytes into the body
+        dyn = {"seg": 0, "len_off": 16 + 24, "len_add": 16} if rans else None
+        sent = (total, 16 + meta_bytes) if rans else None
+        transport.commit_message(msg, request_id, list(layer_names), wire.meta, specs, 1,
+                                 member_tids=list(member_tids or []) or None, dyn_len=dyn,
+                                 sent_bytes=sent)
+        return {"original_size": orig, "wire_nbytes": body_cap + meta_bytes, "direct": True}
 
     def _message_plans(self, meta: dict) -> list:
         """Consumer-side plans of a grouped message, one per layer."""
@@ -272,6 +390,11 @@ class FusedCompressionManager:
         self-describing container."""
         from kvserve_hpdps_b200.ops import kernels as K
         sc, n = meta.get("stream_codec"), meta.get("code_bytes")
+        if meta.get("container") is False:  # the codes themselves (no codec or not yet encoded)
+            data = body.view(torch.uint8).reshape(-1)
+            if data.device != torch.device(device):
+                data = data.to(device)
+            return data[:int(n)]
         if sc is None or n is None or body.device.type != "cuda":
             return decode_bytes(body, device)
         if body.device != torch.device(device):

@@ -275,9 +275,17 @@ class KVCompressionAdapter:
                                               original_shape)
 
     def compress_paged_requests(self, kv_layers, layer_ids, requests, member_tids=None,
-                                trim: bool = True):
+                                trim: bool = True, deferred: bool = False):
         return self._manager.compress_paged_requests(kv_layers, layer_ids, requests, member_tids,
-                                                     trim=trim)
+                                                     trim=trim, deferred=deferred)
+
+    def send_paged_requests(self, transport, request_id, layer_names, kv_layers, layer_ids,
+                            requests, member_tids=None) -> dict:
+        """Compress and send one message (see
+        ``FusedCompressionManager.send_paged_requests``: straight into the
+        consumer's ring on the NVLink transport)."""
+        return self._manager.send_paged_requests(transport, request_id, layer_names, kv_layers,
+                                                 layer_ids, requests, member_tids)
 
     def decompress_paged_requests(self, compressed, dst_layers, dst_requests):
         return self._manager.decompress_paged_requests(compressed, dst_layers, dst_requests)

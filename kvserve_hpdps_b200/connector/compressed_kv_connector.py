@@ -200,6 +200,9 @@ class CompressedKVConnector(KVConnectorBase_V1):
         # transport reports the message sent; completions queued by its thread
         self._ctl_wait: dict[str, tuple[str, float, float]] = {}
         self._ctl_done: deque = deque()
+        # transfer id -> (request id, original bytes, reserved wire bytes, compress ms,
+        # prefill span ms): compression statistics written once the message is out
+        self._stats_wait: dict[str, tuple] = {}
         self._listening = False
         if role == KVConnectorRole.WORKER:
             self._init_worker(cfg)
@@ -258,11 +261,19 @@ class CompressedKVConnector(KVConnectorBase_V1):
             tr.add_sent_listener(self._on_sent)
             self._listening = True
 
-    def _on_sent(self, request_id: str, transfer_ids: list[str], latency_ms: float) -> None:
-        # transport thread: only queue; the engine thread applies the updates
+    def _on_sent(self, request_id: str, transfer_ids: list[str], latency_ms: float,
+                 nbytes: Optional[int] = None) -> None:
+        # transport thread: only queue controller updates (the engine thread
+        # applies them); compression statistics wait for the exact size on
+        # the wire (a coded stream's length is known only on the device)
         for t in transfer_ids:
             if t in self._ctl_wait:
                 self._ctl_done.append((t, latency_ms))
+            stat = self._stats_wait.pop(t, None)
+            if stat is not None:
+                rid, orig, wire, ms, span = stat
+                write_compression_stats(rid, t, orig, nbytes if nbytes else wire,
+                                        compress_ms=ms, prefill_span_ms=span)
 
     def _apply_controller_feedback(self) -> None:
         comp = self._compressor
@@ -319,9 +330,11 @@ class CompressedKVConnector(KVConnectorBase_V1):
             try:
                 with torch.cuda.stream(self._side_stream):
                     self._side_stream.wait_event(ready)
-                    cd = comp.compress_paged_requests([kv_layer], [layer_index(layer_name)],
-                                                      requests, member_tids=tids, trim=False)
-                    self._send_compressed(tids[0], [layer_name], cd, member_tids=tids)
+                    # one grouped message for the layer; on the NVLink ring the
+                    # producer kernels store it straight into the consumer's memory
+                    comp.send_paged_requests(self._transport, tids[0], add_sentinel([layer_name]),
+                                             [kv_layer], [layer_index(layer_name)], requests,
+                                             member_tids=tids)
             except Exception:  # noqa: BLE001
                 # as in the off mode: a compression failure sends this layer's raw
                 # KV, one message per request (the consumer still counts one
@@ -363,20 +376,24 @@ class CompressedKVConnector(KVConnectorBase_V1):
             layers = [self._layer_refs[n] for n in names]
             if comp is not None and comp.supports_paged() and layers[0].is_cuda:
                 try:
-                    with nvtx("kvs.compress"):
-                        cd = comp.compress_paged_requests(layers, [layer_index(n) for n in names],
-                                                          [(rm.block_ids, len(rm.token_ids))],
-                                                          member_tids=[tid], trim=False)
+                    with nvtx("kvs.compress_send"):
+                        info = comp.send_paged_requests(
+                            self._transport, tid, add_sentinel(names), layers,
+                            [layer_index(n) for n in names], [(rm.block_ids, len(rm.token_ids))],
+                            member_tids=[tid])
                 except Exception:  # noqa: BLE001
                     # as the reference does: a compression failure sends the raw KV
                     logger.exception("compression of %s failed; sending raw KV", rid)
-                    cd = None
-                if cd is not None:
-                    nbytes = self._send_compressed(tid, names, cd, member_tids=[tid])
+                    info = None
+                if info is not None:
                     self._expected_msgs[tid] = 1
-                    write_compression_stats(rid, tid, cd.original_size, nbytes,
-                                            compress_ms=(time.monotonic() - t0) * 1e3,
-                                            prefill_span_ms=span)
+                    stat = (rid, info["original_size"], info["wire_nbytes"],
+                            (time.monotonic() - t0) * 1e3, span)
+                    if self._listening:  # written with the exact size once it is out
+                        self._stats_wait[tid] = stat
+                    else:
+                        write_compression_stats(rid, tid, stat[1], stat[2], compress_ms=stat[3],
+                                                prefill_span_ms=stat[4])
                     continue
                 comp = None
             if comp is None and hasattr(self._transport, "send_paged") and layers[0].is_cuda:

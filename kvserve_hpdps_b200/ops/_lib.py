@@ -52,7 +52,15 @@ class LayerLaunch(ctypes.Structure):
                 ("meta", c_void_p), ("kstat", c_void_p), ("vstat", c_void_p), ("err", c_void_p),
                 ("total_tiles", c_int), ("num_heads", c_int), ("engine", c_int),
                 ("stream", c_void_p), ("trace", c_void_p), ("trace_jobs", c_int),
-                ("vparam", c_void_p)]
+                ("vparam", c_void_p), ("ck", c_void_p), ("ck_off", c_longlong)]
+
+
+class RansMsg(ctypes.Structure):
+    """Where an encoded rANS stream goes inside a transfer message."""
+    _fields_ = [("prefix", c_uint32 * 4), ("has_prefix", c_int), ("pad_", c_int),
+                ("msg_off", c_longlong), ("ck", c_void_p), ("trailer", c_void_p),
+                ("counter", c_void_p), ("flag", c_void_p), ("flag_value", c_uint32),
+                ("pad2_", c_int)]
 
 
 class RawItem(ctypes.Structure):
@@ -87,7 +95,9 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_dequant_inverse": ([POINTER(LayerLaunch)], c_int),
         "kvs_rans_max_bytes": ([c_uint64, c_uint32], c_uint64),
         "kvs_rans_staging_bytes": ([c_uint64, c_uint32], c_uint64),
-        "kvs_rans_encode": ([P, c_uint64, c_uint32, P, P, P, P, P, P, c_uint32, P], c_int),
+        "kvs_rans_encode": ([P, c_uint64, c_uint32, P, P, P, P, P, P], c_int),
+        "kvs_rans_msg_size": ([], c_int),
+        "kvs_rans_sizes_words": ([c_uint64, c_uint32], c_uint64),
         "kvs_rans_decode": ([P, c_uint64, P, c_uint64, c_uint32, P, P], c_int),
         "kvs_lc_max_bytes": ([c_uint64], c_uint64),
         "kvs_lc_staging_bytes": ([c_uint64], c_uint64),
@@ -109,7 +119,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "kvs_raw_item_size": ([], c_int),
         "kvs_paged_raw": ([POINTER(RawLaunch), c_int, P], c_int),
         "kvs_copy16": ([P, P, c_longlong, P, P, c_uint32, c_int, P], c_int),
-        "kvs_copy_segments": ([P, c_int, c_int, P, P, c_uint32, P], c_int),
+        "kvs_copy_segments": ([P, c_int, c_int, P, P, c_uint32, P, P, P], c_int),
+        "kvs_zero2": ([P, P], c_int),
         "kvs_wait_flag": ([P, c_uint32, c_uint64, P, P, P], c_int),
         "kvs_set_flag": ([P, c_uint32, P], c_int),
         "kvs_probe_push": ([P, P, c_longlong, P, c_int, P], c_int),
@@ -151,6 +162,7 @@ def lib() -> ctypes.CDLL:
                               ("kvs_layer_params_size", LayerParams),
                               ("kvs_paged_kv_size", PagedKV),
                               ("kvs_raw_launch_size", RawLaunch),
+                              ("kvs_rans_msg_size", RansMsg),
                               ("kvs_raw_item_size", RawItem)):
                 got = getattr(handle, name)()
                 if got != ctypes.sizeof(cls):
@@ -175,4 +187,5 @@ def check(rc: int, what: str) -> None:
 
 
 __all__ = ["lib", "available", "check", "PagedKV", "ReqTable", "LayerParams", "LayerLaunch",
+           "RansMsg",
            "MAX_HEADS", "c_double", "c_ulonglong"]

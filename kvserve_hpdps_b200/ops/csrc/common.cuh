@@ -385,4 +385,58 @@ KVS_DEV void unpack32(const uint32_t (&w)[8], uint32_t (&c)[32]) {
   }
 }
 
+// ------------------------------------------------------ message checksum
+// Message checksum (producer and consumer compute it the same way): over
+// the bytes b_p of a message (p = offset inside the message),
+// S1 = sum_p b_p * 2^(8*(p%4)) and S2 = sum_p (p/4 + 1) * b_p * 2^(8*(p%4)),
+// both mod 2^64 -- the plain and the position-weighted sums of the message's
+// little-endian 32-bit words.  Integer sums are order-independent, so any
+// grid, and any split of a message over several kernels adding into the
+// same two accumulators, gives the same value.
+KVS_DEV void ck_byte(uint8_t b, long long p, unsigned long long& s1, unsigned long long& s2) {
+  const unsigned long long v = static_cast<unsigned long long>(b) << (8 * (p & 3));
+  s1 += v;
+  s2 += static_cast<unsigned long long>((p >> 2) + 1) * v;
+}
+
+// Four words at message offset `off` (a multiple of 16).
+KVS_DEV void ck_word4(const uint4& v, long long off, unsigned long long& s1,
+                      unsigned long long& s2) {
+  const unsigned long long w = static_cast<unsigned long long>((off >> 2) + 1);
+  s1 += static_cast<unsigned long long>(v.x) + v.y + v.z + v.w;
+  s2 += w * v.x + (w + 1) * v.y + (w + 2) * v.z + (w + 3) * v.w;
+}
+
+// Warp reduction of a thread's partial sums into the accumulators.
+KVS_DEV void ck_flush(unsigned long long* ck, unsigned long long s1, unsigned long long s2) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, o);
+    s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+  }
+  if ((threadIdx.x & 31) == 0 && (s1 | s2)) {
+    atomicAdd(ck, s1);
+    atomicAdd(ck + 1, s2);
+  }
+}
+
+// Called by thread 0 of every CTA after its stores and its checksum sums
+// (fenced at system scope by the caller): the last CTA of `total_ctas`
+// stores the finished sums to `trailer` (may be peer memory), fences at
+// system scope and publishes `flag_value` with release semantics.
+KVS_DEV void last_cta_publish(uint32_t* counter, uint32_t total_ctas, unsigned long long* ck,
+                              unsigned long long* trailer, uint32_t* flag, uint32_t flag_value) {
+  const uint32_t done = atomicAdd(counter, 1u);
+  if (done == total_ctas - 1) {
+    __threadfence();
+    if (trailer != nullptr && ck != nullptr) {
+      trailer[0] = atomicAdd(ck, 0ull);  // coherent reads of the finished sums
+      trailer[1] = atomicAdd(ck + 1, 0ull);
+    }
+    __threadfence_system();
+    if (flag != nullptr) st_release_sys(flag, flag_value);
+    *counter = 0;
+  }
+}
+
 }  // namespace kvs

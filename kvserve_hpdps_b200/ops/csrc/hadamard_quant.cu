@@ -1759,6 +1759,7 @@ __global__ void __launch_bounds__(kWsProdThreads, 1) k_quant_ws(LayerLaunch L) {
                                                        static_cast<long long>(grp) * rows + prow];
     };
     float2 vp_next = load_vp(g);
+    unsigned long long ck1 = 0, ck2 = 0;  // message checksum of this thread's code stores
     for (int k = g; k < n; k += kWsGroups) {
       const PJob jb = ws_job(M, k);
       cursor_seek(L, cur, jb.tile);
@@ -1806,17 +1807,21 @@ __global__ void __launch_bounds__(kWsProdThreads, 1) k_quant_ws(LayerLaunch L) {
       if (lane == 0) mbar_arrive(&S.afree[a]);
       group_sync(g);  // staging complete
       if (gw == 0 && lane == 0) trace_mark(L, k, 7);
-      // Coalesced 16-byte copy of the tile's contiguous code region.
+      // Coalesced 16-byte copy of the tile's contiguous code region (the
+      // region may be a peer GPU's receive ring: NVLink stores).
       const int nrows = min(kTileRows, c.rows - c.row0);
       uint8_t* dst0 = code_row(L, c, jb.plane, jb.h, c.row0);
+      const long long dst_msg = L.ck_off + (dst0 - L.codes);
       const int total = nrows * bits;
       for (int q = gtid; q < total; q += kWsGroupThreads) {
         const int r = q / bits, col = q - r * bits;
-        *reinterpret_cast<uint4*>(dst0 + static_cast<long long>(q) * 16) =
-            *reinterpret_cast<const uint4*>(stage + r * P + col * 16);
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + r * P + col * 16);
+        *reinterpret_cast<uint4*>(dst0 + static_cast<long long>(q) * 16) = v;
+        if (L.ck != nullptr) ck_word4(v, dst_msg + 16ll * q, ck1, ck2);
       }
       if (gw == 0 && lane == 0) trace_mark(L, k, 4);
     }
+    if (L.ck != nullptr) ck_flush(L.ck, ck1, ck2);
   }
   tc_fence_before();
   __syncthreads();
@@ -2552,6 +2557,7 @@ int kvs_quant(const LayerLaunch* Lp) {
   const LayerLaunch& L = *Lp;
   if (L.total_tiles <= 0) return 0;
   if (2LL * L.num_heads * L.total_tiles >= (1LL << 31)) return -103;  // job index is 32-bit
+  if (L.ck != nullptr && L.engine != 0) return -2;  // the code-store checksum is engine 0's
   cudaStream_t s = static_cast<cudaStream_t>(L.stream);
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {

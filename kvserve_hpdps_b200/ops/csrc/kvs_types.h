@@ -88,6 +88,13 @@ struct LayerLaunch {
   // like vstat by head; written by k_value_params before the
   // warp-specialized quantize kernel, which reads it (engine 0 only).
   float* vparam;
+  // Optional message checksum of the code stores (engine 0 quantize only):
+  // the quantize kernel adds the checksum of every code byte it writes,
+  // weighted by its message offset ck_off + (address - codes), into ck[2]
+  // (used when `codes` is a peer GPU's receive ring; common.cuh defines
+  // the checksum).  nullptr = off.
+  unsigned long long* ck;
+  long long ck_off;
 };
 constexpr int kTraceCtas = 8;
 

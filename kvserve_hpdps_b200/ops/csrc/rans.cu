@@ -20,6 +20,20 @@ constexpr int kDecWarps = 8;
 constexpr int kRing = 1024;  // words of the decoder's shared-memory ring
 constexpr int kDecWarpSmem = 4096 + 1024 + kRing * 2;
 
+// Where an encoded stream goes inside a transfer message (all optional).
+struct RansMsg {
+  uint32_t prefix[4];           // 16-byte container header stored just before the stream
+  int has_prefix;
+  int pad_;
+  long long msg_off;            // message offset of the stream's first byte (multiple of 16)
+  unsigned long long* ck;       // message checksum accumulators (zeroed by the caller)
+  unsigned long long* trailer;  // receives the finished checksum (may be peer memory)
+  uint32_t* counter;            // completion counter (zero) for the flag publish
+  uint32_t* flag;               // ready flag (may be peer memory)
+  uint32_t flag_value;
+  int pad2_;
+};
+
 KVS_DEV uint32_t lanemask_lt() {
   uint32_t m;
   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
@@ -228,11 +242,18 @@ __global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
   }
 }
 
-// Single CTA: header, exclusive scan of record lengths, directory.
+// Single CTA: header, exclusive scan of record lengths, directory.  The
+// record offsets also go to `dst_off` (local memory) for k_rans_copy, which
+// therefore never reads `out` (it may be a peer GPU's buffer).  With
+// m.has_prefix the 16-byte container header m.prefix is written just before
+// the stream; with m.ck the checksum of everything this kernel writes is
+// added (message offset of out[0] = m.msg_off, a multiple of 16).
 __global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restrict__ rec_len,
                                                          uint32_t n_chunks, uint64_t n,
                                                          uint32_t cs, uint8_t* __restrict__ out,
-                                                         uint64_t* __restrict__ total_out) {
+                                                         uint64_t* __restrict__ total_out,
+                                                         uint64_t* __restrict__ dst_off,
+                                                         const RansMsg m) {
   __shared__ uint64_t part[1024];
   const int tid = threadIdx.x;
   const uint32_t per = (n_chunks + 1023) / 1024;
@@ -250,12 +271,27 @@ __global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restr
   const uint64_t base = pad16(directory_bytes(n_chunks));
   uint64_t* dir = reinterpret_cast<uint64_t*>(out + sizeof(StreamHeader));
   uint64_t run = base + (tid > 0 ? part[tid - 1] : 0);
+  unsigned long long s1 = 0, s2 = 0;
+  // one 64-bit value at stream byte offset `off`: two words of the checksum
+  auto ck64 = [&](uint64_t v, uint64_t off) {
+    const unsigned long long w = static_cast<unsigned long long>((m.msg_off + off) >> 2) + 1;
+    const unsigned long long lo = v & 0xFFFFFFFFull, hi = v >> 32;
+    s1 += lo + hi;
+    s2 += w * lo + (w + 1) * hi;
+  };
   for (uint32_t i = b; i < e; ++i) {
     dir[i] = run;
+    dst_off[i] = run;
+    if (m.ck != nullptr) ck64(run, sizeof(StreamHeader) + 8ull * i);
     run += rec_len[i];
   }
   if (tid == 0) {
     for (uint64_t i = sizeof(StreamHeader) + 8ull * (n_chunks + 1); i < base; ++i) out[i] = 0;
+    if (m.has_prefix) {
+      uint4 pre = make_uint4(m.prefix[0], m.prefix[1], m.prefix[2], m.prefix[3]);
+      *reinterpret_cast<uint4*>(out - 16) = pre;
+      if (m.ck != nullptr) ck_word4(pre, m.msg_off - 16, s1, s2);
+    }
   }
   if (tid == 1023) {
     const uint64_t total = base + part[1023];
@@ -263,37 +299,45 @@ __global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restr
     StreamHeader hd{kMagic, n_chunks, n, cs, static_cast<uint32_t>(kProbBits), total};
     *reinterpret_cast<StreamHeader*>(out) = hd;
     if (total_out) *total_out = total;
+    if (m.ck != nullptr) {
+      ck64(total, sizeof(StreamHeader) + 8ull * n_chunks);
+      const uint64_t* hw = reinterpret_cast<const uint64_t*>(&hd);
+      for (int k = 0; k < 4; ++k) ck64(hw[k], 8ull * k);
+    }
   }
+  if (m.ck != nullptr) ck_flush(m.ck, s1, s2);
   __threadfence_system();
 }
 
-// One warp per record: compact staging -> out (out may be a peer buffer).
-// With `counter` set, the last warp to finish publishes `flag_value` into
-// `flag` with release semantics after a system-scope fence.
+// One warp per record: compact staging -> out (out may be a peer buffer),
+// at the offsets the directory kernel left in `dst_off`.  With m.ck the
+// checksum of the records is added; with m.counter the last CTA stores the
+// finished checksum to m.trailer (when set) and publishes m.flag_value into
+// m.flag with release semantics after a system-scope fence.
 __global__ void __launch_bounds__(256) k_rans_copy(
     const uint8_t* __restrict__ staging, const uint32_t* __restrict__ rec_off,
-    const uint32_t* __restrict__ rec_len, uint32_t n_chunks, uint32_t cs, uint8_t* out,
-    uint32_t* counter, uint32_t* flag, uint32_t flag_value) {
+    const uint32_t* __restrict__ rec_len, const uint64_t* __restrict__ dst_off,
+    uint32_t n_chunks, uint32_t cs, uint8_t* out, const RansMsg m) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk = blockIdx.x * 8 + warp;
+  unsigned long long s1 = 0, s2 = 0;
   if (chunk < n_chunks) {
-    const uint64_t* dir = reinterpret_cast<const uint64_t*>(out + sizeof(StreamHeader));
+    const uint64_t doff = dst_off[chunk];
     const uint4* s = reinterpret_cast<const uint4*>(staging + static_cast<uint64_t>(chunk) * slot_bytes(cs) + rec_off[chunk]);
-    uint4* d = reinterpret_cast<uint4*>(out + dir[chunk]);
+    uint4* d = reinterpret_cast<uint4*>(out + doff);
     const uint32_t n16 = rec_len[chunk] / 16;
-    for (uint32_t i = lane; i < n16; i += 32) d[i] = s[i];
+    for (uint32_t i = lane; i < n16; i += 32) {
+      const uint4 v = s[i];
+      d[i] = v;
+      if (m.ck != nullptr) ck_word4(v, m.msg_off + static_cast<long long>(doff) + 16ll * i, s1, s2);
+    }
   }
-  if (counter != nullptr) {
+  if (m.ck != nullptr) ck_flush(m.ck, s1, s2);
+  if (m.counter != nullptr) {
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t done = atomicAdd(counter, 1u);
-      if (done == gridDim.x - 1) {
-        __threadfence_system();
-        st_release_sys(flag, flag_value);
-        *counter = 0;
-      }
-    }
+    if (threadIdx.x == 0)
+      last_cta_publish(m.counter, gridDim.x, m.ck, m.trailer, m.flag, m.flag_value);
   }
 }
 
@@ -433,23 +477,32 @@ uint64_t kvs_rans_staging_bytes(uint64_t n, uint32_t cs) {
 }
 
 // Encode n bytes into `out` (capacity kvs_rans_max_bytes).  `sizes` holds
-// 2*n_chunks uint32 (record offsets and lengths).  The stream size is
-// written to *total_out (device).  counter/flag (optional) publish
-// completion to a consumer polling `flag`.
+// 4*n_chunks uint32 (record offsets, lengths and the 64-bit output
+// offsets).  The stream size is written to *total_out (device).  `msg`
+// (host pointer, may be null) places the stream inside a transfer message:
+// container header, checksum, and the ready flag published by the last CTA.
 int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging, uint32_t* sizes,
-                    uint8_t* out, uint64_t* total_out, uint32_t* counter, uint32_t* flag,
-                    uint32_t flag_value, void* stream) {
+                    uint8_t* out, uint64_t* total_out, const RansMsg* msg, void* stream) {
   if (n == 0 || cs == 0 || cs % kSuper != 0) return -2;
+  RansMsg m{};
+  if (msg != nullptr) m = *msg;
+  if ((m.msg_off & 15) != 0) return -2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint32_t nc = num_chunks(n, cs);
   uint32_t* rec_off = sizes;
   uint32_t* rec_len = sizes + nc;
+  uint64_t* dst_off = reinterpret_cast<uint64_t*>(sizes + 2 * nc);  // 8-byte aligned
   k_rans_encode<<<(nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32, 0, s>>>(in, n, cs, staging,
                                                                             rec_off, rec_len, nc);
-  k_rans_directory<<<1, 1024, 0, s>>>(rec_len, nc, n, cs, out, total_out);
-  k_rans_copy<<<(nc + 7) / 8, 256, 0, s>>>(staging, rec_off, rec_len, nc, cs, out, counter, flag,
-                                           flag_value);
+  k_rans_directory<<<1, 1024, 0, s>>>(rec_len, nc, n, cs, out, total_out, dst_off, m);
+  k_rans_copy<<<(nc + 7) / 8, 256, 0, s>>>(staging, rec_off, rec_len, dst_off, nc, cs, out, m);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kvs_rans_msg_size(void) { return static_cast<int>(sizeof(RansMsg)); }
+// uint32 words of the `sizes` scratch for n bytes in chunks of cs.
+uint64_t kvs_rans_sizes_words(uint64_t n, uint32_t cs) {
+  return 4ull * num_chunks(n, cs);
 }
 
 // Decode n bytes from a stream of `len` bytes (~0: unknown, the header's
@@ -475,6 +528,7 @@ int kvs_rans_decode(const uint8_t* stream_buf, uint64_t len, uint8_t* out, uint6
 // ===================================================================
 #include <cstdio>
 #include <mutex>
+#include <utility>
 
 #include "kvs_noalloc.h"
 
@@ -488,12 +542,17 @@ constexpr uint32_t kNoAllocMaxChunks =
 
 static __device__ __align__(256) uint8_t g_noalloc_staging[kNoAllocMaxChunks *
                                                            slot_bytes(kNoAllocChunk)];
-static __device__ __align__(256) uint32_t g_noalloc_sizes[2 * kNoAllocMaxChunks];
+// record offsets, record lengths, 64-bit output offsets (kvs_rans_encode's layout)
+static __device__ __align__(256) uint32_t g_noalloc_sizes[4 * kNoAllocMaxChunks];
 static __device__ __align__(256) uint64_t g_noalloc_total[2];
 
-// Device addresses of the scratch arrays, looked up once per device with
-// that device current (host code may not pass the array names themselves:
-// on the host they are stand-ins, not device addresses).
+// Device addresses of the scratch arrays, looked up with the context that
+// is current at the call (host code may not pass the array names
+// themselves: on the host they are stand-ins, not device addresses).  The
+// arrays live in the library's module, which is loaded once per context, so
+// the cache is keyed on the context's unique id: a new context on the same
+// device (after cudaDeviceReset, or a driver-API context made current by
+// the caller) gets its own lookup instead of a stale address.
 struct NoAllocScratch {
   uint8_t* staging;
   uint32_t* sizes;
@@ -501,15 +560,46 @@ struct NoAllocScratch {
 };
 constexpr int kNoAllocMaxDevices = 64;
 static NoAllocScratch g_noalloc_addr[kNoAllocMaxDevices];
-static bool g_noalloc_ready[kNoAllocMaxDevices];
+static unsigned long long g_noalloc_ctx[kNoAllocMaxDevices];  // context id of the entry, 0 = none
 static std::mutex g_noalloc_mu;
+
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+// Unique id of the current context (0 when it cannot be read).  Driver entry
+// points are fetched through the runtime, so the library keeps no link-time
+// dependency on libcuda.
+static unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    tried = true;
+  }
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_cur == nullptr || get_id == nullptr || get_cur(&ctx) != 0 || ctx == nullptr ||
+      get_id(ctx, &id) != 0)
+    return 0;
+  return id;
+}
 
 static int noalloc_scratch(NoAllocScratch* out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
     return KVS_NOALLOC_NO_DEVICE;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ready[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (ctx == 0 || g_noalloc_ctx[dev] != ctx) {
     NoAllocScratch s{nullptr, nullptr, nullptr};
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.staging), g_noalloc_staging) !=
             cudaSuccess ||
@@ -517,14 +607,31 @@ static int noalloc_scratch(NoAllocScratch* out) {
             cudaSuccess ||
         cudaGetSymbolAddress(reinterpret_cast<void**>(&s.total), g_noalloc_total) !=
             cudaSuccess) {
-      cudaGetLastError();
+      cudaGetLastError();  // the failed lookup's own error
       return KVS_NOALLOC_SYMBOL;
     }
     g_noalloc_addr[dev] = s;
-    g_noalloc_ready[dev] = true;
+    // the lookup made the device's primary context current if no context
+    // was; an id that cannot be read (0) means a new lookup on every call
+    g_noalloc_ctx[dev] = current_context_id();
   }
   *out = g_noalloc_addr[dev];
   return KVS_NOALLOC_OK;
+}
+
+// One launch whose own error is returned (cudaLaunchKernelEx reports the
+// error of this launch; an unrelated earlier error stays where it is).
+template <typename... KArgs, typename... Args>
+static cudaError_t noalloc_launch(void (*kernel)(KArgs...), unsigned grid, unsigned block,
+                                  cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace rans
@@ -553,12 +660,21 @@ int kvs_rans_encode_noalloc(const uint8_t* in, uint64_t n, uint8_t* out, uint64_
   const uint32_t nc = num_chunks(n, kNoAllocChunk);
   uint32_t* rec_off = s.sizes;
   uint32_t* rec_len = s.sizes + nc;
-  k_rans_encode<<<(nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32, 0, st>>>(
-      in, n, kNoAllocChunk, s.staging, rec_off, rec_len, nc);
-  k_rans_directory<<<1, 1024, 0, st>>>(rec_len, nc, n, kNoAllocChunk, out, s.total);
-  k_rans_copy<<<(nc + 7) / 8, 256, 0, st>>>(s.staging, rec_off, rec_len, nc, kNoAllocChunk, out,
-                                            nullptr, nullptr, 0u);
-  return cudaGetLastError() == cudaSuccess ? KVS_NOALLOC_OK : KVS_NOALLOC_LAUNCH;
+  uint64_t* dst_off = reinterpret_cast<uint64_t*>(s.sizes + 2 * nc);
+  const RansMsg none{};
+  cudaError_t e = noalloc_launch(k_rans_encode, (nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32,
+                                 st, in, n, kNoAllocChunk, s.staging, rec_off, rec_len, nc);
+  if (e == cudaSuccess)
+    e = noalloc_launch(k_rans_directory, 1, 1024, st, rec_len, nc, n, kNoAllocChunk, out,
+                       s.total, dst_off, none);
+  if (e == cudaSuccess)
+    e = noalloc_launch(k_rans_copy, (nc + 7) / 8, 256, st, s.staging, rec_off, rec_len, dst_off,
+                       nc, kNoAllocChunk, out, none);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // this call's launch error, reported through the return code
+    return KVS_NOALLOC_LAUNCH;
+  }
+  return KVS_NOALLOC_OK;
 }
 
 const char* kvs_noalloc_strerror(int code) {

@@ -71,42 +71,54 @@ __global__ void __launch_bounds__(256) k_copy16(const uint4* __restrict__ src, u
   }
 }
 
+
 // Gather-copy of several byte ranges (any sizes and 16-byte aligned
 // destinations) in one launch: grid.y = segment.  The last CTA to finish
 // publishes `flag_value` into `flag` after a system-scope fence, so a
-// consumer on another GPU that observes the flag sees every segment.
+// consumer on another GPU that observes the flag sees every segment.  With
+// `ck` the copy also sums the message checksum of what it writes (segment
+// bytes at message offset msg_off, as defined in common.cuh), and
+// the last CTA stores the finished sums to `trailer` before the flag.
 struct CopySeg {
   const uint8_t* src;
   uint8_t* dst;
   long long bytes;
+  long long msg_off;  // message offset of dst[0] (checksum weights)
 };
 
 __global__ void __launch_bounds__(256) k_copy_segments(const CopySeg* __restrict__ segs,
                                                        uint32_t* counter, uint32_t* flag,
-                                                       uint32_t flag_value) {
+                                                       uint32_t flag_value, unsigned long long* ck,
+                                                       unsigned long long* trailer) {
   const CopySeg sg = segs[blockIdx.y];
-  const bool aligned = ((reinterpret_cast<uintptr_t>(sg.src) | reinterpret_cast<uintptr_t>(sg.dst)) & 15) == 0;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(sg.src) | reinterpret_cast<uintptr_t>(sg.dst) |
+                         static_cast<uintptr_t>(sg.msg_off)) & 15) == 0;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  unsigned long long s1 = 0, s2 = 0;
   if (aligned) {
     const long long n16 = sg.bytes / 16;
-    for (long long i = tid; i < n16; i += stride)
-      reinterpret_cast<uint4*>(sg.dst)[i] = reinterpret_cast<const uint4*>(sg.src)[i];
-    for (long long i = n16 * 16 + tid; i < sg.bytes; i += stride) sg.dst[i] = sg.src[i];
+    for (long long i = tid; i < n16; i += stride) {
+      const uint4 v = reinterpret_cast<const uint4*>(sg.src)[i];
+      reinterpret_cast<uint4*>(sg.dst)[i] = v;
+      if (ck != nullptr) ck_word4(v, sg.msg_off + 16 * i, s1, s2);
+    }
+    for (long long i = n16 * 16 + tid; i < sg.bytes; i += stride) {
+      sg.dst[i] = sg.src[i];
+      if (ck != nullptr) ck_byte(sg.src[i], sg.msg_off + i, s1, s2);
+    }
   } else {
-    for (long long i = tid; i < sg.bytes; i += stride) sg.dst[i] = sg.src[i];
+    for (long long i = tid; i < sg.bytes; i += stride) {
+      sg.dst[i] = sg.src[i];
+      if (ck != nullptr) ck_byte(sg.src[i], sg.msg_off + i, s1, s2);
+    }
   }
+  if (ck != nullptr) ck_flush(ck, s1, s2);
   __threadfence_system();
   if (counter != nullptr) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t done = atomicAdd(counter, 1u);
-      if (done == gridDim.x * gridDim.y - 1) {
-        __threadfence_system();
-        st_release_sys(flag, flag_value);
-        *counter = 0;
-      }
-    }
+    if (threadIdx.x == 0)
+      last_cta_publish(counter, gridDim.x * gridDim.y, ck, trailer, flag, flag_value);
   }
 }
 
@@ -154,51 +166,38 @@ __global__ void __launch_bounds__(512) k_probe_push(const uint4* __restrict__ sr
 }
 
 
-// Message checksum: over the bytes b_p of a message (p = offset inside the
-// message), S1 = sum_p b_p * 2^(8*(p%4)) and S2 = sum_p (p/4 + 1) * b_p *
-// 2^(8*(p%4)), both mod 2^64 -- i.e. the plain and the position-weighted sums
-// of the message's little-endian 32-bit words.  Integer sums are
-// order-independent, so any grid computes the same value.  A segment is
-// (src, message offset, bytes).
+// Segment of a message checksum (the definition is in common.cuh):
+// (src, message offset, bytes); with `len_ptr` set the length is
+// min(bytes, *len_ptr + len_add), read on the device (a coded stream whose
+// size is recorded in its own header).
 struct CkSeg {
   const uint8_t* src;
   long long off;
   long long bytes;
+  const unsigned long long* len_ptr;
+  long long len_add;
 };
-
-KVS_DEV void ck_byte(uint8_t b, long long p, unsigned long long& s1, unsigned long long& s2) {
-  const unsigned long long v = static_cast<unsigned long long>(b) << (8 * (p & 3));
-  s1 += v;
-  s2 += static_cast<unsigned long long>((p >> 2) + 1) * v;
-}
 
 __global__ void __launch_bounds__(256) k_checksum(const CkSeg* __restrict__ segs,
                                                   unsigned long long* out) {
   const CkSeg sg = segs[blockIdx.y];
+  long long bytes = sg.bytes;
+  if (sg.len_ptr != nullptr) {
+    const unsigned long long dyn = *sg.len_ptr + static_cast<unsigned long long>(sg.len_add);
+    if (dyn < static_cast<unsigned long long>(bytes)) bytes = static_cast<long long>(dyn);
+  }
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   unsigned long long s1 = 0, s2 = 0;
   if (((reinterpret_cast<uintptr_t>(sg.src) | static_cast<uintptr_t>(sg.off)) & 15) == 0) {
-    const long long n16 = sg.bytes / 16;
-    for (long long i = tid; i < n16; i += stride) {
-      const uint4 v = reinterpret_cast<const uint4*>(sg.src)[i];
-      const unsigned long long w = static_cast<unsigned long long>((sg.off >> 2) + 4 * i + 1);
-      s1 += static_cast<unsigned long long>(v.x) + v.y + v.z + v.w;
-      s2 += w * v.x + (w + 1) * v.y + (w + 2) * v.z + (w + 3) * v.w;
-    }
-    for (long long i = n16 * 16 + tid; i < sg.bytes; i += stride) ck_byte(sg.src[i], sg.off + i, s1, s2);
+    const long long n16 = bytes / 16;
+    for (long long i = tid; i < n16; i += stride)
+      ck_word4(reinterpret_cast<const uint4*>(sg.src)[i], sg.off + 16 * i, s1, s2);
+    for (long long i = n16 * 16 + tid; i < bytes; i += stride) ck_byte(sg.src[i], sg.off + i, s1, s2);
   } else {
-    for (long long i = tid; i < sg.bytes; i += stride) ck_byte(sg.src[i], sg.off + i, s1, s2);
+    for (long long i = tid; i < bytes; i += stride) ck_byte(sg.src[i], sg.off + i, s1, s2);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, o);
-    s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
-  }
-  if ((threadIdx.x & 31) == 0 && (s1 | s2)) {
-    atomicAdd(out, s1);
-    atomicAdd(out + 1, s2);
-  }
+  ck_flush(out, s1, s2);
 }
 
 // ------------------------------------------------------- raw paged transfer
@@ -280,42 +279,17 @@ __global__ void __launch_bounds__(256) k_paged_raw(const RawLaunch a) {
         const int i = i0 + k * blockDim.x;
         if (i < n16) {
           dst[i] = v[k];
-          if (a.ck != nullptr) {
-            const unsigned long long w = static_cast<unsigned long long>((foff >> 2) + 4 * i + 1);
-            s1 += static_cast<unsigned long long>(v[k].x) + v[k].y + v[k].z + v[k].w;
-            s2 += w * v[k].x + (w + 1) * v[k].y + (w + 2) * v[k].z + (w + 3) * v[k].w;
-          }
+          if (a.ck != nullptr) ck_word4(v[k], foff + 16ll * i, s1, s2);
         }
       }
     }
   }
-  if (a.ck != nullptr) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, o);
-      s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
-    }
-    if ((threadIdx.x & 31) == 0 && (s1 | s2)) {
-      atomicAdd(a.ck, s1);
-      atomicAdd(a.ck + 1, s2);
-    }
-  }
+  if (a.ck != nullptr) ck_flush(a.ck, s1, s2);
   if (a.counter != nullptr) {
     __threadfence_system();  // this thread's stores (peer ones included) and sums first
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t done = atomicAdd(a.counter, 1u);
-      if (done == gridDim.x - 1) {
-        __threadfence();
-        if (a.trailer != nullptr && a.ck != nullptr) {
-          a.trailer[0] = atomicAdd(a.ck, 0ull);  // coherent reads of the finished sums
-          a.trailer[1] = atomicAdd(a.ck + 1, 0ull);
-        }
-        __threadfence_system();
-        if (a.flag != nullptr) st_release_sys(a.flag, a.flag_value);
-        *a.counter = 0;
-      }
-    }
+    if (threadIdx.x == 0)
+      last_cta_publish(a.counter, gridDim.x, a.ck, a.trailer, a.flag, a.flag_value);
   }
 }
 
@@ -357,8 +331,6 @@ int kvs_copy16(const void* src, void* dst, long long bytes, uint32_t* counter, u
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-// segs: device array of n CopySeg {src, dst, bytes}.
-
 // Checksum of `n` segments (device array of CkSeg) into out[2] (device).
 int kvs_checksum(const void* segs, int n, unsigned long long* out, int blocks_per_seg,
                  void* stream) {
@@ -379,11 +351,22 @@ int kvs_checksum_verify(const void* segs, int n, const unsigned long long* expec
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+// segs: device array of n CopySeg {src, dst, bytes, msg_off}.  With `ck`
+// (int64[2] accumulators, zeroed by the caller) the copy adds the checksum
+// of the written bytes; `trailer` then receives the finished sums from the
+// last CTA before it publishes the flag.
 int kvs_copy_segments(const void* segs, int n, int blocks_per_seg, uint32_t* counter,
-                      uint32_t* flag, uint32_t flag_value, void* stream) {
+                      uint32_t* flag, uint32_t flag_value, unsigned long long* ck,
+                      unsigned long long* trailer, void* stream) {
   if (n <= 0) return 0;
   k_copy_segments<<<dim3(blocks_per_seg, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const CopySeg*>(segs), counter, flag, flag_value);
+      static_cast<const CopySeg*>(segs), counter, flag, flag_value, ck, trailer);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Zero two int64 accumulators (checksum) on the stream.
+int kvs_zero2(unsigned long long* p, void* stream) {
+  k_zero2<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

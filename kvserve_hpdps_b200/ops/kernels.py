@@ -784,7 +784,7 @@ def set_trace(device: Optional[torch.device], jobs_per_cta: int = 256) -> Option
 
 
 def _launch(slots: LayerSlots, items: WorkItems, bmat: torch.Tensor, codes, meta, kstat, vstat,
-            engine: int) -> LayerLaunch:
+            engine: int, ck: Optional[torch.Tensor] = None, ck_off: int = 0) -> LayerLaunch:
     dev = slots.device
     L = LayerLaunch()
     L.kvs = slots._kvs.data_ptr()
@@ -805,14 +805,22 @@ def _launch(slots: LayerSlots, items: WorkItems, bmat: torch.Tensor, codes, meta
     if _trace["buf"] is not None:
         L.trace = _trace["buf"].data_ptr()
         L.trace_jobs = _trace["jobs"]
+    if ck is not None:
+        L.ck = ck.data_ptr()
+        L.ck_off = int(ck_off)
     return L
 
 
 def quantize(slots: LayerSlots, items: WorkItems, codes: Optional[torch.Tensor] = None,
-             meta: Optional[torch.Tensor] = None,
-             engine: int = ENGINE_TCGEN05) -> tuple[torch.Tensor, torch.Tensor]:
-    """Quantize every work item (layer, request) in three launches; returns
-    (codes u8, meta u8) laid out as described by ``items``."""
+             meta: Optional[torch.Tensor] = None, engine: int = ENGINE_TCGEN05,
+             ck: Optional[torch.Tensor] = None,
+             ck_off: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantize every work item (layer, request) in four launches; returns
+    (codes u8, meta u8) laid out as described by ``items``.  ``codes`` may
+    be a view of a peer GPU's receive ring (the quantize kernel's own 16-byte
+    stores write it over NVLink); with ``ck`` (int64[2] on the device, engine
+    0) the kernel adds the message checksum of the code bytes it stores,
+    ``ck_off`` being the message offset of ``codes[0]``."""
     dev = slots.device
     ws = workspace(dev)
     if codes is None:
@@ -822,7 +830,7 @@ def quantize(slots: LayerSlots, items: WorkItems, codes: Optional[torch.Tensor] 
     n_pairs = items.num_items * slots.num_heads * HEAD_DIM
     kstat = ws.buf("kstat", 8 * n_pairs, torch.int32)
     vstat = ws.buf("vstat", 8 * items.total_rows * slots.num_heads, torch.float32)
-    L = _launch(slots, items, slots.bmat_fwd, codes, meta, kstat, vstat, engine)
+    L = _launch(slots, items, slots.bmat_fwd, codes, meta, kstat, vstat, engine, ck, ck_off)
     lb = lib()
     check(lb.kvs_init_key_stats(kstat.data_ptr(), n_pairs, L.stream), "init_key_stats")
     check(lb.kvs_stats(ctypes.byref(L)), "stats")
@@ -945,14 +953,18 @@ def rans_encode(data: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: i
         out = torch.empty(cap, dtype=torch.uint8, device=dev)
     elif out.numel() < cap:
         raise ValueError(f"output buffer too small ({out.numel()} < {cap})")
-    nchunks = (n + chunk - 1) // chunk
     staging = ws.buf("rans_staging", int(lb.kvs_rans_staging_bytes(n, chunk)))
-    sizes = ws.buf("rans_sizes", 8 * nchunks, torch.int32)
+    sizes = ws.buf("rans_sizes", 4 * int(lb.kvs_rans_sizes_words(n, chunk)), torch.int32)
     total = ws.buf("rans_total", 8, torch.int64)
-    counter = ws.counters[0:1] if flag is not None else None
+    msg = None
+    if flag is not None:
+        msg = _lib.RansMsg()
+        msg.counter = ws.counters[0:1].data_ptr()
+        msg.flag, msg.flag_value = flag.data_ptr(), flag_value & 0xFFFFFFFF
     check(lb.kvs_rans_encode(src.data_ptr(), n, chunk, staging.data_ptr(), sizes.data_ptr(),
-                             out.data_ptr(), total.data_ptr(), _ptr(counter), _ptr(flag),
-                             flag_value, _stream(dev)), "rans_encode")
+                             out.data_ptr(), total.data_ptr(),
+                             ctypes.byref(msg) if msg is not None else None, _stream(dev)),
+          "rans_encode")
     if trim:
         _xfer["d2h"] += 8
         return out[:int(total[0].item())]
@@ -991,16 +1003,46 @@ def rans_encode_ptr(src_ptr: int, n: int, out_ptr: int, device: torch.device,
     :func:`rans_max_bytes`; may be a peer GPU's buffer).  With ``flag_ptr``
     the last CTA publishes ``flag_value`` there after a system-scope fence.
     No host synchronisation."""
+    rans_encode_message(src_ptr, n, out_ptr, device, flag_ptr=flag_ptr, flag_value=flag_value,
+                        chunk=chunk)
+
+
+def rans_encode_message(src_ptr: int, n: int, out_ptr: int, device: torch.device,
+                        total: Optional[torch.Tensor] = None,
+                        prefix: Optional[Sequence[int]] = None, msg_off: int = 0,
+                        ck: Optional[torch.Tensor] = None, trailer_ptr: Optional[int] = None,
+                        flag_ptr: Optional[int] = None, flag_value: int = 0,
+                        chunk: int = RANS_CHUNK) -> None:
+    """Encode ``n`` device bytes at ``src_ptr`` straight into a transfer
+    message: the stream is written at ``out_ptr`` (capacity
+    :func:`rans_max_bytes`; may be a peer GPU's receive ring, reached by this
+    framework's own stores), ``prefix`` (four uint32) is stored in the 16
+    bytes before it (the container header), ``total`` (int64[1] on the
+    device) receives the stream size, ``ck`` (int64[2], zeroed) accumulates
+    the message checksum of everything written (``msg_off`` = message
+    offset of ``out_ptr``, a multiple of 16), and the last CTA stores the
+    finished checksum to ``trailer_ptr`` and publishes ``flag_value`` at
+    ``flag_ptr`` (release, system scope).  Three launches, no host
+    synchronisation."""
     lb = lib()
     ws = workspace(device)
-    nchunks = (n + chunk - 1) // chunk
     staging = ws.buf("rans_staging", int(lb.kvs_rans_staging_bytes(n, chunk)))
-    sizes = ws.buf("rans_sizes", 8 * nchunks, torch.int32)
-    total = ws.buf("rans_total", 8, torch.int64)
-    counter = ws.counters[3:4].data_ptr() if flag_ptr is not None else None
+    sizes = ws.buf("rans_sizes", 4 * int(lb.kvs_rans_sizes_words(n, chunk)), torch.int32)
+    if total is None:
+        total = ws.buf("rans_total", 8, torch.int64)
+    m = _lib.RansMsg()
+    if prefix is not None:
+        for i, w in enumerate(prefix):
+            m.prefix[i] = int(w) & 0xFFFFFFFF
+        m.has_prefix = 1
+    m.msg_off = int(msg_off)
+    m.ck = _ptr(ck)
+    m.trailer = trailer_ptr if ck is not None else None
+    if flag_ptr is not None:
+        m.counter = ws.counters[3:4].data_ptr()
+        m.flag, m.flag_value = flag_ptr, flag_value & 0xFFFFFFFF
     check(lb.kvs_rans_encode(src_ptr, n, chunk, staging.data_ptr(), sizes.data_ptr(), out_ptr,
-                             total.data_ptr(), counter, flag_ptr, flag_value, _stream(device)),
-          "rans_encode")
+                             total.data_ptr(), ctypes.byref(m), _stream(device)), "rans_encode")
 
 
 def rans_decode_ptr(stream_ptr: int, n: int, out_ptr: int, device: torch.device,
@@ -1059,14 +1101,19 @@ def _grid_per_seg(segs: Sequence[tuple[int, int, int]], floor: int) -> int:
     return int(max(floor, min(1184, big >> 18)))
 
 
-def copy_segments(segments: Sequence[tuple[int, int, int]], device: torch.device,
+def copy_segments(segments: Sequence[Sequence[int]], device: torch.device,
                   flag_ptr: Optional[int] = None, flag_value: int = 0,
-                  blocks_per_seg: Optional[int] = None) -> None:
-    """Copy several (src_ptr, dst_ptr, nbytes) ranges in one launch on the
-    current stream; destinations may be peer memory.  With ``flag_ptr``, the
-    last CTA publishes ``flag_value`` there (release, system scope) after
-    every segment is written."""
-    segs = [s for s in segments if s[2] > 0]
+                  blocks_per_seg: Optional[int] = None, ck: Optional[torch.Tensor] = None,
+                  trailer_ptr: Optional[int] = None) -> None:
+    """Copy several (src_ptr, dst_ptr, nbytes[, msg_off]) ranges in one launch
+    on the current stream; destinations may be peer memory.  With ``ck``
+    (int64[2] on the device, zeroed by the caller or added to by earlier
+    kernels of the same message) the copy adds the message checksum of the
+    bytes it writes at message offset ``msg_off``; with ``flag_ptr``, the
+    last CTA stores the finished checksum to ``trailer_ptr`` (when both are
+    given) and publishes ``flag_value`` (release, system scope) after every
+    segment is written."""
+    segs = [tuple(s) + (0,) * (4 - len(s)) for s in segments if s[2] > 0]
     if not segs:
         if flag_ptr is not None:
             set_flag(flag_ptr, flag_value, device)
@@ -1081,24 +1128,34 @@ def copy_segments(segments: Sequence[tuple[int, int, int]], device: torch.device
     if blocks_per_seg is None:
         blocks_per_seg = _grid_per_seg(segs, 32)
     check(lib().kvs_copy_segments(dev_segs.data_ptr(), len(segs), blocks_per_seg, counter,
-                                  flag_ptr, flag_value, _stream(device)), "copy_segments")
+                                  flag_ptr, flag_value, _ptr(ck),
+                                  trailer_ptr if ck is not None else None, _stream(device)),
+          "copy_segments")
     # dev_segs may be freed now: the caching allocator only reuses its block
     # for work ordered after this launch on the same stream.
 
 
-def _ck_segments(segments: Sequence[tuple[int, int, int]], device: torch.device) -> torch.Tensor:
-    host = torch.tensor([v for s in segments for v in s] or [0, 0, 0], dtype=torch.int64)
+def zero_checksum(ck: torch.Tensor) -> None:
+    """Zero the int64[2] checksum accumulators on the current stream."""
+    check(lib().kvs_zero2(ck.data_ptr(), _stream(ck.device)), "zero2")
+
+
+def _ck_segments(segments: Sequence[Sequence[int]], device: torch.device) -> torch.Tensor:
+    rows = [tuple(s) + (0,) * (5 - len(s)) for s in segments] or [(0, 0, 0, 0, 0)]
+    host = torch.tensor([v for s in rows for v in s], dtype=torch.int64)
     if device.type == "cuda":
         host = host.pin_memory()
         _xfer["h2d"] += host.numel() * 8
     return host.to(device, non_blocking=True)
 
 
-def checksum(segments: Sequence[tuple[int, int, int]], out: torch.Tensor,
+def checksum(segments: Sequence[Sequence[int]], out: torch.Tensor,
              blocks_per_seg: Optional[int] = None) -> None:
-    """Message checksum of (src_ptr, message_offset, nbytes) segments into
-    ``out`` (int64[2] on the device): the plain and the position-weighted
-    sums of the message's little-endian 32-bit words, mod 2^64."""
+    """Message checksum of (src_ptr, message_offset, nbytes[, len_ptr,
+    len_add]) segments into ``out`` (int64[2] on the device): the plain and
+    the position-weighted sums of the message's little-endian 32-bit words,
+    mod 2^64.  A segment with ``len_ptr`` (device address of a uint64) is
+    ``min(nbytes, *len_ptr + len_add)`` bytes long, read on the device."""
     segs = [s for s in segments if s[2] > 0]
     dev = out.device
     d = _ck_segments(segs, dev)
@@ -1108,11 +1165,12 @@ def checksum(segments: Sequence[tuple[int, int, int]], out: torch.Tensor,
                              _stream(dev)), "checksum")
 
 
-def verify_checksum(segments: Sequence[tuple[int, int, int]], expected_ptr: int,
+def verify_checksum(segments: Sequence[Sequence[int]], expected_ptr: int,
                     device: torch.device, blocks_per_seg: Optional[int] = None) -> None:
-    """Recompute the checksum of ``segments`` on ``device`` and record
-    ERR_CORRUPT in the device error word when it differs from the int64[2]
-    at ``expected_ptr`` (device memory).  Nothing waits on the host."""
+    """Recompute the checksum of ``segments`` (as :func:`checksum`) on
+    ``device`` and record ERR_CORRUPT in the device error word when it
+    differs from the int64[2] at ``expected_ptr`` (device memory).  Nothing
+    waits on the host."""
     segs = [s for s in segments if s[2] > 0]
     d = _ck_segments(segs, device)
     ws = workspace(device)

@@ -113,3 +113,27 @@ class ConsumerChannel:
 
     def close(self) -> None:
         self.sock.close(0)
+
+
+def _takes_nbytes(fn) -> bool:
+    import inspect
+    try:
+        params = inspect.signature(fn).parameters.values()
+    except (TypeError, ValueError):
+        return False
+    return any(p.name == "nbytes" or p.kind == p.VAR_KEYWORD for p in params)
+
+
+def notify_sent(listeners, request_id: str, transfer_ids: list, latency_ms: float,
+                nbytes: int, log) -> None:
+    """Call every sent listener ``fn(request_id, transfer_ids, latency_ms)``;
+    listeners that accept an ``nbytes`` keyword also get the bytes that
+    crossed the link.  A failing listener is logged, not raised."""
+    for fn in list(listeners):
+        try:
+            if _takes_nbytes(fn):
+                fn(request_id, list(transfer_ids), latency_ms, nbytes=nbytes)
+            else:
+                fn(request_id, list(transfer_ids), latency_ms)
+        except Exception as e:  # noqa: BLE001
+            log.error("sent listener failed: %s", e)

@@ -47,7 +47,7 @@ from typing import Any, Optional
 import torch
 
 from kvserve_hpdps_b200.parallel.control import (ACK_OK, ACK_REFUSED, ConsumerChannel,
-                                                 ProducerChannel, channel_port)
+                                                 ProducerChannel, channel_port, notify_sent)
 from kvserve_hpdps_b200.utils.logger import get_logger
 from kvserve_hpdps_b200.utils.stats import write_transfer_stats
 
@@ -76,6 +76,39 @@ def make_pair_group(host: str, port: int, rank: int, backend: str, timeout_s: fl
     else:
         pg = dist.ProcessGroupGloo(store, rank, 2, datetime.timedelta(seconds=timeout_s))
     return pg, store
+
+
+def _deferred_codec(meta: Any) -> Optional[str]:
+    inner = meta.get("metadata") if isinstance(meta, dict) else None
+    return inner.get("deferred_codec") if isinstance(inner, dict) else None
+
+
+def _encode_deferred(meta: dict, body: list[torch.Tensor],
+                     device: torch.device) -> tuple[dict, list[torch.Tensor]]:
+    """Entropy-code a message body the producer left as plain codes
+    (``deferred_codec`` in its metadata) and return the wire metadata and
+    body of the coded message: the 16-byte container header and the stream,
+    trimmed to the stream's own length (read back here, off the engine
+    thread).  The consumer then decodes it like any coded body."""
+    from kvserve_hpdps_b200.compression.codec import encode_bytes
+    inner = dict(meta["metadata"])
+    codec = inner.pop("deferred_codec")
+    inner.pop("container", None)
+    codes = torch.cat([t.contiguous().view(torch.uint8).reshape(-1) for t in body]) \
+        if len(body) > 1 else body[0].contiguous().view(torch.uint8).reshape(-1)
+    if device.type == "cuda":
+        with torch.cuda.device(device):
+            stream = torch.cuda.current_stream(device)
+            coded = encode_bytes(codes, codec)  # reads the size back: a sync on this thread
+            stream.synchronize()
+    else:
+        coded = encode_bytes(codes, codec)
+    out = dict(meta)
+    out["metadata"] = inner
+    out["body_mode"] = "single"
+    out["body_spec"] = tensor_spec(coded)
+    out["compressed_size"] = int(coded.numel())
+    return out, [coded]
 
 
 class NcclTransport:
@@ -145,7 +178,8 @@ class NcclTransport:
             return self._sent.get(transfer_id, 0)
 
     def add_sent_listener(self, fn) -> None:
-        """``fn(request_id, transfer_ids, latency_ms)`` after each message left."""
+        """``fn(request_id, transfer_ids, latency_ms)`` after each message left
+        (with an ``nbytes`` keyword, when it takes one: the bytes sent)."""
         self._listeners.append(fn)
 
     def failed_layers(self, transfer_id: str) -> int:
@@ -209,6 +243,13 @@ class NcclTransport:
             tensors = [t]
         else:
             meta, body, aux = payload
+            if _deferred_codec(meta) is not None:
+                # codes left for the transport to encode: encode them here, on the
+                # send thread, and send only the stream's own bytes
+                if event is not None:
+                    event.synchronize()
+                    event = None
+                meta, body = _encode_deferred(meta, body, self.device)
             msg = {"cmd": "PUT_BUNDLE", "request_id": request_id, "layer_names": layer_names,
                    "meta": meta, "body_specs": [tensor_spec(t) for t in body],
                    "aux_specs": [tensor_spec(t) for t in aux]}
@@ -237,11 +278,8 @@ class NcclTransport:
         now = time.monotonic()
         write_transfer_stats(request_id, (now - t0) * 1e3, nbytes,
                              transport="nccl" if self.backend == "nccl" else self.backend)
-        for fn in list(self._listeners):
-            try:
-                fn(request_id, list(member_tids or [request_id]), (now - t_enqueued) * 1e3)
-            except Exception as e:  # noqa: BLE001
-                logger.error("sent listener failed: %s", e)
+        notify_sent(self._listeners, request_id, list(member_tids or [request_id]),
+                    (now - t_enqueued) * 1e3, nbytes, logger)
         return True
 
     # ------------------------------------------------------------ consumer

@@ -35,12 +35,13 @@ import queue
 import threading
 import time
 from collections import defaultdict, deque
+from dataclasses import dataclass
 from typing import Any, Optional
 
 import torch
 
 from kvserve_hpdps_b200.parallel.control import (ConsumerChannel, ProducerChannel, channel_port,
-                                                 pack, unpack)
+                                                 notify_sent, pack, unpack)
 from kvserve_hpdps_b200.parallel.nccl_transport import FAILED_LAYER_NAMES, FAILED_PAYLOAD
 from kvserve_hpdps_b200.utils.logger import get_logger
 from kvserve_hpdps_b200.utils.stats import write_transfer_stats
@@ -53,6 +54,24 @@ FLAG_STRIDE = 16
 
 def _align(x: int) -> int:
     return (x + ALIGN - 1) // ALIGN * ALIGN
+
+
+@dataclass
+class RingMessage:
+    """Ring space of one message being written by producer kernels."""
+    base: int              # ring offset of the message
+    total: int             # reserved bytes (tensors, alignment, checksum trailer)
+    seq: int
+    slot: int              # ready-flag slot
+    offsets: list          # offset of each tensor inside the message
+    sizes: list            # bytes of each tensor
+    ptrs: list             # device address (consumer memory) of each tensor
+    trailer_ptr: int       # where the finished checksum goes
+    trailer_off: int       # its ring offset
+    ck: torch.Tensor       # int64[2] checksum accumulators (producer memory)
+    flag_ptr: int
+    flag_value: int
+    t0: float
 
 
 class RingAllocator:
@@ -158,7 +177,11 @@ class P2PTransport:
             self._sent: dict[str, int] = defaultdict(int)
             self._failed: dict[str, int] = defaultdict(int)
             self._listeners: list = []
-            self._pending: deque = deque()  # (event, request_id, member_tids, nbytes, t0)
+            # (done event, request_id, member_tids, nbytes, t0, ring offset)
+            self._pending: deque = deque()
+            self._aborted: list = []  # (event, ring offset, size) of uncommitted messages
+            self._unfinished: set = set()  # ring offsets whose stores may still be landing
+            self._free_after_done: dict = {}  # offset -> size, FREE seen before completion
             self._pending_cv = threading.Condition()
             self._io = threading.Thread(target=self._producer_io, daemon=True, name="kvs-p2p-io")
             self._io.start()
@@ -201,9 +224,27 @@ class P2PTransport:
                 logger.error("p2p producer io error: %s", e)
 
     def _on_free(self, regions) -> None:
-        """The consumer returned these (offset, size) ring regions: their flag
-        slots go back to the free list first (once its ring space is
-        released, an offset can belong to a new message), then the space."""
+        """The consumer returned these (offset, size) ring regions.  A region
+        whose message's own stores may still be landing (the consumer can
+        refuse a header before the producer's kernels finished, and a raw
+        or direct message's stores run on the producer's compute stream, not
+        on the transfer stream) is released only once the completion thread
+        has seen that message's done-event; the others go back at once, flag
+        slot first (once its ring space is released, an offset can belong to
+        a new message), then the space."""
+        now = []
+        with self._lock:
+            for off, size in regions:
+                off, size = int(off), int(size)
+                if off in self._unfinished:
+                    self._free_after_done[off] = size
+                else:
+                    now.append((off, size))
+        self._release_regions(now)
+
+    def _release_regions(self, regions) -> None:
+        if not regions:
+            return
         with self._lock:
             for off, _ in regions:
                 slot = self._slot_of.pop(int(off), None)
@@ -217,11 +258,22 @@ class P2PTransport:
     def _completion_loop(self) -> None:
         while not self._closed:
             with self._pending_cv:
-                while not self._pending and not self._closed:
+                while not self._pending and not self._aborted and not self._closed:
                     self._pending_cv.wait(timeout=0.2)
                 if self._closed:
                     return
-                ev, rid, tids, nbytes, t0 = self._pending[0]
+                aborted = list(self._aborted)
+                self._aborted.clear()
+                item = self._pending[0] if self._pending else None
+            for ev, off, size in aborted:  # opened, never committed: back once idle
+                ev.synchronize()
+                with self._lock:
+                    self._unfinished.discard(off)
+                    self._free_after_done.pop(off, None)
+                self._release_regions([(off, size)])
+            if item is None:
+                continue
+            ev, rid, tids, nbytes, t0, base = item
             ev.synchronize()
             with self._pending_cv:
                 self._pending.popleft()
@@ -229,13 +281,26 @@ class P2PTransport:
             with self._lock:  # a message without member ids counts for its request id
                 for t in (tids or [rid]):
                     self._sent[t] += 1
+            self._message_done(base)
+            if isinstance(nbytes, tuple):  # (device count, host addend): coded stream size
+                nbytes = int(nbytes[0].item()) + int(nbytes[1])
             ms = (time.monotonic() - t0) * 1e3
             write_transfer_stats(rid, ms, nbytes, transport="nvlink-p2p")
-            for fn in list(self._listeners):
-                try:
-                    fn(rid, list(tids or [rid]), ms)
-                except Exception as e:  # noqa: BLE001
-                    logger.error("sent listener failed: %s", e)
+            notify_sent(self._listeners, rid, list(tids or [rid]), ms, nbytes, logger)
+
+    def _message_done(self, base: int) -> None:
+        """The stores of the message at ring offset ``base`` have finished: a
+        FREE that arrived before now releases its region and slot here."""
+        with self._lock:
+            self._unfinished.discard(base)
+            late = self._free_after_done.pop(base, None)
+        if late is not None:
+            self._release_regions([(base, late)])
+
+    def _track(self, done, request_id, member_tids, nbytes, t0, base) -> None:
+        with self._pending_cv:
+            self._pending.append((done, request_id, member_tids, nbytes, t0, base))
+            self._pending_cv.notify_all()
 
     def _put(self, request_id: str, layer_names: list[str], tensors: list[torch.Tensor],
              n_body: int, meta: Optional[dict], kind: str,
@@ -258,12 +323,14 @@ class P2PTransport:
         with torch.cuda.stream(self._stream):
             self._stream.wait_event(ready)
             ck = torch.empty(2, dtype=torch.int64, device=self.device)
-            K.checksum([(t.data_ptr(), o, s) for t, o, s in zip(tensors, offs, sizes)], ck)
-            segs = [(t.data_ptr(), self._peer.ptr + base + o, s)
+            K.zero_checksum(ck)
+            # one pass: the copy over NVLink also sums the message checksum,
+            # and its last CTA stores the checksum and publishes the flag
+            segs = [(t.data_ptr(), self._peer.ptr + base + o, s, o)
                     for t, o, s in zip(tensors, offs, sizes)]
-            segs.append((ck.data_ptr(), self._peer.ptr + base + trailer, 16))
             K.copy_segments(segs, self.device, flag_ptr=self._peer.ptr + self.flag_off +
-                            slot * FLAG_STRIDE, flag_value=seq & 0xFFFFFFFF)
+                            slot * FLAG_STRIDE, flag_value=seq & 0xFFFFFFFF, ck=ck,
+                            trailer_ptr=self._peer.ptr + base + trailer)
             for t in tensors + [ck]:
                 t.record_stream(self._stream)
             done = self._stream.record_event()
@@ -273,9 +340,7 @@ class P2PTransport:
             "specs": [{"shape": list(t.shape), "dtype": str(t.dtype).replace("torch.", ""),
                        "off": base + o, "nbytes": s} for t, o, s in zip(tensors, offs, sizes)],
             "region": [base, total], "slot": slot, "seq": seq, "trailer": base + trailer})
-        with self._pending_cv:
-            self._pending.append((done, request_id, member_tids, sum(sizes), t0))
-            self._pending_cv.notify_all()
+        self._track(done, request_id, member_tids, sum(sizes), t0, base)
 
     def _reserve(self, total: int) -> tuple[int, int, int]:
         """Ring space, sequence number and flag slot of a new message.
@@ -307,7 +372,13 @@ class P2PTransport:
                                    f"({total} bytes needed)")
             self._seq += 1
             self._slot_of[base] = slot
+            self._unfinished.add(base)
             return base, self._seq, slot
+
+    def record_unsent(self, request_id: str, member_tids: Optional[list[str]],
+                      err: Exception) -> None:
+        """Count a message its producer could not send (e.g. no ring space)."""
+        self._unsent(request_id, member_tids, err)
 
     def _unsent(self, request_id: str, member_tids: Optional[list[str]], err: Exception) -> None:
         """A message that got no ring space in time is dropped (logged) and
@@ -317,6 +388,79 @@ class P2PTransport:
         with self._lock:
             for t in (member_tids or [request_id]):
                 self._failed[t] += 1
+
+    # ------------------------------------------------ direct-to-ring messages
+    def open_message(self, sizes: list[int]) -> "RingMessage":
+        """Reserve ring space for a message whose tensors (``sizes`` bytes
+        each, in order) producer kernels will write straight into the
+        consumer's ring.  Returns the device addresses to write, the message
+        checksum accumulators (zeroed on the current stream) and the ready
+        flag to publish; :meth:`commit_message` sends the header.  Raises
+        RuntimeError when no ring space or flag slot frees up in time."""
+        assert self.is_sender
+        offs, total = [], 0
+        for n in sizes:
+            offs.append(total)
+            total += _align(int(n))
+        trailer = total
+        total += ALIGN
+        base, seq, slot = self._reserve(total)
+        from kvserve_hpdps_b200.ops import kernels as K
+        ck = torch.empty(2, dtype=torch.int64, device=self.device)
+        K.zero_checksum(ck)
+        ptr = self._peer.ptr + base
+        return RingMessage(base=base, total=total, seq=seq, slot=slot, offsets=offs,
+                           sizes=[int(n) for n in sizes], ptrs=[ptr + o for o in offs],
+                           trailer_ptr=ptr + trailer, trailer_off=base + trailer, ck=ck,
+                           flag_ptr=self._peer.ptr + self.flag_off + slot * FLAG_STRIDE,
+                           flag_value=seq & 0xFFFFFFFF, t0=time.monotonic())
+
+    def view(self, msg: "RingMessage", i: int, dtype: torch.dtype = torch.uint8,
+             shape=None) -> torch.Tensor:
+        """Zero-copy tensor over tensor ``i`` of an open message (peer memory:
+        only this framework's own kernels may write or read it)."""
+        n = msg.sizes[i]
+        esz = torch.empty((), dtype=dtype).element_size()
+        return tensor_view(msg.ptrs[i], n, dtype, shape if shape is not None else [n // esz],
+                           self.local_rank)
+
+    def commit_message(self, msg: "RingMessage", request_id: str, layer_names: list[str],
+                       meta: Optional[dict], specs: list[dict], n_body: int,
+                       kind: str = "bundle", member_tids: Optional[list[str]] = None,
+                       dyn_len: Optional[dict] = None,
+                       sent_bytes: Optional[torch.Tensor] = None) -> None:
+        """Send the header of a message whose kernels have been enqueued on
+        the current stream (the last of them publishes ``msg.flag_value``).
+        ``specs`` give each tensor's shape and dtype; ``dyn_len`` = {"seg":
+        i, "len_off": o, "len_add": a} marks tensor i as a coded stream whose
+        length (read on the device at byte o of the tensor, plus a) bounds
+        the checksum; ``sent_bytes`` (int64 on the device) is the number of
+        bytes that actually crossed the link, read by the completion thread
+        for the transfer statistics."""
+        done = torch.cuda.current_stream(self.device).record_event()
+        full = []
+        for sp, off, n in zip(specs, msg.offsets, msg.sizes):
+            full.append({"shape": list(sp["shape"]), "dtype": sp["dtype"],
+                         "off": msg.base + off, "nbytes": n})
+        hdr = {"cmd": "PUT_RING", "kind": kind, "request_id": request_id,
+               "layer_names": list(layer_names), "meta": meta, "n_body": n_body,
+               "specs": full, "region": [msg.base, msg.total], "slot": msg.slot, "seq": msg.seq,
+               "trailer": msg.trailer_off}
+        if dyn_len is not None:
+            hdr["dyn_len"] = dict(dyn_len)
+        self._outbox.put(hdr)
+        nbytes = sum(msg.sizes) if sent_bytes is None else sent_bytes
+        self._track(done, request_id, member_tids, nbytes, msg.t0, msg.base)
+
+    def abort_message(self, msg: "RingMessage", request_id: str,
+                      member_tids: Optional[list[str]], err: Exception) -> None:
+        """Give up a message after :meth:`open_message` (nothing was
+        committed): its ring space and flag slot return once the work already
+        queued on the current stream has finished, and it counts as failed."""
+        done = torch.cuda.current_stream(self.device).record_event()
+        with self._pending_cv:
+            self._aborted.append((done, msg.base, msg.total))
+        self._unsent(request_id, member_tids, err)
 
     def send_paged(self, request_id: str, layer_names: list[str], kv_layers: list[torch.Tensor],
                    block_ids, member_tids: Optional[list[str]] = None) -> None:
@@ -354,9 +498,7 @@ class P2PTransport:
                        "off": base, "nbytes": nbytes}],
             "block_order": raw.block_order,
             "region": [base, total], "slot": slot, "seq": seq, "trailer": base + trailer})
-        with self._pending_cv:
-            self._pending.append((done, request_id, member_tids, nbytes, t0))
-            self._pending_cv.notify_all()
+        self._track(done, request_id, member_tids, nbytes, t0, base)
 
     def bandwidth_mbps(self, probe_bytes: int = 64 << 20, max_age_s: float = 30.0,
                        timeout_s: float = 5.0) -> Optional[float]:
@@ -413,7 +555,9 @@ class P2PTransport:
 
     def add_sent_listener(self, fn) -> None:
         """``fn(request_id, transfer_ids, latency_ms)`` on the completion thread
-        once a message's stores have finished (time from its send call)."""
+        once a message's stores have finished (time from its send call); a
+        listener that takes an ``nbytes`` keyword also gets the bytes that
+        crossed the link (for a coded stream, its exact length)."""
         self._listeners.append(fn)
 
     def failed_layers(self, transfer_id: str) -> int:
@@ -467,8 +611,8 @@ class P2PTransport:
     def _reject_put(self, msg: dict) -> None:
         """A header that cannot be turned into tensors: the request is
         reported failed at once (no wait for the load timeout) and its ring
-        region goes back to the producer, whose later stores into it queue on
-        the same transfer stream behind this message's."""
+        region goes back to the producer, which reuses it (and its flag slot)
+        only after this message's own stores have finished."""
         rid = msg.get("request_id")
         if isinstance(rid, str):
             with self._lock:
@@ -485,6 +629,13 @@ class P2PTransport:
         ring = {"slot": msg["slot"], "seq": msg["seq"], "region": tuple(msg["region"]),
                 "trailer": msg.get("trailer"),
                 "segs": [(s["off"] - msg["region"][0], s["nbytes"]) for s in msg["specs"]]}
+        dyn = msg.get("dyn_len")
+        if dyn is not None:  # a coded stream: its length is in its own header
+            i = int(dyn["seg"])
+            if not 0 <= i < len(msg["specs"]) or not 0 <= int(dyn["len_off"]) <= \
+                    msg["specs"][i]["nbytes"] - 8:
+                raise ValueError("dyn_len outside its tensor")
+            ring["dyn"] = (i, int(dyn["len_off"]), int(dyn["len_add"]))
         if msg["kind"] == "raw":
             payload = {"__ring_raw__": True, "tensor": views[0], "__ring__": ring,
                        "block_order": msg.get("block_order", "nhd")}
@@ -526,8 +677,11 @@ class P2PTransport:
                     r["seq"] & 0xFFFFFFFF, dev, timeout_s=self.flag_timeout_s)
         if r.get("trailer") is not None:  # corruption -> ERR_CORRUPT in the device error word
             base = r["region"][0]
-            K.verify_checksum([(self._region.ptr + base + o, o, n) for o, n in r["segs"]],
-                              self._region.ptr + r["trailer"], dev)
+            segs = [(self._region.ptr + base + o, o, n) for o, n in r["segs"]]
+            if r.get("dyn") is not None:  # checksum over the stream's own length only
+                i, lo, la = r["dyn"]
+                segs[i] = segs[i] + (segs[i][0] + lo, la)
+            K.verify_checksum(segs, self._region.ptr + r["trailer"], dev)
 
     def release(self, payload: Any, device: Optional[torch.device] = None) -> None:
         """Return the payload's ring space once the work queued so far on the

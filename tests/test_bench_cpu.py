@@ -23,12 +23,34 @@ def _sweep():
 def test_bench_modes_and_labels():
     a = bench.parse_args([])
     assert a.compression == "default" and bench.hybrid_ratio(a) == 0.8
-    assert bench.compression_label(a).startswith("default (Hadamard + hybrid 0.8")
+    # the headline runs the stage set both arms can run: byte codes, no entropy coder
+    assert a.codec == "none"
+    assert bench.compression_label(a) == \
+        "default mode: Hadamard + hybrid 0.8 12/8/6/4, u8 codes, no entropy codec"
+    assert bench.compression_label(a, "rans").endswith("4-bit codes + rANS")
     a = bench.parse_args(["--hybrid-ratio", "0.3", "--codec", "bitpack"])
     assert bench.quant_config(a)["quantizer_config"]["hybrid_ratio"] == 0.3
-    assert "bitpack" in bench.compression_label(a)
+    assert "bit-packed" in bench.compression_label(a)
     assert bench.compression_label(bench.parse_args(["--compression", "off"])) == \
         "off (raw bf16 blocks)"
+
+
+def test_bench_line_config_is_the_same_for_both_arms():
+    """The driver compares the two arms' ``config``: it must not depend on
+    the arm; arm-specific descriptions sit outside it."""
+    ours = bench.parse_args([])
+    ref = bench.parse_args(["--impl", "reference"])
+    res = {"ms": 80.0, "cr": 1.97, "pairs": 1, "launches": 100, "pipeline": "p",
+           "transport": "local"}
+    a = bench.build_line(ours, dict(res), 1)
+    b = bench.build_line(ref, dict(res), 1)
+    assert a["config"] == b["config"]
+    assert a["impl"] == "ours" and b["impl"] == "reference"
+    assert a["value"] == 80.0 / (20 * 8)
+    # N >= 2: value is per pair (weak scaling), aggregate throughput is separate
+    c = bench.build_line(bench.parse_args(["--gpus", "8"]), dict(res, pairs=4), 8)
+    assert c["value"] == a["value"] and c["config"]["global_batch"] == 32
+    assert abs(c["aggregate_gbps"] - 4 * a["aggregate_gbps"]) < 1.0
 
 
 def test_sweep_plan_and_report():

@@ -110,12 +110,19 @@ def _role(producer, port, compression, q):
             conn.wait_for_save()
             conn._transport.wait_for_sent(30)
             torch.cuda.synchronize()
+            time.sleep(0.5)  # the listener that writes the statistics runs on its thread
             # device-timed NVLink push bandwidth (feeds the controller)
             bw = conn._transport.bandwidth_mbps(probe_bytes=32 << 20)
             if bw is None or not 1e4 < bw < 2e6:
                 raise RuntimeError(f"implausible probe bandwidth {bw} MB/s")
             time.sleep(2.0)
-            q.put(("p", "ok"))
+            rows = []
+            path = os.environ.get("KVSERVE_COMPRESSION_STATS_PATH")
+            if path and os.path.exists(path):
+                import json
+                with open(path) as f:
+                    rows = [json.loads(line) for line in f]
+            q.put(("p", rows))
         else:
             conn.bind_connector_metadata(_meta([("d", "t", 70, blocks_c)]))
             conn.start_load_kv(None)
@@ -133,9 +140,22 @@ def _role(producer, port, compression, q):
         q.put(("err", traceback.format_exc()))
 
 
+# default-mode quantizer with one byte per code and no entropy coder
+U8 = {"enabled": True, "pipeline": ["quantizer", "codec"],
+      "quantizer_config": {"model_name": "Qwen2.5-7B-Instruct", "hybrid_ratio": 0.8,
+                           "high_key_max_value": 12, "high_value_max_value": 8,
+                           "low_key_max_value": 6, "low_value_max_value": 4},
+      "codec_config": {"codec_type": "none"}}
+
+
 @pytest.mark.multigpu
-@pytest.mark.parametrize("compression", [None, "default"])
-def test_p2p_ring_handoff_two_gpus(compression):
+@pytest.mark.parametrize("compression", [None, "default", U8], ids=["raw", "default", "u8"])
+def test_p2p_ring_handoff_two_gpus(compression, tmp_path, monkeypatch):
+    """The connector pair over the NVLink ring: raw blocks, the default mode
+    (the rANS compaction kernel stores only the coded stream into the
+    consumer's ring) and byte codes (the quantize kernel stores them into the
+    ring).  The statistics record the bytes that crossed the link."""
+    monkeypatch.setenv("KVSERVE_COMPRESSION_STATS_PATH", str(tmp_path / "comp.jsonl"))
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
@@ -156,3 +176,11 @@ def test_p2p_ring_handoff_two_gpus(compression):
     assert cos > 0.9
     if compression is None:  # raw blocks: one gather into the peer ring, one scatter
         assert exact
+        return
+    rows = results["p"]
+    assert len(rows) == 1
+    ratio = rows[0]["original_bytes"] / rows[0]["compressed_bytes"]
+    if compression == "default":  # the coded stream's own size, not the reserved worst case
+        assert ratio > 5.0, rows
+    else:  # one byte per code plus the fp16 metadata
+        assert 1.5 < ratio < 2.0, rows  # 70 of the 80 block rows hold tokens

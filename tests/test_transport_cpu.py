@@ -4,6 +4,7 @@ transport, and failure paths injected on the host (no GPU involved)."""
 import multiprocessing as mp
 import socket
 import time
+from collections import deque
 
 import pytest
 import torch
@@ -240,14 +241,23 @@ def _slot_state(n_flags, ring_bytes, timeout_s):
     t._slots_cv = threading.Condition(t._lock)
     t._free_slots = deque(range(n_flags))
     t._slot_of, t._inflight_msgs, t._seq = {}, 0, 0
+    t._unfinished, t._free_after_done = set(), {}
     t._alloc = RingAllocator(ring_bytes)
     return t
+
+
+def _reserve_done(t, n):
+    """Reserve a message and mark its stores finished (what the completion
+    thread does once the message's done-event has passed)."""
+    m = t._reserve(n)
+    t._message_done(m[0])
+    return m
 
 
 def test_p2p_flag_slots_are_reused_only_after_their_message_is_returned():
     import threading
     t = _slot_state(3, 1024, 0.3)
-    a, b, c = (t._reserve(256) for _ in range(3))
+    a, b, c = (_reserve_done(t, 256) for _ in range(3))
     assert [m[1] for m in (a, b, c)] == [1, 2, 3]
     assert sorted(m[2] for m in (a, b, c)) == [0, 1, 2] and t._inflight_msgs == 3
     with pytest.raises(RuntimeError):  # every slot pending: bounded wait, then an error
@@ -255,7 +265,7 @@ def test_p2p_flag_slots_are_reused_only_after_their_message_is_returned():
     # returned out of order: the next message takes exactly the freed slot
     # (seq 4 modulo 3 would be b's slot, still pending)
     t._on_free([[a[0], 256]])
-    d = t._reserve(256)
+    d = _reserve_done(t, 256)
     assert d[1] == 4 and d[2] == a[2] and d[0] == a[0] and t._slot_of[d[0]] == a[2]
     # ring space short: the slot taken for the message goes back
     t._on_free([[b[0], 256]])
@@ -264,14 +274,32 @@ def test_p2p_flag_slots_are_reused_only_after_their_message_is_returned():
     assert b[2] in t._free_slots and t._inflight_msgs == 2
     # a FREE from the io thread wakes a waiting reservation
     t.timeout_s = 5.0
-    t._reserve(256)
+    _reserve_done(t, 256)
     timer = threading.Timer(0.2, t._on_free, args=([[c[0], 256]],))
     timer.start()
     t0 = time.time()
-    e = t._reserve(256)
+    e = _reserve_done(t, 256)
     timer.join()
     assert e[2] == c[2] and 0.1 < time.time() - t0 < 3
     assert t._alloc.free_bytes() == 256 and t._inflight_msgs == 3  # [768, 1024) never used
+
+
+def test_p2p_region_freed_early_waits_for_its_own_stores():
+    """A consumer may return a message's region (e.g. it refused the header)
+    while the producer's kernels for that message are still storing into it
+    (raw and direct messages run on the producer's compute stream).  The
+    region and its flag slot must not go to a new message before the
+    completion thread has seen that message's done-event."""
+    t = _slot_state(1, 512, 0.2)
+    a = t._reserve(256)          # stores still in flight
+    t._on_free([[a[0], 256]])    # refused at once by the consumer
+    assert t._free_slots == deque() and t._inflight_msgs == 1
+    with pytest.raises(RuntimeError):  # the only slot is still that message's
+        t._reserve(256)
+    t._message_done(a[0])        # its done-event passed: now it is returned
+    assert list(t._free_slots) == [a[2]] and t._inflight_msgs == 0
+    b = t._reserve(256)
+    assert b[0] == a[0] and b[2] == a[2]
 
 
 def _stress_producer(port, q, threads, per_thread):

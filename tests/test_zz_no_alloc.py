@@ -62,6 +62,25 @@ def test_noalloc_encoder_matches_allocating_encoder_twice():
         assert torch.equal(K.rans_decode(out[:size], n), x)
 
 
+def test_noalloc_encoder_at_its_limit():
+    """An input of exactly the maximum size fills the scratch to its last
+    staging slot and uses every record-size entry; part of it is random
+    bytes, so some chunks take the raw fallback."""
+    enc, mx, cap = _symbols()
+    n = int(mx())
+    x = _symbols_input(n, 3)
+    expected = K.rans_encode(x)
+    c = int(cap(n, 32768))
+    out = torch.empty(c, dtype=torch.uint8, device="cuda")
+    rc = enc(x.data_ptr(), n, out.data_ptr(), c, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    size = int(out[24:32].cpu().view(torch.int64).item())
+    assert size == expected.numel()
+    assert torch.equal(out[:size], expected)
+    assert torch.equal(K.rans_decode(out[:size], n), x)
+
+
 def test_noalloc_encoder_rejects_inputs_beyond_its_scratch():
     enc, mx, cap = _symbols()
     limit = int(mx())
