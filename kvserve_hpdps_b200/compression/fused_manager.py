@@ -249,7 +249,6 @@ class FusedCompressionManager:
         Returns ``{"original_size", "wire_nbytes", "direct"}`` where
         ``wire_nbytes`` is the reserved (upper-bound) size on the direct
         path; the exact size reaches the transport's sent listeners."""
-        from kvserve_hpdps_b200.compression.codec import CODEC_IDS, MAGIC
         from kvserve_hpdps_b200.compression.wire import build_wire
         from kvserve_hpdps_b200.ops import kernels as K
         direct = (hasattr(transport, "open_message") and self.engine == 0
@@ -265,15 +264,31 @@ class FusedCompressionManager:
         plans = [self.plan(l) for l in layer_ids]
         slots = self._slots(kv_layers, plans)
         items = K.WorkItems(slots, [(i, b, n) for i in range(len(kv_layers)) for b, n in requests])
-        dev = kv_layers[0].device
         code_bytes, meta_bytes = max(items.code_bytes, 16), max(items.meta_bytes, 16)
-        rans = self.stream_codec == "rans"
-        body_cap = 16 + K.rans_max_bytes(code_bytes) if rans else code_bytes
+        body_cap = 16 + K.rans_max_bytes(code_bytes) if self.stream_codec == "rans" else code_bytes
         try:
             msg = transport.open_message([body_cap, meta_bytes])
         except RuntimeError as e:
             transport.record_unsent(request_id, list(member_tids or []) or None, e)
             return {"original_size": 0, "wire_nbytes": 0, "direct": True}
+        try:
+            return self._send_direct(transport, msg, request_id, layer_names, kv_layers,
+                                     layer_ids, requests, member_tids, plans, slots, items,
+                                     code_bytes, meta_bytes, body_cap)
+        except Exception as e:
+            # nothing committed: the space comes back once queued work is done
+            transport.abort_message(msg, request_id, list(member_tids or []) or None, e)
+            raise
+
+    def _send_direct(self, transport, msg, request_id, layer_names, kv_layers, layer_ids,
+                     requests, member_tids, plans, slots, items, code_bytes, meta_bytes,
+                     body_cap) -> dict:
+        """Kernels and header of :meth:`send_paged_requests`' direct path."""
+        from kvserve_hpdps_b200.compression.codec import CODEC_IDS, MAGIC
+        from kvserve_hpdps_b200.compression.wire import build_wire
+        from kvserve_hpdps_b200.ops import kernels as K
+        dev = kv_layers[0].device
+        rans = self.stream_codec == "rans"
         meta_local = torch.empty(meta_bytes, dtype=torch.uint8, device=dev)
         total = None
         with nvtx("kvs.quantize_to_ring"):

@@ -52,6 +52,44 @@ class ProducerChannel:
         with self.lock:
             self.sock.send(pack(msg))
 
+    def enable_wakeup(self) -> None:
+        """Let other threads interrupt :meth:`recv_or_wake` (an inproc pair):
+        a thread that owns the socket can then sleep in a long poll and still
+        send a queued message the moment it is queued."""
+        addr = f"inproc://kvs-wake-{id(self)}"
+        self._wake_rx = self.ctx.socket(zmq.PAIR)
+        self._wake_rx.setsockopt(zmq.LINGER, 0)
+        self._wake_rx.bind(addr)
+        self._wake_tx = self.ctx.socket(zmq.PAIR)
+        self._wake_tx.setsockopt(zmq.LINGER, 0)
+        self._wake_tx.connect(addr)
+        self._wake_lock = threading.Lock()
+        self._poller = zmq.Poller()
+        self._poller.register(self.sock, zmq.POLLIN)
+        self._poller.register(self._wake_rx, zmq.POLLIN)
+
+    def wake(self) -> None:
+        """Interrupt the owner thread's :meth:`recv_or_wake` (any thread)."""
+        with self._wake_lock:
+            try:
+                self._wake_tx.send(b"", zmq.NOBLOCK)
+            except zmq.Again:  # already woken many times: it will look anyway
+                pass
+
+    def recv_or_wake(self, timeout_s: float) -> Optional[bytes]:
+        """A message from the peer, or None after ``timeout_s`` or a
+        :meth:`wake` (owner thread only)."""
+        events = dict(self._poller.poll(int(timeout_s * 1000)))
+        if self._wake_rx in events:
+            while True:
+                try:
+                    self._wake_rx.recv(zmq.NOBLOCK)
+                except zmq.Again:
+                    break
+        if self.sock in events:
+            return self.sock.recv()
+        return None
+
     def recv(self, timeout_s: Optional[float] = None) -> Optional[bytes]:
         t = self.timeout_ms if timeout_s is None else int(timeout_s * 1000)
         if self.sock.poll(t, zmq.POLLIN):
@@ -80,6 +118,10 @@ class ProducerChannel:
 
     def close(self) -> None:
         self.sock.close(0)
+        for name in ("_wake_rx", "_wake_tx"):
+            sock = getattr(self, name, None)
+            if sock is not None:
+                sock.close(0)
 
 
 class ConsumerChannel:

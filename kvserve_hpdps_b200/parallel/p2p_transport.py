@@ -52,6 +52,13 @@ ALIGN = 256
 FLAG_STRIDE = 16
 
 
+def _timing_event(stream) -> torch.cuda.Event:
+    """An event with timing enabled, recorded on ``stream`` now."""
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record(stream)
+    return ev
+
+
 def _align(x: int) -> int:
     return (x + ALIGN - 1) // ALIGN * ALIGN
 
@@ -71,7 +78,7 @@ class RingMessage:
     ck: torch.Tensor       # int64[2] checksum accumulators (producer memory)
     flag_ptr: int
     flag_value: int
-    t0: float
+    t0: Any                # timing event recorded before the message's first kernel
 
 
 class RingAllocator:
@@ -157,6 +164,7 @@ class P2PTransport:
         self._outbox: queue.Queue = queue.Queue()
         if is_sender:
             self._ctl = ProducerChannel(host, self.port, timeout_s)
+            self._ctl.enable_wakeup()
             reply = self._ctl.request({"cmd": "RING_HELLO", "device": local_rank}, timeout_s)
             if reply is None:
                 raise TimeoutError(f"no consumer on {host}:{self.port}")
@@ -174,6 +182,10 @@ class P2PTransport:
             self._slots_cv = threading.Condition(self._lock)  # FREE returned flag slots
             self._free_slots: deque = deque(range(self.n_flags))
             self._slot_of: dict[int, int] = {}  # ring offset of a message -> its flag slot
+            self._bw_lock = threading.Lock()
+            self._bw_cache: Optional[tuple[float, float]] = None  # (MB/s, time measured)
+            self._bw_probe = None  # (event, pinned stamps, ring offset, bytes, device stamps)
+            self._probe_src: Optional[torch.Tensor] = None
             self._sent: dict[str, int] = defaultdict(int)
             self._failed: dict[str, int] = defaultdict(int)
             self._listeners: list = []
@@ -212,7 +224,7 @@ class P2PTransport:
                         self._ctl.send(self._outbox.get_nowait())
                     except queue.Empty:
                         break
-                raw = self._ctl.recv(timeout_s=0.005)
+                raw = self._ctl.recv_or_wake(0.05)  # woken at once by a queued header
                 if raw is None:
                     continue
                 msg = unpack(raw)
@@ -222,6 +234,12 @@ class P2PTransport:
                 if self._closed:  # the socket went away under close()
                     break
                 logger.error("p2p producer io error: %s", e)
+
+    def _send_ctl(self, msg: dict) -> None:
+        """Queue a control message for the io thread (which owns the socket)
+        and wake it, so the header leaves without waiting out its poll."""
+        self._outbox.put(msg)
+        self._ctl.wake()
 
     def _on_free(self, regions) -> None:
         """The consumer returned these (offset, size) ring regions.  A region
@@ -257,9 +275,11 @@ class P2PTransport:
 
     def _completion_loop(self) -> None:
         while not self._closed:
+            self._poll_probe()
             with self._pending_cv:
                 while not self._pending and not self._aborted and not self._closed:
                     self._pending_cv.wait(timeout=0.2)
+                    self._poll_probe()
                 if self._closed:
                     return
                 aborted = list(self._aborted)
@@ -275,6 +295,7 @@ class P2PTransport:
                 continue
             ev, rid, tids, nbytes, t0, base = item
             ev.synchronize()
+            start = t0 if isinstance(t0, torch.cuda.Event) else None
             with self._pending_cv:
                 self._pending.popleft()
                 self._pending_cv.notify_all()
@@ -284,7 +305,8 @@ class P2PTransport:
             self._message_done(base)
             if isinstance(nbytes, tuple):  # (device count, host addend): coded stream size
                 nbytes = int(nbytes[0].item()) + int(nbytes[1])
-            ms = (time.monotonic() - t0) * 1e3
+            # device time from the message's first kernel to its last store
+            ms = start.elapsed_time(ev) if start is not None else (time.monotonic() - t0) * 1e3
             write_transfer_stats(rid, ms, nbytes, transport="nvlink-p2p")
             notify_sent(self._listeners, rid, list(tids or [rid]), ms, nbytes, logger)
 
@@ -318,8 +340,7 @@ class P2PTransport:
             self._unsent(request_id, member_tids, e)
             return
         from kvserve_hpdps_b200.ops import kernels as K
-        ready = torch.cuda.current_stream(self.device).record_event()
-        t0 = time.monotonic()
+        ready = _timing_event(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self._stream):
             self._stream.wait_event(ready)
             ck = torch.empty(2, dtype=torch.int64, device=self.device)
@@ -333,14 +354,14 @@ class P2PTransport:
                             trailer_ptr=self._peer.ptr + base + trailer)
             for t in tensors + [ck]:
                 t.record_stream(self._stream)
-            done = self._stream.record_event()
-        self._outbox.put({
+            done = _timing_event(self._stream)
+        self._send_ctl({
             "cmd": "PUT_RING", "kind": kind, "request_id": request_id,
             "layer_names": list(layer_names), "meta": meta, "n_body": n_body,
             "specs": [{"shape": list(t.shape), "dtype": str(t.dtype).replace("torch.", ""),
                        "off": base + o, "nbytes": s} for t, o, s in zip(tensors, offs, sizes)],
             "region": [base, total], "slot": slot, "seq": seq, "trailer": base + trailer})
-        self._track(done, request_id, member_tids, sum(sizes), t0, base)
+        self._track(done, request_id, member_tids, sum(sizes), ready, base)
 
     def _reserve(self, total: int) -> tuple[int, int, int]:
         """Ring space, sequence number and flag slot of a new message.
@@ -413,7 +434,8 @@ class P2PTransport:
                            sizes=[int(n) for n in sizes], ptrs=[ptr + o for o in offs],
                            trailer_ptr=ptr + trailer, trailer_off=base + trailer, ck=ck,
                            flag_ptr=self._peer.ptr + self.flag_off + slot * FLAG_STRIDE,
-                           flag_value=seq & 0xFFFFFFFF, t0=time.monotonic())
+                           flag_value=seq & 0xFFFFFFFF,
+                           t0=_timing_event(torch.cuda.current_stream(self.device)))
 
     def view(self, msg: "RingMessage", i: int, dtype: torch.dtype = torch.uint8,
              shape=None) -> torch.Tensor:
@@ -437,7 +459,7 @@ class P2PTransport:
         the checksum; ``sent_bytes`` (int64 on the device) is the number of
         bytes that actually crossed the link, read by the completion thread
         for the transfer statistics."""
-        done = torch.cuda.current_stream(self.device).record_event()
+        done = _timing_event(torch.cuda.current_stream(self.device))
         full = []
         for sp, off, n in zip(specs, msg.offsets, msg.sizes):
             full.append({"shape": list(sp["shape"]), "dtype": sp["dtype"],
@@ -448,7 +470,7 @@ class P2PTransport:
                "trailer": msg.trailer_off}
         if dyn_len is not None:
             hdr["dyn_len"] = dict(dyn_len)
-        self._outbox.put(hdr)
+        self._send_ctl(hdr)
         nbytes = sum(msg.sizes) if sent_bytes is None else sent_bytes
         self._track(done, request_id, member_tids, nbytes, msg.t0, msg.base)
 
@@ -482,16 +504,16 @@ class P2PTransport:
         except RuntimeError as e:
             self._unsent(request_id, member_tids, e)
             return
-        t0 = time.monotonic()
         dev = raw.device
+        t0 = _timing_event(torch.cuda.current_stream(dev))
         ck = torch.empty(2, dtype=torch.int64, device=dev)
         K.paged_raw(raw, self._peer.ptr + base, True,
                     flag_ptr=self._peer.ptr + self.flag_off + slot * FLAG_STRIDE,
                     flag_value=seq & 0xFFFFFFFF, trailer_ptr=self._peer.ptr + base + trailer,
                     checksum=ck)
-        done = torch.cuda.current_stream(dev).record_event()
+        done = _timing_event(torch.cuda.current_stream(dev))
         shape = [len(kv_layers), 2, len(ids)] + list(raw.block_shape)
-        self._outbox.put({
+        self._send_ctl({
             "cmd": "PUT_RING", "kind": "raw", "request_id": request_id,
             "layer_names": list(layer_names), "meta": None, "n_body": 1,
             "specs": [{"shape": shape, "dtype": str(raw.dtype).replace("torch.", ""),
@@ -501,40 +523,72 @@ class P2PTransport:
         self._track(done, request_id, member_tids, nbytes, t0, base)
 
     def bandwidth_mbps(self, probe_bytes: int = 64 << 20, max_age_s: float = 30.0,
-                       timeout_s: float = 5.0) -> Optional[float]:
+                       timeout_s: float = 5.0, wait: bool = False) -> Optional[float]:
         """Device-timed push bandwidth to the consumer in MB/s (1 MB = 2^20
         bytes): ``probe_bytes`` are stored into a temporarily reserved part of
         the consumer's ring by the probe kernel, timed between the first CTA's
         start and the last CTA's end (globaltimer), with no host round trip in
-        the measured interval.  Cached for ``max_age_s``; None when ring space
-        is not available within ``timeout_s``."""
+        the measured interval.
+
+        The caller never waits on the device (the controller calls this from
+        the engine thread): the cached value is returned (None before the
+        first measurement, when the caller falls back to its configured
+        bandwidth), and a value older than ``max_age_s`` starts a new probe on
+        the transfer stream.  The probe's stamps reach pinned host memory by a
+        stream-ordered copy; the completion thread (or a later call) reads
+        them once the probe's event has passed.  ``wait=True`` blocks until
+        the probe finished, at most ``timeout_s`` (start-up and tests)."""
         assert self.is_sender
+        self._poll_probe()
         now = time.monotonic()
-        cached = getattr(self, "_bw_cache", None)
-        if cached is not None and now - cached[1] < max_age_s:
-            return cached[0]
+        with self._bw_lock:
+            cached = self._bw_cache
+            if (cached is None or now - cached[1] >= max_age_s) and self._bw_probe is None:
+                self._start_probe(int(probe_bytes))
+            probe = self._bw_probe
+        if wait and probe is not None:
+            deadline = time.monotonic() + timeout_s
+            while not probe[0].query() and time.monotonic() < deadline:
+                time.sleep(0.001)
+            self._poll_probe()
+        cached = self._bw_cache
+        return cached[0] if cached else None
+
+    def _start_probe(self, probe_bytes: int) -> None:
+        """Launch one probe (caller holds _bw_lock); skipped when the ring
+        has no room right now."""
         from kvserve_hpdps_b200.ops import kernels as K
-        n = _align(int(probe_bytes))
-        base = self._alloc.alloc(n, timeout_s)
+        n = _align(probe_bytes)
+        with self._alloc.cv:
+            base = self._alloc.try_alloc(n)
         if base is None:
-            return cached[0] if cached else None
-        try:
-            with torch.cuda.device(self.device), torch.cuda.stream(self._stream):
-                src = getattr(self, "_probe_src", None)
-                if src is None or src.numel() < n:
-                    src = torch.zeros(n, dtype=torch.uint8, device=self.device)
-                    self._probe_src = src
-                stamps = torch.tensor([2 ** 63 - 1, 0], dtype=torch.int64, device=self.device)
-                K.probe_push(src, self._peer.ptr + base, n, stamps)
-                self._stream.synchronize()
-                t0, t1 = stamps.tolist()
-        finally:
-            self._alloc.release(base, n)
-        if t1 <= t0:
-            return cached[0] if cached else None
-        mbps = n / (1 << 20) / ((t1 - t0) * 1e-9)
-        self._bw_cache = (mbps, now)
-        return mbps
+            return
+        with torch.cuda.device(self.device), torch.cuda.stream(self._stream):
+            src = self._probe_src
+            if src is None or src.numel() < n:
+                src = torch.zeros(n, dtype=torch.uint8, device=self.device)
+                self._probe_src = src
+            stamps = torch.empty(2, dtype=torch.int64, device=self.device)
+            stamps[0].fill_(2 ** 63 - 1)
+            stamps[1].fill_(0)
+            K.probe_push(src, self._peer.ptr + base, n, stamps)
+            host = torch.empty(2, dtype=torch.int64, pin_memory=True)
+            host.copy_(stamps, non_blocking=True)
+            ev = self._stream.record_event()
+        self._bw_probe = (ev, host, base, n, stamps)
+
+    def _poll_probe(self) -> None:
+        """Finish a probe whose event has passed (no device wait)."""
+        with self._bw_lock:
+            probe = self._bw_probe
+            if probe is None or not probe[0].query():
+                return
+            self._bw_probe = None
+        ev, host, base, n, _ = probe
+        self._alloc.release(base, n)
+        t0, t1 = (int(v) for v in host.tolist())
+        if t1 > t0:
+            self._bw_cache = (n / (1 << 20) / ((t1 - t0) * 1e-9), time.monotonic())
 
     def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
         assert self.is_sender

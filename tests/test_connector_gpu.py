@@ -112,7 +112,7 @@ def _role(producer, port, compression, q):
             torch.cuda.synchronize()
             time.sleep(0.5)  # the listener that writes the statistics runs on its thread
             # device-timed NVLink push bandwidth (feeds the controller)
-            bw = conn._transport.bandwidth_mbps(probe_bytes=32 << 20)
+            bw = conn._transport.bandwidth_mbps(probe_bytes=32 << 20, wait=True)
             if bw is None or not 1e4 < bw < 2e6:
                 raise RuntimeError(f"implausible probe bandwidth {bw} MB/s")
             time.sleep(2.0)

@@ -405,3 +405,40 @@ def test_p2p_consumer_rejects_unusable_headers():
     assert t._ctl.sent == [(b"prod", {"cmd": "FREE", "regions": [[512, 1024]]})]
     t._reject_put({"cmd": "PUT_RING"})  # nothing to report or return
     assert t.drain_received() == {} and len(t._ctl.sent) == 1
+
+
+class _FakeEvent:
+    def __init__(self):
+        self.done = False
+
+    def query(self):
+        return self.done
+
+    def synchronize(self):  # the engine thread must never wait on the device
+        raise AssertionError("bandwidth_mbps waited on the device")
+
+
+def test_p2p_bandwidth_probe_never_blocks_the_caller():
+    """The controller reads the link bandwidth on the engine thread: the
+    transport answers from its cache while a probe is in flight and takes
+    the probe's result (globaltimer stamps copied to pinned host memory)
+    only once its event has passed, releasing the probe's ring space."""
+    import threading
+
+    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport, RingAllocator
+    t = object.__new__(P2PTransport)
+    t.is_sender = True
+    t._bw_lock = threading.Lock()
+    t._alloc = RingAllocator(1 << 20)
+    base = t._alloc.try_alloc(1 << 18)
+    ev = _FakeEvent()
+    stamps = torch.tensor([1_000_000, 1_000_000 + 262_144], dtype=torch.int64)  # 262.144 us
+    t._bw_cache = (5000.0, time.monotonic() - 100.0)  # stale: a probe is already running
+    t._bw_probe = (ev, stamps, base, 1 << 18, None)
+    t0 = time.monotonic()
+    assert t.bandwidth_mbps() == 5000.0  # the old value, at once
+    assert time.monotonic() - t0 < 0.05 and t._bw_probe is not None
+    ev.done = True
+    bw = t.bandwidth_mbps()  # finished probe: 256 KiB in 262.144 us = 953.67 MB/s
+    assert t._bw_probe is None and abs(bw - (1 << 18) / (1 << 20) / 262.144e-6) < 1e-6
+    assert t._alloc.free_bytes() == 1 << 20  # the probe's ring space is back
