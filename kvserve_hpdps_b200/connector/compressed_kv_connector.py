@@ -25,10 +25,20 @@ Worker side:
   all requests of the step on a side stream (one grouped message per layer)
   while the next layers compute; ``wait_for_save`` makes the forward stream
   wait on the side stream;
-* consumer: ``start_load_kv`` drains the transport, waits (bounded) for each
-  scheduled request's payloads and decodes them straight into the registered
-  paged caches at the consumer's block ids (fused dequantize + inverse
-  transform + scatter); raw payloads are scattered with the block-copy kernel.
+* consumer, ``overlap="off"``: ``start_load_kv`` drains the transport, waits
+  (bounded) for each scheduled request's message and decodes it straight
+  into the registered paged caches at the consumer's block ids (fused
+  dequantize + inverse transform + scatter); raw payloads are scattered with
+  the block-copy kernel;
+* consumer, ``overlap="stream"``: loading is layer-wise.  ``start_load_kv``
+  decodes the layers that have arrived on a load stream and returns;
+  ``wait_for_layer_load(l)`` waits on the host only for layer l's message
+  headers and makes the forward stream wait on the device for layer l's
+  decode, so the first layers' attention runs while later layers are still
+  being pushed (the reference's ``wait_for_layer_load`` is a no-op,
+  kvserve_v1/connector/compressed_kv_connector.py:570-571).  A grouped
+  message (one layer of every request of the producer's step) is decoded
+  once for all of its members scheduled in the step.
 
 Transports: ``"p2p"`` (NVLink receive ring, producer kernels store into the
 consumer's memory), ``"nccl"`` (reference protocol over a torch NCCL group)
@@ -42,6 +52,7 @@ import os
 import re
 import time
 from collections import defaultdict, deque
+from contextlib import nullcontext
 from dataclasses import dataclass, field
 from typing import TYPE_CHECKING, Any, Optional
 
@@ -190,7 +201,15 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._layer_refs: dict[str, torch.Tensor] = {}
         self._save_times: dict[str, list[float]] = defaultdict(list)
         self._worker_received: dict[str, deque] = defaultdict(deque)
-        self._grouped_pending: dict[int, dict] = {}
+        self._partial: dict[int, dict] = {}  # records with members still to decode
+        self._step_reqs: dict[str, ReqMeta] = {}
+        self._got: dict[str, int] = {}
+        self._pending_layers: dict[str, set] = {}
+        self._layer_events: dict[str, Any] = {}
+        self._layer_wise = False
+        self._load_stream = None
+        self._fc = None
+        self._deadline = 0.0
         self._side_stream = None
         self._expected_msgs: dict[str, int] = {}
         self._rid2tid: dict[str, str] = {}
@@ -457,6 +476,12 @@ class CompressedKVConnector(KVConnectorBase_V1):
         return (done or None), None
 
     # ================================================================ consumer
+    # Received messages become records shared by every member request they
+    # carry (a stream-mode message holds one layer of every request of the
+    # producer's step): {"names", "payload", "members", "decoded", "prepared",
+    # "cd"}.  A record is queued under each member's transfer id; decoding it
+    # for the members scheduled now marks them decoded, and its ring space goes
+    # back once every member has been decoded.
     def start_load_kv(self, forward_context: Any, **kwargs: Any) -> None:
         if self.is_producer:
             return
@@ -465,44 +490,112 @@ class CompressedKVConnector(KVConnectorBase_V1):
         meta = self._get_connector_metadata()
         if not isinstance(meta, CompressedKVConnectorMetadata):
             return
-        streaming = self._overlap_mode == "stream" and self._num_layers > 0
+        self._fc = forward_context
+        self._step_reqs = {rm.transfer_id: rm for rm in meta.requests}
+        self._got = {t: 0 for t in self._step_reqs}
         # one deadline for the step: with a dead producer the step returns
         # after LOAD_TIMEOUT_S, not after that long for each of its requests
-        deadline = time.monotonic() + LOAD_TIMEOUT_S
-        for rm in meta.requests:
+        self._deadline = time.monotonic() + LOAD_TIMEOUT_S
+        names = sorted(self._kv_caches, key=layer_index)
+        self._layer_wise = (self._overlap_mode == "stream" and bool(names)
+                            and len(names) == self._num_layers and torch.cuda.is_available()
+                            and bool(meta.requests))
+        if self._layer_wise:
+            # Layer-wise load: decode what has arrived on the load stream and
+            # return; wait_for_layer_load(l) waits (host: for layer l's header,
+            # device: for its decode) only for layer l, so the forward of the
+            # first layers runs while later layers are still on the wire.
+            if self._load_stream is None:
+                self._load_stream = torch.cuda.Stream()
+            # decodes start after every earlier kernel of the forward stream
+            # (blocks just handed to these requests may have been read by it)
+            self._load_stream.wait_stream(torch.cuda.current_stream())
+            self._layer_events = {}
+            self._pending_layers = {t: set(names) for t in self._step_reqs}
+            self._decode_available()
+        else:
+            self._pending_layers = {}
+            streaming = self._overlap_mode == "stream" and self._num_layers > 0
             need = self._num_layers if streaming else 1
-            got = 0
-            while got < need:
-                got += self._load_available(rm, forward_context)
-                if got >= need:
+            while True:
+                self._decode_available()
+                if all(self._got[t] >= need for t in self._step_reqs):
                     break
-                if time.monotonic() > deadline:
-                    logger.warning("timeout loading KV of %s (transfer %s): %d/%d messages",
-                                   rm.request_id, rm.transfer_id, got, need)
+                if time.monotonic() > self._deadline:
+                    for t, rm in self._step_reqs.items():
+                        if self._got[t] < need:
+                            logger.warning("timeout loading KV of %s (transfer %s): %d/%d "
+                                           "messages", rm.request_id, t, self._got[t], need)
                     break
-                waiter = getattr(self._transport, "wait_received", None)
-                if waiter is not None:
-                    waiter(0.002)  # wakes as soon as a message header arrives
-                else:
-                    time.sleep(0.002)
+                self._wait_header()
                 self._drain()
-        if torch.cuda.is_available() and meta.requests:
-            # device-side failures of earlier loads (flag timeouts, checksum
-            # mismatches, corrupt streams), read without waiting on the GPU
-            if self._err_monitor is None:
-                from kvserve_hpdps_b200.ops import kernels as K
-                self._err_monitor = K.ErrorMonitor(torch.device("cuda", torch.cuda.current_device()))
-            code = self._err_monitor.poll()
-            if code:
-                from kvserve_hpdps_b200.ops import kernels as K
-                logger.error("device error %d (%s) while loading KV in an earlier step", code,
-                             K.ERR_NAMES.get(code, "?"))
+        self._poll_device_errors(bool(meta.requests))
         timeline("D load_exit")
+
+    def _wait_header(self) -> None:
+        waiter = getattr(self._transport, "wait_received", None)
+        if waiter is not None:
+            waiter(0.002)  # wakes as soon as a message header arrives
+        else:
+            time.sleep(0.002)
+
+    def _poll_device_errors(self, any_requests: bool) -> None:
+        """Device-side failures of earlier loads (flag timeouts, checksum
+        mismatches, corrupt streams), read without waiting on the GPU."""
+        if not (torch.cuda.is_available() and any_requests):
+            return
+        from kvserve_hpdps_b200.ops import kernels as K
+        if self._err_monitor is None:
+            self._err_monitor = K.ErrorMonitor(torch.device("cuda", torch.cuda.current_device()))
+        code = self._err_monitor.poll()
+        if code:
+            logger.error("device error %d (%s) while loading KV in an earlier step", code,
+                         K.ERR_NAMES.get(code, "?"))
+
+    def wait_for_layer_load(self, layer_name: str) -> None:
+        """Stream mode: before layer ``layer_name`` runs, make sure its KV of
+        every request of the step is decoded -- the host waits (bounded by
+        the step's deadline) only until that layer's message headers have
+        arrived, and the forward stream waits on the device for that layer's
+        decode, not for the whole request."""
+        if self.is_producer or not self._layer_wise:
+            return
+        pend = self._pending_layers
+        while any(layer_name in p for p in pend.values()):
+            self._drain()
+            self._decode_available()
+            if not any(layer_name in p for p in pend.values()):
+                break
+            if time.monotonic() > self._deadline:
+                late = [t for t, p in pend.items() if layer_name in p]
+                logger.warning("timeout loading layer %s of %d request(s) (%s)", layer_name,
+                               len(late), ", ".join(late[:4]))
+                for t in late:
+                    pend[t].discard(layer_name)
+                break
+            self._wait_header()
+        ev = self._layer_events.get(layer_name)
+        if ev is not None:
+            torch.cuda.current_stream().wait_event(ev)
+
+    @staticmethod
+    def _members(tid: str, payload: Any) -> list[str]:
+        """Transfer ids a received message carries (grouped messages name
+        their members in the wire metadata)."""
+        if isinstance(payload, dict) and payload.get("__bundle__"):
+            inner = (payload.get("meta") or {}).get("metadata")
+            if isinstance(inner, dict) and inner.get("member_tids"):
+                return [str(t) for t in inner["member_tids"]]
+        return [tid]
 
     def _drain(self) -> None:
         for tid, msgs in (self._transport.drain_received() or {}).items():
-            for m in msgs:
-                self._worker_received[tid].append(m)
+            for names, payload in msgs:
+                members = self._members(tid, payload)
+                rec = {"names": names, "payload": payload, "members": set(members),
+                       "decoded": set(), "prepared": False, "cd": None}
+                for t in members:
+                    self._worker_received[t].append(rec)
 
     def _layer_cache(self, name: str, forward_context: Any) -> Optional[torch.Tensor]:
         t = self._kv_caches.get(name)
@@ -516,69 +609,125 @@ class CompressedKVConnector(KVConnectorBase_V1):
             return None
         return cache[getattr(forward_context, "virtual_engine", 0)]
 
-    def _load_available(self, rm: ReqMeta, forward_context: Any) -> int:
-        """Decode every message available for this request; returns how many
-        messages were consumed."""
-        q = self._worker_received.get(rm.transfer_id)
-        n = 0
-        while q:
-            names, payload = q.popleft()
-            n += 1
-            if payload is None:
-                logger.error("transport reported a failed transfer for %s", rm.request_id)
-                continue
-            try:
-                self._inject(rm, names, payload, forward_context)
-            except Exception as e:  # noqa: BLE001
-                logger.error("decode of %s failed: %s", rm.request_id, e)
-        if q is not None and not q:
-            self._worker_received.pop(rm.transfer_id, None)
-        return n
+    def _decode_available(self) -> None:
+        """Decode every queued record of the step's requests, for the members
+        scheduled now.  Layer-wise mode puts the kernels on the load stream
+        and records one event per decoded layer."""
+        ctx = torch.cuda.stream(self._load_stream) if self._layer_wise else nullcontext()
+        with ctx:
+            for tid in list(self._step_reqs):
+                q = self._worker_received.get(tid)
+                while q:
+                    rec = q.popleft()
+                    if tid not in rec["decoded"]:
+                        self._decode_record(rec)
+                if q is not None and not q:
+                    self._worker_received.pop(tid, None)
+        self._sweep_partial()
 
-    def _inject(self, rm: ReqMeta, names: list[str], payload: Any, forward_context: Any) -> None:
+    def _decode_record(self, rec: dict) -> None:
+        now = [t for t in rec["members"] if t in self._step_reqs and t not in rec["decoded"]]
+        if not now:
+            return
+        names, payload = rec["names"], rec["payload"]
+        plain = strip_sentinel(names) if is_compressed_layer_names(names) else list(names)
+        if payload is None:
+            logger.error("transport reported a failed transfer for %s", ", ".join(now))
+            self._mark(rec, now, plain)
+            return
         tr = self._transport
         dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
             else torch.device("cpu")
-        if hasattr(tr, "prepare"):
-            tr.prepare(payload, dev)
-        if isinstance(payload, dict) and payload.get("__ring_raw__"):
-            payload_t = payload["tensor"]
-        else:
-            payload_t = payload
         t0 = time.monotonic()
         try:
+            if not rec["prepared"] and hasattr(tr, "prepare"):
+                tr.prepare(payload, dev)  # bounded device flag wait + checksum, once
+            rec["prepared"] = True
             with nvtx("kvs.inject"):
-                self._inject_body(rm, names, payload, payload_t, forward_context, t0)
-        finally:  # the ring space returns even when decoding fails
-            if hasattr(tr, "release"):
-                tr.release(payload, dev)
+                self._inject_record(rec, now, plain, payload)
+            if is_compressed_layer_names(names):
+                for t in now:
+                    write_decode_stats(self._step_reqs[t].request_id, t,
+                                       (time.monotonic() - t0) * 1e3)
+        except Exception as e:  # noqa: BLE001
+            logger.error("decode of %s failed: %s", ", ".join(now), e)
+        finally:
+            self._mark(rec, now, plain)
+            if rec["decoded"] >= rec["members"]:
+                if hasattr(tr, "release"):  # after the decode queued on this stream
+                    tr.release(payload, dev)
+                self._partial.pop(id(rec), None)
+            else:
+                rec.setdefault("t", time.monotonic())
+                self._partial[id(rec)] = rec
 
-    def _inject_body(self, rm: ReqMeta, names: list[str], payload: Any, payload_t: Any,
-                     forward_context: Any, t0: float) -> None:
-        if is_compressed_layer_names(names):
-            names = strip_sentinel(names)
-            wire = CompressedWire(payload["meta"], payload["body_chunks"], payload["aux_tensors"])
-            cd = restore_from_wire(wire)
+    def _mark(self, rec: dict, members: list[str], names: list[str]) -> None:
+        rec["decoded"].update(members)
+        for t in members:
+            if t in self._got:
+                self._got[t] += 1
+            pend = self._pending_layers.get(t)
+            if pend:
+                pend.difference_update(names)
+        if self._layer_wise:
+            ev = self._load_stream.record_event()
+            for n in names:
+                self._layer_events[n] = ev
+
+    def _sweep_partial(self) -> None:
+        """Grouped records some of whose members were never scheduled here
+        give their ring space back after twice the load timeout."""
+        if not self._partial:
+            return
+        cutoff = time.monotonic() - 2 * LOAD_TIMEOUT_S
+        for key, rec in list(self._partial.items()):
+            if rec.get("t", 0.0) < cutoff:
+                self._partial.pop(key, None)
+                if hasattr(self._transport, "release"):
+                    self._transport.release(rec["payload"])
+
+    def _inject_record(self, rec: dict, members: list[str], names: list[str],
+                       payload: Any) -> None:
+        fc = self._fc
+        if is_compressed_layer_names(rec["names"]):
+            if rec["cd"] is None:
+                rec["cd"] = restore_from_wire(CompressedWire(payload["meta"], payload["body_chunks"],
+                                                             payload["aux_tensors"]))
+            cd = rec["cd"]
             md = cd.metadata or {}
             comp = self._get_compressor()
             if md.get("layout") in ("items", "items_packed"):
-                self._inject_items(rm, names, cd, comp, forward_context)
-            else:
-                kv = comp.decompress(cd)
-                if kv is None:
-                    raise RuntimeError("decompression returned None")
-                for i, name in enumerate(names):
-                    cache = self._layer_cache(name, forward_context)
-                    if cache is not None:
-                        inject_kv_into_layer_by_blocks(cache, kv[i], rm.block_ids, rm.request_id)
-            write_decode_stats(rm.request_id, rm.transfer_id, (time.monotonic() - t0) * 1e3)
-        else:
-            caches = [self._layer_cache(n, forward_context) for n in names]
-            if self._scatter_raw(rm, caches, payload, payload_t):
+                caches = [self._layer_cache(n, fc) for n in names]
+                if any(c is None for c in caches):
+                    raise RuntimeError("missing KV cache tensor for a layer of the message")
+                tids = md["member_tids"]
+                if len(tids) == 1:
+                    rm = self._step_reqs[members[0]]
+                    comp.decompress_paged_requests(cd, caches,
+                                                   [(rm.block_ids, md["member_tokens"][0])])
+                else:  # one launch for every member scheduled now
+                    sel = {i: self._step_reqs[t].block_ids for i, t in enumerate(tids)
+                           if t in members}
+                    comp.manager.decompress_members(cd, caches, sel)
                 return
-            for cache, part in zip(caches, payload_t):
+            kv = comp.decompress(cd)
+            if kv is None:
+                raise RuntimeError("decompression returned None")
+            rm = self._step_reqs[members[0]]
+            for i, name in enumerate(names):
+                cache = self._layer_cache(name, fc)
                 if cache is not None:
-                    inject_kv_into_layer_by_blocks(cache, part, rm.block_ids, rm.request_id)
+                    inject_kv_into_layer_by_blocks(cache, kv[i], rm.block_ids, rm.request_id)
+            return
+        rm = self._step_reqs[members[0]]
+        payload_t = payload["tensor"] if isinstance(payload, dict) and \
+            payload.get("__ring_raw__") else payload
+        caches = [self._layer_cache(n, fc) for n in names]
+        if self._scatter_raw(rm, caches, payload, payload_t):
+            return
+        for cache, part in zip(caches, payload_t):
+            if cache is not None:
+                inject_kv_into_layer_by_blocks(cache, part, rm.block_ids, rm.request_id)
 
     @staticmethod
     def _scatter_raw(rm: ReqMeta, caches: list, payload: Any, payload_t: Any) -> bool:
@@ -607,38 +756,6 @@ class CompressedKVConnector(KVConnectorBase_V1):
         with nvtx("kvs.scatter_raw"):
             K.paged_raw(raw, payload_t.data_ptr(), gather=False)
         return True
-
-    def _inject_items(self, rm: ReqMeta, names: list[str], cd, comp, forward_context) -> None:
-        """Fused message (one or more requests x layers): decode into the
-        registered caches at this request's blocks."""
-        md = cd.metadata
-        tids = md["member_tids"]
-        caches = [self._layer_cache(n, forward_context) for n in names]
-        if any(c is None for c in caches):
-            raise RuntimeError("missing KV cache tensor for a layer of the message")
-        if len(tids) == 1:
-            comp.decompress_paged_requests(cd, caches, [(rm.block_ids, md["member_tokens"][0])])
-            return
-        # grouped: decode the members scheduled now; keep the rest for later
-        key = id(cd.compressed_tensor)
-        entry = self._grouped_pending.setdefault(key, {"cd": cd, "names": names, "left": set(tids)})
-        meta = self._get_connector_metadata()
-        here = {r.transfer_id: r for r in meta.requests} if meta is not None else {}
-        reqs = []
-        for i, t in enumerate(tids):
-            r = here.get(t)
-            reqs.append((r.block_ids, md["member_tokens"][i]) if r is not None and t in entry["left"]
-                        else (None, md["member_tokens"][i]))
-        sub = [(i, b) for i, (b, _) in enumerate(reqs) if b is not None]
-        if sub:
-            comp.manager.decompress_members(cd, caches, {i: b for i, b in sub})
-            for i, _ in sub:
-                entry["left"].discard(tids[i])
-        if not entry["left"]:
-            self._grouped_pending.pop(key, None)
-
-    def wait_for_layer_load(self, layer_name: str) -> None:
-        return None
 
     # ================================================================ scheduler
     def get_num_new_matched_tokens(self, request: Any, num_computed_tokens: int):

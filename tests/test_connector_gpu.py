@@ -84,6 +84,57 @@ def test_fused_default_handoff_in_process(overlap, monkeypatch):
     assert pair.messages == (L if overlap == "stream" else 2)
 
 
+def test_stream_mode_loads_layer_by_layer(monkeypatch):
+    """Stream mode on the consumer: start_load_kv returns without waiting for
+    the whole request, and wait_for_layer_load(l) makes layer l's KV (of
+    every request of the step, grouped messages included) ready while the
+    producer has not yet sent the last layer."""
+    monkeypatch.setenv("KVSERVE_OVERLAP_MODE", "stream")
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 20.0)
+    from kvserve_hpdps_b200.connector.compressed_kv_connector import (CompressedKVConnector,
+                                                                      KVConnectorRole)
+    from kvserve_hpdps_b200.parallel.fake_transport import FakeTransportPair
+    pair = FakeTransportPair()
+    p = CompressedKVConnector(vllm_config(True, "default"), KVConnectorRole.WORKER)
+    c = CompressedKVConnector(vllm_config(False, "default"), KVConnectorRole.WORKER)
+    p.attach_transport(pair.producer())
+    c.attach_transport(pair.consumer())
+    pc, cc = _caches(24, 1, "cuda"), _caches(24, 2, "cuda", fill=False)
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    reqs_p = [("a", "ta", 100, [3, 9, 1, 17, 5, 20, 11]), ("b", "tb", 40, [0, 6, 22])]
+    reqs_c = [("da", "ta", 100, [4, 2, 8, 10, 12, 14, 16]), ("db", "tb", 40, [23, 1, 3])]
+    names = sorted(pc, key=mod.layer_index)
+    p.bind_connector_metadata(_meta(reqs_p))
+    for name in names[:-1]:  # the last layer is not computed yet
+        p.save_kv_layer(name, pc[name], None)
+    torch.cuda.synchronize()
+
+    def check(name):
+        for (_, _, n, bp), (_, _, _, bcs) in zip(reqs_p, reqs_c):
+            src = pc[name][:, bp].reshape(2, -1, H, D)[:, :n]
+            dst = cc[name][:, bcs].reshape(2, -1, H, D)[:, :n]
+            assert _cos(src, dst) > 0.9, name
+
+    c.bind_connector_metadata(_meta(reqs_c))
+    t0 = time.monotonic()
+    c.start_load_kv(None)
+    c.wait_for_layer_load(names[0])
+    assert time.monotonic() - t0 < 5.0  # no wait for the missing layer
+    torch.cuda.current_stream().synchronize()
+    check(names[0])
+    assert all(int(cc[names[-1]][:, b].abs().sum()) == 0 for _, _, _, b in reqs_c)
+    p.save_kv_layer(names[-1], pc[names[-1]], None)
+    p.wait_for_save()
+    for name in names[1:]:
+        c.wait_for_layer_load(name)
+    torch.cuda.current_stream().synchronize()
+    for name in names:
+        check(name)
+    assert pair.messages == L  # one grouped message per layer for both requests
+
+
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
