@@ -109,6 +109,7 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
                   enable_prefix_caching=False, kv_transfer_config=ktc, seed=0,
                   tensor_parallel_size=args.tp)
         q_out.put(("ready", role))
+        eng = llm.llm_engine
         while True:
             msg = q_in.get()
             if msg[0] == "stop":
@@ -117,8 +118,23 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
             sp = SamplingParams(max_tokens=1 if role == "p" else args.max_tokens, temperature=0.0,
                                 detokenize=False,
                                 extra_args={"kv_transfer_params": {"transfer_id": f"req-{i}"}})
-            out = llm.generate([{"prompt_token_ids": ids}], sp, use_tqdm=False)
-            q_out.put(("done", role, i, time.time(), list(out[0].outputs[0].token_ids)))
+            # drive the engine step by step: the first token's arrival is the
+            # TTFT even when more tokens follow
+            rid = eng.add_request(f"{role}{i}", {"prompt_token_ids": ids}, sp) or f"{role}{i}"
+            t_first, toks = None, []
+            while True:
+                outs = eng.step()
+                fin = False
+                for o in outs:
+                    if getattr(o, "request_id", None) != rid:
+                        continue
+                    toks = list(o.outputs[0].token_ids) if o.outputs else toks
+                    if toks and t_first is None:
+                        t_first = time.time()
+                    fin = fin or o.finished
+                if fin:
+                    break
+            q_out.put(("done", role, i, t_first or time.time(), toks, time.time()))
     except Exception:  # noqa: BLE001
         import traceback
         q_out.put(("error", role, traceback.format_exc()))
@@ -205,6 +221,8 @@ def main(argv=None) -> int:
                 agree.append(got["c"][4][:1] == got["p"][4][:1])
         q = sorted(ttft)
         line = {"metric": "p50 TTFT, 1P1D (Qwen2.5-7B random-init, 8K prompt)",
+                "overlap": os.environ.get("KVSERVE_OVERLAP_MODE", "off"), "tp": args.tp,
+                "max_tokens": args.max_tokens,
                 "impl": args.impl, "compression": args.compression,
                 "transport": args.transport if args.impl == "ours" else "reference NcclTransport",
                 "requests": args.requests, "prompt_len": args.prompt_len,
@@ -221,6 +239,9 @@ def main(argv=None) -> int:
         stats = _stats_summary()
         if stats:
             line["stats"] = stats
+        tl = timeline_breakdown(os.environ.get("KVSERVE_TIMELINE_PATH"), args.warmup)
+        if tl:
+            line["timeline_ms_p50"] = tl
         print(json.dumps(line), flush=True)
     except Exception as e:  # noqa: BLE001
         print(json.dumps({"impl": args.impl, "compression": args.compression,
@@ -234,6 +255,34 @@ def main(argv=None) -> int:
             if p.is_alive():
                 p.terminate()
     return rc
+
+
+def timeline_breakdown(path, skip: int = 0):
+    """Median durations of the connector's timeline markers (both engines
+    append ``<tag> <epoch>`` lines to the same file): the producer's
+    ``wait_for_save`` (P save_enter -> save_exit, compress + send) and the
+    consumer's ``start_load_kv`` (D load_enter -> load_exit)."""
+    if not path or not os.path.exists(path):
+        return None
+    spans: dict = {"P": [], "D": []}
+    open_at: dict = {}
+    with open(path) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) != 3:
+                continue
+            side, tag, t = parts[0], parts[1], float(parts[2])
+            if tag.endswith("_enter"):
+                open_at[side] = t
+            elif tag.endswith("_exit") and side in open_at:
+                spans.setdefault(side, []).append((t - open_at.pop(side)) * 1e3)
+    out = {}
+    for side, name in (("P", "producer_wait_for_save"), ("D", "consumer_start_load_kv")):
+        v = spans.get(side, [])
+        v = [x for x in v if x > 0.05] or v  # steps without a transfer record ~0
+        if v:
+            out[name] = round(statistics.median(v), 3)
+    return out or None
 
 
 def prompts(n: int, prompt_len: int) -> list:

@@ -1,9 +1,9 @@
 // CPU implementation of the interleaved rANS stream (format: rans.cuh) and
 // of the fixed-width bit packing used by the fused kernels.
 //
-// The encoder emulates the 32 warp lanes of the device encoder step by step,
-// so for the same input it produces the same bytes as k_rans_encode +
-// k_rans_directory + k_rans_copy.  It is the oracle of the device codec and
+// The encoder emulates the 32 warp lanes (two interleaved streams) of the
+// device encoder step by step, so for the same input it produces the same
+// bytes as k_rans_encode + k_rans_directory + k_rans_copy.  It is the oracle of the device codec and
 // the codec of CPU-only round trips.
 //
 // Chunks are independent, so both directions run them on a pool of host
@@ -35,10 +35,9 @@ inline uint32_t sym_at(const uint8_t* src, uint32_t n_sym, uint32_t idx) {
   return idx < n_sym ? src[idx] : 0u;
 }
 
-// Encode one chunk into a slot buffer; returns (rec_off, rec_len).
-std::pair<uint32_t, uint32_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t cs,
-                                           uint8_t* slot) {
-  const uint64_t sb = slot_bytes(cs);
+// Encode one chunk; returns its record (the bytes k_rans_copy would place).
+std::vector<uint8_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t cs) {
+  (void)cs;
   const uint32_t n_ss = (n_sym + kSuper - 1) / kSuper;
   uint64_t hist[256] = {0};
   for (uint32_t i = 0; i < n_ss * kSuper; ++i) hist[sym_at(src, n_sym, i)]++;
@@ -54,61 +53,67 @@ std::pair<uint32_t, uint32_t> encode_chunk(const uint8_t* src, uint32_t n_sym, u
     if (freq[s]) enc[s] = make_enc(freq[s], cum);
     cum += freq[s];
   }
-  uint16_t* words = reinterpret_cast<uint16_t*>(slot);
-  const int64_t cap = static_cast<int64_t>(sb / 2);
-  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
-  const int64_t min_w = (16 + fpad + 128) / 2;
-  int64_t wpos = cap;
-  uint32_t x[kLanes];
-  for (int l = 0; l < kLanes; ++l) x[l] = kStateLow;
+  const uint64_t prefix = coded_prefix_bytes(A);
+  const uint64_t raw_len = raw_record_bytes(n_sym);
+  // words of each stream, in emission order (reversed at the end)
+  std::vector<uint16_t> emitted[kStreams];
+  uint32_t x[kStreams][kLanes];
+  for (int k = 0; k < kStreams; ++k)
+    for (int l = 0; l < kLanes; ++l) x[k][l] = kStateLow;
   bool overflow = false;
-  for (int ss = static_cast<int>(n_ss) - 1; ss >= 0 && !overflow; --ss) {
-    if (wpos - kSuper - 8 < min_w) {
+  for (int ss = static_cast<int>(n_ss) - 1; ss >= 0; --ss) {
+    const uint64_t used = emitted[0].size() + emitted[1].size();
+    if (prefix + 2 * (used + kSuper + 16) >= raw_len) {
       overflow = true;
       break;
     }
     for (int m = kSub - 1; m >= 0; --m) {
-      bool emit[kLanes];
-      int cnt = 0;
+      const int k = m & 1;
       uint32_t sym[kLanes];
+      bool emit[kLanes];
+      std::vector<uint16_t> step;
       for (int l = 0; l < kLanes; ++l) {
         sym[l] = sym_at(src, n_sym, static_cast<uint32_t>(ss) * kSuper + l * kSub + m);
-        emit[l] = x[l] >= enc[sym[l]].x_max;
-        cnt += emit[l];
+        emit[l] = x[k][l] >= enc[sym[l]].x_max;
       }
-      int rank = 0;
+      // the device writes a step's words in lane order just below the
+      // previous ones; emitted in reverse, a step's block is reversed too
+      for (int l = kLanes - 1; l >= 0; --l)
+        if (emit[l]) emitted[k].push_back(static_cast<uint16_t>(x[k][l] & 0xFFFFu));
       for (int l = 0; l < kLanes; ++l) {
-        if (emit[l]) {
-          words[wpos - cnt + rank] = static_cast<uint16_t>(x[l] & 0xFFFFu);
-          ++rank;
-          x[l] >>= 16;
-        }
+        if (emit[l]) x[k][l] >>= 16;
         const EncSym& e = enc[sym[l]];
-        const uint32_t q = umulhi32(x[l], e.rcp) >> (e.cmpl_shift >> 16);
-        x[l] = x[l] + e.bias + q * (e.cmpl_shift & 0xFFFFu);
+        const uint32_t q = umulhi32(x[k][l], e.rcp) >> (e.cmpl_shift >> 16);
+        x[k][l] = x[k][l] + e.bias + q * (e.cmpl_shift & 0xFFFFu);
       }
-      wpos -= cnt;
     }
   }
-  if (!overflow) {
-    const int64_t nw = cap - wpos;
-    const int64_t npad = (8 - (nw & 7)) & 7;
-    const int64_t wstart = wpos - npad;
-    const uint64_t rs = static_cast<uint64_t>(wstart) * 2 - 128 - fpad - 16;
-    uint8_t* rec = slot + rs;
-    ChunkHeader hd{n_sym, A, static_cast<uint32_t>(nw), static_cast<uint32_t>(npad)};
-    std::memcpy(rec, &hd, sizeof(hd));
-    uint16_t* fr = reinterpret_cast<uint16_t*>(rec + 16);
-    for (uint32_t s = 0; s < fpad / 2; ++s) fr[s] = static_cast<uint16_t>(s < A ? freq[s] : 0u);
-    std::memcpy(rec + 16 + fpad, x, sizeof(x));
-    for (int64_t i = 0; i < npad; ++i) words[wstart + i] = 0;
-    return {static_cast<uint32_t>(rs), static_cast<uint32_t>(sb - rs)};
+  if (overflow) {
+    std::vector<uint8_t> rec(raw_len, 0);
+    const uint32_t hd[8] = {n_sym, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    std::memcpy(rec.data(), hd, sizeof(hd));
+    std::memcpy(rec.data() + sizeof(ChunkHeader), src, n_sym);
+    return rec;
   }
-  ChunkHeader hd{n_sym, 0u, 0u, 0u};
-  std::memcpy(slot, &hd, sizeof(hd));
-  std::memset(slot + 16, 0, pad16(n_sym));
-  std::memcpy(slot + 16, src, n_sym);
-  return {0u, static_cast<uint32_t>(16 + pad16(n_sym))};
+  uint32_t nw[kStreams], np[kStreams];
+  for (int k = 0; k < kStreams; ++k) {
+    nw[k] = static_cast<uint32_t>(emitted[k].size());
+    np[k] = (8 - (nw[k] & 7)) & 7;
+  }
+  std::vector<uint8_t> rec(prefix + 2ull * (np[0] + nw[0] + np[1] + nw[1]), 0);
+  const uint32_t hd[8] = {n_sym, A, nw[0], nw[1], np[0], np[1], 0u, 0u};
+  std::memcpy(rec.data(), hd, sizeof(hd));
+  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  uint16_t* fr = reinterpret_cast<uint16_t*>(rec.data() + sizeof(ChunkHeader));
+  for (uint32_t s = 0; s < A; ++s) fr[s] = static_cast<uint16_t>(freq[s]);
+  std::memcpy(rec.data() + sizeof(ChunkHeader) + fpad, x, sizeof(x));
+  uint16_t* w = reinterpret_cast<uint16_t*>(rec.data() + prefix);
+  for (int k = 0; k < kStreams; ++k) {
+    w += np[k];  // leading zero padding
+    for (uint32_t i = 0; i < nw[k]; ++i) w[i] = emitted[k][nw[k] - 1 - i];
+    w += nw[k];
+  }
+  return rec;
 }
 
 // Runs fn(i) for every i in [0, n) on up to hardware-concurrency threads,
@@ -146,27 +151,31 @@ void parallel_for(uint32_t n, F&& fn) {
 // Decode chunk c of a validated stream header; 0 or a negative error code.
 int decode_chunk(const uint8_t* stream, uint64_t stream_bytes, const uint64_t* dir,
                  const StreamHeader& hd, uint32_t c, uint8_t* out, uint64_t n) {
-  if (dir[c] > stream_bytes || stream_bytes - dir[c] < 16) return -4;
+  if (dir[c] > stream_bytes || stream_bytes - dir[c] < sizeof(ChunkHeader)) return -4;
   const uint8_t* rec = stream + dir[c];
-  const uint64_t room = stream_bytes - dir[c] - 16;  // bytes after the chunk header
+  const uint64_t room = stream_bytes - dir[c];  // bytes of the record and after it
   ChunkHeader ch;
   std::memcpy(&ch, rec, sizeof(ch));
   const uint64_t first = static_cast<uint64_t>(c) * hd.chunk_symbols;
   if (ch.n_sym > hd.chunk_symbols || ch.alphabet > 256 || ch.n_sym > n - first) return -5;
   uint8_t* dst = out + first;
   if (ch.alphabet == 0) {
-    if (ch.n_sym > room) return -4;
-    std::memcpy(dst, rec + 16, ch.n_sym);
+    if (raw_record_bytes(ch.n_sym) > room) return -4;
+    std::memcpy(dst, rec + sizeof(ChunkHeader), ch.n_sym);
     return 0;
   }
   const uint32_t A = ch.alphabet;
-  const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
+  const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + sizeof(ChunkHeader));
   const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
-  const uint64_t total_words = static_cast<uint64_t>(ch.n_pad) + ch.n_words;
-  if (fpad + 128ull + 2 * total_words > room) return -4;
-  uint32_t x[kLanes];
-  std::memcpy(x, rec + 16 + fpad, sizeof(x));
-  const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
+  uint64_t total_words[kStreams];
+  for (int k = 0; k < kStreams; ++k)
+    total_words[k] = static_cast<uint64_t>(ch.n_pad[k]) + ch.n_words[k];
+  if (coded_prefix_bytes(A) + 2 * (total_words[0] + total_words[1]) > room) return -4;
+  uint32_t x[kStreams][kLanes];
+  std::memcpy(x, rec + sizeof(ChunkHeader) + fpad, sizeof(x));
+  const uint16_t* words[kStreams];
+  words[0] = reinterpret_cast<const uint16_t*>(rec + coded_prefix_bytes(A));
+  words[1] = words[0] + total_words[0];
   uint32_t fc[256];
   thread_local std::vector<uint8_t> lut;
   lut.assign(kProbScale, 0);
@@ -178,26 +187,30 @@ int decode_chunk(const uint8_t* stream, uint64_t stream_bytes, const uint64_t* d
     cum += freq[s];
   }
   if (cum != kProbScale) return -6;
-  uint64_t rptr = ch.n_pad;
+  uint64_t rptr[kStreams] = {ch.n_pad[0], ch.n_pad[1]};
   const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
     for (int m = 0; m < kSub; ++m) {
+      const int k = m & 1;
       for (int l = 0; l < kLanes; ++l) {
-        const uint32_t sl = x[l] & (kProbScale - 1);
+        uint32_t& xs = x[k][l];
+        const uint32_t sl = xs & (kProbScale - 1);
         const uint32_t s = lut[sl];
-        x[l] = (fc[s] & 0xFFFFu) * (x[l] >> kProbBits) + sl - (fc[s] >> 16);
-        if (x[l] < kStateLow) {
-          if (rptr >= total_words) return -7;
-          x[l] = (x[l] << 16) | words[rptr++];
+        xs = (fc[s] & 0xFFFFu) * (xs >> kProbBits) + sl - (fc[s] >> 16);
+        if (xs < kStateLow) {
+          if (rptr[k] >= total_words[k]) return -7;
+          xs = (xs << 16) | words[k][rptr[k]++];
         }
         const uint32_t idx = ss * kSuper + l * kSub + m;
         if (idx < ch.n_sym) dst[idx] = static_cast<uint8_t>(s);
       }
     }
   }
-  for (int l = 0; l < kLanes; ++l)
-    if (x[l] != kStateLow) return -8;
-  if (rptr != total_words) return -9;
+  for (int k = 0; k < kStreams; ++k) {
+    for (int l = 0; l < kLanes; ++l)
+      if (x[k][l] != kStateLow) return -8;
+    if (rptr[k] != total_words[k]) return -9;
+  }
   return 0;
 }
 
@@ -314,17 +327,11 @@ uint64_t kvs_cpu_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t
                              uint64_t out_cap) {
   if (n == 0 || cs == 0 || cs % kSuper != 0) return 0;
   const uint32_t nc = num_chunks(n, cs);
-  const uint64_t sb = slot_bytes(cs);
-  // Each chunk is encoded into a zeroed slot that mirrors the device staging
-  // layout (so record offsets match) and its record is kept for placement.
   std::vector<std::vector<uint8_t>> recs(nc);
   parallel_for(nc, [&](uint32_t c) {
-    thread_local std::vector<uint8_t> slot;
-    slot.assign(sb, 0);
     const uint64_t start = static_cast<uint64_t>(c) * cs;
     const uint32_t n_sym = static_cast<uint32_t>(std::min<uint64_t>(cs, n - start));
-    const auto r = encode_chunk(in + start, n_sym, cs, slot.data());
-    recs[c].assign(slot.data() + r.first, slot.data() + r.first + r.second);
+    recs[c] = encode_chunk(in + start, n_sym, cs);
   });
   const uint64_t base = pad16(directory_bytes(nc));
   std::vector<uint64_t> dir(nc + 1);

@@ -2,12 +2,14 @@
 //
 // Encode = three launches on one stream:
 //   k_rans_encode    one warp per chunk: histogram, normalisation, reverse
-//                    encode into a per-chunk staging slot (raw fallback when
-//                    the coded record would not be smaller than the input);
+//                    encode of the chunk's two interleaved streams into a
+//                    per-chunk staging slot (raw fallback when the coded record
+//                    would not be smaller than the input);
 //   k_rans_directory one CTA: exclusive scan of record sizes, header + dir;
-//   k_rans_copy      one warp per chunk: compacts records into the output,
-//                    which may be a peer GPU's buffer (NVLink stores); the
-//                    last warp can publish a release flag for the consumer.
+//   k_rans_copy      one warp per chunk: compacts each record's three pieces
+//                    (prefix, word blocks of the two streams) into the output,
+//                    which may be a peer GPU's buffer (NVLink stores); the last
+//                    CTA can publish a release flag for the consumer.
 // Decode = k_rans_decode, one warp per chunk, symbols written in place.
 #include "common.cuh"
 #include "rans.cuh"
@@ -16,9 +18,10 @@ namespace kvs {
 namespace rans {
 
 constexpr int kEncWarps = 4;
+constexpr int kHistCopies = 8;  // lane-interleaved histogram copies (spread the atomics)
 constexpr int kDecWarps = 8;
-constexpr int kRing = 1024;  // words of the decoder's shared-memory ring
-constexpr int kDecWarpSmem = 4096 + 1024 + kRing * 2;
+constexpr int kRing = 1024;  // words of one stream's shared-memory ring in the decoder
+constexpr int kDecWarpSmem = 4096 + 1024 + kStreams * kRing * 2;
 
 // Where an encoded stream goes inside a transfer message (all optional).
 struct RansMsg {
@@ -40,14 +43,30 @@ KVS_DEV uint32_t lanemask_lt() {
   return m;
 }
 
-// 16 symbols of lane `lane` in super-step `ss` (zero padded past n_sym).
-KVS_DEV uint4 load_syms(const uint8_t* src, uint32_t ss, int lane, uint32_t n_sym) {
+// The 32 symbols of lane `lane` in super-step `ss` (zero padded past n_sym),
+// as two 16-byte words.
+struct Syms32 {
+  uint4 lo, hi;
+};
+KVS_DEV Syms32 load_syms(const uint8_t* src, uint32_t ss, int lane, uint32_t n_sym) {
   const uint32_t off = ss * kSuper + lane * kSub;
-  if (off + kSub <= n_sym) return *reinterpret_cast<const uint4*>(src + off);
-  uint32_t w[4] = {0, 0, 0, 0};
+  Syms32 r;
+  if (off + kSub <= n_sym) {
+    r.lo = *reinterpret_cast<const uint4*>(src + off);
+    r.hi = *reinterpret_cast<const uint4*>(src + off + 16);
+    return r;
+  }
+  uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   for (uint32_t i = 0; i < kSub; ++i)
     if (off + i < n_sym) w[i >> 2] |= static_cast<uint32_t>(src[off + i]) << ((i & 3) * 8);
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  r.lo = make_uint4(w[0], w[1], w[2], w[3]);
+  r.hi = make_uint4(w[4], w[5], w[6], w[7]);
+  return r;
+}
+
+KVS_DEV void syms_words(const Syms32& v, uint32_t (&w)[8]) {
+  w[0] = v.lo.x; w[1] = v.lo.y; w[2] = v.lo.z; w[3] = v.lo.w;
+  w[4] = v.hi.x; w[5] = v.hi.y; w[6] = v.hi.z; w[7] = v.hi.w;
 }
 
 
@@ -128,14 +147,18 @@ KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncSym* enc, int l
   __syncwarp();
 }
 
-__global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
+// One warp per chunk.  desc[chunk * kDescWords + k] receives: the record
+// length, the prefix length (header + frequencies + states, or the whole raw
+// record), the byte length of each stream's word block and the staging
+// offset of each word block (see rans.cuh).
+__global__ void __launch_bounds__(kEncWarps * 32, 6) k_rans_encode(
     const uint8_t* __restrict__ in, uint64_t n, uint32_t cs, uint8_t* __restrict__ staging,
-    uint32_t* __restrict__ rec_off, uint32_t* __restrict__ rec_len, uint32_t n_chunks) {
-  // a warp's histogram (4 x 256 counts) is dead once its frequencies are
-  // normalised, so its encoder table (256 x 16 B) reuses the same 4 KB
-  __shared__ __align__(16) uint32_t hist[kEncWarps][4 * 256];
+    uint32_t* __restrict__ desc, uint32_t n_chunks) {
+  // a warp's histogram (8 x 256 counts) is dead once its frequencies are
+  // normalised, so its encoder table (256 x 16 B) reuses the first 4 KB
+  __shared__ __align__(16) uint32_t hist[kEncWarps][kHistCopies * 256];
   __shared__ uint32_t freq_s[kEncWarps][256];
-  static_assert(sizeof(EncSym) * 256 == sizeof(uint32_t) * 4 * 256, "table aliasing");
+  static_assert(sizeof(EncSym) * 256 <= sizeof(uint32_t) * kHistCopies * 256, "table aliasing");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk = blockIdx.x * kEncWarps + warp;
   if (chunk >= n_chunks) return;  // warp-uniform
@@ -143,30 +166,32 @@ __global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
   const uint32_t n_sym = static_cast<uint32_t>(min(static_cast<uint64_t>(cs), n - start));
   const uint32_t n_ss = (n_sym + kSuper - 1) / kSuper;
   const uint8_t* src = in + start;
-  const uint64_t sb = slot_bytes(cs);
-  uint8_t* slot = staging + static_cast<uint64_t>(chunk) * sb;
+  uint8_t* slot = staging + static_cast<uint64_t>(chunk) * slot_bytes(cs);
+  uint32_t* d = desc + static_cast<uint64_t>(chunk) * kDescWords;
 
   uint32_t* h = hist[warp];
-  for (int i = lane; i < 4 * 256; i += 32) h[i] = 0;
+  for (int i = lane; i < kHistCopies * 256; i += 32) h[i] = 0;
   __syncwarp();
-  // Histogram in four lane-interleaved copies (lane & 3): spreads the
-  // atomic traffic of skewed symbol distributions over four addresses.
-  uint32_t* hc = h + (lane & 3) * 256;
+  // Histogram in eight lane-interleaved copies (lane & 7): spreads the
+  // atomic traffic of skewed symbol distributions over eight addresses.
+  uint32_t* hc = h + (lane & (kHistCopies - 1)) * 256;
   // the next super-step's symbols are loaded while this one is counted
-  uint4 nxt = load_syms(src, 0, lane, n_sym);
+  Syms32 nxt = load_syms(src, 0, lane, n_sym);
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
-    const uint4 v = nxt;
+    uint32_t w[8];
+    syms_words(nxt, w);
     if (ss + 1 < n_ss) nxt = load_syms(src, ss + 1, lane, n_sym);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) atomicAdd(&hc[(w[i >> 2] >> ((i & 3) * 8)) & 0xFF], 1u);
+    for (int i = 0; i < kSub; ++i) atomicAdd(&hc[(w[i >> 2] >> ((i & 3) * 8)) & 0xFF], 1u);
   }
   __syncwarp();
   int top = -1;
   for (int k = 0; k < 8; ++k) {
     const int s = lane * 8 + k;
-    const uint32_t c = h[s] + h[256 + s] + h[512 + s] + h[768 + s];
-    h[s] = c;
+    uint32_t c = 0;
+#pragma unroll
+    for (int cp = 0; cp < kHistCopies; ++cp) c += h[cp * 256 + s];
+    h[s] = c;  // copy 0 now holds the totals (each lane only reads its own bins)
     if (c > 0) top = s;
   }
 #pragma unroll
@@ -177,27 +202,38 @@ __global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
   EncSym* enc = reinterpret_cast<EncSym*>(hist[warp]);
   build_enc_warp(freq_s[warp], A, enc, lane);
 
-  uint16_t* words = reinterpret_cast<uint16_t*>(slot);
-  const int64_t cap = static_cast<int64_t>(sb / 2);
-  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
-  const int64_t min_w = (16 + fpad + 128) / 2;
-  int64_t wpos = cap;
-  uint32_t x = kStateLow;
+  // Words of stream k grow backwards from the end of region k.
+  const int cap = static_cast<int>(region_bytes(cs) / 2);
+  uint16_t* words0 = reinterpret_cast<uint16_t*>(slot + kPrefixArea);
+  uint16_t* words1 = reinterpret_cast<uint16_t*>(slot + kPrefixArea + region_bytes(cs));
+  const uint64_t prefix = coded_prefix_bytes(A);
+  const uint64_t raw_len = raw_record_bytes(n_sym);
+  int wpos0 = cap, wpos1 = cap;
+  uint32_t x0 = kStateLow, x1 = kStateLow;
   bool overflow = false;
   const uint32_t lt = lanemask_lt();
-  uint4 pre = load_syms(src, n_ss - 1, lane, n_sym);  // prefetched one super-step ahead
+  Syms32 pre = load_syms(src, n_ss - 1, lane, n_sym);  // prefetched one super-step ahead
   for (int ss = static_cast<int>(n_ss) - 1; ss >= 0; --ss) {
-    if (wpos - kSuper - 8 < min_w) {
+    // a super-step emits at most one word per symbol; stop (raw record) as
+    // soon as the coded record could reach the raw one's size (two blocks of
+    // padding included)
+    const int used = (cap - wpos0) + (cap - wpos1);
+    if (prefix + 2ull * static_cast<uint64_t>(used + kSuper + 16) >= raw_len) {
       overflow = true;
       break;
     }
-    const uint4 v = pre;
+    uint32_t w[8];
+    syms_words(pre, w);
     if (ss > 0) pre = load_syms(src, ss - 1, lane, n_sym);
-    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    // sub-steps in decreasing order; even ones update stream 0, odd ones
+    // stream 1, so consecutive steps are independent chains
 #pragma unroll
     for (int m = kSub - 1; m >= 0; --m) {
-      const uint32_t s = (w4[m >> 2] >> ((m & 3) * 8)) & 0xFFu;
+      const uint32_t s = (w[m >> 2] >> ((m & 3) * 8)) & 0xFFu;
       const EncSym e = enc[s];
+      uint32_t& x = (m & 1) ? x1 : x0;
+      int& wpos = (m & 1) ? wpos1 : wpos0;
+      uint16_t* words = (m & 1) ? words1 : words0;
       const bool emit = x >= e.x_max;
       const uint32_t mask = __ballot_sync(0xFFFFFFFFu, emit);
       const int cnt = __popc(mask);
@@ -211,33 +247,46 @@ __global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
     }
   }
   if (!overflow) {
-    const int64_t nw = cap - wpos;
-    const int64_t npad = (8 - (nw & 7)) & 7;
-    const int64_t wstart = wpos - npad;
-    const uint64_t rs = static_cast<uint64_t>(wstart) * 2 - 128 - fpad - 16;
-    uint8_t* rec = slot + rs;
+    const int nw0 = cap - wpos0, nw1 = cap - wpos1;
+    const int np0 = (8 - (nw0 & 7)) & 7, np1 = (8 - (nw1 & 7)) & 7;
+    if (lane < np0) words0[wpos0 - np0 + lane] = 0;
+    if (lane < np1) words1[wpos1 - np1 + lane] = 0;
+    const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
     if (lane == 0) {
-      ChunkHeader hd{n_sym, A, static_cast<uint32_t>(nw), static_cast<uint32_t>(npad)};
-      *reinterpret_cast<ChunkHeader*>(rec) = hd;
-      rec_off[chunk] = static_cast<uint32_t>(rs);
-      rec_len[chunk] = static_cast<uint32_t>(sb - rs);
+      // ChunkHeader {n_sym, A, n_words[2], n_pad[2], 0, 0} as two 16-byte stores
+      reinterpret_cast<uint4*>(slot)[0] =
+          make_uint4(n_sym, A, static_cast<uint32_t>(nw0), static_cast<uint32_t>(nw1));
+      reinterpret_cast<uint4*>(slot)[1] =
+          make_uint4(static_cast<uint32_t>(np0), static_cast<uint32_t>(np1), 0u, 0u);
+      const uint32_t len0 = static_cast<uint32_t>(2 * (nw0 + np0));
+      const uint32_t len1 = static_cast<uint32_t>(2 * (nw1 + np1));
+      d[0] = static_cast<uint32_t>(prefix) + len0 + len1;
+      d[1] = static_cast<uint32_t>(prefix);
+      d[2] = len0;
+      d[3] = len1;
+      d[4] = static_cast<uint32_t>(kPrefixArea + 2 * (wpos0 - np0));
+      d[5] = static_cast<uint32_t>(kPrefixArea + region_bytes(cs) + 2 * (wpos1 - np1));
     }
-    uint16_t* fr = reinterpret_cast<uint16_t*>(rec + 16);
+    uint16_t* fr = reinterpret_cast<uint16_t*>(slot + sizeof(ChunkHeader));
     for (uint32_t s = lane; s < fpad / 2; s += 32)
       fr[s] = static_cast<uint16_t>(s < A ? freq_s[warp][s] : 0u);
-    reinterpret_cast<uint32_t*>(rec + 16 + fpad)[lane] = x;
-    if (lane < npad) words[wstart + lane] = 0;
+    uint32_t* st = reinterpret_cast<uint32_t*>(slot + sizeof(ChunkHeader) + fpad);
+    st[lane] = x0;
+    st[kLanes + lane] = x1;
   } else {
     if (lane == 0) {
-      ChunkHeader hd{n_sym, 0u, 0u, 0u};
-      *reinterpret_cast<ChunkHeader*>(slot) = hd;
-      rec_off[chunk] = 0;
-      rec_len[chunk] = static_cast<uint32_t>(16 + pad16(n_sym));
+      reinterpret_cast<uint4*>(slot)[0] = make_uint4(n_sym, 0u, 0u, 0u);  // raw record header
+      reinterpret_cast<uint4*>(slot)[1] = make_uint4(0u, 0u, 0u, 0u);
+      d[0] = static_cast<uint32_t>(raw_len);
+      d[1] = static_cast<uint32_t>(raw_len);
+      d[2] = d[3] = d[4] = d[5] = 0;
     }
-    for (uint32_t ss = 0; ss < (n_sym + 511) / 512; ++ss) {
-      const uint4 v = load_syms(src, ss, lane, n_sym);
+    for (uint32_t ss = 0; ss < n_ss; ++ss) {
+      const Syms32 v = load_syms(src, ss, lane, n_sym);
       const uint32_t off = ss * kSuper + lane * kSub;
-      if (off < pad16(n_sym)) *reinterpret_cast<uint4*>(slot + 16 + off) = v;
+      uint8_t* dst = slot + sizeof(ChunkHeader) + off;
+      if (off < pad16(n_sym)) *reinterpret_cast<uint4*>(dst) = v.lo;
+      if (off + 16 < pad16(n_sym)) *reinterpret_cast<uint4*>(dst + 16) = v.hi;
     }
   }
 }
@@ -248,7 +297,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 8) k_rans_encode(
 // m.has_prefix the 16-byte container header m.prefix is written just before
 // the stream; with m.ck the checksum of everything this kernel writes is
 // added (message offset of out[0] = m.msg_off, a multiple of 16).
-__global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restrict__ rec_len,
+__global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restrict__ desc,
                                                          uint32_t n_chunks, uint64_t n,
                                                          uint32_t cs, uint8_t* __restrict__ out,
                                                          uint64_t* __restrict__ total_out,
@@ -259,7 +308,7 @@ __global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restr
   const uint32_t per = (n_chunks + 1023) / 1024;
   const uint32_t b = tid * per, e = min(n_chunks, b + per);
   uint64_t s = 0;
-  for (uint32_t i = b; i < e; ++i) s += rec_len[i];
+  for (uint32_t i = b; i < e; ++i) s += desc[static_cast<uint64_t>(i) * kDescWords];
   part[tid] = s;
   __syncthreads();
   for (int o = 1; o < 1024; o <<= 1) {
@@ -283,7 +332,7 @@ __global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restr
     dir[i] = run;
     dst_off[i] = run;
     if (m.ck != nullptr) ck64(run, sizeof(StreamHeader) + 8ull * i);
-    run += rec_len[i];
+    run += desc[static_cast<uint64_t>(i) * kDescWords];
   }
   if (tid == 0) {
     for (uint64_t i = sizeof(StreamHeader) + 8ull * (n_chunks + 1); i < base; ++i) out[i] = 0;
@@ -309,27 +358,36 @@ __global__ void __launch_bounds__(1024) k_rans_directory(const uint32_t* __restr
   __threadfence_system();
 }
 
-// One warp per record: compact staging -> out (out may be a peer buffer),
-// at the offsets the directory kernel left in `dst_off`.  With m.ck the
-// checksum of the records is added; with m.counter the last CTA stores the
-// finished checksum to m.trailer (when set) and publishes m.flag_value into
-// m.flag with release semantics after a system-scope fence.
+// One warp per record: compact its pieces (prefix, then the word blocks of
+// the two streams) from staging into out (out may be a peer buffer), at the
+// offsets the directory kernel left in `dst_off`.  With m.ck the checksum of
+// the records is added; with m.counter the last CTA stores the finished
+// checksum to m.trailer (when set) and publishes m.flag_value into m.flag
+// with release semantics after a system-scope fence.
 __global__ void __launch_bounds__(256) k_rans_copy(
-    const uint8_t* __restrict__ staging, const uint32_t* __restrict__ rec_off,
-    const uint32_t* __restrict__ rec_len, const uint64_t* __restrict__ dst_off,
-    uint32_t n_chunks, uint32_t cs, uint8_t* out, const RansMsg m) {
+    const uint8_t* __restrict__ staging, const uint32_t* __restrict__ desc,
+    const uint64_t* __restrict__ dst_off, uint32_t n_chunks, uint32_t cs, uint8_t* out,
+    const RansMsg m) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk = blockIdx.x * 8 + warp;
   unsigned long long s1 = 0, s2 = 0;
   if (chunk < n_chunks) {
-    const uint64_t doff = dst_off[chunk];
-    const uint4* s = reinterpret_cast<const uint4*>(staging + static_cast<uint64_t>(chunk) * slot_bytes(cs) + rec_off[chunk]);
-    uint4* d = reinterpret_cast<uint4*>(out + doff);
-    const uint32_t n16 = rec_len[chunk] / 16;
-    for (uint32_t i = lane; i < n16; i += 32) {
-      const uint4 v = s[i];
-      d[i] = v;
-      if (m.ck != nullptr) ck_word4(v, m.msg_off + static_cast<long long>(doff) + 16ll * i, s1, s2);
+    const uint32_t* d = desc + static_cast<uint64_t>(chunk) * kDescWords;
+    const uint8_t* slot = staging + static_cast<uint64_t>(chunk) * slot_bytes(cs);
+    uint64_t doff = dst_off[chunk];
+    const uint32_t len[3] = {d[1], d[2], d[3]};
+    const uint32_t src_off[3] = {0u, d[4], d[5]};
+#pragma unroll
+    for (int piece = 0; piece < 3; ++piece) {
+      const uint4* sp = reinterpret_cast<const uint4*>(slot + src_off[piece]);
+      uint4* dp = reinterpret_cast<uint4*>(out + doff);
+      const uint32_t n16 = len[piece] / 16;
+      for (uint32_t i = lane; i < n16; i += 32) {
+        const uint4 v = sp[i];
+        dp[i] = v;
+        if (m.ck != nullptr) ck_word4(v, m.msg_off + static_cast<long long>(doff) + 16ll * i, s1, s2);
+      }
+      doff += len[piece];
     }
   }
   if (m.ck != nullptr) ck_flush(m.ck, s1, s2);
@@ -346,6 +404,15 @@ __global__ void __launch_bounds__(256) k_rans_copy(
 // (~0 when unknown: then against the header's own total): a corrupt stream
 // records ERR_CORRUPT and its chunks are skipped, nothing is read or written
 // outside the buffers.
+//
+// Each stream's words reach shared memory through its own ring of kRing
+// words, filled with asynchronous 16-byte copies (256 words a group) half a
+// super-step ahead: at the start of each half (16 sub-steps, at most 256
+// words of a stream) the copies issued at the previous half's start are
+// waited for, then groups are issued while they fit before (read pointer +
+// kRing).  The previous half left the ring filled beyond its read pointer +
+// 768 and advanced that pointer by at most 256, so every word of the current
+// half has landed, and no copy overwrites a word not yet read.
 __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ stream,
                                                                uint64_t len,
                                                                uint8_t* __restrict__ out,
@@ -355,7 +422,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* lut = dsm + warp * kDecWarpSmem;
   uint32_t* fc = reinterpret_cast<uint32_t*>(lut + 4096);
-  uint16_t* ring = reinterpret_cast<uint16_t*>(lut + 4096 + 1024);
+  uint16_t* ring0 = reinterpret_cast<uint16_t*>(lut + 4096 + 1024);
+  uint16_t* ring1 = ring0 + kRing;
   const uint32_t nc = num_chunks(n_expected, cs);
   if (len < sizeof(StreamHeader)) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, ERR_CORRUPT);
@@ -373,7 +441,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const uint64_t* dir = reinterpret_cast<const uint64_t*>(stream + sizeof(StreamHeader));
   const uint64_t roff = dir[chunk];
   const uint64_t expect = min(static_cast<uint64_t>(cs), n_expected - static_cast<uint64_t>(chunk) * cs);
-  if (roff < dir_end || roff + 16 > hd.total_bytes) {
+  if (roff < dir_end || roff + sizeof(ChunkHeader) > hd.total_bytes) {
     if (lane == 0) record_error(err, ERR_CORRUPT);
     return;
   }
@@ -381,27 +449,28 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const ChunkHeader ch = *reinterpret_cast<const ChunkHeader*>(rec);
   uint8_t* dst = out + static_cast<uint64_t>(chunk) * cs;
   const uint64_t room = hd.total_bytes - roff;  // record bytes available in the stream
-  const uint64_t fpad64 = pad16(2ull * ch.alphabet);
+  const uint64_t words0 = static_cast<uint64_t>(ch.n_pad[0]) + ch.n_words[0];
+  const uint64_t words1 = static_cast<uint64_t>(ch.n_pad[1]) + ch.n_words[1];
   const bool bad = ch.n_sym != expect || ch.alphabet > 256 ||
-                   (ch.alphabet == 0 && 16ull + ch.n_sym > room) ||
+                   (ch.alphabet == 0 && raw_record_bytes(ch.n_sym) > room) ||
                    (ch.alphabet != 0 &&
-                    16ull + fpad64 + 128 + 2ull * (static_cast<uint64_t>(ch.n_pad) + ch.n_words) >
-                        room);
+                    (coded_prefix_bytes(ch.alphabet) + 2 * (words0 + words1) > room ||
+                     (words0 & 7) != 0 || (words1 & 7) != 0));
   if (bad) {
     if (lane == 0) record_error(err, ERR_CORRUPT);
     return;
   }
   const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
   if (ch.alphabet == 0) {
-    for (uint32_t i = lane; i < ch.n_sym; i += 32) dst[i] = rec[16 + i];
+    for (uint32_t i = lane; i < ch.n_sym; i += 32) dst[i] = rec[sizeof(ChunkHeader) + i];
     return;
   }
   const uint32_t A = ch.alphabet;
-  const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + 16);
-  const uint32_t fpad = static_cast<uint32_t>(fpad64);
-  const uint32_t* states = reinterpret_cast<const uint32_t*>(rec + 16 + fpad);
-  const uint16_t* words = reinterpret_cast<const uint16_t*>(rec + 16 + fpad + 128);
-  const uint32_t total_words = ch.n_pad + ch.n_words;
+  const uint16_t* freq = reinterpret_cast<const uint16_t*>(rec + sizeof(ChunkHeader));
+  const uint32_t fpad = static_cast<uint32_t>(pad16(2ull * A));
+  const uint32_t* states = reinterpret_cast<const uint32_t*>(rec + sizeof(ChunkHeader) + fpad);
+  const uint16_t* wsrc0 = reinterpret_cast<const uint16_t*>(rec + coded_prefix_bytes(A));
+  const uint16_t* wsrc1 = wsrc0 + words0;
   if (lane == 0) {
     uint32_t cum = 0;
     for (uint32_t s = 0; s < A; ++s) {
@@ -417,50 +486,65 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
     for (uint32_t k = lane; k < f; k += 32)
       if (c + k < kProbScale) lut[c + k] = static_cast<uint8_t>(s);
   }
-  uint32_t x = states[lane];
-  uint32_t rptr = ch.n_pad, loaded = 0;
+  uint32_t x0 = states[lane], x1 = states[kLanes + lane];
+  uint32_t rp0 = ch.n_pad[0], rp1 = ch.n_pad[1];
+  uint32_t ld0 = 0, ld1 = 0;  // words of each stream issued to its ring
   const uint32_t lt = lanemask_lt();
-  __syncwarp();
-  for (uint32_t ss = 0; ss < n_ss; ++ss) {
-    // Keep kRing - 256 words ahead of the read pointer with asynchronous
-    // 16-byte copies (one group per 256 words, never over unread words); a
-    // super-step reads at most 512 words, so every group except the newest
-    // must have landed.
-    while (loaded < rptr + (kRing - 256) && loaded < total_words) {
+  auto refill = [&](uint16_t* ring, const uint16_t* src, uint32_t& loaded, uint32_t rptr,
+                    uint64_t total) {
+    while (loaded + 256 <= rptr + kRing && loaded < total) {
       const uint32_t idx = loaded + lane * 8;
-      if (idx < total_words)
+      if (idx < total)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
                          smem_u32(ring + (idx & (kRing - 1)))),
-                     "l"(words + idx)
+                     "l"(src + idx)
                      : "memory");
-      asm volatile("cp.async.commit_group;" ::: "memory");
       loaded += 256;
     }
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncwarp();
-    uint32_t o[4] = {0, 0, 0, 0};
+  };
+  auto refill_both = [&]() {
+    refill(ring0, wsrc0, ld0, rp0, words0);
+    refill(ring1, wsrc1, ld1, rp1, words1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  __syncwarp();
+  refill_both();
+  for (uint32_t ss = 0; ss < n_ss; ++ss) {
+    uint32_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-    for (int m = 0; m < kSub; ++m) {
-      const uint32_t sl = x & (kProbScale - 1);
-      const uint32_t s = lut[sl];
-      const uint32_t e = fc[s];
-      x = (e & 0xFFFFu) * (x >> kProbBits) + sl - (e >> 16);
-      const bool need = x < kStateLow;
-      const uint32_t mask = __ballot_sync(0xFFFFFFFFu, need);
-      if (need) x = (x << 16) | ring[(rptr + __popc(mask & lt)) & (kRing - 1)];
-      rptr += __popc(mask);
-      o[m >> 2] |= s << ((m & 3) * 8);
+    for (int half = 0; half < 2; ++half) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+      refill_both();  // the next half's words, in flight during this half
+#pragma unroll
+      for (int mm = 0; mm < kSub / 2; ++mm) {
+        const int m = half * (kSub / 2) + mm;
+        uint32_t& x = (m & 1) ? x1 : x0;
+        uint32_t& rp = (m & 1) ? rp1 : rp0;
+        const uint16_t* ring = (m & 1) ? ring1 : ring0;
+        const uint32_t sl = x & (kProbScale - 1);
+        const uint32_t s = lut[sl];
+        const uint32_t e = fc[s];
+        x = (e & 0xFFFFu) * (x >> kProbBits) + sl - (e >> 16);
+        const bool need = x < kStateLow;
+        const uint32_t mask = __ballot_sync(0xFFFFFFFFu, need);
+        if (need) x = (x << 16) | ring[(rp + __popc(mask & lt)) & (kRing - 1)];
+        rp += __popc(mask);
+        o[m >> 2] |= s << ((m & 3) * 8);
+      }
     }
     const uint32_t off = ss * kSuper + lane * kSub;
     if (off + kSub <= ch.n_sym) {
       *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(dst + off + 16) = make_uint4(o[4], o[5], o[6], o[7]);
     } else {
       for (uint32_t i = 0; i < kSub; ++i)
         if (off + i < ch.n_sym) dst[off + i] = static_cast<uint8_t>(o[i >> 2] >> ((i & 3) * 8));
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
-  if (x != kStateLow || rptr != total_words) record_error(err, ERR_CORRUPT);
+  if (x0 != kStateLow || x1 != kStateLow || rp0 != words0 || rp1 != words1)
+    record_error(err, ERR_CORRUPT);
 }
 
 }  // namespace rans
@@ -477,10 +561,11 @@ uint64_t kvs_rans_staging_bytes(uint64_t n, uint32_t cs) {
 }
 
 // Encode n bytes into `out` (capacity kvs_rans_max_bytes).  `sizes` holds
-// 4*n_chunks uint32 (record offsets, lengths and the 64-bit output
-// offsets).  The stream size is written to *total_out (device).  `msg`
-// (host pointer, may be null) places the stream inside a transfer message:
-// container header, checksum, and the ready flag published by the last CTA.
+// kvs_rans_sizes_words(n, cs) uint32 (per-chunk record descriptors and the
+// 64-bit output offsets).  The stream size is written to *total_out
+// (device).  `msg` (host pointer, may be null) places the stream inside a
+// transfer message: container header, checksum, and the ready flag published
+// by the last CTA.
 int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging, uint32_t* sizes,
                     uint8_t* out, uint64_t* total_out, const RansMsg* msg, void* stream) {
   if (n == 0 || cs == 0 || cs % kSuper != 0) return -2;
@@ -489,20 +574,21 @@ int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging
   if ((m.msg_off & 15) != 0) return -2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint32_t nc = num_chunks(n, cs);
-  uint32_t* rec_off = sizes;
-  uint32_t* rec_len = sizes + nc;
-  uint64_t* dst_off = reinterpret_cast<uint64_t*>(sizes + 2 * nc);  // 8-byte aligned
+  uint32_t* desc = sizes;
+  uint64_t* dst_off = reinterpret_cast<uint64_t*>(sizes + kDescWords * static_cast<uint64_t>(nc) +
+                                                  (nc & 1));  // 8-byte aligned
   k_rans_encode<<<(nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32, 0, s>>>(in, n, cs, staging,
-                                                                            rec_off, rec_len, nc);
-  k_rans_directory<<<1, 1024, 0, s>>>(rec_len, nc, n, cs, out, total_out, dst_off, m);
-  k_rans_copy<<<(nc + 7) / 8, 256, 0, s>>>(staging, rec_off, rec_len, dst_off, nc, cs, out, m);
+                                                                            desc, nc);
+  k_rans_directory<<<1, 1024, 0, s>>>(desc, nc, n, cs, out, total_out, dst_off, m);
+  k_rans_copy<<<(nc + 7) / 8, 256, 0, s>>>(staging, desc, dst_off, nc, cs, out, m);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 int kvs_rans_msg_size(void) { return static_cast<int>(sizeof(RansMsg)); }
 // uint32 words of the `sizes` scratch for n bytes in chunks of cs.
 uint64_t kvs_rans_sizes_words(uint64_t n, uint32_t cs) {
-  return 4ull * num_chunks(n, cs);
+  const uint64_t nc = num_chunks(n, cs);
+  return kDescWords * nc + (nc & 1) + 2 * nc;
 }
 
 // Decode n bytes from a stream of `len` bytes (~0: unknown, the header's
@@ -542,8 +628,8 @@ constexpr uint32_t kNoAllocMaxChunks =
 
 static __device__ __align__(256) uint8_t g_noalloc_staging[kNoAllocMaxChunks *
                                                            slot_bytes(kNoAllocChunk)];
-// record offsets, record lengths, 64-bit output offsets (kvs_rans_encode's layout)
-static __device__ __align__(256) uint32_t g_noalloc_sizes[4 * kNoAllocMaxChunks];
+// record descriptors and 64-bit output offsets (kvs_rans_encode's layout)
+static __device__ __align__(256) uint32_t g_noalloc_sizes[(kDescWords + 2) * kNoAllocMaxChunks + 1];
 static __device__ __align__(256) uint64_t g_noalloc_total[2];
 
 // Device addresses of the scratch arrays, looked up with the context that
@@ -658,18 +744,18 @@ int kvs_rans_encode_noalloc(const uint8_t* in, uint64_t n, uint8_t* out, uint64_
   if (int rc = noalloc_scratch(&s)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint32_t nc = num_chunks(n, kNoAllocChunk);
-  uint32_t* rec_off = s.sizes;
-  uint32_t* rec_len = s.sizes + nc;
-  uint64_t* dst_off = reinterpret_cast<uint64_t*>(s.sizes + 2 * nc);
+  uint32_t* desc = s.sizes;
+  uint64_t* dst_off = reinterpret_cast<uint64_t*>(s.sizes + kDescWords * static_cast<uint64_t>(nc) +
+                                                  (nc & 1));
   const RansMsg none{};
   cudaError_t e = noalloc_launch(k_rans_encode, (nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32,
-                                 st, in, n, kNoAllocChunk, s.staging, rec_off, rec_len, nc);
+                                 st, in, n, kNoAllocChunk, s.staging, desc, nc);
   if (e == cudaSuccess)
-    e = noalloc_launch(k_rans_directory, 1, 1024, st, rec_len, nc, n, kNoAllocChunk, out,
-                       s.total, dst_off, none);
+    e = noalloc_launch(k_rans_directory, 1, 1024, st, desc, nc, n, kNoAllocChunk, out, s.total,
+                       dst_off, none);
   if (e == cudaSuccess)
-    e = noalloc_launch(k_rans_copy, (nc + 7) / 8, 256, st, s.staging, rec_off, rec_len, dst_off,
-                       nc, kNoAllocChunk, out, none);
+    e = noalloc_launch(k_rans_copy, (nc + 7) / 8, 256, st, s.staging, desc, dst_off, nc,
+                       kNoAllocChunk, out, none);
   if (e != cudaSuccess) {
     cudaGetLastError();  // this call's launch error, reported through the return code
     return KVS_NOALLOC_LAUNCH;

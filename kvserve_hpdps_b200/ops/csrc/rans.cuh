@@ -14,15 +14,21 @@
 //   StreamHeader (32 B)
 //   uint64 dir[n_chunks + 1]      record offsets from the stream start
 //   records, each 16-byte aligned:
-//     ChunkHeader (16 B) {n_sym, alphabet A (0 = raw), n_words, n_pad}
-//     A > 0: uint16 freq[A] (padded to 16 B), uint32 state[32],
-//            uint16 words[n_pad + n_words] (first n_pad are padding)
+//     ChunkHeader (32 B) {n_sym, alphabet A (0 = raw), n_words[2], n_pad[2], 0, 0}
+//     A > 0: uint16 freq[A] (padded to 16 B), uint32 state[2][32],
+//            uint16 words0[n_pad[0] + n_words[0]], uint16 words1[n_pad[1] + n_words[1]]
+//            (the first n_pad[k] words of each block are padding; every block is a
+//            multiple of 8 words)
 //     A = 0: n_sym raw bytes (padded to 16 B)
 // Chunk c covers symbols [c*chunk_symbols, min((c+1)*chunk_symbols, n)).
-// Symbol j of a chunk (after zero padding to a multiple of 512) belongs to
-// super-step j/512, lane (j%512)/16 and sub-step j%16.  Decoding runs
-// super-steps and sub-steps in increasing order; at each sub-step the lanes
-// whose state fell below 2^15 read one word each, in lane order.
+// A chunk holds two interleaved rANS streams that share its frequency table:
+// every lane owns one state of each.  Symbol j of a chunk (after zero padding
+// to a multiple of 1024) belongs to super-step j/1024, lane (j%1024)/32,
+// sub-step j%32 and stream j%2.  Decoding runs super-steps and sub-steps in
+// increasing order; at each sub-step the lanes whose state of that sub-step's
+// stream fell below 2^15 read one word each from that stream's words, in lane
+// order.  Consecutive sub-steps therefore update independent states, which
+// gives each lane two dependency chains to interleave.
 #pragma once
 
 #include <cstdint>
@@ -30,10 +36,11 @@
 namespace kvs {
 namespace rans {
 
-constexpr uint32_t kMagic = 0x3152564Bu;  // "KVR1"
+constexpr uint32_t kMagic = 0x3252564Bu;  // "KVR2"
 constexpr int kLanes = 32;
-constexpr int kSub = 16;                              // symbols per lane per super-step
-constexpr int kSuper = kLanes * kSub;                 // 512 symbols per super-step
+constexpr int kStreams = 2;                           // rANS streams per chunk (states per lane)
+constexpr int kSub = 32;                              // symbols per lane per super-step
+constexpr int kSuper = kLanes * kSub;                 // 1024 symbols per super-step
 constexpr uint32_t kChunkSymbols = 32768;             // default chunk size
 constexpr int kProbBits = 12;
 constexpr uint32_t kProbScale = 1u << kProbBits;      // M = 4096
@@ -53,17 +60,29 @@ static_assert(sizeof(StreamHeader) == 32, "header size");
 struct ChunkHeader {
   uint32_t n_sym;
   uint32_t alphabet;
-  uint32_t n_words;
-  uint32_t n_pad;
+  uint32_t n_words[kStreams];
+  uint32_t n_pad[kStreams];
+  uint32_t reserved[2];
 };
-static_assert(sizeof(ChunkHeader) == 16, "chunk header size");
+static_assert(sizeof(ChunkHeader) == 32, "chunk header size");
 
 inline constexpr uint64_t pad16(uint64_t x) { return (x + 15) & ~uint64_t(15); }
 
-// Staging slot per chunk: large enough for the raw fallback record.
-inline constexpr uint64_t slot_bytes(uint32_t chunk_symbols) {
-  return 16 + pad16(chunk_symbols);
+// Bytes of a raw (uncoded) record of n symbols: the largest record.
+inline constexpr uint64_t raw_record_bytes(uint64_t n) { return sizeof(ChunkHeader) + pad16(n); }
+
+// Bytes before the word blocks of a coded record with alphabet A.
+inline constexpr uint64_t coded_prefix_bytes(uint32_t A) {
+  return sizeof(ChunkHeader) + pad16(2ull * A) + 4ull * kStreams * kLanes;
 }
+
+// Staging slot of one chunk (encoder): the record prefix (header,
+// frequencies, states; or the whole raw record) from the slot start, then one
+// region per stream whose words are written backwards from the region's end.
+constexpr uint64_t kPrefixArea = 1024;
+static_assert(kPrefixArea >= sizeof(ChunkHeader) + 512 + 4 * kStreams * kLanes, "prefix area");
+inline constexpr uint64_t region_bytes(uint32_t cs) { return pad16(cs) + 16; }
+inline constexpr uint64_t slot_bytes(uint32_t cs) { return kPrefixArea + kStreams * region_bytes(cs); }
 
 inline constexpr uint64_t directory_bytes(uint32_t n_chunks) {
   return sizeof(StreamHeader) + 8ull * (n_chunks + 1);
@@ -75,8 +94,12 @@ inline constexpr uint32_t num_chunks(uint64_t n, uint32_t cs) {
 
 // Upper bound of an encoded stream (every chunk raw).
 inline constexpr uint64_t max_stream_bytes(uint64_t n, uint32_t cs) {
-  return pad16(directory_bytes(num_chunks(n, cs))) + num_chunks(n, cs) * slot_bytes(cs);
+  return pad16(directory_bytes(num_chunks(n, cs))) + num_chunks(n, cs) * raw_record_bytes(cs);
 }
+
+// Per chunk of the encoder's scratch (uint32 words): record length, prefix
+// length, byte length of each word block, staging offset of each word block.
+constexpr int kDescWords = 6;
 
 // Per-symbol encoder entry.
 struct EncSym {
