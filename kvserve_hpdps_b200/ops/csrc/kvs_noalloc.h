@@ -14,9 +14,9 @@
 // size buffers; this variant needs none.
 //
 // How: its scratch lives in file-scope __device__ arrays of fixed size
-// (about 16.8 MB of staging plus 4 KB of record sizes).  Every GPU that loads
-// the library holds that memory until the process exits.  The caller still
-// passes the input and the output buffers.
+// (about 34 MB of staging plus 16 KB of record descriptors).  Every GPU that
+// loads the library holds that memory until the process exits.  The caller
+// still passes the input and the output buffers.
 //
 // Contract:
 //  * n must be between 1 and kvs_rans_encode_noalloc_max_symbols() bytes;
@@ -26,9 +26,14 @@
 //  * the stream is byte-identical to the one kvs_rans_encode writes for the
 //    same input with 32768-symbol chunks; its total size is stored in the
 //    stream header (bytes 24..31, little endian);
-//  * the first call on a device looks up the device address of the scratch
-//    arrays with that device current; make that first call before any CUDA
-//    stream capture on the device;
+//  * the first call in a CUDA context looks up the device address of the
+//    scratch arrays with that context current (the arrays belong to the
+//    library's module, loaded once per context; the lookup is kept per device
+//    and redone when the current context differs, e.g. after cudaDeviceReset
+//    or under a driver-API context of the caller's); make that first call
+//    before any CUDA stream capture in the context;
+//  * a launch error of this call is returned as KVS_NOALLOC_LAUNCH; an error
+//    left pending by unrelated earlier work is neither reported nor cleared;
 //  * all calls share one scratch area per device and it keeps the previous
 //    call's contents (every byte the encoder reads is written earlier in the
 //    same call, so nothing needs clearing); calls whose work overlaps on the
