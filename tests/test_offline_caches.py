@@ -239,3 +239,56 @@ def test_lm_eval_model_args_split():
     assert p == {} and rest == {"nbits": 2}
     with pytest.raises(ValueError):
         split_cache_args("zip", {})
+
+
+def test_register_lm_eval_model_runs_with_a_cache(model, monkeypatch):
+    """``register_lm_eval`` against a stand-in of lm-eval's registry and HFLM
+    base class (lm-eval itself is not installed): the registered class takes
+    the reference wrapper's bare model_args, builds the cache method, and its
+    ``_model_generate`` (what lm-eval calls for generation tasks) decodes with
+    that cache -- greedy tokens identical to the plain model for the default
+    cache, and mostly identical for the hybrid cache."""
+    import sys
+    import types
+
+    registry: dict = {}
+
+    def register_model(name):
+        def deco(cls):
+            registry[name] = cls
+            return cls
+        return deco
+
+    class HFLM:  # what the registered class needs from lm-eval's base class
+        def __init__(self, pretrained=None, batch_size=1, **kw):
+            self.model = pretrained
+            self.batch_size = batch_size
+            self.tokenizer = types.SimpleNamespace(pad_token_id=0)
+
+    mods = {"lm_eval": types.ModuleType("lm_eval"),
+            "lm_eval.api": types.ModuleType("lm_eval.api"),
+            "lm_eval.api.registry": types.ModuleType("lm_eval.api.registry"),
+            "lm_eval.models": types.ModuleType("lm_eval.models"),
+            "lm_eval.models.huggingface": types.ModuleType("lm_eval.models.huggingface")}
+    mods["lm_eval.api.registry"].register_model = register_model
+    mods["lm_eval.models.huggingface"].HFLM = HFLM
+    for k, v in mods.items():
+        monkeypatch.setitem(sys.modules, k, v)
+    from kvserve_hpdps_b200.offline.lm_harness import register_lm_eval
+    cls = register_lm_eval()
+    assert registry["my_custom_model"] is cls
+    ctx = torch.randint(0, 256, (1, 200), generator=torch.Generator().manual_seed(3))
+    plain = model.generate(input_ids=ctx, max_length=224, do_sample=False, pad_token_id=0)
+    lm = cls(pretrained=model, batch_size=1, cache_type="default")
+    out = lm._model_generate(ctx, 224, None)
+    assert torch.equal(out, plain)
+    lm = cls(pretrained=model, batch_size=1, cache_type="custom", transform_type="hadamard",
+             heads_selection=0.5, high_key_max_value=255, high_value_max_value=255,
+             low_key_max_value=15, low_value_max_value=15,
+             scores=None)
+    out = lm._model_generate(ctx, 224, None)
+    assert out.shape == plain.shape
+    assert torch.equal(out[:, :200], ctx)
+    agree = float((out[:, 200:] == plain[:, 200:]).float().mean())
+    assert agree > 0.5, agree
+    assert lm._kvs.last_cache is not None and type(lm._kvs.last_cache).__name__ == "CustomCache"
