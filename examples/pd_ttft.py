@@ -57,18 +57,60 @@ QWEN25_7B = {
 }
 
 
-def write_model_dir(path: str) -> str:
+LLAMA3_8B = {
+    "architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_act": "silu",
+    "hidden_size": 4096, "intermediate_size": 14336, "num_hidden_layers": 32,
+    "num_attention_heads": 32, "num_key_value_heads": 8, "vocab_size": 128256,
+    "max_position_embeddings": 32768, "rope_theta": 500000.0, "rms_norm_eps": 1e-5,
+    "tie_word_embeddings": False, "torch_dtype": "bfloat16", "bos_token_id": 128000,
+    "eos_token_id": 128009, "attention_dropout": 0.0, "initializer_range": 0.02,
+    "use_cache": True, "head_dim": 128,
+}
+
+QWEN25_32B = dict(QWEN25_7B, hidden_size=5120, intermediate_size=27648, num_hidden_layers=64,
+                  num_attention_heads=40, num_key_value_heads=8, max_window_layers=64)
+
+ARCHS = {"qwen2.5-7b": ("Qwen2.5-7B-Instruct", QWEN25_7B),
+         "llama-3-8b": ("Llama-3-8B-Instruct", LLAMA3_8B),
+         "qwen2.5-32b": ("Qwen2.5-32B-Instruct", QWEN25_32B)}
+
+
+def write_model_dir(path: str, config: dict = QWEN25_7B) -> str:
     os.makedirs(path, exist_ok=True)
     with open(os.path.join(path, "config.json"), "w") as f:
-        json.dump(QWEN25_7B, f)
+        json.dump(config, f)
     return path
 
 
-def compression_spec(name: str):
+def write_controller_library(path: str, model_name: str) -> str:
+    """A profile library over hybrid_ratio 0 / 0.3 / 1.0 of the default
+    quantizer (fused path, rANS), with the compression ratios measured by the
+    handoff sweep on Qwen2.5-7B shapes and accuracy standing in as the
+    reconstruction cosine; harmonic speed in MB/s of original KV."""
+    from kvserve_hpdps_b200.offline.library_export import build_library, write_library
+
+    def spec(cfg):
+        return {"enabled": True, "pipeline": ["quantizer", "codec"],
+                "quantizer_config": dict(cfg, model_name=model_name),
+                "codec_config": {"codec_type": "rans"}, "min_compress_size": 0}
+    base = {"high_key_max_value": 12, "high_value_max_value": 8, "low_key_max_value": 6,
+            "low_value_max_value": 4}
+    evals = [{"candidate": f"h{hr}", "config": dict(base, hybrid_ratio=hr), "accuracy": acc,
+              "compression_ratio": cr, "harmonic_speed_mbps": 4.0e5}
+             for hr, acc, cr in ((0.0, 0.96, 6.4), (0.3, 0.95, 7.1), (1.0, 0.93, 11.0))]
+    write_library(path, build_library(evals, model_name, spec_builder=spec))
+    return path
+
+
+def compression_spec(name: str, args=None):
     if name == "none":
         return None
     if name == "default":
         return "default"
+    if name == "controller":  # BASELINE config 3: slo 200 ms, accuracy 0.92
+        return {"mode": "controller", "library_path": args.library, "epsilon": 0.1,
+                "service_config": {"bandwidth_mbps": 10000, "slo_ms": 200.0,
+                                   "accuracy_requirement": 0.92, "t_model_ms": 0.0}}
     if name == "quantizer":  # the reference's degraded custom pipeline (no codec)
         return {"enabled": True, "pipeline": ["quantizer"],
                 "quantizer_config": {"hybrid_ratio": 0.8, "high_key_max_value": 12,
@@ -93,7 +135,7 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
         from vllm.config import KVTransferConfig
         module = ("kvserve_v1.connector.compressed_kv_connector" if args.impl == "reference"
                   else "kvserve_hpdps_b200.connector.compressed_kv_connector")
-        extra = {"compression": compression_spec(args.compression)}
+        extra = {"compression": compression_spec(args.compression, args)}
         if args.impl != "reference":
             extra["transport"] = args.transport
         ktc = KVTransferConfig(kv_connector="CompressedKVConnector",
@@ -154,7 +196,10 @@ def _stats_summary():
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--compression", choices=["default", "none", "quantizer"], default="default")
+    ap.add_argument("--compression", choices=["default", "none", "quantizer", "controller"],
+                    default="default")
+    ap.add_argument("--arch", choices=sorted(ARCHS), default="qwen2.5-7b",
+                    help="random-init architecture (Qwen2.5-7B, Llama-3-8B, Qwen2.5-32B)")
     ap.add_argument("--transport", default="auto", help="ours: auto | p2p | nccl")
     ap.add_argument("--requests", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=2)
@@ -171,7 +216,12 @@ def main(argv=None) -> int:
     ap.add_argument("--mem-util", type=float, default=0.5)
     ap.add_argument("--timeout", type=float, default=900.0)
     args = ap.parse_args(argv)
-    args.model_dir = write_model_dir(os.path.join(tempfile.gettempdir(), "kvs_qwen25_7b_dummy"))
+    name, arch_cfg = ARCHS[args.arch]
+    args.model_dir = write_model_dir(os.path.join(tempfile.gettempdir(),
+                                                  f"kvs_{args.arch}_dummy", name), arch_cfg)
+    if args.compression == "controller":
+        args.library = write_controller_library(
+            os.path.join(tempfile.gettempdir(), f"kvs_library_{args.arch}.json"), name)
     if args.role != "both":
         return run_one_role(args)
     gpus = args.gpus.split(",")
@@ -204,7 +254,8 @@ def main(argv=None) -> int:
             m = get()
             ready.add(m[1])
         ttft, prefill, first_tokens, agree = [], [], [], []
-        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len)):
+        vocab = ARCHS[args.arch][1]["vocab_size"]
+        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len, vocab)):
             t0 = time.time()
             qp.put(("go", i, ids))
             qc.put(("go", i, ids))
@@ -220,7 +271,7 @@ def main(argv=None) -> int:
                 # transfer): the consumer's must match it exactly for raw KV
                 agree.append(got["c"][4][:1] == got["p"][4][:1])
         q = sorted(ttft)
-        line = {"metric": "p50 TTFT, 1P1D (Qwen2.5-7B random-init, 8K prompt)",
+        line = {"metric": f"p50 TTFT, 1P1D ({name} random-init, {args.prompt_len} prompt)",
                 "overlap": os.environ.get("KVSERVE_OVERLAP_MODE", "off"), "tp": args.tp,
                 "max_tokens": args.max_tokens,
                 "impl": args.impl, "compression": args.compression,
@@ -285,12 +336,11 @@ def timeline_breakdown(path, skip: int = 0):
     return out or None
 
 
-def prompts(n: int, prompt_len: int) -> list:
+def prompts(n: int, prompt_len: int, vocab: int = QWEN25_7B["vocab_size"]) -> list:
     """The deterministic request sequence both sides generate on their own."""
     import random
     rng = random.Random(0)
-    return [[rng.randrange(0, QWEN25_7B["vocab_size"]) for _ in range(prompt_len)]
-            for _ in range(n)]
+    return [[rng.randrange(0, vocab) for _ in range(prompt_len)] for _ in range(n)]
 
 
 def run_one_role(args) -> int:
@@ -311,7 +361,8 @@ def run_one_role(args) -> int:
         m = q_out.get(timeout=args.timeout)
         if m[0] == "error":
             raise RuntimeError(m[2])
-        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len)):
+        vocab = ARCHS[args.arch][1]["vocab_size"]
+        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len, vocab)):
             t0 = time.time()
             q_in.put(("go", i, ids))
             m = q_out.get(timeout=args.timeout)
