@@ -44,6 +44,7 @@ import sys
 import torch
 
 STAGES = ("quant", "dequant", "rans_enc", "rans_dec", "lc_enc", "lc_dec", "block_copy")
+PEER_STAGES = ("quant_peer", "rans_enc_peer")
 METHODS = ("custom", "kivi", "cachegen", "hadamard", "minmax")
 
 
@@ -150,10 +151,16 @@ def run_methods(methods: tuple[str, ...] = METHODS, layers: int = 28, tokens: in
 def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
         only: tuple[str, ...] = STAGES, engine: int = 0, seed: int = 1,
         key_levels=(12, 6, 6, 6), value_levels=(8, 4, 4, 4), warmup: int = 3,
-        code_width: int = 8, hybrid_ratio: float | None = None) -> list[dict]:
+        code_width: int = 8, hybrid_ratio: float | None = None,
+        peer: int | None = None) -> list[dict]:
     """Stage timings.  With ``hybrid_ratio`` the per-layer plans are the
     default compression mode's (head-score mask at that ratio, nibble codes)
-    instead of the fixed ``key_levels``/``value_levels``."""
+    instead of the fixed ``key_levels``/``value_levels``.  With ``peer`` (a
+    second GPU of this process) the stages ``quant_peer`` and
+    ``rans_enc_peer`` time the producer kernels of the direct transfer path:
+    the quantize kernel storing its codes into that GPU's memory over NVLink
+    (message checksum on), and the rANS encoder whose compaction kernel
+    stores the coded stream there."""
     from kvserve_hpdps_b200.models.synthetic import paged_workload
     from kvserve_hpdps_b200.ops import kernels as K
     wl = paged_workload(layers, [tokens], heads, device="cuda", seed=seed, fill=False)
@@ -212,6 +219,27 @@ def run(layers: int = 28, tokens: int = 8192, heads: int = 4, iters: int = 10,
             dec_lc = torch.empty(n, dtype=torch.uint8, device="cuda")
             row("lc_dec", _timeit(lambda: K.lc_decode(lc_stream, n, out=dec_lc), iters, warmup),
                 exact=bool(torch.equal(K.lc_decode(lc_stream, n), codes)))
+    if peer is not None and ("quant_peer" in only or "rans_enc_peer" in only):
+        from kvserve_hpdps_b200.parallel.p2p import DeviceRegion, enable_peer_access
+        from kvserve_hpdps_b200.parallel.p2p_transport import tensor_view
+        here = torch.cuda.current_device()
+        enable_peer_access(here, peer)
+        torch.cuda.set_device(here)
+        region = DeviceRegion(peer, 16 + K.rans_max_bytes(n) + 4096)
+        torch.cuda.set_device(here)
+        ck = torch.zeros(2, dtype=torch.int64, device="cuda")
+        if "quant_peer" in only:
+            codes_peer = tensor_view(region.ptr, n, torch.uint8, [n], peer)
+            row("quant_peer", _timeit(lambda: K.quantize(slots, items, codes=codes_peer, meta=meta,
+                                                         engine=engine, ck=ck), iters, warmup),
+                engine=engine, peer=peer, code_bytes_over_link=n)
+        if "rans_enc_peer" in only:
+            row("rans_enc_peer", _timeit(lambda: K.rans_encode_message(
+                codes.data_ptr(), n, region.ptr + 16, torch.device("cuda", here),
+                prefix=[0, 1, n & 0xFFFFFFFF, n >> 32], msg_off=16, ck=ck), iters, warmup),
+                peer=peer, stream_bytes_over_link=int(stream.numel()))
+        torch.cuda.synchronize()
+        region.close()
     if "block_copy" in only:
         flat = torch.empty(nbytes // layers, dtype=torch.uint8, device="cuda")
         blocks = torch.tensor(wl.block_ids[0], dtype=torch.int32, device="cuda")
@@ -253,6 +281,8 @@ def main(argv=None) -> int:
     ap.add_argument("--methods", default=None,
                     help=f"time offline methods instead of the fused stages: {','.join(METHODS)}")
     ap.add_argument("--device", default=None, help="--methods device (default: cuda if present)")
+    ap.add_argument("--peer", type=int, default=None,
+                    help="second GPU for the direct-path stages (--only quant_peer,rans_enc_peer)")
     args = ap.parse_args(argv)
     if args.methods:
         for r in run_methods(tuple(args.methods.split(",")), args.layers, args.tokens, args.heads,
@@ -264,7 +294,7 @@ def main(argv=None) -> int:
         return 0
     for r in run(args.layers, args.tokens, args.heads, args.iters,
                  tuple(args.only.split(",")), args.engine, warmup=args.warmup,
-                 code_width=args.code_width, hybrid_ratio=args.hybrid_ratio):
+                 code_width=args.code_width, hybrid_ratio=args.hybrid_ratio, peer=args.peer):
         print(json.dumps(r))
     return 0
 
