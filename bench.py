@@ -300,18 +300,24 @@ def _events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def _timed_loop(step, s0: int, steps: int, world: int, device, sampler=None):
+def _timed_loop(step, s0: int, steps: int, world: int, device, side_streams=()):
     """``steps`` steps between a barrier + device synchronisation on both
-    sides, timed with CUDA events on the current stream; returns (max ms
-    over ranks, next step index)."""
+    sides, timed with CUDA events on the current stream (work a step queues
+    on ``side_streams`` starts after the first event and is joined before the
+    second); returns (max ms over ranks, next step index)."""
     barrier(world)
     torch.cuda.synchronize(device)
+    main = torch.cuda.current_stream(device)
     ev0, ev1 = _events()
     ev0.record()
+    for st in side_streams:
+        st.wait_stream(main)
     s = s0
     for _ in range(steps):
         step(s)
         s += 1
+    for st in side_streams:
+        main.wait_stream(st)
     ev1.record()
     torch.cuda.synchronize(device)
     barrier(world)
@@ -526,9 +532,17 @@ def run_path(args, mgr, wl, rank, world, local, e2e: bool, latency: bool, clocks
         mgr.decompress_paged_requests(cd, wl.dst_layers(), reqs)
         tr.release(payload, device)
 
+    # Consecutive messages of a producer alternate between two streams: the
+    # statistics pass of message s+1 (HBM-bound) runs while message s's
+    # quantize kernel stores over NVLink (link-bound).  Kernel scratch is per
+    # stream, and the ring transport orders nothing by stream.
+    prod_streams = [torch.cuda.Stream(device), torch.cuda.Stream(device)] \
+        if role == "producer" else []
+
     def step(s):
         if role == "producer":
-            produce(s, wl.src_req, [f"{s}:{r}" for r in range(wl.B)])
+            with torch.cuda.stream(prod_streams[s % 2]):
+                produce(s, wl.src_req, [f"{s}:{r}" for r in range(wl.B)])
         else:
             consume(s, wl.dst_req)
     out["transport"] = ("nvlink-p2p ring: FusedCompressionManager.send_paged_requests -> "
@@ -559,9 +573,7 @@ def run_path(args, mgr, wl, rank, world, local, e2e: bool, latency: bool, clocks
         sampler.start()
         time.sleep(0.3)
 
-    def timed_step(s):
-        step(s)
-    out["ms"], s = _timed_loop(timed_step, s, args.steps, world, device)
+    out["ms"], s = _timed_loop(step, s, args.steps, world, device, side_streams=prod_streams)
     if sampler:
         out["clocks"] = sampler.stop()
     if role == "producer":

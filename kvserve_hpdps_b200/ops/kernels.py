@@ -70,11 +70,14 @@ def _stream(device: torch.device) -> int:
 
 # ----------------------------------------------------------------- workspace
 class _Workspace:
-    """Per-device scratch reused across launches (grown on demand)."""
+    """Scratch of one (device, stream) reused across launches (grown on
+    demand): kernels queued on different streams may run at the same time,
+    so each stream has its own buffers and completion counters; the device
+    error word is shared by every stream of the device."""
 
-    def __init__(self, device: torch.device):
+    def __init__(self, device: torch.device, err: torch.Tensor):
         self.device = device
-        self.err = torch.zeros(4, dtype=torch.int32, device=device)
+        self.err = err
         self.counters = torch.zeros(64, dtype=torch.int32, device=device)
         self._bufs: dict[str, torch.Tensor] = {}
         self._lock = threading.Lock()
@@ -91,15 +94,24 @@ class _Workspace:
 
 
 _ws: dict[tuple, _Workspace] = {}
+_err_words: dict[int, torch.Tensor] = {}
 _ws_lock = threading.Lock()
 
 
 def workspace(device: torch.device) -> _Workspace:
-    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    """The scratch of ``device``'s current stream."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(idx).cuda_stream
+    key = (device.type, idx, stream)
     with _ws_lock:
-        if key not in _ws:
-            _ws[key] = _Workspace(torch.device("cuda", key[1]))
-        return _ws[key]
+        ws = _ws.get(key)
+        if ws is None:
+            dev = torch.device("cuda", idx)
+            err = _err_words.get(idx)
+            if err is None:
+                err = _err_words[idx] = torch.zeros(4, dtype=torch.int32, device=dev)
+            ws = _ws[key] = _Workspace(dev, err)
+        return ws
 
 
 def read_device_error(device: torch.device, reset: bool = True) -> int:
