@@ -132,6 +132,7 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
         sys.path.insert(0, ROOT)
     try:
         from vllm import LLM, SamplingParams
+        from vllm.sampling_params import RequestOutputKind
         from vllm.config import KVTransferConfig
         module = ("kvserve_v1.connector.compressed_kv_connector" if args.impl == "reference"
                   else "kvserve_hpdps_b200.connector.compressed_kv_connector")
@@ -145,8 +146,10 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
                                kv_ip=args.kv_ip, kv_port=args.port,
                                kv_connector_extra_config=extra)
         llm = LLM(model=args.model_dir, dtype="bfloat16", load_format="dummy",
-                  skip_tokenizer_init=True, max_model_len=args.prompt_len + args.max_tokens + 64,
-                  max_num_batched_tokens=args.prompt_len + 64, max_num_seqs=8,
+                  skip_tokenizer_init=True,
+                  max_model_len=max(args.prompt_len, args.prompt_len_max) + args.max_tokens + 64,
+                  max_num_batched_tokens=max(args.prompt_len, args.prompt_len_max) + 64,
+                  max_num_seqs=8,
                   gpu_memory_utilization=args.mem_util, enforce_eager=True,
                   enable_prefix_caching=False, kv_transfer_config=ktc, seed=0,
                   tensor_parallel_size=args.tp)
@@ -158,24 +161,18 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
                 break
             _, i, ids = msg
             sp = SamplingParams(max_tokens=1 if role == "p" else args.max_tokens, temperature=0.0,
-                                detokenize=False,
+                                detokenize=False, output_kind=RequestOutputKind.CUMULATIVE,
                                 extra_args={"kv_transfer_params": {"transfer_id": f"req-{i}"}})
-            # drive the engine step by step: the first token's arrival is the
-            # TTFT even when more tokens follow
-            rid = eng.add_request(f"{role}{i}", {"prompt_token_ids": ids}, sp) or f"{role}{i}"
+            # drive the engine step by step (one request in flight): the first
+            # token's arrival is the TTFT even when more tokens follow
+            eng.add_request(f"{role}{i}", {"prompt_token_ids": ids}, sp)
             t_first, toks = None, []
-            while True:
-                outs = eng.step()
-                fin = False
-                for o in outs:
-                    if getattr(o, "request_id", None) != rid:
-                        continue
-                    toks = list(o.outputs[0].token_ids) if o.outputs else toks
-                    if toks and t_first is None:
-                        t_first = time.time()
-                    fin = fin or o.finished
-                if fin:
-                    break
+            while eng.has_unfinished_requests():
+                for o in eng.step():
+                    if o.outputs and len(o.outputs[0].token_ids) > len(toks):
+                        toks = list(o.outputs[0].token_ids)  # cumulative outputs
+                        if t_first is None:
+                            t_first = time.time()
             q_out.put(("done", role, i, t_first or time.time(), toks, time.time()))
     except Exception:  # noqa: BLE001
         import traceback
@@ -204,6 +201,8 @@ def main(argv=None) -> int:
     ap.add_argument("--requests", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--prompt-len", type=int, default=8192)
+    ap.add_argument("--prompt-len-max", type=int, default=0,
+                    help="lengths uniform in [--prompt-len, this] (config 3: 2048..16384)")
     ap.add_argument("--max-tokens", type=int, default=1)
     ap.add_argument("--gpus", default="0,1",
                     help="producer GPUs then consumer GPUs (tp of each; one role: its tp GPUs)")
@@ -255,7 +254,8 @@ def main(argv=None) -> int:
             ready.add(m[1])
         ttft, prefill, first_tokens, agree = [], [], [], []
         vocab = ARCHS[args.arch][1]["vocab_size"]
-        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len, vocab)):
+        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len, vocab,
+                                        args.prompt_len_max)):
             t0 = time.time()
             qp.put(("go", i, ids))
             qc.put(("go", i, ids))
@@ -336,11 +336,17 @@ def timeline_breakdown(path, skip: int = 0):
     return out or None
 
 
-def prompts(n: int, prompt_len: int, vocab: int = QWEN25_7B["vocab_size"]) -> list:
-    """The deterministic request sequence both sides generate on their own."""
+def prompts(n: int, prompt_len: int, vocab: int = QWEN25_7B["vocab_size"],
+            prompt_len_max: int = 0) -> list:
+    """The deterministic request sequence both sides generate on their own
+    (lengths uniform in [prompt_len, prompt_len_max] when the latter is set)."""
     import random
     rng = random.Random(0)
-    return [[rng.randrange(0, vocab) for _ in range(prompt_len)] for _ in range(n)]
+    out = []
+    for _ in range(n):
+        t = rng.randint(prompt_len, prompt_len_max) if prompt_len_max > prompt_len else prompt_len
+        out.append([rng.randrange(0, vocab) for _ in range(t)])
+    return out
 
 
 def run_one_role(args) -> int:
@@ -362,7 +368,8 @@ def run_one_role(args) -> int:
         if m[0] == "error":
             raise RuntimeError(m[2])
         vocab = ARCHS[args.arch][1]["vocab_size"]
-        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len, vocab)):
+        for i, ids in enumerate(prompts(args.warmup + args.requests, args.prompt_len, vocab,
+                                        args.prompt_len_max)):
             t0 = time.time()
             q_in.put(("go", i, ids))
             m = q_out.get(timeout=args.timeout)
