@@ -216,11 +216,22 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
+def outlier_channels(num_heads: int, head_dim: int, fraction: float, seed: int) -> torch.Tensor:
+    """Bool [H, D]: round(fraction * D) channels per head, drawn with a seeded
+    CPU generator (the same workload for both arms, built without importing
+    either framework)."""
+    g = torch.Generator().manual_seed(seed)
+    k = max(1, round(fraction * head_dim))
+    mask = torch.zeros(num_heads, head_dim, dtype=torch.bool)
+    for h in range(num_heads):
+        mask[h, torch.randperm(head_dim, generator=g)[:k]] = True
+    return mask
+
+
 class Workload:
     """Source and destination paged caches for one rank."""
 
     def __init__(self, args, device, seed, role="both"):
-        from kvserve_hpdps_b200.models.synthetic import outlier_channels
         L, H, bs, T, B = args.layers, args.kv_heads, args.block_size, args.tokens, args.requests_per_step
         nb = (T + bs - 1) // bs
         self.nblocks = B * nb + 7
@@ -269,8 +280,15 @@ def quant_config(args, codec=None):
     return cfg
 
 
+# the default mode's quantizer in both frameworks (hybrid ratio, high key /
+# value levels, low key / value levels)
+DEFAULT_QUANTIZER = {"hybrid_ratio": 0.8, "high_key_max_value": 12, "high_value_max_value": 8,
+                     "low_key_max_value": 6, "low_value_max_value": 4}
+
+
 def hybrid_ratio(args) -> float:
-    return float(quant_config(args)["quantizer_config"]["hybrid_ratio"])
+    hr = getattr(args, "hybrid_ratio", None)
+    return float(hr) if hr is not None else DEFAULT_QUANTIZER["hybrid_ratio"]
 
 
 def compression_label(args, codec=None) -> str:
@@ -787,8 +805,7 @@ class _RefPipeline:
         from kvserve_v1.compression.compression_manager import CompressedKVData
         from kvserve_v1.compression.tilelang_manager import _canon_meta, _decanon_meta
         from kvserve_v1.tilelang_ops.kv_hadamard_quant import KVHadamardQuantOp
-        qc = {"model_name": MODEL, "hybrid_ratio": hybrid_ratio(args), "high_key_max_value": 12,
-              "high_value_max_value": 8, "low_key_max_value": 6, "low_value_max_value": 4}
+        qc = dict(DEFAULT_QUANTIZER, model_name=MODEL, hybrid_ratio=hybrid_ratio(args))
         self.op = KVHadamardQuantOp(num_heads=args.kv_heads, head_dim=128, base_seed=HADAMARD_SEED,
                                     dtype=torch.bfloat16, quant_type="minmax",
                                     axis_key="channel", axis_value="token", split_type="head",

@@ -104,3 +104,19 @@ def test_rank_pairing_for_every_scaling_point():
             assert r % pairs == (r + pairs) % pairs  # the pair id both sides derive
     with pytest.raises(SystemExit):
         bench._roles(3, 0)
+
+
+def test_reference_arm_imports_nothing_of_this_package():
+    """The reference arm's workload, labels and pipeline set-up come from
+    bench.py itself: running them in a fresh interpreter loads no module of
+    this package."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r); import bench; "
+            "a = bench.parse_args(['--impl', 'reference']); "
+            "bench.compression_label(a); bench.hybrid_ratio(a); "
+            "bench.outlier_channels(4, 128, 0.03, 3); "
+            "print(sorted(m for m in sys.modules if m.startswith('kvserve_hpdps_b200')))" % ROOT)
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.strip().splitlines()[-1] == "[]"
