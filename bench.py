@@ -84,6 +84,8 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--kv-heads", type=int, default=4)
     ap.add_argument("--block-size", type=int, default=16)
+    ap.add_argument("--kv-layout", default="hnd", choices=["hnd", "nhd"],
+                    help="paged block layout: hnd (head-major, vLLM FlashInfer on B200) or nhd")
     ap.add_argument("--codec", default="none", choices=["none", "rans", "bitpack"],
                     help="codec of the headline path (none: the stages both arms can run)")
     ap.add_argument("--no-full-path", action="store_true",
@@ -241,19 +243,29 @@ class Workload:
         perm_dst = torch.randperm(self.nblocks, generator=g).tolist()
         self.src_req = [(perm_src[i * nb:(i + 1) * nb], T) for i in range(B)]
         self.dst_req = [(perm_dst[i * nb:(i + 1) * nb], T) for i in range(B)]
-        shape = (L, 2, self.nblocks, bs, H, 128)
+        self.layout = getattr(args, "kv_layout", "hnd")
         self.src = self.dst = None
         if role in ("both", "producer"):
-            self.src = torch.empty(shape, dtype=torch.bfloat16, device=device)
+            self.src = self._alloc(L, H, bs, device, zero=False)
             gd = torch.Generator(device=device).manual_seed(seed + 17)
             for l in range(L):  # fill layer by layer to bound temporaries
                 self.src[l].normal_(generator=gd)
             m = outlier_channels(H, 128, fraction=0.03, seed=seed + 3).to(device)
             scale = torch.where(m, 12.0, 1.0).to(torch.bfloat16)
             for l in range(L):
-                self.src[l, 0].view(-1, H, 128).mul_(scale)
+                self.src[l, 0].mul_(scale)  # [nb, bs, H, D] * [H, D]
         if role in ("both", "consumer"):
-            self.dst = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+            self.dst = self._alloc(L, H, bs, device, zero=True)
+
+    def _alloc(self, L, H, bs, device, zero):
+        """Logical [L, 2, nblocks, bs, H, D] paged caches.  HND: each block
+        stores its heads one after another (head-major), the layout vLLM's
+        FlashInfer backend allocates on B200; NHD: token-major blocks."""
+        make = torch.zeros if zero else torch.empty
+        if self.layout == "hnd":
+            t = make((L, 2, self.nblocks, H, bs, 128), dtype=torch.bfloat16, device=device)
+            return t.permute(0, 1, 2, 4, 3, 5)
+        return make((L, 2, self.nblocks, bs, H, 128), dtype=torch.bfloat16, device=device)
 
     @property
     def bf16_bytes_per_request(self) -> int:
@@ -1075,6 +1087,8 @@ def build_line(args, res, world):
             "parallelism": "1-GPU round trip" if world == 1 else f"1P1D x{pairs} pairs (TP1)",
             "compression": compression_label(args),
             "requests_per_step": args.requests_per_step,
+            "kv_layout": ("HND head-major blocks (vLLM FlashInfer on B200)"
+                          if args.kv_layout == "hnd" else "NHD token-major blocks"),
             "value_definition": "ms per request of one producer/consumer pair (N=1: one GPU "
                                 "does both halves)",
             "l2": "inputs larger than L2 (%.1f GB of KV per step per producer)"

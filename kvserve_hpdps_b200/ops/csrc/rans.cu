@@ -17,11 +17,29 @@
 namespace kvs {
 namespace rans {
 
+// Occupancy: a chunk is one warp's work, so a launch finishes in one wave
+// only if every chunk's warp is resident at once.  Seven 4-warp CTAs per SM
+// (28 warps, at most 73 registers a thread and 32 KB of shared memory per
+// CTA) keep a 28-layer 8-request step (3585 chunks) in one wave.
 constexpr int kEncWarps = 4;
-constexpr int kHistCopies = 8;  // lane-interleaved histogram copies (spread the atomics)
-constexpr int kDecWarps = 8;
-constexpr int kRing = 1024;  // words of one stream's shared-memory ring in the decoder
+constexpr int kCtasPerSm = 7;
+constexpr int kHistCopies = 4;  // lane-interleaved histogram copies (spread the atomics)
+constexpr int kDecWarps = 4;
+constexpr int kRing = 512;  // words of one stream's shared-memory ring in the decoder
 constexpr int kDecWarpSmem = 4096 + 1024 + kStreams * kRing * 2;
+static_assert(kDecWarps * kDecWarpSmem <= 32 * 1024, "decoder shared memory per CTA");
+
+// Encoder table entry packed into 8 bytes (one 64-bit shared-memory load a
+// step): the reciprocal, and bias (13 bits) | f - 1 (12 bits) | shift (4 bits)
+// of the EncSym it stands for (rans.cuh: make_enc).
+struct EncPacked {
+  uint32_t rcp;
+  uint32_t w;
+};
+KVS_DEV EncPacked pack_enc(const EncSym& e) {
+  const uint32_t f = kProbScale - (e.cmpl_shift & 0xFFFFu);
+  return EncPacked{e.rcp, e.bias | ((f - 1) << 13) | ((e.cmpl_shift >> 16) << 25)};
+}
 
 // Where an encoded stream goes inside a transfer message (all optional).
 struct RansMsg {
@@ -127,7 +145,7 @@ KVS_DEV void normalize_counts_warp(const uint32_t* cnt, uint32_t A, uint64_t tot
 
 // Encoder table from frequencies: lane l owns the contiguous symbols
 // [l*per, (l+1)*per); cumulative frequencies come from a warp scan.
-KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncSym* enc, int lane) {
+KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncPacked* enc, int lane) {
   const uint32_t per = (A + 31) / 32;
   const uint32_t b = lane * per, e = min(A, b + per);
   uint32_t local = 0;
@@ -141,7 +159,7 @@ KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncSym* enc, int l
   uint32_t cum = incl - local;
   for (uint32_t s = b; s < e; ++s) {
     const uint32_t f = freq[s];
-    if (f > 0) enc[s] = make_enc(f, cum);
+    if (f > 0) enc[s] = pack_enc(make_enc(f, cum));
     cum += f;
   }
   __syncwarp();
@@ -151,14 +169,14 @@ KVS_DEV void build_enc_warp(const uint32_t* freq, uint32_t A, EncSym* enc, int l
 // length, the prefix length (header + frequencies + states, or the whole raw
 // record), the byte length of each stream's word block and the staging
 // offset of each word block (see rans.cuh).
-__global__ void __launch_bounds__(kEncWarps * 32, 6) k_rans_encode(
+__global__ void __launch_bounds__(kEncWarps * 32, kCtasPerSm) k_rans_encode(
     const uint8_t* __restrict__ in, uint64_t n, uint32_t cs, uint8_t* __restrict__ staging,
     uint32_t* __restrict__ desc, uint32_t n_chunks) {
-  // a warp's histogram (8 x 256 counts) is dead once its frequencies are
-  // normalised, so its encoder table (256 x 16 B) reuses the first 4 KB
+  // a warp's histogram (4 x 256 counts) is dead once its frequencies are
+  // normalised, so its encoder table (256 x 8 B) reuses its first 2 KB
   __shared__ __align__(16) uint32_t hist[kEncWarps][kHistCopies * 256];
   __shared__ uint32_t freq_s[kEncWarps][256];
-  static_assert(sizeof(EncSym) * 256 <= sizeof(uint32_t) * kHistCopies * 256, "table aliasing");
+  static_assert(sizeof(EncPacked) * 256 <= sizeof(uint32_t) * kHistCopies * 256, "table aliasing");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk = blockIdx.x * kEncWarps + warp;
   if (chunk >= n_chunks) return;  // warp-uniform
@@ -172,8 +190,8 @@ __global__ void __launch_bounds__(kEncWarps * 32, 6) k_rans_encode(
   uint32_t* h = hist[warp];
   for (int i = lane; i < kHistCopies * 256; i += 32) h[i] = 0;
   __syncwarp();
-  // Histogram in eight lane-interleaved copies (lane & 7): spreads the
-  // atomic traffic of skewed symbol distributions over eight addresses.
+  // Histogram in four lane-interleaved copies (lane & 3): spreads the
+  // atomic traffic of skewed symbol distributions over four addresses.
   uint32_t* hc = h + (lane & (kHistCopies - 1)) * 256;
   // the next super-step's symbols are loaded while this one is counted
   Syms32 nxt = load_syms(src, 0, lane, n_sym);
@@ -199,7 +217,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 6) k_rans_encode(
   const uint32_t A = static_cast<uint32_t>(top + 1);
   __syncwarp();
   normalize_counts_warp(h, A, static_cast<uint64_t>(n_ss) * kSuper, freq_s[warp], lane);
-  EncSym* enc = reinterpret_cast<EncSym*>(hist[warp]);
+  EncPacked* enc = reinterpret_cast<EncPacked*>(hist[warp]);
   build_enc_warp(freq_s[warp], A, enc, lane);
 
   // Words of stream k grow backwards from the end of region k.
@@ -230,11 +248,12 @@ __global__ void __launch_bounds__(kEncWarps * 32, 6) k_rans_encode(
 #pragma unroll
     for (int m = kSub - 1; m >= 0; --m) {
       const uint32_t s = (w[m >> 2] >> ((m & 3) * 8)) & 0xFFu;
-      const EncSym e = enc[s];
+      const EncPacked e = enc[s];
+      const uint32_t f = ((e.w >> 13) & 0xFFFu) + 1;
       uint32_t& x = (m & 1) ? x1 : x0;
       int& wpos = (m & 1) ? wpos1 : wpos0;
       uint16_t* words = (m & 1) ? words1 : words0;
-      const bool emit = x >= e.x_max;
+      const bool emit = x >= (f << kXmaxShift);
       const uint32_t mask = __ballot_sync(0xFFFFFFFFu, emit);
       const int cnt = __popc(mask);
       if (emit) {
@@ -242,8 +261,8 @@ __global__ void __launch_bounds__(kEncWarps * 32, 6) k_rans_encode(
         x >>= 16;
       }
       wpos -= cnt;
-      const uint32_t q = __umulhi(x, e.rcp) >> (e.cmpl_shift >> 16);
-      x = x + e.bias + q * (e.cmpl_shift & 0xFFFFu);
+      const uint32_t q = __umulhi(x, e.rcp) >> (e.w >> 25);
+      x = x + (e.w & 0x1FFFu) + q * (kProbScale - f);
     }
   }
   if (!overflow) {
@@ -406,14 +425,14 @@ __global__ void __launch_bounds__(256) k_rans_copy(
 // outside the buffers.
 //
 // Each stream's words reach shared memory through its own ring of kRing
-// words, filled with asynchronous 16-byte copies (256 words a group) half a
-// super-step ahead: at the start of each half (16 sub-steps, at most 256
-// words of a stream) the copies issued at the previous half's start are
-// waited for, then groups are issued while they fit before (read pointer +
-// kRing).  The previous half left the ring filled beyond its read pointer +
-// 768 and advanced that pointer by at most 256, so every word of the current
-// half has landed, and no copy overwrites a word not yet read.
-__global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* __restrict__ stream,
+// (512) words, filled with asynchronous 16-byte copies (128 words a group) a
+// quarter super-step ahead: at the start of each quarter (8 sub-steps, at most
+// 128 words of a stream) the copies issued at the previous quarter's start
+// are waited for, then groups are issued while they fit before (read pointer
+// + kRing).  The previous quarter left the ring filled beyond its read
+// pointer + 384 and advanced that pointer by at most 128, so every word of
+// the current quarter has landed, and no copy overwrites a word not yet read.
+__global__ void __launch_bounds__(kDecWarps * 32, kCtasPerSm) k_rans_decode(const uint8_t* __restrict__ stream,
                                                                uint64_t len,
                                                                uint8_t* __restrict__ out,
                                                                uint64_t n_expected, uint32_t cs,
@@ -492,14 +511,14 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   const uint32_t lt = lanemask_lt();
   auto refill = [&](uint16_t* ring, const uint16_t* src, uint32_t& loaded, uint32_t rptr,
                     uint64_t total) {
-    while (loaded + 256 <= rptr + kRing && loaded < total) {
-      const uint32_t idx = loaded + lane * 8;
+    while (loaded + 128 <= rptr + kRing && loaded < total) {
+      const uint32_t idx = loaded + lane * 4;  // 8 bytes a lane, 128 words a group
       if (idx < total)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(
                          smem_u32(ring + (idx & (kRing - 1)))),
                      "l"(src + idx)
                      : "memory");
-      loaded += 256;
+      loaded += 128;
     }
   };
   auto refill_both = [&]() {
@@ -512,13 +531,13 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_rans_decode(const uint8_t* _
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
     uint32_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    for (int quarter = 0; quarter < 4; ++quarter) {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
       __syncwarp();
-      refill_both();  // the next half's words, in flight during this half
+      refill_both();  // the next quarter's words, in flight during this one
 #pragma unroll
-      for (int mm = 0; mm < kSub / 2; ++mm) {
-        const int m = half * (kSub / 2) + mm;
+      for (int mm = 0; mm < kSub / 4; ++mm) {
+        const int m = quarter * (kSub / 4) + mm;
         uint32_t& x = (m & 1) ? x1 : x0;
         uint32_t& rp = (m & 1) ? rp1 : rp0;
         const uint16_t* ring = (m & 1) ? ring1 : ring0;
@@ -575,8 +594,8 @@ int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint32_t nc = num_chunks(n, cs);
   uint32_t* desc = sizes;
-  uint64_t* dst_off = reinterpret_cast<uint64_t*>(sizes + kDescWords * static_cast<uint64_t>(nc) +
-                                                  (nc & 1));  // 8-byte aligned
+  // 6 words per chunk keep the 64-bit offsets 8-byte aligned for any nc
+  uint64_t* dst_off = reinterpret_cast<uint64_t*>(sizes + kDescWords * static_cast<uint64_t>(nc));
   k_rans_encode<<<(nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32, 0, s>>>(in, n, cs, staging,
                                                                             desc, nc);
   k_rans_directory<<<1, 1024, 0, s>>>(desc, nc, n, cs, out, total_out, dst_off, m);
@@ -588,7 +607,7 @@ int kvs_rans_msg_size(void) { return static_cast<int>(sizeof(RansMsg)); }
 // uint32 words of the `sizes` scratch for n bytes in chunks of cs.
 uint64_t kvs_rans_sizes_words(uint64_t n, uint32_t cs) {
   const uint64_t nc = num_chunks(n, cs);
-  return kDescWords * nc + (nc & 1) + 2 * nc;
+  return (kDescWords + 2) * nc;
 }
 
 // Decode n bytes from a stream of `len` bytes (~0: unknown, the header's
@@ -629,7 +648,7 @@ constexpr uint32_t kNoAllocMaxChunks =
 static __device__ __align__(256) uint8_t g_noalloc_staging[kNoAllocMaxChunks *
                                                            slot_bytes(kNoAllocChunk)];
 // record descriptors and 64-bit output offsets (kvs_rans_encode's layout)
-static __device__ __align__(256) uint32_t g_noalloc_sizes[(kDescWords + 2) * kNoAllocMaxChunks + 1];
+static __device__ __align__(256) uint32_t g_noalloc_sizes[(kDescWords + 2) * kNoAllocMaxChunks];
 static __device__ __align__(256) uint64_t g_noalloc_total[2];
 
 // Device addresses of the scratch arrays, looked up with the context that
@@ -745,8 +764,7 @@ int kvs_rans_encode_noalloc(const uint8_t* in, uint64_t n, uint8_t* out, uint64_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint32_t nc = num_chunks(n, kNoAllocChunk);
   uint32_t* desc = s.sizes;
-  uint64_t* dst_off = reinterpret_cast<uint64_t*>(s.sizes + kDescWords * static_cast<uint64_t>(nc) +
-                                                  (nc & 1));
+  uint64_t* dst_off = reinterpret_cast<uint64_t*>(s.sizes + kDescWords * static_cast<uint64_t>(nc));
   const RansMsg none{};
   cudaError_t e = noalloc_launch(k_rans_encode, (nc + kEncWarps - 1) / kEncWarps, kEncWarps * 32,
                                  st, in, n, kNoAllocChunk, s.staging, desc, nc);

@@ -100,6 +100,7 @@ inline constexpr uint64_t max_stream_bytes(uint64_t n, uint32_t cs) {
 // Per chunk of the encoder's scratch (uint32 words): record length, prefix
 // length, byte length of each word block, staging offset of each word block.
 constexpr int kDescWords = 6;
+static_assert(kDescWords % 2 == 0, "the 64-bit output offsets after the descriptors stay aligned");
 
 // Per-symbol encoder entry.
 struct EncSym {
