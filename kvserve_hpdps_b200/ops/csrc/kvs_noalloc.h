@@ -19,6 +19,7 @@
 // still passes the input and the output buffers.
 //
 // Contract:
+//  * `in` and `out` must be 16-byte aligned (KVS_NOALLOC_UNALIGNED otherwise);
 //  * n must be between 1 and kvs_rans_encode_noalloc_max_symbols() bytes;
 //    larger inputs are rejected with KVS_NOALLOC_TOO_LARGE before anything
 //    is launched, and out_capacity must be at least kvs_rans_max_bytes(n,
@@ -50,6 +51,7 @@
 #define KVS_NOALLOC_NO_DEVICE (-5)
 #define KVS_NOALLOC_SYMBOL (-6)
 #define KVS_NOALLOC_LAUNCH (-7)
+#define KVS_NOALLOC_UNALIGNED (-8)
 
 extern "C" {
 

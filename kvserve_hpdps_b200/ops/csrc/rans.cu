@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, kCtasPerSm) k_rans_decode(cons
   const uint64_t* dir = reinterpret_cast<const uint64_t*>(stream + sizeof(StreamHeader));
   const uint64_t roff = dir[chunk];
   const uint64_t expect = min(static_cast<uint64_t>(cs), n_expected - static_cast<uint64_t>(chunk) * cs);
-  if (roff < dir_end || roff + sizeof(ChunkHeader) > hd.total_bytes) {
+  if (roff < dir_end || roff + sizeof(ChunkHeader) > hd.total_bytes || (roff & 15) != 0) {
     if (lane == 0) record_error(err, ERR_CORRUPT);
     return;
   }
@@ -588,6 +588,10 @@ uint64_t kvs_rans_staging_bytes(uint64_t n, uint32_t cs) {
 int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging, uint32_t* sizes,
                     uint8_t* out, uint64_t* total_out, const RansMsg* msg, void* stream) {
   if (n == 0 || cs == 0 || cs % kSuper != 0) return -2;
+  // the kernels move 16-byte words: input, output and scratch must be aligned
+  if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) |
+        reinterpret_cast<uintptr_t>(staging) | reinterpret_cast<uintptr_t>(sizes)) & 15) != 0)
+    return -3;
   RansMsg m{};
   if (msg != nullptr) m = *msg;
   if ((m.msg_off & 15) != 0) return -2;
@@ -615,6 +619,8 @@ uint64_t kvs_rans_sizes_words(uint64_t n, uint32_t cs) {
 int kvs_rans_decode(const uint8_t* stream_buf, uint64_t len, uint8_t* out, uint64_t n, uint32_t cs,
                     uint32_t* err, void* stream) {
   if (n == 0 || cs == 0) return -2;
+  if (((reinterpret_cast<uintptr_t>(stream_buf) | reinterpret_cast<uintptr_t>(out)) & 15) != 0)
+    return -3;  // 16-byte loads and stores
   const uint32_t nc = num_chunks(n, cs);
   const int smem = kDecWarps * kDecWarpSmem;
   cudaFuncSetAttribute(k_rans_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -759,6 +765,8 @@ int kvs_rans_encode_noalloc(const uint8_t* in, uint64_t n, uint8_t* out, uint64_
     return KVS_NOALLOC_TOO_LARGE;
   }
   if (out_capacity < max_stream_bytes(n, kNoAllocChunk)) return KVS_NOALLOC_OUT_TOO_SMALL;
+  if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) != 0)
+    return KVS_NOALLOC_UNALIGNED;
   NoAllocScratch s;
   if (int rc = noalloc_scratch(&s)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -790,6 +798,7 @@ const char* kvs_noalloc_strerror(int code) {
     case KVS_NOALLOC_NO_DEVICE: return "no current CUDA device";
     case KVS_NOALLOC_SYMBOL: return "cudaGetSymbolAddress of the scratch arrays failed";
     case KVS_NOALLOC_LAUNCH: return "kernel launch failed";
+    case KVS_NOALLOC_UNALIGNED: return "input or output not 16-byte aligned";
     default: return "unknown error";
   }
 }
