@@ -87,6 +87,8 @@ def write_controller_library(path: str, model_name: str) -> str:
     quantizer (fused path, rANS), with the compression ratios measured by the
     handoff sweep on Qwen2.5-7B shapes and accuracy standing in as the
     reconstruction cosine; harmonic speed in MB/s of original KV."""
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
     from kvserve_hpdps_b200.offline.library_export import build_library, write_library
 
     def spec(cfg):
@@ -183,11 +185,14 @@ def _stats_summary():
     """With KVSERVE_*_STATS_PATH set (the engines inherit it), the summary of
     the stats rows they wrote: mean compression ratio and the median
     compress + comm + decompress path."""
-    import os
-    from kvserve_hpdps_b200.utils.stats import summarize
     paths = [os.environ.get(f"KVSERVE_{k}_STATS_PATH") for k in ("COMPRESSION", "DECODE",
                                                                     "TRANSFER")]
-    return summarize(*paths) if any(paths) else None
+    if not any(paths):
+        return None
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    from kvserve_hpdps_b200.utils.stats import summarize
+    return summarize(*paths)
 
 
 def main(argv=None) -> int:

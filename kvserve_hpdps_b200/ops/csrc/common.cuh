@@ -70,6 +70,20 @@ KVS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread for up to `hint_ns` while the phase
+// is incomplete (it resumes when the phase completes): waiting warps then
+// stop competing for issue slots with the warps doing the work.
+KVS_DEV bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on a phase of an mbarrier.  Returns false (and records
 // `code`) when the phase does not complete within `timeout_ns`.
 KVS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
@@ -77,7 +91,7 @@ KVS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t c
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, 100000u)) return true;  // 100 us per suspension
     if (globaltimer() - t0 > timeout_ns) {
       record_error(err, code);
       return false;
@@ -284,6 +298,20 @@ KVS_DEV uint32_t cvt_bf16x2(float lo, float hi) {
 }
 KVS_DEV float bf16lo_to_float(uint32_t p) { return __uint_as_float(p << 16); }
 KVS_DEV float bf16hi_to_float(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
+// Two bf16 sums, each rounded once to bf16.  For bf16 operands this equals
+// rounding their fp32 sum to bf16: the fp32 sum is exact unless the
+// exponents differ by 16 or more, and then both results are the larger
+// operand, the smaller being far below half a bf16 ulp of it.
+KVS_DEV uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// bf16 bits of a float that is already a bf16 value, in both halves.
+KVS_DEV uint32_t bf16x2_splat(float x) {
+  const uint32_t h = __float_as_uint(x) >> 16;
+  return h | (h << 16);
+}
 
 // Packed fp32 pairs (sm_100 f32x2 arithmetic): each instruction performs the
 // two IEEE operations of its scalar form, rounded the same way, so results

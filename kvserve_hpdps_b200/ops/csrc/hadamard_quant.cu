@@ -1125,11 +1125,14 @@ KVS_DEV void ws_quant_half(uint32_t taddr, float sc, float top, bool valid, int 
         mn2 = f2_pack(m.x, m.y);
         rcp2 = f2_pack(m.z, m.w);
       }
-      if constexpr (W == 4) {
+      if constexpr (W == 4 || W == 8) {
         uint32_t b0, b1;
         quantize_bits2(x0, x1, mn2, rcp2, top, b0, b1);
-        nib[k >> 1] = b0 + (b1 << 4);  // low byte: code k | code k+1 << 4
-      } else {  // scalar form (fewer live registers for the wide codes)
+        if constexpr (W == 4)
+          nib[k >> 1] = b0 + (b1 << 4);  // low byte: code k | code k+1 << 4
+        else
+          nib[k >> 1] = __byte_perm(b0, b1, 0x0040);  // low half: code k | code k+1 << 8
+      } else {  // scalar form (fewer live registers for the odd widths)
         float m0, m1, r0, r1;
         f2_unpack(mn2, m0, m1);
         f2_unpack(rcp2, r0, r1);
@@ -1144,12 +1147,21 @@ KVS_DEV void ws_quant_half(uint32_t taddr, float sc, float top, bool valid, int 
         const uint32_t hi = __byte_perm(nib[4 * i + 2], nib[4 * i + 3], 0x0040);
         w[i] = __byte_perm(lo, hi, 0x5410);
       }
+    } else if constexpr (W == 8) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = __byte_perm(nib[2 * i], nib[2 * i + 1], 0x5410);
     } else {
       pack_code_bits<W>(b, w);
     }
     uint32_t* dst = reinterpret_cast<uint32_t*>(row_stage + (2 * half + cc) * 4 * W);
+    if constexpr (W == 4 || W == 8) {  // 16-byte stores: the row pitch is an odd multiple of 16
 #pragma unroll
-    for (int k = 0; k < W; ++k) dst[k] = w[k];
+      for (int k = 0; k < W; k += 4)
+        *reinterpret_cast<uint4*>(dst + k) = make_uint4(w[k], w[k + 1], w[k + 2], w[k + 3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < W; ++k) dst[k] = w[k];
+    }
   }
 }
 
@@ -1813,8 +1825,9 @@ __global__ void __launch_bounds__(kWsProdThreads, 1) k_quant_ws(LayerLaunch L) {
       uint8_t* dst0 = code_row(L, c, jb.plane, jb.h, c.row0);
       const long long dst_msg = L.ck_off + (dst0 - L.codes);
       const int total = nrows * bits;
+      const int sh = (bits & (bits - 1)) == 0 ? __ffs(bits) - 1 : -1;  // log2(bits) or -1
       for (int q = gtid; q < total; q += kWsGroupThreads) {
-        const int r = q / bits, col = q - r * bits;
+        const int r = sh >= 0 ? (q >> sh) : q / bits, col = q - r * bits;
         const uint4 v = *reinterpret_cast<const uint4*>(stage + r * P + col * 16);
         *reinterpret_cast<uint4*>(dst0 + static_cast<long long>(q) * 16) = v;
         if (L.ck != nullptr) ck_word4(v, dst_msg + 16ll * q, ck1, ck2);
@@ -1894,27 +1907,44 @@ KVS_DEV void p_unpack_group(const uint8_t* src, int t, int part, int kv, const f
   }
 }
 
+// Position of key parameter pair P (channels 2P, 2P+1 of the head) in the
+// dequantize kernel's shared table of 16-byte entries (scale(2P) and
+// scale(2P+1) as floats, then min(2P) | min(2P+1) << 16 as bf16 bits, then
+// padding).  The XOR moves P's 16-byte column by its 128-byte row, so that
+// the eight (part, chunk) pairs one quarter-warp reads in ws_unpack_group
+// lie in eight different columns.
+KVS_DEV int kp_pos(int P) { return P ^ ((P >> 3) & 7); }
+
 // Warp-specialized form of p_unpack_group: codes come from the job's code
-// tile in shared memory (staged by a bulk copy), the arithmetic runs on
-// value pairs (f32x2), and key parameters are read in the pair layout
-// kq[p] = (scale(2p), scale(2p+1), -2^23*scale(2p), -2^23*scale(2p+1)),
-// km[p] = (min(2p), min(2p+1)).  Results are identical to p_unpack_group's.
+// tile in shared memory (staged by a bulk copy), q*scale runs on value pairs
+// (f32x2) and the min is added to the bf16 products in bf16x2 (one rounding,
+// the same value as rounding the fp32 sum).  Results are identical to
+// p_unpack_group's.
 template <int W>
-KVS_DEV void ws_unpack_group(const uint8_t* src, int t, int part, int kv, const float4* kq,
-                             const float2* km, float vmn, float vsc, uint8_t* sA) {
+KVS_DEV void ws_unpack_group(const uint8_t* src, int t, int part, int m, int kv,
+                             const float4* kp, float vmn, float vsc, uint8_t* sA) {
   uint32_t w[8];
-  if constexpr (W == 8 || W == 4) {  // 4W-byte groups are 16-byte aligned
+  if constexpr (W == 8) {  // 32-byte group: two 16-byte halves, read in rotated order
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    const uint4 u0 = s[m], u1 = s[m ^ 1];
+    w[0] = u0.x; w[1] = u0.y; w[2] = u0.z; w[3] = u0.w;
+    w[4] = u1.x; w[5] = u1.y; w[6] = u1.z; w[7] = u1.w;
+  } else if constexpr (W == 4) {  // one word per chunk
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    w[0] = m ? u.z : u.x;
+    w[1] = m ? u.w : u.y;
+    w[2] = m ? u.x : u.z;
+    w[3] = m ? u.y : u.w;
+  } else {  // codes straddle words: rotate the 32W-bit group by its half, 16W bits
+    uint32_t v[W];
 #pragma unroll
-    for (int k = 0; k < W / 4; ++k) {
-      const uint4 u = reinterpret_cast<const uint4*>(src)[k];
-      w[4 * k] = u.x;
-      w[4 * k + 1] = u.y;
-      w[4 * k + 2] = u.z;
-      w[4 * k + 3] = u.w;
+    for (int k = 0; k < W; ++k) v[k] = reinterpret_cast<const uint32_t*>(src)[k];
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      const uint32_t r = (W & 1) ? __funnelshift_r(v[(k + W / 2) % W], v[(k + W / 2 + 1) % W], 16)
+                                 : v[(k + W / 2) % W];
+      w[k] = m ? r : v[k];
     }
-  } else {
-#pragma unroll
-    for (int k = 0; k < W; ++k) w[k] = reinterpret_cast<const uint32_t*>(src)[k];
   }
   uint32_t fb[32];  // bits of 2^23 + q
   if constexpr (W == 8) {
@@ -1922,34 +1952,32 @@ KVS_DEV void ws_unpack_group(const uint8_t* src, int t, int part, int kv, const 
     for (int k = 0; k < 32; ++k)
       fb[k] = __byte_perm(w[k >> 2], 0x4B000000u, 0x7650u | (k & 3));
   } else {
-    uint32_t q[32];
-    unpack32<W>(w, q);
+    unpack32<W>(w, fb);
 #pragma unroll
-    for (int k = 0; k < 32; ++k) fb[k] = q[k] | 0x4B000000u;
+    for (int k = 0; k < 32; ++k) fb[k] |= 0x4B000000u;
   }
   const f32x2_t vsc2 = f2_pack(vsc, vsc), vneg2 = f2_pack(-8388608.0f * vsc, -8388608.0f * vsc);
-  const f32x2_t vmn2 = f2_pack(vmn, vmn);
+  const f32x2_t big2 = f2_pack(-8388608.0f, -8388608.0f);
+  const uint32_t vmn2 = bf16x2_splat(vmn);
 #pragma unroll
-  for (int c8 = 0; c8 < 4; ++c8) {
+  for (int cs = 0; cs < 4; ++cs) {
+    const int c8 = cs ^ (2 * m);  // channel chunk of register chunk cs
     uint32_t o[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      const int k = c8 * 8 + 2 * p;
-      f32x2_t sc2 = vsc2, neg2 = vneg2, mn2 = vmn2;
+      const int k = cs * 8 + 2 * p;
+      f32x2_t sc2 = vsc2, neg2 = vneg2;
+      uint32_t mn2 = vmn2;
       if (kv == 0) {
-        const float4 q = kq[(part * 32 + k) >> 1];
-        const float2 m = km[(part * 32 + k) >> 1];
-        sc2 = f2_pack(q.x, q.y);
-        neg2 = f2_pack(q.z, q.w);
-        mn2 = f2_pack(m.x, m.y);
+        const float4 e = kp[kp_pos(part * 16 + c8 * 4 + p)];
+        sc2 = f2_pack(e.x, e.y);
+        neg2 = f2_mul(sc2, big2);  // exact: a power-of-two multiple
+        mn2 = __float_as_uint(e.z);
       }
       float a, b;
       f2_unpack(f2_fma(f2_pack(__uint_as_float(fb[k]), __uint_as_float(fb[k + 1])), sc2, neg2),
                 a, b);
-      const uint32_t prod = cvt_bf16x2(a, b);
-      float c0, c1;
-      f2_unpack(f2_add(f2_pack(bf16lo_to_float(prod), bf16hi_to_float(prod)), mn2), c0, c1);
-      o[p] = cvt_bf16x2(c0, c1);
+      o[p] = bf16x2_add(cvt_bf16x2(a, b), mn2);
     }
     *reinterpret_cast<uint4*>(sA + sw128_offset(t, part * 32 + c8 * 8)) =
         make_uint4(o[0], o[1], o[2], o[3]);
@@ -2137,15 +2165,20 @@ __global__ void __launch_bounds__(kPThreads, 2) k_dequant_tc(LayerLaunch L) {
 //   afree[b]   tcgen05.commit after MMA k: A tile b and the image are free;
 //   dmma[b]    tcgen05.commit after MMA k: accumulator b holds job k;
 //   accfree[b] 8 epilogue-warp arrivals: accumulator b has been read.
-// image | A tiles [2] | output tiles [2] | code tiles [2] (128 rows x 128 B
-// at most) | value (min, scale) rows [2] | barriers | key parameters
+// Code tiles rotate through kDqCodeBufs buffers (job k: buffer k % 3), so a
+// tile's bulk load is issued two unpack periods before it is needed:
+//   cfull[c]   the code tile (and value rows) of job k landed in buffer c;
+//   cfree[c]   8 unpack-warp arrivals: job k's unpack finished reading it.
+// image | A tiles [2] | output tiles [2] | code tiles [3] (128 rows x 128 B
+// at most) | value (min, scale) rows [3] | barriers | key parameters
+constexpr int kDqCodeBufs = 3;
 constexpr int kDqOffA = 32768;
 constexpr int kDqOffO = kDqOffA + 2 * 32768;
 constexpr int kDqOffC = kDqOffO + 2 * 32768;
-constexpr int kDqOffVm = kDqOffC + 2 * 16384;
-constexpr int kDqOffBars = kDqOffVm + 2 * 512;
+constexpr int kDqOffVm = kDqOffC + kDqCodeBufs * 16384;
+constexpr int kDqOffBars = kDqOffVm + kDqCodeBufs * 512;
 constexpr int kDqOffKp = kDqOffBars + 256;
-constexpr int kDqSmem = kDqOffKp + 64 * 16 + 64 * 8 + 1024;
+constexpr int kDqSmem = kDqOffKp + 64 * 16 + 1024;
 static_assert(kDqSmem <= 227 * 1024, "dequant ws shared memory");
 
 __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
@@ -2159,10 +2192,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
   uint64_t* accfree = bars + 6;  // [2]
   uint64_t* imgb = bars + 8;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 9);
-  uint64_t* cfull = bars + 10;   // [2] code tile (and value rows) landed
-  uint64_t* cfree = bars + 12;   // [2] unpack finished reading them
-  float4* kq = reinterpret_cast<float4*>(base + kDqOffKp);         // [64] key scale pairs
-  float2* km = reinterpret_cast<float2*>(base + kDqOffKp + 1024);  // [64] key min pairs
+  uint64_t* cfull = bars + 10;   // [kDqCodeBufs] code tile (and value rows) landed
+  uint64_t* cfree = bars + 10 + kDqCodeBufs;  // [kDqCodeBufs] unpack finished reading them
+  float4* kp = reinterpret_cast<float4*>(base + kDqOffKp);  // [64] key pairs, at kp_pos
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = L.num_heads;
   const WsMap M = ws_map(L);
@@ -2174,8 +2206,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       mbar_init(&afree[b], 1);
       mbar_init(&dmma[b], 1);
       mbar_init(&accfree[b], kWsGroupWarps);
-      mbar_init(&cfull[b], 1);
-      mbar_init(&cfree[b], kWsGroupWarps);
+    }
+    for (int c = 0; c < kDqCodeBufs; ++c) {
+      mbar_init(&cfull[c], 1);
+      mbar_init(&cfree[c], kWsGroupWarps);
     }
     mbar_init(imgb, 1);
     fence_mbar_init();
@@ -2210,10 +2244,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
           const __half* m = meta_base(L, c.r);
           const float mn = bf16_round(__half2float(m[jb.h * 128 + tid]));
           const float sc = bf16_round(__half2float(m[c.lp->H * 128 + jb.h * 128 + tid]));
-          float* q = reinterpret_cast<float*>(kq + (tid >> 1));
-          q[tid & 1] = sc;
-          q[2 + (tid & 1)] = -8388608.0f * sc;
-          reinterpret_cast<float*>(km + (tid >> 1))[tid & 1] = mn;
+          float* e = reinterpret_cast<float*>(kp + kp_pos(tid >> 1));
+          e[tid & 1] = sc;
+          reinterpret_cast<uint16_t*>(e + 2)[tid & 1] =
+              static_cast<uint16_t>(__float_as_uint(mn) >> 16);  // mn is a bf16 value
         }
         kp_key = pk;
         group_sync(0);  // key parameters visible
@@ -2221,11 +2255,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       uint8_t* sA = abuf(b);
       const int bits = seg_bits(c, jb.plane, jb.h);
       const int nrows = min(kTileRows, c.rows - c.row0);
-      const uint8_t* src0 = cbuf(b);
-      const __half* vm = vmbuf(b);  // [0, 128): group min of the tile's rows, [128, 256): scale
-      mbar_wait(&cfull[b], static_cast<uint32_t>((k >> 1) & 1), L.err, ERR_MBAR_TIMEOUT);
+      const int cb = k % kDqCodeBufs;
+      const uint8_t* src0 = cbuf(cb);
+      const __half* vm = vmbuf(cb);  // [0, 128): group min of the tile's rows, [128, 256): scale
+      mbar_wait(&cfull[cb], static_cast<uint32_t>((k / kDqCodeBufs) & 1), L.err, ERR_MBAR_TIMEOUT);
+      if (tid == 0) trace_mark(L, k, 6);
       for (int g = tid; g < kTileRows * 4; g += kWsGroupThreads) {
-        const int t = g & (kTileRows - 1), part = g >> 7;
+        const int t = g >> 2, part = g & 3;  // a warp: 8 rows x 4 parts
+        const int m = (t & 1) ^ (part >> 1);
         const int row = c.row0 + t;
         if (t < nrows && row < c.ntok) {
           float vmn = 0.f, vsc = 0.f;
@@ -2235,14 +2272,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
           }
           const uint8_t* src = src0 + t * 16 * bits + part * 4 * bits;
           switch (bits) {
-            case 1: ws_unpack_group<1>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            case 2: ws_unpack_group<2>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            case 3: ws_unpack_group<3>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            case 4: ws_unpack_group<4>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            case 5: ws_unpack_group<5>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            case 6: ws_unpack_group<6>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            case 7: ws_unpack_group<7>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
-            default: ws_unpack_group<8>(src, t, part, jb.plane, kq, km, vmn, vsc, sA); break;
+            case 1: ws_unpack_group<1>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            case 2: ws_unpack_group<2>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            case 3: ws_unpack_group<3>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            case 4: ws_unpack_group<4>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            case 5: ws_unpack_group<5>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            case 6: ws_unpack_group<6>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            case 7: ws_unpack_group<7>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
+            default: ws_unpack_group<8>(src, t, part, m, jb.plane, kp, vmn, vsc, sA); break;
           }
         } else {
 #pragma unroll
@@ -2252,7 +2289,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&cfree[b]);  // code tile b may be refilled
+      if (lane == 0) mbar_arrive(&cfree[cb]);  // code tile cb may be refilled
       fence_proxy_async_smem();  // generic writes of A tile b before the MMA reads it
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[b]);
@@ -2353,10 +2390,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
     ItemCursor ccur;
     cursor_init(ccur);
     // Code tile of job kk (and, for values, the group min / scale of its
-    // rows) into buffer kk & 1.  After a failed wait only the arrival is
+    // rows) into buffer kk % kDqCodeBufs.  After a failed wait only the arrival is
     // made, so the unpack warps never wait past their limit.
     auto issue_codes = [&](int kk) {
-      const int cb = kk & 1;
+      const int cb = kk % kDqCodeBufs;
       const PJob jn = ws_job(M, kk);
       cursor_seek(L, ccur, jn.tile);
       const ItemCtx& c = ccur.c;
@@ -2369,6 +2406,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
       const uint32_t cbytes = static_cast<uint32_t>(nrows * 16 * seg_bits(c, jn.plane, jn.h));
       const uint32_t vbytes = jn.plane == 1 ? static_cast<uint32_t>(nrows * 2) : 0u;
       mbar_arrive_expect_tx(&cfull[cb], cbytes + 2 * vbytes);
+      trace_mark(L, kk, 7);
       bulk_load(cbuf(cb), code_row(L, c, jn.plane, jn.h, c.row0), cbytes, &cfull[cb]);
       if (vbytes) {
         const __half* meta = meta_base(L, c.r) + 2 * c.lp->H * 128;
@@ -2377,13 +2415,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
         bulk_load(vmbuf(cb) + 128, meta + (G + grp) * c.rows + c.row0, vbytes, &cfull[cb]);
       }
     };
-    for (int k = 0; k < 3 && k < n; ++k) prefetch(k);
-    for (int k = 0; k < 2 && k < n; ++k) issue_codes(k);
+    constexpr int kPrefetchAhead = 6;  // jobs whose code regions are pulled into L2
+    for (int k = 0; k < kPrefetchAhead && k < n; ++k) prefetch(k);
+    for (int k = 0; k < kDqCodeBufs && k < n; ++k) issue_codes(k);
     for (int k = 0; k < n; ++k) {
       const int b = k & 1;
       const PJob jb = ws_job(M, k);
       cursor_seek(L, cur, jb.tile);
-      if (k + 3 < n) prefetch(k + 3);
+      if (k + kPrefetchAhead < n) prefetch(k + kPrefetchAhead);
       const int img_key = cur.c.slot * H + jb.h;
       if (ok && img_key != cur_img) {
         if (k >= 1)  // MMA k-1 finished reading the old image
@@ -2413,9 +2452,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_dequant_ws(LayerLaunch L) {
         trace_mark(L, k, 2);
       }
       __syncwarp();
-      if (k + 2 < n) {  // job k's unpack has read code buffer b: refill it
-        if (ok) ok = wait0(&cfree[b], static_cast<uint32_t>((k >> 1) & 1));
-        issue_codes(k + 2);
+      if (k + kDqCodeBufs < n) {  // job k's unpack has read its code buffer: refill it
+        if (ok)
+          ok = wait0(&cfree[k % kDqCodeBufs], static_cast<uint32_t>((k / kDqCodeBufs) & 1));
+        issue_codes(k + kDqCodeBufs);
       }
     }
   }

@@ -11,6 +11,23 @@
 #include <cstdint>
 #include <cstring>
 
+namespace {
+// Switches the calling thread to `device` and back to the device that was
+// current before, so a helper never leaves another device's context current
+// for the caller's next launch.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = cudaSetDevice(device) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
 extern "C" {
 
 int kvs_device_count(void) {
@@ -20,7 +37,8 @@ int kvs_device_count(void) {
 }
 
 int kvs_malloc(int device, uint64_t bytes, void** out) {
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  DeviceGuard guard(device);
+  if (!guard.ok) return -1;
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess) return -2;
   *out = p;
@@ -28,7 +46,8 @@ int kvs_malloc(int device, uint64_t bytes, void** out) {
 }
 
 int kvs_free(int device, void* p) {
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  DeviceGuard guard(device);
+  if (!guard.ok) return -1;
   return cudaFree(p) == cudaSuccess ? 0 : -2;
 }
 
@@ -39,7 +58,8 @@ int kvs_memset(void* p, int value, uint64_t bytes, void* stream) {
 
 // 64-byte opaque handle.
 int kvs_ipc_get_handle(int device, void* ptr, uint8_t* handle_out) {
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  DeviceGuard guard(device);
+  if (!guard.ok) return -1;
   cudaIpcMemHandle_t h;
   if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return -2;
   std::memcpy(handle_out, &h, sizeof(h));
@@ -47,7 +67,8 @@ int kvs_ipc_get_handle(int device, void* ptr, uint8_t* handle_out) {
 }
 
 int kvs_ipc_open_handle(int device, const uint8_t* handle, void** out) {
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  DeviceGuard guard(device);
+  if (!guard.ok) return -1;
   cudaIpcMemHandle_t h;
   std::memcpy(&h, handle, sizeof(h));
   void* p = nullptr;
@@ -57,7 +78,8 @@ int kvs_ipc_open_handle(int device, const uint8_t* handle, void** out) {
 }
 
 int kvs_ipc_close_handle(int device, void* p) {
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  DeviceGuard guard(device);
+  if (!guard.ok) return -1;
   return cudaIpcCloseMemHandle(p) == cudaSuccess ? 0 : -2;
 }
 
@@ -69,7 +91,8 @@ int kvs_can_access_peer(int device, int peer) {
 }
 
 int kvs_enable_peer_access(int device, int peer) {
-  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  DeviceGuard guard(device);
+  if (!guard.ok) return -1;
   cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
   if (e == cudaErrorPeerAccessAlreadyEnabled) {
     cudaGetLastError();

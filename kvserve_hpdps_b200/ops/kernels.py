@@ -627,7 +627,7 @@ TRACE_EVENTS = ("tile_ready", "mma_issued", "refill_issued", "epi_mma_seen", "ep
                 "acc_free_seen", "epi_quantized", "epi_staged")
 # the dequantize kernel's events, same slots
 TRACE_EVENTS_DEQUANT = ("unpack_start", "unpack_done", "mma_issued", "epi_mma_seen",
-                        "epi_stores_issued", "a_full_seen", "unused6", "unused7")
+                        "epi_stores_issued", "a_full_seen", "codes_ready", "codes_issued")
 _trace = {"buf": None, "jobs": 0}
 
 
