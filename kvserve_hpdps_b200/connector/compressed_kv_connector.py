@@ -211,6 +211,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._fc = None
         self._deadline = 0.0
         self._side_stream = None
+        self._streamed = False  # this step's layers were sent from save_kv_layer
         self._expected_msgs: dict[str, int] = {}
         self._rid2tid: dict[str, str] = {}
         self._pending_send_rids: set[str] = set()
@@ -342,7 +343,25 @@ class CompressedKVConnector(KVConnectorBase_V1):
         for rm in meta.requests:
             self._save_times[rm.request_id].append(now)
         comp = self._get_compressor()
+        if self._side_stream is not None and comp is None and kv_layer.is_cuda:
+            # raw KV, layer by layer: each request's blocks of this layer go
+            # out as their own message on the side stream (the consumer counts
+            # one message per layer for each transfer id)
+            ready = torch.cuda.current_stream().record_event()
+            with torch.cuda.stream(self._side_stream):
+                self._side_stream.wait_event(ready)
+                for rm in meta.requests:
+                    if hasattr(self._transport, "send_paged"):
+                        self._transport.send_paged(rm.transfer_id, [layer_name], [kv_layer],
+                                                   rm.block_ids)
+                    else:
+                        raw = extract_kv_from_layer_by_blocks(kv_layer, rm.block_ids).unsqueeze(0)
+                        self._transport.send(rm.transfer_id, [layer_name], raw)
+                    self._expected_msgs[rm.transfer_id] = self._num_layers
+            self._streamed = True
+            return
         if self._side_stream is not None and comp is not None and comp.supports_paged():
+            self._streamed = True
             ready = torch.cuda.current_stream().record_event()
             requests = [(rm.block_ids, len(rm.token_ids)) for rm in meta.requests]
             tids = [rm.transfer_id for rm in meta.requests]
@@ -381,6 +400,8 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._apply_controller_feedback()
         if self._side_stream is not None:
             torch.cuda.current_stream().wait_stream(self._side_stream)
+        if self._streamed:  # every layer already went out from save_kv_layer
+            self._streamed = False
             self._finish_step(meta)
             timeline("P save_exit")
             return

@@ -52,15 +52,19 @@ def _cos(a, b):
     return float(torch.nn.functional.cosine_similarity(a.float().flatten(), b.float().flatten(), dim=0))
 
 
+@pytest.mark.parametrize("compression", ["default", None])
 @pytest.mark.parametrize("overlap", ["off", "stream"])
-def test_fused_default_handoff_in_process(overlap, monkeypatch):
+def test_fused_default_handoff_in_process(overlap, compression, monkeypatch):
+    """Both overlap modes, compressed and raw: in stream mode every layer goes
+    out from save_kv_layer (one grouped message per layer compressed, one
+    message per layer and request raw), in off mode one message per request."""
     monkeypatch.setenv("KVSERVE_OVERLAP_MODE", overlap)
     from kvserve_hpdps_b200.connector.compressed_kv_connector import (CompressedKVConnector,
                                                                       KVConnectorRole)
     from kvserve_hpdps_b200.parallel.fake_transport import FakeTransportPair
     pair = FakeTransportPair()
-    p = CompressedKVConnector(vllm_config(True, "default"), KVConnectorRole.WORKER)
-    c = CompressedKVConnector(vllm_config(False, "default"), KVConnectorRole.WORKER)
+    p = CompressedKVConnector(vllm_config(True, compression), KVConnectorRole.WORKER)
+    c = CompressedKVConnector(vllm_config(False, compression), KVConnectorRole.WORKER)
     p.attach_transport(pair.producer())
     c.attach_transport(pair.consumer())
     pc, cc = _caches(24, 1, "cuda"), _caches(24, 2, "cuda", fill=False)
@@ -80,8 +84,14 @@ def test_fused_default_handoff_in_process(overlap, monkeypatch):
         for name in pc:
             src = pc[name][:, bp].reshape(2, -1, H, D)[:, :n]
             dst = cc[name][:, bcs].reshape(2, -1, H, D)[:, :n]
-            assert _cos(src, dst) > 0.9, (rp, name)
-    assert pair.messages == (L if overlap == "stream" else 2)
+            if compression is None:
+                assert torch.equal(src, dst), (rp, name)
+            else:
+                assert _cos(src, dst) > 0.9, (rp, name)
+    if overlap == "stream":
+        assert pair.messages == (L if compression else 2 * L)
+    else:
+        assert pair.messages == 2
 
 
 def test_stream_mode_loads_layer_by_layer(monkeypatch):
