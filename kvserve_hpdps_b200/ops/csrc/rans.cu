@@ -23,7 +23,13 @@ namespace rans {
 // CTA) keep a 28-layer 8-request step (3585 chunks) in one wave.
 constexpr int kEncWarps = 4;
 constexpr int kCtasPerSm = 7;
-constexpr int kHistCopies = 4;  // lane-interleaved histogram copies (spread the atomics)
+// Histogram copies: lane l counts into copy l % kHistCopies.  A copy holds
+// two 16-bit counts per word (symbol s in word s / 2, half s & 1; a copy
+// sees at most cs / kHistCopies symbols, below 2^16) and is padded to
+// kHistStride words, so the same symbol in different copies falls in
+// different banks.
+constexpr int kHistCopies = 8;
+constexpr int kHistStride = 129;  // 128 words + 1 (129 mod 32 = 1)
 constexpr int kDecWarps = 4;
 constexpr int kRing = 512;  // words of one stream's shared-memory ring in the decoder
 constexpr int kDecWarpSmem = 4096 + 1024 + kStreams * kRing * 2;
@@ -174,9 +180,11 @@ __global__ void __launch_bounds__(kEncWarps * 32, kCtasPerSm) k_rans_encode(
     uint32_t* __restrict__ desc, uint32_t n_chunks) {
   // a warp's histogram (4 x 256 counts) is dead once its frequencies are
   // normalised, so its encoder table (256 x 8 B) reuses its first 2 KB
-  __shared__ __align__(16) uint32_t hist[kEncWarps][kHistCopies * 256];
+  __shared__ __align__(16) uint32_t hist[kEncWarps][kHistCopies * kHistStride + 4];
   __shared__ uint32_t freq_s[kEncWarps][256];
-  static_assert(sizeof(EncPacked) * 256 <= sizeof(uint32_t) * kHistCopies * 256, "table aliasing");
+  static_assert(sizeof(EncPacked) * 256 <= sizeof(uint32_t) * kHistCopies * kHistStride,
+                "table aliasing");
+  static_assert(kMaxChunkSyms / kHistCopies < 65536, "16-bit histogram counts");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk = blockIdx.x * kEncWarps + warp;
   if (chunk >= n_chunks) return;  // warp-uniform
@@ -188,11 +196,11 @@ __global__ void __launch_bounds__(kEncWarps * 32, kCtasPerSm) k_rans_encode(
   uint32_t* d = desc + static_cast<uint64_t>(chunk) * kDescWords;
 
   uint32_t* h = hist[warp];
-  for (int i = lane; i < kHistCopies * 256; i += 32) h[i] = 0;
+  for (int i = lane; i < kHistCopies * kHistStride; i += 32) h[i] = 0;
   __syncwarp();
-  // Histogram in four lane-interleaved copies (lane & 3): spreads the
-  // atomic traffic of skewed symbol distributions over four addresses.
-  uint32_t* hc = h + (lane & (kHistCopies - 1)) * 256;
+  // Histogram in lane-interleaved copies: spreads the atomic traffic of
+  // skewed symbol distributions over kHistCopies addresses in distinct banks.
+  uint32_t* hc = h + (lane & (kHistCopies - 1)) * kHistStride;
   // the next super-step's symbols are loaded while this one is counted
   Syms32 nxt = load_syms(src, 0, lane, n_sym);
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
@@ -200,17 +208,31 @@ __global__ void __launch_bounds__(kEncWarps * 32, kCtasPerSm) k_rans_encode(
     syms_words(nxt, w);
     if (ss + 1 < n_ss) nxt = load_syms(src, ss + 1, lane, n_sym);
 #pragma unroll
-    for (int i = 0; i < kSub; ++i) atomicAdd(&hc[(w[i >> 2] >> ((i & 3) * 8)) & 0xFF], 1u);
+    for (int i = 0; i < kSub; ++i) {
+      const uint32_t sym = (w[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
+      atomicAdd(&hc[sym >> 1], 1u << ((sym & 1u) * 16));
+    }
   }
   __syncwarp();
   int top = -1;
-  for (int k = 0; k < 8; ++k) {
-    const int s = lane * 8 + k;
-    uint32_t c = 0;
+  uint32_t tot[8];  // this lane's symbols lane*8 .. lane*8+7 (words lane*4 .. lane*4+3)
 #pragma unroll
-    for (int cp = 0; cp < kHistCopies; ++cp) c += h[cp * 256 + s];
-    h[s] = c;  // copy 0 now holds the totals (each lane only reads its own bins)
-    if (c > 0) top = s;
+  for (int k = 0; k < 8; k += 2) {
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int cp = 0; cp < kHistCopies; ++cp) {
+      const uint32_t v = h[cp * kHistStride + lane * 4 + (k >> 1)];
+      lo += v & 0xFFFFu;
+      hi += v >> 16;
+    }
+    tot[k] = lo;
+    tot[k + 1] = hi;
+  }
+  __syncwarp();  // every lane read its words before the totals overwrite them
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    h[lane * 8 + k] = tot[k];  // words 0..255 now hold the 32-bit totals
+    if (tot[k] > 0) top = lane * 8 + k;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) top = max(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
@@ -587,7 +609,7 @@ uint64_t kvs_rans_staging_bytes(uint64_t n, uint32_t cs) {
 // by the last CTA.
 int kvs_rans_encode(const uint8_t* in, uint64_t n, uint32_t cs, uint8_t* staging, uint32_t* sizes,
                     uint8_t* out, uint64_t* total_out, const RansMsg* msg, void* stream) {
-  if (n == 0 || cs == 0 || cs % kSuper != 0) return -2;
+  if (n == 0 || cs == 0 || cs % kSuper != 0 || cs > kMaxChunkSyms) return -2;
   // the kernels move 16-byte words: input, output and scratch must be aligned
   if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) |
         reinterpret_cast<uintptr_t>(staging) | reinterpret_cast<uintptr_t>(sizes)) & 15) != 0)

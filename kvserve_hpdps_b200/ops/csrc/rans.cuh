@@ -42,6 +42,7 @@ constexpr int kStreams = 2;                           // rANS streams per chunk 
 constexpr int kSub = 32;                              // symbols per lane per super-step
 constexpr int kSuper = kLanes * kSub;                 // 1024 symbols per super-step
 constexpr uint32_t kChunkSymbols = 32768;             // default chunk size
+constexpr uint32_t kMaxChunkSyms = 1u << 18;          // largest chunk the GPU encoder takes
 constexpr int kProbBits = 12;
 constexpr uint32_t kProbScale = 1u << kProbBits;      // M = 4096
 constexpr uint32_t kStateLow = 1u << 15;              // L
