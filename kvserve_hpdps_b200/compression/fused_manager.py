@@ -167,7 +167,8 @@ class FusedCompressionManager:
     def compress_paged_requests(self, kv_layers: Sequence[torch.Tensor], layer_ids: Sequence[int],
                                 requests: Sequence[tuple[Sequence[int], int]],
                                 member_tids: Optional[Sequence[str]] = None,
-                                trim: bool = True, deferred: bool = False) -> CompressedKVData:
+                                trim: bool = True, deferred: bool = False,
+                                extra_meta: Optional[dict] = None) -> CompressedKVData:
         """Compress the given layers of several requests into ONE message:
         one codec stream over every (layer, request) item, layer-major.
 
@@ -222,6 +223,7 @@ class FusedCompressionManager:
             meta["container"] = False
             if self.stream_codec != "none":
                 meta["deferred_codec"] = self.stream_codec
+        meta.update(extra_meta or {})
         orig = sum(len(kv_layers) * 2 * n * H * self.head_size * 2 for _, n in requests)
         self._last_batch = batch
         return CompressedKVData(request_id="grp", layer_id=int(layer_ids[-1]),
@@ -231,7 +233,8 @@ class FusedCompressionManager:
     def send_paged_requests(self, transport, request_id: str, layer_names: Sequence[str],
                             kv_layers: Sequence[torch.Tensor], layer_ids: Sequence[int],
                             requests: Sequence[tuple[Sequence[int], int]],
-                            member_tids: Optional[Sequence[str]] = None) -> dict:
+                            member_tids: Optional[Sequence[str]] = None,
+                            extra_meta: Optional[dict] = None) -> dict:
         """Compress the requests and hand them to ``transport`` as ONE
         message, written by the producer kernels straight into the
         consumer's receive ring when the transport offers it (NVLink ring
@@ -246,16 +249,18 @@ class FusedCompressionManager:
         the link); a final copy brings the fp16 metadata and its last CTA
         stores the checksum and publishes the ready flag.
 
-        Returns ``{"original_size", "wire_nbytes", "direct"}`` where
-        ``wire_nbytes`` is the reserved (upper-bound) size on the direct
-        path; the exact size reaches the transport's sent listeners."""
+        ``extra_meta`` joins the message's metadata (controller mode: the
+        profile the consumer decodes with).  Returns ``{"original_size",
+        "wire_nbytes", "direct"}`` where ``wire_nbytes`` is the reserved
+        (upper-bound) size on the direct path; the exact size reaches the
+        transport's sent listeners."""
         from kvserve_hpdps_b200.compression.wire import build_wire
         from kvserve_hpdps_b200.ops import kernels as K
         direct = (hasattr(transport, "open_message") and self.engine == 0
                   and self.stream_codec in ("none", "rans") and kv_layers[0].is_cuda)
         if not direct:
             cd = self.compress_paged_requests(kv_layers, layer_ids, requests, member_tids,
-                                              trim=False, deferred=True)
+                                              trim=False, deferred=True, extra_meta=extra_meta)
             wire = build_wire(cd)
             transport.send_bundle(request_id, list(layer_names), wire.meta, wire.body_chunks,
                                   wire.aux_tensors, member_tids=list(member_tids or []) or None)
@@ -274,7 +279,7 @@ class FusedCompressionManager:
         try:
             return self._send_direct(transport, msg, request_id, layer_names, kv_layers,
                                      layer_ids, requests, member_tids, plans, slots, items,
-                                     code_bytes, meta_bytes, body_cap)
+                                     code_bytes, meta_bytes, body_cap, extra_meta)
         except Exception as e:
             # nothing committed: the space comes back once queued work is done
             transport.abort_message(msg, request_id, list(member_tids or []) or None, e)
@@ -282,7 +287,7 @@ class FusedCompressionManager:
 
     def _send_direct(self, transport, msg, request_id, layer_names, kv_layers, layer_ids,
                      requests, member_tids, plans, slots, items, code_bytes, meta_bytes,
-                     body_cap) -> dict:
+                     body_cap, extra_meta: Optional[dict] = None) -> dict:
         """Kernels and header of :meth:`send_paged_requests`' direct path."""
         from kvserve_hpdps_b200.compression.codec import CODEC_IDS, MAGIC
         from kvserve_hpdps_b200.compression.wire import build_wire
@@ -330,6 +335,7 @@ class FusedCompressionManager:
                 "stream_codec": self.stream_codec, "transform_seed": self.base_seed}
         if not rans:
             info["container"] = False
+        info.update(extra_meta or {})
         orig = sum(len(kv_layers) * 2 * n * H * self.head_size * 2 for _, n in requests)
         cd = CompressedKVData(request_id="grp", layer_id=int(layer_ids[-1]),
                               compressed_tensor=body_view, metadata=info, original_size=orig,

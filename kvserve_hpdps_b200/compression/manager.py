@@ -85,6 +85,7 @@ class KVCompressionAdapter:
         self._manager_cache: dict[str, tuple[Any, Optional[CompressionConfig]]] = {}
         self._last_decompress_timing: Optional[dict] = None
         self._cpu_fallback_mgr = None
+        self._paged_ctl: Optional[bool] = None  # controller mode: every profile fused
         self.spec = compression_spec
         if compression_spec == "default":
             cfg = get_default_compression_config()
@@ -173,6 +174,10 @@ class KVCompressionAdapter:
     def manager(self):
         return self._manager
 
+    @property
+    def controller_mode(self) -> bool:
+        return self._controller is not None
+
     def _fused(self) -> bool:
         return getattr(self._manager, "backend", None) == "kvs_fused"
 
@@ -250,8 +255,40 @@ class KVCompressionAdapter:
         return self._manager is not None and hasattr(self._manager, "compress_quant_layer")
 
     def supports_paged(self) -> bool:
-        """Paged multi-request compression (the fused kernels: CUDA tensors)."""
+        """Paged multi-request compression (the fused kernels: CUDA tensors).
+        In controller mode: when every profile of the library runs on the
+        fused kernels; each message then names the profile it was coded
+        with (``ctrl_profile_cfg``), as the whole-tensor path does."""
+        if self._controller is not None:
+            if self._paged_ctl is None:
+                self._paged_ctl = all(use_fused(dict(p.compression_config or {}))
+                                      for p in self._controller.library.get_all_profiles())
+            return self._paged_ctl
         return self._manager is not None and hasattr(self._manager, "compress_paged_requests")
+
+    def _paged_manager(self, kv_layers, requests, request_id: str):
+        """(manager, extra metadata) for a paged message; (None, None) when
+        the controller picks no compression for it."""
+        if self._controller is None:
+            return self._manager, None
+        volume = float(sum(len(kv_layers) * 2 * int(n) * self._num_kv_heads * self._head_size
+                           * kv_layers[0].element_size() for _, n in requests))
+        profile, ctx = self.select_profile(volume, request_id)
+        if profile is None:
+            logger.debug("controller: no compression for %s (%s)", request_id, ctx.get("reason"))
+            return None, None
+        mgr, _ = self._get_cached_manager(profile.compression_config)
+        return mgr, {"ctrl_profile_cfg": profile.compression_config,
+                     "ctrl_profile_id": profile.profile_id}
+
+    def _decode_manager(self, compressed: CompressedKVData):
+        cfg = (compressed.metadata or {}).get("ctrl_profile_cfg") \
+            if self._controller is not None else None
+        if cfg is not None:
+            return self._get_cached_manager(cfg)[0]
+        if self._manager is None:
+            raise RuntimeError("controller mode: ctrl_profile_cfg missing from metadata")
+        return self._manager
 
     def compress_quant_layer(self, kv_layer, layer_id):
         return self._manager.compress_quant_layer(kv_layer, layer_id)
@@ -275,20 +312,38 @@ class KVCompressionAdapter:
                                               original_shape)
 
     def compress_paged_requests(self, kv_layers, layer_ids, requests, member_tids=None,
-                                trim: bool = True, deferred: bool = False):
-        return self._manager.compress_paged_requests(kv_layers, layer_ids, requests, member_tids,
-                                                     trim=trim, deferred=deferred)
+                                trim: bool = True, deferred: bool = False,
+                                request_id: str = "grp"):
+        """One message for the requests; None when the controller picks no
+        compression."""
+        mgr, extra = self._paged_manager(kv_layers, requests, request_id)
+        if mgr is None:
+            return None
+        return mgr.compress_paged_requests(kv_layers, layer_ids, requests, member_tids,
+                                           trim=trim, deferred=deferred, extra_meta=extra)
 
     def send_paged_requests(self, transport, request_id, layer_names, kv_layers, layer_ids,
-                            requests, member_tids=None) -> dict:
+                            requests, member_tids=None) -> Optional[dict]:
         """Compress and send one message (see
         ``FusedCompressionManager.send_paged_requests``: straight into the
-        consumer's ring on the NVLink transport)."""
-        return self._manager.send_paged_requests(transport, request_id, layer_names, kv_layers,
-                                                 layer_ids, requests, member_tids)
+        consumer's ring on the NVLink transport).  None, with nothing sent,
+        when the controller picks no compression for it (the caller sends
+        the raw KV)."""
+        mgr, extra = self._paged_manager(kv_layers, requests, request_id)
+        if mgr is None:
+            return None
+        return mgr.send_paged_requests(transport, request_id, layer_names, kv_layers, layer_ids,
+                                       requests, member_tids, extra_meta=extra)
 
     def decompress_paged_requests(self, compressed, dst_layers, dst_requests):
-        return self._manager.decompress_paged_requests(compressed, dst_layers, dst_requests)
+        return self._decode_manager(compressed).decompress_paged_requests(compressed, dst_layers,
+                                                                          dst_requests)
+
+    def decompress_members(self, compressed, dst_layers, selection):
+        """Grouped message: decode the members in ``selection`` (member
+        index -> destination block ids) in one launch."""
+        return self._decode_manager(compressed).decompress_members(compressed, dst_layers,
+                                                                   selection)
 
     def warmup(self, block_size: int = 16) -> None:
         if self._manager is not None and hasattr(self._manager, "warmup"):

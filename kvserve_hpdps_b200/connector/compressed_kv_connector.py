@@ -133,6 +133,13 @@ def layer_index(name: str) -> int:
     return int(m.group(1)) if m else 0
 
 
+def _blocks_outer(kv_layer: torch.Tensor) -> bool:
+    """True for a ``[num_blocks, 2, ...]`` (FlashInfer) layer, False for
+    ``[2, num_blocks, ...]`` (FlashAttention); the block utilities tell the
+    two apart the same way."""
+    return kv_layer.shape[0] != 2 and kv_layer.dim() > 1 and kv_layer.shape[1] == 2
+
+
 def max_chunk_bytes() -> int:
     raw = os.environ.get("KVSERVE_MAX_NCCL_CHUNK_BYTES")
     try:
@@ -370,17 +377,21 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     self._side_stream.wait_event(ready)
                     # one grouped message for the layer; on the NVLink ring the
                     # producer kernels store it straight into the consumer's memory
-                    comp.send_paged_requests(self._transport, tids[0], add_sentinel([layer_name]),
-                                             [kv_layer], [layer_index(layer_name)], requests,
-                                             member_tids=tids)
+                    info = comp.send_paged_requests(self._transport, tids[0],
+                                                    add_sentinel([layer_name]), [kv_layer],
+                                                    [layer_index(layer_name)], requests,
+                                                    member_tids=tids)
             except Exception:  # noqa: BLE001
                 # as in the off mode: a compression failure sends this layer's raw
                 # KV, one message per request (the consumer still counts one
                 # message per layer for each transfer id)
                 logger.exception("compression of %s failed; sending raw KV", layer_name)
-                for rm in meta.requests:
-                    raw = extract_kv_from_layer_by_blocks(kv_layer, rm.block_ids).unsqueeze(0)
-                    self._transport.send(rm.transfer_id, [layer_name], raw)
+                info = None
+            if info is None:  # failed, or the controller picked no compression
+                with torch.cuda.stream(self._side_stream):
+                    for rm in meta.requests:
+                        raw = extract_kv_from_layer_by_blocks(kv_layer, rm.block_ids).unsqueeze(0)
+                        self._transport.send(rm.transfer_id, [layer_name], raw)
             for t in tids:
                 self._expected_msgs[t] = self._num_layers
 
@@ -414,10 +425,11 @@ class CompressedKVConnector(KVConnectorBase_V1):
             t0 = time.monotonic()
             span = self._prefill_span(rid)
             layers = [self._layer_refs[n] for n in names]
-            if comp is not None and comp.supports_paged() and layers[0].is_cuda:
+            use = comp  # this request's compressor (None: raw KV)
+            if use is not None and use.supports_paged() and layers[0].is_cuda:
                 try:
                     with nvtx("kvs.compress_send"):
-                        info = comp.send_paged_requests(
+                        info = use.send_paged_requests(
                             self._transport, tid, add_sentinel(names), layers,
                             [layer_index(n) for n in names], [(rm.block_ids, len(rm.token_ids))],
                             member_tids=[tid])
@@ -427,16 +439,21 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     info = None
                 if info is not None:
                     self._expected_msgs[tid] = 1
-                    stat = (rid, info["original_size"], info["wire_nbytes"],
-                            (time.monotonic() - t0) * 1e3, span)
+                    compress_ms = (time.monotonic() - t0) * 1e3
+                    stat = (rid, info["original_size"], info["wire_nbytes"], compress_ms, span)
+                    ctl = getattr(use, "controller_mode", False)
                     if self._listening:  # written with the exact size once it is out
                         self._stats_wait[tid] = stat
+                        if ctl:  # the paged path keys the controller context by transfer id
+                            self._ctl_wait[tid] = (tid, compress_ms, time.monotonic())
                     else:
                         write_compression_stats(rid, tid, stat[1], stat[2], compress_ms=stat[3],
                                                 prefill_span_ms=stat[4])
+                        if ctl:
+                            use.update_controller(tid, compress_ms)
                     continue
-                comp = None
-            if comp is None and hasattr(self._transport, "send_paged") and layers[0].is_cuda:
+                use = None  # failed, or the controller picked no compression
+            if use is None and hasattr(self._transport, "send_paged") and layers[0].is_cuda:
                 # raw KV: one gather launch from the paged caches into the peer ring
                 with nvtx("kvs.send_raw"):
                     self._transport.send_paged(tid, names, layers, rm.block_ids)
@@ -444,14 +461,18 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 continue
             stacked = torch.stack([extract_kv_from_layer_by_blocks(l, rm.block_ids)
                                    for l in layers], 0)
-            cd = comp.compress(stacked, rid) if comp is not None else None
+            if use is not None and _blocks_outer(layers[0]):
+                # compressors take [L, 2 (K, V), blocks, ...]; the raw path keeps
+                # the caches' own order, which the consumer's caches share
+                stacked = stacked.transpose(1, 2).contiguous()
+            cd = use.compress(stacked, rid) if use is not None else None
             if cd is not None:
                 compress_ms = (time.monotonic() - t0) * 1e3
                 if self._listening:  # completed by _apply_controller_feedback
                     self._ctl_wait[tid] = (rid, compress_ms, time.monotonic())
                 nbytes = self._send_compressed(tid, names, cd)
                 if not self._listening:
-                    comp.update_controller(rid, (time.monotonic() - t0) * 1e3)
+                    use.update_controller(rid, (time.monotonic() - t0) * 1e3)
                 write_compression_stats(rid, tid, stacked.numel() * stacked.element_size(), nbytes,
                                         compress_ms=(time.monotonic() - t0) * 1e3,
                                         prefill_span_ms=span)
@@ -729,7 +750,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 else:  # one launch for every member scheduled now
                     sel = {i: self._step_reqs[t].block_ids for i, t in enumerate(tids)
                            if t in members}
-                    comp.manager.decompress_members(cd, caches, sel)
+                    comp.decompress_members(cd, caches, sel)
                 return
             kv = comp.decompress(cd)
             if kv is None:
@@ -737,8 +758,9 @@ class CompressedKVConnector(KVConnectorBase_V1):
             rm = self._step_reqs[members[0]]
             for i, name in enumerate(names):
                 cache = self._layer_cache(name, fc)
-                if cache is not None:
-                    inject_kv_into_layer_by_blocks(cache, kv[i], rm.block_ids, rm.request_id)
+                if cache is not None:  # kv[i] is [2 (K, V), blocks, ...]
+                    part = kv[i].transpose(0, 1) if _blocks_outer(cache) else kv[i]
+                    inject_kv_into_layer_by_blocks(cache, part, rm.block_ids, rm.request_id)
             return
         rm = self._step_reqs[members[0]]
         payload_t = payload["tensor"] if isinstance(payload, dict) and \

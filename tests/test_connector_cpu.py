@@ -289,6 +289,43 @@ def test_default_mode_handoff_on_cpu():
         assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.9
 
 
+def test_compressed_handoff_with_blocks_outer_caches():
+    """FlashInfer-layout caches ([num_blocks, 2, bs, H, D], what vLLM
+    allocates on B200): the whole-tensor compressors get [L, 2, blocks, ...],
+    so keys and values are quantized as keys and values, and the consumer
+    writes each plane back into its own half of the blocks.  Keys and values
+    have scales 100x apart, which a K/V mix-up would not survive."""
+    p, c, pair = make_pair("default")
+    g = torch.Generator().manual_seed(3)
+
+    def fi_caches(fill):
+        out = {}
+        for l in range(L):
+            t = torch.zeros(8, 2, BS, H, D)
+            if fill:
+                t[:, 0] = 10.0 * torch.randn(8, BS, H, D, generator=g)
+                t[:, 1] = 0.1 * torch.randn(8, BS, H, D, generator=g)
+            out[f"model.layers.{l}.self_attn.attn"] = t.to(torch.bfloat16)
+        return out
+    pc, cc = fi_caches(True), fi_caches(False)
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    p.bind_connector_metadata(meta_for("r1", "tid-1", 48, [5, 1, 7]))
+    for name in sorted(pc, key=layer_index):
+        p.save_kv_layer(name, pc[name], None)
+    p.wait_for_save()
+    c.bind_connector_metadata(meta_for("d1", "tid-1", 48, [2, 6, 0]))
+    c.start_load_kv(None)
+    assert pair.messages == 1
+    for name in pc:
+        for plane in (0, 1):
+            a = pc[name][[5, 1, 7], plane].float().flatten()
+            b = cc[name][[2, 6, 0], plane].float().flatten()
+            # 2-bit values of most heads keep cosine ~0.87 on Gaussian data
+            assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.8, (name, plane)
+            assert 0.5 < float(b.norm() / a.norm()) < 2.0, (name, plane)
+
+
 def test_overlap_modes_are_normalized(monkeypatch):
     from kvserve_hpdps_b200.connector.compressed_kv_connector import normalize_overlap_mode
     assert [normalize_overlap_mode(m) for m in ("off", "stream", "tq", "full", "FULL", None,

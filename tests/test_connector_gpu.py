@@ -94,6 +94,62 @@ def test_fused_default_handoff_in_process(overlap, compression, monkeypatch):
         assert pair.messages == 2
 
 
+@pytest.mark.parametrize("blocks_outer", [False, True], ids=["fa_layout", "fi_layout"])
+def test_controller_mode_paged_handoff(blocks_outer, tmp_path, monkeypatch):
+    """Controller mode with a library of fused profiles: the producer sends
+    through the paged kernels (no dense copy of the request), the message
+    names its profile and the consumer decodes with that profile's manager.
+    Both cache layouts ([2, blocks, ...] and [blocks, 2, ...])."""
+    monkeypatch.setenv("KVSERVE_OVERLAP_MODE", "off")
+    from kvserve_hpdps_b200.connector.compressed_kv_connector import (CompressedKVConnector,
+                                                                      KVConnectorRole)
+    from kvserve_hpdps_b200.offline.library_export import build_library, write_library
+    from kvserve_hpdps_b200.offline.search_space import Candidate
+    from kvserve_hpdps_b200.parallel.fake_transport import FakeTransportPair
+
+    def spec(cfg):
+        return {"enabled": True, "pipeline": ["transformer", "quantizer", "codec"],
+                "quantizer_config": dict(cfg), "codec_config": {"codec_type": "rans"},
+                "min_compress_size": 0}
+    evals = [{"candidate": c.key(), "config": c.quantizer_config(), "accuracy": acc,
+              "compression_ratio": cr, "harmonic_speed_mbps": 30000.0}
+             for c, acc, cr in [(Candidate(0.0, 16, 16, 8, 6), 0.995, 3.5),
+                                (Candidate(0.8, 12, 8, 6, 4), 0.97, 6.0)]]
+    path = tmp_path / "lib.json"
+    write_library(str(path), build_library(evals, "Qwen2.5-7B-Instruct", spec_builder=spec))
+    ctl = {"mode": "controller", "library_path": str(path), "epsilon": 0.0,
+           "service_config": {"bandwidth_mbps": 150.0, "slo_ms": 1e9,
+                              "accuracy_requirement": 0.96, "t_model_ms": 0.0}}
+    pair = FakeTransportPair()
+    p = CompressedKVConnector(vllm_config(True, ctl), KVConnectorRole.WORKER)
+    c = CompressedKVConnector(vllm_config(False, ctl), KVConnectorRole.WORKER)
+    p.attach_transport(pair.producer())
+    c.attach_transport(pair.consumer())
+    pc, cc = _caches(24, 1, "cuda"), _caches(24, 2, "cuda", fill=False)
+    if blocks_outer:  # same values, [blocks, 2, bs, H, D]
+        pc = {n: t.transpose(0, 1).contiguous() for n, t in pc.items()}
+        cc = {n: t.transpose(0, 1).contiguous() for n, t in cc.items()}
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    bp, bc, n = [3, 9, 1, 17, 5, 20, 11], [4, 2, 8, 10, 12, 14, 16], 100
+    p.bind_connector_metadata(_meta([("a", "ta", n, bp)]))
+    for name in sorted(pc):
+        p.save_kv_layer(name, pc[name], None)
+    p.wait_for_save()
+    torch.cuda.synchronize()
+    c.bind_connector_metadata(_meta([("da", "ta", n, bc)]))
+    c.start_load_kv(None)
+    torch.cuda.synchronize()
+    comp_p, comp_c = p._get_compressor(), c._get_compressor()
+    assert comp_p.supports_paged() and pair.messages == 1
+    assert len(comp_p._manager_cache) == 1 and len(comp_c._manager_cache) == 1
+    for name in pc:
+        for plane in (0, 1):
+            src = (pc[name][bp, plane] if blocks_outer else pc[name][plane, bp]).reshape(-1, H, D)[:n]
+            dst = (cc[name][bc, plane] if blocks_outer else cc[name][plane, bc]).reshape(-1, H, D)[:n]
+            assert _cos(src, dst) > 0.85, (name, plane)
+
+
 def test_stream_mode_loads_layer_by_layer(monkeypatch):
     """Stream mode on the consumer: start_load_kv returns without waiting for
     the whole request, and wait_for_layer_load(l) makes layer l's KV (of
