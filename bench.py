@@ -659,25 +659,31 @@ def _e2e_local(args, mgr, wl, device):
     L = wl.L
     steps = max(2, min(args.steps, 10))
 
+    errs = K.StepErrors(device)
+
     def one():
         cd = mgr.compress_paged_requests(wl.src_layers(), list(range(L)), wl.src_req, trim=False)
         mgr.decompress_paged_requests(cd, wl.dst_layers(), wl.dst_req)
-        K.read_device_error(device)
+        errs.push()  # this step's error word to pinned host memory
+        errs.check(keep=1)  # the previous step's word, read while this step runs
     for _ in range(2):
         one()
+    errs.check(0)
     torch.cuda.synchronize(device)
     K.reset_transfer_counters()
     ev0, ev1 = _events()
     ev0.record()
     for _ in range(steps):
         one()
+    errs.check(0)  # the last step's result
     ev1.record()
     torch.cuda.synchronize(device)
     c = K.transfer_counters()
     return {"value": round(ev0.elapsed_time(ev1) / (steps * wl.B), 5), "unit": "ms/request",
             "h2d_bytes_per_step": c["h2d"] // steps, "d2h_bytes_per_step": c["d2h"] // steps,
             "steps": steps,
-            "path": "compress_paged_requests -> decompress_paged_requests, error word read"}
+            "path": "compress_paged_requests -> decompress_paged_requests; each step's error "
+                    "word copied to pinned host memory and read while the next step runs"}
 
 
 def _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending):
@@ -692,6 +698,8 @@ def _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending):
     L = wl.L
     steps = max(2, min(args.steps, 10))
 
+    errs = K.StepErrors(device)
+
     def one(s):
         if role == "producer":
             mgr.send_paged_requests(tr, f"e{s}", names, wl.src_layers(), list(range(L)),
@@ -703,11 +711,13 @@ def _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending):
                                                   payload["aux_tensors"]))
             mgr.decompress_paged_requests(cd, wl.dst_layers(), wl.dst_req)
             tr.release(payload, device)
-        K.read_device_error(device)
+        errs.push()  # this step's error word to pinned host memory
+        errs.check(keep=1)  # the previous step's word, read while this step runs
     s = 0
     for _ in range(2):
         one(s)
         s += 1
+    errs.check(0)
     if role == "producer":
         tr.wait_for_sent(120.0)
     torch.cuda.synchronize(device)
@@ -718,6 +728,7 @@ def _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending):
     for _ in range(steps):
         one(s)
         s += 1
+    errs.check(0)  # the last step's result
     if role == "producer" and not tr.wait_for_sent(120.0):
         raise TimeoutError("sends did not complete")
     ev1.record()
@@ -729,7 +740,8 @@ def _e2e_pairs(args, mgr, wl, tr, role, world, pairs, device, names, pending):
     return {"value": round(ms / (steps * wl.B), 5), "unit": "ms/request",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
             "path": "send_paged_requests -> P2PTransport ring -> drain_received/prepare -> "
-                    "restore_from_wire -> decompress_paged_requests, error word read per step"}
+                    "restore_from_wire -> decompress_paged_requests; each step's error word "
+                    "copied to pinned host memory and read while the next step runs"}
 
 
 class _SizeListener:

@@ -153,6 +153,39 @@ class ErrorMonitor:
         return code
 
 
+class StepErrors:
+    """Every step's device error word, read one step late: ``push()`` (after
+    the step's work is enqueued) copies the word into pinned host memory on
+    the current stream and clears it; ``check(keep)`` waits for all but the
+    newest ``keep`` copies and raises on an error.  With ``keep=1`` the host
+    enqueues step s+1 while step s still runs, and still reads every step's
+    result; ``check(0)`` at the end reads the last one."""
+
+    def __init__(self, device: torch.device, depth: int = 4):
+        self.device = device
+        self._free = [torch.zeros(1, dtype=torch.int32).pin_memory() for _ in range(depth)]
+        self._pending: list = []
+
+    def push(self) -> None:
+        if not self._free:
+            self.check(0)
+        host = self._free.pop()
+        ws = workspace(self.device)
+        host.copy_(ws.err[:1], non_blocking=True)
+        ws.err.zero_()
+        self._pending.append((host, torch.cuda.current_stream(self.device).record_event()))
+        _xfer["d2h"] += 4
+
+    def check(self, keep: int = 0) -> None:
+        while len(self._pending) > keep:
+            host, ev = self._pending.pop(0)
+            ev.synchronize()
+            code = int(host[0])
+            self._free.append(host)
+            if code:
+                raise RuntimeError(f"device error {code} ({ERR_NAMES.get(code, '?')})")
+
+
 def check_device_error(device: torch.device, what: str = "kernel") -> None:
     code = read_device_error(device)
     if code:

@@ -569,3 +569,22 @@ def test_rans_decode_rejects_corrupt_streams():
     K.rans_decode(s[:1000], x.numel())  # truncated: the header's total exceeds the buffer
     torch.cuda.synchronize()
     assert K.read_device_error(out.device) == 4
+
+
+def test_step_errors_read_every_step_one_step_late():
+    """StepErrors: each push copies and clears the error word; check(keep=1)
+    reports a step's error once the next step has been pushed, check(0) the
+    last one."""
+    dev = torch.device("cuda", 0)
+    K.read_device_error(dev)  # clear
+    errs = K.StepErrors(dev)
+    errs.push()
+    errs.check(keep=1)  # nothing older than the newest
+    K.workspace(dev).err[0] = 7  # step 2 fails
+    errs.push()
+    errs.check(keep=1)  # step 1 was clean
+    errs.push()  # step 3: the word was cleared by step 2's push
+    with pytest.raises(RuntimeError, match="device error 7"):
+        errs.check(keep=1)
+    errs.check(0)
+    assert K.read_device_error(dev) == 0
