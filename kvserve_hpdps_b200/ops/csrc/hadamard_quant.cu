@@ -1359,7 +1359,9 @@ constexpr int kWsGroupThreads = kWsGroupWarps * 32;
 constexpr int kWsCtrlWarp = kWsGroups * kWsGroupWarps;  // warp 16: MMAs (dequant: loads too)
 constexpr int kWsThreads = (kWsCtrlWarp + 1) * 32;       // 544 (dequantize kernel)
 constexpr int kWsLoadWarp = kWsCtrlWarp + 1;             // warp 17: TMA loads (stats, quant)
-constexpr int kWsProdThreads = (kWsLoadWarp + 1) * 32;   // 576 (stats, quantize kernels)
+constexpr int kWsProdThreads = (kWsLoadWarp + 1) * 32;   // 576 (quantize kernel)
+constexpr int kWsLoadWarp2 = kWsLoadWarp + 1;            // warp 18: second TMA load warp (stats)
+constexpr int kWsStatsThreads = (kWsLoadWarp2 + 1) * 32;  // 608 (stats kernel)
 constexpr int kWsMaxStages = 5;
 constexpr int kWsStagingBytes = 128 * 144;  // 128 rows x (W|1)*16 B for W <= 8
 // Layout from the 1024-aligned base: image | NS stages | staging (quant) |
@@ -1518,15 +1520,20 @@ KVS_DEV void issue_boxes(const BoxDesc& d, uint8_t* tile, uint64_t* bar, uint32_
   __syncwarp();
 }
 
-// Load warp: TMA loads of local jobs [0, n) into the NS-stage ring.  Job j
+// Load warps: TMA loads of local jobs [0, n) into the NS-stage ring.  Job j
 // goes into stage j % NS as soon as the MMA of job j - NS (the stage's
-// previous user) has retired; the block ids of job j + 1 are read while job
-// j's boxes are in flight, so an issue never waits on memory.  All 32 lanes
-// run the loop (lanes 0-15 issue one box each); lane 0 waits on barriers.
-// After a failed wait it stops issuing; before returning it waits (bounded)
-// for the copies it issued into the ring's last stages.
-template <int NS>
-KVS_DEV void ws_loader(const LayerLaunch& L, const WsSmem& S, const WsMap& M) {
+// previous user) has retired.  With `nl` load warps, warp `first` takes jobs
+// first, first + nl, ...: issuing a tile's 16 boxes (lanes 0-15, one box
+// each) and reading the block ids of its jobs take a warp about a
+// microsecond, so the warps' issues overlap.  A warp reads the block ids of
+// its job three issues ahead (the loop is unrolled by three and each
+// descriptor is refilled in place after its boxes are issued), so a read's
+// latency stays off the loop.  Lane 0 waits on barriers.  After a failed wait
+// a warp stops issuing; before returning it waits (bounded) for the copies
+// it issued into the ring's last stages.
+template <int NS, bool kTraceLoader = false>
+KVS_DEV void ws_loader(const LayerLaunch& L, const WsSmem& S, const WsMap& M, int first = 0,
+                       int nl = 1) {
   const int n = M.n;
   const int lane = threadIdx.x & 31;
   ItemCursor ld;
@@ -1536,20 +1543,32 @@ KVS_DEV void ws_loader(const LayerLaunch& L, const WsSmem& S, const WsMap& M) {
     if (lane == 0) r = mbar_wait(bar, parity, L.err, ERR_MBAR_TIMEOUT);
     return __shfl_sync(0xFFFFFFFFu, r ? 1 : 0, 0) != 0;
   };
-  int issued = 0;
-  BoxDesc next = box_desc(L, ld, ws_job(M, 0));
-  for (; issued < n; ++issued) {
-    const int st = issued % NS;
-    if (issued >= NS &&
-        !wait0(&S.sfree[st], static_cast<uint32_t>((issued / NS - 1) & 1)))
-      break;
-    issue_boxes(next, ws_stage(S, st), &S.full[st], L.err);
-    if (lane == 0) trace_mark(L, issued, 2);
-    if (issued + 1 < n) next = box_desc(L, ld, ws_job(M, issued + 1));
+  int job = first;  // the next job this warp issues
+  BoxDesc q0 = box_desc(L, ld, ws_job(M, min(job, n - 1)));
+  BoxDesc q1 = job + nl < n ? box_desc(L, ld, ws_job(M, job + nl)) : q0;
+  BoxDesc q2 = job + 2 * nl < n ? box_desc(L, ld, ws_job(M, job + 2 * nl)) : q0;
+  auto step = [&](BoxDesc& q) -> bool {  // issue `job` from q, refill q
+    const int st = job % NS;
+    if (job >= NS && !wait0(&S.sfree[st], static_cast<uint32_t>((job / NS - 1) & 1)))
+      return false;
+    if (lane == 0 && kTraceLoader) trace_mark(L, job, 6);
+    issue_boxes(q, ws_stage(S, st), &S.full[st], L.err);
+    if (lane == 0) trace_mark(L, job, 2);
+    if (job + 3 * nl < n) q = box_desc(L, ld, ws_job(M, job + 3 * nl));
+    if (lane == 0 && kTraceLoader) trace_mark(L, job, 7);
+    job += nl;
+    return true;
+  };
+  while (job < n) {
+    if (!step(q0) || job >= n) break;
+    if (!step(q1) || job >= n) break;
+    if (!step(q2)) break;
   }
-  // Earlier jobs' copies landed before their stages were refilled.
+  // This warp's copies among the last NS jobs landed (every earlier job's
+  // had landed before its stage was refilled; a stage whose phase moved on
+  // twice must not be waited on with the old parity).
   if (lane == 0)
-    for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+    for (int j = job - nl; j >= first && j >= n - NS; j -= nl)
       mbar_wait(&S.full[j % NS], static_cast<uint32_t>((j / NS) & 1), nullptr, 0);
 }
 
@@ -1616,7 +1635,7 @@ KVS_DEV void ws_mma(const LayerLaunch& L, const WsSmem& S, uint32_t tmem, const 
 }
 
 // ------------------------------------------------------------ stats (ws)
-__global__ void __launch_bounds__(kWsProdThreads, 1) k_stats_ws(LayerLaunch L) {
+__global__ void __launch_bounds__(kWsStatsThreads, 1) k_stats_ws(LayerLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   constexpr int NS = 5;
   const WsSmem S = ws_smem<WsStatsLayout>(smem_raw);
@@ -1633,8 +1652,8 @@ __global__ void __launch_bounds__(kWsProdThreads, 1) k_stats_ws(LayerLaunch L) {
   const uint32_t tmem = *S.tslot;
   if (warp == kWsCtrlWarp) {
     ws_mma<true, NS>(L, S, tmem, M);
-  } else if (warp == kWsLoadWarp) {
-    ws_loader<NS>(L, S, M);
+  } else if (warp == kWsLoadWarp || warp == kWsLoadWarp2) {
+    ws_loader<NS>(L, S, M, warp - kWsLoadWarp, 2);
   } else {
     const int g = warp / kWsGroupWarps, gw = warp % kWsGroupWarps;
     const int quad = gw & 3, half = gw >> 2;
@@ -2579,7 +2598,7 @@ int kvs_stats(const LayerLaunch* Lp) {
   dim3 grid(L.total_tiles, L.num_heads, 2);
   if (L.engine == 0) {
     if (int rc = set_smem(k_stats_ws, WsStatsLayout::kSmem)) return rc;
-    k_stats_ws<<<ws_grid(L), kWsProdThreads, WsStatsLayout::kSmem, s>>>(L);
+    k_stats_ws<<<ws_grid(L), kWsStatsThreads, WsStatsLayout::kSmem, s>>>(L);
   } else if (L.engine == 3) {
     if (int rc = set_smem(k_stats_tc, kPSmem)) return rc;
     k_stats_tc<<<persistent_grid(L), kPThreads, kPSmem, s>>>(L);
