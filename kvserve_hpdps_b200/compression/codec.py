@@ -44,18 +44,37 @@ CODEC_NAMES = {v: k for k, v in CODEC_IDS.items()}
 _NVCOMP_ALGOS = ("ANS", "Bitcomp", "Cascaded", "Deflate", "GDeflate", "LZ4", "Zstd")
 
 
+_NVCOMP_MAPPING = ("nvcomp algorithms map to this framework's own lossless coders (nvCOMP is "
+                   "not used): Bitcomp -> bitpack; ANS, Cascaded, Deflate, GDeflate, LZ4, "
+                   "Zstd -> rans (an entropy coder: the dictionary/LZ algorithms are not "
+                   "reproduced)")
+_mapped_logged: set = set()
+
+
 def resolve_codec(codec_type: Optional[str], algorithm: Optional[str] = None) -> str:
-    """Map a reference or own codec name to one of none | rans | bitpack."""
+    """Map a reference or own codec name to one of none | rans | bitpack | lc.
+
+    The reference's ``nvcomp`` codec names an nvCOMP algorithm; here each
+    maps to an own coder: ``Bitcomp`` -> bit-packing, every other one
+    (``ANS``, ``Cascaded``, ``Deflate``, ``GDeflate``, ``LZ4``, ``Zstd``) ->
+    the rANS entropy coder.  A name other than ``ANS``/``Bitcomp`` is logged
+    once with that mapping, since the dictionary coders are not reproduced."""
     ct = (codec_type or "nvcomp").lower()
     if ct in ("rans", "bitpack", "none", "lc"):
         return ct
     if ct == "nvcomp":
         algo = algorithm or "ANS"
         if algo not in _NVCOMP_ALGOS:
-            raise ValueError(f"invalid nvcomp algorithm {algo!r}")
+            raise ValueError(f"invalid nvcomp algorithm {algo!r}; expected one of "
+                             f"{', '.join(_NVCOMP_ALGOS)} ({_NVCOMP_MAPPING})")
+        if algo not in ("ANS", "Bitcomp") and algo not in _mapped_logged:
+            _mapped_logged.add(algo)
+            from kvserve_hpdps_b200.utils.logger import get_logger
+            get_logger(__name__).warning("nvcomp algorithm %s runs as the rans coder (%s)",
+                                         algo, _NVCOMP_MAPPING)
         return "bitpack" if algo == "Bitcomp" else "rans"
     raise ValueError(f"invalid codec type {codec_type!r}; expected rans, bitpack, none, "
-                     "nvcomp or lc")
+                     f"nvcomp or lc ({_NVCOMP_MAPPING})")
 
 
 def _header(codec: str, n: int, device) -> torch.Tensor:

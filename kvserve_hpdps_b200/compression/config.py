@@ -124,6 +124,11 @@ def validate_spec(spec: Any) -> None:
             raise ValueError(f"unknown pipeline stage {stage!r}")
     if spec.get("quantizer_config"):
         validate_quantizer_config(spec["quantizer_config"])
+    cc = spec.get("codec_config")
+    if cc and "codec" in (spec.get("pipeline") or []):
+        # raises with the nvCOMP-name mapping for an unknown coder
+        from kvserve_hpdps_b200.compression.codec import resolve_codec
+        resolve_codec(cc.get("codec_type"), cc.get("nvcomp_algorithm"))
     overlap = spec.get("overlap", "off")
     if overlap not in ("off", "tq", "full", "stream"):
         raise ValueError(f"overlap must be off|tq|full|stream, got {overlap!r}")

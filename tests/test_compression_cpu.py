@@ -486,3 +486,20 @@ def test_default_mode_falls_back_to_the_generic_pipeline_on_cpu():
     assert out.shape == x.shape
     cos = torch.nn.functional.cosine_similarity(out.float().flatten(), x.float().flatten(), dim=0)
     assert float(cos) > 0.95
+
+
+def test_nvcomp_names_map_to_own_coders_and_say_so():
+    """The reference's nvCOMP algorithm names resolve to this framework's own
+    coders; an unknown name is rejected by the spec validator with the
+    mapping in the error text."""
+    from kvserve_hpdps_b200.compression.codec import resolve_codec
+    from kvserve_hpdps_b200.compression.config import validate_spec
+    assert resolve_codec("nvcomp", "Bitcomp") == "bitpack"
+    assert {resolve_codec("nvcomp", a) for a in
+            ("ANS", "Cascaded", "Deflate", "GDeflate", "LZ4", "Zstd")} == {"rans"}
+    spec = {"enabled": True, "pipeline": ["quantizer", "codec"],
+            "codec_config": {"codec_type": "nvcomp", "nvcomp_algorithm": "Snappy"}}
+    with pytest.raises(ValueError, match="LZ4, Zstd -> rans"):
+        validate_spec(spec)
+    spec["codec_config"]["nvcomp_algorithm"] = "LZ4"
+    validate_spec(spec)
