@@ -66,6 +66,12 @@ _ALIASES: dict[str, tuple[str, ...]] = {
     "offline_search.src.cache.duoattn_utils": ("offline.caches",),
     "offline_search.duo_config": ("offline.duo_scores",),
     "offline_search.duo_config.duo_config": ("offline.duo_scores",),
+    "offline_search.evaluation": ("offline",),
+    "offline_search.evaluation.param_search": ("offline.param_search",),
+    "offline_search.evaluation.param_search.acc_evaluator": ("offline.param_search",),
+    "offline_search.evaluation.param_search.cr_evaluator": ("offline.param_search",),
+    "offline_search.evaluation.lm_eval": ("offline.lm_harness",),
+    "offline_search.evaluation.lm_eval.lm_wrapper": ("offline.lm_harness",),
 }
 
 # reference name -> name in the target modules

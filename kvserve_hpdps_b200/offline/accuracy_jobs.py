@@ -13,6 +13,8 @@ parameters) on one model. The task is either
 
 * ``lm_eval:<task>``: an lm-eval task run through the model class that
   ``lm_harness.register_lm_eval`` adds, when lm-eval is installed; or
+* a local task file (answers or choices per document, :mod:`offline.tasks`):
+  the task's score x100 with the method's cache; or
 * a prompt set scored by ``lm_harness.evaluate_method``: greedy-token
   agreement with the default cache (x100), first-step top-1 agreement and
   KL, and the cache's own compression ratio.  ``synthetic`` draws seeded
@@ -44,6 +46,8 @@ from dataclasses import dataclass, field
 from typing import Any, Iterable, Optional, Sequence
 
 import torch
+
+from kvserve_hpdps_b200.offline.tasks import is_task_file
 
 LM_EVAL_PREFIX = "lm_eval:"
 
@@ -83,8 +87,8 @@ def load_prompts(task: str, vocab_size: int, tokens: int = 512, count: int = 4,
         g = torch.Generator().manual_seed(seed)
         return [torch.randint(0, vocab_size, (tokens,), generator=g) for _ in range(count)]
     if not os.path.exists(task):
-        raise ValueError(f"unknown task {task!r}: expected 'synthetic', a prompt file or "
-                         f"{LM_EVAL_PREFIX}<task>")
+        raise ValueError(f"unknown task {task!r}: expected 'synthetic', a prompt file, a task "
+                         f"file or {LM_EVAL_PREFIX}<task>")
     with open(task) as f:
         text = f.read()
     try:
@@ -123,9 +127,34 @@ def _lm_eval_job(model_name: str, job: Job, model_args: str, limit: Optional[int
             "metrics": {k: v for k, v in metrics.items() if isinstance(v, (int, float))}}
 
 
+def _task_file_job(model, job: Job, scores: Optional[torch.Tensor], limit: Optional[int],
+                   tokenizer=None) -> dict:
+    """A local task file (:mod:`offline.tasks`) with the method's cache: the
+    accuracy is the task's score x100 over its first ``limit`` documents."""
+    from kvserve_hpdps_b200.offline.lm_harness import CacheMethodModel
+    from kvserve_hpdps_b200.offline.tasks import TaskRunner, load_task
+    task = load_task(job.task)
+    params = dict(job.params)
+    if job.method == "custom":
+        params.setdefault("device", str(model.device))
+    cm = CacheMethodModel(model, job.method, scores if job.method != "default" else None,
+                          **params)
+    try:
+        n = len(task.docs) if not limit else min(limit, len(task.docs))
+        r = TaskRunner(cm, tokenizer).run(task, range(n))
+        cache = cm.last_cache
+        cr = float(cache.compute_compression_ratio()) \
+            if hasattr(cache, "compute_compression_ratio") else 1.0
+    finally:
+        cm.close()
+    return {"accuracy": round(100.0 * r["score"], 4), "backend": "task-file",
+            "metrics": {k: v for k, v in r.items() if k != "docs"}, "docs": r["docs"],
+            "compression_ratio": cr}
+
+
 def run_job(model, model_name: str, job: Job, scores: Optional[torch.Tensor] = None,
             tokens: int = 512, prompts: int = 4, max_new_tokens: int = 16,
-            model_args: str = "", limit: Optional[int] = None) -> dict:
+            model_args: str = "", limit: Optional[int] = None, tokenizer=None) -> dict:
     """Run one job; returns its result row."""
     from kvserve_hpdps_b200.offline.lm_harness import evaluate_method
     t0 = time.monotonic()
@@ -133,6 +162,8 @@ def run_job(model, model_name: str, job: Job, scores: Optional[torch.Tensor] = N
            "config": dict(job.params)}
     if job.task.startswith(LM_EVAL_PREFIX):
         row.update(_lm_eval_job(model_name, job, model_args, limit))
+    elif is_task_file(job.task):
+        row.update(_task_file_job(model, job, scores, limit, tokenizer))
     else:
         ps = load_prompts(job.task, int(model.config.vocab_size), tokens, prompts)
         params = dict(job.params)
@@ -260,7 +291,8 @@ def main(argv=None) -> int:
     r.add_argument("--tokens", type=int, default=512)
     r.add_argument("--prompts", type=int, default=4)
     r.add_argument("--new-tokens", type=int, default=16)
-    r.add_argument("--limit", type=int, default=None, help="lm-eval examples per task")
+    r.add_argument("--limit", type=int, default=None,
+                   help="documents per task (lm-eval tasks and task files)")
     r.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     r.add_argument("--out", required=True)
     r.add_argument("--no-resume", action="store_true")
@@ -288,11 +320,16 @@ def main(argv=None) -> int:
     from kvserve_hpdps_b200.offline.cr_methods import random_model
     dtype = torch.bfloat16 if args.device.startswith("cuda") else torch.float32
     model_args = ""
+    tokenizer = None
     if args.model:
-        from transformers import AutoModelForCausalLM
+        from transformers import AutoModelForCausalLM, AutoTokenizer
         model = AutoModelForCausalLM.from_pretrained(args.model, torch_dtype=dtype).to(args.device)
         name = os.path.basename(os.path.normpath(args.model))
         model_args = f"pretrained={args.model}"
+        try:  # text task files need it; id-only tasks and prompt sets do not
+            tokenizer = AutoTokenizer.from_pretrained(args.model, local_files_only=True)
+        except (OSError, ValueError):
+            tokenizer = None
     else:
         model, spec = random_model(args.arch, args.layers, args.hidden, dtype=dtype,
                                    device=args.device)
@@ -305,7 +342,7 @@ def main(argv=None) -> int:
                        json.loads(args.grid) if args.grid else None)
     rows = run_jobs(model, name, jobs, args.out, scores, resume=not args.no_resume,
                     tokens=args.tokens, prompts=args.prompts, max_new_tokens=args.new_tokens,
-                    model_args=model_args, limit=args.limit)
+                    model_args=model_args, limit=args.limit, tokenizer=tokenizer)
     print(json.dumps({"jobs": len(jobs), "ran": len(rows), "out": args.out}))
     return 0
 

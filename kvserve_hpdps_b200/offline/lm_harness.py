@@ -185,7 +185,10 @@ def register_lm_eval(name: str = "my_custom_model"):
             params, scores_name, rest = split_cache_args(cache_type, kwargs)
             super().__init__(*args, **rest)
             from kvserve_hpdps_b200.compression.head_scores import get_scores_from_csv
-            scores = get_scores_from_csv(scores_name) if scores_name else None
+            if isinstance(scores_name, torch.Tensor):  # a table passed in-process
+                scores = scores_name
+            else:
+                scores = get_scores_from_csv(scores_name) if scores_name else None
             self._kvs = CacheMethodModel(self.model, cache_type, scores, **params)
 
         def _model_generate(self, context, max_length, stop, **generation_kwargs):

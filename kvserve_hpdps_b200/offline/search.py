@@ -11,6 +11,13 @@ compression within the accuracy tolerance, and writes
   present are not re-evaluated);
 * ``profile_library.json``: every evaluated candidate exported as a
   controller profile library.
+
+With ``--tasks`` the search runs on a causal LM instead, as the reference's
+driver does: compression ratio from a prefill through the custom cache and
+accuracy as task score relative to the default cache (x100, threshold
+100 - tolerance), from local task files or lm-eval tasks
+(:mod:`offline.param_search`).  The model is a checkpoint under
+``--base-model-path`` or a random-init network of the named architecture.
 """
 
 from __future__ import annotations
@@ -60,20 +67,62 @@ def synthetic_kv(layers: int, tokens: int, heads: int, device) -> torch.Tensor:
 
 def run_search(kv: torch.Tensor, model_name: Optional[str], tolerance: float, out_dir: str,
                budget: int = 20, space: Optional[dict] = None, measure_speed: bool = True) -> dict:
-    os.makedirs(out_dir, exist_ok=True)
+    """Search on a KV stack: accuracy is the attention fidelity of the
+    reconstructed KV (1.0 = exact), the threshold 1 - tolerance/100."""
     ev = KVEvaluator(kv, model_name, measure_speed=measure_speed)
+
+    def evaluate(c: Candidate) -> dict:
+        r = ev.evaluate(c).as_dict()
+        r.pop("candidate")
+        r.pop("config")
+        return r
+
+    return _search(evaluate, 1.0 * (1 - tolerance / 100.0), model_name, tolerance, out_dir,
+                   budget, space)
+
+
+def run_model_search(model_name: str, tasks: list[str], tolerance: float, out_dir: str,
+                     budget: int = 20, space: Optional[dict] = None, limit: int = 5,
+                     seed: int = 42, base_model_path: Optional[str] = None,
+                     base_config_path: Optional[str] = None, task_dirs: tuple = (),
+                     device: str = "cpu", cr_task: Optional[str] = None,
+                     model=None, tokenizer=None, model_kwargs: Optional[dict] = None) -> dict:
+    """Search on a causal LM as the reference's driver does: compression
+    ratio from a prefill through the custom cache, accuracy = task score
+    relative to the default cache x100, threshold 100 - tolerance
+    (kvserve_v1/offline_search/evaluation/param_search/test_search.py:24-27)."""
+    from kvserve_hpdps_b200.offline.param_search import (AccuracyEvaluator, CompressionEvaluator,
+                                                         candidate_params)
+    acc = AccuracyEvaluator(model_name, tasks, limit=limit, device=device, random_seed=seed,
+                            base_model_path=base_model_path, base_config_path=base_config_path,
+                            model=model, tokenizer=tokenizer, task_dirs=task_dirs,
+                            model_kwargs=model_kwargs)
+    cr = CompressionEvaluator(model_name, cr_task or tasks[0], device, base_model_path,
+                              base_config_path, model=acc.model, tokenizer=acc.tokenizer,
+                              scores=acc.scores, task_dirs=task_dirs)
+
+    def evaluate(c: Candidate) -> dict:
+        p = candidate_params(c)
+        return {"compression_ratio": cr.evaluate(p), "accuracy": acc.evaluate(p)}
+
+    res = _search(evaluate, 100.0 - tolerance, model_name, tolerance, out_dir, budget, space)
+    res["tasks"] = list(tasks)
+    res["default_scores"] = list(acc.default_scores)
+    save_results(os.path.join(out_dir, f"tolerance_{tolerance:g}_results.json"), res)
+    return res
+
+
+def _search(evaluate_fn, threshold: float, model_name: Optional[str], tolerance: float,
+            out_dir: str, budget: int, space: Optional[dict]) -> dict:
+    os.makedirs(out_dir, exist_ok=True)
     cache_path = os.path.join(out_dir, "cr_cache.csv")
     cache = load_cache(cache_path)
-    baseline = 1.0  # attention fidelity of the uncompressed KV
-    threshold = baseline * (1 - tolerance / 100.0)
 
     def evaluate(c: Candidate) -> dict:
         key = c.key()
         if key in cache:
             return dict(cache[key])
-        r = ev.evaluate(c).as_dict()
-        r.pop("candidate")
-        r.pop("config")
+        r = evaluate_fn(c)
         cache[key] = r
         append_cache(cache_path, key, r)
         return dict(r)
@@ -99,12 +148,26 @@ def main(argv=None) -> int:
     ap.add_argument("--budget", type=int, default=20)
     ap.add_argument("--out", default="search_results")
     ap.add_argument("--no-speed", action="store_true")
+    ap.add_argument("--tasks", help="comma-separated tasks: search on a model with task accuracy "
+                    "(local task files, or lm-eval task names when lm-eval is installed)")
+    ap.add_argument("--task-dir", action="append", default=[],
+                    help="directory holding <task>.json / <task>.jsonl files")
+    ap.add_argument("--limit", type=int, default=5, help="documents per task")
+    ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--base-model-path", help="directory holding <model>/ checkpoints")
+    ap.add_argument("--base-config-path", help="directory holding <model>_scores.csv")
+    ap.add_argument("--model-layers", type=int, help="random-init model: number of layers")
     args = ap.parse_args(argv)
     device = "cuda" if torch.cuda.is_available() else "cpu"
-    kv = torch.load(args.kv).to(device) if args.kv else \
-        synthetic_kv(args.layers, args.tokens, args.heads, device)
-    res = run_search(kv, args.model, args.tolerance, args.out, args.budget,
-                     measure_speed=not args.no_speed)
+    if args.tasks:
+        res = run_model_search(args.model, args.tasks.split(","), args.tolerance, args.out,
+                               args.budget, limit=args.limit, seed=args.seed,
+                               base_model_path=args.base_model_path,
+                               base_config_path=args.base_config_path,
+                               task_dirs=tuple(args.task_dir), device=device,
+                               model_kwargs={"layers": args.model_layers})
+        print(json.dumps({"best": res["best"], "evaluations": res["evaluations"]}, indent=2))
+        return 0
     print(json.dumps({"best": res["best"], "evaluations": res["evaluations"]}, indent=2))
     return 0
 

@@ -348,6 +348,12 @@ def test_reference_module_paths_alias_this_package():
         "from kvserve_v1.offline_search.duo_config.duo_config import duo_attention_on_the_fly as D",
         "from kvserve_hpdps_b200.offline.duo_scores import duo_scores_on_the_fly",
         "assert D is duo_scores_on_the_fly",
+        "from kvserve_v1.offline_search.evaluation.param_search.acc_evaluator import "
+        "AccuracyEvaluator as AE",
+        "from kvserve_v1.offline_search.evaluation.param_search.cr_evaluator import "
+        "CompressionEvaluator as CE",
+        "from kvserve_hpdps_b200.offline import param_search as PS",
+        "assert AE is PS.AccuracyEvaluator and CE is PS.CompressionEvaluator",
         "print('ALIASES', len(_ALIASES))",
     ])
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([compat.path(), root]))

@@ -76,3 +76,22 @@ def test_cli_collect(tmp_path, capsys):
     assert AJ.main(["collect", str(res)]) == 0
     out = capsys.readouterr().out.splitlines()
     assert out[0].startswith("model,task,method") and ",75.0," in out[2]
+
+
+def test_task_file_jobs_score_with_each_method(model, tmp_path):
+    """A task file as a job's task: accuracy = the task's score x100."""
+    from kvserve_hpdps_b200.offline.lm_harness import CacheMethodModel
+    cm = CacheMethodModel(model, "default")
+    docs = []
+    for i in range(3):
+        ctx = torch.randint(0, 256, (40,), generator=torch.Generator().manual_seed(i)).tolist()
+        docs.append({"context_ids": ctx,
+                     "answers_ids": [cm.generate(torch.tensor([ctx]), 4)[0].tolist()]})
+    task = tmp_path / "qa.json"
+    task.write_text(json.dumps({"kind": "generate", "max_new_tokens": 4, "docs": docs}))
+    jobs = AJ.expand_jobs(["default", "custom"], [str(task)])
+    rows = AJ.run_jobs(model, "tiny", jobs, str(tmp_path / "acc.jsonl"),
+                       torch.full((2, 2), 0.5), limit=2)
+    assert [r["backend"] for r in rows] == ["task-file", "task-file"]
+    assert rows[0]["accuracy"] == 100.0 and rows[0]["docs"] == 2
+    assert 0.0 <= rows[1]["accuracy"] <= 100.0 and rows[1]["compression_ratio"] > 1.0
