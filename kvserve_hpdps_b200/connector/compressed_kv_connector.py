@@ -50,6 +50,7 @@ from __future__ import annotations
 
 import os
 import re
+import threading
 import time
 from collections import defaultdict, deque
 from contextlib import nullcontext
@@ -61,6 +62,7 @@ import torch
 from kvserve_hpdps_b200.compression.manager import (add_sentinel, is_compressed_layer_names,
                                                     strip_sentinel)
 from kvserve_hpdps_b200.compression.wire import CompressedWire, build_wire, restore_from_wire
+from kvserve_hpdps_b200.connector.metrics import KVServeConnectorStats, KVServePromMetrics
 from kvserve_hpdps_b200.utils.kv_utils import (extract_kv_from_layer_by_blocks,
                                                inject_kv_into_layer_by_blocks, make_slot_mapping)
 from kvserve_hpdps_b200.utils.logger import get_logger
@@ -223,6 +225,15 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._rid2tid: dict[str, str] = {}
         self._pending_send_rids: set[str] = set()
         self._err_monitor = None
+        # consumer: blocks whose load failed this step, handed to vLLM's
+        # kv_load_failure_policy by get_block_ids_with_load_errors()
+        self._load_errors: set[int] = set()
+        # interval statistics for vLLM's connector-stats logging / Prometheus;
+        # message key -> (original bytes, compress ms) of compressed messages
+        # not yet reported sent by the transport
+        self._xfer_stats = KVServeConnectorStats()
+        self._sent_orig: dict[str, deque] = defaultdict(deque)
+        self._sent_lock = threading.Lock()
         # controller feedback: transfer id -> (request id, compress ms, time) until the
         # transport reports the message sent; completions queued by its thread
         self._ctl_wait: dict[str, tuple[str, float, float]] = {}
@@ -293,6 +304,13 @@ class CompressedKVConnector(KVConnectorBase_V1):
         # transport thread: only queue controller updates (the engine thread
         # applies them); compression statistics wait for the exact size on
         # the wire (a coded stream's length is known only on the device)
+        with self._sent_lock:
+            q = self._sent_orig.get(request_id)
+            orig, cms = q.popleft() if q else (None, 0.0)
+            if q is not None and not q:
+                self._sent_orig.pop(request_id, None)
+        if nbytes:
+            self._xfer_stats.record_sent(orig if orig else nbytes, nbytes, cms, latency_ms)
         for t in transfer_ids:
             if t in self._ctl_wait:
                 self._ctl_done.append((t, latency_ms))
@@ -301,6 +319,41 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 rid, orig, wire, ms, span = stat
                 write_compression_stats(rid, t, orig, nbytes if nbytes else wire,
                                         compress_ms=ms, prefill_span_ms=span)
+
+    def _kv_bytes(self, num_layers: int, tokens: int, cache: torch.Tensor) -> int:
+        """Bytes of ``tokens`` tokens of K and V over ``num_layers`` layers."""
+        return (num_layers * 2 * tokens * self._num_kv_heads * self._head_size
+                * cache.element_size())
+
+    def _expect_sent(self, key: str, original_bytes: Optional[int] = None) -> Optional[list]:
+        """Before a message goes to the transport under ``key``: queue its
+        statistics entry ``[original bytes (None: raw KV), compress ms]``,
+        completed when the transport reports the message sent (exact wire
+        bytes, transfer time; a transport reports the messages of one key in
+        send order).  Returns the entry, or None without a listener."""
+        if not self._listening:
+            return None
+        entry = [original_bytes, 0.0]
+        with self._sent_lock:
+            self._sent_orig[key].append(entry)
+        return entry
+
+    def _settle_sent(self, key: str, entry: Optional[list], sent: bool,
+                     original_bytes: Optional[int] = None, wire_bytes: int = 0,
+                     compress_ms: float = 0.0) -> None:
+        """After the send call: a message that did not go out takes its entry
+        back; without a listener a sent compressed message is recorded now."""
+        if entry is not None:
+            entry[1] = compress_ms
+            if not sent:
+                with self._sent_lock:
+                    q = self._sent_orig.get(key)
+                    if q and q[-1] is entry:
+                        q.pop()
+                    if q is not None and not q:
+                        self._sent_orig.pop(key, None)
+        elif sent and original_bytes:
+            self._xfer_stats.record_sent(original_bytes, wire_bytes, compress_ms, 0.0)
 
     def _apply_controller_feedback(self) -> None:
         comp = self._compressor
@@ -358,6 +411,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             with torch.cuda.stream(self._side_stream):
                 self._side_stream.wait_event(ready)
                 for rm in meta.requests:
+                    self._expect_sent(rm.transfer_id)
                     if hasattr(self._transport, "send_paged"):
                         self._transport.send_paged(rm.transfer_id, [layer_name], [kv_layer],
                                                    rm.block_ids)
@@ -377,10 +431,18 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     self._side_stream.wait_event(ready)
                     # one grouped message for the layer; on the NVLink ring the
                     # producer kernels store it straight into the consumer's memory
-                    info = comp.send_paged_requests(self._transport, tids[0],
-                                                    add_sentinel([layer_name]), [kv_layer],
-                                                    [layer_index(layer_name)], requests,
-                                                    member_tids=tids)
+                    t0 = time.monotonic()
+                    orig = sum(self._kv_bytes(1, n, kv_layer) for _, n in requests)
+                    entry, info = self._expect_sent(tids[0], orig), None
+                    try:
+                        info = comp.send_paged_requests(self._transport, tids[0],
+                                                        add_sentinel([layer_name]), [kv_layer],
+                                                        [layer_index(layer_name)], requests,
+                                                        member_tids=tids)
+                    finally:
+                        self._settle_sent(tids[0], entry, bool(info and info["wire_nbytes"]),
+                                          orig, info["wire_nbytes"] if info else 0,
+                                          (time.monotonic() - t0) * 1e3)
             except Exception:  # noqa: BLE001
                 # as in the off mode: a compression failure sends this layer's raw
                 # KV, one message per request (the consumer still counts one
@@ -391,6 +453,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 with torch.cuda.stream(self._side_stream):
                     for rm in meta.requests:
                         raw = extract_kv_from_layer_by_blocks(kv_layer, rm.block_ids).unsqueeze(0)
+                        self._expect_sent(rm.transfer_id)
                         self._transport.send(rm.transfer_id, [layer_name], raw)
             for t in tids:
                 self._expected_msgs[t] = self._num_layers
@@ -427,6 +490,8 @@ class CompressedKVConnector(KVConnectorBase_V1):
             layers = [self._layer_refs[n] for n in names]
             use = comp  # this request's compressor (None: raw KV)
             if use is not None and use.supports_paged() and layers[0].is_cuda:
+                orig = self._kv_bytes(len(layers), len(rm.token_ids), layers[0])
+                entry, info = self._expect_sent(tid, orig), None
                 try:
                     with nvtx("kvs.compress_send"):
                         info = use.send_paged_requests(
@@ -437,6 +502,9 @@ class CompressedKVConnector(KVConnectorBase_V1):
                     # as the reference does: a compression failure sends the raw KV
                     logger.exception("compression of %s failed; sending raw KV", rid)
                     info = None
+                self._settle_sent(tid, entry, bool(info and info["wire_nbytes"]), orig,
+                                  info["wire_nbytes"] if info else 0,
+                                  (time.monotonic() - t0) * 1e3)
                 if info is not None:
                     self._expected_msgs[tid] = 1
                     compress_ms = (time.monotonic() - t0) * 1e3
@@ -456,6 +524,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             if use is None and hasattr(self._transport, "send_paged") and layers[0].is_cuda:
                 # raw KV: one gather launch from the paged caches into the peer ring
                 with nvtx("kvs.send_raw"):
+                    self._expect_sent(tid)
                     self._transport.send_paged(tid, names, layers, rm.block_ids)
                 self._expected_msgs[tid] = 1
                 continue
@@ -470,13 +539,17 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 compress_ms = (time.monotonic() - t0) * 1e3
                 if self._listening:  # completed by _apply_controller_feedback
                     self._ctl_wait[tid] = (rid, compress_ms, time.monotonic())
+                orig = stacked.numel() * stacked.element_size()
+                entry = self._expect_sent(tid, orig)
                 nbytes = self._send_compressed(tid, names, cd)
+                self._settle_sent(tid, entry, True, orig, nbytes, (time.monotonic() - t0) * 1e3)
                 if not self._listening:
                     use.update_controller(rid, (time.monotonic() - t0) * 1e3)
                 write_compression_stats(rid, tid, stacked.numel() * stacked.element_size(), nbytes,
                                         compress_ms=(time.monotonic() - t0) * 1e3,
                                         prefill_span_ms=span)
             else:
+                self._expect_sent(tid)
                 self._transport.send(tid, names, stacked)
             self._expected_msgs[tid] = 1
         self._finish_step(meta)
@@ -493,6 +566,13 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._layer_refs.clear()
         if not self._async_send and self._transport is not None:
             self._transport.wait_for_sent()
+            self._drop_sent_entries(rm.transfer_id for rm in meta.requests)
+
+    def _drop_sent_entries(self, tids) -> None:
+        """Statistics entries of messages that never left (refused, dropped)."""
+        with self._sent_lock:
+            for t in tids:
+                self._sent_orig.pop(t, None)
 
     def get_finished(self, finished_req_ids: set[str]):
         if self.is_producer:
@@ -509,10 +589,14 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 failed(tid) if failed is not None else 0)
             if tid is None or out >= self._expected_msgs.get(tid, 1):
                 done.add(rid)
+                n_failed = failed(tid) if (failed is not None and tid is not None) else 0
+                if n_failed:
+                    self._xfer_stats.record_failed_send(n_failed)
         self._pending_send_rids -= done
         for rid in done:
             tid = self._rid2tid.pop(rid, None)
             if tid is not None:
+                self._drop_sent_entries([tid])
                 self._transport.clear_sent(tid)
                 self._expected_msgs.pop(tid, None)
         return (done or None), None
@@ -564,10 +648,12 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 if all(self._got[t] >= need for t in self._step_reqs):
                     break
                 if time.monotonic() > self._deadline:
-                    for t, rm in self._step_reqs.items():
-                        if self._got[t] < need:
-                            logger.warning("timeout loading KV of %s (transfer %s): %d/%d "
-                                           "messages", rm.request_id, t, self._got[t], need)
+                    late = [t for t in self._step_reqs if self._got[t] < need]
+                    for t in late:
+                        logger.warning("timeout loading KV of %s (transfer %s): %d/%d "
+                                       "messages", self._step_reqs[t].request_id, t,
+                                       self._got[t], need)
+                    self._fail_load(late)
                     break
                 self._wait_header()
                 self._drain()
@@ -614,6 +700,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
                                len(late), ", ".join(late[:4]))
                 for t in late:
                     pend[t].discard(layer_name)
+                self._fail_load(late)
                 break
             self._wait_header()
         ev = self._layer_events.get(layer_name)
@@ -675,6 +762,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         plain = strip_sentinel(names) if is_compressed_layer_names(names) else list(names)
         if payload is None:
             logger.error("transport reported a failed transfer for %s", ", ".join(now))
+            self._fail_load(now)
             self._mark(rec, now, plain)
             return
         tr = self._transport
@@ -687,12 +775,14 @@ class CompressedKVConnector(KVConnectorBase_V1):
             rec["prepared"] = True
             with nvtx("kvs.inject"):
                 self._inject_record(rec, now, plain, payload)
-            if is_compressed_layer_names(names):
-                for t in now:
-                    write_decode_stats(self._step_reqs[t].request_id, t,
-                                       (time.monotonic() - t0) * 1e3)
+            ms = (time.monotonic() - t0) * 1e3
+            for t in now:
+                self._xfer_stats.record_decode(ms)
+                if is_compressed_layer_names(names):
+                    write_decode_stats(self._step_reqs[t].request_id, t, ms)
         except Exception as e:  # noqa: BLE001
             logger.error("decode of %s failed: %s", ", ".join(now), e)
+            self._fail_load(now)
         finally:
             self._mark(rec, now, plain)
             if rec["decoded"] >= rec["members"]:
@@ -702,6 +792,43 @@ class CompressedKVConnector(KVConnectorBase_V1):
             else:
                 rec.setdefault("t", time.monotonic())
                 self._partial[id(rec)] = rec
+
+    def _fail_load(self, tids) -> None:
+        """The KV of these requests of the step did not (fully) arrive: their
+        blocks are reported to vLLM, which recomputes them or fails the
+        request (``kv_load_failure_policy``), instead of decoding with stale
+        blocks."""
+        for t in tids:
+            rm = self._step_reqs.get(t)
+            if rm is not None:
+                self._load_errors.update(int(b) for b in rm.block_ids)
+                self._xfer_stats.record_failed_load()
+
+    def get_kv_connector_stats(self) -> Optional[KVServeConnectorStats]:
+        """This worker's transfer statistics since the last call (None when
+        there are none); vLLM aggregates them over workers and logs them."""
+        if self._xfer_stats.is_empty():
+            return None
+        return self._xfer_stats.clone_and_reset()
+
+    @classmethod
+    def build_kv_connector_stats(cls, data: Optional[dict] = None) -> KVServeConnectorStats:
+        return KVServeConnectorStats(data={k: list(v) for k, v in (data or {}).items()})
+
+    @classmethod
+    def build_prom_metrics(cls, vllm_config, metric_types, labelnames, per_engine_labelvalues):
+        return KVServePromMetrics(vllm_config, metric_types, labelnames, per_engine_labelvalues)
+
+    def get_block_ids_with_load_errors(self) -> set[int]:
+        """Blocks of the requests whose load failed in this step (a failed
+        payload, a decode error, or the step's load timeout).  Failures the
+        device reports later (a flag timeout or checksum mismatch inside a
+        kernel, seen by the error monitor) are logged only: the forward has
+        already run by then.  The reference decodes with whatever the blocks
+        hold in every case (kvserve_v1/connector/compressed_kv_connector.py:
+        423-441)."""
+        out, self._load_errors = self._load_errors, set()
+        return out
 
     def _mark(self, rec: dict, members: list[str], names: list[str]) -> None:
         rec["decoded"].update(members)

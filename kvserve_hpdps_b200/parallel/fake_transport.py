@@ -17,7 +17,11 @@ from typing import Any, Optional
 
 import torch
 
+from kvserve_hpdps_b200.parallel.control import notify_sent
 from kvserve_hpdps_b200.parallel.nccl_transport import FAILED_LAYER_NAMES, FAILED_PAYLOAD
+from kvserve_hpdps_b200.utils.logger import get_logger
+
+logger = get_logger(__name__)
 
 
 class FakeTransportPair:
@@ -71,18 +75,19 @@ class _FakeEnd:
 
     def send(self, request_id: str, layer_names: list[str], stacked_kv: torch.Tensor) -> None:
         ok = self._deliver(request_id, (list(layer_names), stacked_kv.clone()))
-        self._count_sent(None, request_id, ok)
+        self._count_sent(None, request_id, ok, stacked_kv.numel() * stacked_kv.element_size())
 
     def _count_sent(self, member_tids: Optional[list[str]], request_id: str,
-                    ok: bool = True) -> None:
-        """A message without member ids counts for its request id."""
+                    ok: bool = True, nbytes: int = 0) -> None:
+        """A message without member ids counts for its request id; listeners
+        hear of accepted messages with their size in bytes."""
         table = self.pair.sent if ok else self.pair.failed
         with self.pair.lock:
             for t in (member_tids or [request_id]):
                 table[t] += 1
         if ok:
-            for fn in list(self.pair.listeners):
-                fn(request_id, list(member_tids or [request_id]), self.pair.delay_s * 1e3)
+            notify_sent(self.pair.listeners, request_id, list(member_tids or [request_id]),
+                        self.pair.delay_s * 1e3, int(nbytes), logger)
 
     def send_bundle(self, request_id, layer_names, meta, body_chunks, aux_tensors,
                     member_tids: Optional[list[str]] = None) -> None:
@@ -90,7 +95,9 @@ class _FakeEnd:
                    "body_chunks": [t.clone() for t in body_chunks],
                    "aux_tensors": [t.clone() for t in aux_tensors]}
         ok = self._deliver(request_id, (list(layer_names), payload))
-        self._count_sent(member_tids, request_id, ok)
+        self._count_sent(member_tids, request_id, ok,
+                         sum(t.numel() * t.element_size() for t in body_chunks)
+                         + sum(t.numel() * t.element_size() for t in aux_tensors))
 
     def sent_layers(self, tid: str) -> int:
         with self.pair.lock:

@@ -89,6 +89,47 @@ def test_generic_compressed_handoff():
         a = pc[name][:, [5, 1, 7]].float().flatten()
         b = cc[name][:, [2, 6, 0]].float().flatten()
         assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.97
+    # vLLM's connector-stats hooks: one message out, one request decoded
+    ps, cs = p.get_kv_connector_stats(), c.get_kv_connector_stats()
+    red = ps.reduce()
+    assert red["Num messages sent"] == 1 and red["Compression ratio"] > 2.0
+    assert ps.data["original_bytes"] == [L * 2 * 3 * BS * H * D * 2]
+    assert cs.reduce()["Num decoded"] == 1 and cs.reduce()["Num failed loads"] == 0
+    assert p.get_kv_connector_stats() is None  # the interval starts over
+
+
+def test_connector_stats_aggregate_pickle_and_prometheus():
+    import pickle
+
+    from prometheus_client import CollectorRegistry, Counter, Gauge, Histogram
+
+    from kvserve_hpdps_b200.connector.metrics import KVServeConnectorStats
+    a = KVServeConnectorStats()
+    a.record_sent(1000, 250, 1.5, 2.0)
+    a.record_decode(0.5)
+    b = CompressedKVConnector.build_kv_connector_stats(pickle.loads(pickle.dumps(a)).data)
+    b.record_sent(3000, 250, 0.5, 6.0)
+    b.record_failed_load(2)
+    agg = a.clone_and_reset().aggregate(b)
+    assert a.is_empty() and not agg.is_empty()
+    r = agg.reduce()
+    assert r["Num messages sent"] == 3 and r["Compression ratio"] == round(5000 / 750, 3)
+    assert r["Avg transfer time (ms)"] == round(10 / 3, 3) and r["Num failed loads"] == 2
+    reg = CollectorRegistry()
+
+    def bound(cls):
+        return type(cls.__name__, (cls,), {"__init__": lambda self, *x, **k: cls.__init__(
+            self, *x, registry=reg, **k)})
+    types_ = {Gauge: bound(Gauge), Counter: bound(Counter), Histogram: bound(Histogram)}
+    prom = CompressedKVConnector.build_prom_metrics(SimpleNamespace(kv_transfer_config=None),
+                                                    types_, ["model", "engine"],
+                                                    {0: ["m", "0"]})
+    prom.observe(agg.data, 0)
+    labels = {"model": "m", "engine": "0"}
+    assert reg.get_sample_value("vllm:kvserve_wire_bytes_total", labels) == 750
+    assert reg.get_sample_value("vllm:kvserve_original_bytes_total", labels) == 5000
+    assert reg.get_sample_value("vllm:kvserve_transfer_seconds_count", labels) == 3
+    assert reg.get_sample_value("vllm:kvserve_failed_loads_total", labels) == 2
 
 
 def test_async_send_reports_raw_requests_finished():
@@ -109,9 +150,16 @@ def test_refused_and_dropped_messages_do_not_hang(monkeypatch):
     pair.refuse_next = 1
     pc, cc = handoff(p, c)  # FAILED sentinel: logged, blocks untouched
     assert not torch.equal(cc[next(iter(cc))][:, [2, 6, 0]], pc[next(iter(pc))][:, [5, 1, 7]])
+    # the blocks go to vLLM's load-failure policy, once
+    assert c.get_block_ids_with_load_errors() == {2, 6, 0}
+    assert c.get_block_ids_with_load_errors() == set()
+    assert c.get_kv_connector_stats().reduce()["Num failed loads"] == 1
     pair.drop_next = 1
     p2, c2, _ = p, c, pair
-    handoff(p2, c2)  # nothing arrives: returns after the timeout
+    handoff(p2, c2, dst_blocks=(3, 4, 5))  # nothing arrives: returns after the timeout
+    assert c.get_block_ids_with_load_errors() == {3, 4, 5}
+    handoff(p, c)  # a good handoff reports nothing
+    assert c.get_block_ids_with_load_errors() == set()
 
 
 def test_scheduler_side_bookkeeping():
@@ -206,6 +254,7 @@ def test_load_timeout_bounds_the_whole_step(monkeypatch):
     t0 = time.monotonic()
     c.start_load_kv(None)
     assert 0.35 < time.monotonic() - t0 < 1.0
+    assert c.get_block_ids_with_load_errors() == {0, 1, 2}
 
 
 def test_async_send_frees_blocks_of_refused_requests():
