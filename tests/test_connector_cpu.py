@@ -383,3 +383,53 @@ def test_overlap_modes_are_normalized(monkeypatch):
     monkeypatch.setenv("KVSERVE_OVERLAP_MODE", "tq")
     p, _, _ = make_pair(None)
     assert p._overlap_mode == "off"
+
+
+def test_paged_send_statistics_with_a_stand_in_compressor(monkeypatch):
+    """The producer's paged compressed branch (GPU caches in production):
+    the statistics entry is queued before the send, completed by the
+    transport's report with the bytes that crossed, and taken back when the
+    compressor sends nothing (its message then goes out raw)."""
+    p, c, pair = make_pair(None)
+
+    class CudaLike(torch.Tensor):  # a CPU tensor the branch takes for a CUDA cache
+        @property
+        def is_cuda(self):
+            return True
+
+    class Comp:
+        controller_mode = False
+        send = True
+
+        def supports_paged(self):
+            return True
+
+        def send_paged_requests(self, tr, tid, names, layers, ids, reqs, member_tids=None):
+            if not self.send:
+                return None
+            body = torch.zeros(1000, dtype=torch.uint8)
+            tr.send_bundle(tid, names, {"m": 1}, [body], [], member_tids=member_tids)
+            return {"original_size": 1, "wire_nbytes": 1000}
+
+    comp = Comp()
+    p._get_compressor = lambda: comp
+    pc = {n: t.as_subclass(CudaLike) for n, t in caches(8, 1).items()}
+    p.bind_connector_metadata(meta_for("r1", "tid-p", 40, [5, 1, 7]))
+    p._layer_refs = dict(pc)
+    p.wait_for_save()
+    st = p.get_kv_connector_stats()
+    assert st.data["original_bytes"] == [L * 2 * 40 * H * D * 2]
+    assert st.data["wire_bytes"] == [1000] and not p._sent_orig
+    # nothing sent by the compressor: the entry is taken back and the raw
+    # message is recorded as raw
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "extract_kv_from_layer_by_blocks",
+                        lambda layer, ids: layer.as_subclass(torch.Tensor)[:, ids])
+    comp.send = False
+    p.bind_connector_metadata(meta_for("r2", "tid-q", 40, [5, 1, 7]))
+    p._layer_refs = dict(pc)
+    p.wait_for_save()
+    st = p.get_kv_connector_stats()
+    raw = L * 2 * 3 * BS * H * D * 2
+    assert st.data["original_bytes"] == [raw] and st.data["wire_bytes"] == [raw]
+    assert not p._sent_orig
