@@ -122,10 +122,14 @@ def validate_spec(spec: Any) -> None:
     for stage in spec.get("pipeline", []) or []:
         if stage not in VALID_PIPELINE_STAGES:
             raise ValueError(f"unknown pipeline stage {stage!r}")
-    if spec.get("quantizer_config"):
+    from kvserve_hpdps_b200.compression.components import custom_impls, resolve_component
+    custom = custom_impls(spec)
+    for kind, impl in custom.items():  # user components: resolvable, their configs their own
+        resolve_component(kind, impl)
+    if spec.get("quantizer_config") and "quantizer" not in custom:
         validate_quantizer_config(spec["quantizer_config"])
     cc = spec.get("codec_config")
-    if cc and "codec" in (spec.get("pipeline") or []):
+    if cc and "codec" in (spec.get("pipeline") or []) and "codec" not in custom:
         # raises with the nvCOMP-name mapping for an unknown coder
         from kvserve_hpdps_b200.compression.codec import resolve_codec
         resolve_codec(cc.get("codec_type"), cc.get("nvcomp_algorithm"))

@@ -57,9 +57,10 @@ def _cfg_key(cfg: dict) -> str:
 
 def use_fused(cfg: dict) -> bool:
     """Whether a custom pipeline config runs on the fused kernels."""
+    from kvserve_hpdps_b200.compression.components import custom_impls
     from kvserve_hpdps_b200.compression.quantizer import fused_compatible
-    if cfg.get("backend") == "generic":
-        return False
+    if cfg.get("backend") == "generic" or custom_impls(cfg):
+        return False  # user components run in the generic pipeline
     if cfg.get("backend") in ("fused", "tilelang"):
         return True
     pipeline = cfg.get("pipeline") or []
@@ -119,9 +120,9 @@ class KVCompressionAdapter:
         self._bandit_state_path = state
         self._service_cfg = dict(spec.get("service_config", {}))
 
-    def _make_config(self, cfg: dict) -> CompressionConfig:
+    def _make_config(self, cfg: dict, custom: frozenset = frozenset()) -> CompressionConfig:
         qc = cfg.get("quantizer_config")
-        if qc is not None:
+        if qc is not None and "quantizer" not in custom:  # a user quantizer gets its own dict
             qc = dict(qc)
             qc["tp_rank"] = self._tp_rank
             qc["tensor_parallel_size"] = self._tp_size
@@ -147,15 +148,17 @@ class KVCompressionAdapter:
             mgr.min_compress_size = int(cfg.get("min_compress_size", 0))
             return mgr, None
         from kvserve_hpdps_b200.compression.codec import KVServeCodec
+        from kvserve_hpdps_b200.compression.components import custom_impls, resolve_component
         from kvserve_hpdps_b200.compression.pipeline_manager import CompressionManager
         from kvserve_hpdps_b200.compression.quantizer import KVServeQuantizer
         from kvserve_hpdps_b200.compression.transformer import KVServeTransformer
         pipeline = cfg.get("pipeline", [])
-        config = self._make_config(cfg)
-        mgr = CompressionManager(config,
-                                 KVServeTransformer if "transformer" in pipeline else None,
-                                 KVServeQuantizer if "quantizer" in pipeline else None,
-                                 KVServeCodec if "codec" in pipeline else None)
+        config = self._make_config(cfg, custom=set(custom_impls(cfg)))
+        built_in = {"transformer": KVServeTransformer, "quantizer": KVServeQuantizer,
+                    "codec": KVServeCodec}
+        classes = [(resolve_component(k, cfg.get(f"{k}_impl")) or built_in[k])
+                   if k in pipeline else None for k in ("transformer", "quantizer", "codec")]
+        mgr = CompressionManager(config, *classes)
         return mgr, config
 
     def _get_cached_manager(self, cfg: dict):
