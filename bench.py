@@ -879,6 +879,48 @@ REF_PIPELINE = ("reference KVHadamardQuantOp.compress_v3 / decompress_v3 per lay
                 "stand-in (baseline/standin); its extract/inject block utilities")
 
 
+def _ref_e2e(args, world, device, step, s0: int, read_cache, read_blocks, h2d_per_step: int,
+             pairs: int, finish=None) -> dict:
+    """End to end through the reference's public API: the same step as the
+    device-timed loop (its extract/inject utilities build their block-index
+    tensors on the device from host lists every call; those copies are the
+    step's host->device bytes), then the step's result read back: 4 bytes of
+    the cache it wrote (a pinned, synchronous device->host copy, as the
+    reference reads its results).  Every rank runs the same steps and reaches
+    the same collectives whether or not its loop failed."""
+    steps = max(2, min(args.steps, 10))
+    host = torch.empty(2, dtype=torch.bfloat16, pin_memory=True)
+    ms, err = -1.0, None
+    try:
+        barrier(world)
+        torch.cuda.synchronize(device)
+        ev0, ev1 = _events()
+        ev0.record()
+        s = s0
+        for _ in range(steps):
+            step(s)
+            host.copy_(read_cache[:, read_blocks[0]].reshape(-1)[:2])  # the step's result
+            s += 1
+        if finish is not None:
+            finish()
+        ev1.record()
+        torch.cuda.synchronize(device)
+        ms = ev0.elapsed_time(ev1)
+    except Exception as e:  # noqa: BLE001
+        err = f"{type(e).__name__}: {e}"
+    worst = allreduce_max(ms, world)
+    failed = allreduce_max(1.0 if err else 0.0, world)
+    if failed:
+        return {"unavailable": err or "failed on another rank"}
+    return {"value": round(worst / (steps * args.requests_per_step), 5), "unit": "ms/request",
+            "h2d_bytes_per_step": int(h2d_per_step), "d2h_bytes_per_step": 4 * (world // pairs),
+            "steps": steps,
+            "path": "the reference's extract_kv_from_layer_by_blocks -> compress_v3 per layer"
+                    + (" -> build_wire -> NcclTransport -> restore_from_wire" if world > 1
+                       else "") + " -> decompress_v3 per layer -> "
+                    "inject_kv_into_layer_by_blocks; each step's result read back"}
+
+
 def run_reference(args, rank, world, local):
     ref_root = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "kvserve_v1")):
@@ -939,6 +981,10 @@ def run_reference(args, rank, world, local):
         n = args.steps * wl.B
         out["stage_ms_per_request"] = {"compress": round(ms_c / n, 5),
                                        "decompress": round((ms - ms_c) / n, 5)}
+    if not args.no_e2e:
+        nb = len(wl.src_req[0][0])
+        out["e2e"] = _ref_e2e(args, world, device, step, s, wl.dst[L - 1], wl.dst_req[-1][0],
+                              wl.B * L * 2 * nb * 8, 1)
     return out
 
 
@@ -1064,7 +1110,13 @@ def run_reference_pairs(args, rank, world, local):
     tot = allreduce_sum(float(sum(sizes[-args.steps * wl.B:])), world)
     n = allreduce_sum(float(len(sizes[-args.steps * wl.B:])), world)
     cr = wl.bf16_bytes_per_request / (tot / n) if n else None
-    return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "pairs": pairs,
+    nb = len((wl.src_req if role == "producer" else wl.dst_req)[0][0])
+    cache, blocks = (wl.src[L - 1], wl.src_req[-1][0]) if role == "producer" else \
+        (wl.dst[L - 1], wl.dst_req[-1][0])
+    e2e = None if args.no_e2e else _ref_e2e(
+        args, world, device, step, s, cache, blocks, 2 * wl.B * L * nb * 8, pairs,
+        finish=wait_sent if role == "producer" else None)
+    return {"ms": ms, "cr": cr, "error": err, "clocks": clocks, "pairs": pairs, "e2e": e2e,
             "pipeline": ("raw: extract_kv_from_layer_by_blocks + stack + NcclTransport.send "
                          "+ inject_kv_into_layer_by_blocks") if raw else
                         REF_PIPELINE + "; its build_wire + NcclTransport.send_bundle",
@@ -1119,6 +1171,8 @@ def build_line(args, res, world):
             line[k] = res[k]
     if args.impl == "reference":
         line["impl"] = "reference"
+        if res.get("e2e"):
+            line["e2e"] = res["e2e"]
     else:
         line["impl"] = "ours"
         line["gpu_launches"] = int(res.get("launches_job", res.get("launches_total",

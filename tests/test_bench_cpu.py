@@ -120,3 +120,42 @@ def test_reference_arm_imports_nothing_of_this_package():
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, out.stderr[-2000:]
     assert out.stdout.strip().splitlines()[-1] == "[]"
+
+
+def test_reference_e2e_loop_and_its_failure_path(monkeypatch):
+    """The reference arm's end-to-end loop: the same steps plus a 4-byte
+    result read per step, value per request; a failing step gives an
+    ``unavailable`` entry instead of breaking the line (CPU stand-ins for
+    events, synchronisation and pinned memory)."""
+    import torch
+
+    class Ev:
+        t = 0.0
+
+        def record(self):
+            Ev.t += 5.0
+            self.at = Ev.t
+
+        def elapsed_time(self, other):
+            return other.at - self.at
+
+    monkeypatch.setattr(bench, "_events", lambda: (Ev(), Ev()))
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
+    real_empty = torch.empty
+    monkeypatch.setattr(torch, "empty", lambda *a, pin_memory=False, **k: real_empty(*a, **k))
+    args = bench.parse_args(["--impl", "reference", "--steps", "3", "--requests-per-step", "2"])
+    cache = torch.arange(2 * 4 * 16 * 2 * 8, dtype=torch.float32).to(torch.bfloat16).view(
+        2, 4, 16, 2, 8)
+    seen = []
+    e2e = bench._ref_e2e(args, 1, "cpu", seen.append, 7, cache, [3, 1], 1234, 1)
+    assert seen == [7, 8, 9] and e2e["steps"] == 3
+    assert e2e["value"] == round(5.0 / (3 * 2), 5) and e2e["unit"] == "ms/request"
+    assert e2e["h2d_bytes_per_step"] == 1234 and e2e["d2h_bytes_per_step"] == 4
+
+    def bad(s):
+        raise RuntimeError("boom")
+    out = bench._ref_e2e(args, 1, "cpu", bad, 0, cache, [0], 1, 1)
+    assert out == {"unavailable": "RuntimeError: boom"}
+    line = bench.build_line(args, {"ms": 30.0, "cr": 2.0, "pairs": 1, "pipeline": "p",
+                                   "transport": "local", "e2e": e2e}, 1)
+    assert line["impl"] == "reference" and line["e2e"] == e2e
