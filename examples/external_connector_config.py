@@ -20,9 +20,13 @@ ROLES = {"kv_producer": 0, "kv_consumer": 1}
 
 def make_kv_transfer_config(*, role: str, decode_host: str = "127.0.0.1", base_port: int = 25010,
                             compression: Any = "default", transport: str = "auto",
-                            overlap: Optional[str] = None):
+                            overlap: Optional[str] = None,
+                            load_failure_policy: str = "recompute"):
     """KVTransferConfig for one side.  ``transport``: auto (NVLink P2P ring
-    when the two GPUs can map each other, else NCCL), p2p or nccl."""
+    when the two GPUs can map each other, else NCCL), p2p or nccl.
+    ``load_failure_policy``: what the decode engine does with a request whose
+    KV did not arrive intact (the connector reports its blocks): recompute
+    them from the prompt, or fail the request."""
     from vllm.config import KVTransferConfig
     if role not in ROLES:
         raise ValueError(f"role must be one of {sorted(ROLES)}, got {role!r}")
@@ -32,7 +36,8 @@ def make_kv_transfer_config(*, role: str, decode_host: str = "127.0.0.1", base_p
     return KVTransferConfig(kv_connector=CONNECTOR_NAME, kv_connector_module_path=CONNECTOR_MODULE,
                             kv_role=role, kv_rank=ROLES[role], kv_parallel_size=2,
                             kv_ip=decode_host, kv_port=base_port,
-                            kv_connector_extra_config=extra)
+                            kv_connector_extra_config=extra,
+                            kv_load_failure_policy=load_failure_policy)
 
 
 def make_sampling_params(*, transfer_id: str, max_tokens: int = 32, temperature: float = 0.0):

@@ -146,7 +146,8 @@ def engine(role: str, gpus: str, args, q_in, q_out) -> None:
                                kv_role="kv_producer" if role == "p" else "kv_consumer",
                                kv_rank=0 if role == "p" else 1, kv_parallel_size=2,
                                kv_ip=args.kv_ip, kv_port=args.port,
-                               kv_connector_extra_config=extra)
+                               kv_connector_extra_config=extra,
+                               kv_load_failure_policy=args.load_failure_policy)
         llm = LLM(model=args.model_dir, dtype="bfloat16", load_format="dummy",
                   skip_tokenizer_init=True,
                   max_model_len=max(args.prompt_len, args.prompt_len_max) + args.max_tokens + 64,
@@ -212,6 +213,9 @@ def main(argv=None) -> int:
     ap.add_argument("--gpus", default="0,1",
                     help="producer GPUs then consumer GPUs (tp of each; one role: its tp GPUs)")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel size of each engine")
+    ap.add_argument("--load-failure-policy", default="fail", choices=["fail", "recompute"],
+                    help="decode engine's answer to KV that did not arrive intact (fail: the "
+                         "request ends with an error, so a measured run shows every failure)")
     ap.add_argument("--role", choices=["both", "producer", "consumer"], default="both",
                     help="producer / consumer: run one engine here and pair with --kv-ip "
                          "(the consumer's host) across nodes")
