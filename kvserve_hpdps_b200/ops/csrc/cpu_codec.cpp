@@ -35,12 +35,38 @@ inline uint32_t sym_at(const uint8_t* src, uint32_t n_sym, uint32_t idx) {
   return idx < n_sym ? src[idx] : 0u;
 }
 
+// One coding step of the 32 lanes of stream k at symbol offset `base` of the
+// super-step (lane l codes symbol base + l * kSub): the words that leave the
+// lanes go out in reverse lane order (the device writes a step's words in lane
+// order just below the previous ones; emitted in reverse, a step's block is
+// reversed too), then every lane's state takes its symbol.
+template <bool kTail>
+inline void encode_step(const uint8_t* src, uint32_t n_sym, uint32_t base, const EncSym* enc,
+                        uint32_t* x, uint16_t* out, uint32_t& n_out) {
+  uint32_t sym[kLanes];
+  for (int l = 0; l < kLanes; ++l)
+    sym[l] = kTail ? sym_at(src, n_sym, base + l * kSub) : src[base + l * kSub];
+  for (int l = kLanes - 1; l >= 0; --l) {
+    if (x[l] >= enc[sym[l]].x_max) {
+      out[n_out++] = static_cast<uint16_t>(x[l] & 0xFFFFu);
+      x[l] >>= 16;
+    }
+  }
+  for (int l = 0; l < kLanes; ++l) {
+    const EncSym& e = enc[sym[l]];
+    const uint32_t q = umulhi32(x[l], e.rcp) >> (e.cmpl_shift >> 16);
+    x[l] = x[l] + e.bias + q * (e.cmpl_shift & 0xFFFFu);
+  }
+}
+
 // Encode one chunk; returns its record (the bytes k_rans_copy would place).
 std::vector<uint8_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t cs) {
   (void)cs;
   const uint32_t n_ss = (n_sym + kSuper - 1) / kSuper;
+  // symbols past n_sym up to the last super-step are coded as zeros
   uint64_t hist[256] = {0};
-  for (uint32_t i = 0; i < n_ss * kSuper; ++i) hist[sym_at(src, n_sym, i)]++;
+  for (uint32_t i = 0; i < n_sym; ++i) hist[src[i]]++;
+  hist[0] += static_cast<uint64_t>(n_ss) * kSuper - n_sym;
   int top = -1;
   for (int s = 0; s < 256; ++s)
     if (hist[s]) top = s;
@@ -55,37 +81,31 @@ std::vector<uint8_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t c
   }
   const uint64_t prefix = coded_prefix_bytes(A);
   const uint64_t raw_len = raw_record_bytes(n_sym);
-  // words of each stream, in emission order (reversed at the end)
-  std::vector<uint16_t> emitted[kStreams];
+  // words of each stream in emission order (reversed at the end); a symbol
+  // sends at most one word out of its state, so half a chunk bounds a stream
+  thread_local std::vector<uint16_t> emitted[kStreams];
+  const uint32_t cap = n_ss * kSuper / kStreams;
+  uint32_t n_emit[kStreams] = {0, 0};
+  for (int k = 0; k < kStreams; ++k)
+    if (emitted[k].size() < cap) emitted[k].resize(cap);
   uint32_t x[kStreams][kLanes];
   for (int k = 0; k < kStreams; ++k)
     for (int l = 0; l < kLanes; ++l) x[k][l] = kStateLow;
   bool overflow = false;
   for (int ss = static_cast<int>(n_ss) - 1; ss >= 0; --ss) {
-    const uint64_t used = emitted[0].size() + emitted[1].size();
+    const uint64_t used = n_emit[0] + n_emit[1];
     if (prefix + 2 * (used + kSuper + 16) >= raw_len) {
       overflow = true;
       break;
     }
+    const uint32_t base = static_cast<uint32_t>(ss) * kSuper;
+    const bool tail = base + kSuper > n_sym;
     for (int m = kSub - 1; m >= 0; --m) {
       const int k = m & 1;
-      uint32_t sym[kLanes];
-      bool emit[kLanes];
-      std::vector<uint16_t> step;
-      for (int l = 0; l < kLanes; ++l) {
-        sym[l] = sym_at(src, n_sym, static_cast<uint32_t>(ss) * kSuper + l * kSub + m);
-        emit[l] = x[k][l] >= enc[sym[l]].x_max;
-      }
-      // the device writes a step's words in lane order just below the
-      // previous ones; emitted in reverse, a step's block is reversed too
-      for (int l = kLanes - 1; l >= 0; --l)
-        if (emit[l]) emitted[k].push_back(static_cast<uint16_t>(x[k][l] & 0xFFFFu));
-      for (int l = 0; l < kLanes; ++l) {
-        if (emit[l]) x[k][l] >>= 16;
-        const EncSym& e = enc[sym[l]];
-        const uint32_t q = umulhi32(x[k][l], e.rcp) >> (e.cmpl_shift >> 16);
-        x[k][l] = x[k][l] + e.bias + q * (e.cmpl_shift & 0xFFFFu);
-      }
+      if (tail)
+        encode_step<true>(src, n_sym, base + m, enc, x[k], emitted[k].data(), n_emit[k]);
+      else
+        encode_step<false>(src, n_sym, base + m, enc, x[k], emitted[k].data(), n_emit[k]);
     }
   }
   if (overflow) {
@@ -97,7 +117,7 @@ std::vector<uint8_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t c
   }
   uint32_t nw[kStreams], np[kStreams];
   for (int k = 0; k < kStreams; ++k) {
-    nw[k] = static_cast<uint32_t>(emitted[k].size());
+    nw[k] = n_emit[k];
     np[k] = (8 - (nw[k] & 7)) & 7;
   }
   std::vector<uint8_t> rec(prefix + 2ull * (np[0] + nw[0] + np[1] + nw[1]), 0);
@@ -110,7 +130,8 @@ std::vector<uint8_t> encode_chunk(const uint8_t* src, uint32_t n_sym, uint32_t c
   uint16_t* w = reinterpret_cast<uint16_t*>(rec.data() + prefix);
   for (int k = 0; k < kStreams; ++k) {
     w += np[k];  // leading zero padding
-    for (uint32_t i = 0; i < nw[k]; ++i) w[i] = emitted[k][nw[k] - 1 - i];
+    const uint16_t* e = emitted[k].data();
+    for (uint32_t i = 0; i < nw[k]; ++i) w[i] = e[nw[k] - 1 - i];
     w += nw[k];
   }
   return rec;
@@ -189,22 +210,43 @@ int decode_chunk(const uint8_t* stream, uint64_t stream_bytes, const uint64_t* d
   if (cum != kProbScale) return -6;
   uint64_t rptr[kStreams] = {ch.n_pad[0], ch.n_pad[1]};
   const uint32_t n_ss = (ch.n_sym + kSuper - 1) / kSuper;
+  const uint8_t* lt = lut.data();
   for (uint32_t ss = 0; ss < n_ss; ++ss) {
+    const uint32_t base = ss * kSuper;
+    // the last super-step of a chunk decodes into a scratch block: its
+    // symbols past n_sym are coded zeros that must not be stored
+    uint8_t tail_buf[kSuper];
+    const bool tail = base + kSuper > ch.n_sym;
+    uint8_t* blk = tail ? tail_buf : dst + base;
     for (int m = 0; m < kSub; ++m) {
       const int k = m & 1;
-      for (int l = 0; l < kLanes; ++l) {
-        uint32_t& xs = x[k][l];
-        const uint32_t sl = xs & (kProbScale - 1);
-        const uint32_t s = lut[sl];
-        xs = (fc[s] & 0xFFFFu) * (xs >> kProbBits) + sl - (fc[s] >> 16);
-        if (xs < kStateLow) {
-          if (rptr[k] >= total_words[k]) return -7;
-          xs = (xs << 16) | words[k][rptr[k]++];
+      uint32_t* xk = x[k];
+      const uint16_t* wk = words[k];
+      uint64_t r = rptr[k];
+      // a step takes at most one word per lane
+      if (r + kLanes > total_words[k]) {
+        for (int l = 0; l < kLanes; ++l) {
+          const uint32_t sl = xk[l] & (kProbScale - 1);
+          const uint32_t s = lt[sl];
+          xk[l] = (fc[s] & 0xFFFFu) * (xk[l] >> kProbBits) + sl - (fc[s] >> 16);
+          if (xk[l] < kStateLow) {
+            if (r >= total_words[k]) return -7;
+            xk[l] = (xk[l] << 16) | wk[r++];
+          }
+          blk[l * kSub + m] = static_cast<uint8_t>(s);
         }
-        const uint32_t idx = ss * kSuper + l * kSub + m;
-        if (idx < ch.n_sym) dst[idx] = static_cast<uint8_t>(s);
+      } else {
+        for (int l = 0; l < kLanes; ++l) {
+          const uint32_t sl = xk[l] & (kProbScale - 1);
+          const uint32_t s = lt[sl];
+          xk[l] = (fc[s] & 0xFFFFu) * (xk[l] >> kProbBits) + sl - (fc[s] >> 16);
+          if (xk[l] < kStateLow) xk[l] = (xk[l] << 16) | wk[r++];
+          blk[l * kSub + m] = static_cast<uint8_t>(s);
+        }
       }
+      rptr[k] = r;
     }
+    if (tail) std::memcpy(dst + base, tail_buf, ch.n_sym - base);
   }
   for (int k = 0; k < kStreams; ++k) {
     for (int l = 0; l < kLanes; ++l)
