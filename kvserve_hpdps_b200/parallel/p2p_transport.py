@@ -285,12 +285,7 @@ class P2PTransport:
                 aborted = list(self._aborted)
                 self._aborted.clear()
                 item = self._pending[0] if self._pending else None
-            for ev, off, size in aborted:  # opened, never committed: back once idle
-                ev.synchronize()
-                with self._lock:
-                    self._unfinished.discard(off)
-                    self._free_after_done.pop(off, None)
-                self._release_regions([(off, size)])
+            self._release_aborted(aborted)
             if item is None:
                 continue
             ev, rid, tids, nbytes, t0, base = item
@@ -309,6 +304,31 @@ class P2PTransport:
             ms = start.elapsed_time(ev) if start is not None else (time.monotonic() - t0) * 1e3
             write_transfer_stats(rid, ms, nbytes, transport="nvlink-p2p")
             notify_sent(self._listeners, rid, list(tids or [rid]), ms, nbytes, logger)
+
+    def _release_aborted(self, aborted) -> None:
+        """Messages reserved but never committed: their ring space and flag
+        slot go back once the work queued before the abort has finished."""
+        for ev, off, size in aborted:
+            if ev is not None:
+                ev.synchronize()
+            with self._lock:
+                self._unfinished.discard(off)
+                self._free_after_done.pop(off, None)
+            self._release_regions([(off, size)])
+
+    def _abandon(self, base: int, total: int, stream, request_id: str,
+                 member_tids: Optional[list[str]], err: Exception) -> None:
+        """A reserved message whose kernels could not be enqueued: it counts
+        as failed and its region returns through the completion thread (after
+        whatever ``stream`` had queued, which may still touch the region)."""
+        try:
+            done = stream.record_event()
+        except Exception:  # noqa: BLE001 - the device may be what failed
+            done = None
+        with self._pending_cv:
+            self._aborted.append((done, base, total))
+            self._pending_cv.notify_all()
+        self._unsent(request_id, member_tids, err)
 
     def _message_done(self, base: int) -> None:
         """The stores of the message at ring offset ``base`` have finished: a
@@ -341,20 +361,24 @@ class P2PTransport:
             return
         from kvserve_hpdps_b200.ops import kernels as K
         ready = _timing_event(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(self._stream):
-            self._stream.wait_event(ready)
-            ck = torch.empty(2, dtype=torch.int64, device=self.device)
-            K.zero_checksum(ck)
-            # one pass: the copy over NVLink also sums the message checksum,
-            # and its last CTA stores the checksum and publishes the flag
-            segs = [(t.data_ptr(), self._peer.ptr + base + o, s, o)
-                    for t, o, s in zip(tensors, offs, sizes)]
-            K.copy_segments(segs, self.device, flag_ptr=self._peer.ptr + self.flag_off +
-                            slot * FLAG_STRIDE, flag_value=seq & 0xFFFFFFFF, ck=ck,
-                            trailer_ptr=self._peer.ptr + base + trailer)
-            for t in tensors + [ck]:
-                t.record_stream(self._stream)
-            done = _timing_event(self._stream)
+        try:
+            with torch.cuda.stream(self._stream):
+                self._stream.wait_event(ready)
+                ck = torch.empty(2, dtype=torch.int64, device=self.device)
+                K.zero_checksum(ck)
+                # one pass: the copy over NVLink also sums the message checksum,
+                # and its last CTA stores the checksum and publishes the flag
+                segs = [(t.data_ptr(), self._peer.ptr + base + o, s, o)
+                        for t, o, s in zip(tensors, offs, sizes)]
+                K.copy_segments(segs, self.device, flag_ptr=self._peer.ptr + self.flag_off +
+                                slot * FLAG_STRIDE, flag_value=seq & 0xFFFFFFFF, ck=ck,
+                                trailer_ptr=self._peer.ptr + base + trailer)
+                for t in tensors + [ck]:
+                    t.record_stream(self._stream)
+                done = _timing_event(self._stream)
+        except Exception as e:  # noqa: BLE001
+            self._abandon(base, total, self._stream, request_id, member_tids, e)
+            return
         self._send_ctl({
             "cmd": "PUT_RING", "kind": kind, "request_id": request_id,
             "layer_names": list(layer_names), "meta": meta, "n_body": n_body,
@@ -505,13 +529,18 @@ class P2PTransport:
             self._unsent(request_id, member_tids, e)
             return
         dev = raw.device
-        t0 = _timing_event(torch.cuda.current_stream(dev))
-        ck = torch.empty(2, dtype=torch.int64, device=dev)
-        K.paged_raw(raw, self._peer.ptr + base, True,
-                    flag_ptr=self._peer.ptr + self.flag_off + slot * FLAG_STRIDE,
-                    flag_value=seq & 0xFFFFFFFF, trailer_ptr=self._peer.ptr + base + trailer,
-                    checksum=ck)
-        done = _timing_event(torch.cuda.current_stream(dev))
+        stream = torch.cuda.current_stream(dev)
+        t0 = _timing_event(stream)
+        try:
+            ck = torch.empty(2, dtype=torch.int64, device=dev)
+            K.paged_raw(raw, self._peer.ptr + base, True,
+                        flag_ptr=self._peer.ptr + self.flag_off + slot * FLAG_STRIDE,
+                        flag_value=seq & 0xFFFFFFFF, trailer_ptr=self._peer.ptr + base + trailer,
+                        checksum=ck)
+        except Exception as e:  # noqa: BLE001
+            self._abandon(base, total, stream, request_id, member_tids, e)
+            return
+        done = _timing_event(stream)
         shape = [len(kv_layers), 2, len(ids)] + list(raw.block_shape)
         self._send_ctl({
             "cmd": "PUT_RING", "kind": "raw", "request_id": request_id,

@@ -4,7 +4,7 @@ transport, and failure paths injected on the host (no GPU involved)."""
 import multiprocessing as mp
 import socket
 import time
-from collections import deque
+from collections import defaultdict, deque
 
 import pytest
 import torch
@@ -442,3 +442,31 @@ def test_p2p_bandwidth_probe_never_blocks_the_caller():
     bw = t.bandwidth_mbps()  # finished probe: 256 KiB in 262.144 us = 953.67 MB/s
     assert t._bw_probe is None and abs(bw - (1 << 18) / (1 << 20) / 262.144e-6) < 1e-6
     assert t._alloc.free_bytes() == 1 << 20  # the probe's ring space is back
+
+
+def test_p2p_reservation_whose_launch_failed_is_returned():
+    """A message reserved in the ring whose kernels could not be enqueued
+    counts as failed, and its region and flag slot go back after the work
+    queued before the failure (the completion thread's job)."""
+    import threading
+    t = _slot_state(1, 512, 0.2)
+    t._pending_cv = threading.Condition()
+    t._aborted, t._failed = [], defaultdict(int)
+    waited = []
+
+    class Ev:
+        def synchronize(self):
+            waited.append(True)
+
+    class Stream:
+        def record_event(self):
+            return Ev()
+
+    base, seq, slot = t._reserve(256)
+    t._abandon(base, 256 + 0, Stream(), "r", ["a", "b"], RuntimeError("launch failed"))
+    assert t._failed == {"a": 1, "b": 1} and len(t._aborted) == 1
+    with pytest.raises(RuntimeError):  # the only slot is still taken
+        t._reserve(256)
+    t._release_aborted(t._aborted)
+    assert waited == [True] and list(t._free_slots) == [slot] and t._inflight_msgs == 0
+    assert t._reserve(256)[0] == base
