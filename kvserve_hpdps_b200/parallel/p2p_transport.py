@@ -706,7 +706,50 @@ class P2PTransport:
                 and all(isinstance(v, int) for v in region) and self._producer_id is not None):
             self._ctl.reply(self._producer_id, pack({"cmd": "FREE", "regions": [list(region)]}))
 
+    def _check_put(self, msg: dict) -> None:
+        """A header's offsets address this GPU's own ring: every tensor, the
+        checksum trailer and the flag slot must lie inside the message's
+        region and the region inside the ring, and every shape must match its
+        byte count, before any view or kernel touches them (a corrupt or
+        foreign header is refused instead of read or written out of bounds)."""
+        def whole(v) -> bool:
+            return isinstance(v, int) and not isinstance(v, bool) and v >= 0
+        region = msg.get("region")
+        if not (isinstance(region, (list, tuple)) and len(region) == 2
+                and all(whole(v) for v in region)):
+            raise ValueError(f"bad region {region!r}")
+        lo, hi = int(region[0]), int(region[0]) + int(region[1])
+        if hi > self.ring_bytes:
+            raise ValueError(f"region [{lo}, {hi}) outside the {self.ring_bytes}-byte ring")
+        if not (whole(msg.get("slot")) and msg["slot"] < self.n_flags and whole(msg.get("seq"))):
+            raise ValueError("bad flag slot or sequence number")
+        if msg.get("kind") not in ("raw", "bundle"):
+            raise ValueError(f"unknown message kind {msg.get('kind')!r}")
+        specs = msg.get("specs")
+        if not isinstance(specs, list) or not specs:
+            raise ValueError("no tensor specs")
+        for sp in specs:
+            off, n, shape = sp.get("off"), sp.get("nbytes"), sp.get("shape")
+            if not (whole(off) and whole(n) and lo <= off and off + n <= hi):
+                raise ValueError(f"tensor [{off}, +{n}) outside its region")
+            dt = getattr(torch, sp["dtype"], None) if isinstance(sp.get("dtype"), str) else None
+            if not isinstance(dt, torch.dtype) or not isinstance(shape, list) \
+                    or not all(whole(d) for d in shape):
+                raise ValueError(f"bad tensor spec {sp!r}")
+            numel = 1
+            for d in shape:
+                numel *= d
+            if numel * dt.itemsize != n:
+                raise ValueError(f"shape {shape} of {sp['dtype']} is not {n} bytes")
+        tr = msg.get("trailer")
+        if tr is not None and not (whole(tr) and lo <= tr and tr + 16 <= hi):
+            raise ValueError("checksum trailer outside its region")
+        if msg["kind"] == "bundle" and not (whole(msg.get("n_body"))
+                                            and msg["n_body"] <= len(specs)):
+            raise ValueError("bad body count")
+
     def _on_put(self, msg: dict) -> None:
+        self._check_put(msg)
         views = [tensor_view(self._region.ptr + s["off"], s["nbytes"], getattr(torch, s["dtype"]),
                              s["shape"], self.local_rank) for s in msg["specs"]]
         ring = {"slot": msg["slot"], "seq": msg["seq"], "region": tuple(msg["region"]),

@@ -395,6 +395,7 @@ def test_p2p_consumer_rejects_unusable_headers():
     t._ctl, t._producer_id = Ctl(), b"prod"
     t._region = type("R", (), {"ptr": 4096})()
     t.local_rank, t.is_sender = 0, False
+    t.ring_bytes, t.n_flags = 1 << 20, 16
     msg = {"cmd": "PUT_RING", "kind": "bundle", "request_id": "r9", "layer_names": ["a"],
            "meta": {}, "n_body": 1, "region": [512, 1024], "slot": 3, "seq": 7,
            "specs": [{"shape": [4], "dtype": "uint8", "off": 512, "nbytes": 4}]}
@@ -470,3 +471,43 @@ def test_p2p_reservation_whose_launch_failed_is_returned():
     t._release_aborted(t._aborted)
     assert waited == [True] and list(t._free_slots) == [slot] and t._inflight_msgs == 0
     assert t._reserve(256)[0] == base
+
+
+def test_p2p_consumer_checks_header_offsets_before_any_access():
+    """Offsets in a PUT_RING header address the consumer's own ring: a
+    header whose tensors, trailer, region or flag slot fall outside, or
+    whose shape does not match its byte count, is refused before a view or
+    kernel would touch the memory."""
+    from kvserve_hpdps_b200.parallel.p2p_transport import P2PTransport
+    t = object.__new__(P2PTransport)
+    t.ring_bytes, t.n_flags = 4096, 8
+    good = {"kind": "bundle", "n_body": 1, "region": [1024, 1024], "slot": 3, "seq": 9,
+            "trailer": 1792, "specs": [{"shape": [256], "dtype": "uint8", "off": 1024,
+                                         "nbytes": 256},
+                                        {"shape": [2, 8], "dtype": "bfloat16", "off": 1280,
+                                         "nbytes": 32}]}
+    t._check_put(good)
+    raw = dict(good, kind="raw", n_body=None)
+    t._check_put(raw)
+
+    def bad(**kw):
+        m = dict(good)
+        m.update(kw)
+        with pytest.raises(ValueError):
+            t._check_put(m)
+    bad(region=[3584, 1024])                       # past the ring
+    bad(region=[-256, 1024])
+    bad(region=[1024])
+    bad(slot=8)                                    # no such flag slot
+    bad(slot=True)
+    bad(kind="tensor")
+    bad(trailer=2040)                              # trailer runs past the region
+    bad(n_body=3)
+    bad(specs=[])
+    bad(specs=[{"shape": [256], "dtype": "uint8", "off": 900, "nbytes": 256}])   # before
+    bad(specs=[{"shape": [1024], "dtype": "uint8", "off": 1280, "nbytes": 1024}])  # after
+    bad(specs=[{"shape": [100], "dtype": "uint8", "off": 1024, "nbytes": 256}])  # shape
+    bad(specs=[{"shape": [256], "dtype": "object", "off": 1024, "nbytes": 256}])
+    bad(specs=[{"shape": [256], "dtype": "manual_seed", "off": 1024, "nbytes": 256}])
+    t._check_put(dict(good, specs=[{"shape": [8], "dtype": "bool", "off": 1024, "nbytes": 8}]))
+    bad(specs=[{"shape": [-1], "dtype": "uint8", "off": 1024, "nbytes": 0}])
