@@ -828,6 +828,18 @@ def set_trace(device: Optional[torch.device], jobs_per_cta: int = 256) -> Option
     return _trace["buf"]
 
 
+def _check_extents(codes: torch.Tensor, meta: torch.Tensor, items: WorkItems) -> None:
+    """The kernels address codes and metadata at the items' offsets: buffers
+    shorter than the items' extents (a message whose layout does not match
+    the consumer's requests) are refused before a launch could read or
+    write past them."""
+    cb = codes.numel() * codes.element_size()
+    mb = meta.numel() * meta.element_size()
+    if cb < items.code_bytes or mb < items.meta_bytes:
+        raise ValueError(f"code/metadata buffers of {cb}/{mb} bytes are shorter than the "
+                         f"{items.code_bytes}/{items.meta_bytes} bytes the work items address")
+
+
 def _launch(slots: LayerSlots, items: WorkItems, bmat: torch.Tensor, codes, meta, kstat, vstat,
             engine: int, ck: Optional[torch.Tensor] = None, ck_off: int = 0) -> LayerLaunch:
     dev = slots.device
@@ -872,6 +884,7 @@ def quantize(slots: LayerSlots, items: WorkItems, codes: Optional[torch.Tensor] 
         codes = torch.empty(max(items.code_bytes, 16), dtype=torch.uint8, device=dev)
     if meta is None:
         meta = torch.empty(max(items.meta_bytes, 16), dtype=torch.uint8, device=dev)
+    _check_extents(codes, meta, items)
     n_pairs = items.num_items * slots.num_heads * HEAD_DIM
     kstat = ws.buf("kstat", 8 * n_pairs, torch.int32)
     vstat = ws.buf("vstat", 8 * items.total_rows * slots.num_heads, torch.float32)
@@ -892,6 +905,7 @@ def dequantize(codes: torch.Tensor, meta: torch.Tensor, dst_slots: LayerSlots, i
                engine: int = ENGINE_TCGEN05) -> None:
     """Dequantize + inverse transform every item into its destination slot
     (paged cache) at the item's block ids (one launch)."""
+    _check_extents(codes, meta, items)
     L = _launch(dst_slots, items, dst_slots.bmat_inv, codes, meta, None, None, engine)
     check(lib().kvs_dequant_inverse(ctypes.byref(L)), "dequant_inverse")
 

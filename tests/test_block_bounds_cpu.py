@@ -96,3 +96,23 @@ def test_work_item_tables_match_per_item_layout():
         K.WorkItems(slots, items[:2], code_offsets=[8, 0])
     with pytest.raises(ValueError):
         K.WorkItems(slots, items[:2], meta_offsets=[0])
+
+
+def test_code_and_metadata_buffers_cover_the_items():
+    """Buffers shorter than the extents the work items address are refused
+    before any launch (a message whose layout does not match the requests)."""
+    from types import SimpleNamespace
+
+    import pytest
+    import torch
+
+    from kvserve_hpdps_b200.ops import kernels as K
+    items = SimpleNamespace(code_bytes=4096, meta_bytes=1056)
+    K._check_extents(torch.empty(4096, dtype=torch.uint8), torch.empty(528, dtype=torch.float16),
+                     items)
+    with pytest.raises(ValueError, match="shorter"):
+        K._check_extents(torch.empty(4080, dtype=torch.uint8),
+                         torch.empty(1056, dtype=torch.uint8), items)
+    with pytest.raises(ValueError, match="shorter"):
+        K._check_extents(torch.empty(8192, dtype=torch.uint8),
+                         torch.empty(1040, dtype=torch.uint8), items)
