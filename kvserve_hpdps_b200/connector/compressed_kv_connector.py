@@ -864,6 +864,8 @@ class CompressedKVConnector(KVConnectorBase_V1):
                                                              payload["aux_tensors"]))
             cd = rec["cd"]
             md = cd.metadata or {}
+            if md.get("num_heads") is not None:
+                self._check_heads(int(md["num_heads"]))
             comp = self._get_compressor()
             if md.get("layout") in ("items", "items_packed"):
                 caches = [self._layer_cache(n, fc) for n in names]
@@ -882,6 +884,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             kv = comp.decompress(cd)
             if kv is None:
                 raise RuntimeError("decompression returned None")
+            self._check_heads(int(kv.shape[-2]))  # [L, 2, blocks, block_size, heads, dim]
             rm = self._step_reqs[members[0]]
             for i, name in enumerate(names):
                 cache = self._layer_cache(name, fc)
@@ -898,6 +901,13 @@ class CompressedKVConnector(KVConnectorBase_V1):
         for cache, part in zip(caches, payload_t):
             if cache is not None:
                 inject_kv_into_layer_by_blocks(cache, part, rm.block_ids, rm.request_id)
+
+    def _check_heads(self, heads: int) -> None:
+        if heads != self._num_kv_heads:
+            raise ValueError(
+                f"the message carries {heads} KV heads per rank but this consumer's caches hold "
+                f"{self._num_kv_heads}: producer and consumer must run the same tensor-parallel "
+                f"size (heterogeneous TP is not supported)")
 
     @staticmethod
     def _scatter_raw(rm: ReqMeta, caches: list, payload: Any, payload_t: Any) -> bool:

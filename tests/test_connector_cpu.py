@@ -338,6 +338,31 @@ def test_default_mode_handoff_on_cpu():
         assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.9
 
 
+def test_head_count_mismatch_is_a_failed_load():
+    """A message built for another per-rank head count (producer and
+    consumer at different TP sizes) is not decoded: the load fails with a
+    message that names the cause, and the blocks go to vLLM's policy."""
+    import logging
+    seen = []
+
+    class Keep(logging.Handler):
+        def emit(self, record):
+            seen.append(record.getMessage())
+    log = logging.getLogger("kvserve_hpdps_b200")
+    h = Keep(level=logging.ERROR)
+    log.addHandler(h)
+    p, c, pair = make_pair("default")
+    c._num_kv_heads = H // 2
+    try:
+        pc, cc = handoff(p, c)
+    finally:
+        log.removeHandler(h)
+    assert any("heterogeneous TP" in m for m in seen)
+    assert c.get_block_ids_with_load_errors() == {2, 6, 0}
+    name = next(iter(cc))  # nothing of the producer's KV was written
+    assert not torch.equal(cc[name][:, [2, 6, 0]], pc[name][:, [5, 1, 7]])
+
+
 def test_compressed_handoff_with_blocks_outer_caches():
     """FlashInfer-layout caches ([num_blocks, 2, bs, H, D], what vLLM
     allocates on B200): the whole-tensor compressors get [L, 2, blocks, ...],
