@@ -14,6 +14,9 @@ Example::
   python examples/cpu_roundtrip.py
   python examples/cpu_roundtrip.py --pipeline quantizer,codec --codec bitpack
   python examples/cpu_roundtrip.py --mode default
+  # one TP rank's share of a 32K-token Qwen2.5-32B TP4 request (2 GiB, 8-layer chunks)
+  python examples/cpu_roundtrip.py --layers 64 --tokens 32768 --heads 2 \
+      --model Qwen2.5-32B-Instruct --tp-size 4 --tp-rank 1
 """
 
 from __future__ import annotations
@@ -33,7 +36,11 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--tokens", type=int, default=2048)
-    ap.add_argument("--heads", type=int, default=4)
+    ap.add_argument("--heads", type=int, default=4, help="KV heads of this rank")
+    ap.add_argument("--model", default="Qwen2.5-7B-Instruct",
+                    help="head-score table (Qwen2.5-32B-Instruct: 64 layers x 8 KV heads)")
+    ap.add_argument("--tp-size", type=int, default=1)
+    ap.add_argument("--tp-rank", type=int, default=0)
     ap.add_argument("--pipeline", default="transformer,quantizer,codec")
     ap.add_argument("--codec", default="rans", help="rans | bitpack | nvcomp | lc")
     ap.add_argument("--seed", type=int, default=0)
@@ -51,7 +58,7 @@ def main(argv=None) -> int:
     kv = kv.to(torch.bfloat16)
     spec = {"enabled": True, "pipeline": args.pipeline.split(","), "backend": "generic",
             "transformer_config": {"transform_type": "hadamard", "seed": 0x3333},
-            "quantizer_config": {"model_name": "Qwen2.5-7B-Instruct", "hybrid_ratio": 0.3,
+            "quantizer_config": {"model_name": args.model, "hybrid_ratio": 0.3,
                                  "high_key_max_value": 16, "high_value_max_value": 16,
                                  "low_key_max_value": 12, "low_value_max_value": 16,
                                  "axis_key": "channel", "axis_value": "token",
@@ -59,7 +66,8 @@ def main(argv=None) -> int:
             "codec_config": {"codec_type": args.codec}, "min_compress_size": 0}
     if args.mode == "default":
         spec = "default"
-    ad = KVCompressionAdapter(spec, H, D, model_name="Qwen2.5-7B-Instruct", num_layers=L)
+    ad = KVCompressionAdapter(spec, H, D, model_name=args.model, num_layers=L,
+                              tp_rank=args.tp_rank, tp_size=args.tp_size)
     x = kv.view(L, 2, 1, T, H, D)
     t0 = time.perf_counter()
     cd = ad.compress(x, "cpu-roundtrip")
@@ -70,7 +78,8 @@ def main(argv=None) -> int:
     nbytes = build_wire(cd).nbytes
     err = error_metrics(x.float(), out.float())
     print(json.dumps({
-        "config": f"CPU round trip, Qwen2.5-7B shapes [{L}, 2, {T}, {H}, 128], " + (
+        "config": f"CPU round trip, {args.model} shapes [{L}, 2, {T}, {H}, 128] "
+                  f"(TP rank {args.tp_rank}/{args.tp_size}), " + (
             "hybrid 0.3, high 16/16, low key 12" if isinstance(spec, dict) else
             "default spec (hybrid 0.8, levels 12/8 high, 6/4 low, Hadamard, rANS)"),
         "mode": args.mode,
