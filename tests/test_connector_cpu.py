@@ -458,3 +458,55 @@ def test_paged_send_statistics_with_a_stand_in_compressor(monkeypatch):
     raw = L * 2 * 3 * BS * H * D * 2
     assert st.data["original_bytes"] == [raw] and st.data["wire_bytes"] == [raw]
     assert not p._sent_orig
+
+
+def test_layer_chunked_request_of_a_tp_rank_through_the_connector(monkeypatch):
+    """The long-request path at a TP rank (config 4's shape, scaled down):
+    rank 1 of 4 of a Qwen2.5-32B-style model (2 KV heads per rank) sends a
+    request above the chunking threshold, so the message is a
+    ``manager_chunks`` body of layer chunks; the consumer rebuilds every
+    layer into its own blocks."""
+    import kvserve_hpdps_b200.compression.pipeline_manager as PM
+    monkeypatch.setattr(PM, "CHUNK_THRESHOLD_BYTES", 64 << 10)
+    layers, heads = 12, 2
+    spec = {"enabled": True, "pipeline": ["transformer", "quantizer", "codec"],
+            "transformer_config": {"seed": 0x3333}, "backend": "generic",
+            "quantizer_config": {"hybrid_ratio": 0.3, "high_key_max_value": 16,
+                                 "high_value_max_value": 16, "low_key_max_value": 12,
+                                 "low_value_max_value": 12, "axis_key": "channel",
+                                 "axis_value": "token", "split_type": "head"},
+            "codec_config": {"codec_type": "rans"}}
+
+    def cfg(producer):
+        c = vllm_config(producer, spec)
+        c.model_config = SimpleNamespace(
+            get_num_kv_heads=lambda pc: heads, get_head_size=lambda: D,
+            get_num_layers=lambda pc: layers, model="/models/Qwen2.5-32B-Instruct",
+            hf_text_config=SimpleNamespace(num_hidden_layers=layers), use_mla=False)
+        return c
+    pair = FakeTransportPair()
+    p = CompressedKVConnector(cfg(True), KVConnectorRole.WORKER)
+    c = CompressedKVConnector(cfg(False), KVConnectorRole.WORKER)
+    for conn in (p, c):
+        conn._tp_rank, conn._tp_size, conn._compressor = 1, 4, None
+    p.attach_transport(pair.producer())
+    c.attach_transport(pair.consumer())
+    g = torch.Generator().manual_seed(7)
+    pc = {f"model.layers.{l}.self_attn.attn":
+          torch.randn(2, 8, BS, heads, D, generator=g).to(torch.bfloat16) for l in range(layers)}
+    cc = {k: torch.zeros_like(v) for k, v in pc.items()}
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    p.bind_connector_metadata(meta_for("r1", "tid-long", 60, [5, 1, 7, 2]))
+    for name in sorted(pc, key=layer_index):
+        p.save_kv_layer(name, pc[name], None)
+    p.wait_for_save()
+    payload = pair.inbox["tid-long"][0][1]
+    assert payload["meta"]["body_mode"] == "manager_chunks" and len(payload["body_chunks"]) == 2
+    c.bind_connector_metadata(meta_for("d1", "tid-long", 60, [0, 3, 6, 4]))
+    c.start_load_kv(None)
+    assert c.get_block_ids_with_load_errors() == set()
+    for name in pc:
+        a = pc[name][:, [5, 1, 7, 2]].float().flatten()
+        b = cc[name][:, [0, 3, 6, 4]].float().flatten()
+        assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.97
