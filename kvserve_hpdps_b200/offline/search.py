@@ -100,12 +100,29 @@ def run_model_search(model_name: str, tasks: list[str], tolerance: float, out_di
     cr = CompressionEvaluator(model_name, cr_task or tasks[0], device, base_model_path,
                               base_config_path, model=acc.model, tokenizer=acc.tokenizer,
                               scores=acc.scores, task_dirs=task_dirs)
+    speed = None
+    if torch.cuda.is_available():
+        # the controller needs each profile's compress/decompress speed: timed
+        # with the fused kernels on synthetic KV of the model's per-rank shape
+        heads = int(getattr(acc.model.config, "num_key_value_heads", 0) or
+                    acc.model.config.num_attention_heads)
+        speed = KVEvaluator(synthetic_kv(4, 2048, heads, "cuda"), model_name)
+    else:
+        print("search: no GPU, profile speeds are not measured (the library gets a "
+              "placeholder of 1e6 MB/s)", file=sys.stderr)
 
     def evaluate(c: Candidate) -> dict:
         p = candidate_params(c)
-        return {"compression_ratio": cr.evaluate(p), "accuracy": acc.evaluate(p)}
+        out = {"compression_ratio": cr.evaluate(p), "accuracy": acc.evaluate(p)}
+        if speed is not None:
+            r = speed.evaluate(c)
+            out.update(encode_mbps=r.encode_mbps, decode_mbps=r.decode_mbps,
+                       harmonic_speed_mbps=r.harmonic_speed_mbps)
+        return out
 
-    res = _search(evaluate, 100.0 - tolerance, model_name, tolerance, out_dir, budget, space)
+    # task accuracy is x100 of the default cache's; library accuracy is a fraction
+    res = _search(evaluate, 100.0 - tolerance, model_name, tolerance, out_dir, budget, space,
+                  library_acc_scale=0.01)
     res["tasks"] = list(tasks)
     res["default_scores"] = list(acc.default_scores)
     save_results(os.path.join(out_dir, f"tolerance_{tolerance:g}_results.json"), res)
@@ -113,7 +130,8 @@ def run_model_search(model_name: str, tasks: list[str], tolerance: float, out_di
 
 
 def _search(evaluate_fn, threshold: float, model_name: Optional[str], tolerance: float,
-            out_dir: str, budget: int, space: Optional[dict]) -> dict:
+            out_dir: str, budget: int, space: Optional[dict],
+            library_acc_scale: float = 1.0) -> dict:
     os.makedirs(out_dir, exist_ok=True)
     cache_path = os.path.join(out_dir, "cr_cache.csv")
     cache = load_cache(cache_path)
@@ -132,7 +150,8 @@ def _search(evaluate_fn, threshold: float, model_name: Optional[str], tolerance:
     results["tolerance"] = tolerance
     results["model_name"] = model_name
     save_results(os.path.join(out_dir, f"tolerance_{tolerance:g}_results.json"), results)
-    lib = build_library(results["history"], model_name or "unknown")
+    hist = [dict(h, accuracy=h["accuracy"] * library_acc_scale) for h in results["history"]]
+    lib = build_library(hist, model_name or "unknown")
     write_library(os.path.join(out_dir, "profile_library.json"), lib)
     return results
 

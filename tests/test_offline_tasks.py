@@ -169,6 +169,11 @@ def test_model_search_writes_results_and_library(model, tmp_path):
     assert saved["threshold"] == 97.0 and len(saved["history"]) == 2
     lib = json.loads((out / "profile_library.json").read_text())
     assert lib and (out / "cr_cache.csv").exists()
+    # the controller compares fractions (accuracy_requirement 0.92): task
+    # accuracy x100 of the default cache goes into the library as a fraction
+    accs = [p["quality_metrics"]["accuracy"] for b in lib["accuracy_buckets"]
+            for p in b["pareto_profiles"]]
+    assert accs and all(0.0 <= a <= 1.0 for a in accs)
     for h in saved["history"]:
         assert h["compression_ratio"] > 1.0 and 0.0 <= h["accuracy"] <= 100.0
 
