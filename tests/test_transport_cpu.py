@@ -511,3 +511,65 @@ def test_p2p_consumer_checks_header_offsets_before_any_access():
     bad(specs=[{"shape": [256], "dtype": "manual_seed", "off": 1024, "nbytes": 256}])
     t._check_put(dict(good, specs=[{"shape": [8], "dtype": "bool", "off": 1024, "nbytes": 8}]))
     bad(specs=[{"shape": [-1], "dtype": "uint8", "off": 1024, "nbytes": 0}])
+
+
+def test_p2p_producer_headers_pass_the_consumer_check(monkeypatch):
+    """Every header the producer builds (raw and bundle sends, paged raw
+    sends, direct-to-ring messages) passes the consumer's offset check after
+    the msgpack round trip: the kernels and CUDA events are stood in for on
+    the CPU, the header dicts are the producer's own."""
+    import threading
+    from types import SimpleNamespace
+
+    import kvserve_hpdps_b200.parallel.p2p_transport as PT
+    from kvserve_hpdps_b200.ops import kernels as K
+    from kvserve_hpdps_b200.parallel.control import pack, unpack
+
+    class Stream:
+        def wait_event(self, ev):
+            pass
+
+        def record_event(self):
+            return None
+
+    monkeypatch.setattr(PT, "_timing_event", lambda stream: None)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: Stream())
+    monkeypatch.setattr(torch.cuda, "stream", lambda s: __import__("contextlib").nullcontext())
+    monkeypatch.setattr(torch.Tensor, "record_stream", lambda self, s: None)
+    for name in ("zero_checksum", "copy_segments", "paged_raw"):
+        monkeypatch.setattr(K, name, lambda *a, **k: None)
+
+    class Raw:  # the paged raw message's descriptors (device-built in production)
+        def __init__(self, layers, items):
+            self.flat_bytes = len(layers) * 2 * len(items[0][1]) * 16 * 4 * 128 * 2
+            self.device, self.block_shape = torch.device("cpu"), (16, 4, 128)
+            self.dtype, self.block_order = torch.bfloat16, "hnd"
+    monkeypatch.setattr(K, "RawItems", Raw)
+
+    ring, flags = 1 << 22, 8
+    prod = _slot_state(flags, ring, 1.0)
+    headers = []
+    prod._send_ctl = headers.append
+    prod._stream, prod.device, prod.local_rank = Stream(), torch.device("cpu"), 0
+    prod.is_sender = True
+    prod._peer = SimpleNamespace(ptr=1 << 40)
+    prod.flag_off = ring
+    prod._pending_cv, prod._pending = threading.Condition(), deque()
+    prod._sent, prod._failed = defaultdict(int), defaultdict(int)
+    cons = object.__new__(PT.P2PTransport)
+    cons.ring_bytes, cons.n_flags = ring, flags
+
+    prod.send("r0", ["l0"], torch.zeros(3, 2, 5, dtype=torch.bfloat16))
+    prod.send_bundle("r1", ["__compressed__", "l0"], {"k": 1},
+                     [torch.zeros(1000, dtype=torch.uint8)],
+                     [torch.zeros(4, 128, dtype=torch.float16), torch.arange(3),
+                      torch.zeros(0, dtype=torch.float32), torch.ones(5, dtype=torch.bool)])
+    prod.send_paged("r2", ["l0", "l1"], [None, None], [4, 9, 1])
+    msg = prod.open_message([16 + 70000, 1056])
+    prod.commit_message(msg, "r3", ["__compressed__", "l0"], {"m": 2},
+                        [{"shape": [16 + 70000], "dtype": "uint8"},
+                         {"shape": [1056], "dtype": "uint8"}], 1,
+                        dyn_len={"seg": 0, "len_off": 8, "len_add": 0})
+    assert [h["request_id"] for h in headers] == ["r0", "r1", "r2", "r3"]
+    for h in headers:
+        cons._check_put(unpack(pack(h)))
