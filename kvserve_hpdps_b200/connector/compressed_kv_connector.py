@@ -108,6 +108,7 @@ logger = get_logger(__name__)
 
 LOAD_TIMEOUT_S = float(os.environ.get("KVSERVE_LOAD_TIMEOUT_S", "60"))
 CONTROLLER_FEEDBACK_TTL_S = 300.0  # as the adapter's controller contexts
+STATS_ENTRY_TTL_S = 30.0  # unreported statistics entries of finished requests
 
 
 def normalize_overlap_mode(mode) -> str:
@@ -234,6 +235,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._xfer_stats = KVServeConnectorStats()
         self._sent_orig: dict[str, deque] = defaultdict(deque)
         self._sent_lock = threading.Lock()
+        self._sent_retired: deque = deque()  # (time, transfer ids) whose messages are out
         # controller feedback: transfer id -> (request id, compress ms, time) until the
         # transport reports the message sent; completions queued by its thread
         self._ctl_wait: dict[str, tuple[str, float, float]] = {}
@@ -566,13 +568,20 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._layer_refs.clear()
         if not self._async_send and self._transport is not None:
             self._transport.wait_for_sent()
-            self._drop_sent_entries(rm.transfer_id for rm in meta.requests)
+            self._retire_sent_entries([rm.transfer_id for rm in meta.requests])
 
-    def _drop_sent_entries(self, tids) -> None:
-        """Statistics entries of messages that never left (refused, dropped)."""
+    def _retire_sent_entries(self, tids) -> None:
+        """The requests' messages are out (or refused, or dropped): statistics
+        entries still queued under their transfer ids belong to messages the
+        transport never reported, and are dropped once the transport thread
+        has had ample time for any late report (it may report a message just
+        after the wait for it returned)."""
+        now = time.monotonic()
+        self._sent_retired.append((now, list(tids)))
         with self._sent_lock:
-            for t in tids:
-                self._sent_orig.pop(t, None)
+            while self._sent_retired and now - self._sent_retired[0][0] > STATS_ENTRY_TTL_S:
+                for t in self._sent_retired.popleft()[1]:
+                    self._sent_orig.pop(t, None)
 
     def get_finished(self, finished_req_ids: set[str]):
         if self.is_producer:
@@ -596,7 +605,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         for rid in done:
             tid = self._rid2tid.pop(rid, None)
             if tid is not None:
-                self._drop_sent_entries([tid])
+                self._retire_sent_entries([tid])
                 self._transport.clear_sent(tid)
                 self._expected_msgs.pop(tid, None)
         return (done or None), None

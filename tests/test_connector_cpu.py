@@ -510,3 +510,21 @@ def test_layer_chunked_request_of_a_tp_rank_through_the_connector(monkeypatch):
         a = pc[name][:, [5, 1, 7, 2]].float().flatten()
         b = cc[name][:, [0, 3, 6, 4]].float().flatten()
         assert float(torch.nn.functional.cosine_similarity(a, b, dim=0)) > 0.97
+
+
+def test_late_transport_reports_still_find_their_statistics_entry(monkeypatch):
+    """A transport may report a message sent just after the producer's wait
+    for it returned: the entry stays until its time-to-live has passed, then
+    unreported entries (refused messages) are dropped."""
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    p, _, _ = make_pair(None)
+    p._expect_sent("t-late", 4000)
+    p._retire_sent_entries(["t-late"])        # the step's wait returned
+    p._on_sent("t-late", ["t-late"], 2.0, nbytes=1000)  # ...then the report
+    st = p.get_kv_connector_stats()
+    assert st.data["original_bytes"] == [4000] and st.data["wire_bytes"] == [1000]
+    p._expect_sent("t-refused", 4000)          # never reported
+    monkeypatch.setattr(mod, "STATS_ENTRY_TTL_S", 0.0)
+    p._retire_sent_entries(["t-refused"])
+    p._retire_sent_entries([])
+    assert "t-refused" not in p._sent_orig
