@@ -78,7 +78,8 @@ def run_search(kv: torch.Tensor, model_name: Optional[str], tolerance: float, ou
         return r
 
     return _search(evaluate, 1.0 * (1 - tolerance / 100.0), model_name, tolerance, out_dir,
-                   budget, space)
+                   budget, space, signature={"mode": "kv", "model": model_name,
+                                             "kv_shape": list(kv.shape)})
 
 
 def run_model_search(model_name: str, tasks: list[str], tolerance: float, out_dir: str,
@@ -122,17 +123,38 @@ def run_model_search(model_name: str, tasks: list[str], tolerance: float, out_di
 
     # task accuracy is x100 of the default cache's; library accuracy is a fraction
     res = _search(evaluate, 100.0 - tolerance, model_name, tolerance, out_dir, budget, space,
-                  library_acc_scale=0.01)
+                  library_acc_scale=0.01,
+                  signature={"mode": "tasks", "model": model_name, "tasks": list(tasks),
+                             "limit": int(limit), "seed": int(seed)})
     res["tasks"] = list(tasks)
     res["default_scores"] = list(acc.default_scores)
     save_results(os.path.join(out_dir, f"tolerance_{tolerance:g}_results.json"), res)
     return res
 
 
+def check_signature(out_dir: str, signature: Optional[dict]) -> None:
+    """The evaluation cache of ``out_dir`` belongs to one search (mode, model,
+    KV shape or tasks, sample): ``search_signature.json`` records it, and a
+    search with another signature refuses to resume from that cache."""
+    if signature is None:
+        return
+    path = os.path.join(out_dir, "search_signature.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            old = json.load(f)
+        if old != json.loads(json.dumps(signature)):
+            raise ValueError(f"{out_dir} holds the cache of another search ({old}); use a new "
+                             f"output directory for {signature}")
+        return
+    with open(path, "w") as f:
+        json.dump(signature, f, indent=2)
+
+
 def _search(evaluate_fn, threshold: float, model_name: Optional[str], tolerance: float,
             out_dir: str, budget: int, space: Optional[dict],
-            library_acc_scale: float = 1.0) -> dict:
+            library_acc_scale: float = 1.0, signature: Optional[dict] = None) -> dict:
     os.makedirs(out_dir, exist_ok=True)
+    check_signature(out_dir, signature)
     cache_path = os.path.join(out_dir, "cr_cache.csv")
     cache = load_cache(cache_path)
 

@@ -73,6 +73,10 @@ def test_kv_evaluator_cpu_and_export(tmp_path):
         "hybrid_ratio": [0.0, 1.0], "high_key_max_value": [16], "high_value_max_value": [16],
         "low_key_max_value": [8, 4], "low_value_max_value": [4]}, measure_speed=False)
     assert [h["candidate"] for h in res2["history"]] == [h["candidate"] for h in res["history"]]
+    # another search (here another KV shape) does not resume from this cache
+    with pytest.raises(ValueError, match="another search"):
+        run_search(kv[:1], "Qwen2.5-7B-Instruct", 5.0, str(tmp_path), budget=2,
+                   measure_speed=False)
 
 
 def test_library_export_selection(tmp_path):
