@@ -159,3 +159,17 @@ def test_reference_e2e_loop_and_its_failure_path(monkeypatch):
     line = bench.build_line(args, {"ms": 30.0, "cr": 2.0, "pairs": 1, "pipeline": "p",
                                    "transport": "local", "e2e": e2e}, 1)
     assert line["impl"] == "reference" and line["e2e"] == e2e
+
+
+def test_environment_check_report_and_exit_code():
+    """``python -m kvserve_hpdps_b200``: versions, native library, GPUs; the
+    exit code says whether the fused path can run on every visible GPU."""
+    from kvserve_hpdps_b200 import __main__ as env
+    rep = env.report()
+    assert rep["package"] and rep["native"]["loaded"] is True and rep["gpus"] == []
+    assert env.exit_code(rep) == 2  # no GPU here
+    b200 = {"index": 0, "name": "B200", "capability": "10.0", "fused_path": True}
+    h100 = dict(b200, capability="9.0", fused_path=False)
+    assert env.exit_code(dict(rep, gpus=[b200])) == 0
+    assert env.exit_code(dict(rep, gpus=[b200, h100])) == 1
+    assert env.exit_code(dict(rep, gpus=[b200], native={"loaded": False})) == 1
