@@ -61,6 +61,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from typing import Optional
 
 import torch
 
@@ -791,6 +792,53 @@ def _cr(args, wl, res, world):
     return orig / tot if tot else None
 
 
+LINK_GBS = 770.0  # measured NVLink 5 peer copy per direction on this pool's B200s
+
+
+def _peaks() -> tuple[float, str]:
+    """HBM copy bandwidth (read + write bytes): MEASURED_PEAKS.json when the
+    driver wrote it, else the earlier measurement of this pool."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def roofline(args, world: int, codec: str, cr: Optional[float], ms: float) -> dict:
+    """The path's roofline per request: the slower of its algorithmic HBM
+    bytes at the copy bandwidth and its bytes over NVLink at the peer-copy
+    bandwidth, and the measured time's fraction of it.  The key statistics
+    span every token of a request-layer, so the input is read twice (a
+    statistics pass, then quantization); codes are one byte (``none``),
+    4-bit nibbles (``rans``) or the bit-packed wire bytes (``bitpack``);
+    the rANS codes make a round trip through HBM on each side (written by
+    the quantize kernel, read by the encoder; written by the decoder, read
+    by the dequantize kernel)."""
+    raw = args.layers * 2 * args.tokens * args.kv_heads * 128 * 2
+    wire = raw / cr if cr else None
+    codes = {"none": raw / 2, "rans": raw / 4}.get(codec, wire or raw / 2)
+    stream = wire if codec == "rans" and wire else codes
+    hbm, src = _peaks()
+    # the message (codes, or the rANS stream) is written once into the
+    # consumer's memory: over NVLink at N >= 2, into the same HBM at N = 1
+    msg = stream if codec == "rans" else codes
+    local = 2 * codes if codec == "rans" else 0  # codes' round trip on each side
+    prod = 2 * raw + local
+    cons = msg + msg + local + raw  # written by the producer, read, decoded, scattered
+    if world == 1:  # one GPU does both halves; nothing crosses NVLink
+        parts = {"hbm": (prod + cons) / hbm}
+    else:  # producer and consumer run side by side, each message pipelined
+        parts = {"hbm-producer": prod / hbm, "nvlink": msg / LINK_GBS,
+                 "hbm-consumer": cons / hbm}
+    parts = {k: v / 1e6 for k, v in parts.items()}  # GB/s -> ms per request
+    bound = max(parts, key=parts.get)
+    return {"bound_ms": round(parts[bound], 5), "limited_by": bound,
+            "fraction": round(parts[bound] / ms, 3) if ms > 0 else None,
+            "terms_ms": {k: round(v, 5) for k, v in parts.items()},
+            "hbm_gbs": hbm, "link_gbs": LINK_GBS, "peaks": src}
+
+
 def _summary(args, wl, res, world, codec):
     ms = res["ms"] / (args.steps * wl.B)
     out = {"compression": compression_label(args, codec), "value": round(ms, 5),
@@ -798,6 +846,7 @@ def _summary(args, wl, res, world, codec):
            "reconstruction": res.get("error"), "launches": res["launches"]}
     cr = _cr(args, wl, res, world)
     out["compression_ratio"] = round(cr, 3) if cr else None
+    out["roofline"] = roofline(args, world, codec, cr, ms)
     for k in ("e2e", "stage_ms_per_request", "single_request_latency_ms"):
         if res.get(k) is not None:
             out[k] = res[k]
@@ -1169,6 +1218,9 @@ def build_line(args, res, world):
     for k in ("stage_ms_per_request", "single_request_latency_ms", "full_path"):
         if res.get(k) is not None:
             line[k] = res[k]
+    if args.compression != "off":  # same config, same algorithmic bytes in both arms
+        line["roofline"] = roofline(args, world, res.get("codec", args.codec), res.get("cr"),
+                                    value)
     if args.impl == "reference":
         line["impl"] = "reference"
         if res.get("e2e"):

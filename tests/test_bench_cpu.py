@@ -173,3 +173,25 @@ def test_environment_check_report_and_exit_code():
     assert env.exit_code(dict(rep, gpus=[b200])) == 0
     assert env.exit_code(dict(rep, gpus=[b200, h100])) == 1
     assert env.exit_code(dict(rep, gpus=[b200], native={"loaded": False})) == 1
+
+
+def test_roofline_terms_of_each_path(monkeypatch):
+    """Algorithmic bytes per 470 MB request: two reads of the input, the
+    codes (or the rANS stream) written into the consumer's memory and read,
+    the rANS codes' round trip on each side, the bf16 output."""
+    monkeypatch.setattr(bench, "_peaks", lambda: (6452.5, "measured"))
+    a = bench.parse_args([])
+    raw = 28 * 2 * 8192 * 4 * 128 * 2
+    r1 = bench.roofline(a, 1, "none", 1.988, 0.587)
+    assert r1["limited_by"] == "hbm"
+    assert abs(r1["bound_ms"] - 4 * raw / 6452.5e6) < 1e-4 and r1["fraction"] == 0.496
+    r2 = bench.roofline(a, 2, "none", 1.988, 0.479)
+    assert r2["limited_by"] == "nvlink" and abs(r2["bound_ms"] - raw / 2 / 770e6) < 1e-4
+    r3 = bench.roofline(a, 2, "rans", 9.18, 0.585)
+    assert r3["limited_by"] == "hbm-producer"
+    assert abs(r3["terms_ms"]["hbm-producer"] - (2 * raw + raw / 2) / 6452.5e6) < 1e-4
+    assert abs(r3["terms_ms"]["nvlink"] - raw / 9.18 / 770e6) < 1e-4
+    line = bench.build_line(bench.parse_args(["--impl", "reference"]),
+                            {"ms": 8 * 20 * 28.06, "cr": 1.988, "pairs": 1, "pipeline": "p",
+                             "transport": "local"}, 1)
+    assert line["roofline"]["fraction"] < 0.02  # the same bound for the reference arm
