@@ -195,3 +195,14 @@ def test_roofline_terms_of_each_path(monkeypatch):
                             {"ms": 8 * 20 * 28.06, "cr": 1.988, "pairs": 1, "pipeline": "p",
                              "transport": "local"}, 1)
     assert line["roofline"]["fraction"] < 0.02  # the same bound for the reference arm
+
+
+def test_full_path_summary_carries_its_roofline():
+    from types import SimpleNamespace
+    a = bench.parse_args([])
+    wl = SimpleNamespace(B=8, bf16_bytes_per_request=28 * 2 * 8192 * 4 * 128 * 2)
+    res = {"ms": 20 * 8 * 0.89, "launches": 220, "wire_bytes_per_step":
+           wl.bf16_bytes_per_request * 8 / 9.18, "e2e": {"value": 0.915}}
+    out = bench._summary(a, wl, res, 1, "rans")
+    assert out["compression_ratio"] == 9.18 and out["e2e"] == {"value": 0.915}
+    assert out["roofline"]["limited_by"] == "hbm" and 0.2 < out["roofline"]["fraction"] < 0.5
