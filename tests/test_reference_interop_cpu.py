@@ -371,6 +371,175 @@ def test_scheduler_side_matches_the_reference(tmp_path):
         (out.stdout[-1500:] + out.stderr[-3000:])
 
 
+SCHED_RANDOM = r"""
+import random, sys
+from types import SimpleNamespace as NS
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+import os
+os.environ["KVSERVE_TRANSPORT"] = "fake"
+from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+from kvserve_hpdps_b200.connector.compressed_kv_connector import CompressedKVConnector as Ours
+from kvserve_v1.connector.compressed_kv_connector import CompressedKVConnector as Ref
+
+BS = 16
+
+def cfg(producer):
+    mc = NS(get_num_kv_heads=lambda pc: 4, get_head_size=lambda: 128,
+            get_num_layers=lambda pc: 2, model="/models/Qwen2.5-7B-Instruct",
+            hf_text_config=NS(num_hidden_layers=2), use_mla=False)
+    kv = NS(is_kv_producer=producer, kv_ip="127.0.0.1", kv_port=29999, kv_role="kv_both",
+            kv_connector_extra_config={"compression": None}, kv_parallel_size=2, kv_rank=0)
+    return NS(kv_transfer_config=kv, cache_config=NS(block_size=BS), model_config=mc,
+              parallel_config=NS())
+
+def rows(m):
+    return [(r.request_id, r.transfer_id, list(r.token_ids), list(r.block_ids),
+             r.slot_mapping.tolist()) for r in m.requests]
+
+def producer_trace(seed):
+    # chunked prefills interleaved over steps, some restarted after preemption
+    rng = random.Random(seed)
+    free = list(range(1000)); rng.shuffle(free)
+    reqs, steps = {}, []
+    for i in range(rng.randint(3, 8)):
+        P = rng.randint(1, 150)
+        cuts = sorted(rng.sample(range(1, P), min(P - 1, rng.randint(0, 3)))) if P > 1 else []
+        reqs[f"r{i}"] = {"P": P, "chunks": [b - a for a, b in zip([0] + cuts, cuts + [P])],
+                         "tid": None if rng.random() < 0.2 else f"T{seed}-{i}",
+                         "start": rng.randint(0, 4)}
+    state = {rid: {"done": 0, "k": 0, "blocks": 0} for rid in reqs}
+    for step in range(12):
+        new, cached, sched, resumed = [], [], {}, set()
+        for rid, r in reqs.items():
+            st = state[rid]
+            if step < r["start"] or st["k"] >= len(r["chunks"]) or rng.random() < 0.3:
+                continue
+            restart = st["k"] > 0 and rng.random() < 0.15
+            if restart:  # preempted: everything again, in new blocks
+                st["done"], st["k"], st["blocks"] = 0, 0, 0
+            n = r["chunks"][st["k"]]
+            need = -(-(st["done"] + n) // BS) - st["blocks"]
+            blocks = [free.pop() for _ in range(need)]
+            if st["k"] == 0 and not restart:
+                new.append((rid, blocks))
+            else:
+                cached.append((rid, st["done"], blocks))
+                if restart:
+                    resumed.add(rid)
+            sched[rid] = n
+            st["done"] += n; st["k"] += 1; st["blocks"] += need
+        fin = [rid for rid in reqs if state[rid]["k"] >= len(reqs[rid]["chunks"])
+               and rng.random() < 0.3 and not state[rid].get("fin")]
+        for rid in fin:
+            state[rid]["fin"] = True
+        steps.append((new, cached, sched, resumed, fin))
+    return reqs, steps
+
+def play_producer(conn, reqs, steps):
+    out = []
+    R = {rid: NS(request_id=rid, prompt_token_ids=list(range(r["P"])),
+                 kv_transfer_params={"transfer_id": r["tid"]} if r["tid"] else None,
+                 all_token_ids=list(range(r["P"] + 1))) for rid, r in reqs.items()}
+    for new, cached, sched, resumed, fin in steps:
+        for rid, blocks in new:
+            out.append(("matched", rid, conn.get_num_new_matched_tokens(R[rid], 0)))
+            conn.update_state_after_alloc(R[rid], NS(get_block_ids=lambda b=blocks: (b,)), 0)
+        so = NS(scheduled_new_reqs=[NS(req_id=rid, prompt_token_ids=R[rid].prompt_token_ids,
+                                       block_ids=(b,), num_computed_tokens=0) for rid, b in new],
+                num_scheduled_tokens=dict(sched),
+                scheduled_cached_reqs=NS(req_ids=[c[0] for c in cached],
+                                         num_computed_tokens=[c[1] for c in cached],
+                                         new_block_ids=[(c[2],) for c in cached],
+                                         resumed_req_ids=set(resumed)))
+        out.append(("meta", rows(conn.build_connector_meta(so))))
+        for rid in fin:
+            out.append(("finished", rid, conn.request_finished(R[rid], [])))
+    return out
+
+def consumer_trace(seed):
+    # new requests with a locally cached prefix, requests first seen resumed,
+    # decode steps of loaded requests
+    rng = random.Random(1000 + seed)
+    free = list(range(1000)); rng.shuffle(free)
+    reqs = {}
+    for i in range(rng.randint(3, 8)):
+        P = rng.randint(1, 150)
+        pre = BS * rng.randint(0, max(0, (P - 1) // BS))
+        reqs[f"d{i}"] = {"P": P, "pre": pre, "tid": None if rng.random() < 0.2 else f"U{seed}-{i}",
+                         "kind": rng.choice(["new", "new", "resumed"]), "start": rng.randint(0, 3),
+                         "blocks": [free.pop() for _ in range(-(-P // BS) + 1)]}
+    return reqs
+
+def play_consumer(conn, reqs, seed):
+    rng = random.Random(2000 + seed)
+    out, seen = [], set()
+    R = {rid: NS(request_id=rid, prompt_token_ids=list(range(r["P"])),
+                 kv_transfer_params={"transfer_id": r["tid"]} if r["tid"] else None,
+                 all_token_ids=list(range(r["P"] + 2))) for rid, r in reqs.items()}
+    for rid, r in reqs.items():  # the scheduler asks, then allocates
+        m = conn.get_num_new_matched_tokens(R[rid], r["pre"])
+        out.append(("matched", rid, m))
+        conn.update_state_after_alloc(R[rid], NS(get_block_ids=lambda b=r["blocks"]: (b,)),
+                                      m[0] or 0)
+    for step in range(6):
+        new, cached = [], []
+        for rid, r in reqs.items():
+            if step < r["start"]:
+                continue
+            if rid not in seen and r["kind"] == "new":
+                new.append(rid); seen.add(rid)
+            elif rid not in seen and r["kind"] == "resumed":
+                cached.append((rid, rng.randint(0, r["P"]), True)); seen.add(rid)
+            elif rid in seen and rng.random() < 0.5:
+                cached.append((rid, r["P"] + step, False))  # a decode step
+        cached.sort(key=lambda c: not c[2])  # vLLM lists resumed requests first
+        so = NS(scheduled_new_reqs=[NS(req_id=rid, prompt_token_ids=R[rid].prompt_token_ids,
+                                       block_ids=(reqs[rid]["blocks"],),
+                                       num_computed_tokens=reqs[rid]["pre"]) for rid in new],
+                num_scheduled_tokens={**{rid: 1 for rid in new}, **{c[0]: 1 for c in cached}},
+                scheduled_cached_reqs=NS(req_ids=[c[0] for c in cached],
+                                         num_computed_tokens=[c[1] for c in cached],
+                                         new_block_ids=[(reqs[c[0]]["blocks"][:2],)
+                                                        for c in cached],
+                                         resumed_req_ids={c[0] for c in cached if c[2]}))
+        out.append(("meta", rows(conn.build_connector_meta(so))))
+    for rid in reqs:
+        out.append(("finished", rid, conn.request_finished(R[rid], [])))
+    return out
+
+n = 0
+for seed in range(40):
+    reqs, steps = producer_trace(seed)
+    a = play_producer(Ours(cfg(True), KVConnectorRole.SCHEDULER), reqs, steps)
+    b = play_producer(Ref(cfg(True), KVConnectorRole.SCHEDULER), reqs, steps)
+    assert a == b, ("producer", seed, [(x, y) for x, y in zip(a, b) if x != y][:2])
+    creqs = consumer_trace(seed)
+    a = play_consumer(Ours(cfg(False), KVConnectorRole.SCHEDULER), creqs, seed)
+    b = play_consumer(Ref(cfg(False), KVConnectorRole.SCHEDULER), creqs, seed)
+    assert a == b, ("consumer", seed, [(x, y) for x, y in zip(a, b) if x != y][:2])
+    n += sum(len(x[1]) for x in a if x[0] == "meta")
+print("RANDOM SCHEDULER OK", n)
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_scheduler_side_matches_the_reference_on_random_traces(tmp_path):
+    """40 seeded random traces per role, played into both connectors'
+    scheduler sides: producer chunked prefills of random sizes interleaved
+    over steps (some restarted in new blocks after preemption, some without
+    a transfer id), consumer requests with a locally cached prefix, requests
+    first seen resumed, and decode steps.  Matched tokens, request metadata
+    and finish answers must be identical at every step."""
+    pytest.importorskip("vllm")
+    code = SCHED_RANDOM.replace("ROOT", repr(ROOT)).replace("REF", repr(REF))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=900, cwd=str(tmp_path))
+    assert out.returncode == 0 and "RANDOM SCHEDULER OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
+
+
 OFFLINE = r"""
 import sys, types
 sys.path.insert(0, ROOT)
