@@ -540,6 +540,75 @@ def test_scheduler_side_matches_the_reference_on_random_traces(tmp_path):
         (out.stdout[-1500:] + out.stderr[-3000:])
 
 
+QUANT_RANDOM = r"""
+import random, sys, types
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+import torch
+from kvserve_hpdps_b200.compression.quantizer import KVServeQuantizer as OQ
+from kvserve_v1.compression.quantizer.kvserve_quantizer import KVServeQuantizer as RQ
+
+def same(a, b):
+    if torch.is_tensor(a):
+        return torch.is_tensor(b) and a.shape == b.shape and a.dtype == b.dtype and torch.equal(a, b)
+    if isinstance(a, dict):
+        return isinstance(b, dict) and a.keys() == b.keys() and all(same(a[k], b[k]) for k in a)
+    if isinstance(a, (list, tuple)):
+        return isinstance(b, (list, tuple)) and len(a) == len(b) and all(map(same, a, b))
+    return a == b
+
+rng = random.Random(11)
+g = torch.Generator().manual_seed(11)
+models = {"Qwen2.5-7B-Instruct": (28, 4), "Llama-3.1-8B-Instruct": (32, 8),
+          "Qwen2.5-32B-Instruct": (64, 8)}
+n = 0
+for case in range(60):
+    model = rng.choice(sorted(models))
+    layers, heads = models[model]
+    tp = rng.choice([t for t in (1, 2, 4) if heads % t == 0])
+    rank = rng.randrange(tp)
+    hk, hv = rng.randint(2, 254), rng.randint(2, 254)
+    kw = dict(model_name=model, hybrid_ratio=rng.choice([0.0, 0.1, 0.3, 0.5, 0.8, 1.0,
+                                                         rng.random()]),
+              high_key_max_value=hk, high_value_max_value=hv,
+              low_key_max_value=rng.randint(2, hk), low_value_max_value=rng.randint(2, hv),
+              axis_key=rng.choice(["channel", "token", "tensor"]),
+              axis_value=rng.choice(["channel", "token", "tensor"]),
+              split_type=rng.choice(["head", "layer"]))
+    if tp > 1:
+        kw.update(tensor_parallel_size=tp, tp_rank=rank)
+    oq, rq = OQ(**kw), RQ(**kw)
+    dtype = rng.choice([torch.bfloat16, torch.float16])
+    for _ in range(2):
+        layer = rng.randrange(layers)
+        shape = (2, rng.randint(1, 6), rng.choice([1, 16]), heads // tp, 128)
+        x = torch.randn(shape, generator=g) * rng.choice([0.1, 1.0, 20.0])
+        x[..., rng.randrange(128)] *= 12  # an outlier channel
+        x = x.to(dtype)
+        qo, mo = oq.quantize(layer, x)
+        qr, mr = rq.quantize(layer, x)
+        assert torch.equal(qo, qr) and same(mo, mr), ("quantize", case, kw, shape, layer)
+        do, dr = oq.dequantize(layer, qo, mo), rq.dequantize(layer, qr, mr)
+        assert same(do, dr), ("dequantize", case, kw, shape, layer)
+        n += 1
+print("QUANT RANDOM OK", n)
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_quantizer_matches_the_reference_on_random_configs(tmp_path):
+    """60 seeded random quantizer configurations (model head-score table,
+    hybrid ratio, the four level counts, key/value axes, head or layer
+    split, TP size and rank) on random bf16/fp16 KV with an outlier channel:
+    codes, metadata and reconstruction equal the reference's quantizer's."""
+    code = QUANT_RANDOM.replace("ROOT", repr(ROOT)).replace("REF", repr(REF))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=900, cwd=str(tmp_path))
+    assert out.returncode == 0 and "QUANT RANDOM OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
+
+
 OFFLINE = r"""
 import sys, types
 sys.path.insert(0, ROOT)
