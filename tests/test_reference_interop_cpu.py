@@ -609,6 +609,54 @@ def test_quantizer_matches_the_reference_on_random_configs(tmp_path):
         (out.stdout[-1500:] + out.stderr[-3000:])
 
 
+TRANSFORM = r"""
+import sys
+sys.path.insert(0, ROOT)
+sys.path.insert(0, STANDIN)
+sys.path.insert(0, REF)
+import torch
+from kvserve_hpdps_b200.compression.transformer import HadamardTransform as OH
+from kvserve_v1.compression.transformer.hadamard_func import HadamardTransform as RH
+g = torch.Generator().manual_seed(5)
+n = 0
+for seed in (0x3333, 0xC0FEBABE):
+    o, r = OH(seed), RH(seed)
+    for D in (128, 96, 64, 80):          # power-of-two chunks for the others
+        for dtype in (torch.float32, torch.bfloat16, torch.float16):
+            for layer in (0, 7, 31):
+                x = (torch.randn(3, 16, 4, D, generator=g) * 4).to(dtype)
+                yo, yr = o.transform(layer, x), r.transform(layer, x)
+                assert yo.dtype == yr.dtype == dtype and yo.shape == yr.shape
+                tol = {torch.float32: 1e-5, torch.bfloat16: 2 ** -7, torch.float16: 2 ** -10}
+                torch.testing.assert_close(yo.float(), yr.float(), rtol=tol[dtype],
+                                           atol=tol[dtype] * 4)
+                zo, zr = o.inverse(layer, yo), r.inverse(layer, yo)
+                torch.testing.assert_close(zo.float(), zr.float(), rtol=tol[dtype],
+                                           atol=tol[dtype] * 4)
+                if dtype == torch.float32:
+                    torch.testing.assert_close(zo, x, rtol=1e-5, atol=1e-5)
+                n += 1
+print("TRANSFORM OK", n)
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_hadamard_transform_matches_the_reference(tmp_path):
+    """The reference's own HadamardTransform (its FWHT extension replaced by
+    the plain-PyTorch stand-in of the same function) against ours: forward
+    and inverse for two seeds, power-of-two and chunked head sizes, fp32 /
+    bf16 / fp16, several layers -- equal within one rounding of the dtype
+    (the FWHT's fp32 summation order may differ); the fp32 round trip
+    returns the input."""
+    code = TRANSFORM.replace("ROOT", repr(ROOT)).replace("REF", repr(REF)).replace(
+        "STANDIN", repr(os.path.join(ROOT, "baseline", "standin")))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0 and "TRANSFORM OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
+
+
 OFFLINE = r"""
 import sys, types
 sys.path.insert(0, ROOT)
