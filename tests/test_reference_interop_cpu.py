@@ -657,6 +657,67 @@ def test_hadamard_transform_matches_the_reference(tmp_path):
         (out.stdout[-1500:] + out.stderr[-3000:])
 
 
+TRANSFORM_WIRE = r"""
+import sys
+sys.path.insert(0, ROOT)
+sys.path.insert(0, STANDIN)
+sys.path.insert(0, REF)
+import torch
+from kvserve_hpdps_b200.compression import wire as OW
+from kvserve_hpdps_b200.compression.manager import KVCompressionAdapter as Ours
+from kvserve_v1.compression import wire as RW
+from kvserve_v1.compression.manager import KVCompressionAdapter as Ref
+L, T, H, D = 4, 256, 4, 128
+g = torch.Generator().manual_seed(3)
+x = torch.randn((L, 2, 1, T, H, D), generator=g)
+x[:, 0, ..., :4] *= 12
+x = x.to(torch.bfloat16)
+qc = {"model_name": "Qwen2.5-7B-Instruct", "hybrid_ratio": 0.3, "high_key_max_value": 16,
+      "high_value_max_value": 16, "low_key_max_value": 12, "low_value_max_value": 16,
+      "axis_key": "channel", "axis_value": "token", "split_type": "head"}
+spec = {"enabled": True, "pipeline": ["transformer", "quantizer"],
+        "transformer_config": {"transform_type": "hadamard", "seed": 0x3333},
+        "quantizer_config": qc, "min_compress_size": 0}
+ours = Ours(dict(spec, backend="generic"), H, D, model_name="Qwen2.5-7B-Instruct", num_layers=28)
+ref = Ref(spec, H, D, model_name="Qwen2.5-7B-Instruct")
+def close(a, b, what):
+    a, b = a.float().reshape(-1), b.float().reshape(-1)
+    err = (a - b).abs().max().item()
+    assert err <= 0.02 * b.abs().max().item(), (what, err)
+cd, rc = ours.compress(x, "a"), ref.compress(x, "b")
+co, cr = cd.compressed_tensor.view(torch.uint8).reshape(-1), rc.compressed_tensor.view(
+    torch.uint8).reshape(-1)
+assert co.shape == cr.shape and (co == cr).float().mean().item() > 0.999, "codes"
+w = OW.build_wire(cd, 512 << 20)
+by_ref = ref.decompress(RW.restore_from_wire(RW.CompressedWire(w.meta, w.body_chunks,
+                                                               w.aux_tensors)))
+close(by_ref, ours.decompress(cd), "ours -> reference")
+rw = RW.build_wire(rc, 512 << 20)
+by_ours = ours.decompress(OW.restore_from_wire(OW.CompressedWire(rw.meta, rw.body_chunks,
+                                                                 rw.aux_tensors)))
+close(by_ours, ref.decompress(rc), "reference -> ours")
+cos = torch.nn.functional.cosine_similarity(by_ours.float().reshape(-1), x.float().reshape(-1), 0)
+assert cos.item() > 0.98, cos
+print("TRANSFORM WIRE OK", (co == cr).float().mean().item())
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_transform_pipeline_messages_cross_between_the_frameworks(tmp_path):
+    """Transformer + quantizer pipeline messages (the reference's Hadamard
+    with the FWHT stand-in): the code bodies agree byte for byte except where
+    the two FWHT summation orders round a value onto the other side of a
+    quantization step (under 0.1 % of the bytes), and each framework decodes
+    the other's message to the other's own reconstruction."""
+    code = TRANSFORM_WIRE.replace("ROOT", repr(ROOT)).replace("REF", repr(REF)).replace(
+        "STANDIN", repr(os.path.join(ROOT, "baseline", "standin")))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0 and "TRANSFORM WIRE OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
+
+
 OFFLINE = r"""
 import sys, types
 sys.path.insert(0, ROOT)
