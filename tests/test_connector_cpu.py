@@ -528,3 +528,70 @@ def test_late_transport_reports_still_find_their_statistics_entry(monkeypatch):
     p._retire_sent_entries(["t-refused"])
     p._retire_sent_entries([])
     assert "t-refused" not in p._sent_orig
+
+
+@pytest.mark.parametrize("compression", [None, "default"])
+def test_soak_with_random_failures(compression, monkeypatch):
+    """Thirty steps of one to three requests of random lengths through a
+    producer/consumer pair, with messages dropped, refused or delayed at
+    random: every request either arrives intact (raw) or close (compressed)
+    in its consumer blocks, or its blocks are reported to vLLM's load-failure
+    policy in that step; nothing accumulates in the connectors."""
+    import random
+
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.15)
+    monkeypatch.setattr(mod, "STATS_ENTRY_TTL_S", 0.0)
+    rng = random.Random(7 if compression else 8)
+    p, c, pair = make_pair(compression)
+    nb = 64
+    pc, cc = caches(nb, 11), caches(nb, 12)
+    p.register_kv_caches(pc)
+    c.register_kv_caches(cc)
+    loaded = failed = 0
+    for step in range(30):
+        free_p, free_c = list(range(nb)), list(range(nb))
+        rng.shuffle(free_p)
+        rng.shuffle(free_c)
+        reqs = []
+        for i in range(rng.randint(1, 3)):
+            ntok = rng.randint(1, 80)
+            k = -(-ntok // BS)
+            reqs.append((f"s{step}r{i}", f"t{step}-{i}", ntok,
+                         [free_p.pop() for _ in range(k)], [free_c.pop() for _ in range(k)]))
+        fault = rng.random()
+        if fault < 0.15:
+            pair.drop_next = 1
+        elif fault < 0.3:
+            pair.refuse_next = 1
+        pm, cm = CompressedKVConnectorMetadata(), CompressedKVConnectorMetadata()
+        for rid, tid, ntok, pb, cb in reqs:
+            pm.add_request(rid, tid, list(range(ntok)), pb, BS)
+            cm.add_request("d" + rid, tid, list(range(ntok)), cb, BS)
+        p.bind_connector_metadata(pm)
+        for name in sorted(pc, key=layer_index):
+            p.save_kv_layer(name, pc[name], None)
+        p.wait_for_save()
+        c.bind_connector_metadata(cm)
+        c.start_load_kv(None)
+        bad = c.get_block_ids_with_load_errors()
+        for rid, tid, ntok, pb, cb in reqs:
+            if set(cb) <= bad:
+                failed += 1
+                continue
+            assert not set(cb) & bad, (step, rid)
+            for name in pc:
+                a, b = pc[name][:, pb].float(), cc[name][:, cb].float()
+                if compression is None:
+                    assert torch.equal(a, b), (step, rid)
+                else:
+                    cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)
+                    assert float(cos) > 0.9, (step, rid, float(cos))
+            loaded += 1
+        c.get_kv_connector_stats()
+        p.get_kv_connector_stats()
+        pair.inbox.clear()  # a dropped step's peers never come
+    assert loaded > 20 and failed > 0
+    p._retire_sent_entries([])
+    assert not p._sent_orig and not p._stats_wait and not p._save_times
+    assert not c._worker_received and not c._partial and not c._load_errors
