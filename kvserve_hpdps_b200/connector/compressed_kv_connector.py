@@ -229,6 +229,9 @@ class CompressedKVConnector(KVConnectorBase_V1):
         # consumer: blocks whose load failed this step, handed to vLLM's
         # kv_load_failure_policy by get_block_ids_with_load_errors()
         self._load_errors: set[int] = set()
+        # consumer: transfer ids whose load failed -> when; their messages
+        # that arrive late are released instead of queued for good
+        self._abandoned: dict[str, float] = {}
         # interval statistics for vLLM's connector-stats logging / Prometheus;
         # message key -> (original bytes, compress ms) of compressed messages
         # not yet reported sent by the transport
@@ -621,12 +624,16 @@ class CompressedKVConnector(KVConnectorBase_V1):
         if self.is_producer:
             return
         timeline("D load_enter")
-        self._drain()
         meta = self._get_connector_metadata()
+        if isinstance(meta, CompressedKVConnectorMetadata):
+            for rm in meta.requests:  # scheduled to load (again): wanted after all
+                self._abandoned.pop(rm.transfer_id, None)
+        self._drain()
         if not isinstance(meta, CompressedKVConnectorMetadata):
             return
         self._fc = forward_context
         self._step_reqs = {rm.transfer_id: rm for rm in meta.requests}
+        self._drop_abandoned()
         self._got = {t: 0 for t in self._step_reqs}
         # one deadline for the step: with a dead producer the step returns
         # after LOAD_TIMEOUT_S, not after that long for each of its requests
@@ -730,10 +737,40 @@ class CompressedKVConnector(KVConnectorBase_V1):
         for tid, msgs in (self._transport.drain_received() or {}).items():
             for names, payload in msgs:
                 members = self._members(tid, payload)
+                # members whose load already failed will not be scheduled to
+                # load again (vLLM recomputes or fails them): count them done
+                gone = {t for t in members if t in self._abandoned}
                 rec = {"names": names, "payload": payload, "members": set(members),
-                       "decoded": set(), "prepared": False, "cd": None}
+                       "decoded": set(gone), "prepared": False, "cd": None}
+                if gone and gone == rec["members"]:
+                    self._release_late(rec)
+                    continue
                 for t in members:
-                    self._worker_received[t].append(rec)
+                    if t not in gone:
+                        self._worker_received[t].append(rec)
+
+    def _release_late(self, rec: dict) -> None:
+        """A message nobody will decode (its requests' loads failed before
+        it arrived): its ring space goes back at once."""
+        logger.info("releasing a late message for %s", ", ".join(sorted(rec["members"])))
+        self._partial.pop(id(rec), None)
+        if hasattr(self._transport, "release"):
+            self._transport.release(rec["payload"])
+
+    def _drop_abandoned(self) -> None:
+        """Queued messages of requests whose load failed in an earlier step
+        are dropped (released once no other member needs them), and failed
+        transfer ids are forgotten after ten load timeouts."""
+        if not self._abandoned:
+            return
+        for t in [t for t in self._worker_received if t in self._abandoned]:
+            for rec in self._worker_received.pop(t):
+                rec["decoded"].add(t)
+                if rec["decoded"] >= rec["members"]:
+                    self._release_late(rec)
+        cutoff = time.monotonic() - 10 * LOAD_TIMEOUT_S
+        for t in [t for t, when in self._abandoned.items() if when < cutoff]:
+            self._abandoned.pop(t, None)
 
     def _layer_cache(self, name: str, forward_context: Any) -> Optional[torch.Tensor]:
         t = self._kv_caches.get(name)
@@ -807,11 +844,13 @@ class CompressedKVConnector(KVConnectorBase_V1):
         blocks are reported to vLLM, which recomputes them or fails the
         request (``kv_load_failure_policy``), instead of decoding with stale
         blocks."""
+        now = time.monotonic()
         for t in tids:
             rm = self._step_reqs.get(t)
             if rm is not None:
                 self._load_errors.update(int(b) for b in rm.block_ids)
                 self._xfer_stats.record_failed_load()
+                self._abandoned[t] = now
 
     def get_kv_connector_stats(self) -> Optional[KVServeConnectorStats]:
         """This worker's transfer statistics since the last call (None when

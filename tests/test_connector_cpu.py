@@ -590,8 +590,29 @@ def test_soak_with_random_failures(compression, monkeypatch):
             loaded += 1
         c.get_kv_connector_stats()
         p.get_kv_connector_stats()
-        pair.inbox.clear()  # a dropped step's peers never come
     assert loaded > 20 and failed > 0
     p._retire_sent_entries([])
     assert not p._sent_orig and not p._stats_wait and not p._save_times
     assert not c._worker_received and not c._partial and not c._load_errors
+
+
+
+def test_late_messages_of_failed_loads_are_released(monkeypatch):
+    """A message that arrives after its request's load timed out (the
+    blocks went to vLLM's policy) is not queued for good: it is released on
+    arrival, and a message already queued for a failed request is dropped at
+    the next step."""
+    import time
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.1)
+    p, c, pair = make_pair(None)
+    released = []
+    pair_cons = c._transport
+    pair_cons.release = lambda payload, dev=None: released.append(payload)
+    pair.delay_s = 0.4
+    handoff(p, c)                      # the message comes after the step gave up
+    assert c.get_block_ids_with_load_errors() == {2, 6, 0}
+    time.sleep(0.5)
+    c.bind_connector_metadata(CompressedKVConnectorMetadata())
+    c.start_load_kv(None)              # drained at the next step: released at once
+    assert len(released) == 1 and not c._worker_received
