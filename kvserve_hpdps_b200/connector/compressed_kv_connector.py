@@ -109,6 +109,8 @@ logger = get_logger(__name__)
 LOAD_TIMEOUT_S = float(os.environ.get("KVSERVE_LOAD_TIMEOUT_S", "60"))
 CONTROLLER_FEEDBACK_TTL_S = 300.0  # as the adapter's controller contexts
 STATS_ENTRY_TTL_S = 30.0  # unreported statistics entries of finished requests
+# a received message no scheduled request claims within this time is released
+UNCLAIMED_TTL_S = float(os.environ.get("KVSERVE_UNCLAIMED_TTL_S", "600"))
 
 
 def normalize_overlap_mode(mode) -> str:
@@ -741,7 +743,8 @@ class CompressedKVConnector(KVConnectorBase_V1):
                 # load again (vLLM recomputes or fails them): count them done
                 gone = {t for t in members if t in self._abandoned}
                 rec = {"names": names, "payload": payload, "members": set(members),
-                       "decoded": set(gone), "prepared": False, "cd": None}
+                       "decoded": set(gone), "prepared": False, "cd": None,
+                       "arrived": time.monotonic()}
                 if gone and gone == rec["members"]:
                     self._release_late(rec)
                     continue
@@ -758,9 +761,17 @@ class CompressedKVConnector(KVConnectorBase_V1):
             self._transport.release(rec["payload"])
 
     def _drop_abandoned(self) -> None:
-        """Queued messages of requests whose load failed in an earlier step
-        are dropped (released once no other member needs them), and failed
-        transfer ids are forgotten after ten load timeouts."""
+        """Queued messages of requests whose load failed in an earlier step,
+        and messages no scheduled request has claimed for ``UNCLAIMED_TTL_S``
+        (a request the decode engine never got), are dropped (released once
+        no other member needs them); failed transfer ids are forgotten after
+        ten load timeouts."""
+        stale = time.monotonic() - UNCLAIMED_TTL_S
+        for t in [t for t, q in self._worker_received.items()
+                  if t not in self._step_reqs and q and q[0].get("arrived", stale) < stale]:
+            logger.warning("no request claimed the KV of transfer %s for %.0f s; dropping it",
+                           t, UNCLAIMED_TTL_S)
+            self._abandoned.setdefault(t, time.monotonic())
         if not self._abandoned:
             return
         for t in [t for t in self._worker_received if t in self._abandoned]:

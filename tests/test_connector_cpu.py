@@ -616,3 +616,25 @@ def test_late_messages_of_failed_loads_are_released(monkeypatch):
     c.bind_connector_metadata(CompressedKVConnectorMetadata())
     c.start_load_kv(None)              # drained at the next step: released at once
     assert len(released) == 1 and not c._worker_received
+
+
+def test_unclaimed_messages_are_released_after_their_ttl(monkeypatch):
+    """KV for a transfer id the decode engine never schedules (its request
+    never reached it) does not hold its ring space for good."""
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    p, c, pair = make_pair(None)
+    released = []
+    c._transport.release = lambda payload, dev=None: released.append(payload)
+    pc = caches(8, 1)
+    p.register_kv_caches(pc)
+    c.register_kv_caches(caches(8, 2))
+    p.bind_connector_metadata(meta_for("r1", "orphan", 40, [5, 1, 7]))
+    for name in sorted(pc, key=layer_index):
+        p.save_kv_layer(name, pc[name], None)
+    p.wait_for_save()
+    c.bind_connector_metadata(CompressedKVConnectorMetadata())
+    c.start_load_kv(None)               # arrives; nobody claims it yet
+    assert "orphan" in c._worker_received and not released
+    monkeypatch.setattr(mod, "UNCLAIMED_TTL_S", 0.0)
+    c.start_load_kv(None)
+    assert not c._worker_received and len(released) == 1
