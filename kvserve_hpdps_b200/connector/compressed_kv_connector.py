@@ -587,6 +587,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
             while self._sent_retired and now - self._sent_retired[0][0] > STATS_ENTRY_TTL_S:
                 for t in self._sent_retired.popleft()[1]:
                     self._sent_orig.pop(t, None)
+                    self._stats_wait.pop(t, None)  # JSONL rows of messages never reported
 
     def get_finished(self, finished_req_ids: set[str]):
         if self.is_producer:
