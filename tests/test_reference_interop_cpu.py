@@ -718,6 +718,80 @@ def test_transform_pipeline_messages_cross_between_the_frameworks(tmp_path):
         (out.stdout[-1500:] + out.stderr[-3000:])
 
 
+CTL_RANDOM = r"""
+import random, sys
+sys.path.insert(0, ROOT)
+sys.path.insert(0, REF)
+from kvserve_hpdps_b200.controller.analytical_model import AnalyticalModel
+from kvserve_hpdps_b200.controller.online_controller import OnlineController as Ours
+from kvserve_hpdps_b200.controller.profile_library import ProfileLibrary as OursLib
+from kvserve_hpdps_b200.offline.library_export import build_library, write_library
+from kvserve_hpdps_b200.offline.search_space import Candidate
+from kvserve_v1.compression.controller.online_controller import OnlineController as Ref
+from kvserve_v1.compression.controller.profile_library import ProfileLibrary as RefLib
+rng = random.Random(3)
+n = 0
+for lib_i in range(25):
+    evals = []
+    for _ in range(rng.randint(1, 9)):
+        hk, hv = rng.choice([16, 12, 8]), rng.choice([16, 12, 8])
+        c = Candidate(rng.choice([0.0, 0.3, 0.5, 0.8, 1.0]), hk, hv,
+                      rng.choice([x for x in (12, 8, 6, 4) if x <= hk]),
+                      rng.choice([x for x in (8, 6, 4) if x <= hv]))
+        evals.append({"candidate": c.key() + f"_{len(evals)}", "config": c.quantizer_config(),
+                      "accuracy": rng.uniform(0.85, 1.0), "compression_ratio": rng.uniform(1.5, 12),
+                      "harmonic_speed_mbps": rng.uniform(500, 200000)})
+    edges = sorted(rng.sample([0.8, 0.85, 0.9, 0.93, 0.95, 0.97, 0.99], rng.randint(2, 5)))
+    bws = sorted(rng.sample([10, 100, 1000, 5000, 20000, 100000, 1000000], rng.randint(2, 6)))
+    path = TMP + f"/lib{lib_i}.json"
+    write_library(path, build_library(evals, "m", acc_edges=edges + [1.0001],
+                                      bw_edges_mbps=bws, k=rng.randint(1, 4)))
+    ours = Ours(OursLib(path), epsilon=0.0, model=AnalyticalModel(reference_transfer_term=True))
+    ref = Ref(RefLib(path), epsilon=0.0)
+    for _ in range(60):
+        V = rng.choice([1e6, 64e6, 470e6, 4e9])
+        B = 10 ** rng.uniform(0, 6.5)
+        slo = rng.choice([1.0, 20.0, 200.0, 2000.0, 1e9])
+        acc = rng.uniform(0.8, 1.0)
+        tm = rng.choice([0.0, 10.0, 100.0])
+        po, co = ours.select_profile(V, B, tm, slo, acc)
+        pr, cr_ = ref.select_profile(V, B, tm, slo, acc)
+        ido = None if po is None else po.profile_id
+        idr = None if pr is None else pr.profile_id
+        assert ido == idr, (lib_i, V, B, slo, acc, ido, idr, co, cr_)
+        for k in ("bucket_id", "interval_id", "action", "num_candidates", "T_hat", "T_eff"):
+            if k in cr_:
+                a, b = co.get(k), cr_[k]
+                assert a == b or (isinstance(b, float) and abs(a - b) <= 1e-9 * max(1, abs(b))), \
+                    (lib_i, k, co, cr_)
+        if po is not None:
+            t = rng.uniform(1, 500)
+            ours.update(co, t)
+            ref.update(cr_, t)
+        n += 1
+    so, sr = ours.get_statistics(), ref.get_statistics()
+    for k in ("total_decisions", "exploit_count", "explore_count", "no_compression_count"):
+        assert so[k] == sr[k], (lib_i, k, so, sr)
+print("RANDOM CONTROLLER OK", n)
+"""
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kvserve_v1")),
+                    reason="reference not installed in baseline/_ref")
+def test_controller_decisions_match_the_reference_on_random_libraries(tmp_path):
+    """25 random profile libraries (random profiles, accuracy buckets,
+    bandwidth intervals and candidate counts), 60 random requests each
+    (volume, bandwidth, model time, SLO, accuracy requirement), with bandit
+    updates in between: both controllers pick the same profile with the same
+    context and keep the same statistics."""
+    code = CTL_RANDOM.replace("ROOT", repr(ROOT)).replace("REF", repr(REF)) \
+        .replace("TMP", repr(str(tmp_path)))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=str(tmp_path))
+    assert out.returncode == 0 and "RANDOM CONTROLLER OK" in out.stdout, \
+        (out.stdout[-1500:] + out.stderr[-3000:])
+
+
 OFFLINE = r"""
 import sys, types
 sys.path.insert(0, ROOT)
