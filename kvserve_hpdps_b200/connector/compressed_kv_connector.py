@@ -757,9 +757,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         """A message nobody will decode (its requests' loads failed before
         it arrived): its ring space goes back at once."""
         logger.info("releasing a late message for %s", ", ".join(sorted(rec["members"])))
-        self._partial.pop(id(rec), None)
-        if hasattr(self._transport, "release"):
-            self._transport.release(rec["payload"])
+        self._release_rec(rec)
 
     def _drop_abandoned(self) -> None:
         """Queued messages of requests whose load failed in an earlier step,
@@ -844,9 +842,7 @@ class CompressedKVConnector(KVConnectorBase_V1):
         finally:
             self._mark(rec, now, plain)
             if rec["decoded"] >= rec["members"]:
-                if hasattr(tr, "release"):  # after the decode queued on this stream
-                    tr.release(payload, dev)
-                self._partial.pop(id(rec), None)
+                self._release_rec(rec, dev)  # after the decode queued on this stream
             else:
                 rec.setdefault("t", time.monotonic())
                 self._partial[id(rec)] = rec
@@ -905,15 +901,38 @@ class CompressedKVConnector(KVConnectorBase_V1):
 
     def _sweep_partial(self) -> None:
         """Grouped records some of whose members were never scheduled here
-        give their ring space back after twice the load timeout."""
+        give their ring space back after twice the load timeout.  The members
+        still waiting lose the record with it: a later load of theirs fails
+        cleanly (reported to vLLM) instead of decoding memory the producer may
+        have reused."""
         if not self._partial:
             return
         cutoff = time.monotonic() - 2 * LOAD_TIMEOUT_S
+        now = time.monotonic()
         for key, rec in list(self._partial.items()):
             if rec.get("t", 0.0) < cutoff:
-                self._partial.pop(key, None)
-                if hasattr(self._transport, "release"):
-                    self._transport.release(rec["payload"])
+                for t in rec["members"] - rec["decoded"]:
+                    q = self._worker_received.get(t)
+                    if q is not None:  # by identity: records hold tensors
+                        rest = deque(r for r in q if r is not rec)
+                        if rest:
+                            self._worker_received[t] = rest
+                        else:
+                            self._worker_received.pop(t, None)
+                    self._abandoned.setdefault(t, now)
+                self._release_rec(rec)
+
+    def _release_rec(self, rec: dict, device=None) -> None:
+        """Return a record's ring space, once, whichever path gets there first."""
+        self._partial.pop(id(rec), None)
+        if rec.get("released"):
+            return
+        rec["released"] = True
+        if hasattr(self._transport, "release"):
+            if device is None:
+                self._transport.release(rec["payload"])
+            else:
+                self._transport.release(rec["payload"], device)
 
     def _inject_record(self, rec: dict, members: list[str], names: list[str],
                        payload: Any) -> None:

@@ -638,3 +638,39 @@ def test_unclaimed_messages_are_released_after_their_ttl(monkeypatch):
     monkeypatch.setattr(mod, "UNCLAIMED_TTL_S", 0.0)
     c.start_load_kv(None)
     assert not c._worker_received and len(released) == 1
+
+
+def test_swept_group_record_is_released_once_and_fails_its_late_members(monkeypatch):
+    """A grouped message decoded for one member while another member is
+    never scheduled: after twice the load timeout its ring space goes back
+    (once, whichever cleanup comes first), and the member that shows up
+    later fails its load cleanly instead of decoding released memory."""
+    import kvserve_hpdps_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.05)
+    p, c, pair = make_pair(None)
+    released = []
+    c._transport.release = lambda payload, dev=None: released.append(id(payload))
+    pc = caches(8, 1)
+    c.register_kv_caches(caches(8, 2))
+    raw = torch.stack([pc[n][:, [5, 1, 7]] for n in sorted(pc, key=layer_index)], 0)
+    payload = {"__bundle__": True, "meta": {"metadata": {"member_tids": ["ga", "gb"]}},
+               "body_chunks": [], "aux_tensors": []}
+    # a grouped record as the transport delivers it; decoding fails here (no
+    # real compressed body), which is enough to exercise the bookkeeping
+    pair.inbox["ga"].append((["__compressed__"] + sorted(pc, key=layer_index), payload))
+    c.bind_connector_metadata(meta_for("da", "ga", 40, [2, 6, 0]))
+    c.start_load_kv(None)
+    assert "gb" in c._worker_received and len(c._partial) == 1
+    import time
+    time.sleep(0.15)
+    c.bind_connector_metadata(CompressedKVConnectorMetadata())
+    c.start_load_kv(None)          # sweep: released once, gb abandoned
+    monkeypatch.setattr(mod, "UNCLAIMED_TTL_S", 0.0)
+    c.start_load_kv(None)          # the unclaimed cleanup finds nothing left to release
+    assert released == [id(payload)] and not c._worker_received and not c._partial
+    c.get_block_ids_with_load_errors()
+    c.bind_connector_metadata(meta_for("db", "gb", 40, [3, 4, 5]))
+    c.start_load_kv(None)          # gb scheduled late: times out cleanly, reported
+    assert c.get_block_ids_with_load_errors() == {3, 4, 5}
+    assert released == [id(payload)]
+    del raw
