@@ -112,9 +112,17 @@ class RingAllocator:
                     return None
                 self.cv.wait(timeout=min(left, 0.1))
 
-    def release(self, off: int, size: int) -> None:
+    def release(self, off: int, size: int) -> bool:
+        """Return [off, off + size) to the free list; a range that overlaps
+        free space (a region returned twice) is refused and logged, so the
+        list never hands the same bytes to two messages."""
         size = _align(size)
         with self.cv:
+            if off < 0 or off + size > self.capacity or any(
+                    o < off + size and off < o + s for o, s in self.free):
+                logger.error("p2p: ring region [%d, %d) returned twice or out of range; ignored",
+                             off, off + size)
+                return False
             self.free.append((off, size))
             self.free.sort()
             merged = []
@@ -125,6 +133,7 @@ class RingAllocator:
                     merged.append((o, s))
             self.free = merged
             self.cv.notify_all()
+        return True
 
     def free_bytes(self) -> int:
         with self.cv:
@@ -263,14 +272,18 @@ class P2PTransport:
     def _release_regions(self, regions) -> None:
         if not regions:
             return
+        owned = []
         with self._lock:
-            for off, _ in regions:
+            for off, size in regions:
                 slot = self._slot_of.pop(int(off), None)
-                if slot is not None:
-                    self._free_slots.append(slot)
-            self._inflight_msgs -= len(regions)
+                if slot is None:  # not (or no longer) a message of ours
+                    logger.error("p2p: FREE of unknown ring region at %d ignored", off)
+                    continue
+                self._free_slots.append(slot)
+                owned.append((off, size))
+            self._inflight_msgs -= len(owned)
             self._slots_cv.notify_all()
-        for off, size in regions:
+        for off, size in owned:
             self._alloc.release(off, size)
 
     def _completion_loop(self) -> None:

@@ -573,3 +573,24 @@ def test_p2p_producer_headers_pass_the_consumer_check(monkeypatch):
     assert [h["request_id"] for h in headers] == ["r0", "r1", "r2", "r3"]
     for h in headers:
         cons._check_put(unpack(pack(h)))
+
+
+def test_p2p_region_returned_twice_is_ignored():
+    """A FREE repeated for the same region (or naming a region the producer
+    never reserved) changes nothing: the free list never hands the same
+    bytes to two messages and the in-flight count stays right."""
+    from kvserve_hpdps_b200.parallel.p2p_transport import RingAllocator
+    t = _slot_state(4, 2048, 0.2)
+    a = _reserve_done(t, 512)
+    b = _reserve_done(t, 512)
+    t._on_free([[a[0], 512]])
+    t._on_free([[a[0], 512]])          # repeated
+    t._on_free([[1536, 512]])          # never reserved
+    assert t._inflight_msgs == 1 and t._alloc.free_bytes() == 2048 - 512
+    c = _reserve_done(t, 512)
+    d = _reserve_done(t, 512)
+    assert len({c[0], d[0], b[0]}) == 3  # three live messages, three regions
+    al = RingAllocator(1024)
+    off = al.try_alloc(256)
+    assert al.release(off, 256) and not al.release(off, 256) and not al.release(900, 256)
+    assert al.free_bytes() == 1024
