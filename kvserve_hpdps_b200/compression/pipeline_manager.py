@@ -16,7 +16,7 @@ pipeline's numerics exactly (its quantizer computes in the KV dtype).
 from __future__ import annotations
 
 import time
-from typing import Any, Optional
+from typing import Optional
 
 import torch
 

@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import json
 import math
-from typing import Iterable, Optional, Sequence
+from typing import Iterable, Sequence
 
 
 def _pareto(profiles: list[dict]) -> list[dict]:

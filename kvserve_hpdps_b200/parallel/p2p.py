@@ -15,7 +15,6 @@ addresses are only written by this framework's own store loops.
 from __future__ import annotations
 
 import ctypes
-from typing import Optional
 
 import torch
 
