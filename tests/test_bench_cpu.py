@@ -206,3 +206,21 @@ def test_full_path_summary_carries_its_roofline():
     out = bench._summary(a, wl, res, 1, "rans")
     assert out["compression_ratio"] == 9.18 and out["e2e"] == {"value": 0.915}
     assert out["roofline"]["limited_by"] == "hbm" and 0.2 < out["roofline"]["fraction"] < 0.5
+
+
+def test_every_package_module_imports():
+    """Each module of the package imports on a CPU-only machine (the native
+    library's own file is not a Python module)."""
+    import importlib
+    import pkgutil
+
+    import kvserve_hpdps_b200 as pkg
+    bad = []
+    for m in pkgutil.walk_packages(pkg.__path__, pkg.__name__ + "."):
+        if m.name.endswith(".libkvs_b200") or ".compat.kvserve_v1" in m.name:
+            continue
+        try:
+            importlib.import_module(m.name)
+        except Exception as e:  # noqa: BLE001
+            bad.append((m.name, repr(e)[:200]))
+    assert not bad, bad
