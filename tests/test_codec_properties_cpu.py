@@ -51,3 +51,56 @@ def test_corrupted_stream_never_crashes(codec, data, where, flip):
     except (RuntimeError, ValueError):
         return  # rejected
     assert out.dtype == torch.uint8 and out.numel() == data.numel()
+
+
+def _same(a, b):
+    if torch.is_tensor(a):
+        return torch.is_tensor(b) and a.dtype == b.dtype and a.shape == b.shape and \
+            torch.equal(a, b)
+    if isinstance(a, dict):
+        return isinstance(b, dict) and a.keys() == b.keys() and all(_same(a[k], b[k]) for k in a)
+    if isinstance(a, (list, tuple)):
+        return isinstance(b, (list, tuple)) and len(a) == len(b) and all(map(_same, a, b))
+    return a == b
+
+
+@st.composite
+def metadata(draw, depth=0):
+    leaf = st.one_of(st.integers(-2 ** 40, 2 ** 40), st.booleans(), st.text(max_size=8),
+                     st.floats(allow_nan=False, allow_infinity=False), st.none(),
+                     st.builds(lambda n, d: torch.arange(n).to(d), st.integers(0, 12),
+                               st.sampled_from([torch.float16, torch.int64, torch.uint8,
+                                                torch.float32])))
+    if depth >= 2:
+        return draw(leaf)
+    return draw(st.one_of(
+        leaf, st.lists(st.deferred(lambda: metadata(depth=depth + 1)), max_size=3),
+        st.dictionaries(st.text("abcdefgh_", min_size=1, max_size=6),
+                        st.deferred(lambda: metadata(depth=depth + 1)), max_size=3)))
+
+
+PLAIN = st.dictionaries(st.text("abcdefgh_", min_size=1, max_size=6),
+                        st.one_of(st.integers(-2 ** 40, 2 ** 40), st.text(max_size=8),
+                                  st.lists(st.integers(0, 9), max_size=4)), max_size=3)
+
+
+@settings(max_examples=60, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(qp=st.lists(metadata(), max_size=4), plain=PLAIN,
+       n=st.integers(0, 5000), chunk=st.sampled_from([16, 1000, 4096, 1 << 20]))
+def test_wire_envelope_round_trips_any_metadata(qp, plain, n, chunk):
+    """Tensors anywhere under ``quantization_params`` travel as aux tensors
+    behind placeholders (the wire contract allows them nowhere else); bodies
+    above the chunk bound are split into byte chunks."""
+    meta = dict(plain, quantization_params=qp)
+    from kvserve_hpdps_b200.compression.config import CompressedKVData
+    from kvserve_hpdps_b200.compression.wire import build_wire, restore_from_wire
+    body = (torch.arange(n) % 251).to(torch.uint8)
+    cd = CompressedKVData(request_id="r", layer_id=3, compressed_tensor=body,
+                          metadata=dict(meta, request_id="r"), original_size=2 * n,
+                          compressed_size=n)
+    w = build_wire(cd, chunk)
+    if n > chunk:
+        assert w.meta["body_mode"] == "byte_chunks" and len(w.body_chunks) > 1
+    back = restore_from_wire(w)
+    assert torch.equal(back.compressed_tensor.reshape(-1), body)
+    assert _same(back.metadata, cd.metadata), (back.metadata, cd.metadata)
