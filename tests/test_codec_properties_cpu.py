@@ -104,3 +104,29 @@ def test_wire_envelope_round_trips_any_metadata(qp, plain, n, chunk):
     back = restore_from_wire(w)
     assert torch.equal(back.compressed_tensor.reshape(-1), body)
     assert _same(back.metadata, cd.metadata), (back.metadata, cd.metadata)
+
+
+@settings(max_examples=60, deadline=None)
+@given(ops=st.lists(st.tuples(st.booleans(), st.integers(1, 3000), st.integers(0, 10 ** 6)),
+                    max_size=60))
+def test_ring_allocator_never_overlaps(ops):
+    """Random reservations and returns (including repeated returns): live
+    regions never overlap, stay inside the ring, and free + live bytes always
+    equal the capacity."""
+    from kvserve_hpdps_b200.parallel.p2p_transport import RingAllocator, _align
+    cap = 16384
+    al = RingAllocator(cap)
+    live: list[tuple[int, int]] = []
+    for alloc, size, pick in ops:
+        if alloc or not live:
+            off = al.try_alloc(size)
+            if off is not None:
+                n = _align(size)
+                assert 0 <= off and off + n <= cap
+                assert all(off + n <= o or o + s <= off for o, s in live)
+                live.append((off, n))
+        else:
+            o, s = live.pop(pick % len(live))
+            assert al.release(o, s)
+            assert not al.release(o, s)  # a second return is refused
+        assert al.free_bytes() + sum(s for _, s in live) == cap
