@@ -5,7 +5,8 @@ What a deployment needs, checked without launching a kernel:
 * the package and torch versions, and whether vLLM's V1 connector base class
   imports (the connector is loaded through ``kv_connector_module_path``);
 * the native library: built, loadable, its struct layouts matching the
-  Python bindings (checked on load);
+  Python bindings (checked on load), its CPU rANS coder round-tripping a
+  small buffer;
 * the GPUs: name, compute capability (the kernels are built for sm_100a
   only, so anything but 10.0 cannot run them), memory;
 * NVLink peer access between every pair of visible GPUs (the ring transport
@@ -38,6 +39,10 @@ def report() -> dict:
         lb = _lib.lib()
         out["native"] = {"path": _lib.LIB_PATH, "loaded": True,
                          "version": int(lb.kvs_library_version())}
+        from kvserve_hpdps_b200.compression.codec import decode_bytes, encode_bytes
+        probe = (torch.arange(5000) % 7).to(torch.uint8)  # the CPU coder, no GPU needed
+        out["native"]["cpu_codec_ok"] = bool(torch.equal(
+            decode_bytes(encode_bytes(probe, "rans")), probe))
     except (RuntimeError, OSError) as e:
         out["native"] = {"path": _lib.LIB_PATH, "loaded": False, "error": str(e)[:300]}
     gpus = []

@@ -167,6 +167,7 @@ def test_environment_check_report_and_exit_code():
     from kvserve_hpdps_b200 import __main__ as env
     rep = env.report()
     assert rep["package"] and rep["native"]["loaded"] is True and rep["gpus"] == []
+    assert rep["native"]["cpu_codec_ok"] is True
     assert env.exit_code(rep) == 2  # no GPU here
     b200 = {"index": 0, "name": "B200", "capability": "10.0", "fused_path": True}
     h100 = dict(b200, capability="9.0", fused_path=False)
