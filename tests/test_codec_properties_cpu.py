@@ -130,3 +130,32 @@ def test_ring_allocator_never_overlaps(ops):
             assert al.release(o, s)
             assert not al.release(o, s)  # a second return is refused
         assert al.free_bytes() + sum(s for _, s in live) == cap
+
+
+@settings(max_examples=25, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(budget=st.integers(1, 12), thr=st.floats(0.5, 1.0), noise=st.integers(0, 2 ** 31 - 1))
+def test_search_invariants(budget, thr, noise):
+    """The constraint-aware search never exceeds its budget, never evaluates
+    a candidate twice, and its best is the highest-CR feasible evaluation."""
+    import random as _r
+
+    from kvserve_hpdps_b200.offline.bo import ConstraintAwareBO, predicted_cr
+    from kvserve_hpdps_b200.offline.search_space import enumerate_space
+    rng = _r.Random(noise)
+    pool = enumerate_space({"hybrid_ratio": [0.0, 0.5, 1.0], "high_key_max_value": [16, 8],
+                            "high_value_max_value": [16, 8], "low_key_max_value": [8, 4],
+                            "low_value_max_value": [8, 4]})
+
+    def evaluate(c):  # accuracy falls with compression, plus noise
+        cr = predicted_cr(c)
+        return {"accuracy": max(0.0, 1.0 - 0.02 * cr + rng.uniform(-0.02, 0.02)),
+                "compression_ratio": cr}
+    res = ConstraintAwareBO(pool, evaluate, thr, budget=budget).run()
+    keys = [h["candidate"] for h in res["history"]]
+    assert len(keys) == res["evaluations"] <= budget and len(set(keys)) == len(keys)
+    feas = [h for h in res["history"] if h["accuracy"] >= thr]
+    if feas:
+        assert res["best"] is not None and res["best"]["compression_ratio"] == max(
+            h["compression_ratio"] for h in feas)
+    else:
+        assert res["best"] is None
