@@ -1,7 +1,9 @@
-"""Property-based checks of the CPU codecs (rANS, LC, bit-pack) through the
-public container API: every byte string round-trips, for any size and
+"""Property-based checks on the CPU: the codecs (rANS, LC) through the
+public container API (every byte string round-trips, for any size and
 symbol distribution; a corrupted stream is rejected or decodes to some
-bytes, never crashes the process."""
+bytes, never crashes the process), the wire envelope over arbitrary
+metadata, the ring allocator's no-overlap invariant and the search
+driver's invariants."""
 
 import pytest
 import torch
